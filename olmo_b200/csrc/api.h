@@ -1,0 +1,68 @@
+// C interface of the sm_100a kernels.  Every function takes raw device pointers and a stream, performs no
+// allocation, and returns 0 on success or a negative code when the launch could not be made.  Kernels that
+// can wait on another agent additionally take a device `status` word that is 0 unless a bounded wait ran out.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+enum ObEpilogue : int {
+  EPI_BF16 = 0,       // C(bf16)  = acc
+  EPI_F32_ACCUM = 1,  // C(fp32) += acc
+  EPI_BF16_ADD = 2,   // C(bf16)  = acc + R(bf16), R has the pitch of C and may alias it
+  EPI_F32_STORE = 3,  // C(fp32)  = acc
+};
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// ---- gemm.cu
+int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb, int ldc,
+                 int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag, int ready_value,
+                 int* status, int num_sms, cudaStream_t stream);
+
+
+// ---- norm.cu
+int ob_norm_rows_per_launch(int M);
+int ob_norm_fwd(const void* x, const void* res, const void* w, const void* b, void* out, float* rstd, float* mean, int M,
+                int D, int ldx, float eps, int is_rms, cudaStream_t stream);
+int ob_norm_bwd(const void* dy, const void* x, const void* w, const float* rstd, const float* mean, const void* dres,
+                void* dx, float* dw_part, float* db_part, int M, int D, int ldx, int lddx, int is_rms,
+                cudaStream_t stream);
+int ob_reduce_rows_f32(const float* part, int nparts, int D, float* out, int accumulate, cudaStream_t stream);
+
+// ---- rope.cu
+int ob_qk_rows_per_launch(int M);
+int ob_qk_norm_rope_fwd(void* qkv, void* qk_out, const void* wq, const void* wk, const float* cos_t, const float* sin_t,
+                        float* rstd_q, float* rstd_k, int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq,
+                        float eps, float clip, int do_norm, int do_rope, cudaStream_t stream);
+int ob_qk_norm_rope_bwd(const void* qkv, void* dqkv, const void* wq, const void* wk, const float* cos_t,
+                        const float* sin_t, const float* rstd_q, const float* rstd_k, float* dwq_part, float* dwk_part,
+                        int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq, float clip, int do_norm,
+                        int do_rope, cudaStream_t stream);
+
+// ---- pointwise.cu
+int ob_swiglu_fwd(const void* h, void* out, int M, int H, cudaStream_t stream);
+int ob_swiglu_bwd(const void* dout, const void* h, void* dh, int M, int H, cudaStream_t stream);
+int ob_embedding_fwd(const long long* ids, const void* table, void* out, int M, int D, int V, cudaStream_t stream);
+int ob_embedding_bwd(const long long* ids, const void* dout, float* grad, int M, int D, int V, cudaStream_t stream);
+int ob_accum_bf16_to_f32(const void* src, float* acc, long long n, cudaStream_t stream);
+int ob_cast_f32_to_bf16(const float* src, void* dst, long long n, cudaStream_t stream);
+
+// ---- loss_optim.cu
+int ob_cross_entropy(void* logits, const long long* labels, float* ce_out, float* z_out, int R, int V, int ld,
+                     long long ignore_index, float z_mult, float grad_scale, int write_grad, cudaStream_t stream);
+int ob_adamw(float* p, const float* g, float* m, float* v, void* p_lowp, long long n, const long long* seg_end,
+             const float* seg_wd, const float* seg_lr, int nseg, float beta1, float beta2, float eps, int step,
+             const float* gscale, cudaStream_t stream);
+int ob_lionw(float* p, const float* g, float* m, void* p_lowp, long long n, const long long* seg_end,
+             const float* seg_wd, const float* seg_lr, int nseg, float beta1, float beta2, const float* gscale,
+             cudaStream_t stream);
+int ob_sumsq_num_partials(long long n);
+int ob_sumsq_f32(const float* g, long long n, float* partials, float* out, int accumulate, cudaStream_t stream);
+int ob_clip_coef(const float* sumsq, float max_norm, float* coef, float* norm_out, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif

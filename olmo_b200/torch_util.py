@@ -1,0 +1,189 @@
+"""
+Process-group and device helpers (reference: ``olmo/torch_util.py:11-171``).
+
+All rank queries work without an initialised process group (they fall back to the launcher's
+environment variables, then to rank 0 / world 1), which is what lets the same code run under
+``torchrun`` over NCCL, as Gloo ranks on CPU, or as a single process.
+"""
+from __future__ import annotations
+
+import gc
+import os
+from typing import Any, Optional, TypeVar
+
+import torch
+import torch.distributed as dist
+
+T = TypeVar("T")
+
+__all__ = [
+    "seed_all",
+    "is_distributed",
+    "get_node_rank",
+    "get_world_size",
+    "get_local_world_size",
+    "get_global_rank",
+    "get_local_rank",
+    "get_fs_local_rank",
+    "move_to_device",
+    "ensure_finite_",
+    "get_default_device",
+    "barrier",
+    "peak_gpu_memory",
+    "synchronize_value",
+    "synchronize_flag",
+    "gc_cuda",
+    "get_cumulative_document_lengths",
+    "SingleAccelerator",
+]
+
+
+def seed_all(seed: int) -> None:
+    """Seed python, numpy and torch (all devices)."""
+    import random
+
+    import numpy as np
+
+    if not 0 <= seed <= 2**32 - 1:
+        raise ValueError(f"Seed {seed} is invalid. It must be on [0; 2^32 - 1]")
+    random.seed(seed)
+    np.random.seed(seed)
+    torch.manual_seed(seed)
+    if torch.cuda.is_available():
+        torch.cuda.manual_seed_all(seed)
+
+
+def is_distributed() -> bool:
+    return dist.is_available() and dist.is_initialized()
+
+
+def _env_int(name: str) -> Optional[int]:
+    v = os.environ.get(name)
+    return None if v is None or v == "" else int(v)
+
+
+def get_node_rank() -> int:
+    v = _env_int("NODE_RANK")
+    if v is not None:
+        return v
+    return (get_global_rank() - get_local_rank()) // get_local_world_size()
+
+
+def get_world_size() -> int:
+    return dist.get_world_size() if is_distributed() else 1
+
+
+def get_local_world_size() -> int:
+    return _env_int("LOCAL_WORLD_SIZE") or 1
+
+
+def get_global_rank() -> int:
+    if is_distributed():
+        return dist.get_rank()
+    return _env_int("RANK") or 0
+
+
+def get_local_rank() -> int:
+    return _env_int("LOCAL_RANK") or 0
+
+
+def get_fs_local_rank() -> int:
+    """Rank among the processes that share this process's filesystem.
+
+    With ``OLMO_SHARED_FS`` set every rank sees the same files, so this is the global rank and
+    only global rank 0 writes shared artefacts; otherwise it is ``FS_LOCAL_RANK`` or the local rank.
+    """
+    if os.environ.get("OLMO_SHARED_FS"):
+        return int(os.environ.get("FS_LOCAL_RANK") or get_global_rank())
+    return int(os.environ.get("FS_LOCAL_RANK") or get_local_rank())
+
+
+def move_to_device(o: T, device: torch.device) -> T:
+    """Recursively move tensors in dicts / lists / tuples; ``non_blocking`` so pinned sources overlap."""
+    if isinstance(o, torch.Tensor):
+        return o.to(device, non_blocking=True)  # type: ignore[return-value]
+    if isinstance(o, dict):
+        return {k: move_to_device(v, device) for k, v in o.items()}  # type: ignore[return-value]
+    if isinstance(o, list):
+        return [move_to_device(x, device) for x in o]  # type: ignore[return-value]
+    if isinstance(o, tuple):
+        return tuple(move_to_device(x, device) for x in o)  # type: ignore[return-value]
+    return o
+
+
+def ensure_finite_(x: torch.Tensor, check_neg_inf: bool = True, check_pos_inf: bool = False) -> None:
+    """Replace ``-inf`` / ``+inf`` in place by the dtype's finite extremes."""
+    if check_neg_inf:
+        x.masked_fill_(x == float("-inf"), torch.finfo(x.dtype).min)
+    if check_pos_inf:
+        x.masked_fill_(x == float("inf"), torch.finfo(x.dtype).max)
+
+
+def get_default_device() -> torch.device:
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        return torch.device("cuda")
+    return torch.device("cpu")
+
+
+def barrier() -> None:
+    if is_distributed():
+        dist.barrier()
+
+
+def peak_gpu_memory(reset: bool = False) -> Optional[float]:
+    """Peak allocated device memory in MB, maximised over ranks; ``None`` without CUDA."""
+    if not torch.cuda.is_available():
+        return None
+    device = torch.device("cuda")
+    peak_mb = torch.cuda.max_memory_allocated(device) / 1_000_000
+    if is_distributed():
+        t = torch.tensor(peak_mb, device=device)
+        dist.reduce(t, 0, dist.ReduceOp.MAX)
+        peak_mb = t.item()
+    if reset:
+        torch.cuda.reset_max_memory_allocated(device)
+    return peak_mb
+
+
+V = TypeVar("V", bool, int, float)
+
+
+def synchronize_value(value: V, device: torch.device) -> V:
+    """Broadcast rank 0's scalar to every rank."""
+    if is_distributed():
+        t = torch.tensor(value, device=device)
+        dist.broadcast(t, 0)
+        return t.item()  # type: ignore[return-value]
+    return value
+
+
+def synchronize_flag(flag: bool, device: torch.device) -> bool:
+    return synchronize_value(flag, device)
+
+
+def gc_cuda() -> None:
+    gc.collect()
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
+
+
+def get_cumulative_document_lengths(doc_lens: torch.Tensor) -> torch.Tensor:
+    """``(B, max_docs)`` zero-padded document lengths -> int32 ``cu_seqlens`` with a leading 0."""
+    flat = doc_lens.reshape(-1)
+    flat = flat[flat != 0]
+    out = torch.zeros(flat.numel() + 1, dtype=torch.int32, device=doc_lens.device)
+    torch.cumsum(flat, 0, dtype=torch.int32, out=out[1:])
+    return out
+
+
+class SingleAccelerator(torch.nn.Module):
+    """Single-device stand-in for a distributed wrapper: exposes ``.module`` and ``process_group=None``."""
+
+    process_group = None
+
+    def __init__(self, module: torch.nn.Module) -> None:
+        super().__init__()
+        self.module = module
+
+    def forward(self, *args: Any, **kwargs: Any):
+        return self.module(*args, **kwargs)

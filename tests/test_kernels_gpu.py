@@ -1,0 +1,237 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference of the same op."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _seed_and_status():
+    torch.manual_seed(0)
+    yield
+    from olmo_b200 import ops
+
+    ops.check_status()
+
+
+def _rand(*shape, scale=1.0):
+    return (torch.randn(*shape, device="cuda", dtype=torch.float32) * scale).to(torch.bfloat16)
+
+
+def _close(got, want, rtol=2e-2, atol=2e-2):
+    got, want = got.float(), want.float()
+    err = (got - want).abs().max().item()
+    ref = want.abs().max().item()
+    assert torch.allclose(got, want, rtol=rtol, atol=atol * max(ref, 1e-6)), f"max err {err} (ref max {ref})"
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (200, 300, 72), (1024, 1024, 1024), (384, 11008, 4096)])
+def test_gemm_nt(M, N, K):
+    from olmo_b200.ops import kernels as k
+
+    a, b = _rand(M, K), _rand(N, K)
+    _close(k.gemm(a, b), a.float() @ b.float().t())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (200, 264, 328), (512, 4096, 1024)])
+def test_gemm_nn_dgrad(M, N, K):
+    from olmo_b200.ops import kernels as k
+
+    a, b = _rand(M, K), _rand(K, N)  # b is [K, N]: MN-major B operand
+    _close(k.gemm(a, b, b_trans=True), a.float() @ b.float())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (136, 264, 200), (4096, 1024, 2048)])
+def test_gemm_tn_wgrad(M, N, K):
+    from olmo_b200.ops import kernels as k
+
+    a, b = _rand(K, M), _rand(K, N)  # both MN-major
+    want = a.float().t() @ b.float()
+    _close(k.gemm(a, b, a_trans=True, b_trans=True), want)
+    acc = torch.ones(M, N, device="cuda", dtype=torch.float32)
+    k.gemm(a, b, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc)
+    _close(acc, want + 1.0, rtol=1e-2, atol=1e-2)
+    st = k.gemm(a, b, a_trans=True, b_trans=True, epilogue=k.EPI_F32_STORE)
+    _close(st, want, rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_residual_epilogue_and_strided_operands():
+    from olmo_b200.ops import kernels as k
+
+    M, N, K = 256, 512, 256
+    big = _rand(M, 3 * K)
+    a = big[:, K : 2 * K]  # row-strided view
+    b, r = _rand(N, K), _rand(M, N)
+    want = a.float() @ b.float().t() + r.float()
+    _close(k.gemm(a, b, epilogue=k.EPI_BF16_ADD, residual=r), want)
+    out = r.clone()
+    k.gemm(a, b, epilogue=k.EPI_BF16_ADD, residual=out, out=out)  # in place
+    _close(out, want)
+
+
+@pytest.mark.parametrize("rms", [True, False])
+@pytest.mark.parametrize("affine", [True, False])
+def test_norm_fwd_bwd(rms, affine):
+    from olmo_b200.ops import kernels as k
+
+    M, D, eps = 300, 1024, 1e-5
+    x, res, dy = _rand(M, D), _rand(M, D), _rand(M, D)
+    w = (1 + 0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16) if affine else None
+    b = (0.1 * torch.randn(D, device="cuda")).to(torch.bfloat16) if (affine and not rms) else None
+
+    xf = x.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True) if affine else None
+    bf = b.float().requires_grad_(True) if b is not None else None
+    if rms:
+        ref = xf * torch.rsqrt(xf.square().mean(-1, keepdim=True) + eps)
+        if affine:
+            ref = ref * wf
+    else:
+        ref = F.layer_norm(xf, (D,), wf, bf, eps)
+    (ref * dy.float()).sum().backward()
+
+    out, rstd, mean = k.norm_fwd(x, w, b, eps, rms, residual=res)
+    _close(out, ref.detach() + res.float())
+    dw = torch.zeros(D, device="cuda") if affine else None
+    db = torch.zeros(D, device="cuda") if b is not None else None
+    dx = k.norm_bwd(dy, x, w, rstd, mean, rms, dweight=dw, dbias=db)
+    _close(dx, xf.grad)
+    if affine:
+        _close(dw, wf.grad, rtol=3e-2, atol=3e-2)
+    if db is not None:
+        _close(db, bf.grad, rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("do_norm,clip,n_kv", [(True, 0.0, 8), (True, 0.0, 2), (False, 0.5, 8), (False, 0.0, 8)])
+def test_qk_norm_rope(do_norm, clip, n_kv):
+    from olmo_b200.ops import kernels as k
+
+    B, T, H, hd, eps, theta = 2, 96, 8, 64, 1e-6, 500000.0
+    Wq, Wk = H * hd, n_kv * hd
+    M = B * T
+    qkv = _rand(M, Wq + 2 * Wk)
+    wq = (1 + 0.1 * torch.randn(Wq, device="cuda")).to(torch.bfloat16) if do_norm else None
+    wk = (1 + 0.1 * torch.randn(Wk, device="cuda")).to(torch.bfloat16) if do_norm else None
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2, device="cuda", dtype=torch.float) / hd))
+    ang = torch.outer(torch.arange(T, device="cuda", dtype=torch.float), inv)
+    cos, sin = ang.cos().contiguous(), ang.sin().contiguous()
+
+    def reference(qkv_f, wq_f, wk_f):
+        x = qkv_f.clamp(-clip, clip) if clip > 0 else qkv_f
+        q, kk, v = x.split((Wq, Wk, Wk), dim=-1)
+
+        def norm(t, w):
+            if not do_norm:
+                return t
+            return t * torch.rsqrt(t.square().mean(-1, keepdim=True) + eps) * w
+
+        def rope(t, nh):
+            t = t.view(B, T, nh, hd)
+            c = torch.cat((cos, cos), -1)[None, :, None, :]
+            s = torch.cat((sin, sin), -1)[None, :, None, :]
+            a, b_ = t.chunk(2, -1)
+            return (t * c + torch.cat((-b_, a), -1) * s).reshape(M, nh * hd)
+
+        return rope(norm(q, wq_f), H), rope(norm(kk, wk_f), n_kv), v
+
+    qkv_f = qkv.float().requires_grad_(True)
+    wq_f = wq.float().requires_grad_(True) if do_norm else None
+    wk_f = wk.float().requires_grad_(True) if do_norm else None
+    rq, rk, rv = reference(qkv_f, wq_f, wk_f)
+    dq, dk, dv = _rand(M, Wq), _rand(M, Wk), _rand(M, Wk)
+    ((rq * dq.float()).sum() + (rk * dk.float()).sum() + (rv * dv.float()).sum()).backward()
+
+    work = qkv.clone()
+    qk, rstd_q, rstd_k = k.qk_norm_rope_fwd(work, wq, wk, cos, sin, T, Wq, Wk, hd, eps, clip, do_norm, True)
+    _close(qk[:, :Wq], rq.detach())
+    _close(qk[:, Wq:], rk.detach())
+    if clip > 0:
+        _close(work[:, Wq + Wk :], rv.detach())
+    dqkv = torch.cat((dq, dk, dv), dim=-1).contiguous()
+    dwq = torch.zeros(Wq, device="cuda") if do_norm else None
+    dwk = torch.zeros(Wk, device="cuda") if do_norm else None
+    k.qk_norm_rope_bwd(work if clip > 0 else qkv, dqkv, wq, wk, cos, sin, rstd_q, rstd_k, T, Wq, Wk, hd, clip, do_norm, True, dwq, dwk)
+    if clip > 0:
+        # q,k masks come from the pre-clamp values; the forward left those untouched in `work`
+        pass
+    _close(dqkv, qkv_f.grad, rtol=3e-2, atol=3e-2)
+    if do_norm:
+        _close(dwq, wq_f.grad, rtol=3e-2, atol=3e-2)
+        _close(dwk, wk_f.grad, rtol=3e-2, atol=3e-2)
+
+
+def test_swiglu():
+    from olmo_b200.ops import kernels as k
+
+    M, H = 333, 1024
+    h, d = _rand(M, 2 * H), _rand(M, H)
+    hf = h.float().requires_grad_(True)
+    v, g = hf.chunk(2, -1)
+    ref = F.silu(g) * v
+    (ref * d.float()).sum().backward()
+    _close(k.swiglu_fwd(h), ref.detach())
+    _close(k.swiglu_bwd(d, h), hf.grad)
+
+
+def test_embedding():
+    from olmo_b200.ops import kernels as k
+
+    V, D = 1000, 256
+    table = _rand(V, D)
+    ids = torch.randint(0, V, (4, 37), device="cuda")
+    out = k.embedding_fwd(ids, table)
+    assert torch.equal(out, table[ids])
+    d = _rand(4, 37, D)
+    grad = torch.zeros(V, D, device="cuda")
+    k.embedding_bwd(ids, d, grad)
+    ref = torch.zeros(V, D, device="cuda").index_add_(0, ids.reshape(-1), d.reshape(-1, D).float())
+    _close(grad, ref, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("z_mult", [0.0, 1e-4])
+def test_cross_entropy(z_mult):
+    from olmo_b200.ops import kernels as k
+
+    R, V = 70, 100352
+    logits = _rand(R, V, scale=2.0)
+    labels = torch.randint(0, V, (R,), device="cuda")
+    labels[::7] = -100
+    lf = logits.float().requires_grad_(True)
+    ce = F.cross_entropy(lf, labels, ignore_index=-100, reduction="none")
+    z = torch.logsumexp(lf, -1).square() * (labels != -100)
+    scale = 1.0 / 4096
+    ((ce.sum() + z_mult * z.sum()) * scale).backward()
+    work = logits.clone()
+    got_ce, got_z = k.cross_entropy_(work, labels, -100, z_mult, scale, True)
+    _close(got_ce, ce.detach(), rtol=1e-2, atol=1e-3)
+    _close(got_z, z.detach(), rtol=1e-2, atol=1e-3)
+    got, want = work.float(), lf.grad
+    assert (got - want).abs().max().item() <= 2e-2 * want.abs().max().item() + 1e-7
+
+
+def test_adamw_and_sumsq():
+    from olmo_b200.ops import kernels as k
+
+    n = 100_003
+    p = torch.randn(n, device="cuda")
+    g = torch.randn(n, device="cuda")
+    ref_p = torch.nn.Parameter(p.clone())
+    opt = torch.optim.AdamW([ref_p], lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    m, v = torch.zeros(n, device="cuda"), torch.zeros(n, device="cuda")
+    lowp = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    seg_end = torch.tensor([n], device="cuda", dtype=torch.int64)
+    seg_wd = torch.tensor([0.1], device="cuda")
+    seg_lr = torch.tensor([3e-4], device="cuda")
+    scale = torch.tensor([0.5], device="cuda")
+    for step in range(1, 4):
+        ref_p.grad = g * 0.5
+        opt.step()
+        k.adamw_flat(p, g, m, v, lowp, seg_end, seg_wd, seg_lr, 0.9, 0.95, 1e-8, step, scale)
+    assert torch.allclose(p, ref_p.detach(), rtol=1e-5, atol=1e-6)
+    assert torch.allclose(lowp.float(), p, rtol=1e-2, atol=1e-3)
+    out = torch.zeros(1, device="cuda")
+    k.sumsq(g, out)
+    assert math.isclose(out.item(), g.double().square().sum().item(), rel_tol=1e-4)
