@@ -1,0 +1,286 @@
+#!/usr/bin/env python
+"""
+Headline benchmark: OLMo-2 training throughput (tokens/s over the whole job, plus per-GPU and MFU) on N B200s of
+one node, synthetic seeded token data, random-init weights, bf16 compute with fp32 master weights and reduction.
+
+    python bench.py --gpus 1 --steps 2 --warmup 3
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 --master-port 29500 \
+        bench.py --gpus 8 --steps 2 --warmup 3
+    python bench.py --impl reference ...        # the unmodified reference (baseline/_ref) on the same config
+
+Per GPU the work is fixed (weak scaling): ``--device-batch`` sequences of ``seq_len`` tokens per optimizer step, split
+into micro-batches of the model's official size, so the global batch is ``N × device_batch`` (1024 sequences at 8 GPUs
+for the 7B preset, as in the official config).
+
+Two measurements are reported: ``value`` times K optimizer steps with CUDA events while the token batches already sit
+on the device; ``e2e`` times K further steps by wall clock through ``Trainer.train_step`` with every step's batch
+copied from pinned host memory and its loss read back.  Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+PRESETS = {
+    # name: (d_model, n_layers, n_heads, ff_proj width, micro-batch per GPU, official global batch, flavour)
+    "olmo2-7b": dict(d_model=4096, n_layers=32, n_heads=32, mlp_hidden_size=22016, microbatch=2, global_batch=1024, flavour="olmo2"),
+    "olmo2-1b": dict(d_model=2048, n_layers=16, n_heads=16, mlp_hidden_size=16384, microbatch=8, global_batch=512, flavour="olmo2"),
+    "olmo2-13b": dict(d_model=5120, n_layers=40, n_heads=40, mlp_hidden_size=27648, microbatch=1, global_batch=1024, flavour="olmo2"),
+    "olmo1-7b": dict(d_model=4096, n_layers=32, n_heads=32, mlp_hidden_size=22016, microbatch=2, global_batch=1024, flavour="olmo1"),
+    "tiny": dict(d_model=256, n_layers=4, n_heads=2, mlp_hidden_size=2048, microbatch=2, global_batch=16, flavour="olmo2"),
+}
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--model", choices=sorted(PRESETS), default="olmo2-7b")
+    p.add_argument("--seq-len", type=int, default=4096)
+    p.add_argument("--device-batch", type=int, default=None, help="sequences per GPU per optimizer step (default: official global batch / 8)")
+    p.add_argument("--activation-checkpointing", default=None)
+    p.add_argument("--no-e2e", action="store_true")
+    return p.parse_args()
+
+
+def make_train_config(args, world: int):
+    from olmo_b200.config import (
+        ActivationCheckpointingStrategy, DistributedStrategy, FSDPConfig, FSDPPrecision, FSDPWrapStrategy, InitFnType,
+        LayerNormType, ModelConfig, OptimizerConfig, OptimizerType, SchedulerConfig, SchedulerType, SchedulerUnits,
+        ShardingStrategy, SpeedMonitorConfig, TrainConfig,
+    )
+
+    ps = PRESETS[args.model]
+    olmo2 = ps["flavour"] == "olmo2"
+    model = ModelConfig(
+        d_model=ps["d_model"], n_heads=ps["n_heads"], n_layers=ps["n_layers"], mlp_hidden_size=ps["mlp_hidden_size"],
+        weight_tying=False, alibi=False, rope=True, rope_theta=500000 if olmo2 else 10000, flash_attention=True,
+        attention_dropout=0.0, include_bias=False, layer_norm_type=LayerNormType.rms if olmo2 else LayerNormType.default,
+        layer_norm_with_affine=olmo2, layer_norm_eps=1e-6 if olmo2 else 1e-5, bias_for_layer_norm=False,
+        attention_layer_norm=olmo2, attention_layer_norm_with_affine=olmo2, norm_after=olmo2, residual_dropout=0.0,
+        embedding_dropout=0.0, max_sequence_length=args.seq_len, vocab_size=100278 if olmo2 else 50280,
+        embedding_size=100352 if olmo2 else 50304, eos_token_id=100257 if olmo2 else 50279, pad_token_id=100277 if olmo2 else 1,
+        init_device="meta", init_fn=InitFnType.normal if olmo2 else InitFnType.mitchell, init_std=0.02,
+        init_cutoff_factor=3 if olmo2 else None, clip_qkv=None if olmo2 else 8.0,
+    )
+    device_batch = args.device_batch or max(ps["microbatch"], ps["global_batch"] // 8)
+    cfg = TrainConfig(
+        run_name=f"bench-{args.model}", model=model,
+        optimizer=OptimizerConfig(name=OptimizerType.adamw, learning_rate=3e-4, weight_decay=0.1, eps=1e-8, betas=(0.9, 0.95),
+                                  decay_norm_and_bias=True, decay_embeddings=False),
+        scheduler=SchedulerConfig(name=SchedulerType.cosine_with_warmup, units=SchedulerUnits.tokens, t_warmup=8388608000, t_max=5e12,
+                                  alpha_f=0.1, warmup_min_lr=0.0),
+        global_train_batch_size=device_batch * world, device_train_microbatch_size=ps["microbatch"], precision="amp_bf16",
+        distributed_strategy=DistributedStrategy.fsdp,
+        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy.FULL_SHARD, wrapping_strategy=FSDPWrapStrategy.by_block_and_size,
+                        precision=FSDPPrecision.mixed),
+        max_grad_norm=1.0, softmax_auxiliary_loss=True, auxiliary_loss_multiplier=1e-5, fused_loss=True,
+        save_folder=tempfile.mkdtemp(prefix="olmo_b200_bench_"), save_overwrite=True, save_data_indices=False,
+        max_duration=10**9, console_log_interval=10**9, speed_monitor=SpeedMonitorConfig(window_size=1),
+        activation_checkpointing=None if args.activation_checkpointing in (None, "none") else ActivationCheckpointingStrategy(args.activation_checkpointing),
+    )
+    return cfg, device_batch
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons of one GPU with nvidia-smi while the timed region runs."""
+
+    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+
+    def __init__(self, index: int):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self) -> None:
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            pass
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[3:7]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_ours(args) -> dict:
+    import torch
+    import torch.distributed as dist
+
+    from olmo_b200 import ops
+    from olmo_b200.data import SyntheticTokenDataset
+    from olmo_b200.launch import build_trainer, derive_batch_sizes
+    from olmo_b200.ops import kernels
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
+
+    cfg, device_batch = make_train_config(args, world)
+    derive_batch_sizes(cfg, world)
+    ps = PRESETS[args.model]
+    trainer = build_trainer(cfg, device=device, train_loader=_dummy_loader(), with_evaluators=False)
+    engine = trainer.dist_model.engine
+    model = trainer.model
+    flops_per_token = model.num_fwd_flops + model.num_bck_flops
+    n_params = model.num_params()
+
+    data = SyntheticTokenDataset(1 << 20, args.seq_len, cfg.model.vocab_size, cfg.model.eos_token_id, seed=cfg.seed)
+    total_steps = args.warmup + 2 * args.steps + 1
+    host_batches = [data.batch((s * world + rank) * device_batch, device_batch, pin=True) for s in range(min(total_steps, 4))]
+
+    def step(i: int, from_host: bool) -> float:
+        ids = host_batches[i % len(host_batches)]
+        batch = {"input_ids": ids if from_host else dev_batches[i % len(dev_batches)]}
+        trainer.global_step += 1
+        trainer.global_train_tokens_seen += device_batch * world * args.seq_len
+        return trainer.train_step(batch, reduce_global_loss=False)["train/CrossEntropyLoss"]
+
+    dev_batches = [b.to(device) for b in host_batches]
+    torch.cuda.synchronize()
+    loss = float("nan")
+    for i in range(args.warmup):
+        loss = step(i, False)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---- device-timed region
+    sampler = ClockSampler(local_rank)
+    barrier()
+    sampler.start()
+    launches0 = kernels.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for i in range(args.steps):
+        loss = step(args.warmup + i, False)
+    ev1.record()
+    barrier()
+    clocks = sampler.stop()
+    launches = kernels.launch_count() - launches0
+    ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_per_step = t.item() / args.steps
+
+    # ---- end-to-end region (pinned host batch -> device every step, loss read back every step)
+    e2e = None
+    if not args.no_e2e:
+        barrier()
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            loss = step(args.warmup + args.steps + i, True)
+        barrier()
+        wall = torch.tensor([time.perf_counter() - t0], device=device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(wall, op=dist.ReduceOp.MAX)
+        e2e_tokens = device_batch * world * args.seq_len * args.steps
+        e2e = {
+            "value": e2e_tokens / wall.item(), "unit": "tokens/s",
+            "h2d_bytes_per_step": device_batch * args.seq_len * 8, "d2h_bytes_per_step": 16,
+            "ms_per_step": wall.item() * 1e3 / args.steps,
+        }
+
+    tokens_per_step = device_batch * world * args.seq_len
+    value = tokens_per_step / (ms_per_step / 1e3)
+    peaks = {}
+    try:
+        peaks = json.loads((REPO / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    per_gpu = value / world
+    result = {
+        "metric": "tokens_per_second (OLMo-2 training, whole job; FSDP FULL_SHARD, device-timed, max over ranks)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic seeded uniform tokens with EOS boundaries; random-init weights",
+        "impl": "ours",
+        "tokens_per_second_per_gpu": per_gpu,
+        "mfu_nominal_2250tf": per_gpu * flops_per_token / 2.25e15,
+        "mfu_of_measured_sustained": (per_gpu * flops_per_token / (peaks["bf16_tflops_sustained"] * 1e12)) if peaks.get("bf16_tflops_sustained") else None,
+        "flops_per_token": flops_per_token, "params": n_params, "final_loss": loss,
+        "config": {
+            "model": args.model, "global_batch": device_batch * world, "seq_len": args.seq_len,
+            "micro_batch": ps["microbatch"], "grad_accum": cfg.device_train_grad_accum,
+            "parallelism": f"fsdp{world}" if world > 1 else "single-gpu flat-shard engine",
+            "activation_checkpointing": args.activation_checkpointing or "none",
+            "optimizer": "adamw fp32 master, clip 1.0, z-loss on", "fused_path": bool(engine.fused),
+            "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
+        },
+        "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
+        "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
+    }
+    if world > 1:
+        dist.destroy_process_group()
+    return result if rank == 0 else {}
+
+
+def _dummy_loader():
+    from torch.utils.data import DataLoader
+
+    from olmo_b200.data import IterableDataset
+
+    return DataLoader(IterableDataset([[0]], 1, world_size=1, rank=0, fs_local_rank=0, num_threads=0), batch_size=1)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        from baseline.ref_bench import run_reference
+
+        out = run_reference(args, PRESETS)
+    else:
+        out = run_ours(args)
+    if out:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,573 @@
+"""
+Checkpointing (reference: ``olmo/checkpoint.py:99-2030``).
+
+Two on-disk layouts:
+
+*Unsharded* (``step{N}-unsharded/``) — byte-compatible with the reference: ``config.yaml``, ``model.pt``
+(``{FQN: fp32 tensor}``), ``optim.pt`` (``{"state": {FQN: {...}}, "param_groups": [...]}``), ``train.pt``.  A sibling
+``*.safetensors`` file is preferred on load.
+
+*Sharded* (``step{N}/``) — this framework's flat-shard format.  Every rank writes the raw contents of its shards,
+
+    model/rank{r}.pt   {"units": {unit name: fp32 master shard}}
+    optim/rank{r}.pt   {"units": {unit name: {"exp_avg": shard, ...}}, "steps": {...}, "param_groups": [...]}
+    train/rank{r}.pt   trainer state
+    metadata.yaml      world/shard sizes and, per unit, the (FQN, shape, offset) table
+
+so saving is one sequential write per rank with no gather, and restoring at the same world size is one read.  A
+different world size, and :meth:`FlatShardCheckpointer.unshard_checkpoint`, reassemble full tensors from the shard
+files through the metadata table.  All four ``sharded_checkpointer`` names of the reference select this format.
+
+Writes go to ``{dir}-tmp`` and are renamed into place after a barrier, so an interrupted save never leaves a
+directory that looks complete; ``config.yaml`` is written and uploaded last for the same reason.
+"""
+from __future__ import annotations
+
+import io
+import logging
+import pickle
+import shutil
+from abc import ABCMeta, abstractmethod
+from concurrent.futures import ThreadPoolExecutor
+from contextlib import contextmanager
+from copy import deepcopy
+from pathlib import Path
+from typing import Any, Dict, Generator, List, Optional, Set, Tuple
+
+import torch
+import torch.nn as nn
+import yaml
+
+from .aliases import PathOrStr
+from .config import ShardedCheckpointerType, TrainConfig
+from .exceptions import OLMoCheckpointError
+from .optim import Optimizer, fix_optim_state_dict
+from .safetensors_util import safetensors_file_to_state_dict
+from .torch_util import barrier, get_fs_local_rank, get_global_rank, get_world_size
+from .util import default_thread_count, dir_is_empty, is_url, resource_path, upload, wait_for
+
+__all__ = [
+    "save_state_dict", "load_state_dict", "load_model_state", "Checkpointer", "FullCheckpointer",
+    "FlatShardCheckpointer", "TorchNewStyleShardedCheckpointer", "TorchLegacyShardedCheckpointer",
+    "LocalShardedCheckpointer", "OlmoCoreCheckpointer", "build_sharded_checkpointer",
+]
+
+log = logging.getLogger(__name__)
+
+MODEL_AND_OPTIM_FOLDER = "model_and_optim"
+
+
+# ------------------------------------------------------------------------------------- file helpers
+
+
+def save_state_dict(
+    checkpoint_dir: PathOrStr, fname: str, state_dict: Dict[str, Any], *, upload_to: Optional[str] = None,
+    save_overwrite: bool = False, synchronize: bool = True,
+) -> None:
+    """``torch.save`` to ``checkpoint_dir/fname`` (sub-folders allowed), then optionally upload it."""
+    target = Path(checkpoint_dir) / fname
+    if save_overwrite:
+        target.unlink(missing_ok=True)
+    elif target.is_file():
+        raise FileExistsError(target)
+    if synchronize:
+        barrier()
+    target.parent.mkdir(exist_ok=True, parents=True)
+    if synchronize:
+        barrier()
+    torch.save(state_dict, target)
+    if upload_to is not None:
+        dest = f"{upload_to.rstrip('/')}/{fname}"
+        log.info("Uploading %s to %s...", target, dest)
+        upload(target, dest, save_overwrite=save_overwrite)
+
+
+def load_state_dict(checkpoint_dir: PathOrStr, fname: str, *, local_cache: Optional[PathOrStr] = None, map_location: Optional[str] = None):
+    """Load ``fname`` from a local or remote checkpoint folder, preferring a ``.safetensors`` sibling."""
+    if fname.endswith(".pt"):
+        try:
+            path = resource_path(str(checkpoint_dir).rstrip("/"), fname[:-3] + ".safetensors", local_cache=local_cache)
+            return safetensors_file_to_state_dict(path, map_location=map_location)
+        except FileNotFoundError:
+            pass
+    path = resource_path(str(checkpoint_dir).rstrip("/"), fname, local_cache=local_cache)
+    return torch.load(path, map_location=map_location, weights_only=False)
+
+
+def _engine_of(dist_model: nn.Module):
+    return getattr(dist_model, "engine", None)
+
+
+def _plain_module(dist_model: nn.Module) -> nn.Module:
+    return getattr(dist_model, "module", dist_model)
+
+
+def _clean_param_groups(optim: Optimizer) -> List[Dict[str, Any]]:
+    groups = []
+    for g in optim.state_dict()["param_groups"]:
+        g = dict(g)
+        g["params"] = list(g["param_names"])
+        groups.append(g)
+    return groups
+
+
+def load_model_state(checkpoint_dir: PathOrStr, model: nn.Module) -> None:
+    """Load only the weights of a sharded checkpoint into an unwrapped model."""
+    state, _, _ = FlatShardCheckpointer(TrainConfig()).unshard_checkpoint(checkpoint_dir, load_optimizer_state=False, load_trainer_state=False)
+    model.load_state_dict(model._make_state_dict_compatible(state)[0] if hasattr(model, "_make_state_dict_compatible") else state)
+
+
+# ------------------------------------------------------------------------------------- base class
+
+
+class Checkpointer(metaclass=ABCMeta):
+    def __init__(self, cfg: TrainConfig, thread_count: Optional[int] = None):
+        self.cfg = cfg
+        self.thread_count = thread_count or default_thread_count()
+
+    @abstractmethod
+    def save_checkpoint(self, dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, train_state: Dict[str, Any], *, upload_to: Optional[str] = None) -> None:
+        raise NotImplementedError
+
+    @abstractmethod
+    def restore_checkpoint(
+        self, load_path: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+        load_optimizer_state: bool = True,
+    ) -> Dict[str, Any]:
+        """Restore model (and optimizer) in place; return the trainer state."""
+        raise NotImplementedError
+
+    def unshard_checkpoint(
+        self, load_path: PathOrStr, *, local_cache: Optional[PathOrStr] = None, load_optimizer_state: bool = True,
+        load_trainer_state: bool = True, device: Optional[torch.device] = None,
+    ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
+        raise NotImplementedError
+
+    @contextmanager
+    def _temporary_wd(self, dir: PathOrStr) -> Generator[Path, None, None]:
+        """Yield ``{dir}-tmp``; on normal exit rename it to ``dir``.  Filesystem-local rank 0 creates and renames,
+        everyone waits until the result is visible (shared filesystems can lag)."""
+        final = Path(dir)
+        if not dir_is_empty(final):
+            if not self.cfg.save_overwrite:
+                raise FileExistsError(final)
+            if get_fs_local_rank() == 0:
+                shutil.rmtree(final, ignore_errors=True)
+        barrier()
+        tmp = final.with_name(final.name + "-tmp")
+        if get_fs_local_rank() == 0:
+            shutil.rmtree(tmp, ignore_errors=True)
+            tmp.mkdir(exist_ok=True, parents=True)
+        wait_for(lambda: tmp.exists(), "Waiting for checkpoint directory", timeout=10.0)
+        barrier()
+        yield tmp
+        barrier()
+        if get_fs_local_rank() == 0:
+            try:
+                tmp.replace(final)
+            except FileNotFoundError:
+                if not final.exists():  # another filesystem-local rank 0 on a shared disk already renamed it
+                    raise
+        wait_for(lambda: final.exists(), "Waiting for checkpoint directory", timeout=10.0)
+        barrier()
+
+    def _save_config(self, dir: PathOrStr, *, upload_to: Optional[str] = None) -> None:
+        if get_global_rank() == 0:
+            log.info("Saving config...")
+            path = Path(dir) / "config.yaml"
+            self.cfg.save(path)
+            if upload_to is not None:
+                upload(path, f"{upload_to}/config.yaml", save_overwrite=self.cfg.save_overwrite)
+
+
+# ---------------------------------------------------------------------------------- unsharded format
+
+
+def _optim_state_by_name(optim: Optimizer) -> Dict[str, Dict[str, Any]]:
+    out = {}
+    for group in optim.param_groups:
+        for name, p in zip(group["param_names"], group["params"]):
+            out[name] = optim.state.get(p, {})
+    return out
+
+
+class FullCheckpointer(Checkpointer):
+    """Whole tensors gathered to rank 0 (``model.pt``, ``optim.pt``, ``train.pt``, ``config.yaml``)."""
+
+    # -- gather
+    def _full_model_state(self, dist_model: nn.Module) -> Dict[str, torch.Tensor]:
+        engine = _engine_of(dist_model)
+        if engine is not None:
+            return engine.full_model_state_dict(rank0_only=True, cpu=True)
+        return {k: v.detach().float().cpu() for k, v in _plain_module(dist_model).state_dict().items()}
+
+    def _full_optim_state(self, dist_model: nn.Module, optim: Optimizer) -> Dict[str, Any]:
+        engine = _engine_of(dist_model)
+        by_name = _optim_state_by_name(optim)
+        state: Dict[str, Dict[str, Any]] = {}
+        if engine is None or not engine.is_sharded:
+            for name, st in by_name.items():
+                if st:
+                    state[name] = {k: (v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v) for k, v in st.items()}
+        else:
+            keep = get_global_rank() == 0
+            tensor_keys = sorted({k for st in by_name.values() for k, v in st.items() if isinstance(v, torch.Tensor) and v.dim() > 0})
+            for unit in engine.units:
+                lo = engine.shard_rank * unit.shard_size
+                for key in tensor_keys:
+                    shard = torch.zeros(unit.shard_size, dtype=torch.float32, device=engine.device)
+                    for s in unit.slots:
+                        st = by_name.get(s.name, {})
+                        if key in st and st[key].numel() > 0:
+                            a = max(s.offset, lo) - lo
+                            shard[a : a + st[key].numel()].copy_(st[key].reshape(-1))
+                    full = engine.full_tensor(unit, shard)
+                    if keep:
+                        for s in unit.slots:
+                            if any(key in by_name.get(s.name, {}) for _ in (0,)) or True:
+                                state.setdefault(s.name, {})[key] = full[s.offset : s.offset + s.numel].view(s.shape).cpu().clone()
+                    del full, shard
+            if keep:
+                for name, st in by_name.items():
+                    for k, v in st.items():
+                        if not (isinstance(v, torch.Tensor) and v.dim() > 0):
+                            state.setdefault(name, {})[k] = v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v
+                # drop entries of parameters that never received state on any rank
+                state = {n: s for n, s in state.items() if "step" in s or not tensor_keys}
+        return {"state": state, "param_groups": _clean_param_groups(optim)}
+
+    def save_checkpoint(self, dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, trainer_state: Dict[str, Any], *, upload_to: Optional[str] = None) -> None:
+        with self._temporary_wd(dir) as tmp:
+            model_state = self._full_model_state(dist_model)
+            if get_global_rank() == 0:
+                log.info("Saving model state...")
+                save_state_dict(tmp, "model.pt", model_state, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False)
+            del model_state
+            barrier()
+            optim_state = self._full_optim_state(dist_model, optim)
+            if get_global_rank() == 0:
+                log.info("Saving optim state...")
+                save_state_dict(tmp, "optim.pt", optim_state, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False)
+                log.info("Saving trainer state...")
+                save_state_dict(tmp, "train.pt", trainer_state, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False)
+            del optim_state
+            barrier()
+            self._save_config(tmp, upload_to=upload_to)
+
+    # -- restore
+    @staticmethod
+    def _normalise_optim_state(optim_state: Dict[str, Any], renames: Dict[str, Set[str]]) -> Dict[str, Any]:
+        """Key the optimizer state by clean FQN (it may arrive keyed by integer ids) and follow model-key renames."""
+        groups = optim_state["param_groups"]
+        if groups and groups[0]["params"] and isinstance(groups[0]["params"][0], int):
+            id_to_name = {}
+            for g in groups:
+                names = [n.replace("_fsdp_wrapped_module.", "") for n in g["param_names"]]
+                id_to_name.update(dict(zip(g["params"], names)))
+                g["param_names"] = g["params"] = names
+            optim_state["state"] = {id_to_name[i]: s for i, s in optim_state["state"].items()}
+        else:
+            for g in groups:
+                g["param_names"] = g["params"] = [n.replace("_fsdp_wrapped_module.", "") for n in g["param_names"]]
+            optim_state["state"] = {k.replace("_fsdp_wrapped_module.", ""): s for k, s in optim_state["state"].items()}
+        for old, news in renames.items():
+            if old in news and len(news) == 1:
+                continue
+            st = optim_state["state"].pop(old, None)
+            if st is not None:
+                for i, new in enumerate(sorted(news)):
+                    optim_state["state"][new] = st if i == 0 else deepcopy(st)
+        for g in groups:
+            g["params"] = g["param_names"] = [new for old in g["params"] for new in sorted(renames.get(old, {old}))]
+        return optim_state
+
+    @staticmethod
+    def load_optim_state_into(dist_model: nn.Module, optim: Optimizer, optim_state: Dict[str, Any]) -> None:
+        """Scatter a full, FQN-keyed optimizer state into the live optimizer (each rank keeps its shard ranges)."""
+        engine = _engine_of(dist_model)
+        ranges = engine.param_shard_ranges() if engine is not None else {}
+        optim_state = fix_optim_state_dict(optim, optim_state)
+        for group, saved in zip(optim.param_groups, optim_state["param_groups"]):
+            for k, v in saved.items():
+                if k not in ("params", "param_names"):
+                    group[k] = v
+        for group in optim.param_groups:
+            for name, p in zip(group["param_names"], group["params"]):
+                saved = optim_state["state"].get(name)
+                if not saved:
+                    continue
+                st = optim.state[p]
+                for key, value in saved.items():
+                    if isinstance(value, torch.Tensor) and value.dim() > 0:
+                        a, b, _ = ranges.get(name, (0, value.numel(), value.numel()))
+                        piece = value.reshape(-1)[a:b].to(p.device, torch.float32).view(p.shape)
+                        if key in st and isinstance(st[key], torch.Tensor) and st[key].shape == piece.shape:
+                            st[key].copy_(piece)
+                        else:
+                            st[key] = piece.clone()
+                    else:
+                        st[key] = value.clone().float().cpu() if isinstance(value, torch.Tensor) else value
+
+    def restore_checkpoint(
+        self, load_path: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+        load_optimizer_state: bool = True,
+    ) -> Dict[str, Any]:
+        module = _plain_module(dist_model)
+        engine = _engine_of(dist_model)
+        model_state = load_state_dict(load_path, "model.pt", local_cache=local_cache, map_location="cpu")
+        renames: Dict[str, Set[str]] = {}
+        if hasattr(module, "_make_state_dict_compatible"):
+            model_state, renames = module._make_state_dict_compatible(model_state)
+        if engine is not None:
+            engine.load_full_model_state_dict(model_state)
+        else:
+            module.load_state_dict(model_state)
+        del model_state
+        if load_optimizer_state:
+            optim_state = load_state_dict(load_path, "optim.pt", local_cache=local_cache, map_location="cpu")
+            optim_state = self._normalise_optim_state(optim_state, renames)
+            self.load_optim_state_into(dist_model, optim, optim_state)
+            del optim_state
+        try:
+            trainer_state = load_state_dict(load_path, "train.pt", local_cache=local_cache)
+        except FileNotFoundError:
+            trainer_state = load_state_dict(load_path, "other.pt", local_cache=local_cache)  # pre-0.3 name
+        barrier()
+        return trainer_state
+
+    def load_checkpoint(
+        self, load_path: PathOrStr, *, local_cache: Optional[PathOrStr] = None, load_optimizer_state: bool = True,
+        device: Optional[torch.device] = None,
+    ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]]]:
+        dev = str(device) if device is not None else "cpu"
+        model_state = load_state_dict(load_path, "model.pt", local_cache=local_cache, map_location=dev)
+        optim_state = load_state_dict(load_path, "optim.pt", local_cache=local_cache, map_location=dev) if load_optimizer_state else None
+        return model_state, optim_state
+
+
+# ------------------------------------------------------------------------------------ sharded format
+
+
+class FlatShardCheckpointer(Checkpointer):
+    """Per-rank raw shard files plus a layout table (see the module docstring)."""
+
+    format_name = "flat_shard_v1"
+
+    def _layout(self, engine) -> Dict[str, Any]:
+        return {
+            "format": self.format_name,
+            "world_size": get_world_size(),
+            "shard_world": engine.shard_world,
+            "num_replicas": engine.num_replicas,
+            "units": [
+                {
+                    "name": u.name, "numel": u.numel, "shard_size": u.shard_size,
+                    "params": [{"name": s.name, "shape": list(s.shape), "offset": s.offset} for s in u.slots],
+                }
+                for u in engine.units
+            ],
+        }
+
+    def save_checkpoint(self, dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, trainer_state: Dict[str, Any], *, upload_to: Optional[str] = None) -> None:
+        engine = _engine_of(dist_model)
+        if engine is None:
+            raise OLMoCheckpointError("sharded checkpoints need a flat-shard engine; use an unsharded checkpoint instead")
+        rank = get_global_rank()
+        with self._temporary_wd(dir) as tmp:
+            # replicas hold identical shards; only the first replica writes model/optim files
+            writes_shards = rank < engine.shard_world
+            if writes_shards:
+                save_state_dict(
+                    tmp, f"model/rank{engine.shard_rank}.pt", {"units": {u.name: u.master.detach().cpu() for u in engine.units}},
+                    upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False,
+                )
+                by_name = _optim_state_by_name(optim)
+                units_state: Dict[str, Dict[str, torch.Tensor]] = {}
+                scalars: Dict[str, Dict[str, Any]] = {}
+                for u in engine.units:
+                    lo = engine.shard_rank * u.shard_size
+                    per_key: Dict[str, torch.Tensor] = {}
+                    for s in u.slots:
+                        for key, value in by_name.get(s.name, {}).items():
+                            if isinstance(value, torch.Tensor) and value.dim() > 0:
+                                buf = per_key.setdefault(key, torch.zeros(u.shard_size, dtype=torch.float32))
+                                a = max(s.offset, lo) - lo
+                                buf[a : a + value.numel()].copy_(value.reshape(-1))
+                            else:
+                                scalars.setdefault(s.name, {})[key] = value.detach().cpu() if isinstance(value, torch.Tensor) else value
+                    units_state[u.name] = per_key
+                save_state_dict(
+                    tmp, f"optim/rank{engine.shard_rank}.pt",
+                    {"units": units_state, "scalars": scalars, "param_groups": _clean_param_groups(optim)},
+                    upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False,
+                )
+            save_state_dict(tmp, f"train/rank{rank}.pt", trainer_state, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite, synchronize=False)
+            if rank == 0:
+                meta = tmp / "metadata.yaml"
+                meta.write_text(yaml.safe_dump(self._layout(engine), sort_keys=False))
+                if upload_to is not None:
+                    upload(meta, f"{upload_to}/metadata.yaml", save_overwrite=self.cfg.save_overwrite)
+            barrier()
+            self._save_config(tmp, upload_to=upload_to)
+
+    @staticmethod
+    def _read_meta(load_path: PathOrStr, local_cache: Optional[PathOrStr]) -> Dict[str, Any]:
+        meta = yaml.safe_load(resource_path(str(load_path).rstrip("/"), "metadata.yaml", local_cache=local_cache).read_text())
+        if meta.get("format") != FlatShardCheckpointer.format_name:
+            raise OLMoCheckpointError(f"{load_path} is not a flat-shard checkpoint (format={meta.get('format')})")
+        return meta
+
+    def restore_checkpoint(
+        self, load_path: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+        load_optimizer_state: bool = True,
+    ) -> Dict[str, Any]:
+        engine = _engine_of(dist_model)
+        if engine is None:
+            raise OLMoCheckpointError("restoring a sharded checkpoint needs a flat-shard engine")
+        meta = self._read_meta(load_path, local_cache)
+        same_layout = meta["shard_world"] == engine.shard_world and [u["numel"] for u in meta["units"]] == [u.numel for u in engine.units]
+        if same_layout:
+            shard = load_state_dict(load_path, f"model/rank{engine.shard_rank}.pt", local_cache=local_cache, map_location="cpu")
+            for u in engine.units:
+                src = shard["units"][u.name]
+                if not torch.isfinite(src).all():
+                    raise OLMoCheckpointError(f"non-finite values in shard of unit {u.name}")
+                u.master.copy_(src)
+                u.lowp.copy_(src) if u.lowp.data_ptr() != u.master.data_ptr() else None
+            engine._params_stale = True
+            if not engine.is_sharded:
+                for u in engine.units:
+                    if u.full.data_ptr() != u.master.data_ptr():
+                        u.full.copy_(u.master)
+                engine._params_stale = False
+            if load_optimizer_state:
+                saved = load_state_dict(load_path, f"optim/rank{engine.shard_rank}.pt", local_cache=local_cache, map_location="cpu")
+                self._load_optim_shards(engine, optim, saved)
+        else:
+            log.info("Checkpoint layout differs from the running job (saved shard world %d); resharding", meta["shard_world"])
+            model_state, optim_state, _ = self.unshard_checkpoint(load_path, local_cache=local_cache, load_optimizer_state=load_optimizer_state, load_trainer_state=False)
+            engine.load_full_model_state_dict(model_state)
+            if load_optimizer_state and optim_state is not None:
+                FullCheckpointer.load_optim_state_into(dist_model, optim, optim_state)
+        rank = get_global_rank()
+        try:
+            trainer_state = load_state_dict(load_path, f"train/rank{rank}.pt", local_cache=local_cache)
+        except FileNotFoundError:
+            trainer_state = load_state_dict(load_path, "train/rank0.pt", local_cache=local_cache)  # world size changed
+        barrier()
+        return trainer_state
+
+    @staticmethod
+    def _load_optim_shards(engine, optim: Optimizer, saved: Dict[str, Any]) -> None:
+        saved = fix_optim_state_dict(optim, saved)
+        for group, sg in zip(optim.param_groups, saved["param_groups"]):
+            for k, v in sg.items():
+                if k not in ("params", "param_names"):
+                    group[k] = v
+        by_name = {name: p for g in optim.param_groups for name, p in zip(g["param_names"], g["params"])}
+        for u in engine.units:
+            lo = engine.shard_rank * u.shard_size
+            for key, buf in saved["units"].get(u.name, {}).items():
+                for s in u.slots:
+                    p = by_name.get(s.name)
+                    if p is None or p.numel() == 0:
+                        continue
+                    a = max(s.offset, lo) - lo
+                    piece = buf[a : a + p.numel()].to(p.device).view(p.shape)
+                    st = optim.state[p]
+                    if key in st and isinstance(st[key], torch.Tensor) and st[key].shape == piece.shape:
+                        st[key].copy_(piece)
+                    else:
+                        st[key] = piece.clone()
+        for name, sc in saved.get("scalars", {}).items():
+            p = by_name.get(name)
+            if p is not None:
+                for k, v in sc.items():
+                    optim.state[p][k] = v.clone() if isinstance(v, torch.Tensor) else v
+
+    def unshard_checkpoint(
+        self, load_path: PathOrStr, *, local_cache: Optional[PathOrStr] = None, load_optimizer_state: bool = True,
+        load_trainer_state: bool = True, device: Optional[torch.device] = None,
+    ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
+        """Reassemble full tensors offline (no process group needed): shard files are read by a thread pool, full
+        buffers start as NaN and are verified finite after the copy so a missing shard cannot go unnoticed."""
+        meta = self._read_meta(load_path, local_cache)
+        sw = meta["shard_world"]
+        dev = "cpu" if device is None else str(device)
+
+        def read(kind: str, r: int):
+            return load_state_dict(load_path, f"{kind}/rank{r}.pt", local_cache=local_cache, map_location="cpu")
+
+        with ThreadPoolExecutor(max_workers=self.thread_count) as pool:
+            model_shards = list(pool.map(lambda r: read("model", r), range(sw)))
+            optim_shards = list(pool.map(lambda r: read("optim", r), range(sw))) if load_optimizer_state else None
+
+        def assemble(per_rank: List[torch.Tensor], unit: Dict[str, Any]) -> torch.Tensor:
+            full = torch.full((unit["numel"],), float("nan"), dtype=torch.float32)
+            for r, piece in enumerate(per_rank):
+                full[r * unit["shard_size"] : (r + 1) * unit["shard_size"]].copy_(piece)
+            return full
+
+        model_state: Dict[str, torch.Tensor] = {}
+        for unit in meta["units"]:
+            full = assemble([ms["units"][unit["name"]] for ms in model_shards], unit)
+            for p in unit["params"]:
+                n = 1
+                for d in p["shape"]:
+                    n *= d
+                t = full[p["offset"] : p["offset"] + n].view(p["shape"]).clone()
+                if not torch.isfinite(t).all():
+                    raise OLMoCheckpointError(f"parameter {p['name']} was not fully covered by the shard files")
+                model_state[p["name"]] = t.to(dev)
+        optim_state: Optional[Dict[str, Any]] = None
+        if optim_shards is not None:
+            state: Dict[str, Dict[str, Any]] = {}
+            for unit in meta["units"]:
+                keys = sorted({k for os_ in optim_shards for k in os_["units"].get(unit["name"], {})})
+                for key in keys:
+                    full = assemble([os_["units"][unit["name"]].get(key, torch.zeros(unit["shard_size"])) for os_ in optim_shards], unit)
+                    for p in unit["params"]:
+                        n = 1
+                        for d in p["shape"]:
+                            n *= d
+                        state.setdefault(p["name"], {})[key] = full[p["offset"] : p["offset"] + n].view(p["shape"]).clone().to(dev)
+            for os_ in optim_shards:
+                for name, sc in os_.get("scalars", {}).items():
+                    for k, v in sc.items():
+                        state.setdefault(name, {}).setdefault(k, v)
+            optim_state = {"state": state, "param_groups": optim_shards[0]["param_groups"]}
+        trainer_state = load_state_dict(load_path, "train/rank0.pt", local_cache=local_cache) if load_trainer_state else None
+        return model_state, optim_state, trainer_state
+
+
+class TorchNewStyleShardedCheckpointer(FlatShardCheckpointer):
+    """``sharded_checkpointer: torch_new`` — stored in the flat-shard format."""
+
+
+class TorchLegacyShardedCheckpointer(FlatShardCheckpointer):
+    """``sharded_checkpointer: torch_legacy`` — stored in the flat-shard format."""
+
+    def __init__(self, cfg: TrainConfig, thread_count: Optional[int] = None, use_shared_mem_impl: bool = False):
+        super().__init__(cfg, thread_count)
+        self.use_shared_mem_impl = use_shared_mem_impl
+
+
+class LocalShardedCheckpointer(FlatShardCheckpointer):
+    """``sharded_checkpointer: local`` — stored in the flat-shard format."""
+
+
+class OlmoCoreCheckpointer(FlatShardCheckpointer):
+    """``sharded_checkpointer: olmo_core`` — stored in the flat-shard format (the ``olmo_core`` package is not required)."""
+
+
+def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckpointerType] = None, use_shared_mem_impl: bool = False) -> Checkpointer:
+    name = name or cfg.sharded_checkpointer
+    if name == ShardedCheckpointerType.torch_new:
+        return TorchNewStyleShardedCheckpointer(cfg)
+    if name == ShardedCheckpointerType.torch_legacy:
+        return TorchLegacyShardedCheckpointer(cfg, use_shared_mem_impl=use_shared_mem_impl)
+    if name == ShardedCheckpointerType.local:
+        return LocalShardedCheckpointer(cfg)
+    if name == ShardedCheckpointerType.olmo_core:
+        return OlmoCoreCheckpointer(cfg)
+    raise NotImplementedError(name)

@@ -34,9 +34,9 @@ int ob_reduce_rows_f32(const float* part, int nparts, int D, float* out, int acc
 
 // ---- rope.cu
 int ob_qk_rows_per_launch(int M);
-int ob_qk_norm_rope_fwd(void* qkv, void* qk_out, const void* wq, const void* wk, const float* cos_t, const float* sin_t,
-                        float* rstd_q, float* rstd_k, int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq,
-                        float eps, float clip, int do_norm, int do_rope, cudaStream_t stream);
+int ob_qk_norm_rope_fwd(const void* qkv, void* qk_out, const void* wq, const void* wk, const float* cos_t,
+                        const float* sin_t, float* rstd_q, float* rstd_k, int M, int T, int pos_offset, int Wq, int Wk,
+                        int hd, int ldq, int ldo, float eps, float clip, int do_norm, int do_rope, cudaStream_t stream);
 int ob_qk_norm_rope_bwd(const void* qkv, void* dqkv, const void* wq, const void* wk, const float* cos_t,
                         const float* sin_t, const float* rstd_q, const float* rstd_k, float* dwq_part, float* dwk_part,
                         int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq, float clip, int do_norm,

@@ -2,7 +2,9 @@
 //
 // Input is the fused projection qkv[M, ldq] = [q (Wq cols) | k (Wk cols) | v].  Per token row:
 //   q <- rope(rmsnorm(q) * wq),  k <- rope(rmsnorm(k) * wk)        (the norm spans all heads jointly)
-// and the result is written to qk_out[M, Wq + Wk]; v is left where it is (optionally clamped in place).
+// and the result is written to out[M, ldo] = [q | k]; v is read by attention from qkv directly.  With clip_qkv
+// (OLMo-1) all three parts are clamped first and the clamped v is written to out as a third part, so that the
+// un-clamped projection survives for the backward mask.
 // RoPE is the rotate-half form: within a head, element j < hd/2 pairs with j + hd/2;
 //   a' = a cos - b sin,  b' = b cos + a sin   in fp32, rounded to bf16 once.
 // Each thread owns pairs of 8-element vectors (a-vector and its partner), so rotation needs no exchange.
@@ -128,28 +130,29 @@ __device__ __forceinline__ void part_fwd(const bf16* __restrict__ in, bf16* __re
 
 template <bool NORM, bool ROPE>
 __global__ void __launch_bounds__(NT)
-qk_fwd_kernel(bf16* __restrict__ qkv, bf16* __restrict__ qk_out, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
+qk_fwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ qk_out, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
               const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ rstd_q,
-              float* __restrict__ rstd_k, int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq, float eps,
-              float clip) {
+              float* __restrict__ rstd_k, int M, int T, int pos_offset, int Wq, int Wk, int hd, int ldq, int ldo,
+              float eps, float clip) {
   __shared__ float red[32];
   const int half = hd >> 1;
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     const int t = row % T + pos_offset;
     const float* cr = cos_t + static_cast<size_t>(t) * half;
     const float* sr = sin_t + static_cast<size_t>(t) * half;
-    bf16* in = qkv + static_cast<size_t>(row) * ldq;
-    bf16* out = qk_out + static_cast<size_t>(row) * (Wq + Wk);
+    const bf16* in = qkv + static_cast<size_t>(row) * ldq;
+    bf16* out = qk_out + static_cast<size_t>(row) * ldo;
     part_fwd<NORM, ROPE>(in, out, wq, cr, sr, Wq, hd, eps, clip, rstd_q ? rstd_q + row : nullptr, red);
     part_fwd<NORM, ROPE>(in + Wq, out + Wq, wk, cr, sr, Wk, hd, eps, clip, rstd_k ? rstd_k + row : nullptr, red);
-    if (clip > 0.f) {  // v is clamped where it lives
-      bf16* v = in + Wq + Wk;
+    if (clip > 0.f) {  // clamped v becomes the third part of the output
+      const bf16* v = in + Wq + Wk;
+      bf16* vo = out + Wq + Wk;
       for (int i = threadIdx.x; i < (Wk >> 3); i += NT) {
         float f[8];
         ld8(v + i * 8, f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = clampf(f[j], clip);
-        st8(v + i * 8, f);
+        st8(vo + i * 8, f);
       }
     }
   }
@@ -267,7 +270,7 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
     bf16* g = dqkv + static_cast<size_t>(row) * ldq;
     part_bwd<NORM, ROPE>(in, g, wq, cr, sr, Wq, hd, clip, NORM ? rstd_q[row] : 1.f, dqa, dqb, red);
     part_bwd<NORM, ROPE>(in + Wq, g + Wq, wk, cr, sr, Wk, hd, clip, NORM ? rstd_k[row] : 1.f, dka, dkb, red);
-    if (clip > 0.f) {  // v was clamped in place in the forward pass: |v| == clip marks a saturated element
+    if (clip > 0.f) {  // clamp passes no gradient where the projection was outside [-clip, clip]
       const bf16* v = in + Wq + Wk;
       bf16* dv = g + Wq + Wk;
       for (int i = threadIdx.x; i < (Wk >> 3); i += NT) {
@@ -276,7 +279,7 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
         ld8(dv + i * 8, d);
 #pragma unroll
         for (int j = 0; j < 8; ++j)
-          if (fabsf(f[j]) >= clip) d[j] = 0.f;
+          if (fabsf(f[j]) > clip) d[j] = 0.f;
         st8(dv + i * 8, d);
       }
     }
@@ -317,17 +320,18 @@ static int qk_check(int Wq, int Wk, int hd, int ldq) {
   return 0;
 }
 
-extern "C" int ob_qk_norm_rope_fwd(void* qkv, void* qk_out, const void* wq, const void* wk, const float* cos_t,
+extern "C" int ob_qk_norm_rope_fwd(const void* qkv, void* qk_out, const void* wq, const void* wk, const float* cos_t,
                                    const float* sin_t, float* rstd_q, float* rstd_k, int M, int T, int pos_offset,
-                                   int Wq, int Wk, int hd, int ldq, float eps, float clip, int do_norm, int do_rope,
-                                   cudaStream_t stream) {
+                                   int Wq, int Wk, int hd, int ldq, int ldo, float eps, float clip, int do_norm,
+                                   int do_rope, cudaStream_t stream) {
   using namespace ob;
   if (M <= 0) return 0;
-  if (qk_check(Wq, Wk, hd, ldq) != 0) return -1;
+  if (qk_check(Wq, Wk, hd, ldq) != 0 || ldo % 8 != 0) return -1;
   const int grid = ob_qk_rows_per_launch(M);
 #define OB_QK_FWD(N_, R_)                                                                                        \
-  qk_fwd_kernel<N_, R_><<<grid, NT, 0, stream>>>((bf16*)qkv, (bf16*)qk_out, (const bf16*)wq, (const bf16*)wk, cos_t, \
-                                                 sin_t, rstd_q, rstd_k, M, T, pos_offset, Wq, Wk, hd, ldq, eps, clip)
+  qk_fwd_kernel<N_, R_><<<grid, NT, 0, stream>>>((const bf16*)qkv, (bf16*)qk_out, (const bf16*)wq, (const bf16*)wk, \
+                                                 cos_t, sin_t, rstd_q, rstd_k, M, T, pos_offset, Wq, Wk, hd, ldq,   \
+                                                 ldo, eps, clip)
   if (do_norm && do_rope) OB_QK_FWD(true, true);
   else if (do_norm) OB_QK_FWD(true, false);
   else if (do_rope) OB_QK_FWD(false, true);

@@ -160,7 +160,18 @@ def ptr(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
-def check(rc: int, what: str) -> int:
+_launches = 0
+
+
+def check(rc: int, what: str, kernels: int = 1) -> int:
+    """Validate a C entry point's return code and count the kernels it launched."""
+    global _launches
     if rc < 0:
         raise OLMoKernelError(f"{what} failed to launch (code {rc})")
+    _launches += kernels
     return rc
+
+
+def launch_count() -> int:
+    """Number of kernels of this library launched by the current process so far."""
+    return _launches

@@ -1,0 +1,73 @@
+"""
+Python side of the tcgen05 flash-attention kernels (``csrc/attention.cu``).
+
+``supports`` reports whether the native kernel covers a call; callers fall back to the library or the
+math back end otherwise (see :mod:`olmo_b200.ops.attention`).
+"""
+from __future__ import annotations
+
+from ctypes import c_float, c_int
+from typing import Optional, Tuple
+
+import torch
+
+from . import check, lib, ptr, status_tensor, stream_ptr
+
+
+def _have_symbol(name: str) -> bool:
+    try:
+        return hasattr(lib(), name)
+    except Exception:
+        return False
+
+
+def supports(q: torch.Tensor, k: torch.Tensor, causal: bool, dropout_p: float, varlen: bool) -> bool:
+    """Forward kernel coverage: bf16, head dim 128, no dropout, self-attention (Tq == Tk), T % 128 == 0."""
+    if varlen or dropout_p != 0.0 or q.dtype != torch.bfloat16 or not q.is_cuda:
+        return False
+    if q.dim() != 4 or q.shape[-1] != 128 or q.shape[1] != k.shape[1] or q.shape[1] % 128 != 0:
+        return False
+    if q.shape[2] % k.shape[2] != 0:
+        return False
+    return _have_symbol("ob_attention_fwd")
+
+
+def supports_backward(q: torch.Tensor, k: torch.Tensor, causal: bool) -> bool:
+    return supports(q, k, causal, 0.0, False) and _have_symbol("ob_attention_bwd")
+
+
+def _strides(t: torch.Tensor) -> Tuple[int, int, int]:
+    assert t.stride(-1) == 1
+    return t.stride(0), t.stride(1), t.stride(2)
+
+
+def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = None):
+    B, T, H, D = q.shape
+    Hkv = k.shape[2]
+    o = torch.empty((B, T, H, D), dtype=q.dtype, device=q.device) if out is None else out
+    lse = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    rc = lib().ob_attention_fwd(
+        ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), c_int(B), c_int(T), c_int(H), c_int(Hkv),
+        *(c_int(s) for s in _strides(q)), *(c_int(s) for s in _strides(k)), *(c_int(s) for s in _strides(v)),
+        *(c_int(s) for s in _strides(o)), c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), stream_ptr(),
+    )
+    check(rc, "ob_attention_fwd")
+    return o, lse
+
+
+def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float) -> None:
+    B, T, H, D = q.shape
+    Hkv = k.shape[2]
+    rc = lib().ob_attention_bwd(
+        ptr(do), ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(dq), ptr(dk), ptr(dv),
+        c_int(B), c_int(T), c_int(H), c_int(Hkv),
+        *(c_int(s) for s in _strides(do)), *(c_int(s) for s in _strides(q)), *(c_int(s) for s in _strides(k)),
+        *(c_int(s) for s in _strides(v)), *(c_int(s) for s in _strides(o)), *(c_int(s) for s in _strides(dq)),
+        *(c_int(s) for s in _strides(dk)), *(c_int(s) for s in _strides(dv)),
+        c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), stream_ptr(),
+    )
+    check(rc, "ob_attention_bwd")
+
+
+def varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale):  # pragma: no cover - not reached while supports() is False for varlen
+    raise NotImplementedError

@@ -12,7 +12,7 @@ from typing import Optional, Tuple
 
 import torch
 
-from . import check, lib, ptr, status_tensor, stream_ptr
+from . import check, launch_count, lib, ptr, status_tensor, stream_ptr  # noqa: F401
 
 EPI_BF16, EPI_F32_ACCUM, EPI_BF16_ADD, EPI_F32_STORE = 0, 1, 2, 3
 
@@ -175,17 +175,18 @@ def qk_norm_rope_fwd(
     do_rope: bool,
     pos_offset: int = 0,
 ):
-    """See ``csrc/rope.cu``.  ``qkv`` is ``[M, Wq+2Wk]``; returns ``(qk_out [M, Wq+Wk], rstd_q, rstd_k)``."""
+    """See ``csrc/rope.cu``.  ``qkv`` is ``[M, Wq+2Wk]``; returns ``(out, rstd_q, rstd_k)`` where ``out`` is
+    ``[M, Wq+Wk]`` (q | k), or ``[M, Wq+2Wk]`` (q | k | clamped v) when ``clip > 0``."""
     _bf16(qkv, "qkv")
     M = qkv.shape[0]
     assert qkv.dim() == 2 and qkv.stride(1) == 1
-    qk = torch.empty((M, Wq + Wk), dtype=torch.bfloat16, device=qkv.device)
+    qk = torch.empty((M, Wq + Wk + (Wk if clip > 0 else 0)), dtype=torch.bfloat16, device=qkv.device)
     rq = torch.empty(M, dtype=torch.float32, device=qkv.device) if do_norm else None
     rk = torch.empty(M, dtype=torch.float32, device=qkv.device) if do_norm else None
     rc = lib().ob_qk_norm_rope_fwd(
         ptr(qkv), ptr(qk), ptr(wq), ptr(wk), ptr(cos), ptr(sin), ptr(rq), ptr(rk),
         c_int(M), c_int(seq_len), c_int(pos_offset), c_int(Wq), c_int(Wk), c_int(head_dim), c_int(qkv.stride(0)),
-        c_float(eps), c_float(clip), c_int(int(do_norm)), c_int(int(do_rope)), stream_ptr(),
+        c_int(qk.stride(0)), c_float(eps), c_float(clip), c_int(int(do_norm)), c_int(int(do_rope)), stream_ptr(),
     )
     check(rc, "ob_qk_norm_rope_fwd")
     return qk, rq, rk
@@ -321,7 +322,7 @@ def sumsq(g: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> torch
     n = g.numel()
     nparts = lib().ob_sumsq_num_partials(c_longlong(n))
     partials = torch.empty(nparts, dtype=torch.float32, device=g.device)
-    check(lib().ob_sumsq_f32(ptr(g), c_longlong(n), ptr(partials), ptr(out), c_int(int(accumulate)), stream_ptr()), "ob_sumsq_f32")
+    check(lib().ob_sumsq_f32(ptr(g), c_longlong(n), ptr(partials), ptr(out), c_int(int(accumulate)), stream_ptr()), "ob_sumsq_f32", kernels=2)
     return out
 
 

@@ -144,19 +144,15 @@ def test_qk_norm_rope(do_norm, clip, n_kv):
     dq, dk, dv = _rand(M, Wq), _rand(M, Wk), _rand(M, Wk)
     ((rq * dq.float()).sum() + (rk * dk.float()).sum() + (rv * dv.float()).sum()).backward()
 
-    work = qkv.clone()
-    qk, rstd_q, rstd_k = k.qk_norm_rope_fwd(work, wq, wk, cos, sin, T, Wq, Wk, hd, eps, clip, do_norm, True)
+    qk, rstd_q, rstd_k = k.qk_norm_rope_fwd(qkv, wq, wk, cos, sin, T, Wq, Wk, hd, eps, clip, do_norm, True)
     _close(qk[:, :Wq], rq.detach())
-    _close(qk[:, Wq:], rk.detach())
+    _close(qk[:, Wq : Wq + Wk], rk.detach())
     if clip > 0:
-        _close(work[:, Wq + Wk :], rv.detach())
+        _close(qk[:, Wq + Wk :], rv.detach())
     dqkv = torch.cat((dq, dk, dv), dim=-1).contiguous()
     dwq = torch.zeros(Wq, device="cuda") if do_norm else None
     dwk = torch.zeros(Wk, device="cuda") if do_norm else None
-    k.qk_norm_rope_bwd(work if clip > 0 else qkv, dqkv, wq, wk, cos, sin, rstd_q, rstd_k, T, Wq, Wk, hd, clip, do_norm, True, dwq, dwk)
-    if clip > 0:
-        # q,k masks come from the pre-clamp values; the forward left those untouched in `work`
-        pass
+    k.qk_norm_rope_bwd(qkv, dqkv, wq, wk, cos, sin, rstd_q, rstd_k, T, Wq, Wk, hd, clip, do_norm, True, dwq, dwk)
     _close(dqkv, qkv_f.grad, rtol=3e-2, atol=3e-2)
     if do_norm:
         _close(dwq, wq_f.grad, rtol=3e-2, atol=3e-2)
