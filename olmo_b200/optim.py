@@ -627,7 +627,7 @@ def get_param_groups(cfg: TrainConfig, model: nn.Module) -> List[Dict[str, Any]]
     module_root = getattr(model, "module", model) if named is not None else model
     for mn, m in module_root.named_modules():
         for pn, p in m.named_parameters(recurse=False):
-            if not p.requires_grad:
+            if named is None and not p.requires_grad:
                 continue
             fpn = f"{mn}.{pn}" if mn else pn
             if pn.endswith("bias"):
