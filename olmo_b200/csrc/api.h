@@ -22,6 +22,17 @@ int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R, int M, in
                  int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag, int ready_value,
                  int* status, int num_sms, cudaStream_t stream);
 
+int ob_gemm_bf16_comm(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb, int ldc,
+                      int a_mn_major, int b_mn_major, int epi, int* status, int num_sms, const void* task, int comm_ctas,
+                      cudaStream_t stream);
+
+// ---- comm.cu (peer-memory collectives; `task` points at an ob::CommTask, see comm.cuh)
+int ob_comm_task_size(void);
+int ob_comm_launch(const void* task, int nctas, cudaStream_t stream);
+int ob_signal(int* flag, int value, cudaStream_t stream);
+int ob_scalar_slots_bytes(void);
+int ob_allreduce_scalar(const float* value, void* const* peers, void* mine, float* out, int rank, int world, int epoch,
+                        int* status, cudaStream_t stream);
 
 // ---- norm.cu
 int ob_norm_rows_per_launch(int M);

@@ -1,0 +1,86 @@
+// Stand-alone launches of the peer-memory collectives (comm.cuh), the flag signal and the small scalar all-reduce
+// that doubles as the end-of-step barrier.
+#include "comm.cuh"
+#include "api.h"
+
+namespace ob {
+namespace {
+
+constexpr int COMM_THREADS = 512;
+
+__global__ void __launch_bounds__(COMM_THREADS) comm_kernel(const __grid_constant__ CommTask task) {
+  comm_run(task, blockIdx.x, gridDim.x);
+}
+
+__global__ void signal_kernel(int* flag, int value) {
+  __threadfence_system();
+  flag_store_release(flag, value);
+}
+
+// Layout of one rank's exchange area (symmetric memory): two parities x (8 values, 8 flags).
+struct ScalarSlots {
+  float vals[2][COMM_MAX_WORLD];
+  int flags[2][COMM_MAX_WORLD];
+};
+
+// Every rank stores its value into slot [rank] of every peer, then waits until all of its own slots carry this epoch
+// and sums them in rank order, so all ranks obtain the bit-identical total.  Returning from this kernel on every rank
+// also implies that every rank has finished everything it enqueued before it.
+__global__ void allreduce_scalar_kernel(const float* __restrict__ value, ScalarSlots* const* __restrict__ peers,
+                                        ScalarSlots* mine, float* __restrict__ out, int rank, int world, int epoch,
+                                        int* status) {
+  __shared__ int ok;
+  const int par = epoch & 1;
+  const int p = threadIdx.x;
+  if (p == 0) ok = 1;
+  __syncthreads();
+  if (p < world) {
+    ScalarSlots* dst = peers[p];
+    dst->vals[par][rank] = *value;
+    __threadfence_system();
+    flag_store_release(&dst->flags[par][rank], epoch);
+    if (!flag_wait_ge(&mine->flags[par][p], epoch, nullptr, status)) ok = 0;
+  }
+  __syncthreads();
+  if (p == 0) {
+    float s = 0.f;
+    if (ok) {
+      for (int q = 0; q < world; ++q) s += *reinterpret_cast<volatile float*>(&mine->vals[par][q]);
+    } else {
+      s = *value;
+    }
+    out[0] = s;
+  }
+}
+
+}  // namespace
+}  // namespace ob
+
+extern "C" int ob_comm_task_size(void) { return static_cast<int>(sizeof(ob::CommTask)); }
+
+extern "C" int ob_comm_launch(const void* task, int nctas, cudaStream_t stream) {
+  using namespace ob;
+  const CommTask* t = reinterpret_cast<const CommTask*>(task);
+  if (t == nullptr || t->world < 1 || t->world > COMM_MAX_WORLD || nctas < 1) return -1;
+  if (t->kind == COMM_ALL_GATHER && (t->elems % 8 != 0)) return -2;
+  if (t->kind == COMM_REDUCE_SCATTER && (t->elems % 4 != 0)) return -2;
+  comm_kernel<<<nctas, COMM_THREADS, 0, stream>>>(*t);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+extern "C" int ob_signal(int* flag, int value, cudaStream_t stream) {
+  ob::signal_kernel<<<1, 1, 0, stream>>>(flag, value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+extern "C" int ob_scalar_slots_bytes(void) { return static_cast<int>(sizeof(ob::ScalarSlots)); }
+
+// `peers` is a device array of `world` pointers to every rank's exchange area (this rank's included).
+extern "C" int ob_allreduce_scalar(const float* value, void* const* peers, void* mine, float* out, int rank, int world,
+                                   int epoch, int* status, cudaStream_t stream) {
+  using namespace ob;
+  if (world < 1 || world > COMM_MAX_WORLD) return -1;
+  allreduce_scalar_kernel<<<1, 32, 0, stream>>>(value, reinterpret_cast<ScalarSlots* const*>(peers),
+                                               reinterpret_cast<ScalarSlots*>(mine), out, rank, world, epoch, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}

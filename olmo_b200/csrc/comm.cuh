@@ -1,0 +1,115 @@
+// Peer-memory collectives as device functions, so that the same code runs either as a stand-alone kernel or as the
+// "communication CTAs" of a GEMM launch (gemm.cu): the first `comm_ctas` blocks of the grid execute a CommTask while the
+// remaining blocks compute tiles, which overlaps NVLink traffic with tensor-core work inside one kernel.
+//
+// All remote accesses are plain loads through peer-mapped pointers (NVLink 5 via NVSwitch).  Nothing here uses TMA or
+// cluster multicast.  Waits on a peer's flag are bounded (common.cuh) and report through the status word.
+#pragma once
+
+#include "common.cuh"
+
+namespace ob {
+
+constexpr int COMM_MAX_WORLD = 8;
+
+enum : int { COMM_NONE = 0, COMM_ALL_GATHER = 1, COMM_REDUCE_SCATTER = 2 };
+
+struct CommTask {
+  int kind;
+  int world;
+  int rank;
+  int wait_value;                 // proceed with peer p once *wait_flags[p] >= wait_value (null flag: no wait)
+  long long elems;                // all-gather: bf16 elements per peer region; reduce-scatter: fp32 elements of my slice
+  long long dst_peer_stride;      // all-gather: elements between consecutive ranks' regions in dst
+  const void* src[COMM_MAX_WORLD];
+  const int* wait_flags[COMM_MAX_WORLD];
+  void* dst;
+  float scale;                    // reduce-scatter: dst += scale * sum_p src[p]
+  float* sumsq_partials;          // reduce-scatter, optional: partial[c] += sum of squares of what CTA c added
+  int* status;
+};
+
+__device__ __forceinline__ uint4 ld_peer_16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+  return v;
+}
+
+// Every thread of the CTA calls this; returns false if the wait ran out (whole CTA agrees).
+__device__ __forceinline__ bool comm_wait_peer(const CommTask& t, int p, int* smem_ok) {
+  if (t.wait_flags[p] == nullptr) return true;
+  __syncthreads();
+  if (threadIdx.x == 0) *smem_ok = flag_wait_ge(t.wait_flags[p], t.wait_value, nullptr, t.status) ? 1 : 0;
+  __syncthreads();
+  return *smem_ok != 0;
+}
+
+// Copy every peer's region (except this rank's own, which is already in place) into dst.  16-byte granularity:
+// `elems` must be a multiple of 8 bf16 elements and all bases 16-byte aligned.
+__device__ __forceinline__ void comm_all_gather(const CommTask& t, int cta, int nctas, int* smem_ok) {
+  const long long vecs = t.elems >> 3;  // 16-byte vectors per peer
+  constexpr int UNROLL = 8;
+  const long long tile = static_cast<long long>(blockDim.x) * UNROLL;  // vectors per CTA iteration
+  for (int q = 1; q < t.world; ++q) {
+    const int p = (t.rank + q) % t.world;  // start with the next rank so that peers are read evenly
+    if (!comm_wait_peer(t, p, smem_ok)) return;
+    const uint4* src = reinterpret_cast<const uint4*>(t.src[p]);
+    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(t.dst) + static_cast<long long>(p) * t.dst_peer_stride);
+    for (long long base = static_cast<long long>(cta) * tile; base < vecs; base += static_cast<long long>(nctas) * tile) {
+      uint4 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
+        if (i < vecs) v[u] = ld_peer_16(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
+        if (i < vecs) dst[i] = v[u];
+      }
+    }
+  }
+}
+
+// dst[i] += scale * (src[0][i] + src[1][i] + ... + src[W-1][i]) over my slice, summed in rank order (deterministic).
+// `elems` must be a multiple of 4 fp32 elements.
+__device__ __forceinline__ void comm_reduce_scatter(const CommTask& t, int cta, int nctas, int* smem_ok, float* red) {
+  for (int p = 0; p < t.world; ++p)
+    if (p != t.rank && !comm_wait_peer(t, p, smem_ok)) return;
+  const long long vecs = t.elems >> 2;
+  float4* dst = reinterpret_cast<float4*>(t.dst);
+  float ss = 0.f;
+  for (long long i = static_cast<long long>(cta) * blockDim.x + threadIdx.x; i < vecs; i += static_cast<long long>(nctas) * blockDim.x) {
+    uint4 v[COMM_MAX_WORLD];
+#pragma unroll
+    for (int p = 0; p < COMM_MAX_WORLD; ++p)
+      if (p < t.world) v[p] = ld_peer_16(reinterpret_cast<const uint4*>(t.src[p]) + i);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < COMM_MAX_WORLD; ++p)
+      if (p < t.world) {
+        acc.x += __uint_as_float(v[p].x);
+        acc.y += __uint_as_float(v[p].y);
+        acc.z += __uint_as_float(v[p].z);
+        acc.w += __uint_as_float(v[p].w);
+      }
+    acc.x *= t.scale; acc.y *= t.scale; acc.z *= t.scale; acc.w *= t.scale;
+    float4 d = dst[i];
+    d.x += acc.x; d.y += acc.y; d.z += acc.z; d.w += acc.w;
+    dst[i] = d;
+    ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+  }
+  if (t.sumsq_partials != nullptr) {
+    ss = block_sum(ss, red);
+    if (threadIdx.x == 0) t.sumsq_partials[cta] += ss;
+  }
+}
+
+__device__ __forceinline__ void comm_run(const CommTask& t, int cta, int nctas) {
+  __shared__ int smem_ok;
+  __shared__ float red[32];
+  if (t.kind == COMM_ALL_GATHER) comm_all_gather(t, cta, nctas, &smem_ok);
+  else if (t.kind == COMM_REDUCE_SCATTER) comm_reduce_scatter(t, cta, nctas, &smem_ok, red);
+}
+
+}  // namespace ob

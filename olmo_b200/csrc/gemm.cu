@@ -10,11 +10,16 @@
 //   warps 2..5  epilogue            (tcgen05.ld 32x32b from one of two 256-column accumulators -> global)
 // The two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
 //
+// Optional communication CTAs: when `comm_ctas` > 0 the first `comm_ctas` blocks of the grid execute a CommTask
+// (comm.cuh: peer all-gather of the next unit's weights, or the gradient reduce-scatter of the previous unit) and
+// exit; the remaining blocks are the persistent GEMM.  One launch therefore overlaps NVLink traffic with the math.
+//
 // Optional readiness flags: when `b_ready` is given, the producer waits (bounded) until
 // b_ready[(first B row of the tile) / rows_per_flag ... (last row) / rows_per_flag] >= ready_value before it
 // loads B.  The parameter all-gather that lands peer shards in local memory sets these flags chunk by chunk,
 // which lets the consuming GEMM start before the whole weight has arrived.
 #include "common.cuh"
+#include "comm.cuh"
 #include "api.h"
 
 namespace ob {
@@ -52,7 +57,14 @@ template <int A_MN, int B_MN, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
-                 const int* __restrict__ b_ready, int rows_per_flag, int ready_value, int* __restrict__ status) {
+                 const int* __restrict__ b_ready, int rows_per_flag, int ready_value, int* __restrict__ status,
+                 const __grid_constant__ CommTask comm_task, int comm_ctas) {
+  if (static_cast<int>(blockIdx.x) < comm_ctas) {  // communication role: no TMEM, no barriers
+    comm_run(comm_task, blockIdx.x, comm_ctas);
+    return;
+  }
+  const int cta = static_cast<int>(blockIdx.x) - comm_ctas;
+  const int num_ctas = static_cast<int>(gridDim.x) - comm_ctas;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -101,7 +113,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       uint32_t phase = 0;
       int issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = cta; t < num_tiles && ok; t += num_ctas) {
         const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
         const int m0 = tc.m * BM, n0 = tc.n * BN;
         if (b_ready != nullptr) {
@@ -155,7 +167,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+      for (int t = cta; t < num_tiles && ok; t += num_ctas) {
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, abort_flag, status, ST_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -195,7 +207,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) are the ones this warp may read
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+    for (int t = cta; t < num_tiles; t += num_ctas) {
       const TileCoord tc = tile_coord(t, tiles_m, tiles_n);
       const int row = tc.m * BM + quarter * 32 + lane;
       const int n0 = tc.n * BN;
@@ -325,7 +337,7 @@ int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, 
 template <int A_MN, int B_MN, int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const void* R, int M, int N, int K,
                        int ldc, int vec_ok, const int* b_ready, int rows_per_flag, int ready_value, int* status,
-                       int num_sms, cudaStream_t stream) {
+                       int num_sms, const CommTask& comm_task, int comm_ctas, cudaStream_t stream) {
   auto kern = gemm_bf16_kernel<A_MN, B_MN, EPI>;
   static bool configured = false;
   if (!configured) {
@@ -334,17 +346,20 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, co
     configured = true;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
-  const int grid = tiles < num_sms ? tiles : num_sms;
-  kern<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc, vec_ok,
-                                                  b_ready, rows_per_flag, ready_value, status);
+  if (comm_ctas < 0 || comm_ctas >= num_sms) return -12;
+  const int gemm_ctas = tiles < num_sms - comm_ctas ? tiles : num_sms - comm_ctas;
+  kern<<<gemm_ctas + comm_ctas, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc,
+                                                                  vec_ok, b_ready, rows_per_flag, ready_value, status,
+                                                                  comm_task, comm_ctas);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
 }  // namespace ob
 
-extern "C" int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb,
-                            int ldc, int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag,
-                            int ready_value, int* status, int num_sms, cudaStream_t stream) {
+static int gemm_dispatch(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb,
+                         int ldc, int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag,
+                         int ready_value, int* status, int num_sms, const ob::CommTask& comm_task, int comm_ctas,
+                         cudaStream_t stream) {
   using namespace ob;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   CUtensorMap ta, tb;
@@ -364,7 +379,7 @@ extern "C" int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R
 #define OB_DISPATCH(AM, BMJ, E)                                                                                      \
   if (a_mn_major == AM && b_mn_major == BMJ && epi == E)                                                             \
     return launch_gemm<AM, BMJ, E>(ta, tb, C, R, M, N, K, ldc, vec_ok, b_ready, rows_per_flag, ready_value, status,  \
-                                   num_sms, stream);
+                                   num_sms, comm_task, comm_ctas, stream);
   OB_DISPATCH(0, 0, EPI_BF16)
   OB_DISPATCH(0, 0, EPI_BF16_ADD)
   OB_DISPATCH(0, 0, EPI_F32_STORE)
@@ -376,4 +391,22 @@ extern "C" int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R
   OB_DISPATCH(1, 0, EPI_BF16)
 #undef OB_DISPATCH
   return -20;  // combination not instantiated
+}
+
+extern "C" int ob_gemm_bf16(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb,
+                            int ldc, int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag,
+                            int ready_value, int* status, int num_sms, cudaStream_t stream) {
+  ob::CommTask none = {};
+  return gemm_dispatch(A, B, C, R, M, N, K, lda, ldb, ldc, a_mn_major, b_mn_major, epi, b_ready, rows_per_flag, ready_value,
+                       status, num_sms, none, 0, stream);
+}
+
+// Same GEMM with `comm_ctas` blocks of the grid executing `*task` (layout of ob::CommTask, see comm.cuh) concurrently.
+extern "C" int ob_gemm_bf16_comm(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda,
+                                 int ldb, int ldc, int a_mn_major, int b_mn_major, int epi, int* status, int num_sms,
+                                 const void* task, int comm_ctas, cudaStream_t stream) {
+  const ob::CommTask* t = reinterpret_cast<const ob::CommTask*>(task);
+  if (t == nullptr || t->world > ob::COMM_MAX_WORLD) return -13;
+  return gemm_dispatch(A, B, C, R, M, N, K, lda, ldb, ldc, a_mn_major, b_mn_major, epi, nullptr, 0, 0, status, num_sms, *t,
+                       comm_ctas, stream);
 }
