@@ -32,7 +32,7 @@ int ob_comm_launch(const void* task, int nctas, cudaStream_t stream);
 int ob_signal(int* flag, int value, cudaStream_t stream);
 int ob_scalar_slots_bytes(void);
 int ob_allreduce_scalar(const float* value, void* const* peers, void* mine, float* out, int rank, int world, int epoch,
-                        int* status, cudaStream_t stream);
+                        int* status, long long wait_cycles, cudaStream_t stream);
 
 // ---- norm.cu
 int ob_norm_rows_per_launch(int M);

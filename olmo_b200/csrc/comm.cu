@@ -28,7 +28,7 @@ struct ScalarSlots {
 // also implies that every rank has finished everything it enqueued before it.
 __global__ void allreduce_scalar_kernel(const float* __restrict__ value, ScalarSlots* const* __restrict__ peers,
                                         ScalarSlots* mine, float* __restrict__ out, int rank, int world, int epoch,
-                                        int* status) {
+                                        int* status, long long wait_cycles) {
   __shared__ int ok;
   const int par = epoch & 1;
   const int p = threadIdx.x;
@@ -39,7 +39,7 @@ __global__ void allreduce_scalar_kernel(const float* __restrict__ value, ScalarS
     dst->vals[par][rank] = *value;
     __threadfence_system();
     flag_store_release(&dst->flags[par][rank], epoch);
-    if (!flag_wait_ge(&mine->flags[par][p], epoch, nullptr, status)) ok = 0;
+    if (!flag_wait_ge(&mine->flags[par][p], epoch, nullptr, status, wait_cycles > 0 ? wait_cycles : OB_WAIT_BUDGET_CYCLES)) ok = 0;
   }
   __syncthreads();
   if (p == 0) {
@@ -77,10 +77,10 @@ extern "C" int ob_scalar_slots_bytes(void) { return static_cast<int>(sizeof(ob::
 
 // `peers` is a device array of `world` pointers to every rank's exchange area (this rank's included).
 extern "C" int ob_allreduce_scalar(const float* value, void* const* peers, void* mine, float* out, int rank, int world,
-                                   int epoch, int* status, cudaStream_t stream) {
+                                   int epoch, int* status, long long wait_cycles, cudaStream_t stream) {
   using namespace ob;
   if (world < 1 || world > COMM_MAX_WORLD) return -1;
   allreduce_scalar_kernel<<<1, 32, 0, stream>>>(value, reinterpret_cast<ScalarSlots* const*>(peers),
-                                               reinterpret_cast<ScalarSlots*>(mine), out, rank, world, epoch, status);
+                                               reinterpret_cast<ScalarSlots*>(mine), out, rank, world, epoch, status, wait_cycles);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }

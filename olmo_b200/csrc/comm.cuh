@@ -27,6 +27,7 @@ struct CommTask {
   float scale;                    // reduce-scatter: dst += scale * sum_p src[p]
   float* sumsq_partials;          // reduce-scatter, optional: partial[c] += sum of squares of what CTA c added
   int* status;
+  long long wait_cycles;          // budget of every flag wait in this task (0: library default)
 };
 
 __device__ __forceinline__ uint4 ld_peer_16(const void* p) {
@@ -39,7 +40,9 @@ __device__ __forceinline__ uint4 ld_peer_16(const void* p) {
 __device__ __forceinline__ bool comm_wait_peer(const CommTask& t, int p, int* smem_ok) {
   if (t.wait_flags[p] == nullptr) return true;
   __syncthreads();
-  if (threadIdx.x == 0) *smem_ok = flag_wait_ge(t.wait_flags[p], t.wait_value, nullptr, t.status) ? 1 : 0;
+  if (threadIdx.x == 0)
+    *smem_ok = flag_wait_ge(t.wait_flags[p], t.wait_value, nullptr, t.status,
+                            t.wait_cycles > 0 ? t.wait_cycles : OB_WAIT_BUDGET_CYCLES) ? 1 : 0;
   __syncthreads();
   return *smem_ok != 0;
 }

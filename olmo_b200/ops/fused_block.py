@@ -227,8 +227,11 @@ def block_backward(
     sin: torch.Tensor,
     sink: GradSink,
     need_dx: bool = True,
+    gemm_kwargs: Optional[Dict[str, Dict[str, Any]]] = None,
 ) -> Optional[torch.Tensor]:
-    """Gradient w.r.t. the block input; parameter gradients are delivered to ``sink``."""
+    """Gradient w.r.t. the block input; parameter gradients are delivered to ``sink``.  ``gemm_kwargs`` may attach a
+    communication task to the two largest input-gradient GEMMs (keys ``ff_out_dgrad`` and ``attn_out_dgrad``)."""
+    gk = gemm_kwargs or {}
     Wq, Wk, hd = spec.Wq, spec.Wk, spec.head_dim
     B, T = saved["B"], saved["T"]
     M = B * T
@@ -248,7 +251,7 @@ def block_backward(
         dx1_res = dy
     act = k.swiglu_fwd(h)  # recomputed
     sink.matrix("ff_out", d_f, act)
-    d_act = k.gemm(d_f, w["ff_out"], b_trans=True)
+    d_act = k.gemm(d_f, w["ff_out"], b_trans=True, **gk.get("ff_out_dgrad", {}))
     del act
     d_h = k.swiglu_bwd(d_act, h)
     del d_act
@@ -269,7 +272,7 @@ def block_backward(
     else:
         d_a = dx1
     sink.matrix("attn_out", d_a, o2)
-    d_o = k.gemm(d_a, w["attn_out"], b_trans=True)
+    d_o = k.gemm(d_a, w["attn_out"], b_trans=True, **gk.get("attn_out_dgrad", {}))
 
     qk, _, _ = k.qk_norm_rope_fwd(  # recomputed rotated q/k
         qkv, _norm_w(w, "q_norm"), _norm_w(w, "k_norm"), cos, sin, T, Wq, Wk, hd, spec.eps, spec.clip_qkv, spec.qk_norm, spec.rope

@@ -47,6 +47,7 @@ def gemm(
     rows_per_flag: int = 0,
     ready_value: int = 0,
     sms: int = 0,
+    comm=None,
 ) -> torch.Tensor:
     """
     ``out[M, N] = op(a) @ op(b)ᵀ`` with fp32 accumulation on tcgen05 tensor cores.
@@ -57,6 +58,8 @@ def gemm(
     So a Linear forward is ``gemm(x, W)``, its input gradient ``gemm(dy, W, b_trans=True)`` and its weight
     gradient ``gemm(dy, x, a_trans=True, b_trans=True, epilogue=EPI_F32_ACCUM, out=grad)``.
     Operands may be row-strided views (last dimension contiguous, pitch a multiple of 8 elements).
+    ``comm=(task, n_ctas)`` makes the first ``n_ctas`` blocks of the launch execute a peer-memory collective
+    (:class:`olmo_b200.parallel.peer.CommTask`) while the others compute.
     """
     _bf16(a, "a")
     _bf16(b, "b")
@@ -78,6 +81,16 @@ def gemm(
     if epilogue == EPI_BF16_ADD:
         assert residual is not None and residual.shape == out.shape and residual.stride() == out.stride()
         _bf16(residual, "residual")
+    if comm is not None:
+        task, n_ctas = comm
+        rc = lib().ob_gemm_bf16_comm(
+            ptr(a), ptr(b), ptr(out), ptr(residual),
+            c_int(M), c_int(N), c_int(K), c_int(a.stride(0)), c_int(b.stride(0)), c_int(out.stride(0)),
+            c_int(int(a_trans)), c_int(int(b_trans)), c_int(epilogue), ptr(status_tensor(a.device)), c_int(sms or num_sms()),
+            ctypes.byref(task), c_int(n_ctas), stream_ptr(),
+        )
+        check(rc, "ob_gemm_bf16_comm")
+        return out
     rc = lib().ob_gemm_bf16(
         ptr(a), ptr(b), ptr(out), ptr(residual),
         c_int(M), c_int(N), c_int(K), c_int(a.stride(0)), c_int(b.stride(0)), c_int(out.stride(0)),

@@ -144,6 +144,7 @@ class FlatShardEngine:
         self._params_stale = True  # `full` buffers need a gather before the next forward
         self._grads_pending = False  # gfull holds unreduced gradients
         self._microbatches_since_reduce = 0
+        self._grad_epoch_open = False
         self.fused_optimizer_ready = False
         self.clip_coef: Optional[torch.Tensor] = None
         self._sumsq: Optional[torch.Tensor] = None
@@ -246,6 +247,14 @@ class FlatShardEngine:
             unit = Unit(uname, index, slots, total, total // sw)
             self.units.append(unit)
         # 3. buffers; module parameters become views of `full`
+        use_peer = (
+            self.is_sharded and dev.type == "cuda" and self.fused
+            and os.environ.get("OLMO_B200_FUSED_COMM", "1").strip().lower() not in ("0", "false", "no", "off")
+        )
+        if use_peer:
+            from .peer import PeerComm
+
+            self.comm = PeerComm.create(self)
         for unit in self.units:
             S, P = unit.shard_size, unit.numel
             lo = self.shard_rank * S
@@ -254,9 +263,14 @@ class FlatShardEngine:
                 flat[s.offset : s.offset + s.numel].copy_(getattr(s.owner, s.attr).detach().reshape(-1).float())
             unit.master = flat[lo : lo + S].clone() if sw > 1 else flat
             unit.grad = torch.zeros(S, dtype=torch.float32, device=dev)
-            unit.full = flat.to(self.compute_dtype) if (self.compute_dtype != torch.float32 or sw > 1) else flat.clone()
+            if self.comm is not None:
+                unit.full = self.comm.full_view(unit.index, P)
+                unit.full.copy_(flat)
+                unit.gfull = self.comm.gfull_view(unit.index, P)
+            else:
+                unit.full = flat.to(self.compute_dtype) if (self.compute_dtype != torch.float32 or sw > 1) else flat.clone()
+                unit.gfull = unit.grad if sw == 1 else None  # type: ignore[assignment]
             unit.lowp = unit.full[lo : lo + S] if sw > 1 else unit.full
-            unit.gfull = unit.grad if sw == 1 else None  # type: ignore[assignment]
             for s in unit.slots:
                 view = unit.full[s.offset : s.offset + s.numel].view(s.shape)
                 param = nn.Parameter(view, requires_grad=not self.fused)
@@ -289,10 +303,6 @@ class FlatShardEngine:
         self._params_stale = False
         if self.fused:
             self._setup_fused()
-        if self.world > 1 and self.device.type == "cuda" and self.fused and os.environ.get("OLMO_B200_FUSED_COMM", "1") not in ("0", "false"):
-            from .peer import PeerComm
-
-            self.comm = PeerComm.create(self)
         if self.is_sharded and self.comm is None:
             for unit in self.units:
                 unit.gfull = torch.zeros(unit.numel, dtype=torch.float32, device=dev)
@@ -404,6 +414,8 @@ class FlatShardEngine:
             if lowp is None:
                 unit.lowp.copy_(unit.master)
         self._params_stale = True
+        if self.comm is not None:
+            self.comm.publish_params()
 
     def after_unfused_optimizer_step(self) -> None:
         """Per-parameter optimizers updated ``master`` in place: refresh the compute-dtype shard."""
@@ -411,13 +423,16 @@ class FlatShardEngine:
             if unit.lowp.data_ptr() != unit.master.data_ptr():
                 unit.lowp.copy_(unit.master)
         self._params_stale = True
+        if self.comm is not None:
+            self.comm.publish_params()
 
     def zero_grad(self) -> None:
         for unit in self.units:
             unit.grad.zero_()
             unit.gfull_dirty.clear()
-            if unit.gfull is not None and unit.gfull.data_ptr() != unit.grad.data_ptr() and not self.fused:
+            if unit.gfull is not None and unit.gfull.data_ptr() != unit.grad.data_ptr():
                 unit.gfull.zero_()
+            unit.reduced = False  # type: ignore[attr-defined]
         self._microbatches_since_reduce = 0
         self._grads_pending = False
 
@@ -454,7 +469,19 @@ class FlatShardEngine:
         if world == 1:
             return
         if self.comm is not None:
-            self.comm.reduce_scatter_units(self.units, scale=1.0 / world)
+            pending = [u for u in self.units if not getattr(u, "reduced", False)]
+            if pending:
+                if not self._grad_epoch_open:
+                    self.comm.begin_grad_epoch()
+                for u in pending:
+                    if not getattr(u, "published", False):
+                        self.comm.publish_grads(u)
+                self.comm.reduce_scatter_units(pending, scale=1.0 / world)
+                for u in pending:
+                    u.reduced = True  # type: ignore[attr-defined]
+            self._grad_epoch_open = False
+            for u in self.units:
+                u.published = False  # type: ignore[attr-defined]
         else:
             for unit in self.units:
                 src = unit.gfull
@@ -523,6 +550,44 @@ class FlatShardEngine:
     def vector_grad(self, param: nn.Parameter) -> torch.Tensor:
         return self.grad_view(param)[0]
 
+    def _unit_of_module_param(self, param: nn.Parameter) -> Unit:
+        return param._ob_unit  # type: ignore[attr-defined]
+
+    def _forward_unit_order(self) -> List[Unit]:
+        """Units in the order the forward pass first touches them."""
+        t = self.model.transformer
+        seq = [t.wte.weight] + [b.att_proj.weight for b in self.model.all_blocks()] + [t.ln_f.weight]
+        if not self.model.config.weight_tying:
+            seq.append(t.ff_out.weight)
+        order: List[Unit] = []
+        for p in seq:
+            if p is None:
+                continue
+            u = self._unit_of_module_param(p)
+            if all(u is not o for o in order):
+                order.append(u)
+        for u in self.units:
+            if all(u is not o for o in order):
+                order.append(u)
+        return order
+
+    def _unit_final_points(self) -> Dict[int, int]:
+        """For the backward pass: unit index -> the block index after whose backward the unit's gradients are final
+        (``n_blocks`` = right after the head and final norm, ``-1`` = after the embedding gradient)."""
+        blocks = self.model.all_blocks()
+        final: Dict[int, int] = {}
+        t = self.model.transformer
+        head = t.wte.weight if self.model.config.weight_tying else t.ff_out.weight
+        for p in (head, t.ln_f.weight):
+            if p is not None:
+                final[self._unit_of_module_param(p).index] = len(blocks)
+        for i in range(len(blocks) - 1, -1, -1):
+            final[self._unit_of_module_param(blocks[i].att_proj.weight).index] = i
+        final[self._unit_of_module_param(t.wte.weight).index] = -1
+        for u in self.units:
+            final.setdefault(u.index, -1)
+        return final
+
     def train_microbatch(
         self,
         input_ids: torch.Tensor,
@@ -530,56 +595,73 @@ class FlatShardEngine:
         loss_divisor: float,
         z_mult: float = 0.0,
         ac_strategy: Optional[ActivationCheckpointingStrategy] = None,
+        is_last: bool = True,
     ) -> Tuple[torch.Tensor, torch.Tensor]:
         """Forward + backward of one micro-batch on the fused path.
 
         ``labels`` uses ``-100`` for ignored positions and is already shifted (``labels[:, t]`` is the target of
         position ``t``).  Gradients of ``(ΣCE + z_mult·Σlse²) / loss_divisor`` are accumulated.  Returns the
         device scalars ``ΣCE / loss_divisor`` and ``z_mult·Σlse² / loss_divisor``.
+
+        With peer-memory collectives, the first micro-batch after an optimizer step pulls each unit's foreign shards
+        one unit ahead of its use from inside the ``att_proj`` / ``ff_proj`` GEMM launches, and the last micro-batch
+        (``is_last``) reduces each unit's gradients from inside the input-gradient GEMMs of the block processed next.
         """
         assert self.fused
         from ..ops import fused_block as fb
         from ..ops import kernels as k
         from ..ops.loss import lm_head_loss
 
-        self.gather_params()
+        comm = self.comm
         model, mcfg = self.model, self.model.config
         t = model.transformer
         B, T = input_ids.shape
         M = B * T
         spec = fb.spec_from_config(mcfg)
         cos, sin = fb.rope_tables(T, spec.head_dim, float(mcfg.rope_theta), self.device)
-        engine = self
-
-        class Sink(fb.GradSink):
-            def __init__(self, block):
-                super().__init__()
-                self.block = block
-                self.params = {
-                    "att_proj": block.att_proj.weight, "attn_out": block.attn_out.weight, "ff_proj": block.ff_proj.weight,
-                    "ff_out": block.ff_out.weight, "attn_norm": block.attn_norm.weight, "ff_norm": block.ff_norm.weight,
-                    "q_norm": None if block.q_norm is None else block.q_norm.weight,
-                    "k_norm": None if block.k_norm is None else block.k_norm.weight,
-                }
-
-            def matrix(self, name, dy, x):
-                engine.matrix_grad(self.params[name], dy, x)
-
-            def vector(self, name, like):
-                return engine.vector_grad(self.params[name])
-
         blocks = model.all_blocks()
+
+        # ---- parameter gather schedule
+        gather_queue: List[Unit] = []
+        gathered: set = set()
+        if comm is not None and self._params_stale:
+            gather_queue = self._forward_unit_order()
+            self._params_stale = False
+        elif comm is None:
+            self.gather_params()
+
+        def need(unit: Unit) -> None:
+            if unit in gather_queue:  # not prefetched in time: pull it now, in stream order
+                gather_queue.remove(unit)
+                comm.launch(comm.ag_task(unit))
+
+        def prefetch_kwargs() -> Dict[str, Dict[str, Any]]:
+            if not gather_queue:
+                return {}
+            nxt = gather_queue.pop(0)
+            return {
+                "att_proj": {"comm": (comm.ag_task(nxt, 0, 2), comm.comm_ctas)},
+                "ff_proj": {"comm": (comm.ag_task(nxt, 1, 2), comm.comm_ctas)},
+            }
+
+        if gather_queue:
+            need(self._unit_of_module_param(t.wte.weight))
         x = k.embedding_fwd(input_ids, t.wte.weight).view(M, mcfg.d_model)
         saved_list: List[Any] = []
         for i, block in enumerate(blocks):
+            if gather_queue:
+                need(self._unit_of_module_param(block.att_proj.weight))
+            gk = prefetch_kwargs() if gather_queue else None
             w = self._weights_of(block)
             if should_checkpoint_block(ac_strategy, i):
-                y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False)
+                y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk)
                 saved_list.append(("ckpt", x))
             else:
-                y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True)
+                y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk)
                 saved_list.append(("full", saved))
             x = y
+        while gather_queue:
+            need(gather_queue[0])
         ln_f = t.ln_f
         xn, rstd_f, mean_f = k.norm_fwd(x, ln_f.weight, None, mcfg.layer_norm_eps, spec.rms)
         head = t.wte.weight if mcfg.weight_tying else t.ff_out.weight
@@ -588,21 +670,59 @@ class FlatShardEngine:
             xn, head, flat_labels, z_mult=z_mult, grad_scale=1.0 / loss_divisor,
             logit_scale=(1.0 / math.sqrt(mcfg.d_model)) if mcfg.scale_logits else 1.0,
             chunk_rows=int(os.environ.get("OLMO_B200_HEAD_CHUNK", "8192")),
-            wgrad=lambda dl, xc: engine.matrix_grad(head, dl, xc),
+            wgrad=lambda dl, xc: self.matrix_grad(head, dl, xc),
         )
         del xn
         dx = k.norm_bwd(dxn, x, ln_f.weight, rstd_f, mean_f, spec.rms,
                         dweight=None if ln_f.weight is None else self.vector_grad(ln_f.weight))
         del dxn, x
+
+        # ---- gradient reduction schedule (last micro-batch only)
+        reduce_now = comm is not None and is_last and not self.reshard
+        ready: List[Unit] = []
+        final_at: Dict[int, int] = {}
+        if reduce_now:
+            comm.begin_grad_epoch()
+            self._grad_epoch_open = True
+            final_at = self._unit_final_points()
+
+            def publish(point: int) -> None:
+                for u in self.units:
+                    if final_at[u.index] == point:
+                        comm.publish_grads(u)
+                        u.published = True  # type: ignore[attr-defined]
+                        ready.append(u)
+
+            publish(len(blocks))
+
+        def reduce_kwargs() -> Optional[Dict[str, Dict[str, Any]]]:
+            if not ready:
+                return None
+            u = ready.pop(0)
+            u.reduced = True  # type: ignore[attr-defined]
+            return {
+                "ff_out_dgrad": {"comm": (comm.rs_task(u, 0, 2), comm.comm_ctas)},
+                "attn_out_dgrad": {"comm": (comm.rs_task(u, 1, 2), comm.comm_ctas)},
+            }
+
         for i in range(len(blocks) - 1, -1, -1):
             kind, payload = saved_list.pop()
             block = blocks[i]
             w = self._weights_of(block)
             if kind == "ckpt":
                 _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True)
-            dx = fb.block_backward(spec, w, payload, dx, cos, sin, Sink(block))
+            dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block),
+                                   gemm_kwargs=reduce_kwargs() if reduce_now else None)
             del payload
+            if reduce_now:
+                publish(i)
         k.embedding_bwd(input_ids, dx, self.grad_view(t.wte.weight)[0])
+        if reduce_now:
+            publish(-1)
+            for u in ready:  # whatever found no GEMM to ride on
+                u.reduced = True  # type: ignore[attr-defined]
+                comm.launch(comm.rs_task(u))
+            ready.clear()
         self.note_microbatch_backward()
         return ce_sum / loss_divisor, z_sum * (z_mult / loss_divisor)
 
@@ -685,6 +805,25 @@ class FlatShardEngine:
                 a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
                 out[s.name] = (max(a - s.offset, 0), max(b - s.offset, 0) if b > a else max(a - s.offset, 0), s.numel)
         return out
+
+
+class _EngineSink:
+    """Gradient sink of the fused backward pass: points each block parameter at its slice of the engine's buffers."""
+
+    def __init__(self, engine: FlatShardEngine, block: OLMoBlock):
+        self.engine = engine
+        self.params = {
+            "att_proj": block.att_proj.weight, "attn_out": block.attn_out.weight, "ff_proj": block.ff_proj.weight,
+            "ff_out": block.ff_out.weight, "attn_norm": block.attn_norm.weight, "ff_norm": block.ff_norm.weight,
+            "q_norm": None if block.q_norm is None else block.q_norm.weight,
+            "k_norm": None if block.k_norm is None else block.k_norm.weight,
+        }
+
+    def matrix(self, name: str, dy: torch.Tensor, x: torch.Tensor) -> None:
+        self.engine.matrix_grad(self.params[name], dy, x)
+
+    def vector(self, name: str, like: torch.Tensor) -> torch.Tensor:
+        return self.engine.vector_grad(self.params[name])
 
 
 class ShardedModel(nn.Module):

@@ -1,0 +1,202 @@
+"""
+Peer-memory runtime of the flat-shard engine: symmetric buffers, flags, and the CommTask descriptors consumed by the
+kernels in ``csrc/comm.cuh``.
+
+Every rank allocates, in CUDA symmetric memory (``torch.distributed._symmetric_memory``: VMM allocations whose handles
+are exchanged once over the process group's store and mapped into every peer),
+
+* ``full_all``   the compute-dtype copy of every unit, end to end.  A rank's own shard of a unit lives *inside* this
+                 buffer, so an all-gather only has to pull the W-1 foreign regions from the peers' buffers;
+* ``gfull_all``  the fp32 full-size gradient accumulators, from which each peer pulls and sums its slice;
+* ``ctrl``       int32 words: ``[0]`` parameter epoch, ``[1+u]`` gradient epoch of unit ``u``, then the slot area of the
+                 scalar all-reduce.
+
+Ordering protocol (all flags are monotone epochs, all waits bounded):
+
+* after its optimizer step a rank publishes ``param_epoch``; a peer's all-gather reads that rank's shard only once the
+  epoch has arrived;
+* after the last micro-batch's backward pass of a unit a rank publishes ``grad_epoch[u]``; a peer reduces its slice of
+  unit ``u`` only once every rank has published it;
+* the scalar all-reduce of Σg² at the end of the step is also the barrier that makes it safe to overwrite shards and
+  zero gradient accumulators for the next step: no rank gets past it before every rank has finished its reads.
+"""
+from __future__ import annotations
+
+import ctypes
+import logging
+import os
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ..ops import check, lib, ptr, status_tensor, stream_ptr
+
+__all__ = ["CommTask", "PeerComm", "COMM_ALL_GATHER", "COMM_REDUCE_SCATTER"]
+
+log = logging.getLogger(__name__)
+
+COMM_NONE, COMM_ALL_GATHER, COMM_REDUCE_SCATTER = 0, 1, 2
+MAX_WORLD = 8
+
+
+class CommTask(ctypes.Structure):
+    """Mirror of ``ob::CommTask`` (csrc/comm.cuh)."""
+
+    _fields_ = [
+        ("kind", ctypes.c_int),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("wait_value", ctypes.c_int),
+        ("elems", ctypes.c_longlong),
+        ("dst_peer_stride", ctypes.c_longlong),
+        ("src", ctypes.c_void_p * MAX_WORLD),
+        ("wait_flags", ctypes.c_void_p * MAX_WORLD),
+        ("dst", ctypes.c_void_p),
+        ("scale", ctypes.c_float),
+        ("sumsq_partials", ctypes.c_void_p),
+        ("status", ctypes.c_void_p),
+        ("wait_cycles", ctypes.c_longlong),
+    ]
+
+
+class PeerComm:
+    def __init__(self, engine, group) -> None:
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.engine = engine
+        self.world, self.rank = engine.shard_world, engine.shard_rank
+        assert self.world <= MAX_WORLD
+        dev = engine.device
+        assert ctypes.sizeof(CommTask) == lib().ob_comm_task_size(), "CommTask layout mismatch"
+        total = sum(u.numel for u in engine.units)
+        self.bases: List[int] = []
+        off = 0
+        for u in engine.units:
+            self.bases.append(off)
+            off += u.numel
+        self.full_all = symm_mem.empty(total, dtype=engine.compute_dtype, device=dev)
+        self.h_full = symm_mem.rendezvous(self.full_all, group)
+        self.gfull_all = symm_mem.empty(total, dtype=torch.float32, device=dev)
+        self.h_gfull = symm_mem.rendezvous(self.gfull_all, group)
+        self.n_units = len(engine.units)
+        self.slot_words = lib().ob_scalar_slots_bytes() // 4
+        self.slot_off = (1 + self.n_units + 15) // 16 * 16
+        self.ctrl = symm_mem.empty(self.slot_off + self.slot_words, dtype=torch.int32, device=dev)
+        self.h_ctrl = symm_mem.rendezvous(self.ctrl, group)
+        self.full_all.zero_()
+        self.gfull_all.zero_()
+        self.ctrl.zero_()
+        self.full_ptrs = [int(p) for p in self.h_full.buffer_ptrs]
+        self.gfull_ptrs = [int(p) for p in self.h_gfull.buffer_ptrs]
+        self.ctrl_ptrs = [int(p) for p in self.h_ctrl.buffer_ptrs]
+        self.slot_ptrs_dev = torch.tensor([p + 4 * self.slot_off for p in self.ctrl_ptrs], dtype=torch.int64, device=dev)
+        self.param_epoch = 0
+        self.grad_epoch = 0
+        self.scalar_epoch = 0
+        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "20"))
+        self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "64"))
+        ms = float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000"))
+        self.wait_cycles = int(ms * 1.9e6)
+        self._scalar_out = torch.zeros(1, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        self.group = group
+
+    @classmethod
+    def create(cls, engine) -> Optional["PeerComm"]:
+        if engine.shard_world != engine.world:
+            log.info("peer-memory collectives cover one shard group spanning the whole job; hybrid sharding uses NCCL")
+            return None
+        return cls(engine, dist.group.WORLD)
+
+    # ------------------------------------------------------------------------------- buffers
+    def full_view(self, unit_index: int, numel: int) -> torch.Tensor:
+        b = self.bases[unit_index]
+        return self.full_all[b : b + numel]
+
+    def gfull_view(self, unit_index: int, numel: int) -> torch.Tensor:
+        b = self.bases[unit_index]
+        return self.gfull_all[b : b + numel]
+
+    # --------------------------------------------------------------------------------- tasks
+    def _base_task(self, kind: int) -> CommTask:
+        t = CommTask()
+        t.kind, t.world, t.rank = kind, self.world, self.rank
+        t.status = status_tensor(self.engine.device).data_ptr()
+        t.wait_cycles = self.wait_cycles
+        t.sumsq_partials = None
+        return t
+
+    def ag_task(self, unit, part: int = 0, parts: int = 1) -> CommTask:
+        """All-gather of slice ``part`` of ``parts`` of every foreign shard of ``unit`` into the local ``full`` buffer."""
+        S = unit.shard_size
+        esz = self.full_all.element_size()
+        step = (S // parts) // 8 * 8
+        a = part * step
+        b = S if part == parts - 1 else a + step
+        t = self._base_task(COMM_ALL_GATHER)
+        t.elems, t.dst_peer_stride = b - a, S
+        base = self.bases[unit.index]
+        for p in range(self.world):
+            t.src[p] = self.full_ptrs[p] + (base + p * S + a) * esz
+            t.wait_flags[p] = self.ctrl_ptrs[p]  # word 0: that rank's parameter epoch
+        t.dst = self.full_ptrs[self.rank] + (base + a) * esz
+        t.wait_value = self.param_epoch
+        return t
+
+    def rs_task(self, unit, part: int = 0, parts: int = 1) -> CommTask:
+        """Reduce-scatter of slice ``part`` of this rank's gradient shard of ``unit`` (sum over ranks, scaled, added)."""
+        S = unit.shard_size
+        step = (S // parts) // 4 * 4
+        a = part * step
+        b = S if part == parts - 1 else a + step
+        t = self._base_task(COMM_REDUCE_SCATTER)
+        t.elems = b - a
+        base = self.bases[unit.index]
+        for p in range(self.world):
+            t.src[p] = self.gfull_ptrs[p] + (base + self.rank * S + a) * 4
+            t.wait_flags[p] = self.ctrl_ptrs[p] + 4 * (1 + unit.index)
+        t.dst = unit.grad.data_ptr() + a * 4
+        t.scale = 1.0 / self.engine.world
+        t.wait_value = self.grad_epoch
+        return t
+
+    # ------------------------------------------------------------------------------ launches
+    def launch(self, task: CommTask, ctas: Optional[int] = None) -> None:
+        check(lib().ob_comm_launch(ctypes.byref(task), ctypes.c_int(ctas or self.standalone_ctas), stream_ptr()), "ob_comm_launch")
+
+    def signal(self, word: int, value: int) -> None:
+        check(lib().ob_signal(ctypes.c_void_p(self.ctrl_ptrs[self.rank] + 4 * word), ctypes.c_int(value), stream_ptr()), "ob_signal")
+
+    def publish_params(self) -> None:
+        """Call after the optimizer step has been enqueued: peers may now read this rank's shards."""
+        self.param_epoch += 1
+        self.signal(0, self.param_epoch)
+
+    def begin_grad_epoch(self) -> None:
+        self.grad_epoch += 1
+
+    def publish_grads(self, unit) -> None:
+        self.signal(1 + unit.index, self.grad_epoch)
+
+    def all_gather_units(self, units: Sequence) -> None:
+        for u in units:
+            self.launch(self.ag_task(u))
+
+    def reduce_scatter_units(self, units: Sequence, scale: float) -> None:
+        del scale  # tasks carry 1/world
+        for u in units:
+            self.launch(self.rs_task(u))
+
+    def all_reduce_scalar_(self, value: torch.Tensor) -> torch.Tensor:
+        """In-place sum of a one-element fp32 tensor over all ranks; also an execution barrier on the stream."""
+        self.scalar_epoch += 1
+        rc = lib().ob_allreduce_scalar(
+            ptr(value), ptr(self.slot_ptrs_dev), ctypes.c_void_p(self.ctrl_ptrs[self.rank] + 4 * self.slot_off), ptr(self._scalar_out),
+            ctypes.c_int(self.rank), ctypes.c_int(self.world), ctypes.c_int(self.scalar_epoch),
+            ptr(status_tensor(self.engine.device)), ctypes.c_longlong(self.wait_cycles), stream_ptr(),
+        )
+        check(rc, "ob_allreduce_scalar")
+        value.copy_(self._scalar_out)
+        return value

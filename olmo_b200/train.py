@@ -566,6 +566,7 @@ class Trainer:
                     mb["input_ids"], self._labels_aligned(mb), float(batch_size_in_tokens),
                     z_mult=1e-4 if self.cfg.softmax_auxiliary_loss else 0.0,
                     ac_strategy=self.model.activation_checkpointing_strategy,
+                    is_last=idx == n - 1,
                 )
                 ce_batch_loss += ce
                 if z_batch_loss is not None:

@@ -1,0 +1,88 @@
+"""Worker for the multi-GPU tests: trains a small OLMo-2 style model for a few steps on WORLD_SIZE ranks and lets rank 0
+save the full fp32 weights.  Launched with ``python -m torch.distributed.run`` by ``test_multi_gpu.py``."""
+import argparse
+import os
+import sys
+import tempfile
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out", required=True)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--global-batch", type=int, default=8)
+    ap.add_argument("--fused-comm", type=int, default=1)
+    ap.add_argument("--strategy", default="FULL_SHARD")
+    args = ap.parse_args()
+    os.environ["OLMO_B200_FUSED_COMM"] = str(args.fused_comm)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+
+    from olmo_b200 import ops
+    from olmo_b200.config import (
+        DistributedStrategy, FSDPConfig, FSDPPrecision, FSDPWrapStrategy, LayerNormType, ModelConfig, OptimizerConfig,
+        OptimizerType, SchedulerConfig, SchedulerType, ShardingStrategy, TrainConfig,
+    )
+    from olmo_b200.launch import build_model_and_engine, derive_batch_sizes
+    from olmo_b200.optim import build_optimizer
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device)
+
+    model = ModelConfig(
+        d_model=256, n_heads=2, n_layers=3, mlp_hidden_size=1024, weight_tying=False, rope=True, rope_theta=500000,
+        flash_attention=True, attention_dropout=0.0, residual_dropout=0.0, embedding_dropout=0.0, include_bias=False,
+        layer_norm_type=LayerNormType.rms, layer_norm_with_affine=True, layer_norm_eps=1e-6, bias_for_layer_norm=False,
+        attention_layer_norm=True, norm_after=True, max_sequence_length=256, vocab_size=500, embedding_size=512,
+        eos_token_id=499, pad_token_id=499, init_device="meta", init_std=0.05,
+    )
+    cfg = TrainConfig(
+        model=model, optimizer=OptimizerConfig(name=OptimizerType.adamw, learning_rate=1e-3, eps=1e-8, weight_decay=0.1),
+        scheduler=SchedulerConfig(name=SchedulerType.constant), precision="amp_bf16",
+        distributed_strategy=DistributedStrategy.fsdp,
+        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy[args.strategy], wrapping_strategy=FSDPWrapStrategy.by_block_and_size, precision=FSDPPrecision.mixed),
+        global_train_batch_size=args.global_batch, device_train_microbatch_size=2, max_grad_norm=1.0, save_folder=tempfile.mkdtemp(),
+    )
+    derive_batch_sizes(cfg, world)
+    dist_model = build_model_and_engine(cfg, device)
+    engine = dist_model.engine
+    assert engine.fused
+    if world > 1 and args.fused_comm and args.strategy == "FULL_SHARD":
+        assert engine.comm is not None, "peer-memory collectives should be active"
+    optim = build_optimizer(cfg, dist_model)
+
+    db = cfg.device_train_batch_size
+    gen = torch.Generator().manual_seed(1234)
+    all_ids = torch.randint(0, 500, (args.steps, args.global_batch, 256), generator=gen)
+    norms = []
+    for step in range(args.steps):
+        engine.zero_grad()
+        mine = all_ids[step, rank * db : (rank + 1) * db].to(device)
+        mbs = mine.split(cfg.device_train_microbatch_size)
+        for i, mb in enumerate(mbs):
+            labels = torch.nn.functional.pad(mb[:, 1:], (0, 1), value=-100)
+            engine.train_microbatch(mb, labels, float(mine.numel()), z_mult=1e-4, is_last=i == len(mbs) - 1)
+        m = optim.clip_grads_and_collect_metrics(step + 1, collect_param_metrics=False, process_group=engine.process_group)
+        norms.append(float(m["total_grad_norm"]))
+        optim.step()
+    ops.check_status()
+    state = engine.full_model_state_dict(rank0_only=True, cpu=True)
+    if rank == 0:
+        torch.save({"state": state, "norms": norms}, args.out)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
