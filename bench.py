@@ -52,6 +52,7 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--device-batch", type=int, default=None, help="sequences per GPU per optimizer step (default: official global batch / 8)")
     p.add_argument("--activation-checkpointing", default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--n-layers", type=int, default=None, help="profiling aid: fewer blocks than the preset (the result is then marked reduced)")
     return p.parse_args()
 
 
@@ -65,7 +66,7 @@ def make_train_config(args, world: int):
     ps = PRESETS[args.model]
     olmo2 = ps["flavour"] == "olmo2"
     model = ModelConfig(
-        d_model=ps["d_model"], n_heads=ps["n_heads"], n_layers=ps["n_layers"], mlp_hidden_size=ps["mlp_hidden_size"],
+        d_model=ps["d_model"], n_heads=ps["n_heads"], n_layers=args.n_layers or ps["n_layers"], mlp_hidden_size=ps["mlp_hidden_size"],
         weight_tying=False, alibi=False, rope=True, rope_theta=500000 if olmo2 else 10000, flash_attention=True,
         attention_dropout=0.0, include_bias=False, layer_norm_type=LayerNormType.rms if olmo2 else LayerNormType.default,
         layer_norm_with_affine=olmo2, layer_norm_eps=1e-6 if olmo2 else 1e-5, bias_for_layer_norm=False,
@@ -247,7 +248,8 @@ def run_ours(args) -> dict:
         "mfu_of_measured_sustained": (per_gpu * flops_per_token / (peaks["bf16_tflops_sustained"] * 1e12)) if peaks.get("bf16_tflops_sustained") else None,
         "flops_per_token": flops_per_token, "params": n_params, "final_loss": loss,
         "config": {
-            "model": args.model, "global_batch": device_batch * world, "seq_len": args.seq_len,
+            "model": args.model if not args.n_layers else f"{args.model} REDUCED to {args.n_layers} layers (profiling only)",
+            "global_batch": device_batch * world, "seq_len": args.seq_len,
             "micro_batch": ps["microbatch"], "grad_accum": cfg.device_train_grad_accum,
             "parallelism": f"fsdp{world}" if world > 1 else "single-gpu flat-shard engine",
             "activation_checkpointing": args.activation_checkpointing or "none",

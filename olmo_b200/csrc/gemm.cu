@@ -34,7 +34,8 @@ constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int CHUNK_BYTES = 64 * BK * 2;  // one 64(mn) x 64(k) box of an MN-major operand
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 192;       // six role warps
+constexpr int NUM_THREADS_COMM = 512;  // launches that carry communication CTAs: more warps to hide NVLink latency
 constexpr int TMEM_COLS = 512;
 constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
 constexpr int GROUP_M = 8;
@@ -54,7 +55,7 @@ __device__ __forceinline__ TileCoord tile_coord(int t, int tiles_m, int tiles_n)
 }
 
 template <int A_MN, int B_MN, int EPI>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(NUM_THREADS_COMM, 1)
 gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                  void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
                  const int* __restrict__ b_ready, int rows_per_flag, int ready_value, int* __restrict__ status,
@@ -202,7 +203,7 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         }
       }
     }
-  } else {
+  } else if (warp < 6) {
     // --------------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter+32) are the ones this warp may read
     int acc = 0;
@@ -348,7 +349,7 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, co
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   if (comm_ctas < 0 || comm_ctas >= num_sms) return -12;
   const int gemm_ctas = tiles < num_sms - comm_ctas ? tiles : num_sms - comm_ctas;
-  kern<<<gemm_ctas + comm_ctas, NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc,
+  kern<<<gemm_ctas + comm_ctas, comm_ctas > 0 ? NUM_THREADS_COMM : NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc,
                                                                   vec_ok, b_ready, rows_per_flag, ready_value, status,
                                                                   comm_task, comm_ctas);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
