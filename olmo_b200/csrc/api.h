@@ -26,6 +26,11 @@ int ob_gemm_bf16_comm(const void* A, const void* B, void* C, const void* R, int 
                       int a_mn_major, int b_mn_major, int epi, int* status, int num_sms, const void* task, int comm_ctas,
                       cudaStream_t stream);
 
+// ---- attention.cu
+int ob_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int T, int H, int Hkv, int q_sb,
+                     int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh, int o_sb, int o_st,
+                     int o_sh, float scale, int causal, int* status, cudaStream_t stream);
+
 // ---- comm.cu (peer-memory collectives; `task` points at an ob::CommTask, see comm.cuh)
 int ob_comm_task_size(void);
 int ob_comm_launch(const void* task, int nctas, cudaStream_t stream);

@@ -1,0 +1,346 @@
+// Causal / full flash-attention forward for head dimension 128 on tcgen05 tensor cores.
+//
+// One CTA computes a 128-row query tile of one (batch, head) against its key/value tiles of 128 rows:
+//   warps 0..7  softmax: thread (row r, half h) owns row r and 64 of the 128 columns of each score tile
+//   warp 8      TMA producer (Q once; K and V double buffered; 128B-swizzled tiles of 2 x [128 rows x 64 elements])
+//   warp 9      MMA issuer   S = Q Kt (tcgen05, both operands K-major)   and   Ot = P V (V is the MN-major operand)
+// TMEM: two score accumulators (2 x 128 columns) and two output accumulators (2 x 128 columns), so the tensor core
+// works on Q Kt of tile j+1 while the softmax warps are busy with tile j.  Each P V product goes to a fresh
+// accumulator; the running output lives in registers and is rescaled there (O = O * alpha + Ot), which avoids
+// read-modify-write of TMEM.  P is handed to the tensor core through shared memory in the 128B-swizzled K-major layout.
+//
+// Layout of operands in global memory: (B, T, heads, 128) with arbitrary row pitch (views into fused QKV buffers are
+// fine); grouped-query attention maps query head h to key/value head h / (H / Hkv).  T must be a multiple of 128.
+// Outputs: O (B, T, H, 128) bf16 and the log-sum-exp (B, H, T) fp32 in natural-log units of the scaled scores.
+#include "common.cuh"
+#include "api.h"
+
+namespace ob {
+
+int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                            uint32_t box_inner, uint32_t box_outer);
+
+namespace {
+
+constexpr int AT_THREADS = 320;
+constexpr int AT_TILE_BYTES = 128 * 128 * 2;  // 32 KiB: one 128 x 128 bf16 tile = two 64-column halves
+constexpr int AT_HALF_BYTES = 128 * 64 * 2;   // 16 KiB
+constexpr int AT_SMEM = 1024 + 6 * AT_TILE_BYTES + 4096;  // alignment slack + tiles + barriers and row-statistic exchange (3.3 KiB)
+
+struct AttnParams {
+  bf16* o;
+  float* lse;
+  int B, T, H, Hkv;
+  long long o_stride_b, o_stride_t, o_stride_h;
+  float scale_log2;  // softmax scale * log2(e)
+  int causal;
+  int* status;
+};
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + AT_TILE_BYTES;       // 2 stages
+  uint8_t* sV = sK + 2 * AT_TILE_BYTES;   // 2 stages
+  uint8_t* sP = sV + 2 * AT_TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + AT_TILE_BYTES);
+  uint64_t* q_full = bars;          // 1
+  uint64_t* k_full = bars + 1;      // 2
+  uint64_t* k_empty = bars + 3;     // 2
+  uint64_t* v_full = bars + 5;      // 2
+  uint64_t* v_empty = bars + 7;     // 2
+  uint64_t* s_full = bars + 9;      // 2
+  uint64_t* s_empty = bars + 11;    // 2
+  uint64_t* o_full = bars + 13;     // 2
+  uint64_t* o_empty = bars + 15;    // 2
+  uint64_t* p_full = bars + 17;     // 1
+  uint64_t* x_bar = bars + 18;      // 1: exchange of row statistics between the two column halves
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* smax = reinterpret_cast<float*>(tmem_slot + 4);  // [2 parities][2 halves][128]
+  float* ssum = smax + 512;                               // [2 halves][128]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_qt = p.T / 128;
+  // heavy (late) query tiles first so that the tail of the grid is made of short CTAs
+  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x) / (p.B * p.H);
+  const int bh = static_cast<int>(blockIdx.x) % (p.B * p.H);
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.Hkv);
+  const int n_kv = p.causal ? qt + 1 : n_qt;
+  const int row0 = b * p.T + qt * 128;  // first query row in the flattened (B*T) index space
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 256);
+      mbar_init(&o_full[s], 1);
+      mbar_init(&o_empty[s], 256);
+    }
+    mbar_init(p_full, 256);
+    mbar_init(x_bar, 256);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 8) {
+    // ------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_v);
+      mbar_expect_tx(q_full, AT_TILE_BYTES);
+      tma_load_2d(sQ, &tm_q, q_full, h * 128, row0);
+      tma_load_2d(sQ + AT_HALF_BYTES, &tm_q, q_full, h * 128 + 64, row0);
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        const int kv_row = b * p.T + j * 128;
+        if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
+        mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
+        tma_load_2d(sK + s * AT_TILE_BYTES, &tm_k, &k_full[s], hk * 128, kv_row);
+        tma_load_2d(sK + s * AT_TILE_BYTES + AT_HALF_BYTES, &tm_k, &k_full[s], hk * 128 + 64, kv_row);
+        if (!mbar_wait(&v_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
+        mbar_expect_tx(&v_full[s], AT_TILE_BYTES);
+        tma_load_2d(sV + s * AT_TILE_BYTES, &tm_v, &v_full[s], hk * 128, kv_row);
+        tma_load_2d(sV + s * AT_TILE_BYTES + AT_HALF_BYTES, &tm_v, &v_full[s], hk * 128 + 64, kv_row);
+      }
+      if (*abort_flag) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000LL) {
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // --------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = make_idesc_bf16(128, 128, 0, 0);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(128, 128, 0, 1);
+      const uint32_t q_addr = smem_u32(sQ);
+      const uint32_t p_addr = smem_u32(sP);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
+
+      auto issue_pv = [&](int i) -> bool {
+        const int s = i & 1;
+        const uint32_t ph = (i >> 1) & 1;
+        if (!mbar_wait(&v_full[s], ph, abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(p_full, static_cast<uint32_t>(i & 1), abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
+        if (!mbar_wait(&o_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
+        tc_fence_after();
+        const uint32_t v_addr = smem_u32(sV + s * AT_TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + 256u + static_cast<uint32_t>(s) * 128u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          // A = P: K-major, 64-column halves;  B = V: MN-major, 16 kv rows per step = 2 KiB, 64-wide d halves 16 KiB apart
+          const uint64_t a_desc = make_smem_desc_sw128(p_addr + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024);
+          const uint64_t b_desc = make_smem_desc_sw128(v_addr + k * 2048, AT_HALF_BYTES, 1024);
+          umma_f16_ss(d_tmem, a_desc, b_desc, idesc_pv, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&o_full[s]);
+        umma_commit(&v_empty[s]);
+        return true;
+      };
+
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_full[s], ph, abort_flag, p.status, ST_TIMEOUT_MMA)) { ok = false; break; }
+        if (!mbar_wait(&s_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t k_addr = smem_u32(sK + s * AT_TILE_BYTES);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(s) * 128u;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint64_t a_desc = make_smem_desc_sw128(q_addr + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024);
+          const uint64_t b_desc = make_smem_desc_sw128(k_addr + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024);
+          umma_f16_ss(d_tmem, a_desc, b_desc, idesc_qk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[s]);
+        umma_commit(&k_empty[s]);
+        if (j > 0) ok = issue_pv(j - 1);
+      }
+      if (ok) issue_pv(n_kv - 1);
+    }
+  } else {
+    // ------------------------------------------------------------------------------ softmax
+    const int quarter = warp & 3;
+    const int half = warp >> 2;
+    const int row = quarter * 32 + lane;           // query row inside the tile == TMEM lane
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int col0 = half * 64;
+    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
+    float o_acc[64];
+#pragma unroll
+    for (int c = 0; c < 64; ++c) o_acc[c] = 0.f;
+    bool ok = true;
+
+    auto fold = [&](int i, float alpha) -> bool {
+      const int s = i & 1;
+      if (!mbar_wait(&o_full[s], static_cast<uint32_t>((i >> 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) return false;
+      tc_fence_after();
+      __syncwarp();
+      const uint32_t t_addr = tmem_base + lane_addr + 256u + static_cast<uint32_t>(s) * 128u + static_cast<uint32_t>(col0);
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_addr + cc * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) o_acc[cc * 32 + c] = o_acc[cc * 32 + c] * alpha + __uint_as_float(r[c]);
+      }
+      tc_fence_before();
+      mbar_arrive(&o_empty[s]);
+      return true;
+    };
+
+    for (int j = 0; j < n_kv; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], static_cast<uint32_t>((j >> 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      __syncwarp();
+      float sc[64];
+      {
+        const uint32_t t_addr = tmem_base + lane_addr + static_cast<uint32_t>(s) * 128u + static_cast<uint32_t>(col0);
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(t_addr, r0);
+        tmem_ld_32x32b_x32(t_addr + 32, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          sc[c] = __uint_as_float(r0[c]) * p.scale_log2;
+          sc[32 + c] = __uint_as_float(r1[c]) * p.scale_log2;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      if (p.causal && j == qt) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (col0 + c > row) sc[c] = -INFINITY;
+      }
+      float pm = sc[0];
+#pragma unroll
+      for (int c = 1; c < 64; ++c) pm = fmaxf(pm, sc[c]);
+      float* mx = smax + (j & 1) * 256;
+      mx[half * 128 + row] = pm;
+      mbar_arrive(x_bar);
+      if (!mbar_wait(x_bar, static_cast<uint32_t>(j & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      const float m_new = fmaxf(m_run, fmaxf(mx[row], mx[128 + row]));
+      const float alpha = exp2f(m_run - m_new);
+      float ls = 0.f;
+      uint32_t pk[32];
+#pragma unroll
+      for (int c = 0; c < 32; ++c) {
+        const float e0 = exp2f(sc[2 * c] - m_new);
+        const float e1 = exp2f(sc[2 * c + 1] - m_new);
+        pk[c] = pack_bf16x2(e0, e1);
+        // the row sum uses the rounded values that the tensor core will multiply with V
+        const float2 rr = unpack_bf16x2(pk[c]);
+        ls += rr.x + rr.y;
+      }
+      l_run = l_run * alpha + ls;
+      m_run = m_new;
+      if (j > 0) {
+        if (!fold(j - 1, alpha_prev)) { ok = false; break; }  // also guarantees that P V (j-1) has finished reading sP
+      }
+      alpha_prev = alpha;
+      // P tile -> shared memory, K-major with 128-byte swizzle: 16-byte chunk index XOR (row mod 8)
+      uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 v4 = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = v4;
+      }
+      fence_proxy_async();
+      mbar_arrive(p_full);
+    }
+    if (ok) ok = fold(n_kv - 1, alpha_prev);
+    // total row sum = sum of the two halves
+    ssum[half * 128 + row] = l_run;
+    if (ok) {
+      mbar_arrive(x_bar);
+      ok = mbar_wait(x_bar, static_cast<uint32_t>(n_kv & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE);
+    }
+    if (ok) {
+      const float l_tot = ssum[row] + ssum[128 + row];
+      const float inv = 1.f / l_tot;
+      const long long t_idx = static_cast<long long>(qt) * 128 + row;
+      bf16* orow = p.o + b * p.o_stride_b + t_idx * p.o_stride_t + h * p.o_stride_h + col0;
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        uint4 o4;
+        o4.x = pack_bf16x2(o_acc[v * 8 + 0] * inv, o_acc[v * 8 + 1] * inv);
+        o4.y = pack_bf16x2(o_acc[v * 8 + 2] * inv, o_acc[v * 8 + 3] * inv);
+        o4.z = pack_bf16x2(o_acc[v * 8 + 4] * inv, o_acc[v * 8 + 5] * inv);
+        o4.w = pack_bf16x2(o_acc[v * 8 + 6] * inv, o_acc[v * 8 + 7] * inv);
+        *reinterpret_cast<uint4*>(orow + v * 8) = o4;
+      }
+      if (half == 0)
+        p.lse[(static_cast<long long>(b) * p.H + h) * p.T + t_idx] = (m_run + log2f(l_tot)) * 0.6931471805599453f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+}  // namespace
+}  // namespace ob
+
+// q, k, v, o: (B, T, heads, 128) bf16 with element strides (batch, token, head); the last dimension is contiguous.
+// The token stride is the row pitch; batch stride must equal T * token stride (rows of a batch are contiguous in the
+// flattened B*T index space) and head stride must be 128.
+extern "C" int ob_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int T, int H, int Hkv,
+                                int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh,
+                                int o_sb, int o_st, int o_sh, float scale, int causal, int* status, cudaStream_t stream) {
+  using namespace ob;
+  if (B <= 0 || T <= 0) return 0;
+  if (T % 128 != 0 || H % Hkv != 0) return -1;
+  if (q_sh != 128 || k_sh != 128 || v_sh != 128) return -2;
+  if (q_sb != T * q_st || k_sb != T * k_st || v_sb != T * v_st) return -3;
+  if ((o_st % 8) != 0 || (o_sh % 8) != 0 || (reinterpret_cast<uintptr_t>(o) & 15) != 0) return -4;
+  CUtensorMap tq, tk, tv;
+  int rc = make_tensor_map_bf16_2d(&tq, q, (uint64_t)H * 128, (uint64_t)B * T, (uint64_t)q_st, 64, 128);
+  if (rc != 0) return rc;
+  rc = make_tensor_map_bf16_2d(&tk, k, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)k_st, 64, 128);
+  if (rc != 0) return rc;
+  rc = make_tensor_map_bf16_2d(&tv, v, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)v_st, 64, 128);
+  if (rc != 0) return rc;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM) != cudaSuccess) return -10;
+    configured = true;
+  }
+  AttnParams p;
+  p.o = reinterpret_cast<bf16*>(o);
+  p.lse = lse;
+  p.B = B; p.T = T; p.H = H; p.Hkv = Hkv;
+  p.o_stride_b = o_sb; p.o_stride_t = o_st; p.o_stride_h = o_sh;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal;
+  p.status = status;
+  const int grid = B * H * (T / 128);
+  attn_fwd_kernel<<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}

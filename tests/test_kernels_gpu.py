@@ -231,3 +231,23 @@ def test_adamw_and_sumsq():
     out = torch.zeros(1, device="cuda")
     k.sumsq(g, out)
     assert math.isclose(out.item(), g.double().square().sum().item(), rel_tol=1e-4)
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("H,Hkv,T", [(4, 4, 512), (4, 2, 256), (2, 1, 1024)])
+def test_native_attention_forward(causal, H, Hkv, T):
+    from olmo_b200.ops import attention as A
+    from olmo_b200.ops import attention_native as N
+
+    B, D = 2, 128
+    # operands are strided views into one fused buffer, as in the model
+    fused = _rand(B * T, (H + 2 * Hkv) * D)
+    q = fused[:, : H * D].view(B, T, H, D)
+    k = fused[:, H * D : (H + Hkv) * D].view(B, T, Hkv, D)
+    v = fused[:, (H + Hkv) * D :].view(B, T, Hkv, D)
+    assert N.supports(q, k, causal, 0.0, False)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = N.forward(q, k, v, causal, scale)
+    ro, rlse = A.math_attention_forward(q, k, v, causal, scale)
+    _close(o, ro, rtol=2e-2, atol=2e-2)
+    assert torch.allclose(lse, rlse, rtol=1e-3, atol=2e-3), (lse - rlse).abs().max().item()
