@@ -344,3 +344,353 @@ extern "C" int ob_attention_fwd(const void* q, const void* k, const void* v, voi
   attn_fwd_kernel<<<grid, AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, p);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
+
+// =====================================================================================================================
+// Backward.  One CTA owns a 128-row key/value tile of one (batch, kv head) and walks over the query tiles that attend
+// to it (all query heads of the group).  Per query tile:
+//     S  = Q Kt,  dP = dO Vt                         (tensor core -> TMEM)
+//     P  = exp2(S * c - lse),  dS = P * (dP - delta) * scale      (256 threads, written to shared memory as bf16)
+//     dV += Pt dO,  dK += dSt Q,  dQ = dS K          (tensor core; dV and dK accumulate in TMEM over the whole walk)
+//     dQ -> fp32 global accumulator with vector reductions (other key tiles add to the same rows)
+// `delta` = rowsum(dO * O) comes from a small pre-pass; a post-pass converts the dQ accumulator to bf16.
+// The same shared-memory tiles serve as K-major and as MN-major operands (two descriptors over one swizzled tile).
+// TMEM columns: [0,128) S then dQ, [128,256) dP, [256,384) dV, [384,512) dK.
+// =====================================================================================================================
+namespace ob {
+namespace {
+
+struct AttnBwdParams {
+  const float* lse;    // (B, H, T) natural log
+  const float* delta;  // (B, H, T)
+  float* dq_acc;       // (B, T, H, 128) fp32, zeroed
+  bf16* dk;
+  bf16* dv;
+  long long dk_sb, dk_st, dk_sh, dv_sb, dv_st, dv_sh;
+  int B, T, H, Hkv;
+  float scale, scale_log2;
+  int causal;
+  int* status;
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+__global__ void __launch_bounds__(AT_THREADS, 1)
+attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                const AttnBwdParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + AT_TILE_BYTES;
+  uint8_t* sQ = sV + AT_TILE_BYTES;
+  uint8_t* sdO = sQ + AT_TILE_BYTES;
+  uint8_t* sP = sdO + AT_TILE_BYTES;
+  uint8_t* sdS = sP + AT_TILE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + AT_TILE_BYTES);
+  uint64_t* kv_full = bars;       // K and V landed
+  uint64_t* qdo_full = bars + 1;  // Q and dO of this iteration landed
+  uint64_t* qdo_empty = bars + 2; // tensor core finished reading Q, dO, P, dS of this iteration
+  uint64_t* sdp_full = bars + 3;  // S and dP complete
+  uint64_t* pds_full = bars + 4;  // P and dS written (256 arrivals)
+  uint64_t* dq_full = bars + 5;   // dQ complete (and dV, dK updated)
+  uint64_t* s_free = bars + 6;    // dQ read out of TMEM (256 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_t = p.T / 128;
+  const int jt = static_cast<int>(blockIdx.x) / (p.B * p.Hkv);  // kv tile; low tiles (most work when causal) first
+  const int bh = static_cast<int>(blockIdx.x) % (p.B * p.Hkv);
+  const int b = bh / p.Hkv, hk = bh % p.Hkv;
+  const int group = p.H / p.Hkv;
+  const int i0 = p.causal ? jt : 0;
+  const int per_head = n_t - i0;
+  const int n_it = per_head * group;
+  const int kv_row = b * p.T + jt * 128;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(sdp_full, 1);
+    mbar_init(pds_full, 256);
+    mbar_init(dq_full, 1);
+    mbar_init(s_free, 256);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 8) {
+    if (lane == 0) {
+      prefetch_tensormap(&tm_q);
+      prefetch_tensormap(&tm_k);
+      prefetch_tensormap(&tm_v);
+      prefetch_tensormap(&tm_do);
+      mbar_expect_tx(kv_full, 2 * AT_TILE_BYTES);
+      tma_load_2d(sK, &tm_k, kv_full, hk * 128, kv_row);
+      tma_load_2d(sK + AT_HALF_BYTES, &tm_k, kv_full, hk * 128 + 64, kv_row);
+      tma_load_2d(sV, &tm_v, kv_full, hk * 128, kv_row);
+      tma_load_2d(sV + AT_HALF_BYTES, &tm_v, kv_full, hk * 128 + 64, kv_row);
+      for (int it = 0; it < n_it; ++it) {
+        const int h = hk * group + it / per_head;
+        const int qrow = b * p.T + (i0 + it % per_head) * 128;
+        if (!mbar_wait(qdo_empty, static_cast<uint32_t>((it & 1) ^ 1), abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
+        mbar_expect_tx(qdo_full, 2 * AT_TILE_BYTES);
+        tma_load_2d(sQ, &tm_q, qdo_full, h * 128, qrow);
+        tma_load_2d(sQ + AT_HALF_BYTES, &tm_q, qdo_full, h * 128 + 64, qrow);
+        tma_load_2d(sdO, &tm_do, qdo_full, h * 128, qrow);
+        tma_load_2d(sdO + AT_HALF_BYTES, &tm_do, qdo_full, h * 128 + 64, qrow);
+      }
+      if (*abort_flag) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000LL) {
+        }
+      }
+    }
+  } else if (warp == 9) {
+    if (lane == 0) {
+      constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);  // A K-major, B K-major
+      constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);  // A K-major, B MN-major
+      constexpr uint32_t idesc_mm = make_idesc_bf16(128, 128, 1, 1);  // both MN-major
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aO = smem_u32(sdO), aP = smem_u32(sP), aS = smem_u32(sdS);
+      const uint32_t tS = tmem_base, tdP = tmem_base + 128u, tdV = tmem_base + 256u, tdK = tmem_base + 384u;
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
+      for (int it = 0; it < n_it && ok; ++it) {
+        const uint32_t ph = static_cast<uint32_t>(it & 1);
+        if (!mbar_wait(qdo_full, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
+        if (!mbar_wait(s_free, ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // S = Q Kt
+          const uint32_t off = (k >> 2) * AT_HALF_BYTES + (k & 3) * 32;
+          umma_f16_ss(tS, make_smem_desc_sw128(aQ + off, 16, 1024), make_smem_desc_sw128(aK + off, 16, 1024), idesc_kk, k > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dP = dO Vt
+          const uint32_t off = (k >> 2) * AT_HALF_BYTES + (k & 3) * 32;
+          umma_f16_ss(tdP, make_smem_desc_sw128(aO + off, 16, 1024), make_smem_desc_sw128(aV + off, 16, 1024), idesc_kk, k > 0 ? 1u : 0u);
+        }
+        umma_commit(sdp_full);
+        if (!mbar_wait(pds_full, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dV += Pt dO   (contraction over the 128 query rows, 16 per step)
+          umma_f16_ss(tdV, make_smem_desc_sw128(aP + k * 2048, AT_HALF_BYTES, 1024), make_smem_desc_sw128(aO + k * 2048, AT_HALF_BYTES, 1024),
+                      idesc_mm, (it > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dK += dSt Q
+          umma_f16_ss(tdK, make_smem_desc_sw128(aS + k * 2048, AT_HALF_BYTES, 1024), make_smem_desc_sw128(aQ + k * 2048, AT_HALF_BYTES, 1024),
+                      idesc_mm, (it > 0 || k > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {  // dQ = dS K    (contraction over the 128 key rows)
+          umma_f16_ss(tS, make_smem_desc_sw128(aS + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024),
+                      make_smem_desc_sw128(aK + k * 2048, AT_HALF_BYTES, 1024), idesc_km, k > 0 ? 1u : 0u);
+        }
+        umma_commit(dq_full);
+        umma_commit(qdo_empty);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = warp >> 2;
+    const int row = quarter * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int col0 = half * 64;
+    bool ok = true;
+    for (int it = 0; it < n_it; ++it) {
+      const uint32_t ph = static_cast<uint32_t>(it & 1);
+      const int h = hk * group + it / per_head;
+      const int qi = i0 + it % per_head;
+      const long long t_idx = static_cast<long long>(qi) * 128 + row;
+      const long long stat = (static_cast<long long>(b) * p.H + h) * p.T + t_idx;
+      const float lse2 = p.lse[stat] * 1.4426950408889634f;
+      const float dl = p.delta[stat];
+      if (!mbar_wait(sdp_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      __syncwarp();
+      uint32_t pk[32], dsk[32];
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t rs[32], rp[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 32), rs);
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0 + cc * 32), rp);
+        tmem_ld_wait();
+#pragma unroll
+        for (int c = 0; c < 16; ++c) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = col0 + cc * 32 + 2 * c + e;
+            float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
+            if (p.causal && qi == jt && col > row) pr = 0.f;
+            pv[e] = pr;
+            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl) * p.scale;
+          }
+          pk[cc * 16 + c] = pack_bf16x2(pv[0], pv[1]);
+          dsk[cc * 16 + c] = pack_bf16x2(dv[0], dv[1]);
+        }
+      }
+      // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle
+      uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+      uint8_t* srow = sdS + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int o = (ch ^ (row & 7)) << 4;
+        *reinterpret_cast<uint4*>(prow + o) = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(srow + o) = make_uint4(dsk[ch * 4 + 0], dsk[ch * 4 + 1], dsk[ch * 4 + 2], dsk[ch * 4 + 3]);
+      }
+      tc_fence_before();
+      fence_proxy_async();
+      mbar_arrive(pds_full);
+      // dQ tile: add this key tile's contribution to the fp32 accumulator
+      if (!mbar_wait(dq_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      tc_fence_after();
+      __syncwarp();
+      float* dq_row = p.dq_acc + ((static_cast<long long>(b) * p.T + t_idx) * p.H + h) * 128 + col0;
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 32), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 8; ++v)
+          red_add_v4(dq_row + cc * 32 + v * 4, __uint_as_float(r[v * 4 + 0]), __uint_as_float(r[v * 4 + 1]),
+                     __uint_as_float(r[v * 4 + 2]), __uint_as_float(r[v * 4 + 3]));
+      }
+      tc_fence_before();
+      mbar_arrive(s_free);
+    }
+    if (ok && n_it > 0) {
+      // dV and dK are complete once the last dq_full has fired (same commit covers all earlier MMAs)
+      const long long t_idx = static_cast<long long>(jt) * 128 + row;
+      bf16* dv_row = p.dv + b * p.dv_sb + t_idx * p.dv_st + hk * p.dv_sh + col0;
+      bf16* dk_row = p.dk + b * p.dk_sb + t_idx * p.dk_st + hk * p.dk_sh + col0;
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        bf16* out = which == 0 ? dv_row : dk_row;
+        const uint32_t t_addr = tmem_base + lane_addr + (which == 0 ? 256u : 384u) + static_cast<uint32_t>(col0);
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_addr + cc * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 o4;
+            o4.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+            o4.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+            o4.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+            o4.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+            *reinterpret_cast<uint4*>(out + cc * 32 + v * 8) = o4;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 512);
+  }
+}
+
+// delta[b, h, t] = sum_d dO * O ; one warp per (b, t, h) row of 128 elements
+__global__ void attn_bwd_delta_kernel(const bf16* __restrict__ dO, const bf16* __restrict__ O, float* __restrict__ delta, int B, int T,
+                                      int H, long long do_sb, long long do_st, long long do_sh, long long o_sb, long long o_st,
+                                      long long o_sh) {
+  const long long w = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const long long total = static_cast<long long>(B) * T * H;
+  if (w >= total) return;
+  const int h = static_cast<int>(w % H);
+  const long long bt = w / H;
+  const int t = static_cast<int>(bt % T);
+  const int b = static_cast<int>(bt / T);
+  const uint2 a = *reinterpret_cast<const uint2*>(dO + b * do_sb + t * do_st + h * do_sh + lane * 4);
+  const uint2 c = *reinterpret_cast<const uint2*>(O + b * o_sb + t * o_st + h * o_sh + lane * 4);
+  const float2 a0 = unpack_bf16x2(a.x), a1 = unpack_bf16x2(a.y), c0 = unpack_bf16x2(c.x), c1 = unpack_bf16x2(c.y);
+  float s = a0.x * c0.x + a0.y * c0.y + a1.x * c1.x + a1.y * c1.y;
+  s = warp_sum(s);
+  if (lane == 0) delta[(static_cast<long long>(b) * H + h) * T + t] = s;
+}
+
+// dq (bf16, strided) = dq_acc (fp32, contiguous (B, T, H, 128))
+__global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, int B, int T, int H, long long sb,
+                                           long long st, long long sh) {
+  const long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // one thread per 8 elements
+  const long long total = static_cast<long long>(B) * T * H * 16;
+  if (v >= total) return;
+  const int c = static_cast<int>(v % 16);
+  const long long bth = v / 16;
+  const int h = static_cast<int>(bth % H);
+  const long long bt = bth / H;
+  const int t = static_cast<int>(bt % T);
+  const int b = static_cast<int>(bt / T);
+  const float4 x = *reinterpret_cast<const float4*>(acc + bth * 128 + c * 8);
+  const float4 y = *reinterpret_cast<const float4*>(acc + bth * 128 + c * 8 + 4);
+  uint4 o;
+  o.x = pack_bf16x2(x.x, x.y);
+  o.y = pack_bf16x2(x.z, x.w);
+  o.z = pack_bf16x2(y.x, y.y);
+  o.w = pack_bf16x2(y.z, y.w);
+  *reinterpret_cast<uint4*>(dq + b * sb + t * st + h * sh + c * 8) = o;
+}
+
+}  // namespace
+}  // namespace ob
+
+// Scratch supplied by the caller: `delta` (B*H*T floats) and `dq_acc` (B*T*H*128 floats; zeroed here).
+extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse,
+                                void* dq, void* dk, void* dv, float* delta, float* dq_acc, int B, int T, int H, int Hkv,
+                                int do_sb, int do_st, int do_sh, int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh,
+                                int v_sb, int v_st, int v_sh, int o_sb, int o_st, int o_sh, int dq_sb, int dq_st, int dq_sh,
+                                int dk_sb, int dk_st, int dk_sh, int dv_sb, int dv_st, int dv_sh, float scale, int causal,
+                                int* status, cudaStream_t stream) {
+  using namespace ob;
+  if (B <= 0 || T <= 0) return 0;
+  if (T % 128 != 0 || H % Hkv != 0) return -1;
+  if (q_sh != 128 || k_sh != 128 || v_sh != 128 || do_sh != 128) return -2;
+  if (q_sb != T * q_st || k_sb != T * k_st || v_sb != T * v_st || do_sb != T * do_st) return -3;
+  if ((dq_st % 8) || (dk_st % 8) || (dv_st % 8) || (dq_sh % 8) || (dk_sh % 8) || (dv_sh % 8)) return -4;
+  CUtensorMap tq, tk, tv, tdo;
+  int rc = make_tensor_map_bf16_2d(&tq, q, (uint64_t)H * 128, (uint64_t)B * T, (uint64_t)q_st, 64, 128);
+  if (rc == 0) rc = make_tensor_map_bf16_2d(&tk, k, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)k_st, 64, 128);
+  if (rc == 0) rc = make_tensor_map_bf16_2d(&tv, v, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)v_st, 64, 128);
+  if (rc == 0) rc = make_tensor_map_bf16_2d(&tdo, dout, (uint64_t)H * 128, (uint64_t)B * T, (uint64_t)do_st, 64, 128);
+  if (rc != 0) return rc;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM) != cudaSuccess) return -10;
+    configured = true;
+  }
+  const long long rows = static_cast<long long>(B) * T * H;
+  if (cudaMemsetAsync(dq_acc, 0, static_cast<size_t>(rows) * 128 * sizeof(float), stream) != cudaSuccess) return -12;
+  attn_bwd_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
+      (const bf16*)dout, (const bf16*)o, delta, B, T, H, do_sb, do_st, do_sh, o_sb, o_st, o_sh);
+  AttnBwdParams p;
+  p.lse = lse; p.delta = delta; p.dq_acc = dq_acc;
+  p.dk = (bf16*)dk; p.dv = (bf16*)dv;
+  p.dk_sb = dk_sb; p.dk_st = dk_st; p.dk_sh = dk_sh; p.dv_sb = dv_sb; p.dv_st = dv_st; p.dv_sh = dv_sh;
+  p.B = B; p.T = T; p.H = H; p.Hkv = Hkv;
+  p.scale = scale; p.scale_log2 = scale * 1.4426950408889634f;
+  p.causal = causal; p.status = status;
+  attn_bwd_kernel<<<B * Hkv * (T / 128), AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, tdo, p);
+  attn_bwd_dq_convert_kernel<<<static_cast<unsigned>((rows * 16 + 255) / 256), 256, 0, stream>>>(dq_acc, (bf16*)dq, B, T, H, dq_sb,
+                                                                                               dq_st, dq_sh);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}

@@ -56,17 +56,21 @@ def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = N
 
 
 def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float) -> None:
+    """Gradients into caller-provided (possibly strided) ``dq``, ``dk``, ``dv``.  Scratch: ``delta`` (B·H·T floats) and
+    an fp32 ``dq`` accumulator (B·T·H·128 floats) that key tiles add into with vector reductions."""
     B, T, H, D = q.shape
     Hkv = k.shape[2]
+    delta = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    dq_acc = torch.empty((B, T, H, D), dtype=torch.float32, device=q.device)
     rc = lib().ob_attention_bwd(
-        ptr(do), ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(dq), ptr(dk), ptr(dv),
+        ptr(do), ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), ptr(dq), ptr(dk), ptr(dv), ptr(delta), ptr(dq_acc),
         c_int(B), c_int(T), c_int(H), c_int(Hkv),
         *(c_int(s) for s in _strides(do)), *(c_int(s) for s in _strides(q)), *(c_int(s) for s in _strides(k)),
         *(c_int(s) for s in _strides(v)), *(c_int(s) for s in _strides(o)), *(c_int(s) for s in _strides(dq)),
         *(c_int(s) for s in _strides(dk)), *(c_int(s) for s in _strides(dv)),
         c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), stream_ptr(),
     )
-    check(rc, "ob_attention_bwd")
+    check(rc, "ob_attention_bwd", kernels=3)
 
 
 def varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale):  # pragma: no cover - not reached while supports() is False for varlen

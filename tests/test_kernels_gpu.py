@@ -251,3 +251,30 @@ def test_native_attention_forward(causal, H, Hkv, T):
     ro, rlse = A.math_attention_forward(q, k, v, causal, scale)
     _close(o, ro, rtol=2e-2, atol=2e-2)
     assert torch.allclose(lse, rlse, rtol=1e-3, atol=2e-3), (lse - rlse).abs().max().item()
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("H,Hkv,T", [(4, 4, 512), (4, 2, 256)])
+def test_native_attention_backward(causal, H, Hkv, T):
+    from olmo_b200.ops import attention as A
+    from olmo_b200.ops import attention_native as N
+
+    B, D = 2, 128
+    fused = _rand(B * T, (H + 2 * Hkv) * D)
+    q = fused[:, : H * D].view(B, T, H, D)
+    k = fused[:, H * D : (H + Hkv) * D].view(B, T, Hkv, D)
+    v = fused[:, (H + Hkv) * D :].view(B, T, Hkv, D)
+    assert N.supports_backward(q, k, causal)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = N.forward(q, k, v, causal, scale)
+    do = _rand(B, T, H, D)
+    dfused = torch.zeros_like(fused)
+    dq = dfused[:, : H * D].view(B, T, H, D)
+    dk = dfused[:, H * D : (H + Hkv) * D].view(B, T, Hkv, D)
+    dv = dfused[:, (H + Hkv) * D :].view(B, T, Hkv, D)
+    N.backward(do, q, k, v, o, lse, dq, dk, dv, causal, scale)
+    ro, rlse = A.math_attention_forward(q, k, v, causal, scale)
+    rdq, rdk, rdv = A._math_attention_backward(do, q, k, v, ro, rlse, causal, scale)
+    _close(dv, rdv, rtol=3e-2, atol=3e-2)
+    _close(dk, rdk, rtol=3e-2, atol=3e-2)
+    _close(dq, rdq, rtol=3e-2, atol=3e-2)
