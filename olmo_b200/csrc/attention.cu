@@ -4,10 +4,12 @@
 //   warps 0..7  softmax: thread (row r, half h) owns row r and 64 of the 128 columns of each score tile
 //   warp 8      TMA producer (Q once; K and V double buffered; 128B-swizzled tiles of 2 x [128 rows x 64 elements])
 //   warp 9      MMA issuer   S = Q Kt (tcgen05, both operands K-major)   and   Ot = P V (V is the MN-major operand)
-// TMEM: two score accumulators (2 x 128 columns) and two output accumulators (2 x 128 columns), so the tensor core
-// works on Q Kt of tile j+1 while the softmax warps are busy with tile j.  Each P V product goes to a fresh
-// accumulator; the running output lives in registers and is rescaled there (O = O * alpha + Ot), which avoids
-// read-modify-write of TMEM.  P is handed to the tensor core through shared memory in the 128B-swizzled K-major layout.
+// TMEM: two score accumulators (2 x 128 columns), so the tensor core works on Q Kt of tile j+1 while the softmax warps
+// are busy with tile j, and one output accumulator (128 columns) into which every P V product accumulates.  The
+// softmax reference maximum is only raised when a row's maximum grows by more than 2^8; in that (rare) case the warp
+// rescales its rows of the output accumulator in TMEM.  This keeps the per-element instruction count of the softmax
+// warps low enough (one FFMA, one EX2, one max, one add, half a convert) for the tensor core to be the limiter.
+// P is handed to the tensor core through shared memory in the 128B-swizzled K-major layout.
 //
 // Layout of operands in global memory: (B, T, heads, 128) with arbitrary row pitch (views into fused QKV buffers are
 // fine); grouped-query attention maps query head h to key/value head h / (H / Hkv).  T must be a multiple of 128.
@@ -54,8 +56,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* v_empty = bars + 7;     // 2
   uint64_t* s_full = bars + 9;      // 2
   uint64_t* s_empty = bars + 11;    // 2
-  uint64_t* o_full = bars + 13;     // 2
-  uint64_t* o_empty = bars + 15;    // 2
+  uint64_t* o_full = bars + 13;     // 1
   uint64_t* p_full = bars + 17;     // 1
   uint64_t* x_bar = bars + 18;      // 1: exchange of row statistics between the two column halves
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
@@ -83,9 +84,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 256);
-      mbar_init(&o_full[s], 1);
-      mbar_init(&o_empty[s], 256);
     }
+    mbar_init(o_full, 1);
     mbar_init(p_full, 256);
     mbar_init(x_bar, 256);
     *abort_flag = 0;
@@ -142,18 +142,17 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         const uint32_t ph = (i >> 1) & 1;
         if (!mbar_wait(&v_full[s], ph, abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
         if (!mbar_wait(p_full, static_cast<uint32_t>(i & 1), abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
-        if (!mbar_wait(&o_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) return false;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(sV + s * AT_TILE_BYTES);
-        const uint32_t d_tmem = tmem_base + 256u + static_cast<uint32_t>(s) * 128u;
+        const uint32_t d_tmem = tmem_base + 256u;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           // A = P: K-major, 64-column halves;  B = V: MN-major, 16 kv rows per step = 2 KiB, 64-wide d halves 16 KiB apart
           const uint64_t a_desc = make_smem_desc_sw128(p_addr + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024);
           const uint64_t b_desc = make_smem_desc_sw128(v_addr + k * 2048, AT_HALF_BYTES, 1024);
-          umma_f16_ss(d_tmem, a_desc, b_desc, idesc_pv, k > 0 ? 1u : 0u);
+          umma_f16_ss(d_tmem, a_desc, b_desc, idesc_pv, (i > 0 || k > 0) ? 1u : 0u);
         }
-        umma_commit(&o_full[s]);
+        umma_commit(o_full);
         umma_commit(&v_empty[s]);
         return true;
       };
@@ -185,30 +184,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     const int row = quarter * 32 + lane;           // query row inside the tile == TMEM lane
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int col0 = half * 64;
-    float m_run = -INFINITY, l_run = 0.f, alpha_prev = 1.f;
-    float o_acc[64];
-#pragma unroll
-    for (int c = 0; c < 64; ++c) o_acc[c] = 0.f;
+    const uint32_t o_addr = tmem_base + lane_addr + 256u + static_cast<uint32_t>(col0);
+    float m_ref = -INFINITY;  // reference maximum of the raw (unscaled) scores used in the exponent
+    float l_run = 0.f;
     bool ok = true;
-
-    auto fold = [&](int i, float alpha) -> bool {
-      const int s = i & 1;
-      if (!mbar_wait(&o_full[s], static_cast<uint32_t>((i >> 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) return false;
-      tc_fence_after();
-      __syncwarp();
-      const uint32_t t_addr = tmem_base + lane_addr + 256u + static_cast<uint32_t>(s) * 128u + static_cast<uint32_t>(col0);
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_addr + cc * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 32; ++c) o_acc[cc * 32 + c] = o_acc[cc * 32 + c] * alpha + __uint_as_float(r[c]);
-      }
-      tc_fence_before();
-      mbar_arrive(&o_empty[s]);
-      return true;
-    };
 
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
@@ -224,8 +203,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         tmem_ld_wait();
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          sc[c] = __uint_as_float(r0[c]) * p.scale_log2;
-          sc[32 + c] = __uint_as_float(r1[c]) * p.scale_log2;
+          sc[c] = __uint_as_float(r0[c]);
+          sc[32 + c] = __uint_as_float(r1[c]);
         }
       }
       tc_fence_before();
@@ -235,32 +214,51 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         for (int c = 0; c < 64; ++c)
           if (col0 + c > row) sc[c] = -INFINITY;
       }
-      float pm = sc[0];
+      float pm0 = fmaxf(sc[0], sc[1]), pm1 = fmaxf(sc[2], sc[3]);
 #pragma unroll
-      for (int c = 1; c < 64; ++c) pm = fmaxf(pm, sc[c]);
+      for (int c = 4; c < 64; c += 4) {
+        pm0 = fmaxf(pm0, fmaxf(sc[c], sc[c + 1]));
+        pm1 = fmaxf(pm1, fmaxf(sc[c + 2], sc[c + 3]));
+      }
       float* mx = smax + (j & 1) * 256;
-      mx[half * 128 + row] = pm;
+      mx[half * 128 + row] = fmaxf(pm0, pm1);
       mbar_arrive(x_bar);
       if (!mbar_wait(x_bar, static_cast<uint32_t>(j & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
-      const float m_new = fmaxf(m_run, fmaxf(mx[row], mx[128 + row]));
-      const float alpha = exp2f(m_run - m_new);
-      float ls = 0.f;
+      const float m_row = fmaxf(mx[row], mx[128 + row]);
+      // raise the reference only when the row maximum outgrows it by more than 2^8 in the exponent's units
+      const bool raise = (m_row - m_ref) * p.scale_log2 > 8.0f;
+      const float m_new = raise ? m_row : m_ref;
+      const float alpha = raise ? exp2f((m_ref - m_new) * p.scale_log2) : 1.0f;
+      const float neg_m = -m_new * p.scale_log2;
+      float ls0 = 0.f, ls1 = 0.f;
       uint32_t pk[32];
 #pragma unroll
       for (int c = 0; c < 32; ++c) {
-        const float e0 = exp2f(sc[2 * c] - m_new);
-        const float e1 = exp2f(sc[2 * c + 1] - m_new);
+        const float e0 = exp2f(fmaf(sc[2 * c], p.scale_log2, neg_m));
+        const float e1 = exp2f(fmaf(sc[2 * c + 1], p.scale_log2, neg_m));
         pk[c] = pack_bf16x2(e0, e1);
-        // the row sum uses the rounded values that the tensor core will multiply with V
-        const float2 rr = unpack_bf16x2(pk[c]);
-        ls += rr.x + rr.y;
+        ls0 += e0;
+        ls1 += e1;
       }
-      l_run = l_run * alpha + ls;
-      m_run = m_new;
+      l_run = l_run * alpha + (ls0 + ls1);
+      m_ref = m_new;
       if (j > 0) {
-        if (!fold(j - 1, alpha_prev)) { ok = false; break; }  // also guarantees that P V (j-1) has finished reading sP
+        // P V (j-1) must have completed: it was reading sP, and the accumulator may need rescaling
+        if (!mbar_wait(o_full, static_cast<uint32_t>((j - 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, raise)) {
+#pragma unroll
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(o_addr + cc * 16, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) r[c] = __float_as_uint(__uint_as_float(r[c]) * alpha);
+            tmem_st_32x32b_x16(o_addr + cc * 16, r);
+          }
+          tmem_st_wait();
+        }
       }
-      alpha_prev = alpha;
       // P tile -> shared memory, K-major with 128-byte swizzle: 16-byte chunk index XOR (row mod 8)
       uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
@@ -268,32 +266,39 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         uint4 v4 = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
         *reinterpret_cast<uint4*>(prow + ((ch ^ (row & 7)) << 4)) = v4;
       }
+      tc_fence_before();
       fence_proxy_async();
       mbar_arrive(p_full);
     }
-    if (ok) ok = fold(n_kv - 1, alpha_prev);
-    // total row sum = sum of the two halves
+    if (ok) ok = mbar_wait(o_full, static_cast<uint32_t>((n_kv - 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE);
     ssum[half * 128 + row] = l_run;
     if (ok) {
       mbar_arrive(x_bar);
       ok = mbar_wait(x_bar, static_cast<uint32_t>(n_kv & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE);
     }
     if (ok) {
+      tc_fence_after();
       const float l_tot = ssum[row] + ssum[128 + row];
       const float inv = 1.f / l_tot;
       const long long t_idx = static_cast<long long>(qt) * 128 + row;
       bf16* orow = p.o + b * p.o_stride_b + t_idx * p.o_stride_t + h * p.o_stride_h + col0;
 #pragma unroll
-      for (int v = 0; v < 8; ++v) {
-        uint4 o4;
-        o4.x = pack_bf16x2(o_acc[v * 8 + 0] * inv, o_acc[v * 8 + 1] * inv);
-        o4.y = pack_bf16x2(o_acc[v * 8 + 2] * inv, o_acc[v * 8 + 3] * inv);
-        o4.z = pack_bf16x2(o_acc[v * 8 + 4] * inv, o_acc[v * 8 + 5] * inv);
-        o4.w = pack_bf16x2(o_acc[v * 8 + 6] * inv, o_acc[v * 8 + 7] * inv);
-        *reinterpret_cast<uint4*>(orow + v * 8) = o4;
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(o_addr + cc * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 o4;
+          o4.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]) * inv, __uint_as_float(r[v * 8 + 1]) * inv);
+          o4.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]) * inv, __uint_as_float(r[v * 8 + 3]) * inv);
+          o4.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]) * inv, __uint_as_float(r[v * 8 + 5]) * inv);
+          o4.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]) * inv, __uint_as_float(r[v * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(orow + cc * 32 + v * 8) = o4;
+        }
       }
       if (half == 0)
-        p.lse[(static_cast<long long>(b) * p.H + h) * p.T + t_idx] = (m_run + log2f(l_tot)) * 0.6931471805599453f;
+        p.lse[(static_cast<long long>(b) * p.H + h) * p.T + t_idx] = (m_ref * p.scale_log2 + log2f(l_tot)) * 0.6931471805599453f;
     }
   }
 
@@ -349,7 +354,8 @@ extern "C" int ob_attention_fwd(const void* q, const void* k, const void* v, voi
 // Backward.  One CTA owns a 128-row key/value tile of one (batch, kv head) and walks over the query tiles that attend
 // to it (all query heads of the group).  Per query tile:
 //     S  = Q Kt,  dP = dO Vt                         (tensor core -> TMEM)
-//     P  = exp2(S * c - lse),  dS = P * (dP - delta) * scale      (256 threads, written to shared memory as bf16)
+//     P  = exp2(S * c - lse),  dS = P * (dP - delta)      (256 threads, bf16 to shared memory; the softmax scale is
+//                                                          applied once, when dK and dQ are written out)
 //     dV += Pt dO,  dK += dSt Q,  dQ = dS K          (tensor core; dV and dK accumulate in TMEM over the whole walk)
 //     dQ -> fp32 global accumulator with vector reductions (other key tiles add to the same rows)
 // `delta` = rowsum(dO * O) comes from a small pre-pass; a post-pass converts the dQ accumulator to bf16.
@@ -510,14 +516,28 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int col0 = half * 64;
     bool ok = true;
+    // row statistics of the next query tile are fetched one iteration ahead so that their latency is hidden
+    auto stat_index = [&](int it_) -> long long {
+      const int h_ = hk * group + it_ / per_head;
+      const long long t_ = static_cast<long long>(i0 + it_ % per_head) * 128 + row;
+      return (static_cast<long long>(b) * p.H + h_) * p.T + t_;
+    };
+    float lse_next = 0.f, dl_next = 0.f;
+    if (n_it > 0) {
+      lse_next = p.lse[stat_index(0)];
+      dl_next = p.delta[stat_index(0)];
+    }
     for (int it = 0; it < n_it; ++it) {
       const uint32_t ph = static_cast<uint32_t>(it & 1);
       const int h = hk * group + it / per_head;
       const int qi = i0 + it % per_head;
       const long long t_idx = static_cast<long long>(qi) * 128 + row;
-      const long long stat = (static_cast<long long>(b) * p.H + h) * p.T + t_idx;
-      const float lse2 = p.lse[stat] * 1.4426950408889634f;
-      const float dl = p.delta[stat];
+      const float lse2 = lse_next * 1.4426950408889634f;
+      const float dl = dl_next;
+      if (it + 1 < n_it) {
+        lse_next = p.lse[stat_index(it + 1)];
+        dl_next = p.delta[stat_index(it + 1)];
+      }
       if (!mbar_wait(sdp_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
       __syncwarp();
@@ -537,7 +557,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
             float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
             if (p.causal && qi == jt && col > row) pr = 0.f;
             pv[e] = pr;
-            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl) * p.scale;
+            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl);
           }
           pk[cc * 16 + c] = pack_bf16x2(pv[0], pv[1]);
           dsk[cc * 16 + c] = pack_bf16x2(dv[0], dv[1]);
@@ -590,10 +610,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
             uint4 o4;
-            o4.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-            o4.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-            o4.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-            o4.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+            const float f = which == 0 ? 1.0f : p.scale;  // dS was kept unscaled: dK = scale * dSt Q
+            o4.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]) * f, __uint_as_float(r[v * 8 + 1]) * f);
+            o4.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]) * f, __uint_as_float(r[v * 8 + 3]) * f);
+            o4.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]) * f, __uint_as_float(r[v * 8 + 5]) * f);
+            o4.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]) * f, __uint_as_float(r[v * 8 + 7]) * f);
             *reinterpret_cast<uint4*>(out + cc * 32 + v * 8) = o4;
           }
         }
@@ -629,9 +650,9 @@ __global__ void attn_bwd_delta_kernel(const bf16* __restrict__ dO, const bf16* _
   if (lane == 0) delta[(static_cast<long long>(b) * H + h) * T + t] = s;
 }
 
-// dq (bf16, strided) = dq_acc (fp32, contiguous (B, T, H, 128))
+// dq (bf16, strided) = scale * dq_acc (fp32, contiguous (B, T, H, 128))
 __global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, int B, int T, int H, long long sb,
-                                           long long st, long long sh) {
+                                           long long st, long long sh, float scale) {
   const long long v = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;  // one thread per 8 elements
   const long long total = static_cast<long long>(B) * T * H * 16;
   if (v >= total) return;
@@ -644,10 +665,10 @@ __global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, bf16* 
   const float4 x = *reinterpret_cast<const float4*>(acc + bth * 128 + c * 8);
   const float4 y = *reinterpret_cast<const float4*>(acc + bth * 128 + c * 8 + 4);
   uint4 o;
-  o.x = pack_bf16x2(x.x, x.y);
-  o.y = pack_bf16x2(x.z, x.w);
-  o.z = pack_bf16x2(y.x, y.y);
-  o.w = pack_bf16x2(y.z, y.w);
+  o.x = pack_bf16x2(x.x * scale, x.y * scale);
+  o.y = pack_bf16x2(x.z * scale, x.w * scale);
+  o.z = pack_bf16x2(y.x * scale, y.y * scale);
+  o.w = pack_bf16x2(y.z * scale, y.w * scale);
   *reinterpret_cast<uint4*>(dq + b * sb + t * st + h * sh + c * 8) = o;
 }
 
@@ -691,6 +712,6 @@ extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, 
   p.causal = causal; p.status = status;
   attn_bwd_kernel<<<B * Hkv * (T / 128), AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, tdo, p);
   attn_bwd_dq_convert_kernel<<<static_cast<unsigned>((rows * 16 + 255) / 256), 256, 0, stream>>>(dq_acc, (bf16*)dq, B, T, H, dq_sb,
-                                                                                               dq_st, dq_sh);
+                                                                                               dq_st, dq_sh, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }

@@ -1,0 +1,181 @@
+"""
+Kernel micro-benchmarks:  ``python -m olmo_b200.ops.microbench {gemm,attention,norm,ce,optim} [options]``
+
+Each case is timed with CUDA events on the launching stream after warm-up, with an L2 flush (a write of a buffer larger
+than L2) between timed iterations, and reported against the measured peaks in ``MEASURED_PEAKS.json`` when present.
+``--once`` runs each kernel a few times without timing, which is the form used under ``ncu``.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from . import check_status
+from . import kernels as k
+
+
+def _peaks() -> dict:
+    p = Path(__file__).resolve().parent.parent.parent / "MEASURED_PEAKS.json"
+    try:
+        return json.loads(p.read_text())
+    except Exception:
+        return {}
+
+
+_flush = None
+
+
+def timeit(fn, iters: int = 10, warmup: int = 3) -> float:
+    global _flush
+    if _flush is None:
+        _flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    for _ in range(warmup):
+        fn()
+    times = []
+    for _ in range(iters):
+        _flush.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench_gemm(args) -> None:
+    peak = _peaks().get("bf16_tflops")
+    shapes = [(8192, 12288, 4096), (8192, 4096, 4096), (8192, 22016, 4096), (8192, 4096, 11008), (8192, 100352, 4096)]
+    if args.small:
+        shapes = [(4096, 8192, 4096)]
+    for M, N, K in shapes:
+        a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+        b = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+        dy = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+        acc = torch.zeros(N, K, device="cuda")
+        cases = {
+            "fwd  x·Wt": lambda: k.gemm(a, b),
+            "dgrad dy·W": lambda: k.gemm(dy, b, b_trans=True),
+            "wgrad dyt·x (+= fp32)": lambda: k.gemm(dy, a, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc),
+        }
+        for name, fn in cases.items():
+            if args.once:
+                for _ in range(3):
+                    fn()
+                continue
+            ms = timeit(fn)
+            tf = 2 * M * N * K / ms / 1e9
+            frac = f" ({tf / peak:.2f} of measured cuBLAS burst)" if peak else ""
+            print(f"gemm {M}x{N}x{K} {name}: {ms:.3f} ms  {tf:.0f} TFLOP/s{frac}", flush=True)
+
+
+def bench_attention(args) -> None:
+    from . import attention_native as N
+
+    B, T, H, D = (1, 4096, 8, 128) if args.small else (2, 4096, 32, 128)
+    qkv = torch.randn(B * T, 3 * H * D, device="cuda", dtype=torch.bfloat16)
+    q = qkv[:, : H * D].view(B, T, H, D)
+    kk = qkv[:, H * D : 2 * H * D].view(B, T, H, D)
+    v = qkv[:, 2 * H * D :].view(B, T, H, D)
+    scale = 1 / math.sqrt(D)
+    o, lse = N.forward(q, kk, v, True, scale)
+    do = torch.randn_like(o)
+    dqkv = torch.empty_like(qkv)
+    dq = dqkv[:, : H * D].view(B, T, H, D)
+    dk = dqkv[:, H * D : 2 * H * D].view(B, T, H, D)
+    dv = dqkv[:, 2 * H * D :].view(B, T, H, D)
+    fwd = lambda: N.forward(q, kk, v, True, scale)  # noqa: E731
+    bwd = lambda: N.backward(do, q, kk, v, o, lse, dq, dk, dv, True, scale)  # noqa: E731
+    if args.once:
+        for _ in range(2):
+            fwd()
+            bwd()
+        return
+    fl = 4 * B * H * T * T * D / 2
+    t1, t2 = timeit(fwd), timeit(bwd)
+    print(f"attention causal B{B} T{T} H{H} D{D}: fwd {t1:.3f} ms {fl / t1 / 1e9:.0f} TFLOP/s | bwd {t2:.3f} ms {2.5 * fl / t2 / 1e9:.0f} TFLOP/s")
+    try:
+        import flash_attn.flash_attn_interface as fai
+
+        t3 = timeit(lambda: fai._flash_attn_forward(q, kk, v, 0.0, scale, True, -1, -1, 0.0, None, False))
+        t4 = timeit(lambda: fai._flash_attn_backward(do, q, kk, v, o, lse, dq, dk, dv, 0.0, scale, True, -1, -1, 0.0, None, False))
+        print(f"  flash-attn library for comparison: fwd {t3:.3f} ms | bwd {t4:.3f} ms")
+    except Exception as e:  # pragma: no cover
+        print(f"  flash-attn library unavailable: {e}")
+
+
+def bench_norm(args) -> None:
+    M, D = (8192, 4096)
+    bw = _peaks().get("hbm_gbs")
+    x, res = torch.randn(M, D, device="cuda", dtype=torch.bfloat16), torch.randn(M, D, device="cuda", dtype=torch.bfloat16)
+    w = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+    dy = torch.randn_like(x)
+    out, rstd, _ = k.norm_fwd(x, w, None, 1e-6, True, residual=res)
+    dw = torch.zeros(D, device="cuda")
+    cases = {
+        "rmsnorm+residual fwd": (lambda: k.norm_fwd(x, w, None, 1e-6, True, residual=res), 3 * M * D * 2),
+        "rmsnorm bwd": (lambda: k.norm_bwd(dy, x, w, rstd, None, True, dweight=dw), 3 * M * D * 2),
+    }
+    h = torch.randn(M, 22016, device="cuda", dtype=torch.bfloat16)
+    cases["swiglu fwd"] = (lambda: k.swiglu_fwd(h), M * 11008 * 3 * 2)
+    for name, (fn, nbytes) in cases.items():
+        if args.once:
+            fn()
+            continue
+        ms = timeit(fn)
+        gbs = nbytes / ms / 1e6
+        frac = f" ({gbs / bw:.2f} of measured copy bandwidth)" if bw else ""
+        print(f"{name}: {ms:.3f} ms  {gbs:.0f} GB/s{frac}")
+
+
+def bench_ce(args) -> None:
+    R, V = (2048 if args.small else 8192), 100352
+    bw = _peaks().get("hbm_gbs")
+    logits = torch.randn(R, V, device="cuda", dtype=torch.bfloat16)
+    labels = torch.randint(0, V, (R,), device="cuda")
+    fn = lambda: k.cross_entropy_(logits, labels, -100, 1e-4, 1.0 / R, True)  # noqa: E731
+    if args.once:
+        fn()
+        return
+    ms = timeit(fn)
+    gbs = 2 * R * V * 2 / ms / 1e6  # algorithmic: read once, write once
+    print(f"cross-entropy fwd+bwd {R}x{V}: {ms:.3f} ms  {gbs:.0f} GB/s" + (f" ({gbs / bw:.2f} of measured copy bandwidth)" if bw else ""))
+
+
+def bench_optim(args) -> None:
+    n = 50_000_000 if args.small else 202_391_552
+    bw = _peaks().get("hbm_gbs")
+    p, g, m, v = (torch.randn(n, device="cuda") for _ in range(4))
+    v.abs_()
+    lowp = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    seg_end = torch.tensor([n], device="cuda", dtype=torch.int64)
+    seg_wd, seg_lr = torch.tensor([0.1], device="cuda"), torch.tensor([3e-4], device="cuda")
+    fn = lambda: k.adamw_flat(p, g, m, v, lowp, seg_end, seg_wd, seg_lr, 0.9, 0.95, 1e-8, 10, None)  # noqa: E731
+    if args.once:
+        fn()
+        return
+    ms = timeit(fn)
+    gbs = n * (16 + 12 + 2) / ms / 1e6
+    print(f"adamw {n} params: {ms:.3f} ms  {gbs:.0f} GB/s" + (f" ({gbs / bw:.2f} of measured copy bandwidth)" if bw else ""))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["gemm", "attention", "norm", "ce", "optim", "all"])
+    ap.add_argument("--small", action="store_true", help="small case (for profiler captures)")
+    ap.add_argument("--once", action="store_true", help="launch without timing (for profiler captures)")
+    args = ap.parse_args()
+    table = {"gemm": bench_gemm, "attention": bench_attention, "norm": bench_norm, "ce": bench_ce, "optim": bench_optim}
+    for name, fn in table.items():
+        if args.what in (name, "all"):
+            fn(args)
+    check_status()
+
+
+if __name__ == "__main__":
+    main()
