@@ -671,6 +671,7 @@ class B200Runtime:
                                  (default off: plain peer loads).
     ``OLMO_B200_WAIT_BUDGET``    iteration budget of every device-side bounded wait.
     ``OLMO_B200_ATTENTION``      ``native`` (tcgen05 kernel) or ``library`` (flash-attn package).
+    ``OLMO_B200_GEMM_2CTA``      use the two-CTA ``cta_group::2`` GEMM kernel (default on).
     """
 
     kernels: bool = True

@@ -35,6 +35,8 @@ int ob_attention_bwd(const void* dout, const void* q, const void* k, const void*
                      int do_sh, int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh,
                      int o_sb, int o_st, int o_sh, int dq_sb, int dq_st, int dq_sh, int dk_sb, int dk_st, int dk_sh,
                      int dv_sb, int dv_st, int dv_sh, float scale, int causal, int* status, cudaStream_t stream);
+void ob_set_gemm_pair_mode(int on);  // 1: two-CTA (cta_group::2) GEMM kernel where applicable
+int ob_get_gemm_pair_mode(void);
 
 // ---- comm.cu (peer-memory collectives; `task` points at an ob::CommTask, see comm.cuh)
 int ob_comm_task_size(void);

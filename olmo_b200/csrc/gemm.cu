@@ -357,12 +357,28 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, co
 
 }  // namespace ob
 
+namespace ob {
+int gemm2_dispatch(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb, int ldc,
+                   int a_mn_major, int b_mn_major, int epi, int* status, int num_sms, const CommTask& comm_task, int comm_ctas,
+                   cudaStream_t stream);
+}
+static int g_gemm_pair_mode = 0;  // 1: use the two-CTA (cta_group::2) kernel of gemm2.cu where it applies
+
+extern "C" void ob_set_gemm_pair_mode(int on) { g_gemm_pair_mode = on; }
+extern "C" int ob_get_gemm_pair_mode(void) { return g_gemm_pair_mode; }
+
 static int gemm_dispatch(const void* A, const void* B, void* C, const void* R, int M, int N, int K, int lda, int ldb,
                          int ldc, int a_mn_major, int b_mn_major, int epi, const int* b_ready, int rows_per_flag,
                          int ready_value, int* status, int num_sms, const ob::CommTask& comm_task, int comm_ctas,
                          cudaStream_t stream) {
   using namespace ob;
   if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (num_sms <= 0) num_sms = 148;
+  if (g_gemm_pair_mode && b_ready == nullptr && M > 128 && num_sms >= 2 + comm_ctas) {
+    const int rc2 = gemm2_dispatch(A, B, C, R, M, N, K, lda, ldb, ldc, a_mn_major, b_mn_major, epi, status, num_sms & ~1,
+                                   comm_task, comm_ctas, stream);
+    if (rc2 != -20) return rc2;
+  }
   CUtensorMap ta, tb;
   int rc;
   // K-major operand: inner = K, outer = rows, box = 64 x rows-per-tile.  MN-major: inner = rows, outer = K, box 64 x 64.

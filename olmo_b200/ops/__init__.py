@@ -104,6 +104,7 @@ def lib() -> ctypes.CDLL:
                     f"{_SO_PATH} is missing and nvcc is unavailable; run `python -m olmo_b200.ops` where nvcc exists"
                 )
         _lib = ctypes.CDLL(str(_SO_PATH))
+        _lib.ob_set_gemm_pair_mode(ctypes.c_int(int(os.environ.get("OLMO_B200_GEMM_2CTA", "1") not in ("0", "", "false"))))
     return _lib
 
 

@@ -278,3 +278,40 @@ def test_native_attention_backward(causal, H, Hkv, T):
     _close(dv, rdv, rtol=3e-2, atol=3e-2)
     _close(dk, rdk, rtol=3e-2, atol=3e-2)
     _close(dq, rdq, rtol=3e-2, atol=3e-2)
+
+
+@pytest.fixture
+def pair_mode():
+    """Route GEMMs through the two-CTA (cta_group::2) kernel for the duration of a test."""
+    import ctypes
+
+    from olmo_b200 import ops
+
+    lib = ops.lib()
+    before = lib.ob_get_gemm_pair_mode()
+    lib.ob_set_gemm_pair_mode(ctypes.c_int(1))
+    yield
+    lib.ob_set_gemm_pair_mode(ctypes.c_int(before))
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (256, 512, 128), (300, 300, 72), (1024, 1024, 1024), (384, 11008, 4096)])
+def test_gemm_pair_nt(pair_mode, M, N, K):
+    from olmo_b200.ops import kernels as k
+
+    a, b = _rand(M, K), _rand(N, K)
+    _close(k.gemm(a, b), a.float() @ b.float().t())
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 128), (264, 264, 328), (512, 4096, 1024)])
+def test_gemm_pair_dgrad_wgrad(pair_mode, M, N, K):
+    from olmo_b200.ops import kernels as k
+
+    a, b = _rand(M, K), _rand(K, N)
+    _close(k.gemm(a, b, b_trans=True), a.float() @ b.float())
+    at, bt = _rand(K, M), _rand(K, N)
+    want = at.float().t() @ bt.float()
+    acc = torch.ones(M, N, device="cuda", dtype=torch.float32)
+    k.gemm(at, bt, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc)
+    _close(acc, want + 1.0, rtol=1e-2, atol=1e-2)
+    r = _rand(M, N)
+    _close(k.gemm(a, b, b_trans=True, epilogue=k.EPI_BF16_ADD, residual=r), a.float() @ b.float() + r.float())
