@@ -223,12 +223,13 @@ def _resolve_string(value: str, root: Any, depth: int = 0) -> Any:
             got = _resolve_string(got, root, depth + 1)
         return got
 
-    whole = _INTERP.fullmatch(value.strip())
-    if whole is not None:
-        return eval_expr(whole.group(1))  # keeps the native type of the target
     prev = None
     while "${" in value and value != prev:
+        whole = _INTERP.fullmatch(value.strip())
+        if whole is not None:
+            return eval_expr(whole.group(1))  # keeps the native type of the target
         prev = value
+        # innermost expressions first, so that "${a:${b}}" ends as one whole-value expression
         value = _INTERP.sub(lambda m: str(eval_expr(m.group(1))), value)
     return value
 

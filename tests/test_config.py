@@ -1,0 +1,176 @@
+"""Typed config engine: YAML quirks, overrides, interpolation, resolvers, legacy rewrites, recipes."""
+import os
+
+import pytest
+
+from olmo_b200.config import (
+    ActivationCheckpointingStrategy,
+    CheckpointType,
+    DistributedStrategy,
+    ModelConfig,
+    OptimizerType,
+    SchedulerType,
+    ShardingStrategy,
+    TrainConfig,
+)
+from olmo_b200.exceptions import OLMoConfigurationError
+from olmo_b200.recipes import MODEL_FAMILIES, RECIPES, recipe_config, write_configs
+from olmo_b200.utils import structured as S
+
+
+def write(tmp_path, text, name="c.yaml"):
+    p = tmp_path / name
+    p.write_text(text)
+    return p
+
+
+def test_yaml_scalars_follow_yaml_1_1_floats():
+    raw = S.load_yaml("a: 3e-4\nb: 1e5\nc: 5e12\nd: 4e12T\ne: 739_328\nf: null\ng: off\n")
+    assert raw["a"] == pytest.approx(3e-4) and isinstance(raw["a"], float)
+    assert raw["b"] == 1e5 and isinstance(raw["c"], float)
+    assert raw["d"] == "4e12T"
+    assert raw["f"] is None
+
+
+def test_load_with_overrides_and_interpolation(tmp_path):
+    p = write(
+        tmp_path,
+        """
+run_name: demo
+model:
+  d_model: 64
+  n_heads: 4
+  n_layers: 2
+optimizer:
+  learning_rate: 3e-4
+scheduler:
+  name: linear_with_warmup
+device_train_microbatch_size: 4
+device_eval_batch_size: ${device_train_microbatch_size}
+save_folder: /tmp/${run_name}/ckpt
+wandb:
+  name: ${run_name}
+""",
+    )
+    cfg = TrainConfig.load(p, overrides=["model.n_layers=3", "optimizer.name=lionw", "max_duration=2ep", "global_train_batch_size=16"])
+    assert cfg.model.d_model == 64 and cfg.model.n_layers == 3
+    assert cfg.optimizer.name == OptimizerType.lionw and cfg.optimizer.learning_rate == pytest.approx(3e-4)
+    assert cfg.scheduler.name == SchedulerType.linear_with_warmup
+    assert cfg.device_eval_batch_size == 4
+    assert cfg.save_folder == "/tmp/demo/ckpt" and cfg.wandb.name == "demo"
+    assert cfg.max_duration == "2ep" and cfg.global_train_batch_size == 16
+
+
+def test_unknown_keys_and_bad_values_are_rejected(tmp_path):
+    with pytest.raises(OLMoConfigurationError):
+        TrainConfig.load(write(tmp_path, "not_a_field: 1\n"))
+    with pytest.raises(OLMoConfigurationError):
+        TrainConfig.load(write(tmp_path, "model:\n  d_model: lots\n"))
+    with pytest.raises(OLMoConfigurationError):
+        TrainConfig.load(write(tmp_path, "optimizer:\n  name: sgd\n"))
+    with pytest.raises(OLMoConfigurationError):
+        TrainConfig.load(write(tmp_path, "run_name: x\n"), overrides=["model.nope=1"])
+    with pytest.raises(OLMoConfigurationError):
+        TrainConfig.load(tmp_path / "missing.yaml")
+
+
+def test_env_and_path_resolvers(tmp_path, monkeypatch):
+    for name in ("a.npy", "b.npy"):
+        (tmp_path / name).write_bytes(b"")
+    monkeypatch.setenv("MY_GLOB", str(tmp_path / "*.npy"))
+    monkeypatch.delenv("NOT_SET_ANYWHERE", raising=False)
+    p = write(
+        tmp_path,
+        """
+run_name: ${oc.env:NOT_SET_ANYWHERE,fallback}
+data:
+  paths: ${path.glob:${oc.env:MY_GLOB}}
+load_path: ${path.choose:/definitely/not/here,%s}
+""" % tmp_path,
+    )
+    cfg = TrainConfig.load(p)
+    assert cfg.run_name == "fallback"
+    assert cfg.data.paths == [str(tmp_path / "a.npy"), str(tmp_path / "b.npy")]
+    assert cfg.load_path == str(tmp_path)
+    with pytest.raises(FileNotFoundError):
+        TrainConfig.load(write(tmp_path, "data:\n  paths: ${path.glob:/definitely/not/here/*.npy}\n", "d.yaml"))
+    cfg = TrainConfig.load(tmp_path / "d.yaml", validate_paths=False)
+    assert cfg.data.paths == []
+
+    (tmp_path / "run" / "step10").mkdir(parents=True)
+    (tmp_path / "run" / "step200").mkdir()
+    (tmp_path / "run" / "step200-unsharded").mkdir()
+    cfg = TrainConfig.load(write(tmp_path, "load_path: ${path.last_checkpoint:%s}\n" % (tmp_path / "run"), "e.yaml"))
+    assert os.path.basename(cfg.load_path).startswith("step200")
+
+
+def test_legacy_settings_are_rewritten(tmp_path):
+    cfg = TrainConfig.load(write(tmp_path, "activation_checkpointing: true\noptimizer:\n  name: decoupled_lionw\n  eps: 1e-8\n"))
+    assert cfg.activation_checkpointing == ActivationCheckpointingStrategy.whole_layer
+    assert cfg.optimizer.name == OptimizerType.lionw
+    cfg = TrainConfig.load(write(tmp_path, "activation_checkpointing: false\n"))
+    assert cfg.activation_checkpointing is None
+
+
+def test_save_load_round_trip_and_helpers(tmp_path):
+    cfg = TrainConfig(model=ModelConfig(d_model=32, n_heads=2, n_layers=1), run_name="rt")
+    cfg.fsdp.sharding_strategy = ShardingStrategy.HYBRID_SHARD
+    cfg.save(tmp_path / "out.yaml")
+    again = TrainConfig.load(tmp_path / "out.yaml", validate_paths=False)
+    assert again == cfg
+    only_model = ModelConfig.load(tmp_path / "out.yaml", key="model")
+    assert only_model == cfg.model
+    clone = cfg.update_with(run_name="other")
+    assert clone.run_name == "other" and cfg.run_name == "rt"
+    d = cfg.asdict(exclude=["model"])
+    assert "model" not in d and d["run_name"] == "rt"
+    made = ModelConfig.new(d_model=16, n_heads=2)
+    assert made.d_model == 16
+    assert cfg.distributed_strategy in (DistributedStrategy.fsdp, None) or isinstance(cfg.distributed_strategy, DistributedStrategy)
+    assert CheckpointType("sharded") == CheckpointType.sharded
+
+
+def test_model_config_derived_quantities():
+    m = ModelConfig(d_model=128, n_heads=8, n_kv_heads=2, n_layers=2)
+    assert m.effective_n_kv_heads == 2
+    assert ModelConfig(d_model=128, n_heads=8, multi_query_attention=True).effective_n_kv_heads == 1
+    assert ModelConfig(d_model=128, n_heads=8).effective_n_kv_heads == 8
+    with pytest.raises(OLMoConfigurationError):
+        ModelConfig(d_model=128, n_heads=8, multi_query_attention=True, n_kv_heads=2).effective_n_kv_heads
+
+
+def test_dotlist_parsing_types():
+    got = S.parse_dotlist(["a.b=1", "a.c=2.5", "x=null", "y=[1,2]", "z=true", "s=hello world", "t=1e-5"])
+    assert got == {"a": {"b": 1, "c": 2.5}, "x": None, "y": [1, 2], "z": True, "s": "hello world", "t": 1e-5}
+    assert S.deep_merge({"a": {"b": 1, "c": 2}}, {"a": {"c": 3}}) == {"a": {"b": 1, "c": 3}}
+
+
+@pytest.mark.parametrize("name", sorted(RECIPES))
+def test_every_recipe_builds(name):
+    cfg = recipe_config(name)
+    fam = MODEL_FAMILIES[RECIPES[name]["family"]]
+    assert cfg.model.d_model == fam["d_model"] and cfg.model.n_layers == fam["n_layers"]
+    assert cfg.model.d_model % cfg.model.n_heads == 0
+    assert cfg.global_train_batch_size % cfg.device_train_microbatch_size == 0
+    assert cfg.device_eval_batch_size == cfg.device_train_microbatch_size
+    assert cfg.run_name == name
+
+
+def test_recipe_overrides_and_written_files(tmp_path):
+    cfg = recipe_config("OLMo2-7B-stage1", ["model.n_layers=2", "optimizer.learning_rate=1e-3"])
+    assert cfg.model.n_layers == 2 and cfg.optimizer.learning_rate == pytest.approx(1e-3)
+    assert cfg.model.mlp_hidden_size == 22016 and cfg.softmax_auxiliary_loss and cfg.fused_loss
+    paths = write_configs(tmp_path)
+    assert len(paths) == len(RECIPES)
+    for p in paths:
+        loaded = TrainConfig.load(p, validate_paths=False)
+        assert loaded == recipe_config(loaded.run_name)
+
+
+def test_committed_config_files_match_the_recipes():
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent / "configs"
+    for name, spec in RECIPES.items():
+        on_disk = TrainConfig.load(root / spec["file"], validate_paths=False)
+        assert on_disk == recipe_config(name), f"configs/{spec['file']} is stale: rerun python -m olmo_b200.recipes --write configs"
