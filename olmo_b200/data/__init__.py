@@ -57,6 +57,16 @@ def build_collator(train_config: TrainConfig) -> DataCollator:
     custom = train_config.data.custom_dataset
     if custom is None:
         return DataCollator.from_train_config(train_config)
+    if custom.collate_fn:
+        # a user-supplied callable replaces the collator altogether (reference: olmo/data/__init__.py:56-88)
+        from .custom_datasets import build_custom_collate_fn
+
+        try:
+            return build_custom_collate_fn(train_config)  # type: ignore[return-value]
+        except AttributeError:
+            raise OLMoConfigurationError(
+                f"collate_fn {custom.collate_fn} not found. Please specify the full module path of the function."
+            ) from None
     fields = custom.collate_config
     kwargs = {} if fields is None else {
         "input_id_field": fields.input_id_field, "attention_mask_field": fields.attention_mask_field,

@@ -138,7 +138,7 @@ class IterableDataset(torch.utils.data.IterableDataset[Dict[str, Any]]):
     def _get_dataset_item(self, idx: int) -> Dict[str, Any]:
         item = self.dataset[idx]
         if isinstance(item, dict):
-            return dict(**item, index=idx)
+            return {**item, "index": idx}
         if dataclasses.is_dataclass(item):
             return dict(**dataclasses.asdict(item), index=idx)  # type: ignore[arg-type]
         return {"input_ids": item, "index": idx}
