@@ -103,6 +103,8 @@ class Optimizer(OptimizerBase):
         """
         self._collecting_metrics = collect_param_metrics
         device = get_default_device() if device is None else device
+        if self._engine is not None:
+            self._engine.finish_grad_sync()  # gradients of all micro-batches are reduced into the local shards first
 
         fast = self._fused_clip(global_step, collect_param_metrics, process_group)
         if fast is not None:
@@ -303,6 +305,8 @@ class LionW(Optimizer):
             eng.fused_optimizer_step(self, "lionw", getattr(self, "_pending_gscale", None))
             self._pending_gscale = None
             return
+        if eng is not None:
+            eng.finish_grad_sync()
         dev = self._device or get_default_device()
         dot = torch.zeros((), dtype=torch.float32, device=dev)
         upd_sq = torch.zeros((), dtype=torch.float32, device=dev)
@@ -387,6 +391,8 @@ class AdamW(Optimizer):
             eng.fused_optimizer_step(self, "adamw", getattr(self, "_pending_gscale", None))
             self._pending_gscale = None
             return
+        if eng is not None:
+            eng.finish_grad_sync()
         dev = get_default_device()
         names: List[str] = []
         norms: List[torch.Tensor] = []

@@ -1,0 +1,110 @@
+"""Multi-process CPU tests over gloo: sharded training equals single-process training, checkpoints re-shard across
+world sizes, cancellation is agreed on by all ranks, and a rank that disappears surfaces as an error on the others."""
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+WORKER = Path(__file__).resolve().parent / "dist_cpu_worker.py"
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def launch(nproc: int, scenario: str, out: Path, work: Path, *extra: str, expect_ok: bool = True, timeout: int = 600):
+    work.mkdir(parents=True, exist_ok=True)
+    env = dict(os.environ, OMP_NUM_THREADS="2", CUDA_VISIBLE_DEVICES="")
+    args = [str(WORKER), scenario, "--out", str(out), "--work", str(work), *extra]
+    if nproc == 1:
+        cmd = [sys.executable, *args]
+    else:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}", "--master-addr", "127.0.0.1",
+               "--master-port", str(_free_port()), *args]
+    proc = subprocess.run(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, timeout=timeout)
+    if expect_ok:
+        assert proc.returncode == 0, proc.stdout[-5000:]
+        return torch.load(out, weights_only=False)
+    return proc
+
+
+def assert_same_training(a, b, what, tol=2e-5):
+    for x, y in zip(a["steps"], b["steps"]):
+        assert abs(x["loss"] - y["loss"]) < 1e-4, f"{what}: {a['steps']} vs {b['steps']}"
+        assert abs(x["norm"] - y["norm"]) < 1e-3 * max(1.0, y["norm"]), f"{what}: {a['steps']} vs {b['steps']}"
+    for name, t in a["state"].items():
+        torch.testing.assert_close(t, b["state"][name], rtol=1e-4, atol=tol, msg=lambda m: f"{what}: {name}: {m}")
+
+
+@pytest.fixture(scope="module")
+def single(tmp_path_factory):
+    d = tmp_path_factory.mktemp("single")
+    return launch(1, "train", d / "one.pt", d / "work")
+
+
+@pytest.mark.parametrize(
+    "nproc,extra",
+    [
+        (2, ("--wrap", "by_block_and_size")),
+        (2, ("--strategy", "NO_SHARD")),
+        (4, ("--strategy", "HYBRID_SHARD", "--replicas", "2")),
+    ],
+)
+def test_sharded_training_matches_single_process(tmp_path, single, nproc, extra):
+    multi = launch(nproc, "train", tmp_path / "multi.pt", tmp_path / "work", *extra)
+    assert multi["world"] == nproc
+    assert_same_training(multi, single, f"{nproc} ranks {extra}")
+
+
+def test_lion_sharded_matches_single(tmp_path):
+    one = launch(1, "train", tmp_path / "one.pt", tmp_path / "w1", "--optimizer", "lionw")
+    two = launch(2, "train", tmp_path / "two.pt", tmp_path / "w2", "--optimizer", "lionw")
+    assert_same_training(two, one, "lion 2 ranks", tol=5e-3)  # sign updates amplify last-bit differences
+
+
+@pytest.mark.parametrize("checkpointer", ["olmo_core"])
+def test_checkpoint_resharding_across_world_sizes(tmp_path, checkpointer):
+    saved = launch(2, "save", tmp_path / "saved.pt", tmp_path / "run", "--checkpointer", checkpointer)
+    sharded, unsharded = Path(saved["sharded"]), Path(saved["unsharded"])
+    assert (sharded / "config.yaml").is_file() and (unsharded / "config.yaml").is_file()
+    assert (unsharded / "model.safetensors").is_file() or (unsharded / "model.pt").is_file()
+
+    # same world size, fewer ranks, and the unsharded checkpoint all restore the same weights and the same next step
+    for nproc, load in ((1, sharded), (4, sharded), (2, unsharded)):
+        got = launch(nproc, "restore", tmp_path / f"r{nproc}_{load.name}.pt", tmp_path / f"w{nproc}_{load.name}", "--load", str(load),
+                     "--checkpointer", checkpointer, "--force-fsdp")
+        assert got["global_step"] == 3
+        for name, t in got["state"].items():
+            torch.testing.assert_close(t, saved["state"][name], rtol=0, atol=0, msg=lambda m: f"{nproc} ranks from {load.name}: {name}: {m}")
+        assert abs(got["next"][0]["loss"] - saved["next"][0]["loss"]) < 1e-4, (nproc, load.name)
+
+    # offline conversion: sharded directory -> full tensors, no process group
+    from olmo_b200.checkpoint import build_sharded_checkpointer
+    from olmo_b200.config import TrainConfig
+
+    cfg = TrainConfig.load(sharded / "config.yaml", validate_paths=False)
+    model_state, optim_state, trainer_state = build_sharded_checkpointer(cfg).unshard_checkpoint(sharded)
+    for name, t in saved["state"].items():
+        torch.testing.assert_close(model_state[name], t, rtol=0, atol=0)
+    assert trainer_state["global_step"] == 3
+    assert optim_state is not None and len(optim_state["state"]) == len(saved["state"])
+
+
+def test_all_ranks_agree_on_cancellation(tmp_path):
+    got = launch(2, "cancel", tmp_path / "c.pt", tmp_path / "w", "--time-limit", "100")
+    assert got["stopped_at"] == 1
+
+
+def test_lost_rank_is_reported_not_hung(tmp_path):
+    out = tmp_path / "lost.pt"
+    proc = launch(2, "lost_rank", out, tmp_path / "w", "--pg-timeout", "8", expect_ok=False, timeout=300)
+    survivor = torch.load(f"{out}.rank0", weights_only=False)
+    assert torch.load(f"{out}.rank1", weights_only=False)["left"]
+    assert survivor["error"] is not None, proc.stdout[-3000:]
+    assert survivor["waited"] < 60
