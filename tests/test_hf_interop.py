@@ -1,0 +1,118 @@
+"""HuggingFace interoperability: auto classes, save/load round trip, and exact agreement between this model and the
+architectures that ship inside ``transformers`` after conversion (an independent implementation of the same maths)."""
+import json
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+import hf_olmo  # noqa: E402,F401  (registers the auto classes)
+from olmo_b200.config import ModelConfig, TokenizerConfig, TrainConfig  # noqa: E402
+from olmo_b200.hf import OLMoConfig, OLMoForCausalLM  # noqa: E402
+from olmo_b200.hf.convert import to_transformers_state_dict, transformers_config_dict, write_hf_olmo_checkpoint, write_transformers_checkpoint  # noqa: E402
+from olmo_b200.models.olmo import OLMo  # noqa: E402
+
+OLMO2 = dict(d_model=64, n_heads=4, n_layers=2, mlp_hidden_size=256, vocab_size=120, embedding_size=128, max_sequence_length=64,
+             weight_tying=False, include_bias=False, rope=True, rope_theta=500000, flash_attention=False, layer_norm_type="rms",
+             layer_norm_with_affine=True, layer_norm_eps=1e-6, bias_for_layer_norm=False, attention_layer_norm=True,
+             attention_layer_norm_with_affine=True, norm_after=True, eos_token_id=119, pad_token_id=118, init_device="cpu", init_std=0.05)
+OLMO1 = dict(d_model=64, n_heads=4, n_layers=2, mlp_hidden_size=256, vocab_size=120, embedding_size=128, max_sequence_length=64,
+             weight_tying=False, include_bias=False, rope=True, flash_attention=False, layer_norm_type="default",
+             layer_norm_with_affine=False, attention_layer_norm=False, clip_qkv=0.5, eos_token_id=119, pad_token_id=118,
+             init_device="cpu", init_fn="mitchell")
+
+
+def native(kwargs):
+    torch.manual_seed(0)
+    m = OLMo(ModelConfig(**kwargs))
+    m.reset_parameters()
+    with torch.no_grad():  # make the norm weights non-trivial
+        for n, p in m.named_parameters():
+            if "norm" in n or "ln_f" in n:
+                p.uniform_(0.5, 1.5)
+    return m.eval()
+
+
+def save_unsharded(model: OLMo, folder):
+    folder.mkdir(parents=True, exist_ok=True)
+    TrainConfig(model=model.config, tokenizer=TokenizerConfig(identifier="missing-tokenizer.json")).save(folder / "config.yaml")
+    torch.save(model.state_dict(), folder / "model.pt")
+    return folder
+
+
+@pytest.mark.parametrize("kwargs,cls_name", [(OLMO2, "Olmo2ForCausalLM"), (OLMO1, "OlmoForCausalLM")])
+def test_converted_weights_reproduce_logits_in_transformers(tmp_path, kwargs, cls_name):
+    model = native(kwargs)
+    out_dir, model_type = write_transformers_checkpoint(save_unsharded(model, tmp_path / "ckpt"), tmp_path / "hf")
+    assert json.loads((out_dir / "config.json").read_text())["architectures"] == [cls_name]
+    hf = transformers.AutoModelForCausalLM.from_pretrained(str(out_dir), torch_dtype=torch.float32, attn_implementation="eager").eval()
+    assert type(hf).__name__ == cls_name
+    ids = torch.randint(0, 118, (2, 17))
+    with torch.no_grad():
+        ours = model(ids).logits
+        theirs = hf(ids).logits
+    torch.testing.assert_close(ours, theirs, rtol=2e-4, atol=2e-4)
+    # greedy continuations agree as well (KV cache paths of both implementations)
+    with torch.no_grad():
+        gen_hf = hf.generate(ids, max_new_tokens=5, do_sample=False, attention_mask=torch.ones_like(ids), pad_token_id=118)
+        gen_ours = OLMoForCausalLM(OLMoConfig(**model.config.asdict()), model=model).generate(
+            ids, max_new_tokens=5, do_sample=False, attention_mask=torch.ones_like(ids), pad_token_id=118
+        )
+    assert gen_hf.tolist() == gen_ours.tolist()
+
+
+def test_state_dict_mapping_rejects_unsupported_architectures():
+    with pytest.raises(ValueError):
+        transformers_config_dict(ModelConfig(**{**OLMO2, "alibi": True, "rope": False}))
+    with pytest.raises(ValueError):
+        transformers_config_dict(ModelConfig(**{**OLMO2, "norm_after": False}))
+    with pytest.raises(ValueError):
+        transformers_config_dict(ModelConfig(**{**OLMO1, "block_type": "llama"}))
+    cfg = ModelConfig(**{**OLMO2, "n_kv_heads": 2})
+    m = native({**OLMO2, "n_kv_heads": 2})
+    sd = to_transformers_state_dict(m.state_dict(), cfg)
+    assert sd["model.layers.0.self_attn.k_proj.weight"].shape == (32, 64)
+    assert sd["model.layers.1.mlp.gate_proj.weight"].shape == (128, 64)
+    assert transformers_config_dict(cfg)["num_key_value_heads"] == 2
+
+
+def test_hf_olmo_layout_round_trip_and_auto_classes(tmp_path):
+    model = native(OLMO2)
+    folder = write_hf_olmo_checkpoint(save_unsharded(model, tmp_path / "ckpt"), tmp_path / "hf_olmo")
+    cfg = transformers.AutoConfig.from_pretrained(str(folder))
+    assert isinstance(cfg, OLMoConfig) and cfg.model_type == "hf_olmo" and cfg.hidden_size == 64 and cfg.num_hidden_layers == 2
+    loaded = transformers.AutoModelForCausalLM.from_pretrained(str(folder), torch_dtype=torch.float32).eval()
+    assert isinstance(loaded, OLMoForCausalLM)
+    ids = torch.randint(0, 118, (2, 9))
+    with torch.no_grad():
+        torch.testing.assert_close(loaded(ids).logits, model(ids).logits)
+        out = loaded(ids, labels=ids)
+    want = torch.nn.functional.cross_entropy(out.logits[:, :-1].reshape(-1, 128), ids[:, 1:].reshape(-1))
+    torch.testing.assert_close(out.loss, want)
+    loaded.save_pretrained(str(tmp_path / "again"))
+    again = OLMoForCausalLM.from_pretrained(str(tmp_path / "again"), torch_dtype=torch.float32).eval()
+    with torch.no_grad():
+        torch.testing.assert_close(again(ids).logits, model(ids).logits)
+
+
+def test_wrapper_toggles_and_embedding_resize():
+    wrapper = OLMoForCausalLM(OLMoConfig(**{**OLMO2, "weight_tying": True}), init_params=True)
+    assert wrapper.get_output_embeddings() is wrapper.get_input_embeddings()
+    wrapper.gradient_checkpointing = True
+    assert wrapper.model.activation_checkpointing_strategy is not None
+    wrapper.gradient_checkpointing = False
+    assert wrapper.model.activation_checkpointing_strategy is None
+    before = wrapper.get_input_embeddings().weight.detach().clone()
+    emb = wrapper.resize_token_embeddings(130, pad_to_multiple_of=64)
+    assert emb.weight.shape == (192, 64) and wrapper.config.embedding_size == 192 and wrapper.model.config.embedding_size == 192
+    torch.testing.assert_close(emb.weight[:128], before)
+    ids = torch.randint(0, 118, (1, 5))
+    assert wrapper(ids).logits.shape == (1, 5, 192)
+    untied = OLMoForCausalLM(OLMoConfig(**OLMO2), init_params=True)
+    untied.resize_token_embeddings(256)
+    assert untied.model.transformer.ff_out.out_features == 256 and untied(ids).logits.shape[-1] == 256
+    with pytest.raises(ValueError):
+        untied(ids, output_attentions=True)
+    cfg = OLMoConfig(n_heads=8, multi_query_attention=True)
+    assert cfg.effective_n_kv_heads == 1 and OLMoConfig(n_heads=8, n_kv_heads=2).effective_n_kv_heads == 2
