@@ -56,6 +56,8 @@ __all__ = [
     "upload",
     "get_bytes_range",
     "find_latest_checkpoint",
+    "list_files",
+    "delete_file",
     "StorageBackend",
     "register_storage_backend",
     "default_thread_count",
@@ -297,6 +299,14 @@ class StorageBackend:
     def find_latest_checkpoint(self, url: str) -> Optional[str]:
         raise NotImplementedError(f"find_latest_checkpoint is not supported for {url}")
 
+    def list_files(self, url: str) -> List[str]:
+        """Full URLs of every file below the folder / prefix ``url``."""
+        raise NotImplementedError(f"listing is not supported for {url}")
+
+    def delete(self, url: str) -> None:
+        """Remove one file."""
+        raise NotImplementedError(f"delete is not supported for {url}")
+
 
 class _LocalBackend(StorageBackend):
     @staticmethod
@@ -326,6 +336,13 @@ class _LocalBackend(StorageBackend):
             return None
         name = _pick_latest(p.name for p in root.iterdir() if p.is_dir())
         return None if name is None else str(root / name)
+
+    def list_files(self, url: str) -> List[str]:
+        root = Path(self._p(url))
+        return sorted(str(p) for p in root.rglob("*") if p.is_file()) if root.is_dir() else []
+
+    def delete(self, url: str) -> None:
+        Path(self._p(url)).unlink(missing_ok=True)
 
 
 def _retry(fn: Callable[[], Any], what: str, max_attempts: int = 3) -> Any:
@@ -480,6 +497,26 @@ class _S3Backend(StorageBackend):
         best = _pick_latest(names)
         return None if best is None else f"{scheme}://{bucket}/{prefix}{best}"
 
+    def list_files(self, url: str) -> List[str]:
+        scheme, bucket, prefix = self._split(url)
+        if prefix and not prefix.endswith("/"):
+            prefix += "/"
+        out: List[str] = []
+        token: Optional[str] = None
+        while True:
+            kwargs = {"Bucket": bucket, "Prefix": prefix}
+            if token:
+                kwargs["ContinuationToken"] = token
+            resp = _retry(lambda: self._client(scheme).list_objects_v2(**kwargs), f"list {url}")
+            out += [f"{scheme}://{bucket}/{item['Key']}" for item in resp.get("Contents", [])]
+            token = resp.get("NextContinuationToken")
+            if not token:
+                return sorted(out)
+
+    def delete(self, url: str) -> None:
+        scheme, bucket, key = self._split(url)
+        _retry(lambda: self._client(scheme).delete_object(Bucket=bucket, Key=key), f"delete {url}")
+
 
 class _GcsBackend(StorageBackend):
     def _bucket(self, name: str):
@@ -533,6 +570,16 @@ class _GcsBackend(StorageBackend):
                 complete.add(d)
         best = _pick_latest(n for n in names if n in complete)
         return None if best is None else f"gs://{bucket}/{prefix}{best}"
+
+    def list_files(self, url: str) -> List[str]:
+        bucket, prefix = self._split(url)
+        if prefix and not prefix.endswith("/"):
+            prefix += "/"
+        return sorted(f"gs://{bucket}/{blob.name}" for blob in self._bucket(bucket).list_blobs(prefix=prefix))
+
+    def delete(self, url: str) -> None:
+        bucket, key = self._split(url)
+        _retry(lambda: self._bucket(bucket).blob(key).delete(), f"delete {url}")
 
 
 _BACKENDS: Dict[str, StorageBackend] = {}
@@ -591,6 +638,18 @@ def find_latest_checkpoint(dir: PathOrStr) -> Optional[PathOrStr]:
     if found is None:
         return None
     return found if is_url(found) else Path(found)
+
+
+def list_files(folder: PathOrStr) -> List[str]:
+    """Every file below a local folder or remote prefix (full paths / URLs, sorted)."""
+    backend, s = _backend_for(folder)
+    return backend.list_files(s)
+
+
+def delete_file(path: PathOrStr) -> None:
+    """Remove one local or remote file."""
+    backend, s = _backend_for(path)
+    backend.delete(s)
 
 
 def resource_path(

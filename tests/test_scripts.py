@@ -1,0 +1,223 @@
+"""User-facing scripts: data preparation, dataloader replay / inspection, ladder laws, storage housekeeping, comparisons."""
+import gzip
+import importlib.util
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+SCRIPTS = ROOT / "scripts"
+
+
+def load_script(name: str):
+    spec = importlib.util.spec_from_file_location(f"script_{name}", SCRIPTS / f"{name}.py")
+    module = importlib.util.module_from_spec(spec)
+    sys.path.insert(0, str(SCRIPTS))
+    try:
+        spec.loader.exec_module(module)
+    finally:
+        sys.path.remove(str(SCRIPTS))
+    return module
+
+
+@pytest.fixture(scope="module")
+def tokenizer_json(tmp_path_factory):
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    words = [f"w{i}" for i in range(40)] + ["<|user|>", "<|assistant|>", "hello", "there", "ok"]
+    vocab = {w: i for i, w in enumerate(words)}
+    vocab["<unk>"] = len(vocab)
+    vocab["<pad>"] = len(vocab)
+    vocab["<eos>"] = len(vocab)
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="<unk>"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.add_special_tokens(["<eos>", "<pad>"])
+    path = tmp_path_factory.mktemp("tok") / "tokenizer.json"
+    tok.save(str(path))
+    return path, vocab
+
+
+def test_prepare_memmap_dataset_round_trip(tmp_path, tokenizer_json):
+    path, vocab = tokenizer_json
+    docs = [" ".join(f"w{(i + j) % 40}" for j in range(5 + i % 7)) for i in range(30)]
+    src = tmp_path / "docs"
+    src.mkdir()
+    with gzip.open(src / "a.json.gz", "wt") as f:
+        f.write("\n".join(json.dumps({"text": d}) for d in docs[:20]))
+    (src / "b.jsonl").write_text("\n".join(json.dumps({"text": d}) for d in docs[20:]))
+    mod = load_script("prepare_memmap_dataset")
+    total = mod.main([str(src), "-o", str(tmp_path / "out"), "--tokenizer", str(path), "--max-tokens", "64", "--validate", "--paths-per-worker", "2"])
+    files = sorted((tmp_path / "out").glob("*.npy"))
+    assert len(files) >= 2  # the 64-token cap forces several parts
+    tokens = np.concatenate([np.memmap(f, dtype=np.uint16, mode="r") for f in files])
+    assert len(tokens) == total == sum(len(d.split()) + 1 for d in docs)
+    assert int((tokens == vocab["<eos>"]).sum()) == 30
+    assert all(np.memmap(f, dtype=np.uint16, mode="r").shape[0] <= 64 for f in files)
+    # and the training dataset reads them
+    from olmo_b200.data import MemMapDataset
+
+    ds = MemMapDataset(*files, chunk_size=8)
+    assert len(ds) == sum(np.memmap(f, dtype=np.uint16, mode="r").shape[0] // 8 for f in files)
+
+
+def test_prepare_tulu_data_masks_only_assistant_turns(tmp_path, tokenizer_json):
+    path, vocab = tokenizer_json
+    convs = [
+        {"messages": [{"role": "user", "content": "hello there"}, {"role": "assistant", "content": "ok w1"}]},
+        {"messages": [{"role": "user", "content": "hello"}]},  # no assistant turn: dropped
+    ]
+    src = tmp_path / "c.jsonl"
+    src.write_text("\n".join(json.dumps(c) for c in convs))
+    mod = load_script("prepare_tulu_data")
+    kept = mod.main([str(tmp_path / "out"), "--source", str(src), "-t", str(path), "-s", "16", "--eos", str(vocab["<eos>"]), "--pad", str(vocab["<pad>"])])
+    assert kept == 1
+    ids = np.memmap(tmp_path / "out" / "input_ids.npy", dtype=np.uint16, mode="r")
+    mask = np.memmap(tmp_path / "out" / "label_mask.npy", dtype=np.bool_, mode="r")
+    assert len(ids) == len(mask) == 16 and ids[0] == vocab["<eos>"]
+    trained = [int(t) for t, m in zip(ids, mask) if m]
+    assert trained == [vocab["ok"], vocab["w1"], vocab["<eos>"]]
+    assert ids[-1] == vocab["<pad>"] and not mask[-1]
+
+
+@pytest.fixture()
+def tiny_run(tmp_path):
+    from olmo_b200.config import DataConfig, ModelConfig, TrainConfig
+
+    files = []
+    for i in range(2):
+        f = tmp_path / f"part{i}.npy"
+        arr = np.memmap(f, dtype=np.uint16, mode="w+", shape=(512,))
+        arr[:] = np.arange(i * 512, (i + 1) * 512) % 1000
+        arr.flush()
+        files.append(str(f))
+    cfg = TrainConfig(
+        run_name="tiny", model=ModelConfig(max_sequence_length=16, vocab_size=1000, embedding_size=1024, pad_token_id=0, eos_token_id=1),
+        data=DataConfig(paths=files, num_workers=0, drop_last=True, pin_memory=False, prefetch_factor=None, persistent_workers=False),
+        global_train_batch_size=4, device_train_microbatch_size=2, seed=11, save_folder=str(tmp_path / "run"),
+    )
+    (tmp_path / "run").mkdir()
+    cfg.save(tmp_path / "run" / "config.yaml")
+    return tmp_path / "run", cfg
+
+
+def test_run_dataloader_and_inspect_agree(tiny_run, capsys):
+    run, cfg = tiny_run
+    replay = load_script("run_dataloader")
+    from olmo_b200.config import TrainConfig
+
+    out = run / "batches"
+    out.mkdir()
+    n = replay.main(TrainConfig.load(run / "config.yaml"), out, world_size=2, rank=1, max_batches=5, batches_per_file=3)
+    assert n == 5
+    files = sorted(out.glob("input_ids-*.npy"))
+    assert [f.name for f in files] == ["input_ids-0000000-0000003.npy", "input_ids-0000003-0000005.npy"]
+    first = np.load(files[0])
+    assert first.shape == (3, 2, 16) and first.dtype == np.uint16  # 3 batches, 2 sequences per rank
+
+    inspect = load_script("inspect_train_data")
+    inspect.main([str(run), "1", "1", "3", "--world_size", "2", "--no_data_indices", "--ids"])
+    printed = capsys.readouterr().out
+    # the replayed batches of rank 1 at steps 1 and 3 are exactly what the inspector derives
+    for step, batch in ((1, first[0]), (3, first[2])):
+        for ex, row in enumerate(batch):
+            assert f"[step={step}, rank=1, example={ex}," in printed
+            assert str(row.tolist()) in printed
+
+    # with recorded indices the same examples come back
+    (run / "data-indices").mkdir()
+    index_of = {}
+    from olmo_b200.data import build_memmap_dataset
+
+    ds = build_memmap_dataset(cfg, cfg.data)
+    for i in range(len(ds)):
+        index_of[tuple(ds[i]["input_ids"].tolist())] = i
+    with gzip.open(run / "data-indices" / "rank1.tsv.gz", "wt") as f:
+        f.write("1\t" + "\t".join(str(index_of[tuple(int(t) for t in row)]) for row in first[0]) + "\n")
+    inspect.main([str(run), "1", "1", "--ids"])
+    printed = capsys.readouterr().out
+    for row in first[0]:
+        assert str(row.tolist()) in printed
+
+
+def test_ladder_power_laws_and_node_counts():
+    from olmo_b200.ladder import batch_size_for, ladder_config, learning_rate_for, node_counts, parse_length, parse_size, size_for_model
+
+    assert parse_size("150M") == 150_000_000 and parse_size("7b") == 7_000_000_000
+    assert parse_length("2xC", 10**9) == 40 * 10**9 and parse_length("5B", 1) == 5 * 10**9 and parse_length("3T", 1) == 3 * 10**12
+    with pytest.raises(ValueError):
+        parse_length("5Q", 1)
+    assert batch_size_for(150_000_000) == 192 and batch_size_for(10**9) == 704
+    assert learning_rate_for(108_000_000) == pytest.approx(0.0047)
+    assert learning_rate_for(864_000_000) == pytest.approx(0.0047 / 2)
+    cfg = ladder_config("1B", "1xC", "t")
+    assert cfg.global_train_batch_size == 704 and cfg.max_duration == f"{20 * 10**9}T"
+    assert cfg.scheduler.t_warmup == round(10**9 / (704 * 2048)) and str(cfg.distributed_strategy) == "ddp"
+    assert cfg.global_train_batch_size % cfg.device_train_microbatch_size == 0
+    assert str(ladder_config("7B", "1xC", "t").distributed_strategy) == "fsdp"
+    assert node_counts(cfg, 8) == [11, 1]
+    total, non_emb = size_for_model("150M")
+    assert 150e6 < non_emb < total < 200e6
+    out = subprocess.run([sys.executable, str(SCRIPTS / "ladder.py"), "size", "--model", "300M"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and len(out.stdout.split()) == 2
+
+
+def test_named_data_mixes(tmp_path, monkeypatch):
+    from olmo_b200.data.named_data_mixes import DATA_PATHS, register_mix, resolve_mix
+
+    (tmp_path / "data_mixes").mkdir()
+    (tmp_path / "data_mixes" / "toy.txt").write_text("# comment\npart/a.npy\n\npart/b.npy  # trailing\n")
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+    assert DATA_PATHS["toy"] == ["part/a.npy", "part/b.npy"] and "toy" in list(DATA_PATHS)
+    assert resolve_mix("toy", "s3://bucket/root/") == ["s3://bucket/root/part/a.npy", "s3://bucket/root/part/b.npy"]
+    register_mix("mem", ["x.npy"])
+    assert DATA_PATHS["mem"] == ["x.npy"]
+    with pytest.raises(KeyError):
+        DATA_PATHS["nope"]
+
+
+def test_storage_cleaner_and_compare(tmp_path, capsys):
+    cleaner = load_script("storage_cleaner")
+    root = tmp_path / "runs"
+    for run, steps in (("good", [100, 200, 300]), ("dead", [0]), ("empty", [])):
+        (root / run).mkdir(parents=True)
+        (root / run / "config.yaml").write_text("run_name: x\n")
+        for s in steps:
+            (root / run / f"step{s}").mkdir()
+            (root / run / f"step{s}" / "model.pt").write_bytes(b"x" * 10)
+    assert sorted(Path(r).name for r in cleaner.clean(str(root), 0, dry_run=True)) == ["dead", "empty"]
+    assert (root / "dead").exists()
+    cleaner.main(["clean", str(root)])
+    assert sorted(p.name for p in root.iterdir()) == ["good"]
+    n = cleaner.main(["move", str(root / "good"), str(tmp_path / "moved"), "--keep-latest", "2"])
+    assert n == 3 and sorted(p.name for p in (tmp_path / "moved").iterdir()) == ["config.yaml", "step200", "step300"]
+
+    cmp_state = load_script("compare_model_state")
+    a = {"w": torch.ones(3), "only_a": torch.zeros(1), "nest": {"v": torch.ones(2)}}
+    b = {"w": torch.ones(3) * 1.5, "nest": {"v": torch.ones(2)}}
+    bad = cmp_state.compare(cmp_state.flatten("", a, {}), cmp_state.flatten("", b, {}), top=5, rtol=0.0)
+    assert bad == 2
+    assert "only in base:    only_a" in capsys.readouterr().out
+
+    traces_a, traces_b = tmp_path / "ta", tmp_path / "tb"
+    for folder, scale in ((traces_a, 1.0), (traces_b, 1.0)):
+        folder.mkdir()
+        for i in range(3):
+            torch.save(torch.full((4,), float(i)) * scale, folder / f"model.transformer.blocks.{i}_0_output.pt")
+    torch.save(torch.full((4,), 9.0), traces_b / "model.transformer.blocks.1_0_output.pt")
+    proc = subprocess.run([sys.executable, str(SCRIPTS / "compare_module_outputs.py"), str(traces_a), str(traces_b)], capture_output=True, text=True, timeout=300)
+    assert proc.returncode == 1 and "first divergence: model.transformer.blocks.1_0_output.pt" in proc.stdout
+
+
+def test_wandb_helpers_parse_and_diff():
+    mod = load_script("compare_wandb_configs")
+    assert mod.parse_run_path("https://wandb.ai/ai2/olmo/runs/abc123?x=1") == "ai2/olmo/abc123"
+    assert mod.parse_run_path("ai2/olmo/abc123") == "ai2/olmo/abc123"
+    rows = list(mod.diff({"a": 1, "m": {"x": [1, 2]}, "save_folder": "p"}, {"a": 2, "m": {"x": [1, 3]}, "save_folder": "q"}))
+    assert rows == [("a", 1, 2), ("m.x.1", 2, 3)]
