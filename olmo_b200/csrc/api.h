@@ -86,6 +86,12 @@ int ob_sumsq_num_partials(long long n);
 int ob_sumsq_f32(const float* g, long long n, float* partials, float* out, int accumulate, cudaStream_t stream);
 int ob_clip_coef(const float* sumsq, float max_norm, float* coef, float* norm_out, cudaStream_t stream);
 
+// 4-bit weight / bf16 activation inference (w4a16.cu).  qweight [N, K/8] int32, scales [N, K/G] bf16, zeros [N, K/G] uint8.
+int ob_w4a16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, int M, int N, int K, int group,
+                  cudaStream_t stream);  // 1 <= M <= 8
+int ob_w4a16_dequant(const void* qweight, const void* scales, const void* zeros, void* out, int N, int K, int group, cudaStream_t stream);
+int ob_gather_columns_bf16(const void* x, const int* perm, void* out, int M, int K, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
