@@ -116,40 +116,50 @@ __global__ void __launch_bounds__(NT) norm_fwd_kernel(const bf16* __restrict__ x
 }
 
 // dx = [dres +] rstd * (g - mean(g) - xhat * mean(g * xhat)),  g = dy * w   (RMS: the mean(g) term is absent)
-template <bool RMS>
-__global__ void __launch_bounds__(NT) norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
-                                                      const bf16* __restrict__ w, const float* __restrict__ rstd_in,
-                                                      const float* __restrict__ mean_in, const bf16* __restrict__ dres,
-                                                      bf16* __restrict__ dx, float* __restrict__ dw_part,
-                                                      float* __restrict__ db_part, int M, int D, int ldx, int lddx) {
+// Backward.  NV = 16-byte vectors per thread (the CTA has D / (8 * NV) threads, at most 512), BIAS = also reduce db.
+// Keeping NV small (1 for D <= 4096) holds the kernel near 64 registers so that several CTAs share an SM and the loads
+// of different rows overlap; with one large CTA per SM the per-row reduction latency was the bound.
+template <bool RMS, int NV, bool BIAS>
+__global__ void __launch_bounds__(512) norm_bwd_kernel(const bf16* __restrict__ dy, const bf16* __restrict__ x,
+                                                       const bf16* __restrict__ w, const float* __restrict__ rstd_in,
+                                                       const float* __restrict__ mean_in, const bf16* __restrict__ dres,
+                                                       bf16* __restrict__ dx, float* __restrict__ dw_part,
+                                                       float* __restrict__ db_part, int M, int D, int ldx, int lddx) {
   __shared__ float red[32];
   const int nvec = D >> 3;
-  float dw_acc[MAXV][8], db_acc[MAXV][8];
+  const int nt = blockDim.x;
+  float dw_acc[NV][8], db_acc[BIAS ? NV : 1][8];
+  float wv[NV][8];
 #pragma unroll
-  for (int i = 0; i < MAXV; ++i)
+  for (int i = 0; i < NV; ++i) {
+    const int vi = threadIdx.x + i * nt;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) dw_acc[i][j] = db_acc[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) {
+      dw_acc[i][j] = 0.f;
+      if (BIAS) db_acc[i][j] = 0.f;
+      wv[i][j] = 1.f;
+    }
+    if (w != nullptr && vi < nvec) load8(w + vi * 8, wv[i]);
+  }
 
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     const float rstd = rstd_in[row];
     const float mean = RMS ? 0.f : mean_in[row];
-    float g[MAXV][8], xh[MAXV][8];
+    float g[NV][8], xh[NV][8];
     float sg = 0.f, sgx = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+    for (int i = 0; i < NV; ++i) {
+      const int vi = threadIdx.x + i * nt;
       if (vi < nvec) {
         float dyv[8], xv[8];
         load8(dy + static_cast<size_t>(row) * D + vi * 8, dyv);
         load8(x + static_cast<size_t>(row) * ldx + vi * 8, xv);
-        float wv[8];
-        if (w != nullptr) load8(w + vi * 8, wv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           xh[i][j] = (xv[j] - mean) * rstd;
           dw_acc[i][j] += dyv[j] * round_bf16(xh[i][j]);
-          db_acc[i][j] += dyv[j];
-          g[i][j] = (w != nullptr) ? dyv[j] * wv[j] : dyv[j];
+          if (BIAS) db_acc[i][j] += dyv[j];
+          g[i][j] = dyv[j] * wv[i][j];
           sg += g[i][j];
           sgx += g[i][j] * xh[i][j];
         }
@@ -159,8 +169,8 @@ __global__ void __launch_bounds__(NT) norm_bwd_kernel(const bf16* __restrict__ d
     if (!RMS) sg = block_sum(sg, red) / D;
     else sg = 0.f;
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+    for (int i = 0; i < NV; ++i) {
+      const int vi = threadIdx.x + i * nt;
       if (vi < nvec) {
         float o[8];
 #pragma unroll
@@ -177,13 +187,13 @@ __global__ void __launch_bounds__(NT) norm_bwd_kernel(const bf16* __restrict__ d
   }
   if (dw_part != nullptr) {
 #pragma unroll
-    for (int i = 0; i < MAXV; ++i) {
-      const int vi = threadIdx.x + i * NT;
+    for (int i = 0; i < NV; ++i) {
+      const int vi = threadIdx.x + i * nt;
       if (vi < nvec) {
         float* p = dw_part + static_cast<size_t>(blockIdx.x) * D + vi * 8;
         *reinterpret_cast<float4*>(p) = make_float4(dw_acc[i][0], dw_acc[i][1], dw_acc[i][2], dw_acc[i][3]);
         *reinterpret_cast<float4*>(p + 4) = make_float4(dw_acc[i][4], dw_acc[i][5], dw_acc[i][6], dw_acc[i][7]);
-        if (db_part != nullptr) {
+        if (BIAS) {
           float* q = db_part + static_cast<size_t>(blockIdx.x) * D + vi * 8;
           *reinterpret_cast<float4*>(q) = make_float4(db_acc[i][0], db_acc[i][1], db_acc[i][2], db_acc[i][3]);
           *reinterpret_cast<float4*>(q + 4) = make_float4(db_acc[i][4], db_acc[i][5], db_acc[i][6], db_acc[i][7]);
@@ -192,6 +202,16 @@ __global__ void __launch_bounds__(NT) norm_bwd_kernel(const bf16* __restrict__ d
     }
   }
 }
+
+template <bool RMS, int NV>
+void launch_norm_bwd(int grid, int threads, cudaStream_t stream, const bf16* dy, const bf16* x, const bf16* w, const float* rstd,
+                     const float* mean, const bf16* dres, bf16* dx, float* dw_part, float* db_part, int M, int D, int ldx, int lddx) {
+  if (db_part != nullptr && dw_part != nullptr)
+    norm_bwd_kernel<RMS, NV, true><<<grid, threads, 0, stream>>>(dy, x, w, rstd, mean, dres, dx, dw_part, db_part, M, D, ldx, lddx);
+  else
+    norm_bwd_kernel<RMS, NV, false><<<grid, threads, 0, stream>>>(dy, x, w, rstd, mean, dres, dx, dw_part, nullptr, M, D, ldx, lddx);
+}
+
 
 // out[d] (+)= sum_p part[p, d]
 __global__ void reduce_rows_f32_kernel(const float* __restrict__ part, int nparts, int D, float* __restrict__ out,
@@ -232,12 +252,20 @@ extern "C" int ob_norm_bwd(const void* dy, const void* x, const void* w, const f
   if (M <= 0) return 0;
   if (D % 8 != 0 || D > 8 * NT * MAXV || ldx % 8 != 0 || lddx % 8 != 0) return -1;
   const int grid = ob_norm_rows_per_launch(M);
-  if (is_rms)
-    norm_bwd_kernel<true><<<grid, NT, 0, stream>>>((const bf16*)dy, (const bf16*)x, (const bf16*)w, rstd, mean,
-                                                   (const bf16*)dres, (bf16*)dx, dw_part, db_part, M, D, ldx, lddx);
-  else
-    norm_bwd_kernel<false><<<grid, NT, 0, stream>>>((const bf16*)dy, (const bf16*)x, (const bf16*)w, rstd, mean,
-                                                    (const bf16*)dres, (bf16*)dx, dw_part, db_part, M, D, ldx, lddx);
+  // one vector per thread up to D = 4096 (<= 512 threads), two up to 8192
+  const int nvec = D / 8;
+  const int nv = nvec <= 512 ? 1 : (nvec <= 1024 ? 2 : 4);
+  int threads = (nvec + nv - 1) / nv;
+  threads = ((threads + 31) / 32) * 32;
+  const bf16 *dyp = (const bf16*)dy, *xp = (const bf16*)x, *wp = (const bf16*)w, *rp = (const bf16*)dres;
+  bf16* dxp = (bf16*)dx;
+#define OB_NORM_BWD(RMS_, NV_) launch_norm_bwd<RMS_, NV_>(grid, threads, stream, dyp, xp, wp, rstd, mean, rp, dxp, dw_part, db_part, M, D, ldx, lddx)
+  if (is_rms) {
+    if (nv == 1) OB_NORM_BWD(true, 1); else if (nv == 2) OB_NORM_BWD(true, 2); else OB_NORM_BWD(true, 4);
+  } else {
+    if (nv == 1) OB_NORM_BWD(false, 1); else if (nv == 2) OB_NORM_BWD(false, 2); else OB_NORM_BWD(false, 4);
+  }
+#undef OB_NORM_BWD
   return cudaGetLastError() == cudaSuccess ? grid : -11;
 }
 

@@ -49,10 +49,15 @@ def _p(t: Optional[torch.Tensor]):
     return ctypes.c_void_p(0 if t is None else t.data_ptr())
 
 
+def _host(t: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Contiguous host copy: the C++ code dereferences the pointer, so a device tensor must never reach it."""
+    return t.detach().to(device="cpu", dtype=dtype).contiguous()
+
+
 def dequant(qweight: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor, group: int, threads: int = 8) -> torch.Tensor:
     """``[N, K]`` fp32 weights (stored column order) from the packed representation (CPU tensors)."""
     n, k = qweight.shape[0], qweight.shape[1] * 8
-    q, s, z = qweight.contiguous().to(torch.int32), scales.contiguous().float(), zeros.contiguous().to(torch.uint8)
+    q, s, z = _host(qweight, torch.int32), _host(scales, torch.float32), _host(zeros, torch.uint8)
     out = torch.empty(n, k, dtype=torch.float32)
     rc = lib().ob_cpu_w4a16_dequant(_p(q), _p(s), _p(z), _p(out), n, k, group, threads)
     if rc != 0:
@@ -64,9 +69,9 @@ def matmul(x: torch.Tensor, qweight: torch.Tensor, scales: torch.Tensor, zeros: 
            perm: Optional[torch.Tensor] = None, threads: int = 8) -> torch.Tensor:
     """``x[M, K] · Wᵀ`` in fp32 on the CPU."""
     n, k = qweight.shape[0], qweight.shape[1] * 8
-    x2 = x.reshape(-1, k).contiguous().float()
-    q, s, z = qweight.contiguous().to(torch.int32), scales.contiguous().float(), zeros.contiguous().to(torch.uint8)
-    pm = None if perm is None else perm.contiguous().to(torch.int32)
+    x2 = _host(x.reshape(-1, k), torch.float32)
+    q, s, z = _host(qweight, torch.int32), _host(scales, torch.float32), _host(zeros, torch.uint8)
+    pm = None if perm is None else _host(perm, torch.int32)
     y = torch.empty(x2.shape[0], n, dtype=torch.float32)
     rc = lib().ob_cpu_w4a16_matmul(_p(x2), _p(q), _p(s), _p(z), _p(pm), _p(y), x2.shape[0], n, k, group, threads)
     if rc != 0:

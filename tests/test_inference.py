@@ -160,7 +160,9 @@ def test_gpu_kernels_match_cpu_reference(M, act_order):
     layer = QuantLinear.from_quantized(q, scales, zeros, G, perm=perm)
     x = torch.randn(M, K).to(torch.bfloat16)
     want = cpu_ref.matmul(x.float(), layer.qweight, layer.scales.float(), layer.zeros, G, layer.perm)
-    dev = layer.to("cuda")
+    import copy
+
+    dev = copy.deepcopy(layer).to("cuda")  # Module.to moves in place; keep the host copy for the reference
     got = dev(x.cuda()).float().cpu()
     torch.testing.assert_close(got, want, rtol=2e-2, atol=2e-2)
     torch.testing.assert_close(dev.dequantize().float().cpu(), cpu_ref.dequant(layer.qweight, layer.scales.float(), layer.zeros, G), rtol=1e-2, atol=1e-3)
