@@ -24,6 +24,16 @@ __device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
   }
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = unpack_bf16x2(w[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
 __device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
   uint4 o;
   o.x = pack_bf16x2(f[0], f[1]);
@@ -142,6 +152,20 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(const bf16* __restrict__ 
     if (w != nullptr && vi < nvec) load8(w + vi * 8, wv[i]);
   }
 
+  // The raw vectors of the next row are fetched before this row's reductions, so that a CTA always has two rows of
+  // loads in flight (the block-wide sums would otherwise serialise memory latency and synchronisation).
+  uint4 dy_raw[NV], x_raw[NV];
+  {
+    const int row = blockIdx.x;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = threadIdx.x + i * nt;
+      if (row < M && vi < nvec) {
+        dy_raw[i] = *reinterpret_cast<const uint4*>(dy + static_cast<size_t>(row) * D + vi * 8);
+        x_raw[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(row) * ldx + vi * 8);
+      }
+    }
+  }
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     const float rstd = rstd_in[row];
     const float mean = RMS ? 0.f : mean_in[row];
@@ -152,8 +176,8 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(const bf16* __restrict__ 
       const int vi = threadIdx.x + i * nt;
       if (vi < nvec) {
         float dyv[8], xv[8];
-        load8(dy + static_cast<size_t>(row) * D + vi * 8, dyv);
-        load8(x + static_cast<size_t>(row) * ldx + vi * 8, xv);
+        unpack8(dy_raw[i], dyv);
+        unpack8(x_raw[i], xv);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           xh[i][j] = (xv[j] - mean) * rstd;
@@ -162,6 +186,19 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(const bf16* __restrict__ 
           g[i][j] = dyv[j] * wv[i][j];
           sg += g[i][j];
           sgx += g[i][j] * xh[i][j];
+        }
+      }
+    }
+    const int next = row + gridDim.x;
+    uint4 res_raw[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int vi = threadIdx.x + i * nt;
+      if (vi < nvec) {
+        if (dres != nullptr) res_raw[i] = *reinterpret_cast<const uint4*>(dres + static_cast<size_t>(row) * D + vi * 8);
+        if (next < M) {
+          dy_raw[i] = *reinterpret_cast<const uint4*>(dy + static_cast<size_t>(next) * D + vi * 8);
+          x_raw[i] = *reinterpret_cast<const uint4*>(x + static_cast<size_t>(next) * ldx + vi * 8);
         }
       }
     }
@@ -177,7 +214,7 @@ __global__ void __launch_bounds__(512) norm_bwd_kernel(const bf16* __restrict__ 
         for (int j = 0; j < 8; ++j) o[j] = rstd * (g[i][j] - sg - xh[i][j] * sgx);
         if (dres != nullptr) {
           float rv[8];
-          load8(dres + static_cast<size_t>(row) * D + vi * 8, rv);
+          unpack8(res_raw[i], rv);
 #pragma unroll
           for (int j = 0; j < 8; ++j) o[j] += rv[j];
         }
@@ -226,7 +263,7 @@ __global__ void reduce_rows_f32_kernel(const float* __restrict__ part, int npart
 }  // namespace
 }  // namespace ob
 
-extern "C" int ob_norm_rows_per_launch(int M) { return M < 1184 ? M : 1184; }  // 148 SMs x 8 CTAs
+extern "C" int ob_norm_rows_per_launch(int M) { return M < 592 ? M : 592; }  // 148 SMs x 4 CTAs of the backward kernel
 
 extern "C" int ob_norm_fwd(const void* x, const void* res, const void* w, const void* b, void* out, float* rstd,
                            float* mean, int M, int D, int ldx, float eps, int is_rms, cudaStream_t stream) {
