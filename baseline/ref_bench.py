@@ -109,6 +109,7 @@ def _run(args, presets) -> dict:
 
     seed_all(cfg.seed)
     olmo_model = OLMo(cfg.model)
+    flops_per_token = olmo_model.num_fwd_flops + olmo_model.num_bck_flops  # read before sharding: FSDP leaves local shards only
     olmo_model.set_activation_checkpointing(cfg.activation_checkpointing)
     wrap_policy = olmo_model.get_fsdp_wrap_policy(cfg.fsdp.wrapping_strategy)
 
@@ -123,7 +124,6 @@ def _run(args, presets) -> dict:
     olmo_model.reset_parameters()
     optim = build_optimizer(cfg, dist_model)
     scheduler = build_scheduler(cfg)
-    flops_per_token = olmo_model.num_fwd_flops + olmo_model.num_bck_flops
 
     trainer = Trainer(
         cfg=cfg, epoch=cfg.epoch, model=olmo_model, dist_model=dist_model, optim=optim, scheduler=scheduler,
