@@ -78,41 +78,64 @@ __device__ __forceinline__ void comm_all_gather(const CommTask& t, int cta, int 
 // `elems` must be a multiple of 4 fp32 elements.  Each thread keeps 8 sixteen-byte loads in flight (U = 8 / W vectors
 // from each of the W ranks) because a communication CTA has few warps to hide NVLink latency with.
 template <int W, int U>
+struct RsTile {
+  uint4 v[W][U];
+  float4 d[U];
+};
+
+template <int W, int U>
+__device__ __forceinline__ void rs_load(const CommTask& t, RsTile<W, U>& r, long long base, long long vecs) {
+  const float4* dst = reinterpret_cast<const float4*>(t.dst);
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
+    if (i < vecs) {
+#pragma unroll
+      for (int p = 0; p < W; ++p) r.v[p][u] = ld_peer_16(reinterpret_cast<const uint4*>(t.src[p]) + i);
+      r.d[u] = dst[i];
+    }
+  }
+}
+
+template <int W, int U>
+__device__ __forceinline__ float rs_finish(const CommTask& t, RsTile<W, U>& r, long long base, long long vecs) {
+  float4* dst = reinterpret_cast<float4*>(t.dst);
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
+    if (i < vecs) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int p = 0; p < W; ++p) {
+        acc.x += __uint_as_float(r.v[p][u].x);
+        acc.y += __uint_as_float(r.v[p][u].y);
+        acc.z += __uint_as_float(r.v[p][u].z);
+        acc.w += __uint_as_float(r.v[p][u].w);
+      }
+      acc.x *= t.scale; acc.y *= t.scale; acc.z *= t.scale; acc.w *= t.scale;
+      float4 d = r.d[u];
+      d.x += acc.x; d.y += acc.y; d.z += acc.z; d.w += acc.w;
+      dst[i] = d;
+      ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+    }
+  }
+  return ss;
+}
+
+// One tile of U vectors from each of the W ranks is in flight per thread.  (Keeping a second tile in registers does not
+// help: a wait for the older tile's loads also waits for the younger one's, so each memory round trip still retires one
+// tile; what counts is the number of bytes requested before the first use.)
+template <int W, int U>
 __device__ __forceinline__ float comm_rs_loop(const CommTask& t, int cta, int nctas) {
   const long long vecs = t.elems >> 2;
-  float4* dst = reinterpret_cast<float4*>(t.dst);
   const long long tile = static_cast<long long>(blockDim.x) * U;
+  const long long stride = static_cast<long long>(nctas) * tile;
   float ss = 0.f;
-  for (long long base = static_cast<long long>(cta) * tile; base < vecs; base += static_cast<long long>(nctas) * tile) {
-    uint4 v[W][U];
-    float4 d[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
-      if (i < vecs) {
-#pragma unroll
-        for (int p = 0; p < W; ++p) v[p][u] = ld_peer_16(reinterpret_cast<const uint4*>(t.src[p]) + i);
-        d[u] = dst[i];
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long i = base + static_cast<long long>(u) * blockDim.x + threadIdx.x;
-      if (i < vecs) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-        for (int p = 0; p < W; ++p) {
-          acc.x += __uint_as_float(v[p][u].x);
-          acc.y += __uint_as_float(v[p][u].y);
-          acc.z += __uint_as_float(v[p][u].z);
-          acc.w += __uint_as_float(v[p][u].w);
-        }
-        acc.x *= t.scale; acc.y *= t.scale; acc.z *= t.scale; acc.w *= t.scale;
-        d[u].x += acc.x; d[u].y += acc.y; d[u].z += acc.z; d[u].w += acc.w;
-        dst[i] = d[u];
-        ss += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
-      }
-    }
+  for (long long base = static_cast<long long>(cta) * tile; base < vecs; base += stride) {
+    RsTile<W, U> r;
+    rs_load<W, U>(t, r, base, vecs);
+    ss += rs_finish<W, U>(t, r, base, vecs);
   }
   return ss;
 }
@@ -123,13 +146,13 @@ __device__ __forceinline__ void comm_reduce_scatter(const CommTask& t, int cta, 
   float ss;
   switch (t.world) {
     case 1: ss = comm_rs_loop<1, 8>(t, cta, nctas); break;
-    case 2: ss = comm_rs_loop<2, 4>(t, cta, nctas); break;
-    case 3: ss = comm_rs_loop<3, 2>(t, cta, nctas); break;
-    case 4: ss = comm_rs_loop<4, 2>(t, cta, nctas); break;
-    case 5: ss = comm_rs_loop<5, 1>(t, cta, nctas); break;
-    case 6: ss = comm_rs_loop<6, 1>(t, cta, nctas); break;
-    case 7: ss = comm_rs_loop<7, 1>(t, cta, nctas); break;
-    default: ss = comm_rs_loop<8, 1>(t, cta, nctas); break;
+    case 2: ss = comm_rs_loop<2, 6>(t, cta, nctas); break;
+    case 3: ss = comm_rs_loop<3, 4>(t, cta, nctas); break;
+    case 4: ss = comm_rs_loop<4, 4>(t, cta, nctas); break;
+    case 5: ss = comm_rs_loop<5, 3>(t, cta, nctas); break;
+    case 6: ss = comm_rs_loop<6, 2>(t, cta, nctas); break;
+    case 7: ss = comm_rs_loop<7, 2>(t, cta, nctas); break;
+    default: ss = comm_rs_loop<8, 2>(t, cta, nctas); break;
   }
   if (t.sumsq_partials != nullptr) {
     ss = block_sum(ss, red);

@@ -257,12 +257,12 @@ def block_backward(
     del d_act
     if spec.norm_after:
         sink.matrix("ff_proj", d_h, x1)
-        dx1 = k.gemm(d_h, w["ff_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1_res)
+        dx1 = k.gemm(d_h, w["ff_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1_res, **gk.get("ff_proj_dgrad", {}))
     else:
         h2, _, _ = k.norm_fwd(x1, _norm_w(w, "ff_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
         sink.matrix("ff_proj", d_h, h2)
         del h2
-        d_h2 = k.gemm(d_h, w["ff_proj"], b_trans=True)
+        d_h2 = k.gemm(d_h, w["ff_proj"], b_trans=True, **gk.get("ff_proj_dgrad", {}))
         dx1 = k.norm_bwd(d_h2, x1, _norm_w(w, "ff_norm"), saved["rstd2"], saved["mean2"], spec.rms, dres=dx1_res, dweight=vec("ff_norm"))
     del d_h
 
@@ -294,12 +294,13 @@ def block_backward(
     if spec.norm_after:
         sink.matrix("att_proj", dqkv, x)
         if not need_dx:
+            assert "att_proj_dgrad" not in gk, "a collective was attached to a GEMM that is skipped"
             return None
-        return k.gemm(dqkv, w["att_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1)
+        return k.gemm(dqkv, w["att_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1, **gk.get("att_proj_dgrad", {}))
     h1, _, _ = k.norm_fwd(x, _norm_w(w, "attn_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
     sink.matrix("att_proj", dqkv, h1)
     del h1
-    d_h1 = k.gemm(dqkv, w["att_proj"], b_trans=True)
+    d_h1 = k.gemm(dqkv, w["att_proj"], b_trans=True, **gk.get("att_proj_dgrad", {}))
     return k.norm_bwd(d_h1, x, _norm_w(w, "attn_norm"), saved["rstd1"], saved["mean1"], spec.rms, dres=dx1, dweight=vec("attn_norm"))
 
 

@@ -630,6 +630,9 @@ class FlatShardEngine:
         elif comm is None:
             self.gather_params()
 
+        if comm is not None:
+            from .peer import BWD_SPANS, FWD_SPANS
+
         def need(unit: Unit) -> None:
             if unit in gather_queue:  # not prefetched in time: pull it now, in stream order
                 gather_queue.remove(unit)
@@ -639,10 +642,7 @@ class FlatShardEngine:
             if not gather_queue:
                 return {}
             nxt = gather_queue.pop(0)
-            return {
-                "att_proj": {"comm": (comm.ag_task(nxt, 0, 2), comm.comm_ctas)},
-                "ff_proj": {"comm": (comm.ag_task(nxt, 1, 2), comm.comm_ctas)},
-            }
+            return {name: {"comm": (comm.ag_task(nxt, span=span), comm.comm_ctas)} for name, span in FWD_SPANS.items()}
 
         if gather_queue:
             need(self._unit_of_module_param(t.wte.weight))
@@ -700,10 +700,7 @@ class FlatShardEngine:
                 return None
             u = ready.pop(0)
             u.reduced = True  # type: ignore[attr-defined]
-            return {
-                "ff_out_dgrad": {"comm": (comm.rs_task(u, 0, 2), comm.comm_ctas)},
-                "attn_out_dgrad": {"comm": (comm.rs_task(u, 1, 2), comm.comm_ctas)},
-            }
+            return {name: {"comm": (comm.rs_task(u, span=span), comm.rs_ctas)} for name, span in BWD_SPANS.items()}
 
         for i in range(len(blocks) - 1, -1, -1):
             kind, payload = saved_list.pop()

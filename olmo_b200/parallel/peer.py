@@ -60,6 +60,12 @@ class CommTask(ctypes.Structure):
     ]
 
 
+#: how a unit's collective is divided over the four GEMMs of a block, in sixteenths, proportional to GEMM duration at
+#: the 7B shapes (att_proj 0.55 ms, attn_out 0.18 ms, ff_proj 1.04 ms, ff_out 0.62 ms; same for the input-gradient GEMMs)
+FWD_SPANS = {"att_proj": (0, 4, 16), "attn_out": (4, 5, 16), "ff_proj": (5, 12, 16), "ff_out": (12, 16, 16)}
+BWD_SPANS = {"ff_out_dgrad": (0, 4, 16), "ff_proj_dgrad": (4, 11, 16), "attn_out_dgrad": (11, 12, 16), "att_proj_dgrad": (12, 16, 16)}
+
+
 class PeerComm:
     def __init__(self, engine, group) -> None:
         import torch.distributed._symmetric_memory as symm_mem
@@ -94,7 +100,11 @@ class PeerComm:
         self.param_epoch = 0
         self.grad_epoch = 0
         self.scalar_epoch = 0
-        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "20"))
+        # Communication CTAs per fused launch.  A gather is a pure copy and needs few CTAs to keep pace with the GEMM it
+        # rides on; a reduce-scatter moves twice the bytes and does arithmetic, so it gets more.  Both are even numbers
+        # (the two-CTA GEMM schedules CTA pairs).
+        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "8"))
+        self.rs_ctas = int(os.environ.get("OLMO_B200_RS_CTAS", "16"))
         self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "64"))
         ms = float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000"))
         self.wait_cycles = int(ms * 1.9e6)
@@ -128,13 +138,23 @@ class PeerComm:
         t.sumsq_partials = None
         return t
 
-    def ag_task(self, unit, part: int = 0, parts: int = 1) -> CommTask:
-        """All-gather of slice ``part`` of ``parts`` of every foreign shard of ``unit`` into the local ``full`` buffer."""
+    @staticmethod
+    def _slice(S: int, part: int, parts: int, span, align: int):
+        """``[a, b)`` of a shard of ``S`` elements: either part ``part`` of ``parts`` or ``span = (lo, hi, denominator)``."""
+        if span is not None:
+            lo, hi, den = span
+            a = (S * lo // den) // align * align
+            b = S if hi == den else (S * hi // den) // align * align
+            return a, b
+        step = (S // parts) // align * align
+        a = part * step
+        return a, (S if part == parts - 1 else a + step)
+
+    def ag_task(self, unit, part: int = 0, parts: int = 1, span=None) -> CommTask:
+        """All-gather of one slice of every foreign shard of ``unit`` into the local ``full`` buffer."""
         S = unit.shard_size
         esz = self.full_all.element_size()
-        step = (S // parts) // 8 * 8
-        a = part * step
-        b = S if part == parts - 1 else a + step
+        a, b = self._slice(S, part, parts, span, 8)
         t = self._base_task(COMM_ALL_GATHER)
         t.elems, t.dst_peer_stride = b - a, S
         base = self.bases[unit.index]
@@ -145,12 +165,10 @@ class PeerComm:
         t.wait_value = self.param_epoch
         return t
 
-    def rs_task(self, unit, part: int = 0, parts: int = 1) -> CommTask:
-        """Reduce-scatter of slice ``part`` of this rank's gradient shard of ``unit`` (sum over ranks, scaled, added)."""
+    def rs_task(self, unit, part: int = 0, parts: int = 1, span=None) -> CommTask:
+        """Reduce-scatter of one slice of this rank's gradient shard of ``unit`` (sum over ranks, scaled, added)."""
         S = unit.shard_size
-        step = (S // parts) // 4 * 4
-        a = part * step
-        b = S if part == parts - 1 else a + step
+        a, b = self._slice(S, part, parts, span, 4)
         t = self._base_task(COMM_REDUCE_SCATTER)
         t.elems = b - a
         base = self.bases[unit.index]
