@@ -49,18 +49,18 @@ struct PartGeom {
   int width;  // Wq or Wk
 };
 
-// One part (q or k) of one row, forward.
-template <bool NORM, bool ROPE>
+// One part (q or k) of one row, forward.  NP = vector pairs per thread.
+template <bool NORM, bool ROPE, int NP>
 __device__ __forceinline__ void part_fwd(const bf16* __restrict__ in, bf16* __restrict__ out, const bf16* __restrict__ w,
                                          const float* __restrict__ cosr, const float* __restrict__ sinr, int width,
                                          int hd, float eps, float clip, float* rstd_out, float* red) {
   const int half = hd >> 1;
   const int ppv = half >> 3;  // vector pairs per head
   const int npairs = width >> 4;
-  float a[MAXP][8], b[MAXP][8];
+  float a[NP][8], b[NP][8];
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < MAXP; ++i) {
+  for (int i = 0; i < NP; ++i) {
     const int p = threadIdx.x + i * NT;
     if (p < npairs) {
       const int col = (p / ppv) * hd + (p % ppv) * 8;
@@ -84,7 +84,7 @@ __device__ __forceinline__ void part_fwd(const bf16* __restrict__ in, bf16* __re
     if (threadIdx.x == 0 && rstd_out != nullptr) *rstd_out = rstd;
   }
 #pragma unroll
-  for (int i = 0; i < MAXP; ++i) {
+  for (int i = 0; i < NP; ++i) {
     const int p = threadIdx.x + i * NT;
     if (p < npairs) {
       const int jj = (p % ppv) * 8;
@@ -128,7 +128,10 @@ __device__ __forceinline__ void part_fwd(const bf16* __restrict__ in, bf16* __re
   }
 }
 
-template <bool NORM, bool ROPE>
+// grid = (row walkers, 2): blockIdx.y == 0 handles the q part of a row, 1 the k part (and the clamped v copy).  The two
+// parts are independent (separate norms), so giving each its own CTA halves the per-thread state and doubles the number
+// of rows in flight.
+template <bool NORM, bool ROPE, int NP>
 __global__ void __launch_bounds__(NT)
 qk_fwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ qk_out, const bf16* __restrict__ wq, const bf16* __restrict__ wk,
               const float* __restrict__ cos_t, const float* __restrict__ sin_t, float* __restrict__ rstd_q,
@@ -136,15 +139,19 @@ qk_fwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ qk_out, const bf1
               float eps, float clip) {
   __shared__ float red[32];
   const int half = hd >> 1;
+  const bool is_k = blockIdx.y == 1;
+  const int col0 = is_k ? Wq : 0;
+  const int width = is_k ? Wk : Wq;
+  const bf16* w = is_k ? wk : wq;
+  float* rstd_out = is_k ? rstd_k : rstd_q;
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     const int t = row % T + pos_offset;
     const float* cr = cos_t + static_cast<size_t>(t) * half;
     const float* sr = sin_t + static_cast<size_t>(t) * half;
     const bf16* in = qkv + static_cast<size_t>(row) * ldq;
     bf16* out = qk_out + static_cast<size_t>(row) * ldo;
-    part_fwd<NORM, ROPE>(in, out, wq, cr, sr, Wq, hd, eps, clip, rstd_q ? rstd_q + row : nullptr, red);
-    part_fwd<NORM, ROPE>(in + Wq, out + Wq, wk, cr, sr, Wk, hd, eps, clip, rstd_k ? rstd_k + row : nullptr, red);
-    if (clip > 0.f) {  // clamped v becomes the third part of the output
+    part_fwd<NORM, ROPE, NP>(in + col0, out + col0, w, cr, sr, width, hd, eps, clip, rstd_out ? rstd_out + row : nullptr, red);
+    if (is_k && clip > 0.f) {  // clamped v becomes the third part of the output
       const bf16* v = in + Wq + Wk;
       bf16* vo = out + Wq + Wk;
       for (int i = threadIdx.x; i < (Wk >> 3); i += NT) {
@@ -159,18 +166,18 @@ qk_fwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ qk_out, const bf1
 }
 
 // One part of one row, backward, in place on the gradient buffer.
-template <bool NORM, bool ROPE>
+template <bool NORM, bool ROPE, int NP>
 __device__ __forceinline__ void part_bwd(const bf16* __restrict__ in, bf16* __restrict__ grad, const bf16* __restrict__ w,
                                          const float* __restrict__ cosr, const float* __restrict__ sinr, int width,
-                                         int hd, float clip, float rstd, float (&dw_a)[MAXP][8], float (&dw_b)[MAXP][8],
+                                         int hd, float clip, float rstd, float (&dw_a)[NP][8], float (&dw_b)[NP][8],
                                          float* red) {
   const int half = hd >> 1;
   const int ppv = half >> 3;
   const int npairs = width >> 4;
-  float ga[MAXP][8], gb[MAXP][8], xa[MAXP][8], xb[MAXP][8];
+  float ga[NP][8], gb[NP][8], xa[NP][8], xb[NP][8];
   float sgx = 0.f;
 #pragma unroll
-  for (int i = 0; i < MAXP; ++i) {
+  for (int i = 0; i < NP; ++i) {
     const int p = threadIdx.x + i * NT;
     if (p < npairs) {
       const int jj = (p % ppv) * 8;
@@ -220,7 +227,7 @@ __device__ __forceinline__ void part_bwd(const bf16* __restrict__ in, bf16* __re
   }
   if (NORM) sgx = block_sum(sgx, red) / width;
 #pragma unroll
-  for (int i = 0; i < MAXP; ++i) {
+  for (int i = 0; i < NP; ++i) {
     const int p = threadIdx.x + i * NT;
     if (p < npairs) {
       const int col = (p / ppv) * hd + (p % ppv) * 8;
@@ -247,8 +254,8 @@ __device__ __forceinline__ void part_bwd(const bf16* __restrict__ in, bf16* __re
   }
 }
 
-template <bool NORM, bool ROPE>
-__global__ void __launch_bounds__(NT)
+template <bool NORM, bool ROPE, int NP>
+__global__ void __launch_bounds__(NT, NP == 1 ? 3 : 1)
 qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16* __restrict__ wq,
               const bf16* __restrict__ wk, const float* __restrict__ cos_t, const float* __restrict__ sin_t,
               const float* __restrict__ rstd_q, const float* __restrict__ rstd_k, float* __restrict__ dwq_part,
@@ -256,11 +263,17 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
   __shared__ float red[32];
   const int half = hd >> 1;
   const int ppv = half >> 3;
-  float dqa[MAXP][8], dqb[MAXP][8], dka[MAXP][8], dkb[MAXP][8];
+  const bool is_k = blockIdx.y == 1;
+  const int col0 = is_k ? Wq : 0;
+  const int width = is_k ? Wk : Wq;
+  const bf16* w = is_k ? wk : wq;
+  const float* rstd_in = is_k ? rstd_k : rstd_q;
+  float* dw_part = is_k ? dwk_part : dwq_part;
+  float dwa[NP][8], dwb[NP][8];
 #pragma unroll
-  for (int i = 0; i < MAXP; ++i)
+  for (int i = 0; i < NP; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) dqa[i][j] = dqb[i][j] = dka[i][j] = dkb[i][j] = 0.f;
+    for (int j = 0; j < 8; ++j) dwa[i][j] = dwb[i][j] = 0.f;
 
   for (int row = blockIdx.x; row < M; row += gridDim.x) {
     const int t = row % T + pos_offset;
@@ -268,9 +281,8 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
     const float* sr = sin_t + static_cast<size_t>(t) * half;
     const bf16* in = qkv + static_cast<size_t>(row) * ldq;
     bf16* g = dqkv + static_cast<size_t>(row) * ldq;
-    part_bwd<NORM, ROPE>(in, g, wq, cr, sr, Wq, hd, clip, NORM ? rstd_q[row] : 1.f, dqa, dqb, red);
-    part_bwd<NORM, ROPE>(in + Wq, g + Wq, wk, cr, sr, Wk, hd, clip, NORM ? rstd_k[row] : 1.f, dka, dkb, red);
-    if (clip > 0.f) {  // clamp passes no gradient where the projection was outside [-clip, clip]
+    part_bwd<NORM, ROPE, NP>(in + col0, g + col0, w, cr, sr, width, hd, clip, NORM ? rstd_in[row] : 1.f, dwa, dwb, red);
+    if (is_k && clip > 0.f) {  // clamp passes no gradient where the projection was outside [-clip, clip]
       const bf16* v = in + Wq + Wk;
       bf16* dv = g + Wq + Wk;
       for (int i = threadIdx.x; i < (Wk >> 3); i += NT) {
@@ -284,26 +296,17 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
       }
     }
   }
-  if (NORM && dwq_part != nullptr) {
+  if (NORM && dw_part != nullptr) {
 #pragma unroll
-    for (int i = 0; i < MAXP; ++i) {
+    for (int i = 0; i < NP; ++i) {
       const int p = threadIdx.x + i * NT;
       const int col = (p / ppv) * hd + (p % ppv) * 8;
-      if (p < (Wq >> 4)) {
-        float* o = dwq_part + static_cast<size_t>(blockIdx.x) * Wq + col;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          o[j] = dqa[i][j];
-          o[j + half] = dqb[i][j];
-        }
-      }
-      if (p < (Wk >> 4)) {
-        float* o = dwk_part + static_cast<size_t>(blockIdx.x) * Wk + col;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          o[j] = dka[i][j];
-          o[j + half] = dkb[i][j];
-        }
+      if (p < (width >> 4)) {
+        float* o = dw_part + static_cast<size_t>(blockIdx.x) * width + col;
+        *reinterpret_cast<float4*>(o) = make_float4(dwa[i][0], dwa[i][1], dwa[i][2], dwa[i][3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(dwa[i][4], dwa[i][5], dwa[i][6], dwa[i][7]);
+        *reinterpret_cast<float4*>(o + half) = make_float4(dwb[i][0], dwb[i][1], dwb[i][2], dwb[i][3]);
+        *reinterpret_cast<float4*>(o + half + 4) = make_float4(dwb[i][4], dwb[i][5], dwb[i][6], dwb[i][7]);
       }
     }
   }
@@ -312,7 +315,7 @@ qk_bwd_kernel(const bf16* __restrict__ qkv, bf16* __restrict__ dqkv, const bf16*
 }  // namespace
 }  // namespace ob
 
-extern "C" int ob_qk_rows_per_launch(int M) { return M < 1184 ? M : 1184; }
+extern "C" int ob_qk_rows_per_launch(int M) { return M < 592 ? M : 592; }  // x 2 parts = 8 CTAs per SM
 
 static int qk_check(int Wq, int Wk, int hd, int ldq) {
   if (hd % 16 != 0 || Wq % hd != 0 || Wk % hd != 0 || ldq % 8 != 0) return -1;
@@ -328,10 +331,18 @@ extern "C" int ob_qk_norm_rope_fwd(const void* qkv, void* qk_out, const void* wq
   if (M <= 0) return 0;
   if (qk_check(Wq, Wk, hd, ldq) != 0 || ldo % 8 != 0) return -1;
   const int grid = ob_qk_rows_per_launch(M);
-#define OB_QK_FWD(N_, R_)                                                                                        \
-  qk_fwd_kernel<N_, R_><<<grid, NT, 0, stream>>>((const bf16*)qkv, (bf16*)qk_out, (const bf16*)wq, (const bf16*)wk, \
-                                                 cos_t, sin_t, rstd_q, rstd_k, M, T, pos_offset, Wq, Wk, hd, ldq,   \
-                                                 ldo, eps, clip)
+  const dim3 grid2(grid, 2);
+  const bool one = (Wq > Wk ? Wq : Wk) <= 16 * NT;  // one vector pair per thread suffices
+#define OB_QK_FWD(N_, R_)                                                                                              \
+  do {                                                                                                                 \
+    if (one)                                                                                                           \
+      qk_fwd_kernel<N_, R_, 1><<<grid2, NT, 0, stream>>>((const bf16*)qkv, (bf16*)qk_out, (const bf16*)wq, (const bf16*)wk, cos_t, \
+                                                         sin_t, rstd_q, rstd_k, M, T, pos_offset, Wq, Wk, hd, ldq, ldo, eps, clip); \
+    else                                                                                                               \
+      qk_fwd_kernel<N_, R_, MAXP><<<grid2, NT, 0, stream>>>((const bf16*)qkv, (bf16*)qk_out, (const bf16*)wq, (const bf16*)wk,     \
+                                                            cos_t, sin_t, rstd_q, rstd_k, M, T, pos_offset, Wq, Wk, hd, ldq, ldo,  \
+                                                            eps, clip);                                                \
+  } while (0)
   if (do_norm && do_rope) OB_QK_FWD(true, true);
   else if (do_norm) OB_QK_FWD(true, false);
   else if (do_rope) OB_QK_FWD(false, true);
@@ -351,10 +362,19 @@ extern "C" int ob_qk_norm_rope_bwd(const void* qkv, void* dqkv, const void* wq, 
   if (M <= 0) return 0;
   if (qk_check(Wq, Wk, hd, ldq) != 0) return -1;
   const int grid = ob_qk_rows_per_launch(M);
-#define OB_QK_BWD(N_, R_)                                                                                           \
-  qk_bwd_kernel<N_, R_><<<grid, NT, 0, stream>>>((const bf16*)qkv, (bf16*)dqkv, (const bf16*)wq, (const bf16*)wk,   \
-                                                 cos_t, sin_t, rstd_q, rstd_k, dwq_part, dwk_part, M, T, pos_offset, \
-                                                 Wq, Wk, hd, ldq, clip)
+  const dim3 grid2(grid, 2);
+  const bool one = (Wq > Wk ? Wq : Wk) <= 16 * NT;
+#define OB_QK_BWD(N_, R_)                                                                                              \
+  do {                                                                                                                 \
+    if (one)                                                                                                           \
+      qk_bwd_kernel<N_, R_, 1><<<grid2, NT, 0, stream>>>((const bf16*)qkv, (bf16*)dqkv, (const bf16*)wq, (const bf16*)wk, cos_t,   \
+                                                         sin_t, rstd_q, rstd_k, dwq_part, dwk_part, M, T, pos_offset, Wq, Wk, hd, \
+                                                         ldq, clip);                                                   \
+    else                                                                                                               \
+      qk_bwd_kernel<N_, R_, MAXP><<<grid2, NT, 0, stream>>>((const bf16*)qkv, (bf16*)dqkv, (const bf16*)wq, (const bf16*)wk,       \
+                                                            cos_t, sin_t, rstd_q, rstd_k, dwq_part, dwk_part, M, T, pos_offset,    \
+                                                            Wq, Wk, hd, ldq, clip);                                    \
+  } while (0)
   if (do_norm && do_rope) OB_QK_BWD(true, true);
   else if (do_norm) OB_QK_BWD(true, false);
   else if (do_rope) OB_QK_BWD(false, true);

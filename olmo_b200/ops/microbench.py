@@ -123,6 +123,21 @@ def bench_norm(args) -> None:
     }
     h = torch.randn(M, 22016, device="cuda", dtype=torch.bfloat16)
     cases["swiglu fwd"] = (lambda: k.swiglu_fwd(h), M * 11008 * 3 * 2)
+    dact = torch.randn(M, 11008, device="cuda", dtype=torch.bfloat16)
+    cases["swiglu bwd"] = (lambda: k.swiglu_bwd(dact, h), M * 11008 * 5 * 2)
+    # QK-norm + RoPE over the fused projection of the 7B shape (q | k | v, 3 x 4096 columns)
+    from .fused_block import rope_tables
+
+    T, hd = 4096, 128
+    qkv = torch.randn(M, 3 * D, device="cuda", dtype=torch.bfloat16)
+    dqkv = torch.randn_like(qkv)
+    cos, sin = rope_tables(T, hd, 500000.0, torch.device("cuda"))
+    _, rq, rk = k.qk_norm_rope_fwd(qkv, w, w, cos, sin, T, D, D, hd, 1e-6, 0.0, True, True)
+    dwq, dwk = torch.zeros(D, device="cuda"), torch.zeros(D, device="cuda")
+    cases["qk-norm+rope fwd"] = (lambda: k.qk_norm_rope_fwd(qkv, w, w, cos, sin, T, D, D, hd, 1e-6, 0.0, True, True), 4 * M * D * 2)
+    cases["qk-norm+rope bwd"] = (
+        lambda: k.qk_norm_rope_bwd(qkv, dqkv, w, w, cos, sin, rq, rk, T, D, D, hd, 0.0, True, True, dwq=dwq, dwk=dwk), 6 * M * D * 2,
+    )
     for name, (fn, nbytes) in cases.items():
         if args.once:
             fn()
