@@ -21,12 +21,15 @@ namespace ob {
 
 int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
                             uint32_t box_inner, uint32_t box_outer);
+int make_tensor_map_f32_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                           uint32_t box_inner, uint32_t box_outer);
 
 namespace {
 
 constexpr int AT_THREADS = 320;
 constexpr int AT_TILE_BYTES = 128 * 128 * 2;  // 32 KiB: one 128 x 128 bf16 tile = two 64-column halves
 constexpr int AT_HALF_BYTES = 128 * 64 * 2;   // 16 KiB
+constexpr int AT_SMEM_BWD = 1024 + 6 * AT_TILE_BYTES + 512;  // alignment slack + tiles + barriers
 constexpr int AT_SMEM = 1024 + 6 * AT_TILE_BYTES + 4096;  // alignment slack + tiles + barriers and row-statistic exchange (3.3 KiB)
 
 struct AttnParams {
@@ -385,7 +388,7 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
 __global__ void __launch_bounds__(AT_THREADS, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                const AttnBwdParams p) {
+                const __grid_constant__ CUtensorMap tm_dq, const AttnBwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -402,7 +405,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint64_t* pds_full = bars + 4;  // P and dS written (256 arrivals)
   uint64_t* dq_full = bars + 5;   // dQ complete (and dV, dK updated)
   uint64_t* s_free = bars + 6;    // dQ read out of TMEM (256 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  // The dQ tile leaves through the P / dS buffers, which are idle between the last MMA of an iteration and the softmax
+  // of the next one: column half h stages its columns [0,32) in its 16 KiB half of sP and [32,64) in its half of sdS,
+  // i.e. exactly the bytes that the same 128 threads overwrite with P and dS later, so only they need to synchronise.
+  uint64_t* stage_full = bars + 7;  // [2] a half's 128 threads have staged their dQ rows
+  uint64_t* stage_free = bars + 9;  // [2] the reduce-add stores have finished reading that half's staging bytes
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -425,6 +433,10 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     mbar_init(pds_full, 256);
     mbar_init(dq_full, 1);
     mbar_init(s_free, 256);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&stage_full[i], 128);
+      mbar_init(&stage_free[i], 1);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -443,6 +455,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       prefetch_tensormap(&tm_k);
       prefetch_tensormap(&tm_v);
       prefetch_tensormap(&tm_do);
+      prefetch_tensormap(&tm_dq);
       mbar_expect_tx(kv_full, 2 * AT_TILE_BYTES);
       tma_load_2d(sK, &tm_k, kv_full, hk * 128, kv_row);
       tma_load_2d(sK + AT_HALF_BYTES, &tm_k, kv_full, hk * 128 + 64, kv_row);
@@ -563,6 +576,14 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           dsk[cc * 16 + c] = pack_bf16x2(dv[0], dv[1]);
         }
       }
+      // the reduce-add stores of the previous iteration must have read their staging bytes before P / dS overwrite them
+      if (it > 0) {
+        if (quarter == 0 && lane == 0) {
+          bulk_wait_group_read0();
+          mbar_arrive(&stage_free[half]);
+        }
+        if (!mbar_wait(&stage_free[half], static_cast<uint32_t>((it - 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+      }
       // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle
       uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
       uint8_t* srow = sdS + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
@@ -575,24 +596,35 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       tc_fence_before();
       fence_proxy_async();
       mbar_arrive(pds_full);
-      // dQ tile: add this key tile's contribution to the fp32 accumulator
+      // dQ tile: add this key tile's contribution to the fp32 accumulator.  The tile leaves through shared memory and
+      // a TMA reduce-add store (two rounds of 32 columns per half), which keeps the additions off the load/store units.
       if (!mbar_wait(dq_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
       __syncwarp();
-      float* dq_row = p.dq_acc + ((static_cast<long long>(b) * p.T + t_idx) * p.H + h) * 128 + col0;
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 32), r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int v = 0; v < 8; ++v)
-          red_add_v4(dq_row + cc * 32 + v * 4, __uint_as_float(r[v * 4 + 0]), __uint_as_float(r[v * 4 + 1]),
-                     __uint_as_float(r[v * 4 + 2]), __uint_as_float(r[v * 4 + 3]));
-      }
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0), r0);
+      tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + 32), r1);
+      tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(s_free);
+      mbar_arrive(s_free);  // the accumulator columns may be overwritten by the next S
+      uint8_t* stage0 = sP + half * AT_HALF_BYTES;   // fp32 [128 rows][32 columns], 128-byte swizzle: columns col0 .. col0+31
+      uint8_t* stage1 = sdS + half * AT_HALF_BYTES;  // columns col0+32 .. col0+63
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const int o = row * 128 + ((ch ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(stage0 + o) = make_uint4(r0[ch * 4 + 0], r0[ch * 4 + 1], r0[ch * 4 + 2], r0[ch * 4 + 3]);
+        *reinterpret_cast<uint4*>(stage1 + o) = make_uint4(r1[ch * 4 + 0], r1[ch * 4 + 1], r1[ch * 4 + 2], r1[ch * 4 + 3]);
+      }
+      fence_proxy_async();
+      mbar_arrive(&stage_full[half]);
+      if (quarter == 0 && lane == 0) {
+        if (!mbar_wait(&stage_full[half], ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
+        tma_reduce_add_2d(&tm_dq, stage0, h * 128 + col0, b * p.T + qi * 128);
+        tma_reduce_add_2d(&tm_dq, stage1, h * 128 + col0 + 32, b * p.T + qi * 128);
+        bulk_commit_group();
+      }
     }
+    if (quarter == 0 && lane == 0) bulk_wait_group0();  // every reduce-add of this thread has been performed
     if (ok && n_it > 0) {
       // dV and dK are complete once the last dq_full has fired (same commit covers all earlier MMAs)
       const long long t_idx = static_cast<long long>(jt) * 128 + row;
@@ -693,10 +725,12 @@ extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, 
   if (rc == 0) rc = make_tensor_map_bf16_2d(&tk, k, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)k_st, 64, 128);
   if (rc == 0) rc = make_tensor_map_bf16_2d(&tv, v, (uint64_t)Hkv * 128, (uint64_t)B * T, (uint64_t)v_st, 64, 128);
   if (rc == 0) rc = make_tensor_map_bf16_2d(&tdo, dout, (uint64_t)H * 128, (uint64_t)B * T, (uint64_t)do_st, 64, 128);
+  CUtensorMap tdq;
+  if (rc == 0) rc = make_tensor_map_f32_2d(&tdq, dq_acc, (uint64_t)H * 128, (uint64_t)B * T, (uint64_t)H * 128, 32, 128);
   if (rc != 0) return rc;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM) != cudaSuccess) return -10;
+    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, AT_SMEM_BWD) != cudaSuccess) return -10;
     configured = true;
   }
   const long long rows = static_cast<long long>(B) * T * H;
@@ -710,7 +744,7 @@ extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, 
   p.B = B; p.T = T; p.H = H; p.Hkv = Hkv;
   p.scale = scale; p.scale_log2 = scale * 1.4426950408889634f;
   p.causal = causal; p.status = status;
-  attn_bwd_kernel<<<B * Hkv * (T / 128), AT_THREADS, AT_SMEM, stream>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<<<B * Hkv * (T / 128), AT_THREADS, AT_SMEM_BWD, stream>>>(tq, tk, tv, tdo, tdq, p);
   attn_bwd_dq_convert_kernel<<<static_cast<unsigned>((rows * 16 + 255) / 256), 256, 0, stream>>>(dq_acc, (bf16*)dq, B, T, H, dq_sb,
                                                                                                dq_st, dq_sh, scale);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;

@@ -315,6 +315,19 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Block-wide sum for blocks of up to 1024 threads; `scratch` holds 32 floats. Result valid in all threads.
+// TMA reduce-add store of a shared-memory tile into a 2-D tensor (element type and box come from the tensor map).
+// x is the innermost coordinate; x * element size must be a multiple of 16 bytes and no coordinate may be negative.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, const void* smem_src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"(map), "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Returns once the bulk operations committed by this thread have finished READING shared memory.
+__device__ __forceinline__ void bulk_wait_group_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Returns once they have completed altogether.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ float block_sum(float v, float* scratch) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = (blockDim.x + 31) >> 5;
   v = warp_sum(v);

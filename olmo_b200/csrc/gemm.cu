@@ -335,6 +335,22 @@ int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, 
   return r == CUDA_SUCCESS ? 0 : -3;
 }
 
+// 2-D fp32 tensor map with 128-byte swizzle (used for reduce-add stores of fp32 tiles; box_inner * 4 must be 128).
+int make_tensor_map_f32_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                           uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return -1;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (ld * 4) % 16 != 0 || box_inner * 4 != 128) return -2;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
 template <int A_MN, int B_MN, int EPI>
 static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const void* R, int M, int N, int K,
                        int ldc, int vec_ok, const int* b_ready, int rows_per_flag, int ready_value, int* status,
