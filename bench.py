@@ -52,6 +52,11 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--device-batch", type=int, default=None, help="sequences per GPU per optimizer step (default: official global batch / 8)")
     p.add_argument("--activation-checkpointing", default=None)
     p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--sharding", default="FULL_SHARD", choices=["FULL_SHARD", "SHARD_GRAD_OP", "HYBRID_SHARD", "NO_SHARD"],
+                   help="sharding strategy of the flat-shard engine (HYBRID_SHARD: --replicas groups)")
+    p.add_argument("--replicas", type=int, default=None, help="model replicas for HYBRID_SHARD (default: 2)")
+    p.add_argument("--checkpoint-timing", action="store_true",
+                   help="after the timed steps also time a sharded checkpoint save, its restore and the offline unshard")
     p.add_argument("--n-layers", type=int, default=None, help="profiling aid: fewer blocks than the preset (the result is then marked reduced)")
     return p.parse_args()
 
@@ -85,8 +90,9 @@ def make_train_config(args, world: int):
                                   alpha_f=0.1, warmup_min_lr=0.0),
         global_train_batch_size=device_batch * world, device_train_microbatch_size=ps["microbatch"], precision="amp_bf16",
         distributed_strategy=DistributedStrategy.fsdp,
-        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy.FULL_SHARD, wrapping_strategy=FSDPWrapStrategy.by_block_and_size,
-                        precision=FSDPPrecision.mixed),
+        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy[args.sharding], wrapping_strategy=FSDPWrapStrategy.by_block_and_size,
+                        precision=FSDPPrecision.mixed,
+                        hybrid_sharding_num_model_replicas=(args.replicas or 2) if args.sharding == "HYBRID_SHARD" else None),
         max_grad_norm=1.0, softmax_auxiliary_loss=True, auxiliary_loss_multiplier=1e-5, fused_loss=True,
         save_folder=tempfile.mkdtemp(prefix="olmo_b200_bench_"), save_overwrite=True, save_data_indices=False,
         max_duration=10**9, console_log_interval=10**9, speed_monitor=SpeedMonitorConfig(window_size=1),
@@ -229,6 +235,10 @@ def run_ours(args) -> dict:
             "ms_per_step": wall.item() * 1e3 / args.steps,
         }
 
+    checkpoint = None
+    if args.checkpoint_timing:
+        checkpoint = time_checkpoint_cycle(trainer, cfg, rank, world, barrier)
+
     tokens_per_step = device_batch * world * args.seq_len
     value = tokens_per_step / (ms_per_step / 1e3)
     peaks = {}
@@ -238,7 +248,7 @@ def run_ours(args) -> dict:
         pass
     per_gpu = value / world
     result = {
-        "metric": "tokens_per_second (OLMo-2 training, whole job; FSDP FULL_SHARD, device-timed, max over ranks)",
+        "metric": f"tokens_per_second ({'OLMo-2' if ps['flavour'] == 'olmo2' else 'OLMo-1'} training, whole job; FSDP {args.sharding}, device-timed, max over ranks)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic seeded uniform tokens with EOS boundaries; random-init weights",
@@ -251,17 +261,48 @@ def run_ours(args) -> dict:
             "model": args.model if not args.n_layers else f"{args.model} REDUCED to {args.n_layers} layers (profiling only)",
             "global_batch": device_batch * world, "seq_len": args.seq_len,
             "micro_batch": ps["microbatch"], "grad_accum": cfg.device_train_grad_accum,
-            "parallelism": f"fsdp{world}" if world > 1 else "single-gpu flat-shard engine",
+            "parallelism": (f"fsdp{world}" if args.sharding == "FULL_SHARD" else f"{args.sharding.lower()}{world}") if world > 1 else "single-gpu flat-shard engine",
             "activation_checkpointing": args.activation_checkpointing or "none",
             "optimizer": "adamw fp32 master, clip 1.0, z-loss on", "fused_path": bool(engine.fused),
             "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
         },
-        "clocks": clocks, "e2e": e2e, "gpu_launches": launches,
+        "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "checkpoint": checkpoint,
         "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
     }
     if world > 1:
         dist.destroy_process_group()
     return result if rank == 0 else {}
+
+
+def time_checkpoint_cycle(trainer, cfg, rank: int, world: int, barrier) -> dict:
+    """Wall-clock seconds (max over ranks) of a sharded save, a restore of it, and the offline unshard on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from olmo_b200.checkpoint import build_sharded_checkpointer
+
+    def timed(fn) -> float:
+        barrier()
+        t0 = time.perf_counter()
+        out = fn()
+        barrier()
+        t = torch.tensor([time.perf_counter() - t0], device=trainer.device, dtype=torch.float64)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        timed.last = out
+        return t.item()
+
+    save_s = timed(trainer.save_checkpoint)
+    path = timed.last[0]
+    restore_s = timed(lambda: trainer.restore_checkpoint(path))
+    unshard_s = None
+    if rank == 0:
+        t0 = time.perf_counter()
+        build_sharded_checkpointer(cfg).unshard_checkpoint(path, load_optimizer_state=True, load_trainer_state=True)
+        unshard_s = time.perf_counter() - t0
+    barrier()
+    size = sum(f.stat().st_size for f in Path(path).rglob("*") if f.is_file()) if rank == 0 else 0
+    return {"sharded_save_s": save_s, "restore_s": restore_s, "unshard_s": unshard_s, "bytes_on_disk": size, "path": str(path)}
 
 
 def _dummy_loader():
