@@ -168,6 +168,11 @@ def run_ours(args) -> dict:
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
 
     cfg, device_batch = make_train_config(args, world)
+    if world > 1:  # one save folder for the whole job (every rank made its own temporary directory)
+        shared = [cfg.save_folder]
+        dist.broadcast_object_list(shared, src=0)
+        cfg.save_folder = shared[0]
+        os.environ.setdefault("OLMO_SHARED_FS", "1")
     derive_batch_sizes(cfg, world)
     ps = PRESETS[args.model]
     trainer = build_trainer(cfg, device=device, train_loader=_dummy_loader(), with_evaluators=False)
