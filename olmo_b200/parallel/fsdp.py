@@ -378,8 +378,13 @@ class FlatShardEngine:
         from ..ops import kernels as k
 
         self.finish_grad_sync()
-        for i, unit in enumerate(self.units):
-            k.sumsq(unit.grad, self._sumsq, accumulate=i > 0)
+        comm = self.comm
+        if comm is not None and comm.fuse_sumsq and not self.reshard:
+            # every shard was written exactly once this step, by reduce-scatter kernels that also summed its squares
+            torch.sum(comm.rs_partials, dim=0, keepdim=True, out=self._sumsq)
+        else:
+            for i, unit in enumerate(self.units):
+                k.sumsq(unit.grad, self._sumsq, accumulate=i > 0)
         if self.is_sharded:
             if self.comm is not None:
                 self.comm.all_reduce_scalar_(self._sumsq)
@@ -433,6 +438,8 @@ class FlatShardEngine:
             if unit.gfull is not None and unit.gfull.data_ptr() != unit.grad.data_ptr():
                 unit.gfull.zero_()
             unit.reduced = False  # type: ignore[attr-defined]
+        if self.comm is not None:
+            self.comm.rs_partials.zero_()
         self._microbatches_since_reduce = 0
         self._grads_pending = False
 

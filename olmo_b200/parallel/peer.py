@@ -109,6 +109,10 @@ class PeerComm:
         ms = float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000"))
         self.wait_cycles = int(ms * 1.9e6)
         self._scalar_out = torch.zeros(1, dtype=torch.float32, device=dev)
+        # Σg² of what the reduce-scatter kernels add to the local shards, one slot per communication CTA: the gradient
+        # norm then needs no separate pass over the shards (OLMO_B200_RS_SUMSQ=0 restores the separate pass)
+        self.fuse_sumsq = os.environ.get("OLMO_B200_RS_SUMSQ", "1").strip().lower() not in ("0", "false", "no", "off")
+        self.rs_partials = torch.zeros(256, dtype=torch.float32, device=dev)
         torch.cuda.synchronize()
         dist.barrier(group=group)
         self.group = group
@@ -176,13 +180,17 @@ class PeerComm:
             t.src[p] = self.gfull_ptrs[p] + (base + self.rank * S + a) * 4
             t.wait_flags[p] = self.ctrl_ptrs[p] + 4 * (1 + unit.index)
         t.dst = unit.grad.data_ptr() + a * 4
+        if self.fuse_sumsq:
+            t.sumsq_partials = self.rs_partials.data_ptr()
         t.scale = 1.0 / self.engine.world
         t.wait_value = self.grad_epoch
         return t
 
     # ------------------------------------------------------------------------------ launches
     def launch(self, task: CommTask, ctas: Optional[int] = None) -> None:
-        check(lib().ob_comm_launch(ctypes.byref(task), ctypes.c_int(ctas or self.standalone_ctas), stream_ptr()), "ob_comm_launch")
+        n = ctas or self.standalone_ctas
+        assert n <= self.rs_partials.numel()
+        check(lib().ob_comm_launch(ctypes.byref(task), ctypes.c_int(n), stream_ptr()), "ob_comm_launch")
 
     def signal(self, word: int, value: int) -> None:
         check(lib().ob_signal(ctypes.c_void_p(self.ctrl_ptrs[self.rank] + 4 * word), ctypes.c_int(value), stream_ptr()), "ob_signal")
