@@ -221,3 +221,27 @@ def test_wandb_helpers_parse_and_diff():
     assert mod.parse_run_path("ai2/olmo/abc123") == "ai2/olmo/abc123"
     rows = list(mod.diff({"a": 1, "m": {"x": [1, 2]}, "save_folder": "p"}, {"a": 2, "m": {"x": [1, 3]}, "save_folder": "q"}))
     assert rows == [("a", 1, 2), ("m.x.1", 2, 3)]
+
+
+def test_anneal_config_maker_and_olmo_alias(tmp_path):
+    mod = load_script("anneal_config_maker")
+    out = tmp_path / "anneal.yaml"
+    mod.main(["--base", "OLMo2-7B-stage1", "--load-path", "/ckpt/step928646", "--start-lr", "6.1499e-05", "--tokens", "50e9", "--name", "anneal",
+              "--seed", "42", "--data-glob", str(tmp_path / "*.npy"), "-o", str(out)])
+    from olmo_b200.config import SchedulerType, TrainConfig
+
+    cfg = TrainConfig.load(out, validate_paths=False)
+    assert cfg.stop_at == 11931 and cfg.max_duration == "50000000000T" and cfg.seed == 42
+    assert cfg.scheduler.name == SchedulerType.linear_with_warmup and cfg.scheduler.alpha_f == 0.0 and cfg.scheduler.t_warmup == 0
+    assert cfg.optimizer.learning_rate == pytest.approx(6.1499e-05) and cfg.load_path == "/ckpt/step928646"
+    assert cfg.restore_dataloader is False and cfg.no_pre_train_checkpoint is True and cfg.model.d_model == 4096
+
+    # code written against the reference's package name resolves to this framework
+    import olmo.optim
+    from olmo.config import TrainConfig as AliasedConfig
+    from olmo.model import OLMo as AliasedOLMo
+
+    import olmo_b200.models.olmo
+    import olmo_b200.optim
+
+    assert AliasedConfig is TrainConfig and AliasedOLMo is olmo_b200.models.olmo.OLMo and olmo.optim is olmo_b200.optim
