@@ -68,6 +68,10 @@ BWD_SPANS = {"ff_out_dgrad": (0, 4, 16), "ff_proj_dgrad": (4, 11, 16), "attn_out
 
 class PeerComm:
     def __init__(self, engine, group) -> None:
+        # These kernels only use plain peer loads and stores.  Asking torch not to bind the buffers to an NVLink multicast
+        # object (best effort: the variable is ignored by releases that do not know it) keeps a rank that dies from
+        # disturbing its peers through such a binding.
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
 
         self.engine = engine
