@@ -29,12 +29,14 @@ int ob_gemm_bf16_comm(const void* A, const void* B, void* C, const void* R, int 
 // ---- attention.cu
 int ob_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int T, int H, int Hkv, int q_sb,
                      int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh, int o_sb, int o_st,
-                     int o_sh, float scale, int causal, int* status, cudaStream_t stream);
+                     int o_sh, float scale, int causal, int* status, const int* doc_start, cudaStream_t stream);
 int ob_attention_bwd(const void* dout, const void* q, const void* k, const void* v, const void* o, const float* lse, void* dq,
                      void* dk, void* dv, float* delta, float* dq_acc, int B, int T, int H, int Hkv, int do_sb, int do_st,
                      int do_sh, int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh,
                      int o_sb, int o_st, int o_sh, int dq_sb, int dq_st, int dq_sh, int dk_sb, int dk_st, int dk_sh,
-                     int dv_sb, int dv_st, int dv_sh, float scale, int causal, int* status, cudaStream_t stream);
+                     int dv_sb, int dv_st, int dv_sh, float scale, int causal, int* status, const int* doc_start,
+                     cudaStream_t stream);
+// doc_start (optional, causal only): int32 [B, T], position of the first token of the document each token belongs to.
 void ob_set_gemm_pair_mode(int on);  // 1: two-CTA (cta_group::2) GEMM kernel where applicable
 int ob_get_gemm_pair_mode(void);
 

@@ -40,6 +40,9 @@ struct AttnParams {
   float scale_log2;  // softmax scale * log2(e)
   int causal;
   int* status;
+  // Optional intra-document masking (implies causal): doc_start[b * T + t] is the position, inside its sequence, of the
+  // first token of the document that token t belongs to; query t then attends to keys doc_start .. t only.
+  const int* doc_start;
 };
 
 __global__ void __launch_bounds__(AT_THREADS, 1)
@@ -75,8 +78,11 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   const int bh = static_cast<int>(blockIdx.x) % (p.B * p.H);
   const int b = bh / p.H, h = bh % p.H;
   const int hk = h / (p.H / p.Hkv);
-  const int n_kv = p.causal ? qt + 1 : n_qt;
   const int row0 = b * p.T + qt * 128;  // first query row in the flattened (B*T) index space
+  // key tiles j_lo .. j_lo + n_kv - 1 are visited; with document masking tiles that end before the document of the
+  // tile's first query row starts hold nothing this tile may attend to (doc_start is non-decreasing along a sequence)
+  const int j_lo = p.doc_start != nullptr ? p.doc_start[row0] >> 7 : 0;
+  const int n_kv = (p.causal ? qt + 1 : n_qt) - j_lo;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -115,7 +121,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
-        const int kv_row = b * p.T + j * 128;
+        const int kv_row = b * p.T + (j_lo + j) * 128;
         if (!mbar_wait(&k_empty[s], ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
         mbar_expect_tx(&k_full[s], AT_TILE_BYTES);
         tma_load_2d(sK + s * AT_TILE_BYTES, &tm_k, &k_full[s], hk * 128, kv_row);
@@ -188,9 +194,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int col0 = half * 64;
     const uint32_t o_addr = tmem_base + lane_addr + 256u + static_cast<uint32_t>(col0);
-    float m_ref = -INFINITY;  // reference maximum of the raw (unscaled) scores used in the exponent
+    // reference maximum of the raw (unscaled) scores used in the exponent; a large finite start (not -inf) keeps rows
+    // whose first visited tile is entirely masked free of inf - inf
+    float m_ref = -1.0e30f;
     float l_run = 0.f;
     bool ok = true;
+    const int my_doc_start = p.doc_start != nullptr ? p.doc_start[row0 + row] : 0;
 
     for (int j = 0; j < n_kv; ++j) {
       const int s = j & 1;
@@ -212,10 +221,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      if (p.causal && j == qt) {
+      if (p.causal && j_lo + j == qt) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)
           if (col0 + c > row) sc[c] = -INFINITY;
+      }
+      if ((j_lo + j) * 128 < my_doc_start) {  // this tile reaches back before the row's document
+        const int first = my_doc_start - (j_lo + j) * 128 - col0;  // columns below `first` belong to earlier documents
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          if (c < first) sc[c] = -INFINITY;
       }
       float pm0 = fmaxf(sc[0], sc[1]), pm1 = fmaxf(sc[2], sc[3]);
 #pragma unroll
@@ -321,10 +336,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 // flattened B*T index space) and head stride must be 128.
 extern "C" int ob_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int T, int H, int Hkv,
                                 int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh,
-                                int o_sb, int o_st, int o_sh, float scale, int causal, int* status, cudaStream_t stream) {
+                                int o_sb, int o_st, int o_sh, float scale, int causal, int* status, const int* doc_start,
+                                cudaStream_t stream) {
   using namespace ob;
   if (B <= 0 || T <= 0) return 0;
   if (T % 128 != 0 || H % Hkv != 0) return -1;
+  if (doc_start != nullptr && !causal) return -5;  // document masking is defined for causal attention only
   if (q_sh != 128 || k_sh != 128 || v_sh != 128) return -2;
   if (q_sb != T * q_st || k_sb != T * k_st || v_sb != T * v_st) return -3;
   if ((o_st % 8) != 0 || (o_sh % 8) != 0 || (reinterpret_cast<uintptr_t>(o) & 15) != 0) return -4;
@@ -341,6 +358,7 @@ extern "C" int ob_attention_fwd(const void* q, const void* k, const void* v, voi
     configured = true;
   }
   AttnParams p;
+  p.doc_start = doc_start;
   p.o = reinterpret_cast<bf16*>(o);
   p.lse = lse;
   p.B = B; p.T = T; p.H = H; p.Hkv = Hkv;
@@ -369,6 +387,7 @@ namespace ob {
 namespace {
 
 struct AttnBwdParams {
+  const int* doc_start;  // optional intra-document masking, as in the forward kernel
   const float* lse;    // (B, H, T) natural log
   const float* delta;  // (B, H, T)
   float* dq_acc;       // (B, T, H, 128) fp32, zeroed
@@ -421,7 +440,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   const int b = bh / p.Hkv, hk = bh % p.Hkv;
   const int group = p.H / p.Hkv;
   const int i0 = p.causal ? jt : 0;
-  const int per_head = n_t - i0;
+  int per_head = n_t - i0;
+  if (p.doc_start != nullptr) {
+    // query tiles whose first row's document starts after this key tile ends cannot attend to it, nor can later ones
+    per_head = 0;
+    while (i0 + per_head < n_t && p.doc_start[b * p.T + (i0 + per_head) * 128] <= jt * 128 + 127) ++per_head;
+  }
   const int n_it = per_head * group;
   const int kv_row = b * p.T + jt * 128;
 
@@ -536,9 +560,12 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       return (static_cast<long long>(b) * p.H + h_) * p.T + t_;
     };
     float lse_next = 0.f, dl_next = 0.f;
+    int ds_next = 0;
+    auto doc_index = [&](int it_) -> long long { return static_cast<long long>(b) * p.T + (i0 + it_ % per_head) * 128 + row; };
     if (n_it > 0) {
       lse_next = p.lse[stat_index(0)];
       dl_next = p.delta[stat_index(0)];
+      if (p.doc_start != nullptr) ds_next = p.doc_start[doc_index(0)];
     }
     for (int it = 0; it < n_it; ++it) {
       const uint32_t ph = static_cast<uint32_t>(it & 1);
@@ -547,9 +574,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const long long t_idx = static_cast<long long>(qi) * 128 + row;
       const float lse2 = lse_next * 1.4426950408889634f;
       const float dl = dl_next;
+      const int first_col = ds_next - jt * 128;  // key columns below this index lie before the row's document
       if (it + 1 < n_it) {
         lse_next = p.lse[stat_index(it + 1)];
         dl_next = p.delta[stat_index(it + 1)];
+        if (p.doc_start != nullptr) ds_next = p.doc_start[doc_index(it + 1)];
       }
       if (!mbar_wait(sdp_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
@@ -569,6 +598,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
             const int col = col0 + cc * 32 + 2 * c + e;
             float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
             if (p.causal && qi == jt && col > row) pr = 0.f;
+            if (col < first_col) pr = 0.f;
             pv[e] = pr;
             dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl);
           }
@@ -713,10 +743,11 @@ extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, 
                                 int do_sb, int do_st, int do_sh, int q_sb, int q_st, int q_sh, int k_sb, int k_st, int k_sh,
                                 int v_sb, int v_st, int v_sh, int o_sb, int o_st, int o_sh, int dq_sb, int dq_st, int dq_sh,
                                 int dk_sb, int dk_st, int dk_sh, int dv_sb, int dv_st, int dv_sh, float scale, int causal,
-                                int* status, cudaStream_t stream) {
+                                int* status, const int* doc_start, cudaStream_t stream) {
   using namespace ob;
   if (B <= 0 || T <= 0) return 0;
   if (T % 128 != 0 || H % Hkv != 0) return -1;
+  if (doc_start != nullptr && !causal) return -5;
   if (q_sh != 128 || k_sh != 128 || v_sh != 128 || do_sh != 128) return -2;
   if (q_sb != T * q_st || k_sb != T * k_st || v_sb != T * v_st || do_sb != T * do_st) return -3;
   if ((dq_st % 8) || (dk_st % 8) || (dv_st % 8) || (dq_sh % 8) || (dk_sh % 8) || (dv_sh % 8)) return -4;
@@ -738,6 +769,7 @@ extern "C" int ob_attention_bwd(const void* dout, const void* q, const void* k, 
   attn_bwd_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(
       (const bf16*)dout, (const bf16*)o, delta, B, T, H, do_sb, do_st, do_sh, o_sb, o_st, o_sh);
   AttnBwdParams p;
+  p.doc_start = doc_start;
   p.lse = lse; p.delta = delta; p.dq_acc = dq_acc;
   p.dk = (bf16*)dk; p.dv = (bf16*)dv;
   p.dk_sb = dk_sb; p.dk_st = dk_st; p.dk_sh = dk_sh; p.dv_sb = dv_sb; p.dv_st = dv_st; p.dv_sh = dv_sh;

@@ -298,7 +298,7 @@ class OLMoSequentialBlock(OLMoBlock):
     ) -> Tuple[torch.Tensor, Optional[KV]]:
         from ..ops import fused_block
 
-        if cu_doc_lens is None and fused_block.eligible(self, x, attention_bias, layer_past, use_cache):
+        if fused_block.eligible(self, x, attention_bias, layer_past, use_cache, doc_masking=cu_doc_lens is not None):
             return fused_block.run_block(self, x, max_doc_len=max_doc_len, cu_doc_lens=cu_doc_lens), None
 
         cfg = self.config

@@ -71,6 +71,13 @@ def _expand_kv(k: torch.Tensor, H: int) -> torch.Tensor:
     return k if Hkv == H else k.repeat_interleave(H // Hkv, dim=2)
 
 
+def _doc_mask(doc_start: torch.Tensor) -> torch.Tensor:
+    """``[B, T]`` document starts -> boolean ``[B, 1, T, T]`` of pairs (query, key) with ``doc_start[query] <= key``."""
+    T = doc_start.shape[1]
+    keys = torch.arange(T, device=doc_start.device)
+    return (keys.view(1, 1, 1, T) >= doc_start.view(doc_start.shape[0], 1, T, 1).to(torch.int64))
+
+
 def _mask(Tq: int, Tk: int, causal: bool, device, cu: Optional[torch.Tensor] = None) -> Optional[torch.Tensor]:
     """Boolean ``(Tq, Tk)`` mask of allowed pairs (bottom-right aligned causal, like flash-attention)."""
     allowed = None
@@ -87,7 +94,7 @@ def _mask(Tq: int, Tk: int, causal: bool, device, cu: Optional[torch.Tensor] = N
 
 def math_attention_forward(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool, scale: Optional[float] = None,
-    cu_seqlens: Optional[torch.Tensor] = None,
+    cu_seqlens: Optional[torch.Tensor] = None, doc_start: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor]:
     """fp32 softmax attention; returns ``out (B,Tq,H,D)`` in the input dtype and ``lse (B,H,Tq)`` fp32."""
     B, Tq, H, D = q.shape
@@ -100,13 +107,15 @@ def math_attention_forward(
     allowed = _mask(Tq, Tk, causal, q.device, cu_seqlens)
     if allowed is not None:
         s = s.masked_fill(~allowed, float("-inf"))
+    if doc_start is not None:
+        s = s.masked_fill(~_doc_mask(doc_start), float("-inf"))
     lse = torch.logsumexp(s, dim=-1)
     p = torch.exp(s - lse.unsqueeze(-1))
     out = torch.matmul(p, vf).transpose(1, 2).to(q.dtype)
     return out, lse
 
 
-def _math_attention_backward(do, q, k, v, out, lse, causal, scale, cu_seqlens=None):
+def _math_attention_backward(do, q, k, v, out, lse, causal, scale, cu_seqlens=None, doc_start=None):
     B, Tq, H, D = q.shape
     Tk, Hkv = k.shape[1], k.shape[2]
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
@@ -118,6 +127,8 @@ def _math_attention_backward(do, q, k, v, out, lse, causal, scale, cu_seqlens=No
     allowed = _mask(Tq, Tk, causal, q.device, cu_seqlens)
     if allowed is not None:
         s = s.masked_fill(~allowed, float("-inf"))
+    if doc_start is not None:
+        s = s.masked_fill(~_doc_mask(doc_start), float("-inf"))
     p = torch.exp(s - lse.unsqueeze(-1))
     dv = torch.matmul(p.transpose(-1, -2), dof)
     dp = torch.matmul(dof, vf.transpose(-1, -2))
@@ -137,28 +148,31 @@ def _math_attention_backward(do, q, k, v, out, lse, causal, scale, cu_seqlens=No
 
 def attention_forward(
     q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, causal: bool = True, scale: Optional[float] = None,
-    out: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None, doc_start: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, torch.Tensor, str]:
-    """Forward without autograd bookkeeping: returns ``(out, lse, backend)``."""
+    """Forward without autograd bookkeeping: returns ``(out, lse, backend)``.  ``doc_start`` (int32 ``[B, T]``, causal
+    only) restricts every query to the keys of its own document; the native kernel and the math path implement it."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     be = backend_for(q, k, causal)
+    if doc_start is not None and be == "library":
+        be = "math"  # the library expresses document masking through packed variable-length calls only
     if be == "native":
         from . import attention_native
 
-        o, lse = attention_native.forward(q, k, v, causal, scale, out=out)
+        o, lse = attention_native.forward(q, k, v, causal, scale, out=out, doc_start=doc_start)
         return o, lse, be
     if be == "library":
         fai = _library()
         o, lse, _, _ = fai._flash_attn_forward(q, k, v, 0.0, scale, causal, -1, -1, 0.0, None, False)
         return o, lse, be
-    o, lse = math_attention_forward(q, k, v, causal, scale)
+    o, lse = math_attention_forward(q, k, v, causal, scale, doc_start=doc_start)
     return o, lse, be
 
 
 def attention_backward(
     do: torch.Tensor, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, lse: torch.Tensor,
     dq: torch.Tensor, dk: torch.Tensor, dv: torch.Tensor, causal: bool = True, scale: Optional[float] = None,
-    backend: Optional[str] = None,
+    backend: Optional[str] = None, doc_start: Optional[torch.Tensor] = None,
 ) -> None:
     """Backward into caller-provided (possibly strided) ``dq``, ``dk``, ``dv``."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
@@ -167,14 +181,16 @@ def attention_backward(
         from . import attention_native
 
         if attention_native.supports_backward(q, k, causal):
-            attention_native.backward(do, q, k, v, out, lse, dq, dk, dv, causal, scale)
+            attention_native.backward(do, q, k, v, out, lse, dq, dk, dv, causal, scale, doc_start=doc_start)
             return
-        be = "library" if _library() is not None else "math"
+        be = "library" if (_library() is not None and doc_start is None) else "math"
+    if doc_start is not None and be == "library":
+        be = "math"
     if be == "library":
         fai = _library()
         fai._flash_attn_backward(do, q, k, v, out, lse, dq, dk, dv, 0.0, scale, causal, -1, -1, 0.0, None, False)
         return
-    g = _math_attention_backward(do, q, k, v, out, lse, causal, scale)
+    g = _math_attention_backward(do, q, k, v, out, lse, causal, scale, doc_start=doc_start)
     dq.copy_(g[0])
     dk.copy_(g[1])
     dv.copy_(g[2])

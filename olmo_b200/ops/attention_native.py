@@ -22,7 +22,9 @@ def _have_symbol(name: str) -> bool:
 
 
 def supports(q: torch.Tensor, k: torch.Tensor, causal: bool, dropout_p: float, varlen: bool) -> bool:
-    """Forward kernel coverage: bf16, head dim 128, no dropout, self-attention (Tq == Tk), T % 128 == 0."""
+    """Forward kernel coverage: bf16, head dim 128, no dropout, self-attention (Tq == Tk), T % 128 == 0.  ``varlen`` means
+    packed sequences described by cumulative lengths; document masking inside fixed-length sequences is expressed with
+    ``doc_start`` instead (see :func:`doc_start_from_lengths`) and is covered when ``causal``."""
     if varlen or dropout_p != 0.0 or q.dtype != torch.bfloat16 or not q.is_cuda:
         return False
     if q.dim() != 4 or q.shape[-1] != 128 or q.shape[1] != k.shape[1] or q.shape[1] % 128 != 0:
@@ -41,21 +43,43 @@ def _strides(t: torch.Tensor) -> Tuple[int, int, int]:
     return t.stride(0), t.stride(1), t.stride(2)
 
 
-def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = None):
+def doc_start_from_lengths(doc_lens: torch.Tensor, seq_len: int) -> torch.Tensor:
+    """``[B, max_docs]`` document lengths (zero padded, each row summing to ``seq_len``) -> int32 ``[B, seq_len]`` with, for
+    every token, the position of the first token of its document."""
+    lens = doc_lens.to(torch.int64)
+    ends = lens.cumsum(dim=1)
+    starts = ends - lens
+    pos = torch.arange(seq_len, device=doc_lens.device).unsqueeze(0).expand(lens.shape[0], -1)
+    doc_of = torch.searchsorted(ends, pos.contiguous(), right=True).clamp_(max=lens.shape[1] - 1)
+    return starts.gather(1, doc_of).to(torch.int32).contiguous()
+
+
+def doc_start_from_cu(cu_doc_lens: torch.Tensor, batch: int, seq_len: int) -> torch.Tensor:
+    """Cumulative document boundaries over the flattened ``batch * seq_len`` token axis -> int32 ``[batch, seq_len]``."""
+    cu = cu_doc_lens.to(torch.int64)
+    pos = torch.arange(batch * seq_len, device=cu.device)
+    doc_of = torch.searchsorted(cu, pos, right=True) - 1
+    start = cu[doc_of.clamp_(min=0)]
+    return (start - (pos // seq_len) * seq_len).clamp_(min=0).view(batch, seq_len).to(torch.int32).contiguous()
+
+
+def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = None, doc_start: Optional[torch.Tensor] = None):
     B, T, H, D = q.shape
+    if doc_start is not None:
+        assert causal and doc_start.dtype == torch.int32 and doc_start.shape == (B, T) and doc_start.is_contiguous()
     Hkv = k.shape[2]
     o = torch.empty((B, T, H, D), dtype=q.dtype, device=q.device) if out is None else out
     lse = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
     rc = lib().ob_attention_fwd(
         ptr(q), ptr(k), ptr(v), ptr(o), ptr(lse), c_int(B), c_int(T), c_int(H), c_int(Hkv),
         *(c_int(s) for s in _strides(q)), *(c_int(s) for s in _strides(k)), *(c_int(s) for s in _strides(v)),
-        *(c_int(s) for s in _strides(o)), c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), stream_ptr(),
+        *(c_int(s) for s in _strides(o)), c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), ptr(doc_start), stream_ptr(),
     )
     check(rc, "ob_attention_fwd")
     return o, lse
 
 
-def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float) -> None:
+def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float, doc_start: Optional[torch.Tensor] = None) -> None:
     """Gradients into caller-provided (possibly strided) ``dq``, ``dk``, ``dv``.  Scratch: ``delta`` (B·H·T floats) and
     an fp32 ``dq`` accumulator (B·T·H·128 floats) that key tiles add into with vector reductions."""
     B, T, H, D = q.shape
@@ -68,7 +92,7 @@ def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float) -> Non
         *(c_int(s) for s in _strides(do)), *(c_int(s) for s in _strides(q)), *(c_int(s) for s in _strides(k)),
         *(c_int(s) for s in _strides(v)), *(c_int(s) for s in _strides(o)), *(c_int(s) for s in _strides(dq)),
         *(c_int(s) for s in _strides(dk)), *(c_int(s) for s in _strides(dv)),
-        c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), stream_ptr(),
+        c_float(scale), c_int(int(causal)), ptr(status_tensor(q.device)), ptr(doc_start), stream_ptr(),
     )
     check(rc, "ob_attention_bwd", kernels=3)
 

@@ -101,11 +101,14 @@ def config_supported(cfg) -> bool:
     )
 
 
-def eligible(block, x: torch.Tensor, attention_bias, layer_past, use_cache: bool) -> bool:
-    """True when this call can run on the fused path (training/eval forward without cache or explicit bias)."""
+def eligible(block, x: torch.Tensor, attention_bias, layer_past, use_cache: bool, doc_masking: bool = False) -> bool:
+    """True when this call can run on the fused path (training/eval forward without cache or explicit bias).  With
+    intra-document masking the native attention kernel must cover the shape (head dim 128, T a multiple of 128)."""
     if not (x.is_cuda and enabled()) or attention_bias is not None or layer_past is not None or use_cache:
         return False
-    if x.dtype != torch.bfloat16 and not (torch.is_autocast_enabled() and torch.get_autocast_gpu_dtype() == torch.bfloat16):
+    if doc_masking and (block.config.d_model // block.config.n_heads != 128 or x.shape[1] % 128 != 0):
+        return False
+    if x.dtype != torch.bfloat16 and not (torch.is_autocast_enabled() and torch.get_autocast_dtype("cuda") == torch.bfloat16):
         return False
     if block._activation_checkpoint_fn is not None:  # fine-grained checkpointing is a portable-path feature
         return False
@@ -170,6 +173,7 @@ def block_forward(
     sin: torch.Tensor,
     save: bool = True,
     gemm_kwargs: Optional[Dict[str, Dict[str, Any]]] = None,
+    doc_start: Optional[torch.Tensor] = None,
 ) -> Tuple[torch.Tensor, Optional[Dict[str, Any]]]:
     """``x`` is ``[B·T, d]`` bf16.  ``w`` maps ``att_proj, attn_out, ff_proj, ff_out`` to weights and
     ``attn_norm, ff_norm, q_norm, k_norm`` to norm weights or ``None``.  ``gemm_kwargs[name]`` may carry the
@@ -191,7 +195,7 @@ def block_forward(
     q = _split_heads(qk, 0, Wq, B, T, hd)
     kk = _split_heads(qk, Wq, Wk, B, T, hd)
     v = _split_heads(qk, Wq + Wk, Wk, B, T, hd) if spec.clip_qkv > 0 else _split_heads(qkv, Wq + Wk, Wk, B, T, hd)
-    o, lse, backend = attn.attention_forward(q, kk, v, causal=True)
+    o, lse, backend = attn.attention_forward(q, kk, v, causal=True, doc_start=doc_start)
     o2 = o.view(B * T, Wq)
     del qk, q, kk
 
@@ -214,7 +218,7 @@ def block_forward(
             saved.update(rstd2=rstd2, mean2=mean2)
     if not save:
         return y, None
-    saved.update(x=x, qkv=qkv, rstd_q=rstd_q, rstd_k=rstd_k, o=o, lse=lse, x1=x1, h=h, B=B, T=T, attn_backend=backend)
+    saved.update(x=x, qkv=qkv, rstd_q=rstd_q, rstd_k=rstd_k, o=o, lse=lse, x1=x1, h=h, B=B, T=T, attn_backend=backend, doc_start=doc_start)
     return y, saved
 
 
@@ -284,7 +288,7 @@ def block_backward(
     attn.attention_backward(
         d_o.view(B, T, spec.n_heads, hd), q, kk, v, saved["o"], saved["lse"],
         _split_heads(dqkv, 0, Wq, B, T, hd), _split_heads(dqkv, Wq, Wk, B, T, hd), _split_heads(dqkv, Wq + Wk, Wk, B, T, hd),
-        causal=True, backend=saved["attn_backend"],
+        causal=True, backend=saved["attn_backend"], doc_start=saved.get("doc_start"),
     )
     del qk, q, kk, d_o
     k.qk_norm_rope_bwd(
@@ -327,10 +331,10 @@ def _block_weights(block, dtype=torch.bfloat16) -> Dict[str, Optional[torch.Tens
 
 class _FusedBlock(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, spec, B, T, cos, sin, x, *params):
+    def forward(ctx, spec, B, T, cos, sin, doc_start, x, *params):
         w = dict(zip(_PARAM_ORDER, params))
         need_grad = torch.is_grad_enabled() and (x.requires_grad or any(p is not None and p.requires_grad for p in params))
-        y, saved = block_forward(spec, w, x, B, T, cos, sin, save=need_grad)
+        y, saved = block_forward(spec, w, x, B, T, cos, sin, save=need_grad, doc_start=doc_start)
         ctx.spec, ctx.saved, ctx.w, ctx.cos, ctx.sin = spec, saved, w, cos, sin
         return y
 
@@ -344,15 +348,18 @@ class _FusedBlock(torch.autograd.Function):
             g = sink.grads.get(name)
             p = ctx.w[name]
             grads.append(None if (g is None or p is None) else g.to(p.dtype))
-        return (None, None, None, None, None, dx, *grads)
+        return (None, None, None, None, None, None, dx, *grads)
 
 
 def run_block(block, x: torch.Tensor, max_doc_len=None, cu_doc_lens=None) -> torch.Tensor:
     """Autograd-visible fused block for ``(B, T, d)`` input.  Parameters held in fp32 are cast to bf16 on the
     way in (the engine avoids this by keeping bf16 compute copies)."""
-    if cu_doc_lens is not None:
-        raise NotImplementedError("document masking runs on the portable path")
     B, T, D = x.shape
+    doc_start = None
+    if cu_doc_lens is not None:  # intra-document masking: the kernels take per-token document starts
+        from .attention_native import doc_start_from_cu
+
+        doc_start = doc_start_from_cu(cu_doc_lens, B, T)
     spec = getattr(block, "_fused_spec", None)
     if spec is None:
         spec = block._fused_spec = spec_from_config(block.config)
@@ -361,5 +368,5 @@ def run_block(block, x: torch.Tensor, max_doc_len=None, cu_doc_lens=None) -> tor
     x2 = x.reshape(B * T, D)
     if x2.dtype != torch.bfloat16:
         x2 = x2.to(torch.bfloat16)
-    y = _FusedBlock.apply(spec, B, T, cos, sin, x2.contiguous(), *[w[n] for n in _PARAM_ORDER])
+    y = _FusedBlock.apply(spec, B, T, cos, sin, doc_start, x2.contiguous(), *[w[n] for n in _PARAM_ORDER])
     return y.view(B, T, D)

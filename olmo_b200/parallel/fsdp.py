@@ -603,8 +603,10 @@ class FlatShardEngine:
         z_mult: float = 0.0,
         ac_strategy: Optional[ActivationCheckpointingStrategy] = None,
         is_last: bool = True,
+        doc_start: Optional[torch.Tensor] = None,
     ) -> Tuple[torch.Tensor, torch.Tensor]:
-        """Forward + backward of one micro-batch on the fused path.
+        """Forward + backward of one micro-batch on the fused path.  ``doc_start`` (int32 ``[B, T]``) turns on
+        intra-document attention masking.
 
         ``labels`` uses ``-100`` for ignored positions and is already shifted (``labels[:, t]`` is the target of
         position ``t``).  Gradients of ``(ΣCE + z_mult·Σlse²) / loss_divisor`` are accumulated.  Returns the
@@ -661,10 +663,10 @@ class FlatShardEngine:
             gk = prefetch_kwargs() if gather_queue else None
             w = self._weights_of(block)
             if should_checkpoint_block(ac_strategy, i):
-                y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk)
+                y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk, doc_start=doc_start)
                 saved_list.append(("ckpt", x))
             else:
-                y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk)
+                y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start)
                 saved_list.append(("full", saved))
             x = y
         while gather_queue:
@@ -714,7 +716,7 @@ class FlatShardEngine:
             block = blocks[i]
             w = self._weights_of(block)
             if kind == "ckpt":
-                _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True)
+                _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start)
             dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block),
                                    gemm_kwargs=reduce_kwargs() if reduce_now else None)
             del payload

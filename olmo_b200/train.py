@@ -542,10 +542,24 @@ class Trainer:
             return False
         if batch.get("attention_mask") is not None and not bool(torch.all(batch["attention_mask"] == 1)):
             return False
-        if batch.get("attention_bias") is not None or batch.get("doc_lens") is not None:
+        if batch.get("attention_bias") is not None:
             return False
+        if batch.get("doc_lens") is not None:  # document masking needs the native attention kernel's shape coverage
+            mc = self.cfg.model
+            if mc.d_model // mc.n_heads != 128 or batch["input_ids"].shape[1] % 128 != 0:
+                return False
         steps = self.cfg.module_outputs_save_steps
         return not (steps is not None and self.global_step in steps)
+
+    @staticmethod
+    def _doc_start(batch: Dict[str, Any]) -> Optional[torch.Tensor]:
+        """Per-token document starts for intra-document masking on the fused path (``None`` without ``doc_lens``)."""
+        doc_lens = batch.get("doc_lens")
+        if doc_lens is None:
+            return None
+        from .ops.attention_native import doc_start_from_lengths
+
+        return doc_start_from_lengths(doc_lens, batch["input_ids"].shape[1])
 
     def _labels_aligned(self, batch: Dict[str, Any]) -> torch.Tensor:
         """``(B, T)`` labels where entry ``t`` is the target of position ``t`` (last position ignored)."""
@@ -567,6 +581,7 @@ class Trainer:
                     z_mult=1e-4 if self.cfg.softmax_auxiliary_loss else 0.0,
                     ac_strategy=self.model.activation_checkpointing_strategy,
                     is_last=idx == n - 1,
+                    doc_start=self._doc_start(mb),
                 )
                 ce_batch_loss += ce
                 if z_batch_loss is not None:
