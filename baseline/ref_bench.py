@@ -85,7 +85,7 @@ def _run(args, presets) -> dict:
         init_device="meta", init_fn=InitFnType.normal if olmo2 else InitFnType.mitchell, init_std=0.02,
         init_cutoff_factor=3 if olmo2 else None, clip_qkv=None if olmo2 else 8.0,
     )
-    device_batch = args.device_batch or max(ps["microbatch"], ps["global_batch"] // 8)
+    device_batch = args.device_batch or max(ps["microbatch"], min(32, ps["global_batch"] // 8))  # same default as the main arm
     ac = None if args.activation_checkpointing in (None, "none") else ActivationCheckpointingStrategy(args.activation_checkpointing)
     cfg = TrainConfig(
         run_name=f"bench-ref-{args.model}", model=model_cfg,

@@ -9,8 +9,12 @@ one node, synthetic seeded token data, random-init weights, bf16 compute with fp
     python bench.py --impl reference ...        # the unmodified reference (baseline/_ref) on the same config
 
 Per GPU the work is fixed (weak scaling): ``--device-batch`` sequences of ``seq_len`` tokens per optimizer step, split
-into micro-batches of the model's official size, so the global batch is ``N × device_batch`` (1024 sequences at 8 GPUs
-for the 7B preset, as in the official config).
+into micro-batches of the model's official size (2 for the 7B preset), so the global batch is ``N × device_batch``.
+The official run accumulates 64 micro-batches per GPU and step (1024 sequences over 8 GPUs, ``--device-batch 128``:
+26 s per step here, 52 s for the reference arm); the default is 32 sequences (16 micro-batches) so that a run with
+many timed steps still finishes in minutes.  Throughput hardly depends on it, because only the once-per-step work
+(optimizer, gather, reduce-scatter; about 40 ms) is amortised differently; both figures are given in the repository's
+design notes.
 
 Two measurements are reported: ``value`` times K optimizer steps with CUDA events while the token batches already sit
 on the device; ``e2e`` times K further steps by wall clock through ``Trainer.train_step`` with every step's batch
@@ -49,7 +53,8 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--model", choices=sorted(PRESETS), default="olmo2-7b")
     p.add_argument("--seq-len", type=int, default=4096)
-    p.add_argument("--device-batch", type=int, default=None, help="sequences per GPU per optimizer step (default: official global batch / 8)")
+    p.add_argument("--device-batch", type=int, default=None,
+                   help="sequences per GPU per optimizer step (default: 32; the official global batch / 8 is 128 for the 7B preset)")
     p.add_argument("--activation-checkpointing", default=None)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--sharding", default="FULL_SHARD", choices=["FULL_SHARD", "SHARD_GRAD_OP", "HYBRID_SHARD", "NO_SHARD"],
@@ -81,7 +86,7 @@ def make_train_config(args, world: int):
         init_device="meta", init_fn=InitFnType.normal if olmo2 else InitFnType.mitchell, init_std=0.02,
         init_cutoff_factor=3 if olmo2 else None, clip_qkv=None if olmo2 else 8.0,
     )
-    device_batch = args.device_batch or max(ps["microbatch"], ps["global_batch"] // 8)
+    device_batch = args.device_batch or max(ps["microbatch"], min(32, ps["global_batch"] // 8))
     cfg = TrainConfig(
         run_name=f"bench-{args.model}", model=model,
         optimizer=OptimizerConfig(name=OptimizerType.adamw, learning_rate=3e-4, weight_decay=0.1, eps=1e-8, betas=(0.9, 0.95),
@@ -265,6 +270,7 @@ def run_ours(args) -> dict:
         "config": {
             "model": args.model if not args.n_layers else f"{args.model} REDUCED to {args.n_layers} layers (profiling only)",
             "global_batch": device_batch * world, "seq_len": args.seq_len,
+            "official_global_batch_at_8_gpus": ps["global_batch"], "sequences_per_gpu_per_step": device_batch,
             "micro_batch": ps["microbatch"], "grad_accum": cfg.device_train_grad_accum,
             "parallelism": (f"fsdp{world}" if args.sharding == "FULL_SHARD" else f"{args.sharding.lower()}{world}") if world > 1 else "single-gpu flat-shard engine",
             "activation_checkpointing": args.activation_checkpointing or "none",
