@@ -71,7 +71,10 @@ def build_evaluator(train_config: TrainConfig, eval_config: EvaluatorConfig, tok
 def build_evaluators(cfg: TrainConfig, device: torch.device) -> List[Evaluator]:
     if not cfg.evaluators:
         return []
-    from ..tokenizer import Tokenizer
+    tokenizer = None
+    if any(e.type == EvaluatorType.downstream for e in cfg.evaluators):
+        # only in-context tasks render text; perplexity evaluators read token files and need no vocabulary
+        from ..tokenizer import Tokenizer
 
-    tokenizer = Tokenizer.from_train_config(cfg)
+        tokenizer = Tokenizer.from_train_config(cfg)
     return [build_evaluator(cfg, eval_cfg, tokenizer, device) for eval_cfg in cfg.evaluators]
