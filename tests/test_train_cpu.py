@@ -71,3 +71,60 @@ def test_loss_decreases_and_checkpoint_round_trip(tmp_path):
         it2 = iter(t2.train_loader)  # data position restored: the next batch is batch #9
         again = t2.train_step(next(it2))["train/CrossEntropyLoss"]
         assert abs(again - next_loss) < 1e-5
+
+
+def test_trainer_eval_runs_a_downstream_task(tmp_path, monkeypatch):
+    """``Trainer.eval`` drives a multiple-choice task end to end: request batches through the model, the ranked
+    classification metric, and the metric key the reference logs under (``olmo/eval/evaluator.py:31-45``)."""
+    datasets = pytest.importorskip("datasets")
+    from olmo_b200.config import EvaluatorConfig, EvaluatorType
+    from olmo_b200.eval import build_downstream_evaluator
+
+    class CharTokenizer:
+        pad_token_id = 0
+        eos_token_id = 1
+
+        def encode(self, s, add_special_tokens=True):
+            return [ord(c) for c in s] + ([self.eos_token_id] if add_special_tokens else [])
+
+        def decode(self, ids, skip_special_tokens=True):
+            return "".join(chr(i) for i in ids if i > 1)
+
+    rows = [{"goal": f"goal {i}", "sol1": "ab" * (1 + i % 3), "sol2": "cd" * (1 + i % 2), "label": i % 2} for i in range(6)]
+    datasets.Dataset.from_list(rows).save_to_disk(str(tmp_path / "hf_datasets" / "piqa" / "plain_text" / "validation"))
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "run")
+    cfg.device_eval_batch_size = 4
+    cfg.eval_subset_num_batches = -1
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    ev_cfg = EvaluatorConfig(label="piqa", type=EvaluatorType.downstream)
+    evaluator = build_downstream_evaluator(cfg, ev_cfg, CharTokenizer(), torch.device("cpu"), is_unit_test=True)
+    assert len(evaluator.eval_loader.dataset) == 12  # two continuations per document
+    trainer.evaluators = [evaluator]
+    results = trainer.eval()
+    assert list(results) == ["eval/downstream/piqa_len_norm"]
+
+    # the same number computed by hand: length-normalised continuation log-likelihood, argmax per document
+    model = trainer.dist_model.module if hasattr(trainer.dist_model, "module") else trainer.model
+    model.eval()
+    ds = evaluator.eval_loader.dataset
+    scores = {}
+    with torch.no_grad():
+        for i in range(len(ds)):
+            item = ds[i]
+            ids = torch.as_tensor(item["query"]).unsqueeze(0)
+            logp = torch.log_softmax(model(ids).logits[0].float(), dim=-1)
+            ctx_len, cont = int(item["ctx_len"]), torch.as_tensor(item["continuation"])
+            lp = logp[ctx_len - 1 : ctx_len - 1 + len(cont)].gather(1, cont.unsqueeze(1)).sum()
+            scores.setdefault(int(item["doc_id"]), {})[int(item["cont_id"])] = (float(lp) / int(item["cont_str_len"]), int(item["label_id"]))
+    correct = [max(conts, key=lambda c: conts[c][0]) == next(iter(conts.values()))[1] for conts in scores.values()]
+    assert results["eval/downstream/piqa_len_norm"] == pytest.approx(sum(correct) / len(correct))
+
+    # a subset limit caps the number of batches
+    evaluator.subset_num_batches = 1
+    seen = []
+    monkeypatch.setattr(evaluator, "compute_metrics", lambda: seen.append(len(evaluator.eval_metric.scores)) or {})
+    trainer.eval()
+    assert seen == [4]
