@@ -1,0 +1,325 @@
+"""
+Offline evaluation pipeline: every model of an experiment is scored on every task of every task set, each
+(model, task) result is cached in a workspace folder, and the results are written as rows.
+
+This is the role of the reference's ``evaluation/`` folder, which wires third-party workflow and task libraries
+together (``evaluation/steps/run_catwalk.py:25-351``: build the task, build the model, predict and compute metrics,
+post-process, write rows; ``evaluation/experiments/utils.libsonnet``: the models × task-sets cross product).  Here the
+steps are plain functions over this framework's own model, tokenizer and task classes, and an experiment is a YAML
+file:
+
+    workspace: runs/eval-workspace
+    output: runs/eval-rows.jsonl            # also written next to it as .tsv
+    wandb: {project: ..., entity: ..., name: ...}   # optional
+    models:
+      - model_path: /checkpoints/step1000-unsharded
+        prediction_kwargs: {limit: 500}    # overrides the task sets' values for this model
+    task_sets:
+      - rc_tasks                            # a name under evaluation/task_sets/, or an inline mapping
+      - name: my_ppl
+        tasks:
+          - {task_name: ppl, task_kwargs: {files: [/data/val.jsonl.gz]}, prediction_kwargs: {model_max_length: 2048}}
+
+Two task kinds exist.  A *ranked-classification* task is any label of
+:data:`olmo_b200.eval.downstream.label_to_task_map` and reports that task's metric.  A *perplexity* task (``ppl``) reads
+documents from ``.jsonl[.gz]`` files with a ``text`` field, or token ids from ``.npy`` memmaps, and reports
+``ppl_token``, ``ppl_char``, ``ppl_word``, ``ppl_byte`` and ``bits_per_byte``.
+"""
+from __future__ import annotations
+
+import gzip
+import hashlib
+import json
+import logging
+import math
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Dict, Iterable, Iterator, List, Optional, Sequence, Tuple
+
+import torch
+import torch.nn.functional as F
+
+log = logging.getLogger(__name__)
+
+__all__ = [
+    "EvalModel", "load_experiment", "resolve_task_set", "construct_task", "predict_and_calculate_metrics", "run_experiment",
+    "write_rows", "TASK_SET_DIR",
+]
+
+#: task-set files shipped with the repository (``<repo>/evaluation/task_sets/*.yaml``)
+TASK_SET_DIR = Path(__file__).resolve().parent.parent.parent / "evaluation" / "task_sets"
+
+
+# --------------------------------------------------------------------------------------------- model
+@dataclass
+class EvalModel:
+    """A loaded model with its tokenizer.  ``model_path`` is a native checkpoint folder (sharded or unsharded)."""
+
+    model_path: str
+    model: Any
+    tokenizer: Any
+    device: torch.device
+
+    @classmethod
+    def load(cls, model_path: str, device: Optional[str] = None, dtype: Optional[str] = None, tokenizer: Optional[str] = None) -> "EvalModel":
+        from ..models.olmo import OLMo
+        from ..tokenizer import Tokenizer
+
+        dev = torch.device(device or ("cuda" if torch.cuda.is_available() else "cpu"))
+        model = OLMo.from_checkpoint(model_path, device="cpu")
+        dtype = dtype or ("bf16" if dev.type == "cuda" else "fp32")
+        model = model.to({"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[dtype]).to(dev).eval()
+        if tokenizer is None:
+            tok = Tokenizer.from_checkpoint(model_path)
+        else:
+            tok = Tokenizer.from_file(tokenizer) if tokenizer.endswith(".json") else Tokenizer.from_pretrained(tokenizer)
+        return cls(model_path, model, tok, dev)
+
+    @property
+    def max_length(self) -> int:
+        return self.model.config.max_sequence_length
+
+    @torch.no_grad()
+    def logits(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        return self.model(input_ids.to(self.device), attention_mask=None if attention_mask is None else attention_mask.to(self.device)).logits
+
+
+# ------------------------------------------------------------------------------------- configuration
+def _read_yaml(path: Path) -> Any:
+    import yaml
+
+    with open(path) as f:
+        return yaml.safe_load(f)
+
+
+def resolve_task_set(entry: Any, search: Sequence[Path] = ()) -> Dict[str, Any]:
+    """A task set is ``{name, tasks: [{task_name, task_kwargs?, prediction_kwargs?}]}``; a string names a YAML file."""
+    if isinstance(entry, str):
+        for folder in list(search) + [TASK_SET_DIR]:
+            for candidate in (folder / entry, folder / f"{entry}.yaml"):
+                if candidate.is_file():
+                    entry = _read_yaml(candidate)
+                    break
+            if not isinstance(entry, str):
+                break
+        else:
+            raise FileNotFoundError(f"task set '{entry}' not found under {[str(p) for p in list(search) + [TASK_SET_DIR]]}")
+    if "task_names" in entry:  # short form: the same kwargs for a list of labels
+        shared = {k: entry.get(k, {}) for k in ("task_kwargs", "prediction_kwargs")}
+        entry = {"name": entry["name"], "tasks": [{"task_name": t, **json.loads(json.dumps(shared))} for t in entry["task_names"]]}
+    for task in entry["tasks"]:
+        task.setdefault("task_kwargs", {})
+        task.setdefault("prediction_kwargs", {})
+    return entry
+
+
+def load_experiment(path: str) -> Dict[str, Any]:
+    file = Path(path)
+    spec = _read_yaml(file)
+    if not spec.get("models") or not spec.get("task_sets"):
+        raise ValueError("an experiment needs 'models' and 'task_sets'")
+    spec["task_sets"] = [resolve_task_set(t, search=[file.parent, file.parent / "task_sets"]) for t in spec["task_sets"]]
+    spec["models"] = [{"model_path": m} if isinstance(m, str) else dict(m) for m in spec["models"]]
+    return spec
+
+
+# --------------------------------------------------------------------------------------------- tasks
+@dataclass
+class PerplexityTask:
+    """Documents from text or token files, scored in disjoint windows of ``model_max_length`` tokens, each window
+    conditioned on the end-of-text token."""
+
+    files: Sequence[str]
+    text_field: str = "text"
+    memmap_dtype: str = "uint16"
+    name: str = "ppl"
+
+    def documents(self, tokenizer) -> Iterator[Tuple[List[int], str]]:
+        import numpy as np
+
+        for file in self.files:
+            if str(file).endswith(".npy"):
+                tokens = np.memmap(file, dtype=getattr(np, self.memmap_dtype), mode="r")
+                eos = tokenizer.eos_token_id
+                start = 0
+                for end in list(np.nonzero(tokens == eos)[0]) + [len(tokens)]:
+                    ids = tokens[start:end].astype(np.int64).tolist()
+                    start = end + 1
+                    if ids:
+                        yield ids, tokenizer.decode(ids)
+            else:
+                opener = gzip.open if str(file).endswith(".gz") else open
+                with opener(file, "rt", encoding="utf-8") as f:
+                    for line in f:
+                        if line.strip():
+                            text = json.loads(line)[self.text_field]
+                            yield tokenizer.encode(text, add_special_tokens=False), text
+
+
+def construct_task(task_name: str, tokenizer, task_kwargs: Optional[Dict[str, Any]] = None, model_max_length: Optional[int] = None):
+    """Build the task object: a :class:`PerplexityTask` for ``ppl``, else the labelled multiple-choice dataset."""
+    task_kwargs = dict(task_kwargs or {})
+    if task_name == "ppl":
+        return PerplexityTask(**task_kwargs)
+    from .downstream import label_to_task_map
+
+    if task_name not in label_to_task_map:
+        raise KeyError(f"unknown task '{task_name}'; ranked-classification labels: {sorted(label_to_task_map)[:8]}… or 'ppl'")
+    entry = label_to_task_map[task_name]
+    cls, fixed = entry if isinstance(entry, tuple) else (entry, {})
+    kwargs = {**fixed, **task_kwargs}
+    if model_max_length is not None:
+        kwargs.setdefault("model_ctx_len", model_max_length)
+    return cls(tokenizer=tokenizer, **kwargs)
+
+
+def _score_perplexity(model: EvalModel, task: PerplexityTask, limit: Optional[int], max_length: int, batch_size: int) -> Dict[str, Any]:
+    eos = model.tokenizer.eos_token_id
+    totals = {"logprob": 0.0, "tokens": 0, "chars": 0, "words": 0, "bytes": 0, "documents": 0}
+    windows: List[List[int]] = []
+
+    def flush() -> None:
+        if not windows:
+            return
+        width = max(len(w) for w in windows)
+        ids = torch.full((len(windows), width), model.model.config.pad_token_id, dtype=torch.long)
+        mask = torch.zeros(len(windows), width)
+        for i, w in enumerate(windows):  # right padding: causal attention never looks at it
+            ids[i, : len(w)] = torch.tensor(w)
+            mask[i, : len(w)] = 1
+        logp = F.log_softmax(model.logits(ids).float(), dim=-1).cpu()
+        gathered = logp[:, :-1].gather(2, ids[:, 1:].unsqueeze(-1)).squeeze(-1)
+        totals["logprob"] += float((gathered * mask[:, 1:]).sum())
+        windows.clear()
+
+    for n, (ids, text) in enumerate(task.documents(model.tokenizer)):
+        if limit is not None and n >= limit:
+            break
+        totals["documents"] += 1
+        totals["tokens"] += len(ids)
+        totals["chars"] += len(text)
+        totals["words"] += len(text.split())
+        totals["bytes"] += len(text.encode("utf-8"))
+        for start in range(0, len(ids), max_length - 1):
+            windows.append([eos] + ids[start : start + max_length - 1])
+            if len(windows) == batch_size:
+                flush()
+    flush()
+    nll = -totals["logprob"]
+    metrics = {f"ppl_{unit[:-1]}": math.exp(nll / max(1, totals[unit])) for unit in ("tokens", "chars", "words", "bytes")}
+    metrics["bits_per_byte"] = nll / max(1, totals["bytes"]) / math.log(2)
+    return {"metrics": metrics, "num_instances": totals["documents"], "num_tokens": totals["tokens"]}
+
+
+def _score_ranked(model: EvalModel, task, limit: Optional[int], batch_size: int, num_recorded_inputs: int) -> Dict[str, Any]:
+    from .metrics import ICLMetric
+
+    metric = ICLMetric(metric_type=task.metric_type)
+    doc_limit = None
+    if limit is not None:  # keep whole documents: every continuation of the first ``limit`` documents
+        doc_limit = sorted({int(task[i]["doc_id"]) for i in range(len(task))})[:limit]
+        doc_limit = set(doc_limit)
+    items = [task[i] for i in range(len(task)) if doc_limit is None or int(task[i]["doc_id"]) in doc_limit]
+    recorded = []
+    for start in range(0, len(items), batch_size):
+        batch = task.collate_fn(items[start : start + batch_size])
+        logits = model.logits(batch["input_ids"]).cpu()
+        dc_logits = model.logits(batch["dc_input_ids"]).cpu() if task.metric_type == "pmi_dc" else None
+        metric.update(batch, logits, dc_logits)
+    for item in items[:num_recorded_inputs]:
+        recorded.append({"query": model.tokenizer.decode(item["query"]), "continuation": model.tokenizer.decode(item["continuation"]),
+                         "label_id": int(item["label_id"])})
+    documents = len({int(it["doc_id"]) for it in items})
+    return {"metrics": {task.metric_type: float(metric.compute())}, "num_instances": documents, "recorded_inputs": recorded}
+
+
+def predict_and_calculate_metrics(model: EvalModel, task, prediction_kwargs: Optional[Dict[str, Any]] = None) -> Dict[str, Any]:
+    """Run one task.  Understood ``prediction_kwargs``: ``limit`` (documents), ``batch_size``, ``model_max_length``,
+    ``num_recorded_inputs``."""
+    kw = dict(prediction_kwargs or {})
+    limit = kw.get("limit")
+    batch_size = int(kw.get("batch_size", 8))
+    max_length = min(int(kw.get("model_max_length") or model.max_length), model.max_length)
+    started = time.time()
+    if isinstance(task, PerplexityTask):
+        out = _score_perplexity(model, task, limit, max_length, batch_size)
+    else:
+        out = _score_ranked(model, task, limit, batch_size, int(kw.get("num_recorded_inputs", 0)))
+    out["processing_time"] = time.time() - started
+    return out
+
+
+# ------------------------------------------------------------------------------------------ pipeline
+def _step_key(model_spec: Dict[str, Any], task: Dict[str, Any], prediction_kwargs: Dict[str, Any]) -> str:
+    blob = json.dumps({"model": model_spec, "task": task["task_name"], "task_kwargs": task["task_kwargs"], "pred": prediction_kwargs},
+                      sort_keys=True, default=str)
+    return hashlib.sha256(blob.encode()).hexdigest()[:24]
+
+
+def run_experiment(spec: Dict[str, Any], loader=EvalModel.load) -> List[Dict[str, Any]]:
+    """The models × task-sets cross product.  A (model, task, kwargs) result found in the workspace is reused, so an
+    interrupted or extended experiment only computes what is new.  Returns one row per (model, task set, task)."""
+    workspace = Path(spec.get("workspace") or "eval-workspace")
+    workspace.mkdir(parents=True, exist_ok=True)
+    rows: List[Dict[str, Any]] = []
+    for model_spec in spec["models"]:
+        model: Optional[EvalModel] = None
+        identity = {k: v for k, v in model_spec.items() if k not in ("prediction_kwargs", "gpus_needed")}
+        for task_set in spec["task_sets"]:
+            for task in task_set["tasks"]:
+                pred = {**task["prediction_kwargs"], **model_spec.get("prediction_kwargs", {})}
+                cache = workspace / f"{_step_key(identity, task, pred)}.json"
+                if cache.is_file():
+                    result = json.loads(cache.read_text())
+                    log.info("reusing %s for %s / %s", cache.name, model_spec["model_path"], task["task_name"])
+                else:
+                    if model is None:
+                        model = loader(**{k: v for k, v in identity.items() if k in ("model_path", "device", "dtype", "tokenizer")})
+                    built = construct_task(task["task_name"], model.tokenizer, task["task_kwargs"], pred.get("model_max_length"))
+                    result = predict_and_calculate_metrics(model, built, pred)
+                    tmp = cache.with_suffix(".tmp")
+                    tmp.write_text(json.dumps(result))
+                    tmp.replace(cache)
+                row = {
+                    "model_path": model_spec["model_path"], "revision": model_spec.get("revision"), "task_set": task_set["name"],
+                    "task": task.get("task_rename") or task["task_name"], "split": task["task_kwargs"].get("split"),
+                    "limit": pred.get("limit"), "num_instances": result.get("num_instances"),
+                    "processing_time": result.get("processing_time"), **{f"metric_{k}": v for k, v in result["metrics"].items()},
+                }
+                rows.append(row)
+    if spec.get("output"):
+        write_rows(rows, spec["output"])
+    if spec.get("wandb"):
+        _log_to_wandb(rows, spec["wandb"])
+    return rows
+
+
+def write_rows(rows: List[Dict[str, Any]], output: str) -> Tuple[Path, Path]:
+    """JSON lines plus a tab-separated table with the union of all columns."""
+    out = Path(output)
+    out.parent.mkdir(parents=True, exist_ok=True)
+    with open(out, "w") as f:
+        for row in rows:
+            f.write(json.dumps(row) + "\n")
+    columns: List[str] = []
+    for row in rows:
+        columns += [c for c in row if c not in columns]
+    table = out.with_suffix(".tsv")
+    with open(table, "w") as f:
+        f.write("\t".join(columns) + "\n")
+        for row in rows:
+            f.write("\t".join("" if row.get(c) is None else str(row[c]) for c in columns) + "\n")
+    return out, table
+
+
+def _log_to_wandb(rows: List[Dict[str, Any]], settings: Dict[str, Any]) -> None:
+    """One summary entry per (task set, task, metric), as the reference's metrics step does (``evaluation/steps/wandb_metrics.py``)."""
+    import wandb  # optional dependency: only needed when an experiment asks for it
+
+    run = wandb.init(project=settings.get("project"), entity=settings.get("entity"), name=settings.get("name"), config={"rows": len(rows)})
+    for row in rows:
+        for key, value in row.items():
+            if key.startswith("metric_"):
+                run.summary[f"{row['task_set']}/{row['task']}/{key[7:]}"] = value
+    run.finish()

@@ -1,0 +1,139 @@
+"""Offline evaluation pipeline: task construction, perplexity arithmetic, caching in the workspace, rows."""
+import gzip
+import json
+import math
+
+import numpy as np
+import pytest
+import torch
+import yaml
+
+from olmo_b200.config import ActivationType, LayerNormType, ModelConfig
+from olmo_b200.eval import offline
+from olmo_b200.models.olmo import OLMo
+
+datasets = pytest.importorskip("datasets")
+EOS = 1
+
+
+class CharTokenizer:
+    pad_token_id = 0
+    eos_token_id = EOS
+
+    def encode(self, s, add_special_tokens=True):
+        return [min(ord(c), 127) for c in s] + ([EOS] if add_special_tokens else [])
+
+    def decode(self, ids, skip_special_tokens=True):
+        return "".join(chr(i) for i in ids if i > 1)
+
+
+@pytest.fixture()
+def eval_model():
+    torch.manual_seed(0)
+    cfg = ModelConfig(
+        d_model=32, n_heads=2, n_layers=2, mlp_hidden_size=64, activation_type=ActivationType.swiglu, rope=True,
+        layer_norm_type=LayerNormType.rms, include_bias=False, vocab_size=128, embedding_size=128, max_sequence_length=32,
+        eos_token_id=EOS, pad_token_id=0, weight_tying=False, init_device="cpu",
+    )
+    return offline.EvalModel("tiny", OLMo(cfg).eval(), CharTokenizer(), torch.device("cpu"))
+
+
+def test_perplexity_metrics_match_a_direct_computation(tmp_path, eval_model):
+    docs = ["the cat sat on the mat", "a much longer document that needs more than one window of thirty-two tokens to score"]
+    text_file = tmp_path / "val.jsonl.gz"
+    with gzip.open(text_file, "wt") as f:
+        for d in docs:
+            f.write(json.dumps({"text": d}) + "\n")
+    task = offline.construct_task("ppl", eval_model.tokenizer, {"files": [str(text_file)]})
+    out = offline.predict_and_calculate_metrics(eval_model, task, {"batch_size": 2, "model_max_length": 16})
+
+    nll = 0.0
+    with torch.no_grad():
+        for d in docs:
+            ids = eval_model.tokenizer.encode(d, add_special_tokens=False)
+            for start in range(0, len(ids), 15):
+                window = torch.tensor([[EOS] + ids[start : start + 15]])
+                logp = torch.log_softmax(eval_model.model(window).logits[0].float(), dim=-1)
+                nll -= float(logp[:-1].gather(1, window[0, 1:, None]).sum())
+    chars = sum(map(len, docs))
+    words = sum(len(d.split()) for d in docs)
+    assert out["num_instances"] == 2 and out["num_tokens"] == chars
+    assert out["metrics"]["ppl_token"] == pytest.approx(math.exp(nll / chars), rel=1e-5)
+    assert out["metrics"]["ppl_word"] == pytest.approx(math.exp(nll / words), rel=1e-5)
+    assert out["metrics"]["bits_per_byte"] == pytest.approx(nll / chars / math.log(2), rel=1e-5)
+
+    # the same documents as a token memmap (separated by the end token) give the same numbers
+    tokens = []
+    for d in docs:
+        tokens += eval_model.tokenizer.encode(d, add_special_tokens=True)
+    np.array(tokens, dtype=np.uint16).tofile(tmp_path / "val.npy")
+    mm = offline.construct_task("ppl", eval_model.tokenizer, {"files": [str(tmp_path / "val.npy")]})
+    again = offline.predict_and_calculate_metrics(eval_model, mm, {"model_max_length": 16})
+    assert again["metrics"]["ppl_token"] == pytest.approx(out["metrics"]["ppl_token"], rel=1e-6)
+    limited = offline.predict_and_calculate_metrics(eval_model, mm, {"model_max_length": 16, "limit": 1})
+    assert limited["num_instances"] == 1
+
+
+def test_experiment_runs_the_cross_product_and_reuses_cached_steps(tmp_path, monkeypatch, eval_model):
+    rows = [{"goal": f"goal {i}", "sol1": "ab" * (1 + i % 3), "sol2": "cd", "label": i % 2} for i in range(8)]
+    datasets.Dataset.from_list(rows).save_to_disk(str(tmp_path / "hf_datasets" / "piqa" / "plain_text" / "validation"))
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+    text_file = tmp_path / "val.jsonl"
+    text_file.write_text(json.dumps({"text": "hello evaluation"}) + "\n")
+    (tmp_path / "task_sets").mkdir()
+    (tmp_path / "task_sets" / "my_rc.yaml").write_text(yaml.safe_dump(
+        {"name": "my_rc", "task_names": ["piqa"], "prediction_kwargs": {"limit": 6, "num_recorded_inputs": 2}}))
+    experiment = {
+        "workspace": str(tmp_path / "ws"), "output": str(tmp_path / "out" / "rows.jsonl"),
+        "models": [{"model_path": "tiny-a"}, {"model_path": "tiny-b", "prediction_kwargs": {"limit": 4}}],
+        "task_sets": ["my_rc", {"name": "ppl_set", "tasks": [{"task_name": "ppl", "task_rename": "ppl_hello", "task_kwargs": {"files": [str(text_file)]}}]}],
+    }
+    (tmp_path / "exp.yaml").write_text(yaml.safe_dump(experiment))
+    spec = offline.load_experiment(str(tmp_path / "exp.yaml"))
+    assert spec["task_sets"][0]["tasks"][0] == {"task_name": "piqa", "task_kwargs": {}, "prediction_kwargs": {"limit": 6, "num_recorded_inputs": 2}}
+
+    loads = []
+
+    def loader(model_path, **kwargs):
+        loads.append(model_path)
+        return offline.EvalModel(model_path, eval_model.model, eval_model.tokenizer, eval_model.device)
+
+    out = offline.run_experiment(spec, loader=loader)
+    assert [(r["model_path"], r["task_set"], r["task"]) for r in out] == [
+        ("tiny-a", "my_rc", "piqa"), ("tiny-a", "ppl_set", "ppl_hello"), ("tiny-b", "my_rc", "piqa"), ("tiny-b", "ppl_set", "ppl_hello")]
+    assert out[0]["num_instances"] == 6 and out[2]["num_instances"] == 4 and out[2]["limit"] == 4
+    assert 0.0 <= out[0]["metric_len_norm"] <= 1.0 and out[1]["metric_ppl_token"] > 1.0
+    assert loads == ["tiny-a", "tiny-b"]
+    assert len(list((tmp_path / "ws").glob("*.json"))) == 4
+
+    lines = [json.loads(l) for l in (tmp_path / "out" / "rows.jsonl").read_text().splitlines()]
+    assert lines == json.loads(json.dumps(out))
+    table = (tmp_path / "out" / "rows.tsv").read_text().splitlines()
+    assert table[0].split("\t")[:4] == ["model_path", "revision", "task_set", "task"] and len(table) == 5
+    assert "metric_len_norm" in table[0] and "metric_bits_per_byte" in table[0]
+
+    # a second run finds every step in the workspace: no model is loaded, numbers are identical
+    loads.clear()
+    second = offline.run_experiment(spec, loader=loader)
+    assert loads == [] and [r["metric_len_norm"] for r in second[::2]] == [r["metric_len_norm"] for r in out[::2]]
+    # a new task set only computes what is new
+    spec["task_sets"].append({"name": "more", "tasks": [{"task_name": "ppl", "task_kwargs": {"files": [str(text_file)]}, "prediction_kwargs": {"model_max_length": 8}}]})
+    third = offline.run_experiment(spec, loader=loader)
+    assert loads == ["tiny-a", "tiny-b"] and len(third) == 6
+
+    with pytest.raises(KeyError):
+        offline.construct_task("no_such_task", eval_model.tokenizer)
+    with pytest.raises(FileNotFoundError):
+        offline.resolve_task_set("no_such_set")
+
+
+def test_shipped_task_sets_name_known_tasks():
+    from olmo_b200.eval.downstream import label_to_task_map
+
+    files = sorted(offline.TASK_SET_DIR.glob("*.yaml"))
+    assert {f.stem for f in files} >= {"rc_tasks", "mmlu_tasks", "bpb_tasks", "ppl_val_example"}
+    for file in files:
+        task_set = offline.resolve_task_set(file.stem)
+        assert task_set["name"] == file.stem and task_set["tasks"]
+        for task in task_set["tasks"]:
+            assert task["task_name"] == "ppl" or task["task_name"] in label_to_task_map, (file.name, task["task_name"])
