@@ -152,6 +152,41 @@ for _name, _mb in (("20M", 16), ("60M", 8), ("150M", 4), ("300M", 4), ("700M", 2
         "evaluators": _CORE_TASKS,
     }
 
+# The development runs the official OLMo-2 configs were distilled from (reference: configs/peteish{1,7,13}-{weka,google,
+# s3}.yaml, which differ from one another only in storage roots).  One file per size here; the storage root comes from
+# OLMO_DATA_GLOB / OLMO_REMOTE_SAVE_FOLDER instead of a file per storage system.
+for _size, _official, _extra in (
+    ("1", "OLMo2-1B-stage1", {"device_train_microbatch_size": 4, "fsdp": {"sharding_strategy": "SHARD_GRAD_OP", "wrapping_strategy": "by_block_and_size", "precision": "mixed"}}),
+    ("7", "OLMo2-7B-stage1", {"activation_checkpointing": "one_in_four"}),
+    ("13", "OLMo2-13B-stage1", {}),
+):
+    RECIPES[f"peteish{_size}"] = {
+        **deepcopy(RECIPES[_official]), "file": f"peteish{_size}.yaml",
+        "wandb": {"name": "${run_name}", "project": "olmo-medium" if _size != "1" else "olmo-small", "group": "${run_name}"},
+        "save_num_checkpoints_to_keep": -1, "save_interval_unsharded": None,
+        "remote_save_folder": "${oc.env:OLMO_REMOTE_SAVE_FOLDER,null}", **_extra,
+    }
+
+# Mid-training anneal from a stage-1 checkpoint: linear decay to zero over 50B tokens, data position not restored
+# (reference: configs/annealing/*.yaml; ``scripts/anneal_config_maker.py`` derives these from a checkpoint's own config).
+RECIPES["OLMo2-7B-anneal-example"] = {
+    **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": "annealing/OLMo2-7B-anneal-example.yaml",
+}
+
+# Training on a user-supplied ``torch.utils.data.Dataset`` instead of token memmaps (reference:
+# configs/custom_dataset_example.yaml): ``name`` is ``module.Class`` (or a class name plus ``module``), ``args`` its
+# constructor arguments, ``collate_config`` maps the dataset's field names onto the batch keys the trainer reads.
+RECIPES["custom-dataset-example"] = {
+    **deepcopy(RECIPES["OLMo-20M"]), "file": "custom_dataset_example.yaml", "evaluators": [],
+    "data": {
+        "paths": None, "num_workers": 0, "prefetch_factor": None, "persistent_workers": False,
+        "custom_dataset": {
+            "name": "my_package.my_module.MyDataset", "args": {"path": "/data/my-corpus", "sequence_length": 4096},
+            "collate_config": {"input_id_field": "token_ids", "label_mask_field": None, "metadata_field": None},
+        },
+    },
+}
+
 _COMMON: Dict[str, Any] = {
     "seed": 6198,
     "dry_run": False,
@@ -204,6 +239,8 @@ def recipe_dict(name: str) -> Dict[str, Any]:
     if out["model"]["vocab_size"] < 65536:
         out["data"]["memmap_dtype"] = "uint16"
     out["evaluators"] = [{"label": label, "type": "downstream"} for label in spec.pop("evaluators")]
+    if "data" in spec:
+        out["data"] = S.deep_merge(out["data"], spec.pop("data"))
     out.update(spec)
     return out
 

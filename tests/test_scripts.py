@@ -245,3 +245,63 @@ def test_anneal_config_maker_and_olmo_alias(tmp_path):
     import olmo_b200.optim
 
     assert AliasedConfig is TrainConfig and AliasedOLMo is olmo_b200.models.olmo.OLMo and olmo.optim is olmo_b200.optim
+
+
+def test_release_helper_stamps_and_extracts_notes(tmp_path):
+    mod = load_script("release")
+    changelog = tmp_path / "CHANGELOG.md"
+    changelog.write_text(
+        "# Changelog\n\n## Unreleased\n\n### Added\n\n- new thing\n\n### Fixed\n\n- a bug\n\n## [v0.1.0] - 2024-01-01\n\n### Changed\n\n- old change\n")
+    assert mod.stamp(changelog, "0.2.0", today="2024-02-02") is True
+    assert mod.stamp(changelog, "0.2.0") is False  # idempotent
+    text = changelog.read_text()
+    assert text.index("## Unreleased") < text.index("## [v0.2.0] - 2024-02-02") < text.index("### Added") < text.index("## [v0.1.0]")
+    notes = mod.notes(changelog, "v0.2.0")
+    assert notes.startswith("## What's new") and "### Added 🎉" in notes and "### Fixed ✅" in notes and "- a bug" in notes
+    assert "old change" not in notes
+    assert "### Changed ⚠️" in mod.notes(changelog, "v0.1.0")
+    with pytest.raises(RuntimeError):
+        mod.notes(changelog, "v9.9.9")
+    # the repository's own changelog parses and can be stamped with the package version
+    copy = tmp_path / "repo-changelog.md"
+    copy.write_text((ROOT / "CHANGELOG.md").read_text())
+    assert mod.stamp(copy, mod.package_version()) is True
+    assert "- " in mod.notes(copy, f"v{mod.package_version()}")
+
+
+def test_add_code_eval_writes_ppl_documents(tmp_path, monkeypatch):
+    datasets = pytest.importorskip("datasets")
+    rows = [{"task_id": f"T/{i}", "prompt": f"def f{i}():\n", "canonical_solution": f"    return {i}\n", "entry_point": f"f{i}"} for i in range(3)]
+    datasets.Dataset.from_list(rows).save_to_disk(str(tmp_path / "hf_datasets" / "openai_humaneval" / "none" / "test"))
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+    mod = load_script("add_code_eval")
+    assert mod.main([str(tmp_path / "out"), "--dataset", "openai_humaneval", "--split", "test"]) == 0
+    with gzip.open(tmp_path / "out" / "openai_humaneval_test.jsonl.gz", "rt") as f:
+        docs = [json.loads(line) for line in f]
+    assert [d["id"] for d in docs] == ["T/0", "T/1", "T/2"]
+    assert docs[1]["text"] == "def f1():\n    return 1\n" and docs[1]["metadata"] == {"entry_point": "f1"}
+    # the files feed the offline pipeline's perplexity task
+    from olmo_b200.eval.offline import construct_task
+
+    class Tok:
+        eos_token_id = 0
+
+        def encode(self, s, add_special_tokens=False):
+            return [1 + (ord(c) % 50) for c in s]
+
+    task = construct_task("ppl", Tok(), {"files": [str(tmp_path / "out" / "openai_humaneval_test.jsonl.gz")]})
+    assert [text for _, text in task.documents(Tok())] == [d["text"] for d in docs]
+
+
+def test_flops_figure_renders_an_svg(tmp_path):
+    mod = load_script("flops_by_perf_figure")
+    flops = mod.training_flops("OLMo2-1B-stage1", 4e12)
+    assert 2.5e22 < flops < 6e22  # about 6·N·D for 1.5 B parameters and 4 T tokens, attention on top
+    points = tmp_path / "points.csv"
+    points.write_text("model,flops,score,group\nA-1B,OLMo2-1B-stage1:4e12,43.5,ours\nB-7B,1.8e23,61.0,ours\nC,9e22,55.2,others\n")
+    assert mod.main([str(points), str(tmp_path / "fig.svg"), "--title", "FLOPs vs score"]) == 0
+    svg = (tmp_path / "fig.svg").read_text()
+    assert svg.startswith("<svg") and svg.count("<circle") == 3 + 2 and "A-1B" in svg and "others" in svg and "10^23" in svg
+    import xml.dom.minidom
+
+    xml.dom.minidom.parseString(svg)  # well-formed
