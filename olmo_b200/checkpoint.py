@@ -268,7 +268,7 @@ class FullCheckpointer(Checkpointer):
             optim_state["state"] = {id_to_name[i]: s for i, s in optim_state["state"].items()}
         else:
             for g in groups:
-                g["param_names"] = g["params"] = [n.replace("_fsdp_wrapped_module.", "") for n in g["param_names"]]
+                g["param_names"] = g["params"] = [n.replace("_fsdp_wrapped_module.", "") for n in g.get("param_names", g["params"])]
             optim_state["state"] = {k.replace("_fsdp_wrapped_module.", ""): s for k, s in optim_state["state"].items()}
         for old, news in renames.items():
             if old in news and len(news) == 1:
@@ -491,6 +491,8 @@ class FlatShardCheckpointer(Checkpointer):
     ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
         """Reassemble full tensors offline (no process group needed): shard files are read by a thread pool, full
         buffers start as NaN and are verified finite after the copy so a missing shard cannot go unnoticed."""
+        if is_torch_dcp_checkpoint(load_path):
+            return unshard_torch_dcp_checkpoint(load_path, load_optimizer_state=load_optimizer_state, load_trainer_state=load_trainer_state)
         meta = self._read_meta(load_path, local_cache)
         sw = meta["shard_world"]
         dev = "cpu" if device is None else str(device)
@@ -538,6 +540,72 @@ class FlatShardCheckpointer(Checkpointer):
             optim_state = {"state": state, "param_groups": optim_shards[0]["param_groups"]}
         trainer_state = load_state_dict(load_path, "train/rank0.pt", local_cache=local_cache) if load_trainer_state else None
         return model_state, optim_state, trainer_state
+
+
+def is_torch_dcp_checkpoint(load_path: PathOrStr) -> bool:
+    """True for the layout the reference's ``torch_new`` sharded checkpointer writes: a ``model_and_optim/`` folder
+    in ``torch.distributed.checkpoint`` format (``olmo/checkpoint.py:99-144``, ``:892-966``)."""
+    if is_url(load_path):
+        return False
+    return (Path(load_path) / "model_and_optim" / ".metadata").is_file()
+
+
+def unshard_torch_dcp_checkpoint(
+    load_path: PathOrStr, *, load_optimizer_state: bool = True, load_trainer_state: bool = True
+) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
+    """Read a sharded checkpoint written by the reference's ``torch_new`` checkpointer (model and optimizer as FSDP
+    sharded state dicts under ``model_and_optim/``, trainer state under ``train/rank*.pt``) into full tensors, in one
+    CPU process.  The chunk layout is whatever the writing job's world size produced; the checkpoint library's reader
+    reassembles whole tensors from the chunk table, so no process group is needed.  Optimizer state comes back keyed
+    by parameter name, which ``FullCheckpointer`` accepts on restore."""
+    from torch.distributed.checkpoint import FileSystemReader
+    from torch.distributed.checkpoint.metadata import BytesStorageMetadata, TensorStorageMetadata
+    from torch.distributed.checkpoint.state_dict_loader import _load_state_dict
+
+    folder = Path(load_path) / "model_and_optim"
+    reader = FileSystemReader(str(folder))
+    table = reader.read_metadata().state_dict_metadata
+    wanted: Dict[str, Any] = {}
+    for key, entry in table.items():
+        if not (key.startswith("model.") or load_optimizer_state):
+            continue
+        if isinstance(entry, TensorStorageMetadata):
+            wanted[key] = torch.empty(entry.size, dtype=entry.properties.dtype)
+        elif isinstance(entry, BytesStorageMetadata):
+            wanted[key] = io.BytesIO()  # replaced by the unpickled object on load
+    _load_state_dict(wanted, storage_reader=reader, no_dist=True)
+
+    model_state: Dict[str, torch.Tensor] = {}
+    optim_state: Optional[Dict[str, Any]] = {"state": {}, "param_groups": []} if load_optimizer_state else None
+    flat_groups: Dict[int, Dict[str, Any]] = {}
+    for key, value in wanted.items():
+        if key.startswith("model."):
+            model_state[key[len("model.") :].replace("_fsdp_wrapped_module.", "")] = value
+        elif optim_state is not None and key.startswith("optim.state."):
+            # "optim.state.<parameter name>.<state key>": the state key has no dot, the parameter name does
+            name, _, state_key = key[len("optim.state.") :].rpartition(".")
+            optim_state["state"].setdefault(name.replace("_fsdp_wrapped_module.", ""), {})[state_key] = value
+        elif optim_state is not None and key == "optim.param_groups":  # stored as one pickled list
+            optim_state["param_groups"] = value
+        elif optim_state is not None and key.startswith("optim.param_groups."):  # or one entry per group and field
+            index, _, field_name = key[len("optim.param_groups.") :].partition(".")
+            flat_groups.setdefault(int(index), {})[field_name] = value
+    if not model_state:
+        raise OLMoCheckpointError(f"no model tensors found in {folder}")
+    if optim_state is not None and flat_groups:
+        optim_state["param_groups"] = [flat_groups[i] for i in sorted(flat_groups)]
+    if optim_state is not None:
+        for group in optim_state["param_groups"]:
+            if isinstance(group, dict) and "params" in group:
+                group["params"] = [str(n).replace("_fsdp_wrapped_module.", "") for n in group["params"]]
+
+    trainer_state = None
+    if load_trainer_state:
+        for candidate in ("train/rank0.pt", "train.pt"):
+            if (Path(load_path) / candidate).is_file():
+                trainer_state = torch.load(Path(load_path) / candidate, map_location="cpu", weights_only=False)
+                break
+    return model_state, optim_state, trainer_state
 
 
 class TorchNewStyleShardedCheckpointer(FlatShardCheckpointer):

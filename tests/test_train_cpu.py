@@ -128,3 +128,58 @@ def test_trainer_eval_runs_a_downstream_task(tmp_path, monkeypatch):
     monkeypatch.setattr(evaluator, "compute_metrics", lambda: seen.append(len(evaluator.eval_metric.scores)) or {})
     trainer.eval()
     assert seen == [4]
+
+
+def test_sharded_checkpoint_of_the_reference_layout_is_unsharded_offline(tmp_path):
+    """A ``model_and_optim/`` folder in torch's distributed-checkpoint format plus ``train/rank0.pt`` (what the
+    reference's ``torch_new`` sharded checkpointer writes, ``olmo/checkpoint.py:99-144,892-966``) becomes an unsharded
+    checkpoint that a trainer restores, optimizer moments included."""
+    import importlib.util
+
+    import torch.distributed.checkpoint as dcp
+
+    from olmo_b200.checkpoint import is_torch_dcp_checkpoint
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "a")
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    batches = iter(trainer.train_loader)
+    for _ in range(3):
+        trainer.global_step += 1
+        trainer.global_train_examples_seen_this_epoch += cfg.global_train_batch_size
+        trainer.global_train_tokens_seen += cfg.global_train_batch_size * cfg.model.max_sequence_length
+        trainer.train_step(next(batches))
+    named = list(trainer.dist_model.engine.named_parameters_for_optimizer())
+    model_state = {n: p.detach().clone() for n, p in named}
+    optim_state = {
+        "state": {n: {k: v.detach().clone() for k, v in trainer.optim.state[p].items()} for n, p in named},
+        "param_groups": [{**{k: v for k, v in g.items() if k not in ("params", "param_names")}, "params": list(g["param_names"])} for g in trainer.optim.param_groups],
+    }
+    src = tmp_path / "step3"
+    (src / "train").mkdir(parents=True)
+    # the writer flattens nested mappings into dotted keys, exactly as it does for sharded state dicts
+    dcp.save({"model": model_state, "optim": optim_state}, storage_writer=dcp.FileSystemWriter(str(src / "model_and_optim")), no_dist=True)
+    torch.save(trainer.trainer_state_dict(), src / "train" / "rank0.pt")
+    cfg.save(src / "config.yaml")
+    assert is_torch_dcp_checkpoint(src) and not is_torch_dcp_checkpoint(tmp_path)
+
+    spec = importlib.util.spec_from_file_location("unshard_script", str(__import__("pathlib").Path(__file__).resolve().parent.parent / "scripts" / "unshard.py"))
+    unshard = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(unshard)
+    from olmo_b200.config import ShardedCheckpointerType
+
+    out = tmp_path / "step3-unsharded"
+    unshard.main(src, out, ShardedCheckpointerType.torch_new)
+    loaded = torch.load(out / "model.pt", map_location="cpu")
+    assert set(loaded) == set(model_state) and all(torch.equal(loaded[n], model_state[n]) for n in loaded)
+
+    cfg2 = tiny_train_config(tmp_path / "b")
+    t2 = build_trainer(cfg2, device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+    t2.restore_checkpoint(str(out))
+    assert t2.global_step == 3
+    for n, p in t2.dist_model.engine.named_parameters_for_optimizer():
+        assert torch.equal(p.detach(), model_state[n]), n
+        assert torch.allclose(t2.optim.state[p]["exp_avg_sq"], optim_state["state"][n]["exp_avg_sq"]), n
+    expect = trainer.train_step(next(batches))["train/CrossEntropyLoss"]
+    again = t2.train_step(next(iter(t2.train_loader)))["train/CrossEntropyLoss"]
+    assert abs(again - expect) < 1e-5
