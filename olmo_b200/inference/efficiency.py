@@ -85,6 +85,7 @@ def load_quantized(quantized_dir: str, device: str = "cpu"):
     cfg.init_device = "cpu"
     model = OLMo(cfg, init_params=False)
     for block in model.all_blocks():
+        block._fused_ok = False  # packed weights: module path only
         for name in BLOCK_LINEARS:
             old = getattr(block, name, None)
             if isinstance(old, torch.nn.Linear):

@@ -137,6 +137,9 @@ def quantize_model(
                     kept_in[name].append(x[:256].clone())
             return hook
 
+        # a block with packed 4-bit linears runs through its modules, never through the fused training kernels
+        # (which read dense weights), and the statistics hooks below only fire on the module path
+        block._fused_ok = False
         hooks = [getattr(block, n).register_forward_pre_hook(make_hook(n)) for n in names]
         for x, kw in states:
             block(x, **kw)

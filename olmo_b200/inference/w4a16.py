@@ -122,10 +122,15 @@ class QuantLinear(nn.Module):
                       "ob_gather_columns_bf16")
                 xb = gathered
             m = xb.shape[0]
-            if m <= 8:
+            if m <= 64:
+                # decode-sized inputs: the matrix-vector kernel takes up to 8 rows per launch and reads the packed
+                # weights once per launch (0.5 byte per weight), so up to 64 rows cost less traffic than
+                # reconstructing the matrix (2.5 bytes per weight) and multiplying it (2 more)
                 y = torch.empty(m, self.out_features, dtype=torch.bfloat16, device=x.device)
-                check(lib().ob_w4a16_gemv(ptr(xb), ptr(self.qweight), ptr(self.scales), ptr(self.zeros), ptr(y), m, self.out_features,
-                                          self.in_features, self.group, stream_ptr()), "ob_w4a16_gemv")
+                for lo in range(0, m, 8):
+                    rows = min(8, m - lo)
+                    check(lib().ob_w4a16_gemv(ptr(xb[lo:]), ptr(self.qweight), ptr(self.scales), ptr(self.zeros), ptr(y[lo:]), rows,
+                                              self.out_features, self.in_features, self.group, stream_ptr()), "ob_w4a16_gemv")
             else:
                 y = k.gemm(xb, self.dequantize())
             y = y.to(x.dtype)

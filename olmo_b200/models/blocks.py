@@ -34,6 +34,7 @@ from .layers import (
 )
 
 __all__ = [
+    "StaticKV",
     "OLMoBlock",
     "OLMoSequentialBlock",
     "OLMoLlamaBlock",
@@ -43,6 +44,21 @@ __all__ = [
 ]
 
 KV = Tuple[torch.Tensor, torch.Tensor]
+
+
+class StaticKV:
+    """Preallocated key/value window of one block for fixed-shape (graph-capturable) decoding.
+
+    ``k`` and ``v`` are ``[rows, kv_heads, window, head_dim]``.  Keys are stored *after* the rotary embedding, rotated
+    by their token's index in its own sequence (``rope_pos``: int64 ``[rows]``, the index of the token being decoded),
+    so a row's place in the window carries no meaning and rows may be shifted inside it without touching values.
+    ``pos`` is a one-element int64 tensor on the device (the column the new token is written to), ``length`` the
+    number of leading columns the attention reads (a Python int: one captured graph per distinct value)."""
+
+    __slots__ = ("k", "v", "pos", "length", "rope_pos")
+
+    def __init__(self, k: torch.Tensor, v: torch.Tensor, pos: torch.Tensor, length: int, rope_pos: torch.Tensor):
+        self.k, self.v, self.pos, self.length, self.rope_pos = k, v, pos, length, rope_pos
 
 
 def activation_checkpoint_function(cfg: ModelConfig) -> Callable:
@@ -230,6 +246,8 @@ class OLMoBlock(nn.Module):
         q = q.view(B, T, cfg.n_heads, hd).transpose(1, 2)
         k = k.view(B, T, cfg.effective_n_kv_heads, hd).transpose(1, 2)
         v = v.view(B, T, cfg.effective_n_kv_heads, hd).transpose(1, 2)
+        if isinstance(layer_past, StaticKV):
+            return self.attn_out(self._static_window_attention(q, k, v, attention_bias, layer_past).transpose(1, 2).reshape(B, T, C)), None
         if layer_past is not None:
             past_k, past_v = layer_past
             k = torch.cat((past_k, k), dim=-2)
@@ -252,6 +270,31 @@ class OLMoBlock(nn.Module):
         )
         att = att.transpose(1, 2).contiguous().view(B, T, C)
         return self.attn_out(att), present
+
+    def _static_window_attention(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor], cache: StaticKV) -> torch.Tensor:
+        """One decode step against a :class:`StaticKV` window: rotate the new query/key by the write column, store
+        key and value there, attend over the first ``cache.length`` columns under the additive ``bias``
+        (``[rows, 1, 1, window]``: padding and not-yet-written columns carry the dtype's minimum).  Every shape is
+        fixed and the column arrives as a device tensor, so the step can be captured in a CUDA graph."""
+        cfg = self.config
+        assert q.shape[2] == 1 and bias is not None, "the static window decodes one token per row under an explicit bias"
+        if cfg.rope:
+            sin, cos = self.rotary_emb.get_rotary_embedding(cfg.max_sequence_length, q.device)
+            # one angle row per sequence: [rows, 1, 1, head_dim]
+            sin = sin[0, 0].index_select(0, cache.rope_pos)[:, None, None, :]
+            cos = cos[0, 0].index_select(0, cache.rope_pos)[:, None, None, :]
+            q_, k_ = (q.float(), k.float()) if cfg.rope_full_precision else (q, k)
+            with torch.autocast(q.device.type, enabled=False):
+                sin, cos = sin.type_as(q_), cos.type_as(q_)
+                q = self.rotary_emb.apply_rotary_pos_emb(sin, cos, q_).type_as(q)
+                k = self.rotary_emb.apply_rotary_pos_emb(sin, cos, k_).type_as(k)
+        cache.k.index_copy_(2, cache.pos, k.to(cache.k.dtype))
+        cache.v.index_copy_(2, cache.pos, v.to(cache.v.dtype))
+        n = cache.length
+        keys, values = cache.k[:, :, :n].to(q.dtype), cache.v[:, :, :n].to(q.dtype)
+        return F.scaled_dot_product_attention(
+            q, keys, values, attn_mask=bias[..., :n].to(q.dtype), enable_gqa=q.shape[1] != keys.shape[1]
+        )
 
     def forward(self, x, attention_bias=None, layer_past=None, use_cache=False, max_doc_len=None, cu_doc_lens=None):
         raise NotImplementedError

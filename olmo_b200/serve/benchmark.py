@@ -40,6 +40,9 @@ def main(argv=None) -> int:
     ap.add_argument("--dtype", choices=["bf16", "fp32"], default="bf16")
     ap.add_argument("--quantize", choices=["none", "rtn"], default="none")
     ap.add_argument("--device", default=None)
+    ap.add_argument("--kv-cache", choices=["auto", "static", "dynamic"], default="auto")
+    ap.add_argument("--window", type=int, default=None, help="static mode: columns per row (default: prompt + completion, rounded up)")
+    ap.add_argument("--no-graphs", action="store_true", help="static mode without CUDA graphs")
     args = ap.parse_args(argv)
 
     import torch
@@ -56,13 +59,14 @@ def main(argv=None) -> int:
         spec["n_layers"] = args.n_layers
     cfg = ModelConfig.new(**spec)
     torch.manual_seed(0)
-    model = OLMo(cfg).to(torch.bfloat16 if args.dtype == "bf16" else torch.float32)
+    model = OLMo(cfg).to(torch.bfloat16 if args.dtype == "bf16" else torch.float32).to(device).eval()
     if args.quantize == "rtn":
         from ..inference.quantize import quantize_model
 
-        quantize_model(model, [torch.full((1, 8), cfg.eos_token_id)], method="rtn")
-    model = model.to(device).eval()
-    engine = Engine(model, _IdTokenizer(), max_batch=args.max_batch, device=device)
+        quantize_model(model, [torch.full((1, 8), cfg.eos_token_id, device=device)], method="rtn")
+    window = args.window or min(cfg.max_sequence_length, -(-(args.prompt_len + args.max_tokens + 1) // 128) * 128)
+    engine = Engine(model, _IdTokenizer(), max_batch=args.max_batch, device=device, kv_cache=args.kv_cache, window=window,
+                    cuda_graphs=False if args.no_graphs else None)
     gen = torch.Generator().manual_seed(1)
     prompts = [torch.randint(2, cfg.vocab_size, (args.prompt_len,), generator=gen).tolist() for _ in range(args.requests)]
     params = SamplingParams(max_tokens=args.max_tokens, temperature=0.0, ignore_eos=True)
@@ -83,6 +87,8 @@ def main(argv=None) -> int:
         "metric": "generated_tokens_per_second", "value": generated / elapsed, "family": args.family, "n_layers": cfg.n_layers,
         "dtype": args.dtype, "quantize": args.quantize, "requests": args.requests, "max_batch": args.max_batch,
         "prompt_len": args.prompt_len, "max_tokens": args.max_tokens, "seconds": elapsed,
+        "kv_cache": "dynamic" if engine._static is None else "static", "cuda_graphs": bool(engine._static and engine._static.cuda_graphs),
+        "graph_replays": 0 if engine._static is None else engine._static.graph_replays,
         "ttft_median_s": ttft[len(ttft) // 2], "ttft_max_s": ttft[-1], **{k: int(v) for k, v in engine.stats.items()},
     }))
     return 0

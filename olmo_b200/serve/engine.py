@@ -6,7 +6,11 @@ for an OLMo-2 checkpoint (``scripts/olmo2_modal_openai.py``) and its efficiency 
 ``generate`` (``inference/efficiency/run_efficiency_benchmark.py:16-114``).  This module is the first-party equivalent:
 requests join and leave a running decode batch between steps.
 
-Layout of the running batch.  All rows share one key/value window of length ``L`` per block (``[rows, kv_heads, L,
+Two decode back ends.  The *static* one (``olmo_b200/serve/static_cache.py``: preallocated windows, fixed shapes, one
+CUDA graph per length bucket) is the default on a GPU for rotary models; the *dynamic* one below works for every
+architecture and on every device.
+
+Layout of the dynamic running batch.  All rows share one key/value window of length ``L`` per block (``[rows, kv_heads, L,
 head_dim]``, keys stored before the rotary embedding, as ``OLMo.forward`` returns them).  A row's tokens are
 right-aligned in the window and the columns to their left are masked out, so rows of different lengths decode
 together; rotary and ALiBi terms depend only on distances inside the window and are unaffected by the shift.  New
@@ -73,6 +77,7 @@ class GenerationRequest:
     _done: threading.Event = field(default_factory=threading.Event, repr=False)
     _generator: Optional[torch.Generator] = field(default=None, repr=False)
     _emitted: int = field(default=0, repr=False)  # characters of ``text`` already passed to ``on_token``
+    _row: int = field(default=-1, repr=False)  # row of the static key/value window, when that mode is on
 
     @property
     def finished(self) -> bool:
@@ -98,13 +103,31 @@ class Engine:
     """Owns the model and the running batch.  Thread-safe ``submit``; the batch itself is advanced either by the
     background thread (``start``) or by calling ``step`` / ``run_until_idle`` from one thread."""
 
-    def __init__(self, model, tokenizer, max_batch: int = 32, device: Optional[torch.device] = None):
+    def __init__(
+        self, model, tokenizer, max_batch: int = 32, device: Optional[torch.device] = None, kv_cache: str = "auto",
+        window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None,
+    ):
+        """``kv_cache``: ``"static"`` decodes against preallocated windows with fixed shapes (CUDA graphs on a GPU;
+        :mod:`olmo_b200.serve.static_cache`), ``"dynamic"`` concatenates caches through ``OLMo.forward``; ``"auto"``
+        picks static on a GPU when the architecture allows it.  ``window`` bounds prompt + completion per request in
+        static mode (default: the model's context length)."""
+        from .static_cache import StaticWindow, supports_static_window
+
         self.model = model.eval()
         self.tokenizer = tokenizer
         self.config = model.config
         self.device = device or next(model.parameters()).device
         # learned absolute positions do not survive the shift of a left-padded window: one row at a time then
         self.max_batch = max_batch if (self.config.rope or self.config.alibi) else 1
+        if kv_cache not in ("auto", "static", "dynamic"):
+            raise ValueError(f"kv_cache must be auto, static or dynamic, not {kv_cache!r}")
+        if kv_cache == "static" and not supports_static_window(self.config):
+            raise ValueError("the static key/value window needs rotary position embeddings and ungrouped blocks")
+        use_static = kv_cache == "static" or (kv_cache == "auto" and self.device.type == "cuda" and supports_static_window(self.config))
+        self._static: Optional[StaticWindow] = (
+            StaticWindow(self.model, self.max_batch, window=window, bucket=bucket, cuda_graphs=cuda_graphs) if use_static else None
+        )
+        self._active: Optional[torch.Tensor] = None  # rows of the static window in the order of ``_rows``
         self.eos_token_id = getattr(tokenizer, "eos_token_id", None)
         if self.eos_token_id is None:
             self.eos_token_id = self.config.eos_token_id
@@ -131,7 +154,7 @@ class Engine:
         params = params or SamplingParams()
         params.validate()
         prompt = list(prompt_ids) or [self.eos_token_id]
-        limit = self.config.max_sequence_length
+        limit = self.config.max_sequence_length if self._static is None else self._static.window
         if len(prompt) + 1 > limit:
             raise ContextLengthError(f"prompt of {len(prompt)} tokens leaves no room in a context of {limit}")
         request = GenerationRequest(next(self._ids), prompt, params, on_token)
@@ -197,6 +220,10 @@ class Engine:
             request.error, request.finish_reason = exc, "error"
             request.finished_at = time.monotonic()
             request._done.set()
+        if self._static is not None:
+            for request in self._rows:
+                self._static.release(request._row)
+            self._active = None
         self._rows, self._kv, self._mask, self._last = [], None, None, None
 
     @torch.no_grad()
@@ -231,6 +258,13 @@ class Engine:
         self.stats["requests"] += len(requests)
         kv = [(k, v) for k, v in out.attn_key_values]
         tokens = self._sample(requests, out.logits[:, -1, :])
+        if self._static is not None:
+            for request, row in zip(requests, self._static.admit(kv, mask, tokens)):
+                request._row = row
+            self._rows = self._rows + requests
+            self._active = None
+            self._retire()
+            return
         # merge into the running window
         if self._rows:
             assert self._kv is not None and self._mask is not None and self._last is not None
@@ -250,6 +284,16 @@ class Engine:
 
     # ----------------------------------------------------------------------------------- decode
     def _decode(self) -> None:
+        if self._static is not None:
+            if self._active is None:
+                self._active = torch.tensor([r._row for r in self._rows], device=self.device)
+            logits = self._static.decode(self._active)
+            tokens = self._sample(self._rows, logits.index_select(0, self._active))
+            self._static.advance(self._active, tokens)
+            self.stats["decode_tokens"] += len(self._rows)
+            self.stats["decode_steps"] += 1
+            self._retire()
+            return
         assert self._kv is not None and self._mask is not None and self._last is not None
         mask = torch.cat((self._mask, self._mask.new_ones(self._mask.shape[0], 1)), dim=1)
         out = self.model(
@@ -313,7 +357,8 @@ class Engine:
             if cut >= 0:
                 text, request.finish_reason = text[:cut], "stop"
             request.text = text
-            budget = min(params.max_tokens, self.config.max_sequence_length - len(request.prompt_ids))
+            context = self.config.max_sequence_length if self._static is None else self._static.window
+            budget = min(params.max_tokens, context - len(request.prompt_ids))
             if request.finish_reason is None and len(request.token_ids) >= budget:
                 request.finish_reason = "length"
         if request.on_token is not None:
@@ -334,6 +379,17 @@ class Engine:
         """Drop finished rows and trim the padding every remaining row shares."""
         keep = [i for i, r in enumerate(self._rows) if not r.finished]
         done = [r for r in self._rows if r.finished]
+        if self._static is not None:
+            if done:
+                now = time.monotonic()
+                for r in done:
+                    self._static.release(r._row)
+                    r.finished_at = now
+                    r._done.set()
+                self._rows = [self._rows[i] for i in keep]
+                self._active = None
+                self._static.compact()
+            return
         if done:
             now = time.monotonic()
             if keep:

@@ -231,31 +231,104 @@ def test_openai_routes():
 @pytest.mark.gpu
 def test_engine_on_gpu_with_native_attention_shapes():
     """The engine on the device: batched decoding with padding agrees with cache-free greedy decoding of each prompt,
-    for full-precision weights and for 4-bit weights (whose matrix-vector kernel serves the decode steps)."""
+    for both decode back ends (the static one replays CUDA graphs), with full-precision weights and with 4-bit weights
+    (whose matrix-vector kernel serves the decode steps)."""
     from olmo_b200.inference.quantize import quantize_model
 
     model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512).cuda()
+
+    def reference(prompt):
+        ids, out = list(prompt), []
+        with torch.no_grad():
+            for _ in range(10):
+                token = int(model(torch.tensor([ids], device="cuda")).logits[0, -1].argmax())
+                if token == EOS:
+                    break
+                ids.append(token)
+                out.append(token)
+        return out
+
     for quantized in (False, True):
         if quantized:
             quantize_model(model, [torch.full((1, 8), 5, device="cuda")], method="rtn", group=128)
-        engine = Engine(model, CharTokenizer(), max_batch=4)
-        done = engine.generate(PROMPTS, SamplingParams(max_tokens=10, temperature=0.0))
-        agree = total = 0
-        for prompt, request in zip(PROMPTS, done):
-            ids, out = list(prompt), []
-            with torch.no_grad():
-                for _ in range(10):
-                    token = int(model(torch.tensor([ids], device="cuda")).logits[0, -1].argmax())
-                    if token == EOS:
-                        break
-                    ids.append(token)
-                    out.append(token)
-            if quantized:  # bf16 rounding differs between the row counts: compare the first choice only
-                out, got = out[:1], request.token_ids[:1]
-            else:
+        expected = [reference(p) for p in PROMPTS]
+        for kv_cache in ("dynamic", "static"):
+            engine = Engine(model, CharTokenizer(), max_batch=4, kv_cache=kv_cache, bucket=16)
+            done = engine.generate(PROMPTS, SamplingParams(max_tokens=10, temperature=0.0))
+            if kv_cache == "static":
+                assert engine._static.cuda_graphs and engine._static.graph_replays == engine.stats["decode_steps"] > 0
+            agree = total = 0
+            for out, request in zip(expected, done):
                 got = request.token_ids
-            n = min(len(out), len(got))
-            agree += sum(a == b for a, b in zip(out[:n], got[:n]))
-            total += max(len(out), len(got))
-        # a near-tie may flip one argmax between the batched and the single-row kernels
-        assert agree >= 0.8 * total, (quantized, agree, total)
+                if quantized:  # bf16 rounding differs between the row counts: compare the first choice only
+                    out, got = out[:1], got[:1]
+                n = min(len(out), len(got))
+                agree += sum(a == b for a, b in zip(out[:n], got[:n]))
+                total += max(len(out), len(got))
+            # a near-tie may flip one argmax between the batched and the single-row kernels
+            assert agree >= 0.8 * total, (quantized, kv_cache, agree, total)
+
+
+@pytest.mark.parametrize("variant", [dict(), dict(n_kv_heads=2, attention_layer_norm=True, norm_after=True, rope_full_precision=False)])
+def test_static_window_matches_single_sequence_greedy(variant):
+    """Fixed-shape decoding: rows join mid-flight, long prompts push the window right, retired rows let it slide
+    back, and every request still equals cache-free greedy decoding of its own prompt."""
+    model = tiny_model(**variant)
+    engine = Engine(model, CharTokenizer(), max_batch=3, kv_cache="static", bucket=8)
+    window = engine._static
+    assert window is not None and window.window == 48 and window.kv_bytes() > 0
+    greedy = SamplingParams(max_tokens=12, temperature=0.0)
+    requests = [engine.submit(p, greedy) for p in PROMPTS[:2]]  # lengths 11 and 1
+    for _ in range(5):
+        engine.step()
+    requests.append(engine.submit(PROMPTS[2], greedy))  # 19 tokens: longer than the window's write column
+    engine.step()
+    assert window.cur >= len(PROMPTS[2])
+    requests += [engine.submit(p, greedy) for p in PROMPTS[3:]]
+    engine.run_until_idle()
+    for prompt, request in zip(PROMPTS, requests):
+        assert request.token_ids == greedy_reference(model, prompt, 12), prompt
+    assert window.free_rows == 3 and window.cur == 0
+
+    # a request that runs to the end of the window finishes by length; with neighbours retiring the window compacts
+    long_prompt = [66] * 30
+    capped = engine.submit(long_prompt, SamplingParams(max_tokens=100, temperature=0.0, ignore_eos=True))
+    short = engine.submit(PROMPTS[1], SamplingParams(max_tokens=30, temperature=0.0, ignore_eos=True))
+    engine.run_until_idle()
+    assert len(capped.token_ids) == 18 and capped.finish_reason == "length"
+    assert short.token_ids == greedy_reference_no_eos(model, PROMPTS[1], 30)
+    with pytest.raises(ContextLengthError):
+        engine.submit([65] * 48)
+
+
+def greedy_reference_no_eos(model, prompt, steps):
+    ids, out = list(prompt), []
+    with torch.no_grad():
+        for _ in range(steps):
+            token = int(model(torch.tensor([ids])).logits[0, -1].argmax())
+            ids.append(token)
+            out.append(token)
+    return out
+
+
+def test_static_window_slides_left_when_it_fills():
+    model = tiny_model()
+    engine = Engine(model, CharTokenizer(), max_batch=2, kv_cache="static", window=24, bucket=4)
+    window = engine._static
+    # a stream of short requests keeps the window busy far longer than its width
+    params = SamplingParams(max_tokens=9, temperature=0.0, ignore_eos=True)
+    requests = []
+    for i in range(8):
+        requests.append(engine.submit(PROMPTS[i % len(PROMPTS)][:6], params))
+        engine.step()
+        engine.step()
+    engine.run_until_idle()
+    for i, request in enumerate(requests):
+        assert request.token_ids == greedy_reference_no_eos(model, PROMPTS[i % len(PROMPTS)][:6], 9), i
+    assert engine.stats["decode_steps"] + 8 > window.window  # more columns were written than the window holds
+
+
+def test_static_window_is_refused_where_it_cannot_work():
+    with pytest.raises(ValueError):
+        Engine(tiny_model(alibi=True, rope=False), CharTokenizer(), kv_cache="static")
+    assert Engine(tiny_model(alibi=True, rope=False), CharTokenizer(), kv_cache="auto")._static is None
