@@ -6,7 +6,7 @@ __all__ = ["Engine", "SamplingParams", "GenerationRequest", "ContextLengthError"
 
 
 def load_engine(checkpoint_dir: str, device: str = "cuda", dtype: str = "bf16", quantize: str = "none", max_batch: int = 32,
-                tokenizer: str = ""):
+                tokenizer: str = "", kv_cache: str = "auto", window=None):
     """Engine over a native checkpoint directory (sharded or unsharded) or a directory written by the 4-bit
     quantisation driver; the tokenizer defaults to the one the checkpoint's config names."""
     import torch
@@ -29,4 +29,4 @@ def load_engine(checkpoint_dir: str, device: str = "cuda", dtype: str = "bf16", 
         model = model.to(device)
     tok = Tokenizer.from_file(tokenizer) if tokenizer and tokenizer.endswith(".json") else (
         Tokenizer.from_pretrained(tokenizer) if tokenizer else Tokenizer.from_checkpoint(checkpoint_dir))
-    return Engine(model, tok, max_batch=max_batch, device=torch.device(device))
+    return Engine(model, tok, max_batch=max_batch, device=torch.device(device), kv_cache=kv_cache, window=window)

@@ -26,6 +26,10 @@ def main(argv=None) -> int:
                     help="rtn: 4-bit round-to-nearest on load; load: the folder was written by the quantisation driver")
     ap.add_argument("--tokenizer", default="", help="tokenizer JSON file or identifier (default: from the checkpoint's config)")
     ap.add_argument("--max-batch", type=int, default=32, help="rows decoded together")
+    ap.add_argument("--kv-cache", choices=["auto", "static", "dynamic"], default="auto",
+                    help="static: preallocated key/value windows and CUDA graphs (default on a GPU for rotary models)")
+    ap.add_argument("--window", type=int, default=None,
+                    help="static mode: longest prompt + completion per request; sizes the key/value memory (default: the context length)")
     ap.add_argument("--api-key", default=None, help="require 'Authorization: Bearer KEY'")
     args = ap.parse_args(argv)
 
@@ -36,7 +40,7 @@ def main(argv=None) -> int:
 
     device = args.device or ("cuda" if torch.cuda.is_available() else "cpu")
     engine = load_engine(args.checkpoint_dir, device=device, dtype=args.dtype if device != "cpu" else "fp32", quantize=args.quantize,
-                         max_batch=args.max_batch, tokenizer=args.tokenizer)
+                         max_batch=args.max_batch, tokenizer=args.tokenizer, kv_cache=args.kv_cache, window=args.window)
     app = create_app(engine, model_name=args.model_name or Path(args.checkpoint_dir.rstrip("/")).name, api_key=args.api_key)
     uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     return 0

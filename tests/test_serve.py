@@ -332,3 +332,35 @@ def test_static_window_is_refused_where_it_cannot_work():
     with pytest.raises(ValueError):
         Engine(tiny_model(alibi=True, rope=False), CharTokenizer(), kv_cache="static")
     assert Engine(tiny_model(alibi=True, rope=False), CharTokenizer(), kv_cache="auto")._static is None
+
+
+def test_load_engine_from_a_checkpoint_folder(tmp_path):
+    """``load_engine`` (what ``scripts/serve_openai.py`` calls): model, tokenizer and engine from an unsharded checkpoint."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    from olmo_b200.config import TokenizerConfig, TrainConfig
+    from olmo_b200.serve import load_engine
+
+    words = [f"w{i}" for i in range(60)]
+    vocab = {w: i + 2 for i, w in enumerate(words)}
+    vocab["<pad>"], vocab["<eos>"] = 0, 1
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="<pad>"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.add_special_tokens(["<eos>", "<pad>"])
+    tok.save(str(tmp_path / "tokenizer.json"))
+
+    model = tiny_model(vocab_size=62, embedding_size=64)
+    ckpt = tmp_path / "step0-unsharded"
+    ckpt.mkdir()
+    torch.save(model.state_dict(), ckpt / "model.pt")
+    cfg = TrainConfig(model=model.config, tokenizer=TokenizerConfig(identifier=str(tmp_path / "tokenizer.json")))
+    cfg.save(ckpt / "config.yaml")
+
+    engine = load_engine(str(ckpt), device="cpu", dtype="fp32", max_batch=2, kv_cache="static", window=32)
+    prompt = engine.tokenizer.encode("w1 w2 w3 w4", add_special_tokens=False)
+    assert prompt == [3, 4, 5, 6]
+    done = engine.generate([prompt], SamplingParams(max_tokens=6, temperature=0.0))[0]
+    assert done.token_ids == greedy_reference(model, prompt, 6)
+    assert done.text == engine.tokenizer.decode(done.token_ids)
