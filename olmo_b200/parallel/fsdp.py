@@ -53,7 +53,7 @@ from ..config import (
 from ..exceptions import OLMoConfigurationError
 from ..models.blocks import OLMoBlock, should_checkpoint_block
 from ..models.olmo import OLMo, OLMoOutput
-from ..torch_util import get_global_rank, get_world_size, is_distributed
+from ..torch_util import get_global_rank, get_world_size, is_distributed, nvtx_range
 
 __all__ = ["FlatShardEngine", "ShardedModel", "Unit", "ParamSlot", "build_sharded_model"]
 
@@ -662,12 +662,13 @@ class FlatShardEngine:
                 need(self._unit_of_module_param(block.att_proj.weight))
             gk = prefetch_kwargs() if gather_queue else None
             w = self._weights_of(block)
-            if should_checkpoint_block(ac_strategy, i):
-                y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk, doc_start=doc_start)
-                saved_list.append(("ckpt", x))
-            else:
-                y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start)
-                saved_list.append(("full", saved))
+            with nvtx_range(f"fwd_block_{i}"):
+                if should_checkpoint_block(ac_strategy, i):
+                    y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk, doc_start=doc_start)
+                    saved_list.append(("ckpt", x))
+                else:
+                    y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start)
+                    saved_list.append(("full", saved))
             x = y
         while gather_queue:
             need(gather_queue[0])
@@ -675,12 +676,13 @@ class FlatShardEngine:
         xn, rstd_f, mean_f = k.norm_fwd(x, ln_f.weight, None, mcfg.layer_norm_eps, spec.rms)
         head = t.wte.weight if mcfg.weight_tying else t.ff_out.weight
         flat_labels = labels.reshape(-1)
-        ce_sum, z_sum, dxn = lm_head_loss(
-            xn, head, flat_labels, z_mult=z_mult, grad_scale=1.0 / loss_divisor,
-            logit_scale=(1.0 / math.sqrt(mcfg.d_model)) if mcfg.scale_logits else 1.0,
-            chunk_rows=int(os.environ.get("OLMO_B200_HEAD_CHUNK", "8192")),
-            wgrad=lambda dl, xc: self.matrix_grad(head, dl, xc),
-        )
+        with nvtx_range("lm_head_loss"):
+            ce_sum, z_sum, dxn = lm_head_loss(
+                xn, head, flat_labels, z_mult=z_mult, grad_scale=1.0 / loss_divisor,
+                logit_scale=(1.0 / math.sqrt(mcfg.d_model)) if mcfg.scale_logits else 1.0,
+                chunk_rows=int(os.environ.get("OLMO_B200_HEAD_CHUNK", "8192")),
+                wgrad=lambda dl, xc: self.matrix_grad(head, dl, xc),
+            )
         del xn
         dx = k.norm_bwd(dxn, x, ln_f.weight, rstd_f, mean_f, spec.rms,
                         dweight=None if ln_f.weight is None else self.vector_grad(ln_f.weight))
@@ -717,8 +719,9 @@ class FlatShardEngine:
             w = self._weights_of(block)
             if kind == "ckpt":
                 _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start)
-            dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block),
-                                   gemm_kwargs=reduce_kwargs() if reduce_now else None)
+            with nvtx_range(f"bwd_block_{i}"):
+                dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block),
+                                       gemm_kwargs=reduce_kwargs() if reduce_now else None)
             del payload
             if reduce_now:
                 publish(i)

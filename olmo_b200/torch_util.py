@@ -17,6 +17,7 @@ import torch.distributed as dist
 T = TypeVar("T")
 
 __all__ = [
+    "nvtx_range",
     "seed_all",
     "is_distributed",
     "get_node_rank",
@@ -187,3 +188,28 @@ class SingleAccelerator(torch.nn.Module):
 
     def forward(self, *args: Any, **kwargs: Any):
         return self.module(*args, **kwargs)
+
+
+class nvtx_range:
+    """``with nvtx_range("name"):`` marks a span for timeline profilers when ``OLMO_B200_NVTX=1`` and the process has a
+    GPU; otherwise it does nothing (no import, no call into the driver)."""
+
+    _enabled: Optional[bool] = None
+
+    def __init__(self, name: str):
+        self.name = name
+
+    @classmethod
+    def enabled(cls) -> bool:
+        if cls._enabled is None:
+            cls._enabled = os.environ.get("OLMO_B200_NVTX", "0").strip().lower() in ("1", "true", "yes", "on") and torch.cuda.is_available()
+        return cls._enabled
+
+    def __enter__(self) -> "nvtx_range":
+        if self.enabled():
+            torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc) -> None:
+        if self.enabled():
+            torch.cuda.nvtx.range_pop()

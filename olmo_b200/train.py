@@ -60,6 +60,7 @@ from .torch_util import (
     get_world_size,
     is_distributed,
     move_to_device,
+    nvtx_range,
     peak_gpu_memory,
     synchronize_flag,
     synchronize_value,
@@ -645,8 +646,10 @@ class Trainer:
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             ev0.record()
         self._zero_grad()
-        batch = self._stage_batch(batch)
-        ce_batch_loss, z_batch_loss = self.train_batch(batch)
+        with nvtx_range("stage_batch"):
+            batch = self._stage_batch(batch)
+        with nvtx_range("forward_backward"):
+            ce_batch_loss, z_batch_loss = self.train_batch(batch)
 
         if reduce_global_loss and is_distributed():
             dist.reduce(ce_batch_loss, 0)
@@ -656,15 +659,17 @@ class Trainer:
                 z_batch_loss.div_(get_world_size())
 
         collect = self.should_log_optim_metrics_this_step()
-        optim_metrics = self.optim.clip_grads_and_collect_metrics(
-            self.global_step, collect_param_metrics=collect, process_group=getattr(self.dist_model, "process_group", None),
-            device=self.device,
-        )
+        with nvtx_range("clip_grads"):
+            optim_metrics = self.optim.clip_grads_and_collect_metrics(
+                self.global_step, collect_param_metrics=collect, process_group=getattr(self.dist_model, "process_group", None),
+                device=self.device,
+            )
         for group in self.optim.param_groups:
             group["lr"] = self.scheduler.get_lr(self.cfg.optimizer.learning_rate, self.scheduler_current, self.scheduler_max)
             group["max_grad_norm"] = self.scheduler.get_max_grad_norm(self.cfg.max_grad_norm, self.scheduler_current, self.scheduler_max)
             group["max_grad_norm_ratio"] = self.scheduler.get_max_grad_norm(self.cfg.max_grad_norm_ratio, self.scheduler_current, self.scheduler_max)
-        self.optim.step()
+        with nvtx_range("optimizer_step"):
+            self.optim.step()
         if timed:
             ev1.record()
 
@@ -702,7 +707,7 @@ class Trainer:
 
     def eval_step(self, batch: Dict[str, Any], evaluator: Evaluator) -> None:
         batch = move_to_device(batch, self.device)
-        with torch.no_grad():
+        with torch.no_grad(), nvtx_range("eval_step"):
             ce_loss, logits = self.eval_batch(batch)
         evaluator.update_metrics(batch, ce_loss, logits)
         barrier()
