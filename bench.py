@@ -275,6 +275,7 @@ def run_ours(args) -> dict:
             "parallelism": (f"fsdp{world}" if args.sharding == "FULL_SHARD" else f"{args.sharding.lower()}{world}") if world > 1 else "single-gpu flat-shard engine",
             "activation_checkpointing": args.activation_checkpointing or "none",
             "optimizer": "adamw fp32 master, clip 1.0, z-loss on", "fused_path": bool(engine.fused),
+            "recomputable_activations": "kept" if getattr(engine, "keep_recomputable", False) else "recomputed in backward",
             "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
         },
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "checkpoint": checkpoint,

@@ -174,10 +174,13 @@ def block_forward(
     save: bool = True,
     gemm_kwargs: Optional[Dict[str, Dict[str, Any]]] = None,
     doc_start: Optional[torch.Tensor] = None,
+    keep_recomputable: bool = False,
 ) -> Tuple[torch.Tensor, Optional[Dict[str, Any]]]:
     """``x`` is ``[B·T, d]`` bf16.  ``w`` maps ``att_proj, attn_out, ff_proj, ff_out`` to weights and
     ``attn_norm, ff_norm, q_norm, k_norm`` to norm weights or ``None``.  ``gemm_kwargs[name]`` may carry the
-    readiness-flag arguments of a weight that is still arriving from peers."""
+    readiness-flag arguments of a weight that is still arriving from peers.  ``keep_recomputable`` also saves the
+    rotated q/k and the SwiGLU output, which the backward pass otherwise recomputes (two bandwidth-bound kernels per
+    block traded for ``(Wq + Wk + hidden/2)·2`` bytes per token)."""
     gk = gemm_kwargs or {}
     Wq, Wk, hd = spec.Wq, spec.Wk, spec.head_dim
     saved: Dict[str, Any] = {}
@@ -197,6 +200,7 @@ def block_forward(
     v = _split_heads(qk, Wq + Wk, Wk, B, T, hd) if spec.clip_qkv > 0 else _split_heads(qkv, Wq + Wk, Wk, B, T, hd)
     o, lse, backend = attn.attention_forward(q, kk, v, causal=True, doc_start=doc_start)
     o2 = o.view(B * T, Wq)
+    qk_keep = qk if (save and keep_recomputable) else None
     del qk, q, kk
 
     if spec.norm_after:
@@ -219,6 +223,8 @@ def block_forward(
     if not save:
         return y, None
     saved.update(x=x, qkv=qkv, rstd_q=rstd_q, rstd_k=rstd_k, o=o, lse=lse, x1=x1, h=h, B=B, T=T, attn_backend=backend, doc_start=doc_start)
+    if keep_recomputable:
+        saved.update(qk=qk_keep, act=act)
     return y, saved
 
 
@@ -253,7 +259,9 @@ def block_backward(
     else:
         d_f = dy
         dx1_res = dy
-    act = k.swiglu_fwd(h)  # recomputed
+    act = saved.pop("act", None)
+    if act is None:
+        act = k.swiglu_fwd(h)  # recomputed
     sink.matrix("ff_out", d_f, act)
     d_act = k.gemm(d_f, w["ff_out"], b_trans=True, **gk.get("ff_out_dgrad", {}))
     del act
@@ -278,9 +286,11 @@ def block_backward(
     sink.matrix("attn_out", d_a, o2)
     d_o = k.gemm(d_a, w["attn_out"], b_trans=True, **gk.get("attn_out_dgrad", {}))
 
-    qk, _, _ = k.qk_norm_rope_fwd(  # recomputed rotated q/k
-        qkv, _norm_w(w, "q_norm"), _norm_w(w, "k_norm"), cos, sin, T, Wq, Wk, hd, spec.eps, spec.clip_qkv, spec.qk_norm, spec.rope
-    )
+    qk = saved.pop("qk", None)
+    if qk is None:
+        qk, _, _ = k.qk_norm_rope_fwd(  # recomputed rotated q/k
+            qkv, _norm_w(w, "q_norm"), _norm_w(w, "k_norm"), cos, sin, T, Wq, Wk, hd, spec.eps, spec.clip_qkv, spec.qk_norm, spec.rope
+        )
     q = _split_heads(qk, 0, Wq, B, T, hd)
     kk = _split_heads(qk, Wq, Wk, B, T, hd)
     v = _split_heads(qk, Wq + Wk, Wk, B, T, hd) if spec.clip_qkv > 0 else _split_heads(qkv, Wq + Wk, Wk, B, T, hd)

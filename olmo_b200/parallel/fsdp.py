@@ -138,6 +138,10 @@ class FlatShardEngine:
             and model.config.block_group_size >= 1
         )
         self.reshard = os.environ.get("OLMO_B200_RESHARD", "0") not in ("0", "", "false")
+        # Keep the rotated q/k and the SwiGLU output of every block for the backward pass instead of recomputing them:
+        # "1"/"0" force it, "auto" decides after the first complete step from the memory that is still free.
+        keep = os.environ.get("OLMO_B200_KEEP_ACTS", "auto").strip().lower()
+        self.keep_recomputable: Optional[bool] = {"1": True, "true": True, "0": False, "false": False}.get(keep)
         self.units: List[Unit] = []
         self._unit_of_param: Dict[str, Tuple[Unit, ParamSlot]] = {}
         self._opt_params: List[Tuple[str, nn.Parameter]] = []
@@ -667,7 +671,8 @@ class FlatShardEngine:
                     y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk, doc_start=doc_start)
                     saved_list.append(("ckpt", x))
                 else:
-                    y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start)
+                    y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start,
+                                                keep_recomputable=bool(self.keep_recomputable))
                     saved_list.append(("full", saved))
             x = y
         while gather_queue:
@@ -718,7 +723,8 @@ class FlatShardEngine:
             block = blocks[i]
             w = self._weights_of(block)
             if kind == "ckpt":
-                _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start)
+                # recomputed right before its use: keeping q/k and the activation output costs nothing lasting
+                _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start, keep_recomputable=True)
             with nvtx_range(f"bwd_block_{i}"):
                 dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block),
                                        gemm_kwargs=reduce_kwargs() if reduce_now else None)
@@ -733,7 +739,24 @@ class FlatShardEngine:
                 comm.launch(comm.rs_task(u))
             ready.clear()
         self.note_microbatch_backward()
+        if self.keep_recomputable is None and is_last:
+            self._decide_keep_recomputable(M, spec, sum(1 for i in range(len(blocks)) if not should_checkpoint_block(ac_strategy, i)))
         return ce_sum / loss_divisor, z_sum * (z_mult / loss_divisor)
+
+    def _decide_keep_recomputable(self, tokens: int, spec, n_blocks: int) -> None:
+        """After the first full step the allocator has seen the step's peak, so the memory still free on the device is
+        what the extra saved activations may use.  They are kept when they fit with a margin (12 GiB, or a quarter of
+        the device if that is smaller)."""
+        hidden_half = self.model.config.ff_proj_width // 2
+        per_token = (spec.Wq + spec.Wk + (spec.Wk if spec.clip_qkv > 0 else 0) + hidden_half) * 2
+        extra = per_token * tokens * n_blocks
+        free, total = torch.cuda.mem_get_info(self.device)
+        margin = min(12 << 30, total // 4)
+        self.keep_recomputable = free > extra + margin
+        log.info(
+            "activations that the backward pass can recompute (%.1f GiB per micro-batch) will be %s: %.1f GiB free after the first step",
+            extra / 2**30, "kept" if self.keep_recomputable else "recomputed", free / 2**30,
+        )
 
     @torch.no_grad()
     def eval_loss(self, input_ids: torch.Tensor, labels: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
