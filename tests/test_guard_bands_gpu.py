@@ -55,10 +55,11 @@ def test_gemm_outputs_stay_inside(M, N, K):
     out.check(f"gemm NT {M}x{N}x{K}")
     torch.testing.assert_close(out.view.float(), a.float() @ b.float().t(), rtol=3e-2, atol=3e-1)
 
-    at, bt = _rand(K, M), _rand(K, N)
-    acc = Guarded((M, N), torch.float32, fill=torch.zeros(M, N, device="cuda"))
+    Mt = (M + 7) // 8 * 8  # the transposed operand is M-major: its row pitch must be a multiple of 16 bytes
+    at, bt = _rand(K, Mt), _rand(K, N)
+    acc = Guarded((Mt, N), torch.float32, fill=torch.zeros(Mt, N, device="cuda"))
     k.gemm(at, bt, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc.view)
-    acc.check(f"gemm TN accumulate {M}x{N}x{K}")
+    acc.check(f"gemm TN accumulate {Mt}x{N}x{K}")
     torch.testing.assert_close(acc.view, at.float().t() @ bt.float(), rtol=3e-2, atol=3e-1)
 
 
