@@ -225,6 +225,8 @@ def block_forward(
     saved.update(x=x, qkv=qkv, rstd_q=rstd_q, rstd_k=rstd_k, o=o, lse=lse, x1=x1, h=h, B=B, T=T, attn_backend=backend, doc_start=doc_start)
     if keep_recomputable:
         saved.update(qk=qk_keep, act=act)
+        if not spec.norm_after:  # pre-norm blocks also recompute the two normalised GEMM inputs
+            saved.update(h1=h_in, h2=h2)
     return y, saved
 
 
@@ -271,7 +273,9 @@ def block_backward(
         sink.matrix("ff_proj", d_h, x1)
         dx1 = k.gemm(d_h, w["ff_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1_res, **gk.get("ff_proj_dgrad", {}))
     else:
-        h2, _, _ = k.norm_fwd(x1, _norm_w(w, "ff_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
+        h2 = saved.pop("h2", None)
+        if h2 is None:
+            h2, _, _ = k.norm_fwd(x1, _norm_w(w, "ff_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
         sink.matrix("ff_proj", d_h, h2)
         del h2
         d_h2 = k.gemm(d_h, w["ff_proj"], b_trans=True, **gk.get("ff_proj_dgrad", {}))
@@ -311,7 +315,9 @@ def block_backward(
             assert "att_proj_dgrad" not in gk, "a collective was attached to a GEMM that is skipped"
             return None
         return k.gemm(dqkv, w["att_proj"], b_trans=True, epilogue=k.EPI_BF16_ADD, residual=dx1, **gk.get("att_proj_dgrad", {}))
-    h1, _, _ = k.norm_fwd(x, _norm_w(w, "attn_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
+    h1 = saved.pop("h1", None)
+    if h1 is None:
+        h1, _, _ = k.norm_fwd(x, _norm_w(w, "attn_norm"), None, spec.eps, spec.rms, save_stats=False)  # recomputed
     sink.matrix("att_proj", dqkv, h1)
     del h1
     d_h1 = k.gemm(dqkv, w["att_proj"], b_trans=True, **gk.get("att_proj_dgrad", {}))

@@ -749,6 +749,8 @@ class FlatShardEngine:
         the device if that is smaller)."""
         hidden_half = self.model.config.ff_proj_width // 2
         per_token = (spec.Wq + spec.Wk + (spec.Wk if spec.clip_qkv > 0 else 0) + hidden_half) * 2
+        if not spec.norm_after:
+            per_token += 2 * self.model.config.d_model * 2
         extra = per_token * tokens * n_blocks
         free, total = torch.cuda.mem_get_info(self.device)
         margin = min(12 << 30, total // 4)
