@@ -305,3 +305,15 @@ def test_flops_figure_renders_an_svg(tmp_path):
     import xml.dom.minidom
 
     xml.dom.minidom.parseString(svg)  # well-formed
+
+
+def test_ci_data_pipeline_smoke_command(tmp_path):
+    """The command the CI workflow runs on the committed fixtures."""
+    proc = subprocess.run(
+        [sys.executable, str(SCRIPTS / "prepare_memmap_dataset.py"), str(ROOT / "test_fixtures" / "sample-docs.json.gz"), "-o", str(tmp_path / "tokens"),
+         "--tokenizer", str(ROOT / "test_fixtures" / "word-tokenizer.json"), "--validate", "--ack-deprecated"],
+        capture_output=True, text=True, timeout=300,
+    )
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    files = list((tmp_path / "tokens").rglob("*.npy"))
+    assert files and sum(np.memmap(f, dtype=np.uint16, mode="r").shape[0] for f in files) == 2765 + 48  # words + one end token per document
