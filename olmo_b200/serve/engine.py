@@ -30,11 +30,15 @@ from typing import Callable, Deque, Dict, List, Optional, Sequence, Tuple
 import torch
 import torch.nn.functional as F
 
-__all__ = ["SamplingParams", "GenerationRequest", "Engine", "ContextLengthError"]
+__all__ = ["SamplingParams", "GenerationRequest", "Engine", "ContextLengthError", "QueueFullError"]
 
 
 class ContextLengthError(ValueError):
     """The prompt does not leave room for a single new token."""
+
+
+class QueueFullError(RuntimeError):
+    """More requests are waiting than the engine was told to hold."""
 
 
 @dataclass
@@ -78,6 +82,7 @@ class GenerationRequest:
     _generator: Optional[torch.Generator] = field(default=None, repr=False)
     _emitted: int = field(default=0, repr=False)  # characters of ``text`` already passed to ``on_token``
     _row: int = field(default=-1, repr=False)  # row of the static key/value window, when that mode is on
+    _cancelled: bool = field(default=False, repr=False)
 
     @property
     def finished(self) -> bool:
@@ -105,7 +110,7 @@ class Engine:
 
     def __init__(
         self, model, tokenizer, max_batch: int = 32, device: Optional[torch.device] = None, kv_cache: str = "auto",
-        window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None,
+        window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None, max_queue: int = 0,
     ):
         """``kv_cache``: ``"static"`` decodes against preallocated windows with fixed shapes (CUDA graphs on a GPU;
         :mod:`olmo_b200.serve.static_cache`), ``"dynamic"`` concatenates caches through ``OLMo.forward``; ``"auto"``
@@ -128,6 +133,7 @@ class Engine:
             StaticWindow(self.model, self.max_batch, window=window, bucket=bucket, cuda_graphs=cuda_graphs) if use_static else None
         )
         self._active: Optional[torch.Tensor] = None  # rows of the static window in the order of ``_rows``
+        self.max_queue = max_queue  # 0 = unbounded; otherwise ``submit`` refuses when that many requests wait
         self.eos_token_id = getattr(tokenizer, "eos_token_id", None)
         if self.eos_token_id is None:
             self.eos_token_id = self.config.eos_token_id
@@ -161,9 +167,23 @@ class Engine:
         if params.seed is not None:
             request._generator = torch.Generator(device="cpu").manual_seed(int(params.seed))
         with self._wake:
+            if self.max_queue and len(self._queue) >= self.max_queue:
+                raise QueueFullError(f"{len(self._queue)} requests are already waiting")
             self._queue.append(request)
             self._wake.notify()
         return request
+
+    def cancel(self, request: GenerationRequest) -> None:
+        """Stop generating for ``request`` (a client went away).  A waiting request leaves the queue at once; a
+        running one is marked and gives its row back at the next step boundary."""
+        with self._wake:
+            if request in self._queue:
+                self._queue.remove(request)
+                request.finish_reason = "cancelled"
+                request.finished_at = time.monotonic()
+                request._done.set()
+                return
+        request._cancelled = True
 
     def generate(self, prompts: Sequence[Sequence[int]], params=None) -> List[GenerationRequest]:
         """Synchronous convenience: submit, then advance the batch (or wait for the background thread)."""
@@ -346,7 +366,9 @@ class Engine:
 
     def _record(self, request: GenerationRequest, token: int, logprob: Optional[float]) -> None:
         params = request.params
-        if (token == self.eos_token_id and not params.ignore_eos) or token in params.stop_token_ids:
+        if request._cancelled:
+            request.finish_reason = "cancelled"
+        elif (token == self.eos_token_id and not params.ignore_eos) or token in params.stop_token_ids:
             request.finish_reason = "stop"
         else:
             request.token_ids.append(token)

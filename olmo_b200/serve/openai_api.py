@@ -12,7 +12,7 @@ import time
 import uuid
 from typing import Any, AsyncIterator, Callable, Dict, List, Optional, Sequence, Tuple
 
-from .engine import ContextLengthError, Engine, GenerationRequest, SamplingParams
+from .engine import ContextLengthError, Engine, GenerationRequest, QueueFullError, SamplingParams
 
 __all__ = ["create_app", "default_chat_template"]
 
@@ -128,7 +128,13 @@ def create_app(
                     callback = None if sink is None else sink(len(requests))
                     requests.append(engine.submit(prompt, p, callback))
         except ContextLengthError as exc:
+            for r in requests:
+                engine.cancel(r)
             raise _BadRequest(str(exc), code="context_length_exceeded") from exc
+        except QueueFullError as exc:
+            for r in requests:
+                engine.cancel(r)
+            raise _BadRequest(f"the server is busy: {exc}", code="queue_full", status=429) from exc
         return requests
 
     async def wait_all(requests: List[GenerationRequest]) -> None:
@@ -151,13 +157,18 @@ def create_app(
         for chunk in first:
             yield f"data: {json.dumps(chunk)}\n\n".encode()
         open_choices = len(requests)
-        while open_choices:
-            index, delta, reason = await queue.get()
-            if reason is not None:
-                open_choices -= 1
-            if delta or reason is not None:
-                yield f"data: {json.dumps(frame(index, delta, reason))}\n\n".encode()
-        yield b"data: [DONE]\n\n"
+        try:
+            while open_choices:
+                index, delta, reason = await queue.get()
+                if reason is not None:
+                    open_choices -= 1
+                if delta or reason is not None:
+                    yield f"data: {json.dumps(frame(index, delta, reason))}\n\n".encode()
+            yield b"data: [DONE]\n\n"
+        finally:  # the client went away (the response generator was closed): free the rows
+            for r in requests:
+                if not r.finished:
+                    engine.cancel(r)
 
     def make_sink(queue: "asyncio.Queue", loop):
         def sink(index: int):

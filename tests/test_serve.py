@@ -364,3 +364,25 @@ def test_load_engine_from_a_checkpoint_folder(tmp_path):
     done = engine.generate([prompt], SamplingParams(max_tokens=6, temperature=0.0))[0]
     assert done.token_ids == greedy_reference(model, prompt, 6)
     assert done.text == engine.tokenizer.decode(done.token_ids)
+
+
+def test_cancellation_and_queue_limit():
+    from olmo_b200.serve import QueueFullError
+
+    model = tiny_model()
+    engine = Engine(model, CharTokenizer(), max_batch=1, max_queue=2)
+    long_run = SamplingParams(max_tokens=30, temperature=0.0, ignore_eos=True)
+    running = engine.submit(PROMPTS[0], long_run)
+    engine.step()  # prefill: the only row is taken
+    waiting = [engine.submit(PROMPTS[1], long_run), engine.submit(PROMPTS[2], long_run)]
+    with pytest.raises(QueueFullError):
+        engine.submit(PROMPTS[3], long_run)
+    engine.cancel(waiting[0])  # leaves the queue at once
+    assert waiting[0].finish_reason == "cancelled" and waiting[0]._done.is_set()
+    for _ in range(3):
+        engine.step()
+    engine.cancel(running)  # gives its row back at the next step
+    engine.step()
+    assert running.finish_reason == "cancelled" and 0 < len(running.token_ids) < 30
+    engine.run_until_idle()
+    assert waiting[1].finish_reason == "length" and waiting[1].token_ids == greedy_reference_no_eos(model, PROMPTS[2], 29)
