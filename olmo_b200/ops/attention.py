@@ -265,7 +265,7 @@ def varlen_attention(
     if q.is_cuda and q.dtype in (torch.bfloat16, torch.float16) and _requested_backend() != "math":
         from . import attention_native
 
-        if dropout_p == 0.0 and attention_native.supports(q[None], k[None], causal, dropout_p, True):
+        if _requested_backend() != "library" and attention_native.supports_varlen(q, k, causal, dropout_p):
             return attention_native.varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale)
         fn = library_fn
         if fn is None and _library() is not None:

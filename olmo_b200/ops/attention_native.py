@@ -97,5 +97,36 @@ def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float, doc_st
     check(rc, "ob_attention_bwd", kernels=3)
 
 
-def varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale):  # pragma: no cover - not reached while supports() is False for varlen
-    raise NotImplementedError
+def supports_varlen(q: torch.Tensor, k: torch.Tensor, causal: bool, dropout_p: float) -> bool:
+    """Packed sequences ``(total_tokens, H, D)``: covered (through the document-masking kernels) when the single long
+    row they form meets the kernel's shape rules and attention is causal."""
+    return causal and q.dim() == 3 and supports(q[None], k[None], causal, dropout_p, False) and supports_backward(q[None], k[None], causal)
+
+
+class _PackedAttention(torch.autograd.Function):
+    """Causal attention over one packed row with per-token document starts."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, doc_start, scale):
+        o, lse = forward(q, k, v, True, scale, doc_start=doc_start)
+        ctx.save_for_backward(q, k, v, o, lse, doc_start)
+        ctx.scale = scale
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, doc_start = ctx.saved_tensors
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        backward(do.contiguous(), q, k, v, o, lse, dq, dk, dv, True, ctx.scale, doc_start=doc_start)
+        return dq, dk, dv, None, None
+
+
+def varlen(q, k, v, cu_seqlens, max_seqlen, causal, scale):
+    """Intra-document causal attention over packed ``(total_tokens, H, D)`` tensors described by cumulative lengths:
+    the pack is one row of ``total_tokens`` positions whose queries see the keys of their own document only (the
+    kernels skip key tiles that lie wholly before a query tile's first document)."""
+    assert causal, "packed sequences are covered for causal attention"
+    total = q.shape[0]
+    scale = scale if scale is not None else 1.0 / (q.shape[-1] ** 0.5)
+    doc_start = doc_start_from_cu(cu_seqlens, 1, total)
+    return _PackedAttention.apply(q[None].contiguous(), k[None].contiguous(), v[None].contiguous(), doc_start, scale)[0]

@@ -354,3 +354,33 @@ def test_native_attention_document_masking(H, Hkv):
     from olmo_b200 import ops
 
     ops.check_status()
+
+
+@pytest.mark.parametrize("H,Hkv", [(2, 2), (4, 1)])
+def test_native_attention_packed_sequences(H, Hkv):
+    """Packed variable-length attention (cumulative document lengths over one token axis) through the public entry
+    point: the native document-masking kernels against the fp32 math path, forward and backward."""
+    from olmo_b200.ops import attention as A
+    from olmo_b200.ops import attention_native as N
+
+    total, D = 2048, 128
+    cu = torch.tensor([0, 300, 301, 1024, 1500, 2048], device="cuda", dtype=torch.int32)
+    q0, k0, v0 = _rand(total, H, D), _rand(total, Hkv, D), _rand(total, Hkv, D)
+    assert N.supports_varlen(q0, k0, True, 0.0)
+
+    def run(fn):
+        q, k, v = (t.clone().requires_grad_(True) for t in (q0, k0, v0))
+        out = fn(q, k, v)
+        out.backward(torch.ones_like(out) * 0.01)
+        return out, q.grad, k.grad, v.grad
+
+    got = run(lambda q, k, v: A.varlen_attention(q, k, v, cu, 724, causal=True))
+    want = run(lambda q, k, v: A._VarlenMath.apply(q, k, v, cu, True, 1.0 / math.sqrt(D)))
+    for g, w in zip(got, want):
+        _close(g, w, rtol=3e-2, atol=3e-2)
+    # a query never sees the previous document: changing document 0 leaves the outputs of document 2 untouched
+    q1, k1, v1 = q0.clone(), k0.clone(), v0.clone()
+    k1[:300] += 1.0
+    v1[:300] -= 1.0
+    out1 = A.varlen_attention(q1, k1, v1, cu, 724, causal=True)
+    assert torch.equal(out1[301:1024], got[0][301:1024].detach())
