@@ -137,3 +137,45 @@ def test_shipped_task_sets_name_known_tasks():
         assert task_set["name"] == file.stem and task_set["tasks"]
         for task in task_set["tasks"]:
             assert task["task_name"] == "ppl" or task["task_name"] in label_to_task_map, (file.name, task["task_name"])
+
+
+def test_run_eval_command_line_on_a_checkpoint_folder(tmp_path, monkeypatch):
+    """``evaluation/run_eval.py`` end to end: checkpoint folder -> model + tokenizer -> rows on disk."""
+    import importlib.util
+    from pathlib import Path
+
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    from olmo_b200.config import TokenizerConfig, TrainConfig
+
+    words = ["hello", "evaluation", "the", "cat", "sat", "on", "mat"]
+    vocab = {"<pad>": 0, **{w: i + 1 for i, w in enumerate(words)}, "<eos>": len(words) + 1}
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="<pad>"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.save(str(tmp_path / "tokenizer.json"))
+    torch.manual_seed(0)
+    cfg = ModelConfig(
+        d_model=32, n_heads=2, n_layers=1, mlp_hidden_size=64, activation_type=ActivationType.swiglu, rope=True,
+        layer_norm_type=LayerNormType.rms, include_bias=False, vocab_size=len(vocab), embedding_size=16, max_sequence_length=16,
+        eos_token_id=len(words) + 1, pad_token_id=0, weight_tying=False, init_device="cpu",
+    )
+    ckpt = tmp_path / "step0-unsharded"
+    ckpt.mkdir()
+    torch.save(OLMo(cfg).state_dict(), ckpt / "model.pt")
+    TrainConfig(model=cfg, tokenizer=TokenizerConfig(identifier=str(tmp_path / "tokenizer.json"))).save(ckpt / "config.yaml")
+    (tmp_path / "val.jsonl").write_text(json.dumps({"text": "the cat sat on the mat"}) + "\n" + json.dumps({"text": "hello evaluation"}) + "\n")
+    experiment = {
+        "models": [str(ckpt)],
+        "task_sets": [{"name": "ppl", "tasks": [{"task_name": "ppl", "task_kwargs": {"files": [str(tmp_path / "val.jsonl")]}}]}],
+    }
+    (tmp_path / "exp.yaml").write_text(yaml.safe_dump(experiment))
+    script = Path(__file__).resolve().parent.parent / "evaluation" / "run_eval.py"
+    spec = importlib.util.spec_from_file_location("run_eval_script", script)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    assert mod.main([str(tmp_path / "exp.yaml"), "--workspace", str(tmp_path / "ws"), "--output", str(tmp_path / "rows.jsonl"), "--device", "cpu"]) == 0
+    rows = [json.loads(l) for l in (tmp_path / "rows.jsonl").read_text().splitlines()]
+    assert len(rows) == 1 and rows[0]["num_instances"] == 2 and rows[0]["metric_ppl_token"] > 1.0
+    assert (tmp_path / "rows.tsv").is_file()
