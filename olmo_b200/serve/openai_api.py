@@ -1,7 +1,7 @@
 """
 OpenAI-compatible HTTP front end for :class:`olmo_b200.serve.engine.Engine`.
 
-Endpoints: ``GET /health``, ``GET /v1/models``, ``POST /v1/completions``, ``POST /v1/chat/completions`` (both with
+Endpoints: ``GET /health``, ``GET /metrics`` (Prometheus text), ``GET /v1/models``, ``POST /v1/completions``, ``POST /v1/chat/completions`` (both with
 ``stream: true`` as server-sent events).  This is the surface the reference reaches by deploying a third-party server
 for an OLMo-2 instruct checkpoint (``scripts/olmo2_modal_openai.py``: ``MODEL_NAME``, ``serve()``); here it runs on the
 framework's own model and scheduler.  An optional bearer token guards the ``/v1`` routes, as that deployment does.
@@ -180,6 +180,25 @@ def create_app(
     @app.get("/health")
     async def health():
         return {"status": "ok", **{k: int(v) for k, v in engine.stats.items()}}
+
+    @app.get("/metrics")
+    async def metrics():
+        """Prometheus text exposition of the engine's counters."""
+        from fastapi.responses import PlainTextResponse
+
+        with engine._lock:
+            waiting, running = len(engine._queue), len(engine._rows)
+        lines = []
+        for name, value, kind, text in [
+            ("olmo_requests_total", engine.stats["requests"], "counter", "requests admitted to the decode batch"),
+            ("olmo_prompt_tokens_total", engine.stats["prefill_tokens"], "counter", "prompt tokens processed"),
+            ("olmo_generated_tokens_total", engine.stats["decode_tokens"] + engine.stats["requests"], "counter", "tokens generated"),
+            ("olmo_decode_steps_total", engine.stats["decode_steps"], "counter", "decode steps run"),
+            ("olmo_requests_waiting", waiting, "gauge", "requests in the queue"),
+            ("olmo_requests_running", running, "gauge", "rows of the decode batch in use"),
+        ]:
+            lines += [f"# HELP {name} {text}", f"# TYPE {name} {kind}", f"{name} {int(value)}"]
+        return PlainTextResponse("\n".join(lines) + "\n", media_type="text/plain; version=0.0.4")
 
     @app.get("/v1/models")
     async def models():

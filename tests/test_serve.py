@@ -215,6 +215,11 @@ def test_openai_routes():
         streamed = "".join(json.loads(e)["choices"][0]["text"] for e in events[:-1])
         assert streamed == CharTokenizer().decode(greedy_reference(model, [ord(c) for c in "hello world"], 6))
 
+        exposition = client.get("/metrics").text
+        assert "# TYPE olmo_generated_tokens_total counter" in exposition
+        counters = dict(line.split() for line in exposition.splitlines() if line and not line.startswith("#"))
+        assert int(counters["olmo_requests_total"]) == engine.stats["requests"] > 0 and counters["olmo_requests_running"] == "0"
+
         for bad, status, code in [
             ({"prompt": "x" * 60}, 400, "context_length_exceeded"),
             ({"prompt": "x", "model": "other"}, 404, "model_not_found"),
