@@ -1,0 +1,268 @@
+// y = x · Wᵀ for 4-bit weights and a decode-sized activation batch (9..256 rows), on the tcgen05 tensor cores with the
+// dequantisation fused into the operand staging: the packed weights are read from HBM exactly once (half a byte per
+// weight) and never exist as a bf16 matrix in global memory.
+//
+// Roles are swapped with respect to the training GEMM: the *weights* are the 128-row A operand (so a CTA owns 128
+// output features) and the *activations* are the B operand (UMMA N = the batch, padded to 32/64/128/256), i.e. the
+// accumulator in TMEM is yᵀ: lane = output feature, column = batch row.
+//
+// One CTA per 128 output features, 192 threads:
+//   warps 0..3  dequantise: thread r owns weight row n0 + r.  Per 64-wide K block it loads 32 bytes of packed weights,
+//               turns them into 64 bf16 and writes them as row r of a 128 x 64 K-major tile in the 128-byte-swizzled
+//               layout tcgen05 expects (16-byte chunk c of row r lives at chunk position c ^ (r % 8)), then makes the
+//               writes visible to the async proxy and arrives on the stage's barrier.  After the K loop the same warps
+//               read their 32 TMEM lanes and store y (lanes = consecutive features, so stores of a warp are contiguous).
+//   warp 4      TMA producer of the activation tile (MB x 64, rows beyond M are zero-filled by the copy engine)
+//   warp 5      MMA issuer (one lane), owns the TMEM allocation
+// A stage is full when 128 dequantising threads and the TMA transaction have arrived; it is released by tcgen05.commit.
+// Every wait is bounded and reports through the status word; an aborting CTA still releases its TMEM.
+//
+// Counterpart in the reference's vendored AutoGPTQ: the Triton quant_matmul kernel (tensor-core path for batches).
+#include "common.cuh"
+#include "api.h"
+
+namespace ob {
+
+int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                            uint32_t box_inner, uint32_t box_outer);
+
+namespace {
+
+constexpr int WM_ROWS = 128;  // weight rows (output features) per CTA = UMMA M
+constexpr int WM_BK = 64;     // K entries per stage: one 128-byte swizzled row
+constexpr int WM_STAGES = 4;
+constexpr int WM_THREADS = 192;
+constexpr int WM_A_BYTES = WM_ROWS * WM_BK * 2;  // 16 KiB
+
+template <int MB>
+struct WmCfg {
+  static constexpr int B_BYTES = MB * WM_BK * 2;
+  static constexpr int STAGE_BYTES = WM_A_BYTES + B_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + WM_STAGES * STAGE_BYTES + 256;
+};
+
+__device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// eight 4-bit codes of one word -> eight bf16 (two per 32-bit lane), value = (code - zero) * scale rounded once
+__device__ __forceinline__ uint4 dequant_word(uint32_t word, float zero, float scale) {
+  float f[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) f[i] = (static_cast<float>((word >> (4 * i)) & 0xFu) - zero) * scale;
+  uint4 o;
+  o.x = pack_bf16x2(f[0], f[1]);
+  o.y = pack_bf16x2(f[2], f[3]);
+  o.z = pack_bf16x2(f[4], f[5]);
+  o.w = pack_bf16x2(f[6], f[7]);
+  return o;
+}
+
+template <int MB>
+__global__ void __launch_bounds__(WM_THREADS)
+w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __restrict__ qweight, const bf16* __restrict__ scales,
+                 const uint8_t* __restrict__ zeros, bf16* __restrict__ y, int M, int N, int K, int group, int* __restrict__ status) {
+  using Cfg = WmCfg<MB>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                           // WM_STAGES x 16 KiB, each 1024-byte aligned
+  uint8_t* sB = smem + WM_STAGES * WM_A_BYTES;  // WM_STAGES x B_BYTES (multiples of 4 KiB)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + WM_STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + WM_STAGES;
+  uint64_t* done_bar = empty_bar + WM_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = static_cast<int>(blockIdx.x) * WM_ROWS;
+  const int k_blocks = K / WM_BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < WM_STAGES; ++s) {
+      mbar_init(&full_bar[s], WM_ROWS + 1);  // 128 dequantising threads + the TMA producer's expect_tx arrival
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(done_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, MB);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp < 4) {
+    // ------------------------------------------------------------ dequantise into the A stages, then the epilogue
+    const int r = threadIdx.x;  // 0..127: row of the tile, TMEM lane of the result
+    const int n = n0 + r;
+    const int groups = K / group;
+    const uint32_t* wrow = qweight + static_cast<size_t>(n) * (K / 8);
+    const bf16* srow = scales + static_cast<size_t>(n) * groups;
+    const uint8_t* zrow = zeros + static_cast<size_t>(n) * groups;
+    const uint32_t row_off = static_cast<uint32_t>(r) * 128u;
+    const uint32_t sw = static_cast<uint32_t>(r & 7);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    uint4 w_lo = ldg_stream_v4(wrow), w_hi = ldg_stream_v4(wrow + 4);
+    for (int kb = 0; kb < k_blocks; ++kb) {
+      const uint4 c_lo = w_lo, c_hi = w_hi;
+      if (kb + 1 < k_blocks) {  // next block's codes are in flight while this one is unpacked
+        w_lo = ldg_stream_v4(wrow + (kb + 1) * 8);
+        w_hi = ldg_stream_v4(wrow + (kb + 1) * 8 + 4);
+      }
+      const int g = (kb * WM_BK) / group;  // a 64-wide block never straddles a group (group is a multiple of 64)
+      const float s = __bfloat162float(srow[g]);
+      const float z = static_cast<float>(zrow[g]);
+      if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
+        ok = false;
+        break;
+      }
+      uint8_t* row = sA + stage * WM_A_BYTES + row_off;
+      const uint32_t words[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        *reinterpret_cast<uint4*>(row + ((static_cast<uint32_t>(c) ^ sw) << 4)) = dequant_word(words[c], z, s);
+      }
+      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
+      mbar_arrive(&full_bar[stage]);
+      if (++stage == WM_STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    if (ok && mbar_wait(done_bar, 0u, abort_flag, status, ST_TIMEOUT_EPILOGUE)) {
+      tc_fence_after();
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+#pragma unroll 1
+      for (int c = 0; c < MB / 32; ++c) {
+        if (c * 32 >= M) break;  // warp-uniform
+        uint32_t acc[32];
+        tmem_ld_32x32b_x32(t_addr + c * 32, acc);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = c * 32 + j;
+          if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16_rn(__uint_as_float(acc[j]));
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ------------------------------------------------------------------------- activation tiles by TMA
+    if (lane == 0) {
+      prefetch_tensormap(&tma_x);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(&full_bar[stage], Cfg::B_BYTES);
+        tma_load_2d(sB + stage * Cfg::B_BYTES, &tma_x, &full_bar[stage], kb * WM_BK, 0);
+        if (++stage == WM_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) {  // aborting: give copies already in flight a bounded time to land before shared memory is released
+        const long long t0 = clock64();
+        while (clock64() - t0 < 2000000LL) {
+        }
+      }
+    }
+  } else {
+    // ----------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(WM_ROWS, MB, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        if (!mbar_wait(&full_bar[stage], phase, abort_flag, status, ST_TIMEOUT_MMA)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_addr = smem_u32(sA + stage * WM_A_BYTES);
+        const uint32_t b_addr = smem_u32(sB + stage * Cfg::B_BYTES);
+#pragma unroll
+        for (int k = 0; k < WM_BK / 16; ++k) {
+          const uint64_t a_desc = make_smem_desc_sw128(a_addr + k * 32, 16, 1024);
+          const uint64_t b_desc = make_smem_desc_sw128(b_addr + k * 32, 16, 1024);
+          umma_f16_ss(tmem_base, a_desc, b_desc, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+        }
+        umma_commit(&empty_bar[stage]);
+        if (++stage == WM_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) umma_commit(done_bar);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, MB);
+  }
+}
+
+template <int MB>
+int launch_mma(const CUtensorMap& tx, const uint32_t* q, const bf16* s, const uint8_t* z, bf16* y, int M, int N, int K, int group,
+               int* status, cudaStream_t stream) {
+  using Cfg = WmCfg<MB>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(w4a16_mma_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess) return -4;
+    configured = true;
+  }
+  w4a16_mma_kernel<MB><<<N / WM_ROWS, WM_THREADS, Cfg::SMEM_BYTES, stream>>>(tx, q, s, z, y, M, N, K, group, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+}  // namespace
+}  // namespace ob
+
+extern "C" {
+
+// 1 if ob_w4a16_gemm_small covers the shape: up to 256 activation rows, features in whole 128-row tiles, K in whole
+// 64-entry blocks that never straddle a quantisation group.
+int ob_w4a16_gemm_small_supported(int M, int N, int K, int group) {
+  return (M >= 1 && M <= 256 && N % ob::WM_ROWS == 0 && K % ob::WM_BK == 0 && group % ob::WM_BK == 0 && K % group == 0) ? 1 : 0;
+}
+
+// y[M, N] (bf16, row pitch N) = x[M, K] (bf16, contiguous) · Wᵀ with W given as packed 4-bit codes.
+int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, int M, int N, int K,
+                        int group, int* status, cudaStream_t stream) {
+  using namespace ob;
+  if (!ob_w4a16_gemm_small_supported(M, N, K, group)) return -1;
+  const int mb = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
+  CUtensorMap tx;
+  // rows beyond M are outside the tensor: the copy engine fills them with zeros, which is the padding of the batch
+  int rc = make_tensor_map_bf16_2d(&tx, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(K), WM_BK,
+                                   static_cast<uint32_t>(mb));
+  if (rc != 0) return rc - 10;
+  const uint32_t* q = static_cast<const uint32_t*>(qweight);
+  const bf16* s = static_cast<const bf16*>(scales);
+  const uint8_t* z = static_cast<const uint8_t*>(zeros);
+  bf16* yp = static_cast<bf16*>(y);
+  switch (mb) {
+    case 32: return launch_mma<32>(tx, q, s, z, yp, M, N, K, group, status, stream);
+    case 64: return launch_mma<64>(tx, q, s, z, yp, M, N, K, group, status, stream);
+    case 128: return launch_mma<128>(tx, q, s, z, yp, M, N, K, group, status, stream);
+    default: return launch_mma<256>(tx, q, s, z, yp, M, N, K, group, status, stream);
+  }
+}
+
+}  // extern "C"

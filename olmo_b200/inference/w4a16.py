@@ -122,10 +122,19 @@ class QuantLinear(nn.Module):
                       "ob_gather_columns_bf16")
                 xb = gathered
             m = xb.shape[0]
-            if m <= 64:
-                # decode-sized inputs: the matrix-vector kernel takes up to 8 rows per launch and reads the packed
-                # weights once per launch (0.5 byte per weight), so up to 64 rows cost less traffic than
-                # reconstructing the matrix (2.5 bytes per weight) and multiplying it (2 more)
+            fused_ok = 8 < m <= 256 and lib().ob_w4a16_gemm_small_supported(m, self.out_features, self.in_features, self.group)
+            if fused_ok:
+                # decode batches: dequantisation fused into the operand staging of a tcgen05 GEMM; the packed weights
+                # are read once and no bf16 copy of the matrix is written
+                from ..ops import status_tensor
+
+                y = torch.empty(m, self.out_features, dtype=torch.bfloat16, device=x.device)
+                check(lib().ob_w4a16_gemm_small(ptr(xb), ptr(self.qweight), ptr(self.scales), ptr(self.zeros), ptr(y), m, self.out_features,
+                                                self.in_features, self.group, ptr(status_tensor(x.device)), stream_ptr()), "ob_w4a16_gemm_small")
+            elif m <= 64:
+                # the matrix-vector kernel takes up to 8 rows per launch and reads the packed weights once per launch
+                # (0.5 byte per weight), so up to 64 rows cost less traffic than reconstructing the matrix (2.5 bytes
+                # per weight) and multiplying it (2 more)
                 y = torch.empty(m, self.out_features, dtype=torch.bfloat16, device=x.device)
                 for lo in range(0, m, 8):
                     rows = min(8, m - lo)
