@@ -54,12 +54,12 @@ def main(argv=None) -> int:
 
     device = torch.device(args.device or ("cuda" if torch.cuda.is_available() else "cpu"))
     spec = model_dict(args.family)
-    spec["init_device"] = "cpu"
+    spec["init_device"] = str(device)  # random weights are drawn on the device: no multi-gigabyte host copy
     if args.n_layers:
         spec["n_layers"] = args.n_layers
     cfg = ModelConfig.new(**spec)
     torch.manual_seed(0)
-    model = OLMo(cfg).to(torch.bfloat16 if args.dtype == "bf16" else torch.float32).to(device).eval()
+    model = OLMo(cfg).to(torch.bfloat16 if args.dtype == "bf16" else torch.float32).eval()
     if args.quantize == "rtn":
         from ..inference.quantize import quantize_model
 
