@@ -94,8 +94,9 @@ int ob_w4a16_gemv(const void* x, const void* qweight, const void* scales, const 
 int ob_w4a16_dequant(const void* qweight, const void* scales, const void* zeros, void* out, int N, int K, int group, cudaStream_t stream);
 // Fused dequantise -> tcgen05 GEMM for 1..256 activation rows (w4a16_mma.cu); `status` is the library's status word.
 int ob_w4a16_gemm_small_supported(int M, int N, int K, int group);
-int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, int M, int N, int K,
-                        int group, int* status, cudaStream_t stream);
+int ob_w4a16_gemm_small_splits(int N, int K);
+int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, float* partial, int M, int N,
+                        int K, int group, int splits, int* status, cudaStream_t stream);
 int ob_gather_columns_bf16(const void* x, const int* perm, void* out, int M, int K, cudaStream_t stream);
 
 #ifdef __cplusplus

@@ -6,15 +6,20 @@
 // output features) and the *activations* are the B operand (UMMA N = the batch, padded to 32/64/128/256), i.e. the
 // accumulator in TMEM is yᵀ: lane = output feature, column = batch row.
 //
-// One CTA per 128 output features, 192 threads:
-//   warps 0..3  dequantise: thread r owns weight row n0 + r.  Per 64-wide K block it loads 32 bytes of packed weights,
-//               turns them into 64 bf16 and writes them as row r of a 128 x 64 K-major tile in the 128-byte-swizzled
-//               layout tcgen05 expects (16-byte chunk c of row r lives at chunk position c ^ (r % 8)), then makes the
-//               writes visible to the async proxy and arrives on the stage's barrier.  After the K loop the same warps
-//               read their 32 TMEM lanes and store y (lanes = consecutive features, so stores of a warp are contiguous).
-//   warp 4      TMA producer of the activation tile (MB x 64, rows beyond M are zero-filled by the copy engine)
-//   warp 5      MMA issuer (one lane), owns the TMEM allocation
-// A stage is full when 128 dequantising threads and the TMA transaction have arrived; it is released by tcgen05.commit.
+// Grid (features / 128, K splits), 320 threads per CTA:
+//   warps 0..7  dequantise: threads r and r + 128 share weight row n0 + r, each owning half of every 64-wide K block.
+//               A thread keeps the packed codes of the next four blocks in registers (the loads are the only long
+//               latency of the loop), turns 16 bytes into 32 bf16 and writes them into row r of a 128 x 64 K-major
+//               tile in the 128-byte-swizzled layout tcgen05 expects (16-byte chunk c of row r lives at chunk position
+//               c ^ (r % 8)), then makes the writes visible to the async proxy and arrives on the stage's barrier.
+//               After the K loop the same warps read TMEM (warp w may touch lanes 32·(w % 4)..; the two warps of a
+//               lane quarter take alternate 32-column chunks) and store y: lanes are consecutive features, so a warp's
+//               stores are contiguous.
+//   warp 8      TMA producer of the activation tile (MB x 64, rows beyond M are zero-filled by the copy engine)
+//   warp 9      MMA issuer (one lane), owns the TMEM allocation
+// A stage is full when 256 dequantising threads and the TMA transaction have arrived; it is released by tcgen05.commit.
+// With K splits (chosen when there are too few 128-feature tiles to fill the GPU) every CTA covers a range of K blocks
+// and adds its partial result to a zeroed fp32 workspace, which the caller converts to bf16.
 // Every wait is bounded and reports through the status word; an aborting CTA still releases its TMEM.
 //
 // Counterpart in the reference's vendored AutoGPTQ: the Triton quant_matmul kernel (tensor-core path for batches).
@@ -31,7 +36,9 @@ namespace {
 constexpr int WM_ROWS = 128;  // weight rows (output features) per CTA = UMMA M
 constexpr int WM_BK = 64;     // K entries per stage: one 128-byte swizzled row
 constexpr int WM_STAGES = 4;
-constexpr int WM_THREADS = 192;
+constexpr int WM_DEQ_THREADS = 256;
+constexpr int WM_THREADS = WM_DEQ_THREADS + 64;
+constexpr int WM_AHEAD = 4;  // K blocks whose packed codes a thread holds in registers
 constexpr int WM_A_BYTES = WM_ROWS * WM_BK * 2;  // 16 KiB
 
 template <int MB>
@@ -63,7 +70,8 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t word, float zero, float s
 template <int MB>
 __global__ void __launch_bounds__(WM_THREADS)
 w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __restrict__ qweight, const bf16* __restrict__ scales,
-                 const uint8_t* __restrict__ zeros, bf16* __restrict__ y, int M, int N, int K, int group, int* __restrict__ status) {
+                 const uint8_t* __restrict__ zeros, bf16* __restrict__ y, float* __restrict__ partial, int M, int N, int K, int group,
+                 int blocks_per_split, int* __restrict__ status) {
   using Cfg = WmCfg<MB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -78,18 +86,20 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n0 = static_cast<int>(blockIdx.x) * WM_ROWS;
-  const int k_blocks = K / WM_BK;
+  const int kb_begin = static_cast<int>(blockIdx.y) * blocks_per_split;
+  const int kb_end = min(K / WM_BK, kb_begin + blocks_per_split);
+  const int k_blocks = kb_end - kb_begin;  // >= 1 by construction of the grid
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WM_STAGES; ++s) {
-      mbar_init(&full_bar[s], WM_ROWS + 1);  // 128 dequantising threads + the TMA producer's expect_tx arrival
+      mbar_init(&full_bar[s], WM_DEQ_THREADS + 1);  // dequantising threads + the TMA producer's expect_tx arrival
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(done_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_slot, MB);
     tmem_relinquish();
   }
@@ -98,12 +108,13 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp < 4) {
+  if (warp < 8) {
     // ------------------------------------------------------------ dequantise into the A stages, then the epilogue
-    const int r = threadIdx.x;  // 0..127: row of the tile, TMEM lane of the result
+    const int r = threadIdx.x & (WM_ROWS - 1);  // row of the tile, TMEM lane of the result
+    const int half = threadIdx.x >> 7;          // which 32 of the block's 64 K entries
     const int n = n0 + r;
     const int groups = K / group;
-    const uint32_t* wrow = qweight + static_cast<size_t>(n) * (K / 8);
+    const uint32_t* wrow = qweight + static_cast<size_t>(n) * (K / 8) + half * 4;
     const bf16* srow = scales + static_cast<size_t>(n) * groups;
     const uint8_t* zrow = zeros + static_cast<size_t>(n) * groups;
     const uint32_t row_off = static_cast<uint32_t>(r) * 128u;
@@ -111,50 +122,65 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    uint4 w_lo = ldg_stream_v4(wrow), w_hi = ldg_stream_v4(wrow + 4);
-    for (int kb = 0; kb < k_blocks; ++kb) {
-      const uint4 c_lo = w_lo, c_hi = w_hi;
-      if (kb + 1 < k_blocks) {  // next block's codes are in flight while this one is unpacked
-        w_lo = ldg_stream_v4(wrow + (kb + 1) * 8);
-        w_hi = ldg_stream_v4(wrow + (kb + 1) * 8 + 4);
-      }
-      const int g = (kb * WM_BK) / group;  // a 64-wide block never straddles a group (group is a multiple of 64)
-      const float s = __bfloat162float(srow[g]);
-      const float z = static_cast<float>(zrow[g]);
-      if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
-        ok = false;
-        break;
-      }
-      uint8_t* row = sA + stage * WM_A_BYTES + row_off;
-      const uint32_t words[8] = {c_lo.x, c_lo.y, c_lo.z, c_lo.w, c_hi.x, c_hi.y, c_hi.z, c_hi.w};
+    uint4 ahead[WM_AHEAD];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        *reinterpret_cast<uint4*>(row + ((static_cast<uint32_t>(c) ^ sw) << 4)) = dequant_word(words[c], z, s);
-      }
-      fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
-      mbar_arrive(&full_bar[stage]);
-      if (++stage == WM_STAGES) {
-        stage = 0;
-        phase ^= 1u;
+    for (int a = 0; a < WM_AHEAD; ++a) {
+      if (a < k_blocks) ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + a) * 8);
+    }
+    for (int kb0 = 0; kb0 < k_blocks && ok; kb0 += WM_AHEAD) {
+#pragma unroll
+      for (int a = 0; a < WM_AHEAD; ++a) {
+        const int kb = kb0 + a;
+        if (kb >= k_blocks) break;
+        const uint4 codes = ahead[a];
+        if (kb + WM_AHEAD < k_blocks) ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + kb + WM_AHEAD) * 8);
+        const int g = ((kb_begin + kb) * WM_BK) / group;  // a 64-wide block never straddles a group
+        const float s = __bfloat162float(srow[g]);
+        const float z = static_cast<float>(zrow[g]);
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        uint8_t* row = sA + stage * WM_A_BYTES + row_off;
+        const uint32_t words[4] = {codes.x, codes.y, codes.z, codes.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t chunk = static_cast<uint32_t>(half * 4 + c);
+          *reinterpret_cast<uint4*>(row + ((chunk ^ sw) << 4)) = dequant_word(words[c], z, s);
+        }
+        fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
+        mbar_arrive(&full_bar[stage]);
+        if (++stage == WM_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
     }
     if (ok && mbar_wait(done_bar, 0u, abort_flag, status, ST_TIMEOUT_EPILOGUE)) {
       tc_fence_after();
-      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16);
+      const uint32_t t_addr = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
 #pragma unroll 1
-      for (int c = 0; c < MB / 32; ++c) {
+      for (int c = half; c < MB / 32; c += 2) {  // the two warps of a lane quarter take alternate column chunks
         if (c * 32 >= M) break;  // warp-uniform
         uint32_t acc[32];
         tmem_ld_32x32b_x32(t_addr + c * 32, acc);
         tmem_ld_wait();
+        if (partial != nullptr) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int m = c * 32 + j;
-          if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16_rn(__uint_as_float(acc[j]));
+          for (int j = 0; j < 32; ++j) {
+            const int m = c * 32 + j;
+            if (m < M) atomicAdd(partial + static_cast<size_t>(m) * N + n, __uint_as_float(acc[j]));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int m = c * 32 + j;
+            if (m < M) y[static_cast<size_t>(m) * N + n] = __float2bfloat16_rn(__uint_as_float(acc[j]));
+          }
         }
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 8) {
     // ------------------------------------------------------------------------- activation tiles by TMA
     if (lane == 0) {
       prefetch_tensormap(&tma_x);
@@ -167,7 +193,7 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
           break;
         }
         mbar_expect_tx(&full_bar[stage], Cfg::B_BYTES);
-        tma_load_2d(sB + stage * Cfg::B_BYTES, &tma_x, &full_bar[stage], kb * WM_BK, 0);
+        tma_load_2d(sB + stage * Cfg::B_BYTES, &tma_x, &full_bar[stage], (kb_begin + kb) * WM_BK, 0);
         if (++stage == WM_STAGES) {
           stage = 0;
           phase ^= 1u;
@@ -212,22 +238,23 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, MB);
   }
 }
 
 template <int MB>
-int launch_mma(const CUtensorMap& tx, const uint32_t* q, const bf16* s, const uint8_t* z, bf16* y, int M, int N, int K, int group,
-               int* status, cudaStream_t stream) {
+int launch_mma(const CUtensorMap& tx, const uint32_t* q, const bf16* s, const uint8_t* z, bf16* y, float* partial, int M, int N, int K,
+               int group, int splits, int blocks_per_split, int* status, cudaStream_t stream) {
   using Cfg = WmCfg<MB>;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(w4a16_mma_kernel<MB>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES) != cudaSuccess) return -4;
     configured = true;
   }
-  w4a16_mma_kernel<MB><<<N / WM_ROWS, WM_THREADS, Cfg::SMEM_BYTES, stream>>>(tx, q, s, z, y, M, N, K, group, status);
+  const dim3 grid(N / WM_ROWS, splits);
+  w4a16_mma_kernel<MB><<<grid, WM_THREADS, Cfg::SMEM_BYTES, stream>>>(tx, q, s, z, y, partial, M, N, K, group, blocks_per_split, status);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -242,11 +269,31 @@ int ob_w4a16_gemm_small_supported(int M, int N, int K, int group) {
   return (M >= 1 && M <= 256 && N % ob::WM_ROWS == 0 && K % ob::WM_BK == 0 && group % ob::WM_BK == 0 && K % group == 0) ? 1 : 0;
 }
 
-// y[M, N] (bf16, row pitch N) = x[M, K] (bf16, contiguous) · Wᵀ with W given as packed 4-bit codes.
-int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, int M, int N, int K,
-                        int group, int* status, cudaStream_t stream) {
+// Number of K splits the kernel wants for this shape: 1 when the 128-feature tiles alone fill the GPU, otherwise enough
+// splits to reach about one CTA per SM, each split keeping at least eight K blocks.  With more than one split the caller
+// passes a zeroed fp32 [M, N] workspace and converts it to bf16 afterwards.
+int ob_w4a16_gemm_small_splits(int N, int K) {
+  const int tiles = N / ob::WM_ROWS;
+  const int k_blocks = K / ob::WM_BK;
+  if (tiles <= 0 || k_blocks <= 0 || tiles >= 120) return 1;
+  int splits = (148 + tiles - 1) / tiles;
+  if (splits > k_blocks / 8) splits = k_blocks / 8;
+  if (splits < 1) splits = 1;
+  const int per = (k_blocks + splits - 1) / splits;
+  return (k_blocks + per - 1) / per;  // no empty split
+}
+
+// y[M, N] (bf16, row pitch N) = x[M, K] (bf16, contiguous) · Wᵀ with W given as packed 4-bit codes.  `splits` must be
+// the value of ob_w4a16_gemm_small_splits; when it is greater than 1 the result is *added* to `partial` (fp32 [M, N])
+// and `y` is not written.
+int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, float* partial, int M, int N,
+                        int K, int group, int splits, int* status, cudaStream_t stream) {
   using namespace ob;
   if (!ob_w4a16_gemm_small_supported(M, N, K, group)) return -1;
+  const int k_blocks = K / WM_BK;
+  if (splits < 1 || splits > k_blocks || (splits > 1) != (partial != nullptr)) return -1;
+  const int per = (k_blocks + splits - 1) / splits;
+  if ((k_blocks + per - 1) / per != splits) return -1;
   const int mb = M <= 32 ? 32 : (M <= 64 ? 64 : (M <= 128 ? 128 : 256));
   CUtensorMap tx;
   // rows beyond M are outside the tensor: the copy engine fills them with zeros, which is the padding of the batch
@@ -258,10 +305,10 @@ int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, 
   const uint8_t* z = static_cast<const uint8_t*>(zeros);
   bf16* yp = static_cast<bf16*>(y);
   switch (mb) {
-    case 32: return launch_mma<32>(tx, q, s, z, yp, M, N, K, group, status, stream);
-    case 64: return launch_mma<64>(tx, q, s, z, yp, M, N, K, group, status, stream);
-    case 128: return launch_mma<128>(tx, q, s, z, yp, M, N, K, group, status, stream);
-    default: return launch_mma<256>(tx, q, s, z, yp, M, N, K, group, status, stream);
+    case 32: return launch_mma<32>(tx, q, s, z, yp, partial, M, N, K, group, splits, per, status, stream);
+    case 64: return launch_mma<64>(tx, q, s, z, yp, partial, M, N, K, group, splits, per, status, stream);
+    case 128: return launch_mma<128>(tx, q, s, z, yp, partial, M, N, K, group, splits, per, status, stream);
+    default: return launch_mma<256>(tx, q, s, z, yp, partial, M, N, K, group, splits, per, status, stream);
   }
 }
 

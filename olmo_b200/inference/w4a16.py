@@ -9,6 +9,8 @@ AutoGPTQ under ``inference/compression/dependencies``.
 """
 from __future__ import annotations
 
+import ctypes
+
 from typing import Optional, Tuple
 
 import torch
@@ -129,8 +131,14 @@ class QuantLinear(nn.Module):
                 from ..ops import status_tensor
 
                 y = torch.empty(m, self.out_features, dtype=torch.bfloat16, device=x.device)
-                check(lib().ob_w4a16_gemm_small(ptr(xb), ptr(self.qweight), ptr(self.scales), ptr(self.zeros), ptr(y), m, self.out_features,
-                                                self.in_features, self.group, ptr(status_tensor(x.device)), stream_ptr()), "ob_w4a16_gemm_small")
+                # layers with few 128-feature tiles split K over several CTAs, which add into a zeroed fp32 buffer
+                splits = lib().ob_w4a16_gemm_small_splits(self.out_features, self.in_features)
+                partial = torch.zeros(m, self.out_features, dtype=torch.float32, device=x.device) if splits > 1 else None
+                check(lib().ob_w4a16_gemm_small(ptr(xb), ptr(self.qweight), ptr(self.scales), ptr(self.zeros), ptr(y), ptr(partial), m,
+                                                self.out_features, self.in_features, self.group, splits, ptr(status_tensor(x.device)),
+                                                stream_ptr()), "ob_w4a16_gemm_small")
+                if partial is not None:
+                    check(lib().ob_cast_f32_to_bf16(ptr(partial), ptr(y), ctypes.c_longlong(partial.numel()), stream_ptr()), "ob_cast_f32_to_bf16")
             elif m <= 64:
                 # the matrix-vector kernel takes up to 8 rows per launch and reads the packed weights once per launch
                 # (0.5 byte per weight), so up to 64 rows cost less traffic than reconstructing the matrix (2.5 bytes

@@ -191,10 +191,23 @@ def test_fused_dequant_tensor_core_gemm_matches_cpu_reference(M, N, K, G):
     xd = x.cuda()
     sentinel = -7.0
     y = torch.full((M + 3, N), sentinel, dtype=torch.bfloat16, device="cuda")  # three guard rows
-    ops.check(lib.ob_w4a16_gemm_small(ops.ptr(xd), ops.ptr(dev.qweight), ops.ptr(dev.scales), ops.ptr(dev.zeros), ops.ptr(y), M, N, K, G,
-                                      ops.ptr(ops.status_tensor(xd.device)), ops.stream_ptr()), "ob_w4a16_gemm_small")
+    ops.check(lib.ob_w4a16_gemm_small(ops.ptr(xd), ops.ptr(dev.qweight), ops.ptr(dev.scales), ops.ptr(dev.zeros), ops.ptr(y), None, M, N, K, G,
+                                      1, ops.ptr(ops.status_tensor(xd.device)), ops.stream_ptr()), "ob_w4a16_gemm_small")
     ops.check_status()
     assert bool((y[M:] == sentinel).all())
+    # the same product with K split over several CTAs that add into an fp32 buffer (guard rows again)
+    k_blocks = K // 64
+    for splits in sorted({2, max(1, k_blocks // 8), lib.ob_w4a16_gemm_small_splits(N, K)} - {1}):
+        per = -(-k_blocks // splits)
+        if -(-k_blocks // per) != splits:
+            continue
+        partial = torch.zeros(M + 3, N, dtype=torch.float32, device="cuda")
+        partial[M:] = sentinel
+        ops.check(lib.ob_w4a16_gemm_small(ops.ptr(xd), ops.ptr(dev.qweight), ops.ptr(dev.scales), ops.ptr(dev.zeros), None, ops.ptr(partial),
+                                          M, N, K, G, splits, ops.ptr(ops.status_tensor(xd.device)), ops.stream_ptr()), "ob_w4a16_gemm_small")
+        ops.check_status()
+        assert bool((partial[M:] == sentinel).all())
+        torch.testing.assert_close(partial[:M].cpu(), want, rtol=2e-2, atol=6e-2)
     torch.testing.assert_close(y[:M].float().cpu(), want, rtol=2e-2, atol=6e-2)  # outputs reach ±16: half a bf16 step is 0.03
     via_matrix = (xd.float() @ dev.dequantize().float().t()).cpu()
     torch.testing.assert_close(y[:M].float().cpu(), via_matrix, rtol=1e-2, atol=2e-2)
