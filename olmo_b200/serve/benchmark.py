@@ -72,6 +72,8 @@ def main(argv=None) -> int:
     params = SamplingParams(max_tokens=args.max_tokens, temperature=0.0, ignore_eos=True)
 
     engine.generate(prompts[: min(2, len(prompts))], SamplingParams(max_tokens=4, temperature=0.0, ignore_eos=True))  # warm-up
+    # a second warm-up at full width captures the decode graph of the first length bucket outside the timed region
+    engine.generate(prompts[: args.max_batch], SamplingParams(max_tokens=2, temperature=0.0, ignore_eos=True))
     for key in engine.stats:
         engine.stats[key] = 0
     if device.type == "cuda":
@@ -89,7 +91,11 @@ def main(argv=None) -> int:
         "prompt_len": args.prompt_len, "max_tokens": args.max_tokens, "seconds": elapsed,
         "kv_cache": "dynamic" if engine._static is None else "static", "cuda_graphs": bool(engine._static and engine._static.cuda_graphs),
         "graph_replays": 0 if engine._static is None else engine._static.graph_replays,
-        "ttft_median_s": ttft[len(ttft) // 2], "ttft_max_s": ttft[-1], **{k: int(v) for k, v in engine.stats.items()},
+        "ttft_median_s": ttft[len(ttft) // 2], "ttft_max_s": ttft[-1],
+        "decode_tokens_per_second": engine.stats["decode_tokens"] / max(engine.stats["decode_seconds"], 1e-9),
+        "decode_ms_per_step": 1e3 * engine.stats["decode_seconds"] / max(engine.stats["decode_steps"], 1),
+        "prefill_tokens_per_second": engine.stats["prefill_tokens"] / max(engine.stats["prefill_seconds"], 1e-9),
+        **{k: (round(v, 4) if k.endswith("_seconds") else int(v)) for k, v in engine.stats.items()},
     }))
     return 0
 

@@ -148,7 +148,9 @@ class Engine:
         self._kv: Optional[List[Tuple[torch.Tensor, torch.Tensor]]] = None
         self._mask: Optional[torch.Tensor] = None  # [rows, L] 1 = real token
         self._last: Optional[torch.Tensor] = None  # [rows] token to feed next
-        self.stats: Dict[str, float] = {"prefill_tokens": 0, "decode_tokens": 0, "decode_steps": 0, "requests": 0}
+        # seconds are host wall clock around a whole step; every step ends with a device-to-host read of the sampled tokens
+        self.stats: Dict[str, float] = {"prefill_tokens": 0, "decode_tokens": 0, "decode_steps": 0, "requests": 0,
+                                        "prefill_seconds": 0.0, "decode_seconds": 0.0}
 
     # ------------------------------------------------------------------------------- submission
     def submit(
@@ -253,10 +255,13 @@ class Engine:
         with self._lock:
             room = self.max_batch - len(self._rows)
             admitted = [self._queue.popleft() for _ in range(min(room, len(self._queue)))]
+        started = time.perf_counter()
         if admitted:
             self._prefill(admitted)
+            self.stats["prefill_seconds"] += time.perf_counter() - started
         elif self._rows:
             self._decode()
+            self.stats["decode_seconds"] += time.perf_counter() - started
         else:
             return False
         return True

@@ -179,7 +179,7 @@ def create_app(
 
     @app.get("/health")
     async def health():
-        return {"status": "ok", **{k: int(v) for k, v in engine.stats.items()}}
+        return {"status": "ok", **{k: (round(v, 3) if isinstance(v, float) else int(v)) for k, v in engine.stats.items()}}
 
     @app.get("/metrics")
     async def metrics():
