@@ -211,5 +211,5 @@ def test_fused_dequant_tensor_core_gemm_matches_cpu_reference(M, N, K, G):
     torch.testing.assert_close(y[:M].float().cpu(), want, rtol=2e-2, atol=6e-2)  # outputs reach ±16: half a bf16 step is 0.03
     via_matrix = (xd.float() @ dev.dequantize().float().t()).cpu()
     torch.testing.assert_close(y[:M].float().cpu(), via_matrix, rtol=1e-2, atol=2e-2)
-    # the module takes the same path for this batch size
-    torch.testing.assert_close(dev(xd).float().cpu(), y[:M].float().cpu(), rtol=0, atol=0)
+    # the module takes the same kernel for this batch size (with its own choice of K splits, hence not bit-identical)
+    torch.testing.assert_close(dev(xd).float().cpu(), y[:M].float().cpu(), rtol=1e-2, atol=6e-2)
