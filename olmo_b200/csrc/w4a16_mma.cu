@@ -54,16 +54,26 @@ __device__ __forceinline__ uint4 ldg_stream_v4(const void* p) {
   return v;
 }
 
-// eight 4-bit codes of one word -> eight bf16 (two per 32-bit lane), value = (code - zero) * scale rounded once
-__device__ __forceinline__ uint4 dequant_word(uint32_t word, float zero, float scale) {
-  float f[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) f[i] = (static_cast<float>((word >> (4 * i)) & 0xFu) - zero) * scale;
+// Eight 4-bit codes of one word -> eight bf16, value = (code - zero) * scale rounded once, two values per instruction.
+// A code c dropped into the low mantissa bits of bf16 128.0 (0x4300) reads 128 + c exactly; subtracting 128 + zero is
+// exact and the product with the bf16 scale is rounded once, which is what the scalar fp32 formula gives.  The pairs
+// come out as (c0,c4) (c1,c5) (c2,c6) (c3,c7); two byte permutes per pair of words restore K order.
+__device__ __forceinline__ uint32_t bf16x2_sub_mul(uint32_t v, uint32_t zero_plus_128, uint32_t scale) {
+  const __nv_bfloat162 r = __hmul2(__hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v), *reinterpret_cast<const __nv_bfloat162*>(&zero_plus_128)),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&scale));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+__device__ __forceinline__ uint4 dequant_word(uint32_t word, uint32_t zero_plus_128, uint32_t scale) {
+  const uint32_t a = bf16x2_sub_mul((word & 0x000F000Fu) | 0x43004300u, zero_plus_128, scale);          // c0, c4
+  const uint32_t b = bf16x2_sub_mul(((word >> 4) & 0x000F000Fu) | 0x43004300u, zero_plus_128, scale);   // c1, c5
+  const uint32_t c = bf16x2_sub_mul(((word >> 8) & 0x000F000Fu) | 0x43004300u, zero_plus_128, scale);   // c2, c6
+  const uint32_t d = bf16x2_sub_mul(((word >> 12) & 0x000F000Fu) | 0x43004300u, zero_plus_128, scale);  // c3, c7
   uint4 o;
-  o.x = pack_bf16x2(f[0], f[1]);
-  o.y = pack_bf16x2(f[2], f[3]);
-  o.z = pack_bf16x2(f[4], f[5]);
-  o.w = pack_bf16x2(f[6], f[7]);
+  o.x = __byte_perm(a, b, 0x5410);  // c0, c1
+  o.y = __byte_perm(c, d, 0x5410);  // c2, c3
+  o.z = __byte_perm(a, b, 0x7632);  // c4, c5
+  o.w = __byte_perm(c, d, 0x7632);  // c6, c7
   return o;
 }
 
@@ -135,8 +145,10 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
         const uint4 codes = ahead[a];
         if (kb + WM_AHEAD < k_blocks) ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + kb + WM_AHEAD) * 8);
         const int g = ((kb_begin + kb) * WM_BK) / group;  // a 64-wide block never straddles a group
-        const float s = __bfloat162float(srow[g]);
-        const float z = static_cast<float>(zrow[g]);
+        const uint32_t s16 = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + g));
+        const uint32_t s = s16 | (s16 << 16);  // the group's bf16 scale in both halves
+        const uint32_t z16 = 0x4300u | static_cast<uint32_t>(zrow[g]);  // bf16 128 + zero (zero is 0..15)
+        const uint32_t z = z16 | (z16 << 16);
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
           ok = false;
           break;
