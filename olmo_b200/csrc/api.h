@@ -95,6 +95,12 @@ int ob_w4a16_dequant(const void* qweight, const void* scales, const void* zeros,
 // Fused dequantise -> tcgen05 GEMM for 1..256 activation rows (w4a16_mma.cu); `status` is the library's status word.
 int ob_w4a16_gemm_small_supported(int M, int N, int K, int group);
 int ob_w4a16_gemm_small_splits(int N, int K);
+// Single-token decode against preallocated key/value windows (decode.cu).
+int ob_decode_qkv(const void* qkv, const void* wq, const void* wk, const float* cos_t, const float* sin_t, const long long* rope_pos,
+                  const long long* write_col, void* q_out, void* k_cache, void* v_cache, int R, int Wq, int Wk, int hd, int window,
+                  int table_len, float eps, float clip, int qk_norm, int rope, cudaStream_t stream);
+int ob_decode_attention(const void* q, const void* k_cache, const void* v_cache, const void* bias, void* out, int R, int H, int Hkv, int hd,
+                        int window, int length, float scale, cudaStream_t stream);
 int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, float* partial, int M, int N,
                         int K, int group, int splits, int* status, cudaStream_t stream);
 int ob_gather_columns_bf16(const void* x, const int* perm, void* out, int M, int K, cudaStream_t stream);

@@ -341,3 +341,44 @@ def sumsq(g: torch.Tensor, out: torch.Tensor, accumulate: bool = False) -> torch
 
 def clip_coef(sumsq_t: torch.Tensor, max_norm: float, coef: torch.Tensor, norm_out: Optional[torch.Tensor] = None) -> None:
     check(lib().ob_clip_coef(ptr(sumsq_t), c_float(max_norm), ptr(coef), ptr(norm_out), stream_ptr()), "ob_clip_coef")
+
+
+# ------------------------------------------------------------------------------- decode (serving)
+
+
+def decode_qkv(
+    qkv: torch.Tensor, wq: Optional[torch.Tensor], wk: Optional[torch.Tensor], cos: torch.Tensor, sin: torch.Tensor,
+    rope_pos: torch.Tensor, write_col: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, Wq: int, Wk: int, hd: int,
+    eps: float, clip: float, qk_norm: bool, rope: bool, q_out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """One decode step's q/k/v post-processing: ``qkv [R, Wq + 2·Wk]`` -> rotated (and normalised) ``q [R, Wq]``; the new
+    key and value rows are written into ``k_cache`` / ``v_cache`` (``[R, Hkv, window, hd]``) at column ``write_col[0]``.
+    ``rope_pos [R]`` (int64) is each sequence's token index, ``cos`` / ``sin`` are fp32 ``[table_len, hd/2]``."""
+    _bf16(qkv, "qkv")
+    R = qkv.shape[0]
+    assert qkv.is_contiguous() and qkv.shape[1] == Wq + 2 * Wk and k_cache.is_contiguous() and v_cache.is_contiguous()
+    assert rope_pos.dtype == torch.int64 and write_col.dtype == torch.int64 and cos.dtype == torch.float32
+    q = torch.empty((R, Wq), dtype=torch.bfloat16, device=qkv.device) if q_out is None else q_out
+    check(lib().ob_decode_qkv(
+        ptr(qkv), ptr(wq), ptr(wk), ptr(cos), ptr(sin), ptr(rope_pos), ptr(write_col), ptr(q), ptr(k_cache), ptr(v_cache),
+        c_int(R), c_int(Wq), c_int(Wk), c_int(hd), c_int(k_cache.shape[2]), c_int(cos.shape[0]), c_float(eps), c_float(clip),
+        c_int(int(qk_norm)), c_int(int(rope)), stream_ptr(),
+    ), "ob_decode_qkv")
+    return q
+
+
+def decode_attention(
+    q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, bias: torch.Tensor, length: int, scale: float, n_heads: int,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """``softmax(q·Kᵀ·scale + bias)·V`` of one query per sequence over the first ``length`` columns of the windows.
+    ``q [R, H·128]``, caches ``[R, Hkv, window, 128]``, ``bias`` bf16 with ``R·window`` elements (additive)."""
+    _bf16(q, "q")
+    R, Hkv, window, hd = k_cache.shape
+    assert q.is_contiguous() and bias.dtype == torch.bfloat16 and bias.is_contiguous() and bias.numel() == R * window
+    o = torch.empty_like(q) if out is None else out
+    check(lib().ob_decode_attention(
+        ptr(q), ptr(k_cache), ptr(v_cache), ptr(bias), ptr(o), c_int(R), c_int(n_heads), c_int(Hkv), c_int(hd), c_int(window),
+        c_int(length), c_float(scale), stream_ptr(),
+    ), "ob_decode_attention")
+    return o

@@ -43,6 +43,7 @@ def main(argv=None) -> int:
     ap.add_argument("--kv-cache", choices=["auto", "static", "dynamic"], default="auto")
     ap.add_argument("--window", type=int, default=None, help="static mode: columns per row (default: prompt + completion, rounded up)")
     ap.add_argument("--no-graphs", action="store_true", help="static mode without CUDA graphs")
+    ap.add_argument("--no-decode-kernels", action="store_true", help="static mode with the module-level decode step")
     args = ap.parse_args(argv)
 
     import torch
@@ -66,7 +67,7 @@ def main(argv=None) -> int:
         quantize_model(model, [torch.full((1, 8), cfg.eos_token_id, device=device)], method="rtn")
     window = args.window or min(cfg.max_sequence_length, -(-(args.prompt_len + args.max_tokens + 1) // 128) * 128)
     engine = Engine(model, _IdTokenizer(), max_batch=args.max_batch, device=device, kv_cache=args.kv_cache, window=window,
-                    cuda_graphs=False if args.no_graphs else None)
+                    cuda_graphs=False if args.no_graphs else None, decode_kernels=False if args.no_decode_kernels else None)
     gen = torch.Generator().manual_seed(1)
     prompts = [torch.randint(2, cfg.vocab_size, (args.prompt_len,), generator=gen).tolist() for _ in range(args.requests)]
     params = SamplingParams(max_tokens=args.max_tokens, temperature=0.0, ignore_eos=True)
@@ -91,6 +92,7 @@ def main(argv=None) -> int:
         "prompt_len": args.prompt_len, "max_tokens": args.max_tokens, "seconds": elapsed,
         "kv_cache": "dynamic" if engine._static is None else "static", "cuda_graphs": bool(engine._static and engine._static.cuda_graphs),
         "graph_replays": 0 if engine._static is None else engine._static.graph_replays,
+        "decode_kernels": bool(engine._static and engine._static.fused),
         "ttft_median_s": ttft[len(ttft) // 2], "ttft_max_s": ttft[-1],
         "decode_tokens_per_second": engine.stats["decode_tokens"] / max(engine.stats["decode_seconds"], 1e-9),
         "decode_ms_per_step": 1e3 * engine.stats["decode_seconds"] / max(engine.stats["decode_steps"], 1),

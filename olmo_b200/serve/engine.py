@@ -111,11 +111,13 @@ class Engine:
     def __init__(
         self, model, tokenizer, max_batch: int = 32, device: Optional[torch.device] = None, kv_cache: str = "auto",
         window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None, max_queue: int = 0,
+        decode_kernels: Optional[bool] = None,
     ):
         """``kv_cache``: ``"static"`` decodes against preallocated windows with fixed shapes (CUDA graphs on a GPU;
         :mod:`olmo_b200.serve.static_cache`), ``"dynamic"`` concatenates caches through ``OLMo.forward``; ``"auto"``
         picks static on a GPU when the architecture allows it.  ``window`` bounds prompt + completion per request in
-        static mode (default: the model's context length)."""
+        static mode (default: the model's context length).  ``decode_kernels``: use this library's decode kernels in
+        static mode (default: whenever they cover the model; ``False`` keeps the module-level step)."""
         from .static_cache import StaticWindow, supports_static_window
 
         self.model = model.eval()
@@ -130,7 +132,8 @@ class Engine:
             raise ValueError("the static key/value window needs rotary position embeddings and ungrouped blocks")
         use_static = kv_cache == "static" or (kv_cache == "auto" and self.device.type == "cuda" and supports_static_window(self.config))
         self._static: Optional[StaticWindow] = (
-            StaticWindow(self.model, self.max_batch, window=window, bucket=bucket, cuda_graphs=cuda_graphs) if use_static else None
+            StaticWindow(self.model, self.max_batch, window=window, bucket=bucket, cuda_graphs=cuda_graphs, fused=decode_kernels)
+            if use_static else None
         )
         self._active: Optional[torch.Tensor] = None  # rows of the static window in the order of ``_rows``
         self.max_queue = max_queue  # 0 = unbounded; otherwise ``submit`` refuses when that many requests wait

@@ -31,7 +31,8 @@ def supports_static_window(config) -> bool:
 
 
 class StaticWindow:
-    def __init__(self, model, rows: int, window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None):
+    def __init__(self, model, rows: int, window: Optional[int] = None, bucket: int = 128, cuda_graphs: Optional[bool] = None,
+                 fused: Optional[bool] = None):
         cfg = model.config
         assert supports_static_window(cfg)
         self.model, self.config = model, cfg
@@ -54,6 +55,7 @@ class StaticWindow:
         self.cur = 0  # next write column
         self.used: List[bool] = [False] * rows
         self.first_col: List[int] = [0] * rows  # leftmost live column of each used row
+        self.fused = self._fused_ok() if fused is None else (fused and self._fused_ok())
         self._graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
         self._pool = None
         self.graph_replays = 0
@@ -139,7 +141,56 @@ class StaticWindow:
         return rows
 
     # ---------------------------------------------------------------------------------- decode
+    def _fused_ok(self) -> bool:
+        """The decode kernels of this library cover bf16 models of the architectures the fused training path covers,
+        with head dimension 128 (every released OLMo model)."""
+        from ..ops import enabled
+        from ..ops import fused_block as fb
+
+        cfg = self.config
+        return (
+            self.device.type == "cuda" and enabled() and self.dtype == torch.bfloat16 and fb.config_supported(cfg)
+            and cfg.d_model // cfg.n_heads == 128 and not cfg.embedding_layer_norm
+        )
+
+    def _forward_fused(self, length: int) -> None:
+        """The step as a short chain of kernels per block: projection, one kernel for QK-norm + rotary + cache write,
+        one attention kernel over the window, projection, norm(+residual), projection, SwiGLU, projection,
+        norm(+residual).  The projections go through the block's own modules, so dense and 4-bit weights both work."""
+        from ..ops import fused_block as fb
+        from ..ops import kernels as k
+
+        cfg, t = self.config, self.model.transformer
+        spec = fb.spec_from_config(cfg)
+        cos, sin = fb.rope_tables(cfg.max_sequence_length, spec.head_dim, float(cfg.rope_theta), self.device)
+        scale = 1.0 / (spec.head_dim ** 0.5)
+        bias = self.bias.view(self.rows, self.window)
+
+        def w(norm):
+            return None if norm is None else norm.weight
+
+        x = t.wte(self.tokens).view(self.rows, cfg.d_model)
+        for layer, block in enumerate(t.blocks):
+            h = x if spec.norm_after else k.norm_fwd(x, w(block.attn_norm), None, spec.eps, spec.rms, save_stats=False)[0]
+            qkv = block.att_proj(h)
+            q = k.decode_qkv(qkv, w(block.q_norm), w(block.k_norm), cos, sin, self.rope_pos, self.pos, self.k[layer], self.v[layer],
+                             spec.Wq, spec.Wk, spec.head_dim, spec.eps, spec.clip_qkv, spec.qk_norm, spec.rope)
+            o = k.decode_attention(q, self.k[layer], self.v[layer], bias, length, scale, spec.n_heads)
+            a = block.attn_out(o)
+            if spec.norm_after:
+                x1 = k.norm_fwd(a, w(block.attn_norm), None, spec.eps, spec.rms, residual=x, save_stats=False)[0]
+                f = block.ff_out(k.swiglu_fwd(block.ff_proj(x1)))
+                x = k.norm_fwd(f, w(block.ff_norm), None, spec.eps, spec.rms, residual=x1, save_stats=False)[0]
+            else:
+                x1 = x + a
+                h2 = k.norm_fwd(x1, w(block.ff_norm), None, spec.eps, spec.rms, save_stats=False)[0]
+                x = x1 + block.ff_out(k.swiglu_fwd(block.ff_proj(h2)))
+        x = t.ln_f(x)
+        self.logits.copy_(self.model.output_projection(x))
+
     def _forward(self, length: int) -> None:
+        if self.fused:
+            return self._forward_fused(length)
         t = self.model.transformer
         x = t.wte(self.tokens)
         if self.config.embedding_layer_norm:

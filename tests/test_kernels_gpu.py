@@ -384,3 +384,67 @@ def test_native_attention_packed_sequences(H, Hkv):
     v1[:300] -= 1.0
     out1 = A.varlen_attention(q1, k1, v1, cu, 724, causal=True)
     assert torch.equal(out1[301:1024], got[0][301:1024].detach())
+
+
+@pytest.mark.parametrize("qk_norm,clip,Hkv", [(True, 0.0, 4), (False, 1.5, 4), (True, 0.0, 2)])
+def test_decode_qkv_kernel(qk_norm, clip, Hkv):
+    """QK-norm + rotary + cache write of one decode step against the same arithmetic in fp32 PyTorch."""
+    from olmo_b200.ops import kernels as k
+    from olmo_b200.ops.fused_block import rope_tables
+
+    R, H, hd, window, T = 5, 4, 128, 40, 64
+    Wq, Wk = H * hd, Hkv * hd
+    qkv = _rand(R, Wq + 2 * Wk)
+    wq, wk = (_rand(Wq) * 0.1 + 1.0), (_rand(Wk) * 0.1 + 1.0)
+    cos, sin = rope_tables(T, hd, 10000.0, torch.device("cuda"))
+    rope_pos = torch.tensor([0, 3, 17, 63, 200], device="cuda")  # the last one is clamped to the table
+    col = torch.tensor([7], device="cuda")
+    kc = torch.full((R, Hkv, window, hd), 9.0, device="cuda", dtype=torch.bfloat16)
+    vc = torch.full((R, Hkv, window, hd), 9.0, device="cuda", dtype=torch.bfloat16)
+    q = k.decode_qkv(qkv, wq if qk_norm else None, wk if qk_norm else None, cos, sin, rope_pos, col, kc, vc, Wq, Wk, hd, 1e-6, clip, qk_norm, True)
+
+    x = qkv.float()
+    if clip > 0:
+        x = x.clamp(-clip, clip)
+    qf, kf, vf = x[:, :Wq], x[:, Wq : Wq + Wk], x[:, Wq + Wk :]
+    if qk_norm:
+        qf = qf * torch.rsqrt(qf.pow(2).mean(-1, keepdim=True) + 1e-6) * wq.float()
+        kf = kf * torch.rsqrt(kf.pow(2).mean(-1, keepdim=True) + 1e-6) * wk.float()
+    tok = rope_pos.clamp(max=T - 1)
+    c = torch.cat((cos[tok], cos[tok]), -1)[:, None, :]
+    s = torch.cat((sin[tok], sin[tok]), -1)[:, None, :]
+
+    def rot(t, heads):
+        t = t.view(R, heads, hd)
+        a, b = t.chunk(2, dim=-1)
+        return (t * c + torch.cat((-b, a), -1) * s).reshape(R, heads * hd)
+
+    _close(q, rot(qf, H), rtol=2e-2, atol=2e-2)
+    _close(kc[:, :, 7, :].reshape(R, Wk), rot(kf, Hkv), rtol=2e-2, atol=2e-2)
+    _close(vc[:, :, 7, :].reshape(R, Wk), vf, rtol=1e-2, atol=1e-2)
+    untouched = torch.ones(window, dtype=torch.bool, device="cuda")
+    untouched[7] = False
+    assert bool((kc[:, :, untouched] == 9.0).all()) and bool((vc[:, :, untouched] == 9.0).all())
+
+
+@pytest.mark.parametrize("H,Hkv,length", [(4, 4, 128), (8, 2, 37), (2, 1, 3)])
+def test_decode_attention_kernel(H, Hkv, length):
+    """One query per sequence over a masked key/value window against softmax attention in fp32."""
+    from olmo_b200.ops import kernels as k
+
+    R, hd, window = 6, 128, 160
+    q = _rand(R, H * hd)
+    kc, vc = _rand(R, Hkv, window, hd), _rand(R, Hkv, window, hd)
+    floor = torch.finfo(torch.bfloat16).min
+    bias = torch.full((R, window), floor, device="cuda", dtype=torch.bfloat16)
+    for r in range(R - 1):  # row r sees a right-aligned stretch of the first `length` columns; the last row is idle
+        first = (r * 7) % length
+        bias[r, first:length] = 0.0
+    out = k.decode_attention(q, kc, vc, bias, length, 1.0 / math.sqrt(hd), H)
+    assert torch.isfinite(out.float()).all()
+    g = H // Hkv
+    kf = kc[:, :, :length].float().repeat_interleave(g, dim=1)
+    vf = vc[:, :, :length].float().repeat_interleave(g, dim=1)
+    scores = torch.einsum("rhd,rhjd->rhj", q.float().view(R, H, hd), kf) / math.sqrt(hd) + bias[:, None, :length].float()
+    want = torch.einsum("rhj,rhjd->rhd", torch.softmax(scores, dim=-1), vf).reshape(R, H * hd)
+    _close(out[: R - 1], want[: R - 1], rtol=2e-2, atol=2e-2)

@@ -391,3 +391,37 @@ def test_cancellation_and_queue_limit():
     assert running.finish_reason == "cancelled" and 0 < len(running.token_ids) < 30
     engine.run_until_idle()
     assert waiting[1].finish_reason == "length" and waiting[1].token_ids == greedy_reference_no_eos(model, PROMPTS[2], 29)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("variant", [dict(attention_layer_norm=True, norm_after=True), dict(layer_norm_type=LayerNormType.default, layer_norm_with_affine=False, clip_qkv=4.0), dict(n_kv_heads=1, attention_layer_norm=True, norm_after=True)])
+def test_decode_kernels_match_the_module_level_step(variant):
+    """One decode step on identical window state: this library's decode kernels against the module-level step (bf16)."""
+    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, **variant).to(torch.bfloat16).cuda()
+    engine = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=False)
+    window = engine._static
+    assert window.fused
+    for p in PROMPTS[:3]:
+        engine.submit(p, SamplingParams(max_tokens=8, temperature=0.0, ignore_eos=True))
+    engine.step()  # prefill: three rows live, one idle
+    engine.step()  # one decode step, so the window holds keys written by the decode kernels too
+    active = torch.tensor([r._row for r in engine._rows], device="cuda")
+    fused = window.decode(active).index_select(0, active).clone()
+    window.fused = False
+    plain = window.decode(active).index_select(0, active).clone()  # same column, same tokens: the step is idempotent
+    window.fused = True
+    assert torch.isfinite(fused).all()
+    torch.testing.assert_close(fused, plain, rtol=5e-2, atol=5e-2)
+    assert (fused.argmax(-1) == plain.argmax(-1)).float().mean() >= 0.66
+    engine.run_until_idle()
+
+
+@pytest.mark.gpu
+def test_decode_kernels_under_cuda_graphs_generate_the_same_tokens():
+    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, attention_layer_norm=True, norm_after=True).to(torch.bfloat16).cuda()
+    params = SamplingParams(max_tokens=12, temperature=0.0, ignore_eos=True)
+    eager = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=False).generate(PROMPTS, params)
+    engine = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=True)
+    graphed = engine.generate(PROMPTS, params)
+    assert engine._static.fused and engine._static.graph_replays == engine.stats["decode_steps"] > 0
+    assert [r.token_ids for r in graphed] == [r.token_ids for r in eager]  # same kernels, same inputs, replayed
