@@ -17,7 +17,8 @@
 //               stores are contiguous.
 //   warp 8      TMA producer of the activation tile (MB x 64, rows beyond M are zero-filled by the copy engine)
 //   warp 9      MMA issuer (one lane), owns the TMEM allocation
-// A stage is full when 256 dequantising threads and the TMA transaction have arrived; it is released by tcgen05.commit.
+// A stage is full when the eight dequantising warps (one arrival each, after a warp-wide sync) and the TMA transaction
+// have arrived; it is released by tcgen05.commit.
 // With K splits (chosen when there are too few 128-feature tiles to fill the GPU) every CTA covers a range of K blocks
 // and adds its partial result to a zeroed fp32 workspace, which the caller converts to bf16.
 // Every wait is bounded and reports through the status word; an aborting CTA still releases its TMEM.
@@ -102,7 +103,7 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < WM_STAGES; ++s) {
-      mbar_init(&full_bar[s], WM_DEQ_THREADS + 1);  // dequantising threads + the TMA producer's expect_tx arrival
+      mbar_init(&full_bar[s], WM_DEQ_THREADS / 32 + 1);  // one arrival per dequantising warp + the TMA producer's expect_tx
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(done_bar, 1);
@@ -149,7 +150,8 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
         const uint32_t s = s16 | (s16 << 16);  // the group's bf16 scale in both halves
         const uint32_t z16 = 0x4300u | static_cast<uint32_t>(zrow[g]);  // bf16 128 + zero (zero is 0..15)
         const uint32_t z = z16 | (z16 << 16);
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER)) {
+        // the warp decides together: the arrival below is made by one lane on behalf of all 32
+        if (!__all_sync(0xffffffffu, mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER))) {
           ok = false;
           break;
         }
@@ -161,7 +163,8 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
           *reinterpret_cast<uint4*>(row + ((chunk ^ sw) << 4)) = dequant_word(words[c], z, s);
         }
         fence_proxy_async();  // generic-proxy stores -> visible to the tensor core's reads
-        mbar_arrive(&full_bar[stage]);
+        __syncwarp();         // every lane's stores and fence precede the warp's single arrival
+        if (lane == 0) mbar_arrive(&full_bar[stage]);
         if (++stage == WM_STAGES) {
           stage = 0;
           phase ^= 1u;

@@ -397,7 +397,8 @@ def test_cancellation_and_queue_limit():
 @pytest.mark.parametrize("variant", [dict(attention_layer_norm=True, norm_after=True), dict(layer_norm_type=LayerNormType.default, layer_norm_with_affine=False, clip_qkv=4.0), dict(n_kv_heads=1, attention_layer_norm=True, norm_after=True)])
 def test_decode_kernels_match_the_module_level_step(variant):
     """One decode step on identical window state: this library's decode kernels against the module-level step (bf16)."""
-    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, **variant).to(torch.bfloat16).cuda()
+    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, attention_dropout=0.0, residual_dropout=0.0, embedding_dropout=0.0,
+                       **variant).to(torch.bfloat16).cuda()
     engine = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=False)
     window = engine._static
     assert window.fused
@@ -418,7 +419,8 @@ def test_decode_kernels_match_the_module_level_step(variant):
 
 @pytest.mark.gpu
 def test_decode_kernels_under_cuda_graphs_generate_the_same_tokens():
-    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, attention_layer_norm=True, norm_after=True).to(torch.bfloat16).cuda()
+    model = tiny_model(d_model=256, n_heads=2, mlp_hidden_size=512, attention_layer_norm=True, norm_after=True, attention_dropout=0.0,
+                       residual_dropout=0.0, embedding_dropout=0.0).to(torch.bfloat16).cuda()
     params = SamplingParams(max_tokens=12, temperature=0.0, ignore_eos=True)
     eager = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=False).generate(PROMPTS, params)
     engine = Engine(model, CharTokenizer(), max_batch=4, kv_cache="static", bucket=16, cuda_graphs=True)
