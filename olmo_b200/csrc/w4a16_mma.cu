@@ -24,6 +24,8 @@
 // Every wait is bounded and reports through the status word; an aborting CTA still releases its TMEM.
 //
 // Counterpart in the reference's vendored AutoGPTQ: the Triton quant_matmul kernel (tensor-core path for batches).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "api.h"
 
@@ -288,10 +290,16 @@ int ob_w4a16_gemm_small_supported(int M, int N, int K, int group) {
 // splits to reach about one CTA per SM, each split keeping at least eight K blocks.  With more than one split the caller
 // passes a zeroed fp32 [M, N] workspace and converts it to bf16 afterwards.
 int ob_w4a16_gemm_small_splits(int N, int K) {
+  static int target = 0;  // CTAs the launch should reach; OLMO_B200_W4_TARGET_CTAS overrides the default of one per SM
+  if (target == 0) {
+    const char* env = getenv("OLMO_B200_W4_TARGET_CTAS");
+    target = env != nullptr ? atoi(env) : 148;
+    if (target < 1) target = 148;
+  }
   const int tiles = N / ob::WM_ROWS;
   const int k_blocks = K / ob::WM_BK;
-  if (tiles <= 0 || k_blocks <= 0 || tiles >= 120) return 1;
-  int splits = (148 + tiles - 1) / tiles;
+  if (tiles <= 0 || k_blocks <= 0 || tiles * 5 >= target * 4) return 1;
+  int splits = (target + tiles - 1) / tiles;
   if (splits > k_blocks / 8) splits = k_blocks / 8;
   if (splits < 1) splits = 1;
   const int per = (k_blocks + splits - 1) / splits;
