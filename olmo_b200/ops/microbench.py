@@ -179,13 +179,48 @@ def bench_optim(args) -> None:
     print(f"adamw {n} params: {ms:.3f} ms  {gbs:.0f} GB/s" + (f" ({gbs / bw:.2f} of measured copy bandwidth)" if bw else ""))
 
 
+def bench_decode(args) -> None:
+    """Serving kernels at OLMo-2 7B shapes, 32 sequences: the 4-bit GEMM with fused dequantisation (ff_proj: 22016 x 4096),
+    the q/k/v post-processing kernel and the window attention kernel (256 of 512 columns live)."""
+    from ..inference.w4a16 import QuantLinear
+
+    bw = _peaks().get("hbm_gbs")
+    R, d, H, hd, hidden, window, length = 32, 4096, 32, 128, 22016, 512, 256
+    torch.manual_seed(0)
+    ql = QuantLinear.from_linear_rtn(torch.nn.Linear(d, hidden, bias=False), group=128).cuda()
+    x = torch.randn(R, d, device="cuda", dtype=torch.bfloat16)
+    cases = {"w4a16 fused gemm 32x22016x4096": (lambda: ql(x), hidden * d // 2 + hidden * (d // 128) * 3)}
+    qkv = torch.randn(R, 3 * d, device="cuda", dtype=torch.bfloat16)
+    wn = torch.ones(d, device="cuda", dtype=torch.bfloat16)
+    from .fused_block import rope_tables
+
+    cos, sin = rope_tables(4096, hd, 500000.0, torch.device("cuda"))
+    kc = torch.randn(R, H, window, hd, device="cuda", dtype=torch.bfloat16)
+    vc = torch.randn(R, H, window, hd, device="cuda", dtype=torch.bfloat16)
+    rope_pos = torch.arange(R, device="cuda") + 200
+    col = torch.tensor([length - 1], device="cuda")
+    bias = torch.zeros(R, window, device="cuda", dtype=torch.bfloat16)
+    cases["decode qkv (qk-norm + rope + cache write) 32x12288"] = (
+        lambda: k.decode_qkv(qkv, wn, wn, cos, sin, rope_pos, col, kc, vc, d, d, hd, 1e-6, 0.0, True, True), R * 3 * d * 2 * 2)
+    q = torch.randn(R, d, device="cuda", dtype=torch.bfloat16)
+    cases["decode attention 32 seqs x 32 heads x 256 columns"] = (
+        lambda: k.decode_attention(q, kc, vc, bias, length, hd ** -0.5, H), 2 * R * H * length * hd * 2)
+    for name, (fn, nbytes) in cases.items():
+        if args.once:
+            fn()
+            continue
+        ms = timeit(fn)
+        gbs = nbytes / ms / 1e6
+        print(f"{name}: {ms * 1e3:.1f} us  {gbs:.0f} GB/s" + (f" ({gbs / bw:.2f} of measured copy bandwidth)" if bw else ""))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attention", "norm", "ce", "optim", "all"])
+    ap.add_argument("what", choices=["gemm", "attention", "norm", "ce", "optim", "decode", "all"])
     ap.add_argument("--small", action="store_true", help="small case (for profiler captures)")
     ap.add_argument("--once", action="store_true", help="launch without timing (for profiler captures)")
     args = ap.parse_args()
-    table = {"gemm": bench_gemm, "attention": bench_attention, "norm": bench_norm, "ce": bench_ce, "optim": bench_optim}
+    table = {"gemm": bench_gemm, "attention": bench_attention, "norm": bench_norm, "ce": bench_ce, "optim": bench_optim, "decode": bench_decode}
     for name, fn in table.items():
         if args.what in (name, "all"):
             fn(args)
