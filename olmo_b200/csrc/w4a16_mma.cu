@@ -81,7 +81,7 @@ __device__ __forceinline__ uint4 dequant_word(uint32_t word, uint32_t zero_plus_
 }
 
 template <int MB>
-__global__ void __launch_bounds__(WM_THREADS)
+__global__ void __launch_bounds__(WM_THREADS, 2)
 w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __restrict__ qweight, const bf16* __restrict__ scales,
                  const uint8_t* __restrict__ zeros, bf16* __restrict__ y, float* __restrict__ partial, int M, int N, int K, int group,
                  int blocks_per_split, int* __restrict__ status) {
@@ -136,9 +136,17 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
     uint32_t phase = 0;
     bool ok = true;
     uint4 ahead[WM_AHEAD];
+    uint32_t ahead_sz[WM_AHEAD];  // the block's group scale (bf16 bits) and zero point, fetched with the codes
+    auto load_sz = [&](int kb_abs) -> uint32_t {
+      const int g = (kb_abs * WM_BK) / group;  // a 64-wide block never straddles a group
+      return static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + g)) | (static_cast<uint32_t>(zrow[g]) << 16);
+    };
 #pragma unroll
     for (int a = 0; a < WM_AHEAD; ++a) {
-      if (a < k_blocks) ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + a) * 8);
+      if (a < k_blocks) {
+        ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + a) * 8);
+        ahead_sz[a] = load_sz(kb_begin + a);
+      }
     }
     for (int kb0 = 0; kb0 < k_blocks && ok; kb0 += WM_AHEAD) {
 #pragma unroll
@@ -146,11 +154,14 @@ w4a16_mma_kernel(const __grid_constant__ CUtensorMap tma_x, const uint32_t* __re
         const int kb = kb0 + a;
         if (kb >= k_blocks) break;
         const uint4 codes = ahead[a];
-        if (kb + WM_AHEAD < k_blocks) ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + kb + WM_AHEAD) * 8);
-        const int g = ((kb_begin + kb) * WM_BK) / group;  // a 64-wide block never straddles a group
-        const uint32_t s16 = static_cast<uint32_t>(*reinterpret_cast<const uint16_t*>(srow + g));
+        const uint32_t sz = ahead_sz[a];
+        if (kb + WM_AHEAD < k_blocks) {
+          ahead[a] = ldg_stream_v4(wrow + static_cast<size_t>(kb_begin + kb + WM_AHEAD) * 8);
+          ahead_sz[a] = load_sz(kb_begin + kb + WM_AHEAD);
+        }
+        const uint32_t s16 = sz & 0xFFFFu;
         const uint32_t s = s16 | (s16 << 16);  // the group's bf16 scale in both halves
-        const uint32_t z16 = 0x4300u | static_cast<uint32_t>(zrow[g]);  // bf16 128 + zero (zero is 0..15)
+        const uint32_t z16 = 0x4300u | (sz >> 16);  // bf16 128 + zero (zero is 0..15)
         const uint32_t z = z16 | (z16 << 16);
         // the warp decides together: the arrival below is made by one lane on behalf of all 32
         if (!__all_sync(0xffffffffu, mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, status, ST_TIMEOUT_PRODUCER))) {
