@@ -5,9 +5,9 @@
 //                     their full widths (the OLMo-2 "QK-norm"), rotary embedding of q and k at the sequence's own token
 //                     index, q written out, the new key and value written into the window at the shared write column.
 //   decode_attention  one CTA per (query head, sequence): softmax(q·Kᵀ·scale + bias)·V over the first `length` columns of
-//                     the window; keys are stored already rotated.  Each warp streams every eighth column with one
+//                     the window; keys are stored already rotated.  Each warp streams every fourth column with one
 //                     coalesced 256-byte load per key and per value, keeps a running (max, sum, output) triple, and the
-//                     eight warps are merged through shared memory.  Grouped-query attention reads the shared key head.
+//                     four warps are merged through shared memory.  Grouped-query attention reads the shared key head.
 //
 // Everything that changes from step to step (write column, per-sequence token index, bias) is read from device memory, so
 // a captured CUDA graph of the step can be replayed.  Indices read from memory are clamped before use.
@@ -18,7 +18,7 @@ namespace ob {
 namespace {
 
 constexpr int DQ_THREADS = 256;
-constexpr int DA_WARPS = 8;
+constexpr int DA_WARPS = 4;  // eight warps per CTA measured no faster (48 vs 45 us at 32 x 32 x 256)
 constexpr int DA_HD = 128;
 
 __device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
