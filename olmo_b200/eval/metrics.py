@@ -4,7 +4,6 @@ reference uses ``torchmetrics``; ``olmo/eval/downstream.py:28-165``, ``olmo/eval
 """
 from __future__ import annotations
 
-import math
 from typing import Any, Dict, List, Optional, Tuple
 
 import torch

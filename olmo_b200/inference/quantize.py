@@ -11,7 +11,6 @@ see.  Reference counterpart: ``inference/compression/run_quantization.py`` + ``o
 from __future__ import annotations
 
 import logging
-import math
 from typing import Any, Dict, Iterable, List, Optional, Sequence, Tuple
 
 import torch

@@ -7,7 +7,7 @@ math every sm_100a kernel is tested against.  Math follows the reference's ``olm
 from __future__ import annotations
 
 import math
-from typing import Dict, Optional, Tuple
+from typing import Optional, Tuple
 
 import torch
 import torch.nn as nn

@@ -22,7 +22,6 @@ import time
 import warnings
 from datetime import datetime
 from enum import Enum
-from itertools import cycle, islice
 from pathlib import Path
 from queue import Queue
 from threading import Thread

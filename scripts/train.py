@@ -13,7 +13,6 @@ import os
 import sys
 from datetime import timedelta
 from pathlib import Path
-from typing import Optional
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
