@@ -147,34 +147,48 @@ decode_attention_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k_c
     qv[0] = a.x * scale; qv[1] = a.y * scale; qv[2] = b.x * scale; qv[3] = b.y * scale;
   }
   float m = -INFINITY, l = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int j0 = warp; j0 < length; j0 += DA_WARPS * 2) {  // two columns per iteration for independent reductions
-    const int j1 = j0 + DA_WARPS;
-    const bool two = j1 < length;
-    const uint2 ku0 = *reinterpret_cast<const uint2*>(kbase + static_cast<size_t>(j0) * DA_HD + lane * 4);
-    const uint2 ku1 = two ? *reinterpret_cast<const uint2*>(kbase + static_cast<size_t>(j1) * DA_HD + lane * 4) : make_uint2(0u, 0u);
-    const uint2 vu0 = *reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(j0) * DA_HD + lane * 4);
-    const uint2 vu1 = two ? *reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(j1) * DA_HD + lane * 4) : make_uint2(0u, 0u);
-    float2 a = unpack_bf16x2(ku0.x), b = unpack_bf16x2(ku0.y);
-    float s0 = qv[0] * a.x + qv[1] * a.y + qv[2] * b.x + qv[3] * b.y;
-    a = unpack_bf16x2(ku1.x); b = unpack_bf16x2(ku1.y);
-    float s1 = qv[0] * a.x + qv[1] * a.y + qv[2] * b.x + qv[3] * b.y;
+  constexpr int COLS = 4;  // columns per iteration: eight independent 256-byte loads in flight per warp
+  for (int j0 = warp; j0 < length; j0 += DA_WARPS * COLS) {
+    uint2 ku[COLS], vu[COLS];
+    bool live[COLS];
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
+      const int j = j0 + c * DA_WARPS;
+      live[c] = j < length;
+      ku[c] = live[c] ? *reinterpret_cast<const uint2*>(kbase + static_cast<size_t>(j) * DA_HD + lane * 4) : make_uint2(0u, 0u);
+      vu[c] = live[c] ? *reinterpret_cast<const uint2*>(vbase + static_cast<size_t>(j) * DA_HD + lane * 4) : make_uint2(0u, 0u);
+    }
+    float s[COLS];
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
+      const float2 a = unpack_bf16x2(ku[c].x), b = unpack_bf16x2(ku[c].y);
+      s[c] = qv[0] * a.x + qv[1] * a.y + qv[2] * b.x + qv[3] * b.y;
+    }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
-      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+#pragma unroll
+      for (int c = 0; c < COLS; ++c) s[c] += __shfl_xor_sync(0xffffffffu, s[c], o);
     }
-    s0 += __bfloat162float(brow[j0]);
-    s1 = two ? s1 + __bfloat162float(brow[j1]) : -INFINITY;
-    const float m_new = fmaxf(m, fmaxf(s0, s1));
-    const float corr = __expf(m - m_new);  // 0 on the first iteration (m = -inf)
-    const float p0 = __expf(s0 - m_new), p1 = __expf(s1 - m_new);
-    l = l * corr + p0 + p1;
-    a = unpack_bf16x2(vu0.x); b = unpack_bf16x2(vu0.y);
-    const float2 c = unpack_bf16x2(vu1.x), d = unpack_bf16x2(vu1.y);
-    acc[0] = acc[0] * corr + p0 * a.x + p1 * c.x;
-    acc[1] = acc[1] * corr + p0 * a.y + p1 * c.y;
-    acc[2] = acc[2] * corr + p0 * b.x + p1 * d.x;
-    acc[3] = acc[3] * corr + p0 * b.y + p1 * d.y;
+    float m_new = m;
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
+      s[c] = live[c] ? s[c] + __bfloat162float(brow[j0 + c * DA_WARPS]) : -INFINITY;
+      m_new = fmaxf(m_new, s[c]);
+    }
+    const float corr = __expf(m - m_new);  // 0 on the first iteration (m = -inf); column j0 is always live, so m_new is finite
+    l *= corr;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] *= corr;
+#pragma unroll
+    for (int c = 0; c < COLS; ++c) {
+      const float p = __expf(s[c] - m_new);
+      const float2 a = unpack_bf16x2(vu[c].x), b = unpack_bf16x2(vu[c].y);
+      l += p;
+      acc[0] += p * a.x;
+      acc[1] += p * a.y;
+      acc[2] += p * b.x;
+      acc[3] += p * b.y;
+    }
     m = m_new;
   }
   if (lane == 0) {
