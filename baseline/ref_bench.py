@@ -29,7 +29,7 @@ def _unavailable(reason: str) -> dict:
 def run_reference(args, presets) -> dict:
     ref_root = HERE / "_ref"
     if not (ref_root / "olmo" / "model.py").is_file():
-        return _unavailable("baseline/_ref is missing: install it with pip --no-deps --target baseline/_ref /root/reference")
+        return _unavailable("baseline/_ref is missing: install the reference there with pip --no-index --no-deps --target baseline/_ref <reference checkout>")
     sys.path.insert(0, str(ref_root))
     sys.path.insert(0, str(HERE / "shims"))
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
