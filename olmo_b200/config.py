@@ -672,6 +672,15 @@ class B200Runtime:
     ``OLMO_B200_WAIT_BUDGET``    iteration budget of every device-side bounded wait.
     ``OLMO_B200_ATTENTION``      ``native`` (tcgen05 kernel) or ``library`` (flash-attn package).
     ``OLMO_B200_GEMM_2CTA``      use the two-CTA ``cta_group::2`` GEMM kernel (default on).
+    ``OLMO_B200_KEEP_ACTS``      ``auto`` (default), ``1`` or ``0``: keep the rotated q/k and SwiGLU outputs of every
+                                 block for the backward pass instead of recomputing them; ``auto`` decides after the
+                                 first step from the device memory still free (read in ``parallel/fsdp.py``).
+    ``OLMO_B200_COMM_CTAS``, ``OLMO_B200_RS_CTAS``, ``OLMO_B200_RS_SUMSQ``   communication CTAs riding on GEMM launches
+                                 for the all-gather / reduce-scatter and the fused gradient-norm partials
+                                 (read in ``parallel/peer.py``).
+    ``OLMO_B200_HEAD_CHUNK``     rows of logits materialised at a time by the LM-head + loss path (default 8192).
+    ``OLMO_B200_NVTX``           ``1`` adds NVTX spans around trainer phases and every block's forward / backward.
+    ``OLMO_B200_W4_TARGET_CTAS`` CTAs the 4-bit decode GEMM aims at when it splits K (default 444).
     """
 
     kernels: bool = True
