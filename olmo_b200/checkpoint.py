@@ -223,9 +223,9 @@ class FullCheckpointer(Checkpointer):
                             shard[a : a + st[key].numel()].copy_(st[key].reshape(-1))
                     full = engine.full_tensor(unit, shard)
                     if keep:
+                        # every slot gets the key; slots that never received state on any rank are dropped below
                         for s in unit.slots:
-                            if any(key in by_name.get(s.name, {}) for _ in (0,)) or True:
-                                state.setdefault(s.name, {})[key] = full[s.offset : s.offset + s.numel].view(s.shape).cpu().clone()
+                            state.setdefault(s.name, {})[key] = full[s.offset : s.offset + s.numel].view(s.shape).cpu().clone()
                     del full, shard
             if keep:
                 for name, st in by_name.items():
