@@ -281,10 +281,7 @@ def test_meta_device_and_compatibility_of_old_state_dicts():
     assert all(p.is_meta for p in m.parameters())
     live = make(layer_norm_with_affine=True)
     sd = live.state_dict()
-    old = {}
-    for k, v in sd.items():
-        k = k.replace(".attn_norm.", ".norm.") if False else k
-        old[k] = v
+    old = dict(sd)
     # checkpoints older than the attn_norm/ff_norm split stored one ``norm`` per block
     for i in range(2):
         old[f"transformer.blocks.{i}.norm.weight"] = old.pop(f"transformer.blocks.{i}.attn_norm.weight")
