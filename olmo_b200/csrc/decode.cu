@@ -1,7 +1,7 @@
 // Single-token decode step against preallocated key/value windows (serving): two bandwidth-bound kernels that replace the
 // dozens of small element-wise launches a module-level decode step makes per block.
 //
-//   decode_qkv        one CTA per sequence: optional clip of the fused q|k|v projection, optional RMS norm of q and k over
+//   decode_qkv        two CTAs per sequence (query; key and value): optional clip of the fused q|k|v projection, optional RMS norm of q and k over
 //                     their full widths (the OLMo-2 "QK-norm"), rotary embedding of q and k at the sequence's own token
 //                     index, q written out, the new key and value written into the window at the shared write column.
 //   decode_attention  one CTA per (query head, sequence): softmax(q·Kᵀ·scale + bias)·V over the first `length` columns of
@@ -42,59 +42,59 @@ __device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
 }
 
 // qkv [R, Wq + 2 Wk]; q_out [R, Wq]; caches [R, Hkv, window, hd]; cos/sin [table_len, hd/2] fp32.
+// Grid (R, 2): CTA (r, 0) handles the query of sequence r, CTA (r, 1) its key and value, so the two row reductions of
+// the QK-norm run side by side.
 __global__ void __launch_bounds__(DQ_THREADS)
 decode_qkv_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ wq, const bf16* __restrict__ wk, const float* __restrict__ cos_t,
                   const float* __restrict__ sin_t, const long long* __restrict__ rope_pos, const long long* __restrict__ write_col,
                   bf16* __restrict__ q_out, bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int Wq, int Wk, int hd, int window,
                   int table_len, float eps, float clip, int qk_norm, int rope) {
-  extern __shared__ float row[];  // Wq + Wk floats: q then k, after the optional clip
+  extern __shared__ float row[];  // max(Wq, Wk) floats: this CTA's vector after the optional clip
   __shared__ float scratch[32];
   const int r = blockIdx.x;
-  const bf16* src = qkv + static_cast<size_t>(r) * (Wq + 2 * Wk);
+  const bool is_q = blockIdx.y == 0;
+  const int width = is_q ? Wq : Wk;
+  const bf16* src = qkv + static_cast<size_t>(r) * (Wq + 2 * Wk) + (is_q ? 0 : Wq);
+  const bf16* w = is_q ? wq : wk;
   const int col = static_cast<int>(min(max(write_col[0], 0LL), static_cast<long long>(window - 1)));
   const int tok = static_cast<int>(min(max(rope_pos[r], 0LL), static_cast<long long>(table_len - 1)));
   const int hkv = Wk / hd;
   const int half = hd >> 1;
 
-  float ss_q = 0.f, ss_k = 0.f;
-  for (int c = threadIdx.x; c < (Wq + Wk) / 8; c += DQ_THREADS) {
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < width / 8; c += DQ_THREADS) {
     float f[8];
     load8(src + c * 8, f);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (clip > 0.f) f[i] = fminf(fmaxf(f[i], -clip), clip);
       row[c * 8 + i] = f[i];
-      if (c * 8 < Wq) ss_q += f[i] * f[i]; else ss_k += f[i] * f[i];
+      ss += f[i] * f[i];
     }
   }
-  // the value goes to the window as it is (clipped): [r, head, col, :]
-  for (int c = threadIdx.x; c < Wk / 8; c += DQ_THREADS) {
-    float f[8];
-    load8(src + Wq + Wk + c * 8, f);
-    if (clip > 0.f) {
+  if (!is_q) {  // the value goes to the window as it is (clipped): [r, head, col, :]
+    for (int c = threadIdx.x; c < Wk / 8; c += DQ_THREADS) {
+      float f[8];
+      load8(src + Wk + c * 8, f);
+      if (clip > 0.f) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) f[i] = fminf(fmaxf(f[i], -clip), clip);
+        for (int i = 0; i < 8; ++i) f[i] = fminf(fmaxf(f[i], -clip), clip);
+      }
+      const int e = c * 8, head = e / hd, d = e % hd;
+      store8(v_cache + ((static_cast<size_t>(r) * hkv + head) * window + col) * hd + d, f);
     }
-    const int e = c * 8, head = e / hd, d = e % hd;
-    store8(v_cache + ((static_cast<size_t>(r) * hkv + head) * window + col) * hd + d, f);
   }
-  float rstd_q = 1.f, rstd_k = 1.f;
+  float rstd = 1.f;
   if (qk_norm) {
-    ss_q = block_sum(ss_q, scratch);
-    ss_k = block_sum(ss_k, scratch);
-    rstd_q = rsqrtf(ss_q / static_cast<float>(Wq) + eps);
-    rstd_k = rsqrtf(ss_k / static_cast<float>(Wk) + eps);
+    ss = block_sum(ss, scratch);
+    rstd = rsqrtf(ss / static_cast<float>(width) + eps);
   }
   __syncthreads();  // `row` complete
 
   const float* cs = cos_t + static_cast<size_t>(tok) * half;
   const float* sn = sin_t + static_cast<size_t>(tok) * half;
-  for (int c = threadIdx.x; c < (Wq + Wk) / 8; c += DQ_THREADS) {
-    const bool is_q = c * 8 < Wq;
-    const int e0 = is_q ? c * 8 : c * 8 - Wq;  // element index inside q or k
-    const float* x = is_q ? row : row + Wq;
-    const bf16* w = is_q ? wq : wk;
-    const float rstd = is_q ? rstd_q : rstd_k;
+  for (int c = threadIdx.x; c < width / 8; c += DQ_THREADS) {
+    const int e0 = c * 8;
     const int d0 = e0 % hd;
     const int partner0 = d0 < half ? e0 + half : e0 - half;
     float wv[8], wp[8], out[8];
@@ -104,7 +104,7 @@ decode_qkv_kernel(const bf16* __restrict__ qkv, const bf16* __restrict__ wq, con
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      float a = x[e0 + i], b = x[partner0 + i];
+      float a = row[e0 + i], b = row[partner0 + i];
       if (qk_norm) {
         a = a * rstd * wv[i];
         b = b * rstd * wp[i];
@@ -229,14 +229,14 @@ int ob_decode_qkv(const void* qkv, const void* wq, const void* wk, const float* 
   using namespace ob;
   if (R < 1 || hd < 16 || hd % 16 != 0 || Wq % hd != 0 || Wk % hd != 0 || window < 1 || table_len < 1) return -1;
   if (qk_norm && (wq == nullptr || wk == nullptr)) return -1;
-  const size_t smem = static_cast<size_t>(Wq + Wk) * sizeof(float);
+  const size_t smem = static_cast<size_t>(Wq > Wk ? Wq : Wk) * sizeof(float);
   if (smem > 96 * 1024) return -1;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(decode_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024) != cudaSuccess) return -4;
     configured = true;
   }
-  decode_qkv_kernel<<<R, DQ_THREADS, smem, stream>>>(static_cast<const bf16*>(qkv), static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
+  decode_qkv_kernel<<<dim3(R, 2), DQ_THREADS, smem, stream>>>(static_cast<const bf16*>(qkv), static_cast<const bf16*>(wq), static_cast<const bf16*>(wk),
                                                      cos_t, sin_t, rope_pos, write_col, static_cast<bf16*>(q_out), static_cast<bf16*>(k_cache),
                                                      static_cast<bf16*>(v_cache), Wq, Wk, hd, window, table_len, eps, clip, qk_norm, rope);
   return cudaGetLastError() == cudaSuccess ? 0 : -2;
