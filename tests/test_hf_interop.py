@@ -116,3 +116,19 @@ def test_wrapper_toggles_and_embedding_resize():
         untied(ids, output_attentions=True)
     cfg = OLMoConfig(n_heads=8, multi_query_attention=True)
     assert cfg.effective_n_kv_heads == 1 and OLMoConfig(n_heads=8, n_kv_heads=2).effective_n_kv_heads == 2
+
+
+def test_transformers_generate_uses_the_key_value_cache_and_matches_greedy_decoding():
+    """``generate`` of the transformers wrapper (greedy, with its cache plumbing through ``prepare_inputs_for_generation``)
+    produces the tokens a cache-free argmax loop over the native model produces."""
+    wrapper = OLMoForCausalLM(OLMoConfig(**OLMO2), init_params=True).eval()
+    torch.manual_seed(3)
+    ids = torch.randint(0, 118, (1, 7))
+    out = wrapper.generate(ids, max_new_tokens=8, do_sample=False, pad_token_id=wrapper.config.pad_token_id)
+    want = ids[0].tolist()
+    with torch.no_grad():
+        for _ in range(8):
+            want.append(int(wrapper.model(torch.tensor([want])).logits[0, -1].argmax()))
+            if want[-1] == wrapper.config.eos_token_id:  # generation stops after emitting the end token
+                break
+    assert out[0].tolist() == want and len(want) > 9
