@@ -70,6 +70,7 @@ class GenerationRequest:
     prompt_ids: List[int]
     params: SamplingParams
     on_token: Optional[Callable[["GenerationRequest", int, str], None]] = None
+    on_done: Optional[Callable[["GenerationRequest"], None]] = None  # called from the engine's thread when the request ends
     token_ids: List[int] = field(default_factory=list)
     token_logprobs: List[float] = field(default_factory=list)
     text: str = ""
@@ -87,6 +88,13 @@ class GenerationRequest:
     @property
     def finished(self) -> bool:
         return self.finish_reason is not None
+
+    def _complete(self) -> None:
+        """Mark the request finished: wake blocking waiters and run the completion callback (once)."""
+        self._done.set()
+        callback, self.on_done = self.on_done, None
+        if callback is not None:
+            callback(self)
 
     def wait(self, timeout: Optional[float] = None) -> "GenerationRequest":
         if not self._done.wait(timeout):
@@ -161,6 +169,7 @@ class Engine:
         prompt_ids: Sequence[int],
         params: Optional[SamplingParams] = None,
         on_token: Optional[Callable[[GenerationRequest, int, str], None]] = None,
+        on_done: Optional[Callable[[GenerationRequest], None]] = None,
     ) -> GenerationRequest:
         params = params or SamplingParams()
         params.validate()
@@ -168,7 +177,7 @@ class Engine:
         limit = self.config.max_sequence_length if self._static is None else self._static.window
         if len(prompt) + 1 > limit:
             raise ContextLengthError(f"prompt of {len(prompt)} tokens leaves no room in a context of {limit}")
-        request = GenerationRequest(next(self._ids), prompt, params, on_token)
+        request = GenerationRequest(next(self._ids), prompt, params, on_token, on_done)
         if params.seed is not None:
             request._generator = torch.Generator(device="cpu").manual_seed(int(params.seed))
         with self._wake:
@@ -186,7 +195,7 @@ class Engine:
                 self._queue.remove(request)
                 request.finish_reason = "cancelled"
                 request.finished_at = time.monotonic()
-                request._done.set()
+                request._complete()
                 return
         request._cancelled = True
 
@@ -244,7 +253,7 @@ class Engine:
         for request in self._rows + pending:
             request.error, request.finish_reason = exc, "error"
             request.finished_at = time.monotonic()
-            request._done.set()
+            request._complete()
         if self._static is not None:
             for request in self._rows:
                 self._static.release(request._row)
@@ -415,7 +424,7 @@ class Engine:
                 for r in done:
                     self._static.release(r._row)
                     r.finished_at = now
-                    r._done.set()
+                    r._complete()
                 self._rows = [self._rows[i] for i in keep]
                 self._active = None
                 self._static.compact()
@@ -433,7 +442,7 @@ class Engine:
             self._rows = [self._rows[i] for i in keep]
             for r in done:
                 r.finished_at = now
-                r._done.set()
+                r._complete()
         if self._rows and self._mask is not None and self._kv is not None:
             slack = int(self._mask.shape[1] - int(self._mask.sum(dim=1).max()))
             if slack > 0:

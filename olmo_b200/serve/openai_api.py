@@ -118,7 +118,7 @@ def create_app(
             raise _BadRequest("'n' must be an integer between 1 and 16")
         return body
 
-    def submit_all(prompts: List[List[int]], params: SamplingParams, n: int, sink=None) -> List[GenerationRequest]:
+    def submit_all(prompts: List[List[int]], params: SamplingParams, n: int, sink=None, on_done=None) -> List[GenerationRequest]:
         requests = []
         try:
             for prompt in prompts:
@@ -126,7 +126,7 @@ def create_app(
                     # choices of one prompt must differ: derive a stream per choice from the request's seed
                     p = params if params.seed is None or n == 1 else SamplingParams(**{**params.__dict__, "seed": params.seed + k})
                     callback = None if sink is None else sink(len(requests))
-                    requests.append(engine.submit(prompt, p, callback))
+                    requests.append(engine.submit(prompt, p, callback, on_done))
         except ContextLengthError as exc:
             for r in requests:
                 engine.cancel(r)
@@ -137,10 +137,30 @@ def create_app(
             raise _BadRequest(f"the server is busy: {exc}", code="queue_full", status=429) from exc
         return requests
 
-    async def wait_all(requests: List[GenerationRequest]) -> None:
+    async def submit_and_wait(prompts: List[List[int]], params: SamplingParams, n: int) -> List[GenerationRequest]:
+        """Submit, then sleep on an event the engine's thread sets through the loop: a waiting request holds no thread."""
         loop = asyncio.get_running_loop()
+        finished = asyncio.Event()
+        total = len(prompts) * n
+        count = {"done": 0}
+
+        def one_done() -> None:  # runs in the event loop
+            count["done"] += 1
+            if count["done"] >= total:
+                finished.set()
+
+        requests = submit_all(prompts, params, n, on_done=lambda _r: loop.call_soon_threadsafe(one_done))
+        try:
+            await finished.wait()
+        except asyncio.CancelledError:  # the client went away
+            for r in requests:
+                if not r.finished:
+                    engine.cancel(r)
+            raise
         for r in requests:
-            await loop.run_in_executor(None, r.wait)
+            if r.error is not None:
+                raise r.error
+        return requests
 
     def usage(requests: List[GenerationRequest], n: int) -> Dict[str, int]:
         prompt_tokens = sum(len(r.prompt_ids) for r in requests[::n])
@@ -222,8 +242,7 @@ def create_app(
                             "choices": [{"index": index, "text": delta, "logprobs": None, "finish_reason": reason}]}
 
                 return StreamingResponse(stream(requests, queue, frame), media_type="text/event-stream")
-            requests = submit_all(prompts, params, n)
-            await wait_all(requests)
+            requests = await submit_and_wait(prompts, params, n)
         except _BadRequest as exc:
             return error(exc.message, exc.status, exc.code)
         except Exception as exc:  # the engine failed the request
@@ -262,8 +281,7 @@ def create_app(
 
                 first = [frame(i, "", None, role="assistant") for i in range(len(requests))]
                 return StreamingResponse(stream(requests, queue, frame, first), media_type="text/event-stream")
-            requests = submit_all(prompts, params, n)
-            await wait_all(requests)
+            requests = await submit_and_wait(prompts, params, n)
         except _BadRequest as exc:
             return error(exc.message, exc.status, exc.code)
         except Exception as exc:  # the engine failed the request
