@@ -427,3 +427,29 @@ def test_decode_kernels_under_cuda_graphs_generate_the_same_tokens():
     graphed = engine.generate(PROMPTS, params)
     assert engine._static.fused and engine._static.graph_replays == engine.stats["decode_steps"] > 0
     assert [r.token_ids for r in graphed] == [r.token_ids for r in eager]  # same kernels, same inputs, replayed
+
+
+def test_many_concurrent_http_requests_share_the_batch():
+    pytest.importorskip("fastapi")
+    httpx = pytest.importorskip("httpx")
+    import asyncio
+
+    model = tiny_model()
+    engine = Engine(model, CharTokenizer(), max_batch=4)
+    app = create_app(engine, model_name="tiny-olmo")
+    prompts = ["hello world", "a", "the quick brown fox", "olmo!", "zz top", "serve me tokens"] * 2
+
+    async def run():
+        async with httpx.AsyncClient(transport=httpx.ASGITransport(app=app), base_url="http://test") as client:
+            calls = [client.post("/v1/completions", json={"prompt": p, "max_tokens": 6, "temperature": 0}) for p in prompts]
+            return await asyncio.gather(*calls)
+
+    engine.start()  # the ASGI transport does not run the application's lifespan
+    try:
+        replies = asyncio.run(run())
+    finally:
+        engine.stop()
+    for prompt, reply in zip(prompts, replies):
+        assert reply.status_code == 200
+        assert reply.json()["choices"][0]["text"] == CharTokenizer().decode(greedy_reference(model, [ord(c) for c in prompt], 6))
+    assert engine.stats["requests"] == len(prompts) and engine.stats["decode_steps"] < 6 * len(prompts)
