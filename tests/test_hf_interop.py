@@ -132,3 +132,35 @@ def test_transformers_generate_uses_the_key_value_cache_and_matches_greedy_decod
             if want[-1] == wrapper.config.eos_token_id:  # generation stops after emitting the end token
                 break
     assert out[0].tolist() == want and len(want) > 9
+
+
+def test_text_generation_pipeline_with_converted_checkpoint_and_tokenizer(tmp_path):
+    """A checkpoint converted with its tokenizer file loads through ``AutoTokenizer`` / ``AutoModelForCausalLM`` and runs
+    in a transformers text-generation pipeline."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    from olmo_b200.hf import OLMoTokenizerFast
+
+    vocab = {f"w{i}": i for i in range(118)}
+    vocab["<pad>"], vocab["<eos>"] = 118, 119
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="<pad>"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.add_special_tokens(["<pad>", "<eos>"])
+    tok.save(str(tmp_path / "tokenizer.json"))
+
+    model = native(OLMO2)
+    folder = write_hf_olmo_checkpoint(save_unsharded(model, tmp_path / "ckpt"), tmp_path / "hf_olmo", tokenizer_path=tmp_path / "tokenizer.json")
+    tokenizer = transformers.AutoTokenizer.from_pretrained(str(folder))
+    assert isinstance(tokenizer, OLMoTokenizerFast)
+    assert tokenizer("w1 w2 w3")["input_ids"][:3] == [1, 2, 3]
+    loaded = transformers.AutoModelForCausalLM.from_pretrained(str(folder), torch_dtype=torch.float32).eval()
+    pipe = transformers.pipeline("text-generation", model=loaded, tokenizer=tokenizer)
+    text = pipe("w5 w6 w7", max_new_tokens=4, do_sample=False)[0]["generated_text"]
+    words = text.split()
+    assert words[:3] == ["w5", "w6", "w7"] and 3 < len(words) <= 7
+    ids = [vocab[w] for w in words[:3]]
+    with torch.no_grad():
+        first = int(model(torch.tensor([ids])).logits[0, -1].argmax())
+    assert words[3] == {v: k for k, v in vocab.items()}[first]
