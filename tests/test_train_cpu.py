@@ -183,3 +183,25 @@ def test_sharded_checkpoint_of_the_reference_layout_is_unsharded_offline(tmp_pat
     expect = trainer.train_step(next(batches))["train/CrossEntropyLoss"]
     again = t2.train_step(next(iter(t2.train_loader)))["train/CrossEntropyLoss"]
     assert abs(again - expect) < 1e-5
+
+
+def test_kept_activation_decision_follows_free_memory(monkeypatch):
+    """``OLMO_B200_KEEP_ACTS=auto``: the extra activations are kept only when they fit in the memory still free after the
+    first step with a margin (the decision itself needs no GPU: the memory query is replaced)."""
+    from types import SimpleNamespace
+
+    from olmo_b200.ops.fused_block import spec_from_config
+    from olmo_b200.parallel.fsdp import FlatShardEngine
+    from olmo_b200.recipes import recipe_config
+
+    cfg = recipe_config("OLMo2-7B-stage1").model
+    spec = spec_from_config(cfg)
+    tokens, blocks = 2 * 4096, cfg.n_layers
+    extra = (spec.Wq + spec.Wk + cfg.ff_proj_width // 2) * 2 * tokens * blocks  # bytes of rotated q/k + SwiGLU output
+    assert 9.5e9 < extra < 11e9
+    total = 192 << 30
+    for free, expect in [(extra + (13 << 30), True), (extra + (11 << 30), False), (4 << 30, False)]:
+        engine = SimpleNamespace(model=SimpleNamespace(config=cfg), device=torch.device("cpu"), keep_recomputable=None)
+        monkeypatch.setattr(torch.cuda, "mem_get_info", lambda device=None, f=free: (f, total))
+        FlatShardEngine._decide_keep_recomputable(engine, tokens, spec, blocks)
+        assert engine.keep_recomputable is expect, (free, expect)
