@@ -64,7 +64,7 @@ class SamplingParams:
             raise ValueError("top_k must be non-negative")
 
 
-@dataclass
+@dataclass(eq=False)  # requests are compared and looked up by identity
 class GenerationRequest:
     id: int
     prompt_ids: List[int]
