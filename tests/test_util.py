@@ -177,3 +177,18 @@ def test_rank_helpers_read_the_launcher_environment(monkeypatch):
     assert T.get_fs_local_rank() == 5  # shared file system: only global rank 0 writes
     monkeypatch.setenv("FS_LOCAL_RANK", "0")
     assert T.get_fs_local_rank() == 0
+
+
+def test_olmo_data_package_locates_files(tmp_path, monkeypatch):
+    from olmo_data.data import get_data_path, is_data_dir, is_data_file
+
+    assert is_data_dir("tokenizers") and not is_data_file("tokenizers/absent.json")
+    (tmp_path / "tokenizers").mkdir()
+    (tmp_path / "tokenizers" / "mine.json").write_text("{}")
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+    assert is_data_file("tokenizers/mine.json")
+    with get_data_path("tokenizers/mine.json") as path:
+        assert path == tmp_path / "tokenizers" / "mine.json"
+    with pytest.raises(FileNotFoundError):
+        with get_data_path("hf_datasets/none"):
+            pass
