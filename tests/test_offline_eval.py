@@ -179,3 +179,20 @@ def test_run_eval_command_line_on_a_checkpoint_folder(tmp_path, monkeypatch):
     rows = [json.loads(l) for l in (tmp_path / "rows.jsonl").read_text().splitlines()]
     assert len(rows) == 1 and rows[0]["num_instances"] == 2 and rows[0]["metric_ppl_token"] > 1.0
     assert (tmp_path / "rows.tsv").is_file()
+
+
+def test_fixture_experiment_runs_from_the_repository_root(tmp_path, monkeypatch):
+    """The committed example experiment (tiny checkpoint + synthetic corpus under ``test_fixtures/``)."""
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    proc = subprocess.run(
+        [sys.executable, "evaluation/run_eval.py", "evaluation/experiments/fixture_config.yaml", "--workspace", str(tmp_path / "ws"),
+         "--output", str(tmp_path / "rows.jsonl")], cwd=root, capture_output=True, text=True, timeout=600,
+    )
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    row = json.loads((tmp_path / "rows.jsonl").read_text().splitlines()[0])
+    assert row["task"] == "ppl_sample_docs" and row["num_instances"] == 48
+    assert 30 < row["metric_ppl_token"] < 200  # an untrained model over a 68-word vocabulary: near-uniform
