@@ -185,7 +185,7 @@ class StaticWindow:
                 x1 = x + a
                 h2 = k.norm_fwd(x1, w(block.ff_norm), None, spec.eps, spec.rms, save_stats=False)[0]
                 x = x1 + block.ff_out(k.swiglu_fwd(block.ff_proj(h2)))
-        x = t.ln_f(x)
+        x = k.norm_fwd(x, w(t.ln_f), None, spec.eps, spec.rms, save_stats=False)[0]
         self.logits.copy_(self.model.output_projection(x))
 
     def _forward(self, length: int) -> None:
