@@ -1,8 +1,8 @@
 """Serving: a continuous-batching generation engine and an OpenAI-compatible HTTP front end."""
 from .engine import ContextLengthError, Engine, GenerationRequest, QueueFullError, SamplingParams
-from .openai_api import create_app, default_chat_template
+from .openai_api import create_app, default_chat_template, load_chat_template
 
-__all__ = ["Engine", "SamplingParams", "GenerationRequest", "ContextLengthError", "QueueFullError", "create_app", "default_chat_template", "load_engine"]
+__all__ = ["Engine", "SamplingParams", "GenerationRequest", "ContextLengthError", "QueueFullError", "create_app", "default_chat_template", "load_chat_template", "load_engine"]
 
 
 def load_engine(checkpoint_dir: str, device: str = "cuda", dtype: str = "bf16", quantize: str = "none", max_batch: int = 32,

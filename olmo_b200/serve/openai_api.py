@@ -14,7 +14,7 @@ from typing import Any, AsyncIterator, Callable, Dict, List, Optional, Sequence,
 
 from .engine import ContextLengthError, Engine, GenerationRequest, QueueFullError, SamplingParams
 
-__all__ = ["create_app", "default_chat_template"]
+__all__ = ["create_app", "default_chat_template", "load_chat_template"]
 
 
 def default_chat_template(messages: Sequence[Dict[str, Any]], bos: str = "<|endoftext|>") -> str:
@@ -31,6 +31,40 @@ def default_chat_template(messages: Sequence[Dict[str, Any]], bos: str = "<|endo
         parts.append(bos + "\n" if role == "assistant" and i + 1 < len(messages) else "\n")
     parts.append("<|assistant|>\n")
     return "".join(parts)
+
+
+def load_chat_template(path: str, bos_token: str = "<|endoftext|>", eos_token: str = "<|endoftext|>") -> Callable[[Sequence[Dict[str, Any]]], str]:
+    """A chat template from a file: either a Jinja template as text, or a ``tokenizer_config.json`` whose ``chat_template``
+    entry holds one (the form instruct checkpoints on the HuggingFace Hub ship).  The template sees ``messages``,
+    ``add_generation_prompt=True``, ``bos_token`` and ``eos_token``, like ``apply_chat_template`` in transformers."""
+    import jinja2
+    from jinja2.sandbox import ImmutableSandboxedEnvironment
+
+    text = open(path, encoding="utf-8").read()
+    if path.endswith(".json"):
+        config = json.loads(text)
+        text = config["chat_template"]
+        bos_token = config.get("bos_token") or bos_token
+        eos_token = config.get("eos_token") or eos_token
+        if isinstance(bos_token, dict):
+            bos_token = bos_token.get("content", "")
+        if isinstance(eos_token, dict):
+            eos_token = eos_token.get("content", "")
+
+    def raise_exception(message: str):
+        raise ValueError(message)
+
+    env = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True, undefined=jinja2.StrictUndefined)
+    env.globals["raise_exception"] = raise_exception
+    template = env.from_string(text)
+
+    def render(messages: Sequence[Dict[str, Any]]) -> str:
+        try:
+            return template.render(messages=list(messages), add_generation_prompt=True, bos_token=bos_token, eos_token=eos_token)
+        except jinja2.TemplateError as exc:
+            raise ValueError(f"chat template failed: {exc}") from exc
+
+    return render
 
 
 class _BadRequest(Exception):

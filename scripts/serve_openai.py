@@ -30,6 +30,8 @@ def main(argv=None) -> int:
                     help="static: preallocated key/value windows and CUDA graphs (default on a GPU for rotary models)")
     ap.add_argument("--window", type=int, default=None,
                     help="static mode: longest prompt + completion per request; sizes the key/value memory (default: the context length)")
+    ap.add_argument("--chat-template", default=None,
+                    help="Jinja chat template file, or a tokenizer_config.json with a 'chat_template' entry (default: the OLMo-2 instruct layout)")
     ap.add_argument("--max-queue", type=int, default=0, help="answer 429 when this many requests are waiting (0: no limit)")
     ap.add_argument("--api-key", default=None, help="require 'Authorization: Bearer KEY'")
     args = ap.parse_args(argv)
@@ -43,7 +45,12 @@ def main(argv=None) -> int:
     engine = load_engine(args.checkpoint_dir, device=device, dtype=args.dtype if device != "cpu" else "fp32", quantize=args.quantize,
                          max_batch=args.max_batch, tokenizer=args.tokenizer, kv_cache=args.kv_cache, window=args.window)
     engine.max_queue = args.max_queue
-    app = create_app(engine, model_name=args.model_name or Path(args.checkpoint_dir.rstrip("/")).name, api_key=args.api_key)
+    extra = {}
+    if args.chat_template:
+        from olmo_b200.serve import load_chat_template
+
+        extra["chat_template"] = load_chat_template(args.chat_template)
+    app = create_app(engine, model_name=args.model_name or Path(args.checkpoint_dir.rstrip("/")).name, api_key=args.api_key, **extra)
     uvicorn.run(app, host=args.host, port=args.port, log_level="info")
     return 0
 

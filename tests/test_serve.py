@@ -453,3 +453,19 @@ def test_many_concurrent_http_requests_share_the_batch():
         assert reply.status_code == 200
         assert reply.json()["choices"][0]["text"] == CharTokenizer().decode(greedy_reference(model, [ord(c) for c in prompt], 6))
     assert engine.stats["requests"] == len(prompts) and engine.stats["decode_steps"] < 6 * len(prompts)
+
+
+def test_chat_template_from_file(tmp_path):
+    pytest.importorskip("jinja2")
+    from olmo_b200.serve import load_chat_template
+
+    jinja = "{{ bos_token }}{% for m in messages %}{{ '<|' + m['role'] + '|>\\n' + m['content'] + '\\n' }}{% endfor %}{% if add_generation_prompt %}{{ '<|assistant|>\\n' }}{% endif %}"
+    (tmp_path / "template.jinja").write_text(jinja)
+    render = load_chat_template(str(tmp_path / "template.jinja"))
+    messages = [{"role": "user", "content": "Hi"}]
+    assert render(messages) == default_chat_template(messages)
+    (tmp_path / "tokenizer_config.json").write_text(json.dumps({"chat_template": jinja, "bos_token": {"content": "<s>"}, "eos_token": "</s>"}))
+    assert load_chat_template(str(tmp_path / "tokenizer_config.json"))(messages).startswith("<s><|user|>")
+    (tmp_path / "strict.jinja").write_text("{% if messages[0]['role'] != 'user' %}{{ raise_exception('first message must come from the user') }}{% endif %}ok")
+    with pytest.raises(ValueError, match="first message"):
+        load_chat_template(str(tmp_path / "strict.jinja"))([{"role": "system", "content": "x"}])
