@@ -280,6 +280,8 @@ def run_ours(args) -> dict:
         },
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "checkpoint": checkpoint,
         "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
+        # the caching allocator's peak does not see peer-memory (symmetric) buffers; this is the device's own count
+        "device_mem_in_use_gb": (lambda free_total: (free_total[1] - free_total[0]) / 1e9)(torch.cuda.mem_get_info()),
     }
     if world > 1:
         dist.destroy_process_group()
