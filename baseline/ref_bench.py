@@ -86,6 +86,7 @@ def _run(args, presets) -> dict:
         init_cutoff_factor=3 if olmo2 else None, clip_qkv=None if olmo2 else 8.0,
     )
     device_batch = args.device_batch or max(ps["microbatch"], min(32, ps["global_batch"] // 8))  # same default as the main arm
+    sharding = ShardingStrategy[getattr(args, "sharding", "FULL_SHARD")]
     ac = None if args.activation_checkpointing in (None, "none") else ActivationCheckpointingStrategy(args.activation_checkpointing)
     cfg = TrainConfig(
         run_name=f"bench-ref-{args.model}", model=model_cfg,
@@ -95,8 +96,9 @@ def _run(args, presets) -> dict:
                                   alpha_f=0.1, warmup_min_lr=0.0),
         global_train_batch_size=device_batch * world, device_train_microbatch_size=ps["microbatch"], precision="amp_bf16",
         distributed_strategy=DistributedStrategy.fsdp,
-        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy.FULL_SHARD, wrapping_strategy=FSDPWrapStrategy.by_block_and_size,
-                        precision=FSDPPrecision.mixed),
+        fsdp=FSDPConfig(sharding_strategy=sharding, wrapping_strategy=FSDPWrapStrategy.by_block_and_size,
+                        precision=FSDPPrecision.mixed,
+                        hybrid_sharding_num_model_replicas=(args.replicas or 2) if sharding == ShardingStrategy.HYBRID_SHARD else None),
         max_grad_norm=1.0, softmax_auxiliary_loss=True, auxiliary_loss_multiplier=1e-5, fused_loss=True,
         save_folder=tempfile.mkdtemp(prefix="olmo_ref_bench_"), save_overwrite=True, save_data_indices=False,
         max_duration=10**9, console_log_interval=10**9, speed_monitor=SpeedMonitorConfig(window_size=1),
@@ -116,10 +118,17 @@ def _run(args, presets) -> dict:
     def dummy_init_fn(module: torch.nn.Module) -> None:
         module.to_empty(device=get_default_device())
 
+    device_mesh = None
+    if sharding in (ShardingStrategy.HYBRID_SHARD, ShardingStrategy._HYBRID_SHARD_ZERO2):
+        # the 2-D mesh scripts/train.py of the reference builds: (replicas, ranks per replica)
+        from torch.distributed.device_mesh import init_device_mesh
+
+        replicas = cfg.fsdp.hybrid_sharding_num_model_replicas or 2
+        device_mesh = init_device_mesh("cuda", (replicas, world // replicas))
     dist_model = FSDP(
         olmo_model, sharding_strategy=cfg.fsdp.sharding_strategy, mixed_precision=cfg.fsdp_precision,
         auto_wrap_policy=wrap_policy, use_orig_params=cfg.fsdp.use_orig_params, limit_all_gathers=True,
-        device_id=local_rank, param_init_fn=dummy_init_fn,
+        device_id=local_rank, param_init_fn=dummy_init_fn, device_mesh=device_mesh,
     )
     olmo_model.reset_parameters()
     optim = build_optimizer(cfg, dist_model)
@@ -160,7 +169,7 @@ def _run(args, presets) -> dict:
         torch.cuda.synchronize()
 
     sys.path.insert(0, str(HERE.parent))
-    from bench import ClockSampler  # timing helpers only
+    from bench import ClockSampler, bench_config  # timing / reporting helpers only
 
     loss = float("nan")
     for i in range(args.warmup):
@@ -196,18 +205,14 @@ def _run(args, presets) -> dict:
     tokens_per_step = device_batch * world * seq
     value = tokens_per_step / (ms_per_step / 1e3)
     result = {
-        "metric": "tokens_per_second (OLMo-2 training, whole job; FSDP FULL_SHARD, device-timed, max over ranks)",
+        "metric": f"tokens_per_second ({'OLMo-2' if olmo2 else 'OLMo-1'} training, whole job; FSDP {sharding.name}, device-timed, max over ranks)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic seeded uniform tokens with EOS boundaries; random-init weights", "impl": "reference",
         "tokens_per_second_per_gpu": value / world, "mfu_nominal_2250tf": value / world * flops_per_token / 2.25e15,
         "flops_per_token": flops_per_token, "final_loss": loss,
-        "config": {
-            "model": args.model, "global_batch": device_batch * world, "seq_len": seq, "micro_batch": ps["microbatch"],
-            "grad_accum": cfg.device_train_grad_accum, "parallelism": f"torch FSDP1 FULL_SHARD x{world} (NCCL), cuBLAS, flash-attn",
-            "activation_checkpointing": args.activation_checkpointing or "none",
-            "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
-        },
+        "config": bench_config(args, ps, device_batch, world, cfg.device_train_grad_accum),
+        "implementation": {"engine": f"torch FSDP1 {sharding.name} (NCCL), cuBLAS, flash-attn"},
         "clocks": clocks, "e2e": e2e, "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
     }
     dist.destroy_process_group()

@@ -63,6 +63,11 @@ def parse_args() -> argparse.Namespace:
     p.add_argument("--checkpoint-timing", action="store_true",
                    help="after the timed steps also time a sharded checkpoint save, its restore and the offline unshard")
     p.add_argument("--n-layers", type=int, default=None, help="profiling aid: fewer blocks than the preset (the result is then marked reduced)")
+    p.add_argument("--schedule", choices=["auto", "resident", "sharded"], default="auto",
+                   help="FULL_SHARD execution schedule of the flat-shard engine: 'resident' keeps every unit gathered between uses "
+                        "(one gather and one reduce-scatter per unit and optimizer step), 'sharded' streams the block units "
+                        "(gather in forward and backward, reduce-scatter every micro-batch), 'auto' takes resident while it fits")
+    p.add_argument("--no-check", action="store_true", help="skip the comparison of the peer-memory collectives with NCCL before the timed region")
     return p.parse_args()
 
 
@@ -154,6 +159,53 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def bench_config(args, ps: dict, device_batch: int, world: int, grad_accum: int) -> dict:
+    """The ``config`` entry of the JSON line.  Both arms call this, so the two lines carry the same keys and values."""
+    return {
+        "model": args.model, "global_batch": device_batch * world, "seq_len": args.seq_len, "micro_batch": ps["microbatch"],
+        "grad_accum": grad_accum,
+        "parallelism": f"fsdp {args.sharding.lower()} x{world}" + (f" ({args.replicas or 2} replicas)" if args.sharding == "HYBRID_SHARD" else ""),
+        "activation_checkpointing": args.activation_checkpointing or "none",
+        "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
+    }
+
+
+class PhaseTimer:
+    """CUDA events at the phase boundaries of one training step (the engine and the optimizer call ``mark``)."""
+
+    def __init__(self) -> None:
+        self.marks = []
+
+    def mark(self, name: str) -> None:
+        import torch
+
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        self.marks.append((name, ev))
+
+    def summary(self, world: int, device) -> dict:
+        """Milliseconds per phase, summed over the step, as min / median / max over ranks.  A mark names the phase that
+        *starts* there; ``barrier_wait`` is the end-of-step scalar all-reduce, whose duration is the time this rank spent
+        waiting for the slowest rank."""
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.synchronize()
+        names = ["forward", "backward", "grad_sync", "barrier_wait", "clip", "optimizer"]
+        acc = {n: 0.0 for n in names}
+        for (name, ev), (_, nxt) in zip(self.marks, self.marks[1:]):
+            if name in acc:
+                acc[name] += ev.elapsed_time(nxt)
+        t = torch.tensor([acc[n] for n in names], device=device, dtype=torch.float64)
+        if world > 1:
+            every = [torch.empty_like(t) for _ in range(world)]
+            dist.all_gather(every, t)
+            m = torch.stack(every)
+        else:
+            m = t[None]
+        return {n: {"min": m[:, i].min().item(), "median": m[:, i].median().item(), "max": m[:, i].max().item()} for i, n in enumerate(names)}
+
+
 def run_ours(args) -> dict:
     import torch
     import torch.distributed as dist
@@ -172,6 +224,7 @@ def run_ours(args) -> dict:
         dist.init_process_group("nccl", device_id=device)
     assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE={world}"
 
+    os.environ["OLMO_B200_SCHEDULE"] = args.schedule
     cfg, device_batch = make_train_config(args, world)
     if world > 1:  # one save folder for the whole job (every rank made its own temporary directory)
         shared = [cfg.save_folder]
@@ -207,6 +260,11 @@ def run_ours(args) -> dict:
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+
+    # ---- the peer-memory collectives of the last warm-up step against NCCL on the same buffers
+    multi_gpu_check = None
+    if world > 1 and not args.no_check and getattr(engine, "comm", None) is not None:
+        multi_gpu_check = engine.verify_collectives_against_nccl()
 
     # ---- device-timed region
     sampler = ClockSampler(local_rank)
@@ -245,6 +303,16 @@ def run_ours(args) -> dict:
             "ms_per_step": wall.item() * 1e3 / args.steps,
         }
 
+    # ---- one more step with per-phase CUDA events on every rank (not part of either timed region)
+    phases = None
+    if engine.fused:
+        engine.phase_timer = PhaseTimer()
+        barrier()
+        step(args.warmup + 2 * args.steps, False)
+        barrier()
+        phases = engine.phase_timer.summary(world, device)
+        engine.phase_timer = None
+
     checkpoint = None
     if args.checkpoint_timing:
         checkpoint = time_checkpoint_cycle(trainer, cfg, rank, world, barrier)
@@ -257,8 +325,10 @@ def run_ours(args) -> dict:
     except Exception:
         pass
     per_gpu = value / world
+    schedule = getattr(engine, "schedule", "resident") if world > 1 else "single device"
+    sm_mhz = clocks.get("sm_mhz")
     result = {
-        "metric": f"tokens_per_second ({'OLMo-2' if ps['flavour'] == 'olmo2' else 'OLMo-1'} training, whole job; FSDP {args.sharding}, device-timed, max over ranks)",
+        "metric": f"tokens_per_second ({'OLMo-2' if ps['flavour'] == 'olmo2' else 'OLMo-1'} training, whole job; FSDP {args.sharding}, {schedule} schedule, device-timed, max over ranks)",
         "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic seeded uniform tokens with EOS boundaries; random-init weights",
@@ -267,17 +337,22 @@ def run_ours(args) -> dict:
         "mfu_nominal_2250tf": per_gpu * flops_per_token / 2.25e15,
         "mfu_of_measured_sustained": (per_gpu * flops_per_token / (peaks["bf16_tflops_sustained"] * 1e12)) if peaks.get("bf16_tflops_sustained") else None,
         "flops_per_token": flops_per_token, "params": n_params, "final_loss": loss,
-        "config": {
-            "model": args.model if not args.n_layers else f"{args.model} REDUCED to {args.n_layers} layers (profiling only)",
-            "global_batch": device_batch * world, "seq_len": args.seq_len,
+        # the same keys, with the same values, as the reference arm prints for the same command line
+        "config": bench_config(args, ps, device_batch, world, cfg.device_train_grad_accum),
+        "schedule": schedule,
+        "schedule_note": {
+            "resident": "every unit stays gathered between uses: one gather and one reduce-scatter per unit and optimizer step (what SHARD_GRAD_OP asks for; FULL_SHARD gets it while it fits)",
+            "sharded": "block units are streamed: gathered in forward and again in backward, gradients reduce-scattered every micro-batch, all from inside the block GEMM launches",
+        }.get(schedule, "one device: nothing to gather or reduce"),
+        "implementation": {
+            "engine": "flat-shard engine, peer-memory collectives" if getattr(engine, "comm", None) is not None else ("flat-shard engine" + (", NCCL collectives" if world > 1 else "")),
             "official_global_batch_at_8_gpus": ps["global_batch"], "sequences_per_gpu_per_step": device_batch,
-            "micro_batch": ps["microbatch"], "grad_accum": cfg.device_train_grad_accum,
-            "parallelism": (f"fsdp{world}" if args.sharding == "FULL_SHARD" else f"{args.sharding.lower()}{world}") if world > 1 else "single-gpu flat-shard engine",
-            "activation_checkpointing": args.activation_checkpointing or "none",
             "optimizer": "adamw fp32 master, clip 1.0, z-loss on", "fused_path": bool(engine.fused),
             "recomputable_activations": "kept" if getattr(engine, "keep_recomputable", False) else "recomputed in backward",
-            "l2": "inputs larger than L2: each step touches >100 GB of parameters, optimizer state and activations",
+            "reduced_model": f"REDUCED to {args.n_layers} layers (profiling only)" if args.n_layers else None,
         },
+        "ms_per_step_x_sm_ghz": (ms_per_step * sm_mhz / 1e3) if sm_mhz else None,
+        "phases_ms": phases, "multi_gpu_check": multi_gpu_check,
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "checkpoint": checkpoint,
         "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
         # the caching allocator's peak does not see peer-memory (symmetric) buffers; this is the device's own count

@@ -435,6 +435,8 @@ class FlatShardCheckpointer(Checkpointer):
                 u.master.copy_(src)
                 u.lowp.copy_(src) if u.lowp.data_ptr() != u.master.data_ptr() else None
             engine._params_stale = True
+            if getattr(engine, "comm", None) is not None:
+                engine.params_changed()  # peers gather from these shards: open a new parameter epoch once all ranks are done
             if not engine.is_sharded:
                 for u in engine.units:
                     if u.full.data_ptr() != u.master.data_ptr():

@@ -44,6 +44,7 @@ int ob_get_gemm_pair_mode(void);
 int ob_comm_task_size(void);
 int ob_comm_launch(const void* task, int nctas, cudaStream_t stream);
 int ob_signal(int* flag, int value, cudaStream_t stream);
+int ob_wait_flags(const void* const* flags, int n, int value, int* status, long long wait_cycles, cudaStream_t stream);
 int ob_scalar_slots_bytes(void);
 int ob_allreduce_scalar(const float* value, void* const* peers, void* mine, float* out, int rank, int world, int epoch,
                         int* status, long long wait_cycles, cudaStream_t stream);

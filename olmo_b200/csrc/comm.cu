@@ -8,8 +8,24 @@ namespace {
 
 constexpr int COMM_THREADS = 512;
 
-__global__ void __launch_bounds__(COMM_THREADS) comm_kernel(const __grid_constant__ CommTask task) {
-  comm_run(task, blockIdx.x, gridDim.x);
+constexpr int COMM_SMEM = 1024 + COMM_MAX_STAGES * COMM_STAGE_BYTES + 256;
+
+__global__ void __launch_bounds__(COMM_THREADS) comm_kernel(const __grid_constant__ CommTask task, int smem_bytes) {
+  extern __shared__ uint8_t comm_smem[];
+  comm_run(task, blockIdx.x, gridDim.x, smem_bytes > 0 ? comm_smem : nullptr, smem_bytes);
+}
+
+struct WaitList {
+  const int* flags[COMM_MAX_WORLD];
+  int n;
+};
+
+// One thread per flag waits (bounded) until the flag has reached `value`.  Placed in a stream in front of work that
+// overwrites a buffer which peers may still be reading.
+__global__ void wait_flags_kernel(const __grid_constant__ WaitList list, int value, int* status, long long wait_cycles) {
+  const int p = threadIdx.x;
+  if (p < list.n && list.flags[p] != nullptr)
+    flag_wait_ge(list.flags[p], value, nullptr, status, wait_cycles > 0 ? wait_cycles : OB_WAIT_BUDGET_CYCLES);
 }
 
 __global__ void signal_kernel(int* flag, int value) {
@@ -64,7 +80,28 @@ extern "C" int ob_comm_launch(const void* task, int nctas, cudaStream_t stream) 
   if (t == nullptr || t->world < 1 || t->world > COMM_MAX_WORLD || nctas < 1) return -1;
   if (t->kind == COMM_ALL_GATHER && (t->elems % 8 != 0)) return -2;
   if (t->kind == COMM_REDUCE_SCATTER && (t->elems % 4 != 0)) return -2;
-  comm_kernel<<<nctas, COMM_THREADS, 0, stream>>>(*t);
+  int smem = 0;
+  if (t->mode & COMM_MODE_BULK) {
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(comm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, COMM_SMEM) != cudaSuccess) return -10;
+      configured = true;
+    }
+    smem = COMM_SMEM;
+  }
+  comm_kernel<<<nctas, COMM_THREADS, smem, stream>>>(*t, smem);
+  return cudaGetLastError() == cudaSuccess ? 0 : -11;
+}
+
+// Waits until each of the `n` flags (device addresses, possibly in peers' memory; null entries are skipped) is >= value.
+extern "C" int ob_wait_flags(const void* const* flags, int n, int value, int* status, long long wait_cycles,
+                             cudaStream_t stream) {
+  using namespace ob;
+  if (n < 0 || n > COMM_MAX_WORLD) return -1;
+  WaitList list = {};
+  list.n = n;
+  for (int i = 0; i < n; ++i) list.flags[i] = reinterpret_cast<const int*>(flags[i]);
+  wait_flags_kernel<<<1, 32, 0, stream>>>(list, value, status, wait_cycles);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 

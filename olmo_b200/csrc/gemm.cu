@@ -60,13 +60,13 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
                  void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
                  const int* __restrict__ b_ready, int rows_per_flag, int ready_value, int* __restrict__ status,
                  const __grid_constant__ CommTask comm_task, int comm_ctas) {
+  extern __shared__ uint8_t smem_raw[];
   if (static_cast<int>(blockIdx.x) < comm_ctas) {  // communication role: no TMEM, no barriers
-    comm_run(comm_task, blockIdx.x, comm_ctas);
+    comm_run(comm_task, blockIdx.x, comm_ctas, smem_raw, SMEM_BYTES);
     return;
   }
   const int cta = static_cast<int>(blockIdx.x) - comm_ctas;
   const int num_ctas = static_cast<int>(gridDim.x) - comm_ctas;
-  extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;

@@ -107,8 +107,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS_COMM, 1)
 gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                   void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
                   int* __restrict__ status, const __grid_constant__ CommTask comm_task, int comm_ctas) {
+  extern __shared__ uint8_t smem_raw[];
   if (static_cast<int>(blockIdx.x) < comm_ctas) {  // communication pairs (comm_ctas is even): no TMEM, no barriers
-    comm_run(comm_task, blockIdx.x, comm_ctas);
+    comm_run(comm_task, blockIdx.x, comm_ctas, smem_raw, G2_SMEM);
     return;
   }
   const uint32_t rank = cluster_ctarank();
@@ -116,7 +117,6 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
   const int pair = (static_cast<int>(blockIdx.x) - comm_ctas) >> 1;
   const int num_pairs = (static_cast<int>(gridDim.x) - comm_ctas) >> 1;
 
-  extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + G2_STAGES * G2_A_BYTES;

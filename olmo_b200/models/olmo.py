@@ -159,19 +159,59 @@ class OLMo(nn.Module):
             return inv_sqrt_d, cutoff  # output head
         raise NotImplementedError(cfg.init_fn)
 
-    def reset_parameters(self) -> None:
-        log.info("Initializing model parameters...")
+    def initialisable_modules(self) -> List[nn.Module]:
+        """The modules :meth:`reset_parameters` initialises one by one: embeddings, final norm, output projection and
+        every block (or block group)."""
         t = self.transformer
-        init_normal(t.wte, *self._top_level_std("wte"))  # type: ignore[arg-type]
-        if hasattr(t, "wpe"):
+        mods: List[nn.Module] = [t.wte]
+        for name in ("wpe", "emb_norm", "ff_out"):
+            if hasattr(t, name):
+                mods.append(getattr(t, name))
+        mods.append(t.ln_f)
+        mods += list(t.blocks if self.config.block_group_size == 1 else t.block_groups)  # type: ignore[union-attr]
+        if self.config.block_group_size > 1:  # a block inside a group can also be addressed on its own
+            mods += list(self.all_blocks())
+        return mods
+
+    def reset_parameters(self, only: Optional[set] = None, seed: Optional[int] = None) -> None:
+        """Initialise the parameters.  ``only`` (ids of modules from :meth:`initialisable_modules`) restricts the call
+        to those modules, which lets a sharded engine materialise and initialise one unit at a time.  With ``seed`` every
+        module draws from a random stream of its own that is a function of ``(seed, module name)``, so the values do not
+        depend on which other modules are initialised in the same call, nor on their order."""
+        if only is None:
+            log.info("Initializing model parameters...")
+        t = self.transformer
+
+        def want(m: nn.Module) -> bool:
+            return only is None or id(m) in only
+
+        def reseed(name: str) -> None:
+            if seed is not None:
+                from ..initialization import param_generator
+
+                s = param_generator(seed, name).initial_seed()
+                torch.manual_seed(s)
+                if torch.cuda.is_available():
+                    torch.cuda.manual_seed(s)
+
+        if want(t.wte):
+            reseed("wte")
+            init_normal(t.wte, *self._top_level_std("wte"))  # type: ignore[arg-type]
+        if hasattr(t, "wpe") and want(t.wpe):
+            reseed("wpe")
             init_normal(t.wpe, *self._top_level_std("wpe"))  # type: ignore[arg-type]
-        t.ln_f.reset_parameters()  # type: ignore[operator]
-        if hasattr(t, "emb_norm"):
+        if want(t.ln_f):
+            t.ln_f.reset_parameters()  # type: ignore[operator]
+        if hasattr(t, "emb_norm") and want(t.emb_norm):
             t.emb_norm.reset_parameters()  # type: ignore[operator]
-        if hasattr(t, "ff_out"):
+        if hasattr(t, "ff_out") and want(t.ff_out):
+            reseed("ff_out")
             init_normal(t.ff_out, *self._top_level_std("ff_out"))  # type: ignore[arg-type]
         for unit in t.blocks if self.config.block_group_size == 1 else t.block_groups:  # type: ignore[union-attr]
-            unit.reset_parameters()
+            for block in ([unit] if self.config.block_group_size == 1 else unit):  # type: ignore[union-attr]
+                if want(unit) or want(block):
+                    reseed(f"block{block.layer_id}")
+                    block.reset_parameters()
 
     # ------------------------------------------------------------------------------ bias tables
     def get_alibi_attention_bias(self, seq_len: int, device: torch.device) -> torch.Tensor:

@@ -27,16 +27,33 @@ Execution
               parameters plus ``torch.distributed`` collectives.  Same layout, same checkpoints.
 
 Strategy mapping: ``FULL_SHARD``/``SHARD_GRAD_OP`` shard over all ranks, ``HYBRID_SHARD``/``_HYBRID_SHARD_ZERO2``
-shard inside a replica group and all-reduce across groups, ``NO_SHARD`` and ``ddp`` replicate.  With 180 GB per
-device the gathered compute copy of every unit stays resident between uses and gradients of all micro-batches are
-accumulated locally in fp32, so each optimizer step pays one gather and one reduction per unit instead of one per
-micro-batch; ``OLMO_B200_RESHARD=1`` restores the gather-per-use / reduce-per-micro-batch schedule.
+shard inside a replica group and all-reduce across groups, ``NO_SHARD`` and ``ddp`` replicate.
+
+Schedules (fused path with peer-memory collectives)
+---------------------------------------------------
+``resident``  the gathered compute copy and the full-size fp32 gradient accumulator of *every* unit stay allocated
+              (6 bytes per parameter that do not shrink with the number of ranks).  Gradients of all micro-batches are
+              accumulated locally, so an optimizer step pays one gather and one reduce-scatter per unit.  This is what
+              ``SHARD_GRAD_OP`` asks for, and what ``FULL_SHARD`` gets while it fits, because it is the faster schedule.
+``sharded``   the ``FULL_SHARD`` schedule proper (reference: ``scripts/train.py:210-220``, and ``olmo/train.py:796-803``:
+              no ``no_sync`` on the FSDP path, i.e. a reduction per micro-batch).  Units that consist of transformer
+              blocks are *streamed*: a rank keeps only its shards of them, two full-size parameter slots and three
+              full-size gradient slots.  Every micro-batch gathers block *i+1* from inside block *i*'s four forward GEMMs,
+              gathers block *i-1* again from inside block *i*'s weight-gradient GEMMs in the backward pass, and
+              reduce-scatters block *i*'s gradients from inside block *i-1*'s input-gradient GEMMs into the fp32 gradient
+              shard (summing Σg² on the last micro-batch).  The embedding, the final norm and the output projection are
+              used at the two ends of the pass, where there is no GEMM to hide their traffic behind; they stay resident
+              and are gathered / reduced once per step.
+
+``OLMO_B200_SCHEDULE=resident|sharded|auto`` selects it (``auto``, the default: ``sharded`` for ``FULL_SHARD`` when the
+resident set would take more than 60 % of the device together with the optimizer shards).
 """
 from __future__ import annotations
 
 import logging
 import math
 import os
+from contextlib import contextmanager
 from dataclasses import dataclass, field
 from typing import Any, Callable, Dict, Iterable, Iterator, List, Optional, Sequence, Tuple
 
@@ -90,6 +107,9 @@ class Unit:
     seg_wd: Optional[torch.Tensor] = field(default=None, repr=False)
     seg_lr: Optional[torch.Tensor] = field(default=None, repr=False)
     seg_meta: List[Tuple[int, int]] = field(default_factory=list, repr=False)  # (group index, end offset in shard)
+    streamed: bool = False  # sharded schedule: no resident `full` / `gfull`; gathered into rotating slots
+    stream_pos: int = -1  # position among the streamed units in forward order
+    zero_ranges: List[Tuple[int, int]] = field(default_factory=list, repr=False)  # what is not a matrix: vectors, padding
 
     def slot(self, name: str) -> ParamSlot:
         for s in self.slots:
@@ -137,7 +157,15 @@ class FlatShardEngine:
             and model.config.embedding_dropout == 0.0
             and model.config.block_group_size >= 1
         )
-        self.reshard = os.environ.get("OLMO_B200_RESHARD", "0") not in ("0", "", "false")
+        sched = os.environ.get("OLMO_B200_SCHEDULE", "auto").strip().lower()
+        if os.environ.get("OLMO_B200_RESHARD", "0") not in ("0", "", "false"):
+            sched = "sharded"
+        if sched not in ("auto", "resident", "sharded"):
+            raise OLMoConfigurationError("OLMO_B200_SCHEDULE must be one of auto, resident, sharded")
+        self._schedule_request = sched
+        self.schedule = "resident"  # decided in _build, once the unit sizes are known
+        self.stream: Optional["_StreamState"] = None
+        self.phase_timer: Any = None  # optional object with ``mark(name)``: CUDA events at phase boundaries (bench.py)
         # Keep the rotated q/k and the SwiGLU output of every block for the backward pass instead of recomputing them:
         # "1"/"0" force it, "auto" decides after the first complete step from the memory that is still free.
         keep = os.environ.get("OLMO_B200_KEEP_ACTS", "auto").strip().lower()
@@ -203,7 +231,7 @@ class FlatShardEngine:
         return self.shard_world > 1
 
     # -------------------------------------------------------------------------------- build
-    def _collect_units(self) -> List[Tuple[str, List[Tuple[str, nn.Parameter, nn.Module, str]]]]:
+    def _collect_units(self) -> List[Tuple[str, List[Tuple[str, nn.Parameter, nn.Module, str]], List[nn.Module]]]:
         wrap = None
         if self.cfg.distributed_strategy == DistributedStrategy.fsdp and self.cfg.fsdp is not None:
             wrap = self.cfg.fsdp.wrapping_strategy
@@ -225,23 +253,44 @@ class FlatShardEngine:
                         taken.add(id(p))
                         entries.append((names[id(p)], p, sub, attr))
             if entries:
-                out.append((uname, entries))
+                out.append((uname, entries, list(modules)))
         return out
+
+    def _decide_schedule(self, use_peer: bool) -> str:
+        if not use_peer:
+            return "resident"
+        req = self._schedule_request
+        if req == "auto":
+            if self.sharding_strategy != ShardingStrategy.FULL_SHARD:
+                return "resident"
+            P = sum(u.numel for u in self.units)
+            need = 6 * P + 16 * P // self.shard_world
+            req = "sharded" if need > 0.6 * torch.cuda.get_device_properties(self.device).total_memory else "resident"
+        return req
+
+    def _materialise_unit(self, uname: str, entries, seed: int) -> None:
+        """Allocate and initialise the parameters of one unit in fp32 on the device.  Every module's random stream is a
+        function of ``(seed, module name)`` only, so the weights do not depend on the world size, the sharding strategy
+        or the wrapping, and no rank ever holds more than its shards plus one unit."""
+        dev = self.device
+        mine = {(id(owner), attr) for _, _, owner, attr in entries}
+        for name, p, owner, attr in entries:
+            if p.is_meta:
+                owner._parameters[attr] = nn.Parameter(torch.empty(p.shape, dtype=torch.float32, device=dev), requires_grad=p.requires_grad)
+        def all_mine(m: nn.Module) -> bool:
+            return all((id(sub), attr) in mine for sub in m.modules() for attr, _ in sub.named_parameters(recurse=False))
+
+        self.model.reset_parameters(only={id(m) for m in self.model.initialisable_modules() if all_mine(m)}, seed=seed)
 
     def _build(self, seed: int) -> None:
         model, dev = self.model, self.device
-        # 1. materialise and initialise the full model identically on every rank
-        if any(p.is_meta for p in model.parameters()):
-            model.to_empty(device=dev)
-            torch.manual_seed(seed)
-            if dev.type == "cuda":
-                torch.cuda.manual_seed(seed)
-            model.reset_parameters()
-        else:
+        # 1. flat layout (shapes only: parameters may still be on the meta device)
+        meta = any(p.is_meta for p in model.parameters())
+        if not meta:
             model.to(dev)
-        # 2. flat layout
         sw = self.shard_world
-        for index, (uname, entries) in enumerate(self._collect_units()):
+        collected = self._collect_units()
+        for index, (uname, entries, _mods) in enumerate(collected):
             offset = 0
             slots = []
             for name, p, owner, attr in entries:
@@ -250,73 +299,118 @@ class FlatShardEngine:
             total = _round_up(max(offset, 1), sw * 1024)
             unit = Unit(uname, index, slots, total, total // sw)
             self.units.append(unit)
-        # 3. buffers; module parameters become views of `full`
+        # 2. schedule; which units are streamed
         use_peer = (
-            self.is_sharded and dev.type == "cuda" and self.fused
+            self.is_sharded and dev.type == "cuda" and self.fused and self.shard_world == self.world
             and os.environ.get("OLMO_B200_FUSED_COMM", "1").strip().lower() not in ("0", "false", "no", "off")
         )
-        if use_peer:
+        self.schedule = self._decide_schedule(use_peer)
+        if self.schedule == "sharded":
+            block_prefixes = ("transformer.blocks.", "transformer.block_groups.")
+            pos = 0
+            for unit in self.units:
+                if unit.slots and all(s.name.startswith(block_prefixes) for s in unit.slots):
+                    unit.streamed, unit.stream_pos = True, pos
+                    pos += 1
+                    cur, gaps = 0, []
+                    for sl in unit.slots:  # everything that is not a matrix is cleared before each backward use
+                        if len(sl.shape) >= 2:
+                            if sl.offset > cur:
+                                gaps.append((cur, sl.offset))
+                            cur = sl.offset + sl.numel
+                    if cur < unit.numel:
+                        gaps.append((cur, unit.numel))
+                    unit.zero_ranges = gaps
+            if pos == 0:
+                self.schedule = "resident"
+        # 3. buffers; module parameters become views of `full` (placeholders on the meta device for streamed units)
+        if self.is_sharded and dev.type == "cuda" and self.fused and os.environ.get("OLMO_B200_FUSED_COMM", "1").strip().lower() not in ("0", "false", "no", "off"):
             from .peer import PeerComm
 
             self.comm = PeerComm.create(self)
-        for unit in self.units:
+        for unit, (uname, entries, _mods) in zip(self.units, collected):
+            if meta:
+                self._materialise_unit(uname, entries, seed)
             S, P = unit.shard_size, unit.numel
             lo = self.shard_rank * S
             flat = torch.zeros(P, dtype=torch.float32, device=dev)
-            for s in unit.slots:
-                flat[s.offset : s.offset + s.numel].copy_(getattr(s.owner, s.attr).detach().reshape(-1).float())
+            for sl in unit.slots:
+                flat[sl.offset : sl.offset + sl.numel].copy_(getattr(sl.owner, sl.attr).detach().reshape(-1).float())
             unit.master = flat[lo : lo + S].clone() if sw > 1 else flat
             unit.grad = torch.zeros(S, dtype=torch.float32, device=dev)
-            if self.comm is not None:
+            streamed = unit.streamed and self.comm is not None
+            unit.streamed = streamed
+            if streamed:
+                unit.full = unit.gfull = None  # type: ignore[assignment]
+                unit.lowp = self.comm.lowp_view(unit)
+                unit.lowp.copy_(unit.master)
+            elif self.comm is not None:
                 unit.full = self.comm.full_view(unit.index, P)
                 unit.full.copy_(flat)
                 unit.gfull = self.comm.gfull_view(unit.index, P)
             else:
                 unit.full = flat.to(self.compute_dtype) if (self.compute_dtype != torch.float32 or sw > 1) else flat.clone()
                 unit.gfull = unit.grad if sw == 1 else None  # type: ignore[assignment]
-            unit.lowp = unit.full[lo : lo + S] if sw > 1 else unit.full
-            for s in unit.slots:
-                view = unit.full[s.offset : s.offset + s.numel].view(s.shape)
+            if not streamed:
+                unit.lowp = unit.full[lo : lo + S] if sw > 1 else unit.full
+            for sl in unit.slots:
+                if streamed:
+                    view = torch.empty(sl.shape, dtype=self.compute_dtype, device="meta")
+                else:
+                    view = unit.full[sl.offset : sl.offset + sl.numel].view(sl.shape)
                 param = nn.Parameter(view, requires_grad=not self.fused)
                 param._ob_unit = unit  # type: ignore[attr-defined]
-                param._ob_slot = s  # type: ignore[attr-defined]
-                s.owner._parameters[s.attr] = param
-                self._unit_of_param[s.name] = (unit, s)
+                param._ob_slot = sl  # type: ignore[attr-defined]
+                sl.owner._parameters[sl.attr] = param
+                self._unit_of_param[sl.name] = (unit, sl)
             del flat
+        if self.comm is None or not any(u.streamed for u in self.units):
+            self.schedule = "resident"
         if dev.type == "cuda":
             torch.cuda.empty_cache()
         # 4. optimizer-facing parameters: one per (parameter ∩ local shard)
         for unit in self.units:
             lo = self.shard_rank * unit.shard_size
             hi = lo + unit.shard_size
-            for s in unit.slots:
-                a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
+            for sl in unit.slots:
+                a, b = max(sl.offset, lo), min(sl.offset + sl.numel, hi)
                 if b > a:
                     data = unit.master[a - lo : b - lo]
                     gview = unit.grad[a - lo : b - lo]
-                    if b - a == s.numel:
-                        data, gview = data.view(s.shape), gview.view(s.shape)
+                    if b - a == sl.numel:
+                        data, gview = data.view(sl.shape), gview.view(sl.shape)
                 else:
                     data = unit.master[0:0]
                     gview = unit.grad[0:0]
                 p = nn.Parameter(data, requires_grad=True)
                 p.grad = gview
                 p._ob_range = (unit.index, a - lo, max(b, a) - lo)  # type: ignore[attr-defined]
-                self._opt_params.append((s.name, p))
-        self._params_stale = sw > 1  # `full` was filled from the initial weights; only shards differ after a step
-        self._params_stale = False
+                self._opt_params.append((sl.name, p))
+        self._params_stale = False  # `full` was filled from the initial weights
         if self.fused:
             self._setup_fused()
         if self.is_sharded and self.comm is None:
             for unit in self.units:
                 unit.gfull = torch.zeros(unit.numel, dtype=torch.float32, device=dev)
+        if meta:
+            torch.manual_seed(seed)
+            if dev.type == "cuda":
+                torch.cuda.manual_seed(seed)
+        if self.schedule == "sharded":
+            self.stream = _StreamState(self)
+            torch.cuda.synchronize(dev)
+            dist.barrier(group=self.shard_group)  # every rank's shards are in place before anyone gathers
         log.info(
-            "FlatShardEngine: %d units, %.2fB parameters, shard world %d, replicas %d, %s path",
+            "FlatShardEngine: %d units, %.2fB parameters, shard world %d, replicas %d, %s path, %s schedule",
             len(self.units), sum(s.numel for u in self.units for s in u.slots) / 1e9, self.shard_world, self.num_replicas,
-            "fused" if self.fused else "portable",
+            "fused" if self.fused else "portable", self.schedule,
         )
 
     # ----------------------------------------------------------------------- optimizer side
+    def _mark(self, name: str) -> None:
+        if self.phase_timer is not None:
+            self.phase_timer.mark(name)
+
     def named_parameters_for_optimizer(self) -> List[Tuple[str, nn.Parameter]]:
         return list(self._opt_params)
 
@@ -381,25 +475,29 @@ class FlatShardEngine:
         then the clip coefficient as a device scalar.  Returns the total gradient norm (device tensor)."""
         from ..ops import kernels as k
 
+        self._mark("grad_sync")
         self.finish_grad_sync()
         comm = self.comm
-        if comm is not None and comm.fuse_sumsq and not self.reshard:
-            # every shard was written exactly once this step, by reduce-scatter kernels that also summed its squares
+        if comm is not None and comm.fuse_sumsq:
+            # every shard received its last addition of the step from a reduce-scatter kernel that also summed its squares
             torch.sum(comm.rs_partials, dim=0, keepdim=True, out=self._sumsq)
         else:
             for i, unit in enumerate(self.units):
                 k.sumsq(unit.grad, self._sumsq, accumulate=i > 0)
+        self._mark("barrier_wait")
         if self.is_sharded:
             if self.comm is not None:
                 self.comm.all_reduce_scalar_(self._sumsq)
             else:
                 dist.all_reduce(self._sumsq, group=process_group or self.shard_group)
+        self._mark("clip")
         k.clip_coef(self._sumsq, float(max_norm) if max_norm is not None else float("inf"), self.clip_coef, self._norm_out)
         return self._norm_out[0].clone()
 
     def fused_optimizer_step(self, optim, kind: str, gscale: Optional[torch.Tensor]) -> None:
         from ..ops import kernels as k
 
+        self._mark("optimizer")
         self.finish_grad_sync()
         self._ensure_fused_state(optim, kind)
         self._refresh_segments(optim)
@@ -425,6 +523,49 @@ class FlatShardEngine:
         self._params_stale = True
         if self.comm is not None:
             self.comm.publish_params()
+        self._mark("end")
+
+    def verify_collectives_against_nccl(self) -> Dict[str, Any]:
+        """Check the peer-memory collectives of the step that just ran against NCCL on the same local buffers.
+
+        Call between an optimizer step and the next ``zero_grad``.  Resident units: the fp32 gradient shard must equal
+        ``reduce_scatter(gfull) / world`` (``gfull`` still holds this rank's unreduced gradients of the step), and after
+        a gather ``full`` must equal ``all_gather(lowp)`` bit for bit.  Streamed units: a gather into a parameter slot is
+        compared with NCCL's; their gradient slots have been reused by then, so their reduction is covered by the
+        multi-GPU tests instead.  Only local memory is handed to NCCL.  Collective: every rank calls it."""
+        assert self.comm is not None
+        world = self.shard_world
+        worst_rs, bad_ag, checked_rs, checked_ag = 0.0, 0, 0, 0
+        self.gather_params()
+        for unit in self.units:
+            shard = unit.lowp.contiguous()
+            ref = torch.empty(unit.numel, dtype=shard.dtype, device=self.device)
+            dist.all_gather_into_tensor(ref, shard, group=self.shard_group)
+            if unit.streamed:
+                st = self.stream
+                st.content[unit.stream_pos % st.n_full] = None
+                st.ensure(unit.stream_pos)
+                mine = self.comm.full_slot(unit.stream_pos % st.n_full)[: unit.numel]
+            else:
+                mine = unit.full
+            bad_ag += int((mine.view(torch.int16) != ref.view(torch.int16)).sum().item()) if shard.dtype == torch.bfloat16 else int((mine != ref).sum().item())
+            checked_ag += unit.numel
+            del ref
+            if not unit.streamed and getattr(unit, "reduced", False):
+                out = torch.empty(unit.shard_size, dtype=torch.float32, device=self.device)
+                dist.reduce_scatter_tensor(out, unit.gfull.clone(), group=self.shard_group)
+                out.div_(world)
+                denom = out.abs().max().clamp_min(1e-30)
+                worst_rs = max(worst_rs, float(((unit.grad - out).abs().max() / denom).item()))
+                checked_rs += unit.shard_size
+        t = torch.tensor([worst_rs, float(bad_ag)], device=self.device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.shard_group)
+        worst_rs, bad_ag = float(t[0]), int(t[1])
+        return {
+            "ok": bool(worst_rs < 1e-5 and bad_ag == 0), "reduce_scatter_max_rel_err_vs_nccl": worst_rs,
+            "all_gather_mismatched_elements_vs_nccl": bad_ag, "gradient_elements_checked": checked_rs,
+            "parameter_elements_checked": checked_ag, "schedule": self.schedule,
+        }
 
     def after_unfused_optimizer_step(self) -> None:
         """Per-parameter optimizers updated ``master`` in place: refresh the compute-dtype shard."""
@@ -440,7 +581,7 @@ class FlatShardEngine:
             unit.grad.zero_()
             unit.gfull_dirty.clear()
             if unit.gfull is not None and unit.gfull.data_ptr() != unit.grad.data_ptr():
-                unit.gfull.zero_()
+                unit.gfull.zero_()  # streamed units have none: their gradient slots are overwritten, not accumulated into
             unit.reduced = False  # type: ignore[attr-defined]
         if self.comm is not None:
             self.comm.rs_partials.zero_()
@@ -454,7 +595,7 @@ class FlatShardEngine:
             return
         if self.is_sharded:
             if self.comm is not None:
-                self.comm.all_gather_units(self.units)
+                self.comm.all_gather_units([u for u in self.units if not u.streamed])
             else:
                 for unit in self.units:
                     dist.all_gather_into_tensor(unit.full, unit.lowp.contiguous(), group=self.shard_group) if self._has_agit() else self._all_gather_fallback(unit)
@@ -480,7 +621,7 @@ class FlatShardEngine:
         if world == 1:
             return
         if self.comm is not None:
-            pending = [u for u in self.units if not getattr(u, "reduced", False)]
+            pending = [u for u in self.units if not u.streamed and not getattr(u, "reduced", False)]
             if pending:
                 if not self._grad_epoch_open:
                     self.comm.begin_grad_epoch()
@@ -529,8 +670,6 @@ class FlatShardEngine:
         self._microbatches_since_reduce += 1
         if not self.fused:
             self._collect_autograd_grads()
-        if self.reshard:
-            self.finish_grad_sync()
 
     # ----------------------------------------------------------------- fused forward/backward
     def _weights_of(self, block: OLMoBlock) -> Dict[str, Optional[torch.Tensor]]:
@@ -621,6 +760,8 @@ class FlatShardEngine:
         (``is_last``) reduces each unit's gradients from inside the input-gradient GEMMs of the block processed next.
         """
         assert self.fused
+        if self.stream is not None:
+            return self._train_microbatch_streamed(input_ids, labels, loss_divisor, z_mult, ac_strategy, is_last, doc_start)
         from ..ops import fused_block as fb
         from ..ops import kernels as k
         from ..ops.loss import lm_head_loss
@@ -659,6 +800,7 @@ class FlatShardEngine:
 
         if gather_queue:
             need(self._unit_of_module_param(t.wte.weight))
+        self._mark("forward")
         x = k.embedding_fwd(input_ids, t.wte.weight).view(M, mcfg.d_model)
         saved_list: List[Any] = []
         for i, block in enumerate(blocks):
@@ -689,12 +831,13 @@ class FlatShardEngine:
                 wgrad=lambda dl, xc: self.matrix_grad(head, dl, xc),
             )
         del xn
+        self._mark("backward")
         dx = k.norm_bwd(dxn, x, ln_f.weight, rstd_f, mean_f, spec.rms,
                         dweight=None if ln_f.weight is None else self.vector_grad(ln_f.weight))
         del dxn, x
 
         # ---- gradient reduction schedule (last micro-batch only)
-        reduce_now = comm is not None and is_last and not self.reshard
+        reduce_now = comm is not None and is_last
         ready: List[Unit] = []
         final_at: Dict[int, int] = {}
         if reduce_now:
@@ -743,6 +886,128 @@ class FlatShardEngine:
             self._decide_keep_recomputable(M, spec, sum(1 for i in range(len(blocks)) if not should_checkpoint_block(ac_strategy, i)))
         return ce_sum / loss_divisor, z_sum * (z_mult / loss_divisor)
 
+    def _train_microbatch_streamed(self, input_ids, labels, loss_divisor, z_mult, ac_strategy, is_last, doc_start):
+        """One micro-batch of the sharded schedule: block units pass through the parameter and gradient slots, their
+        collectives ride on the block GEMMs of every micro-batch (see the module docstring)."""
+        from ..ops import fused_block as fb
+        from ..ops import kernels as k
+        from ..ops.loss import lm_head_loss
+        from .peer import BWD_SPANS, FWD_SPANS, WGRAD_SPANS
+
+        comm, st = self.comm, self.stream
+        model, mcfg = self.model, self.model.config
+        t = model.transformer
+        B, T = input_ids.shape
+        M = B * T
+        spec = fb.spec_from_config(mcfg)
+        cos, sin = fb.rope_tables(T, spec.head_dim, float(mcfg.rope_theta), self.device)
+        blocks = model.all_blocks()
+        n_stream = len(st.seq)
+
+        if self._params_stale:  # resident units (embedding, final norm, head): once per optimizer step
+            comm.all_gather_units([u for u in self.units if not u.streamed])
+            self._params_stale = False
+
+        # ---- forward
+        self._mark("forward")
+        x = k.embedding_fwd(input_ids, t.wte.weight).view(M, mcfg.d_model)
+        saved_list: List[Any] = []
+        for i, block in enumerate(blocks):
+            pos = st.block_pos[i]
+            gk = None
+            if pos >= 0:
+                st.ensure(pos)
+                if st.last_block[pos] == i and pos + 1 < n_stream:
+                    gk = st.prefetch(pos + 1, FWD_SPANS)
+            w = st.weights(i) if pos >= 0 else self._weights_of(block)
+            with nvtx_range(f"fwd_block_{i}"):
+                if should_checkpoint_block(ac_strategy, i):
+                    y, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk, doc_start=doc_start)
+                    saved_list.append(("ckpt", x))
+                else:
+                    y, saved = fb.block_forward(spec, w, x, B, T, cos, sin, save=True, gemm_kwargs=gk, doc_start=doc_start,
+                                                keep_recomputable=bool(self.keep_recomputable))
+                    saved_list.append(("full", saved))
+            x = y
+        ln_f = t.ln_f
+        xn, rstd_f, mean_f = k.norm_fwd(x, ln_f.weight, None, mcfg.layer_norm_eps, spec.rms)
+        head = t.wte.weight if mcfg.weight_tying else t.ff_out.weight
+        with nvtx_range("lm_head_loss"):
+            ce_sum, z_sum, dxn = lm_head_loss(
+                xn, head, labels.reshape(-1), z_mult=z_mult, grad_scale=1.0 / loss_divisor,
+                logit_scale=(1.0 / math.sqrt(mcfg.d_model)) if mcfg.scale_logits else 1.0,
+                chunk_rows=int(os.environ.get("OLMO_B200_HEAD_CHUNK", "8192")),
+                wgrad=lambda dl, xc: self.matrix_grad(head, dl, xc),
+            )
+        del xn
+        self._mark("backward")
+        dx = k.norm_bwd(dxn, x, ln_f.weight, rstd_f, mean_f, spec.rms,
+                        dweight=None if ln_f.weight is None else self.vector_grad(ln_f.weight))
+        del dxn, x
+
+        # ---- resident units are reduced once per step, by stand-alone launches on the last micro-batch
+        final_at: Dict[int, int] = {}
+        if is_last:
+            comm.begin_grad_epoch()
+            final_at = {u: p for u, p in self._unit_final_points().items() if not self.units[u].streamed}
+
+        def reduce_resident(point: int) -> None:
+            for u in self.units:
+                if final_at.get(u.index) == point:
+                    comm.publish_grads(u)
+                    comm.launch(comm.rs_task(u))
+                    u.reduced = True  # type: ignore[attr-defined]
+
+        if is_last:
+            reduce_resident(len(blocks))
+
+        # ---- backward
+        for i in range(len(blocks) - 1, -1, -1):
+            kind, payload = saved_list.pop()
+            block = blocks[i]
+            pos = st.block_pos[i]
+            if pos < 0:  # a block that lives in a resident unit
+                w = self._weights_of(block)
+                if kind == "ckpt":
+                    _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start, keep_recomputable=True)
+                with nvtx_range(f"bwd_block_{i}"):
+                    dx = fb.block_backward(spec, w, payload, dx, cos, sin, _EngineSink(self, block), gemm_kwargs=st.rs_kwargs(BWD_SPANS, is_last))
+                st.rs_done()
+                del payload
+                if is_last:
+                    reduce_resident(i)
+                continue
+            st.ensure(pos)
+            w = st.weights(i)
+            if kind == "ckpt":
+                _, payload = fb.block_forward(spec, w, payload, B, T, cos, sin, save=True, doc_start=doc_start, keep_recomputable=True)
+            if st.last_block[pos] == i:  # first block of this unit in backward order: take a gradient slot
+                st.open_grads(pos)
+            wk = None
+            if st.first_block[pos] == i and pos - 1 >= 0:  # re-gather the unit the backward pass needs next
+                wk = st.prefetch(pos - 1, WGRAD_SPANS)
+            with nvtx_range(f"bwd_block_{i}"):
+                dx = fb.block_backward(spec, w, payload, dx, cos, sin, st.sink(i, wk),
+                                       gemm_kwargs=st.rs_kwargs(BWD_SPANS, is_last))
+            st.rs_done()
+            del payload
+            if st.first_block[pos] == i:  # the unit's gradients of this micro-batch are complete
+                st.publish_grads(pos, is_last)
+        k.embedding_bwd(input_ids, dx, self.grad_view(t.wte.weight)[0])
+        st.flush_rs(is_last)
+        if is_last:
+            reduce_resident(-1)
+            for u in self.units:
+                if not u.streamed and not getattr(u, "reduced", False):
+                    comm.publish_grads(u)
+                    comm.launch(comm.rs_task(u))
+                    u.reduced = True  # type: ignore[attr-defined]
+        self._grads_pending = False
+        self._microbatches_since_reduce += 1
+        if self.keep_recomputable is None and is_last:
+            self._decide_keep_recomputable(M, spec, sum(1 for i in range(len(blocks)) if not should_checkpoint_block(ac_strategy, i)))
+        return ce_sum / loss_divisor, z_sum * (z_mult / loss_divisor)
+
     def _decide_keep_recomputable(self, tokens: int, spec, n_blocks: int) -> None:
         """After the first full step the allocator has seen the step's peak, so the memory still free on the device is
         what the extra saved activations may use.  They are kept when they fit with a margin (12 GiB, or a quarter of
@@ -775,8 +1040,20 @@ class FlatShardEngine:
         spec = fb.spec_from_config(mcfg)
         cos, sin = fb.rope_tables(T, spec.head_dim, float(mcfg.rope_theta), self.device)
         x = k.embedding_fwd(input_ids, t.wte.weight).view(B * T, mcfg.d_model)
-        for block in model.all_blocks():
-            x, _ = fb.block_forward(spec, self._weights_of(block), x, B, T, cos, sin, save=False)
+        st = self.stream
+        for i, block in enumerate(model.all_blocks()):
+            gk = None
+            if st is not None and st.block_pos[i] >= 0:
+                from .peer import FWD_SPANS
+
+                pos = st.block_pos[i]
+                st.ensure(pos)
+                if st.last_block[pos] == i and pos + 1 < len(st.seq):
+                    gk = st.prefetch(pos + 1, FWD_SPANS)
+                w = st.weights(i)
+            else:
+                w = self._weights_of(block)
+            x, _ = fb.block_forward(spec, w, x, B, T, cos, sin, save=False, gemm_kwargs=gk)
         xn, _, _ = k.norm_fwd(x, t.ln_f.weight, None, mcfg.layer_norm_eps, spec.rms, save_stats=False)
         head = t.wte.weight if mcfg.weight_tying else t.ff_out.weight
         ce_sum, _, _ = lm_head_loss(xn, head, labels.reshape(-1), need_grad=False,
@@ -826,8 +1103,50 @@ class FlatShardEngine:
                 a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
                 if b > a:
                     unit.master[a - lo : b - lo].copy_(src[a - s.offset : b - s.offset].to(unit.master.device, torch.float32))
-                unit.full[s.offset : s.offset + s.numel].copy_(src.to(unit.full.device, unit.full.dtype))
+                if unit.full is not None:
+                    unit.full[s.offset : s.offset + s.numel].copy_(src.to(unit.full.device, unit.full.dtype))
+            if unit.streamed:
+                unit.lowp.copy_(unit.master)
         self._params_stale = False
+        self.params_changed(resident_current=True)
+
+    def params_changed(self, resident_current: bool = False) -> None:
+        """The master shards were overwritten from outside the optimizer (checkpoint restore, state-dict load): refresh
+        what peers gather from and, with peer-memory collectives, open a new parameter epoch once every rank is done."""
+        if not resident_current:
+            for unit in self.units:
+                if unit.lowp.data_ptr() != unit.master.data_ptr():
+                    unit.lowp.copy_(unit.master)
+            self._params_stale = True
+        if self.comm is not None:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.shard_group)
+            self.comm.publish_params()
+
+    @contextmanager
+    def summon_full_params(self) -> Iterator[None]:
+        """Inside the context the module parameters of streamed units are real, gathered tensors (compute dtype), so the
+        plain ``nn.Module`` forward (generation, module-level evaluation, tracing) works.  A no-op in the resident
+        schedule.  Collective: every rank of the shard group must enter."""
+        streamed = [u for u in self.units if u.streamed]
+        if not streamed:
+            yield
+            return
+        held = []
+        for unit in streamed:
+            full = torch.empty(unit.numel, dtype=unit.lowp.dtype, device=self.device)
+            dist.all_gather_into_tensor(full, unit.lowp.contiguous(), group=self.shard_group)
+            for sl in unit.slots:
+                placeholder = sl.owner._parameters[sl.attr]
+                real = nn.Parameter(full[sl.offset : sl.offset + sl.numel].view(sl.shape), requires_grad=False)
+                real._ob_unit, real._ob_slot = unit, sl  # type: ignore[attr-defined]
+                sl.owner._parameters[sl.attr] = real
+                held.append((sl, placeholder))
+        try:
+            yield
+        finally:
+            for sl, placeholder in held:
+                sl.owner._parameters[sl.attr] = placeholder
 
     def param_shard_ranges(self) -> Dict[str, Tuple[int, int, int]]:
         """``FQN -> (start, end, numel)``: the element range of the parameter held by this rank."""
@@ -839,6 +1158,137 @@ class FlatShardEngine:
                 a, b = max(s.offset, lo), min(s.offset + s.numel, hi)
                 out[s.name] = (max(a - s.offset, 0), max(b - s.offset, 0) if b > a else max(a - s.offset, 0), s.numel)
         return out
+
+
+class _StreamState:
+    """Book-keeping of the sharded schedule: which streamed unit sits in which parameter slot, which gradient slot a
+    unit writes to, and the reduce-scatter that is waiting for GEMMs to ride on."""
+
+    def __init__(self, engine: FlatShardEngine):
+        from .peer import N_FULL_SLOTS, N_GSLOTS
+
+        self.engine = engine
+        self.comm = engine.comm
+        self.n_full, self.n_g = N_FULL_SLOTS, N_GSLOTS
+        self.seq: List[Unit] = sorted((u for u in engine.units if u.streamed), key=lambda u: u.stream_pos)
+        self.content: List[Optional[Tuple[int, int]]] = [None] * self.n_full  # (stream position, parameter epoch)
+        self.block_pos: List[int] = []
+        self.block_slots: List[Dict[str, ParamSlot]] = []
+        self.first_block: Dict[int, int] = {}
+        self.last_block: Dict[int, int] = {}
+        for i, block in enumerate(engine.model.all_blocks()):
+            params = {
+                "att_proj": block.att_proj.weight, "attn_out": block.attn_out.weight, "ff_proj": block.ff_proj.weight,
+                "ff_out": block.ff_out.weight, "attn_norm": block.attn_norm.weight, "ff_norm": block.ff_norm.weight,
+                "q_norm": None if block.q_norm is None else block.q_norm.weight,
+                "k_norm": None if block.k_norm is None else block.k_norm.weight,
+            }
+            unit: Unit = params["att_proj"]._ob_unit  # type: ignore[union-attr]
+            pos = unit.stream_pos if unit.streamed else -1
+            self.block_pos.append(pos)
+            self.block_slots.append({key: p._ob_slot for key, p in params.items() if p is not None})  # type: ignore[attr-defined]
+            if pos >= 0:
+                self.first_block.setdefault(pos, i)
+                self.last_block[pos] = i
+        self._weights: Dict[Tuple[int, int], Dict[str, Optional[torch.Tensor]]] = {}
+        self.gslot_of: Dict[int, int] = {}  # stream position -> gradient slot of the current micro-batch
+        self.pending: Optional[Unit] = None  # unit whose gradients are published but not yet reduced
+        self._riding: Optional[Unit] = None
+
+    # ---- parameters
+    def present(self, pos: int) -> bool:
+        return self.content[pos % self.n_full] == (pos, self.comm.param_epoch)
+
+    def ensure(self, pos: int) -> None:
+        """Gather unit ``pos`` with a stand-alone launch unless its slot already holds the current weights."""
+        if not self.present(pos):
+            self.comm.launch(self.comm.stream_ag_task(self.seq[pos], pos % self.n_full))
+            self.content[pos % self.n_full] = (pos, self.comm.param_epoch)
+
+    def prefetch(self, pos: int, spans: Dict[str, Tuple[int, int, int]]) -> Optional[Dict[str, Dict[str, Any]]]:
+        """GEMM keyword arguments that make the named GEMMs carry the gather of unit ``pos`` (``None`` if it is there)."""
+        if self.present(pos):
+            return None
+        slot = pos % self.n_full
+        self.content[slot] = (pos, self.comm.param_epoch)
+        unit = self.seq[pos]
+        return {name: {"comm": (self.comm.stream_ag_task(unit, slot, span=span), self.comm.comm_ctas)} for name, span in spans.items()}
+
+    def weights(self, block_index: int) -> Dict[str, Optional[torch.Tensor]]:
+        pos = self.block_pos[block_index]
+        slot = pos % self.n_full
+        hit = self._weights.get((block_index, slot))
+        if hit is None:
+            buf = self.comm.full_slot(slot)
+            hit = {key: None for key in ("att_proj", "attn_out", "ff_proj", "ff_out", "attn_norm", "ff_norm", "q_norm", "k_norm")}
+            for key, sl in self.block_slots[block_index].items():
+                hit[key] = buf[sl.offset : sl.offset + sl.numel].view(sl.shape)
+            self._weights[(block_index, slot)] = hit
+        return hit
+
+    # ---- gradients
+    def open_grads(self, pos: int) -> None:
+        """Take the next gradient slot for unit ``pos``: wait until peers have drained its previous use, then clear the
+        parts that kernels add into (norm weights, padding); matrices are written with plain stores."""
+        g = pos % self.n_g
+        self.comm.open_gslot(g)
+        self.gslot_of[pos] = g
+        buf = self.comm.gslot(g)
+        for a, b in self.seq[pos].zero_ranges:
+            buf[a:b].zero_()
+
+    def sink(self, block_index: int, wgrad_comm: Optional[Dict[str, Dict[str, Any]]]) -> "_StreamSink":
+        pos = self.block_pos[block_index]
+        return _StreamSink(self.comm.gslot(self.gslot_of[pos]), self.block_slots[block_index], wgrad_comm or {})
+
+    def publish_grads(self, pos: int, is_last: bool) -> None:
+        if self.pending is not None:  # nothing carried the previous unit's reduction: do it now
+            self.flush_rs(is_last)
+        self.comm.publish_gslot(self.gslot_of[pos])
+        self.pending = self.seq[pos]
+
+    def rs_kwargs(self, spans: Dict[str, Tuple[int, int, int]], is_last: bool) -> Optional[Dict[str, Dict[str, Any]]]:
+        """GEMM keyword arguments that make the input-gradient GEMMs of the next block carry the pending reduction."""
+        if self.pending is None:
+            return None
+        unit, self.pending = self.pending, None
+        self._riding = unit
+        g = self.gslot_of[unit.stream_pos]
+        return {name: {"comm": (self.comm.stream_rs_task(unit, g, span=span, with_sumsq=is_last), self.comm.rs_ctas)} for name, span in spans.items()}
+
+    def rs_done(self) -> None:
+        """Call after the block whose GEMMs carried a reduction: tell peers this rank has finished reading the slot."""
+        if self._riding is not None:
+            self.comm.release_gslot(self.gslot_of[self._riding.stream_pos])
+            self._riding = None
+
+    def flush_rs(self, is_last: bool) -> None:
+        """Stand-alone reduction of the unit that found no GEMM to ride on (the first block's unit)."""
+        if self.pending is not None:
+            unit, self.pending = self.pending, None
+            g = self.gslot_of[unit.stream_pos]
+            self.comm.launch(self.comm.stream_rs_task(unit, g, with_sumsq=is_last))
+            self.comm.release_gslot(g)
+
+
+class _StreamSink:
+    """Gradient sink of a streamed block: matrices are stored (not accumulated) into the unit's gradient slot, and the
+    weight-gradient GEMMs may carry the re-gather of the next unit."""
+
+    def __init__(self, gbuf: torch.Tensor, slots: Dict[str, ParamSlot], comm_kwargs: Dict[str, Dict[str, Any]]):
+        self.gbuf, self.slots, self.comm_kwargs = gbuf, slots, comm_kwargs
+
+    def _view(self, name: str) -> torch.Tensor:
+        sl = self.slots[name]
+        return self.gbuf[sl.offset : sl.offset + sl.numel].view(sl.shape)
+
+    def matrix(self, name: str, dy: torch.Tensor, x: torch.Tensor) -> None:
+        from ..ops import kernels as k
+
+        k.gemm(dy, x, a_trans=True, b_trans=True, epilogue=k.EPI_F32_STORE, out=self._view(name), **self.comm_kwargs.get(name, {}))
+
+    def vector(self, name: str, like: torch.Tensor) -> torch.Tensor:
+        return self._view(name)
 
 
 class _EngineSink:
@@ -881,7 +1331,8 @@ class ShardedModel(nn.Module):
 
     def forward(self, *args, **kwargs) -> OLMoOutput:
         self.engine.gather_params()
-        return self.module(*args, **kwargs)
+        with self.engine.summon_full_params():
+            return self.module(*args, **kwargs)
 
 
 def build_sharded_model(model: OLMo, cfg: TrainConfig, device: torch.device, **kwargs) -> ShardedModel:

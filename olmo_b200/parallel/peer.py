@@ -8,8 +8,17 @@ are exchanged once over the process group's store and mapped into every peer),
 * ``full_all``   the compute-dtype copy of every unit, end to end.  A rank's own shard of a unit lives *inside* this
                  buffer, so an all-gather only has to pull the W-1 foreign regions from the peers' buffers;
 * ``gfull_all``  the fp32 full-size gradient accumulators, from which each peer pulls and sums its slice;
-* ``ctrl``       int32 words: ``[0]`` parameter epoch, ``[1+u]`` gradient epoch of unit ``u``, then the slot area of the
-                 scalar all-reduce.
+* ``ctrl``       int32 words: ``[0]`` parameter epoch, ``[1+u]`` gradient epoch of unit ``u``, the ready / done words of
+                 the streamed gradient slots, then the slot area of the scalar all-reduce.
+
+In the *sharded* schedule (see :mod:`olmo_b200.parallel.fsdp`) the units that hold transformer blocks are not kept
+gathered.  For those units a rank keeps only
+
+* ``lowp_all``   its own compute-dtype shards, in symmetric memory, which peers gather from;
+* ``full_slots`` two local buffers of the largest streamed unit's size that gathered units rotate through;
+* ``gslots``     three full-size fp32 gradient buffers in symmetric memory that the units rotate through in the backward
+                 pass, each guarded by a *ready* word (this rank has finished writing use ``q``) and a *done* word (this
+                 rank has finished reading use ``q`` from every peer).
 
 Ordering protocol (all flags are monotone epochs, all waits bounded):
 
@@ -57,13 +66,21 @@ class CommTask(ctypes.Structure):
         ("sumsq_partials", ctypes.c_void_p),
         ("status", ctypes.c_void_p),
         ("wait_cycles", ctypes.c_longlong),
+        ("mode", ctypes.c_int),
+        ("reserved", ctypes.c_int),
     ]
+
+
+COMM_MODE_BULK, COMM_MODE_SELF = 1, 2
+N_GSLOTS, N_FULL_SLOTS = 3, 2
 
 
 #: how a unit's collective is divided over the four GEMMs of a block, in sixteenths, proportional to GEMM duration at
 #: the 7B shapes (att_proj 0.55 ms, attn_out 0.18 ms, ff_proj 1.04 ms, ff_out 0.62 ms; same for the input-gradient GEMMs)
 FWD_SPANS = {"att_proj": (0, 4, 16), "attn_out": (4, 5, 16), "ff_proj": (5, 12, 16), "ff_out": (12, 16, 16)}
 BWD_SPANS = {"ff_out_dgrad": (0, 4, 16), "ff_proj_dgrad": (4, 11, 16), "attn_out_dgrad": (11, 12, 16), "att_proj_dgrad": (12, 16, 16)}
+#: the same division over the four weight-gradient GEMMs of a block (they carry the backward pass's re-gather)
+WGRAD_SPANS = {"ff_out": (0, 4, 16), "ff_proj": (4, 11, 16), "attn_out": (11, 12, 16), "att_proj": (12, 16, 16)}
 
 
 class PeerComm:
@@ -79,19 +96,43 @@ class PeerComm:
         assert self.world <= MAX_WORLD
         dev = engine.device
         assert ctypes.sizeof(CommTask) == lib().ob_comm_task_size(), "CommTask layout mismatch"
-        total = sum(u.numel for u in engine.units)
+        # resident units: gathered copy and full-size gradient accumulator of every unit, end to end
         self.bases: List[int] = []
         off = 0
         for u in engine.units:
             self.bases.append(off)
-            off += u.numel
+            if not getattr(u, "streamed", False):
+                off += u.numel
+        total = max(off, 1024)
         self.full_all = symm_mem.empty(total, dtype=engine.compute_dtype, device=dev)
         self.h_full = symm_mem.rendezvous(self.full_all, group)
         self.gfull_all = symm_mem.empty(total, dtype=torch.float32, device=dev)
         self.h_gfull = symm_mem.rendezvous(self.gfull_all, group)
+        # streamed units: own shards + rotating slots
+        streamed = [u for u in engine.units if getattr(u, "streamed", False)]
+        self.lowp_bases = {}
+        off = 0
+        for u in streamed:
+            self.lowp_bases[u.index] = off
+            off += u.shard_size
+        self.slot_numel = max([u.numel for u in streamed], default=0)
+        self.lowp_all = self.gslots = self.full_slots = None
+        self.lowp_ptrs: List[int] = []
+        self.gslot_ptrs: List[int] = []
+        if streamed:
+            self.lowp_all = symm_mem.empty(off, dtype=engine.compute_dtype, device=dev)
+            self.h_lowp = symm_mem.rendezvous(self.lowp_all, group)
+            self.gslots = symm_mem.empty(N_GSLOTS * self.slot_numel, dtype=torch.float32, device=dev)
+            self.h_gslots = symm_mem.rendezvous(self.gslots, group)
+            self.full_slots = torch.zeros(N_FULL_SLOTS * self.slot_numel, dtype=engine.compute_dtype, device=dev)
+            self.lowp_all.zero_()
+            self.gslots.zero_()
+            self.lowp_ptrs = [int(p) for p in self.h_lowp.buffer_ptrs]
+            self.gslot_ptrs = [int(p) for p in self.h_gslots.buffer_ptrs]
         self.n_units = len(engine.units)
         self.slot_words = lib().ob_scalar_slots_bytes() // 4
-        self.slot_off = (1 + self.n_units + 15) // 16 * 16
+        self.gslot_word0 = 1 + self.n_units  # ready words of the gradient slots, then their done words
+        self.slot_off = (1 + self.n_units + 2 * N_GSLOTS + 15) // 16 * 16
         self.ctrl = symm_mem.empty(self.slot_off + self.slot_words, dtype=torch.int32, device=dev)
         self.h_ctrl = symm_mem.rendezvous(self.ctrl, group)
         self.full_all.zero_()
@@ -100,6 +141,9 @@ class PeerComm:
         self.full_ptrs = [int(p) for p in self.h_full.buffer_ptrs]
         self.gfull_ptrs = [int(p) for p in self.h_gfull.buffer_ptrs]
         self.ctrl_ptrs = [int(p) for p in self.h_ctrl.buffer_ptrs]
+        self.gslot_use = [0] * N_GSLOTS  # how often each gradient slot has been handed out (same on every rank)
+        # bulk-async copies through shared memory (default) or plain per-thread peer loads
+        self.bulk = os.environ.get("OLMO_B200_COMM_BULK", "1").strip().lower() not in ("0", "false", "no", "off")
         self.slot_ptrs_dev = torch.tensor([p + 4 * self.slot_off for p in self.ctrl_ptrs], dtype=torch.int64, device=dev)
         self.param_epoch = 0
         self.grad_epoch = 0
@@ -107,9 +151,9 @@ class PeerComm:
         # Communication CTAs per fused launch.  A gather is a pure copy and needs few CTAs to keep pace with the GEMM it
         # rides on; a reduce-scatter moves twice the bytes and does arithmetic, so it gets more.  Both are even numbers
         # (the two-CTA GEMM schedules CTA pairs).
-        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "8"))
-        self.rs_ctas = int(os.environ.get("OLMO_B200_RS_CTAS", "16"))
-        self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "64"))
+        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "4" if self.bulk else "8"))
+        self.rs_ctas = int(os.environ.get("OLMO_B200_RS_CTAS", "8" if self.bulk else "16"))
+        self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "16" if self.bulk else "64"))
         ms = float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000"))
         self.wait_cycles = int(ms * 1.9e6)
         self._scalar_out = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -137,6 +181,16 @@ class PeerComm:
         b = self.bases[unit_index]
         return self.gfull_all[b : b + numel]
 
+    def lowp_view(self, unit) -> torch.Tensor:
+        b = self.lowp_bases[unit.index]
+        return self.lowp_all[b : b + unit.shard_size]
+
+    def full_slot(self, slot: int) -> torch.Tensor:
+        return self.full_slots[slot * self.slot_numel : (slot + 1) * self.slot_numel]
+
+    def gslot(self, slot: int) -> torch.Tensor:
+        return self.gslots[slot * self.slot_numel : (slot + 1) * self.slot_numel]
+
     # --------------------------------------------------------------------------------- tasks
     def _base_task(self, kind: int) -> CommTask:
         t = CommTask()
@@ -144,6 +198,7 @@ class PeerComm:
         t.status = status_tensor(self.engine.device).data_ptr()
         t.wait_cycles = self.wait_cycles
         t.sumsq_partials = None
+        t.mode = COMM_MODE_BULK if self.bulk else 0
         return t
 
     @staticmethod
@@ -189,6 +244,62 @@ class PeerComm:
         t.scale = 1.0 / self.engine.world
         t.wait_value = self.grad_epoch
         return t
+
+    def stream_ag_task(self, unit, slot: int, span=None) -> CommTask:
+        """Gather of one slice of every rank's shard of a streamed ``unit`` (this rank's own included) into local
+        full-size slot ``slot``."""
+        S = unit.shard_size
+        esz = self.lowp_all.element_size()
+        a, b = self._slice(S, 0, 1, span, 8)
+        t = self._base_task(COMM_ALL_GATHER)
+        t.mode |= COMM_MODE_SELF
+        t.elems, t.dst_peer_stride = b - a, S
+        base = self.lowp_bases[unit.index]
+        for p in range(self.world):
+            t.src[p] = self.lowp_ptrs[p] + (base + a) * esz
+            t.wait_flags[p] = None if p == self.rank else self.ctrl_ptrs[p]
+        t.dst = self.full_slots.data_ptr() + (slot * self.slot_numel + a) * esz
+        t.wait_value = self.param_epoch
+        return t
+
+    def stream_rs_task(self, unit, gslot: int, span=None, with_sumsq: bool = False) -> CommTask:
+        """Reduce-scatter of one slice of this rank's shard of a streamed ``unit`` out of every rank's gradient slot
+        ``gslot``, added to the fp32 gradient shard.  Waits for use ``gslot_use[gslot]`` of the slot to be ready."""
+        S = unit.shard_size
+        a, b = self._slice(S, 0, 1, span, 4)
+        t = self._base_task(COMM_REDUCE_SCATTER)
+        t.elems = b - a
+        for p in range(self.world):
+            t.src[p] = self.gslot_ptrs[p] + (gslot * self.slot_numel + self.rank * S + a) * 4
+            t.wait_flags[p] = self.ctrl_ptrs[p] + 4 * (self.gslot_word0 + gslot)
+        t.dst = unit.grad.data_ptr() + a * 4
+        if with_sumsq and self.fuse_sumsq:
+            t.sumsq_partials = self.rs_partials.data_ptr()
+        t.scale = 1.0 / self.engine.world
+        t.wait_value = self.gslot_use[gslot]
+        return t
+
+    def open_gslot(self, gslot: int) -> int:
+        """Hand out gradient slot ``gslot`` for its next use: first wait (on the stream, bounded) until every peer has
+        finished reading the previous use.  Returns the new use number."""
+        prev = self.gslot_use[gslot]
+        if prev > 0:
+            word = self.gslot_word0 + N_GSLOTS + gslot
+            flags = (ctypes.c_void_p * MAX_WORLD)()
+            for p in range(self.world):
+                flags[p] = None if p == self.rank else self.ctrl_ptrs[p] + 4 * word
+            check(lib().ob_wait_flags(flags, ctypes.c_int(self.world), ctypes.c_int(prev), ptr(status_tensor(self.engine.device)),
+                                      ctypes.c_longlong(self.wait_cycles), stream_ptr()), "ob_wait_flags")
+        self.gslot_use[gslot] = prev + 1
+        return prev + 1
+
+    def publish_gslot(self, gslot: int) -> None:
+        """This rank's gradients of the slot's current use are complete."""
+        self.signal(self.gslot_word0 + gslot, self.gslot_use[gslot])
+
+    def release_gslot(self, gslot: int) -> None:
+        """This rank has finished reading the slot's current use from every peer."""
+        self.signal(self.gslot_word0 + N_GSLOTS + gslot, self.gslot_use[gslot])
 
     # ------------------------------------------------------------------------------ launches
     def launch(self, task: CommTask, ctas: Optional[int] = None) -> None:

@@ -19,8 +19,14 @@ def main() -> None:
     ap.add_argument("--global-batch", type=int, default=8)
     ap.add_argument("--fused-comm", type=int, default=1)
     ap.add_argument("--strategy", default="FULL_SHARD")
+    ap.add_argument("--schedule", default="resident", choices=["resident", "sharded", "auto"])
+    ap.add_argument("--bulk", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=3)
+    ap.add_argument("--activation-checkpointing", default=None)
     args = ap.parse_args()
     os.environ["OLMO_B200_FUSED_COMM"] = str(args.fused_comm)
+    os.environ["OLMO_B200_SCHEDULE"] = args.schedule
+    os.environ["OLMO_B200_COMM_BULK"] = str(args.bulk)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
     from olmo_b200 import ops
@@ -40,7 +46,7 @@ def main() -> None:
         dist.init_process_group("nccl", device_id=device)
 
     model = ModelConfig(
-        d_model=256, n_heads=2, n_layers=3, mlp_hidden_size=1024, weight_tying=False, rope=True, rope_theta=500000,
+        d_model=256, n_heads=2, n_layers=args.layers, mlp_hidden_size=1024, weight_tying=False, rope=True, rope_theta=500000,
         flash_attention=True, attention_dropout=0.0, residual_dropout=0.0, embedding_dropout=0.0, include_bias=False,
         layer_norm_type=LayerNormType.rms, layer_norm_with_affine=True, layer_norm_eps=1e-6, bias_for_layer_norm=False,
         attention_layer_norm=True, norm_after=True, max_sequence_length=256, vocab_size=500, embedding_size=512,
@@ -59,8 +65,14 @@ def main() -> None:
     assert engine.fused
     if world > 1 and args.fused_comm and args.strategy == "FULL_SHARD":
         assert engine.comm is not None, "peer-memory collectives should be active"
+        assert engine.schedule == args.schedule, (engine.schedule, args.schedule)
+        if args.schedule == "sharded":
+            assert sum(u.streamed for u in engine.units) == args.layers and engine.comm.full_slots is not None
     optim = build_optimizer(cfg, dist_model)
 
+    from olmo_b200.config import ActivationCheckpointingStrategy
+
+    ac = ActivationCheckpointingStrategy(args.activation_checkpointing) if args.activation_checkpointing else None
     db = cfg.device_train_batch_size
     gen = torch.Generator().manual_seed(1234)
     all_ids = torch.randint(0, 500, (args.steps, args.global_batch, 256), generator=gen)
@@ -71,14 +83,20 @@ def main() -> None:
         mbs = mine.split(cfg.device_train_microbatch_size)
         for i, mb in enumerate(mbs):
             labels = torch.nn.functional.pad(mb[:, 1:], (0, 1), value=-100)
-            engine.train_microbatch(mb, labels, float(mine.numel()), z_mult=1e-4, is_last=i == len(mbs) - 1)
+            engine.train_microbatch(mb, labels, float(mine.numel()), z_mult=1e-4, is_last=i == len(mbs) - 1, ac_strategy=ac)
         m = optim.clip_grads_and_collect_metrics(step + 1, collect_param_metrics=False, process_group=engine.process_group)
         norms.append(float(m["total_grad_norm"]))
         optim.step()
     ops.check_status()
     state = engine.full_model_state_dict(rank0_only=True, cpu=True)
+    # the fused evaluation pass and the module-level forward (streamed units gathered for its duration) must agree
+    probe = all_ids[0, :2].to(device)
+    ce_sum, n_tok = engine.eval_loss(probe, torch.nn.functional.pad(probe[:, 1:], (0, 1), value=-100))
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        logits = dist_model(probe).logits
+    ce_module = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]).float(), probe[:, 1:].reshape(-1), reduction="sum")
     if rank == 0:
-        torch.save({"state": state, "norms": norms}, args.out)
+        torch.save({"state": state, "norms": norms, "eval_ce": float(ce_sum) / float(n_tok), "module_ce": float(ce_module) / float(n_tok)}, args.out)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -51,6 +51,37 @@ def test_two_ranks_match_one(tmp_path, fused_comm):
     _compare(multi, single, f"2 ranks (fused_comm={fused_comm}) vs 1")
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("bulk", [1, 0])
+def test_sharded_schedule_matches_one(tmp_path, bulk):
+    """The FULL_SHARD schedule proper (block units streamed through parameter and gradient slots, a gather in forward and
+    in backward and a reduce-scatter per micro-batch, all riding on block GEMMs) against one GPU on the same batch."""
+    single = _run(1, tmp_path / "one.pt", "--layers", "5")
+    multi = _run(2, tmp_path / f"sharded_{bulk}.pt", "--schedule", "sharded", "--layers", "5", "--bulk", str(bulk))
+    _compare(multi, single, f"2 ranks sharded schedule (bulk={bulk}) vs 1")
+    assert abs(multi["eval_ce"] - multi["module_ce"]) < 2e-2 * abs(multi["module_ce"]), (multi["eval_ce"], multi["module_ce"])
+    assert abs(multi["eval_ce"] - single["eval_ce"]) < 2e-2 * abs(single["eval_ce"])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_schedule_with_activation_checkpointing(tmp_path):
+    single = _run(1, tmp_path / "one.pt", "--layers", "4", "--activation-checkpointing", "whole_layer")
+    multi = _run(2, tmp_path / "sharded_ac.pt", "--schedule", "sharded", "--layers", "4", "--activation-checkpointing", "whole_layer")
+    _compare(multi, single, "2 ranks sharded schedule + whole_layer checkpointing vs 1")
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+@pytest.mark.parametrize("schedule", ["resident", "sharded"])
+def test_fused_collectives_are_reproducible(tmp_path, schedule):
+    """Peers are summed in rank order and every partial sum has one writer, so two runs from the same seed must give
+    bit-identical weights and gradient norms."""
+    a = _run(2, tmp_path / "a.pt", "--schedule", schedule, "--layers", "4")
+    b = _run(2, tmp_path / "b.pt", "--schedule", schedule, "--layers", "4")
+    assert a["norms"] == b["norms"]
+    for name, t in a["state"].items():
+        assert torch.equal(t, b["state"][name]), name
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
 def test_hybrid_shard_matches_one(tmp_path):
     single = _run(1, tmp_path / "one.pt")
