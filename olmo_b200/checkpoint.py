@@ -43,13 +43,14 @@ from .config import ShardedCheckpointerType, TrainConfig
 from .exceptions import OLMoCheckpointError
 from .optim import Optimizer, fix_optim_state_dict
 from .safetensors_util import safetensors_file_to_state_dict
-from .torch_util import barrier, get_fs_local_rank, get_global_rank, get_world_size
+import torch.distributed as dist
+
+from .torch_util import barrier, get_fs_local_rank, get_global_rank, get_world_size, is_distributed
 from .util import default_thread_count, dir_is_empty, is_url, resource_path, upload, wait_for
 
 __all__ = [
     "save_state_dict", "load_state_dict", "load_model_state", "Checkpointer", "FullCheckpointer",
-    "FlatShardCheckpointer", "TorchNewStyleShardedCheckpointer", "TorchLegacyShardedCheckpointer",
-    "LocalShardedCheckpointer", "OlmoCoreCheckpointer", "build_sharded_checkpointer",
+    "FlatShardCheckpointer", "build_sharded_checkpointer",
 ]
 
 log = logging.getLogger(__name__)
@@ -211,7 +212,22 @@ class FullCheckpointer(Checkpointer):
                     state[name] = {k: (v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v) for k, v in st.items()}
         else:
             keep = get_global_rank() == 0
-            tensor_keys = sorted({k for st in by_name.values() for k, v in st.items() if isinstance(v, torch.Tensor) and v.dim() > 0})
+            # Scalar entries (``step``, running gradient norms) and the set of tensor keys are collected from every rank:
+            # a rank whose shard of a parameter is empty may hold no state for it at all, and rank 0 is such a rank for
+            # the parameters at the end of every unit.
+            local_scalars: Dict[str, Dict[str, Tuple[bool, Any]]] = {}
+            for name, st in by_name.items():
+                for k, v in st.items():
+                    if isinstance(v, torch.Tensor) and v.dim() > 0:
+                        continue
+                    local_scalars.setdefault(name, {})[k] = (True, float(v.item())) if isinstance(v, torch.Tensor) else (False, v)
+            local_keys = sorted({k for st in by_name.values() for k, v in st.items() if isinstance(v, torch.Tensor) and v.dim() > 0})
+            every: List[Any] = [None] * get_world_size()
+            if is_distributed():
+                dist.all_gather_object(every, (local_keys, local_scalars))
+            else:
+                every = [(local_keys, local_scalars)]
+            tensor_keys = sorted({k for keys, _ in every for k in keys})
             for unit in engine.units:
                 lo = engine.shard_rank * unit.shard_size
                 for key in tensor_keys:
@@ -228,10 +244,15 @@ class FullCheckpointer(Checkpointer):
                             state.setdefault(s.name, {})[key] = full[s.offset : s.offset + s.numel].view(s.shape).cpu().clone()
                     del full, shard
             if keep:
-                for name, st in by_name.items():
-                    for k, v in st.items():
-                        if not (isinstance(v, torch.Tensor) and v.dim() > 0):
-                            state.setdefault(name, {})[k] = v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v
+                for _, scalars in every:
+                    for name, entries in scalars.items():
+                        cur = state.setdefault(name, {})
+                        for k, (was_tensor, v) in entries.items():
+                            if k == "step" and k in cur:  # ranks that skipped empty shards lag behind: the furthest count is the true one
+                                v = max(v, float(cur[k]))
+                            elif k in cur:
+                                continue
+                            cur[k] = torch.tensor(v, dtype=torch.float32) if was_tensor else v
                 # drop entries of parameters that never received state on any rank
                 state = {n: s for n, s in state.items() if "step" in s or not tensor_keys}
         return {"state": state, "param_groups": _clean_param_groups(optim)}
@@ -424,6 +445,9 @@ class FlatShardCheckpointer(Checkpointer):
         engine = _engine_of(dist_model)
         if engine is None:
             raise OLMoCheckpointError("restoring a sharded checkpoint needs a flat-shard engine")
+        foreign = self._foreign_layout(load_path)
+        if foreign is not None:
+            return self._restore_foreign(load_path, foreign, dist_model, optim, load_optimizer_state=load_optimizer_state)
         meta = self._read_meta(load_path, local_cache)
         same_layout = meta["shard_world"] == engine.shard_world and [u["numel"] for u in meta["units"]] == [u.numel for u in engine.units]
         if same_layout:
@@ -460,6 +484,37 @@ class FlatShardCheckpointer(Checkpointer):
         return trainer_state
 
     @staticmethod
+    def _foreign_layout(load_path: PathOrStr) -> Optional[str]:
+        """Name of the reference layout found at ``load_path`` (local directories only), or ``None`` for this framework's own."""
+        if is_url(load_path):
+            return None
+        from .checkpoint_compat import detect_layout
+
+        try:
+            layout = detect_layout(load_path)
+        except OLMoCheckpointError:
+            return None
+        return layout if layout in ("torch_new", "torch_legacy", "local", "olmo_core") else None
+
+    def _restore_foreign(self, load_path: PathOrStr, layout: str, dist_model: nn.Module, optim: Optimizer, *, load_optimizer_state: bool) -> Dict[str, Any]:
+        """Resume from a sharded checkpoint the reference wrote: every rank reassembles the full tensors on the host and
+        keeps its own ranges (the writing job's world size does not have to match)."""
+        from .checkpoint_compat import unshard_reference_checkpoint
+
+        log.info("%s is a '%s' checkpoint of the reference implementation; unsharding it on the host", load_path, layout)
+        engine = _engine_of(dist_model)
+        model_state, optim_state, trainer_state = unshard_reference_checkpoint(
+            load_path, layout=layout, load_optimizer_state=load_optimizer_state, load_trainer_state=True
+        )
+        engine.load_full_model_state_dict(model_state)
+        del model_state
+        if load_optimizer_state and optim_state is not None:
+            optim_state = FullCheckpointer._normalise_optim_state(optim_state, {})
+            FullCheckpointer.load_optim_state_into(dist_model, optim, optim_state)
+        barrier()
+        return trainer_state or {}
+
+    @staticmethod
     def _load_optim_shards(engine, optim: Optimizer, saved: Dict[str, Any]) -> None:
         saved = fix_optim_state_dict(optim, saved)
         for group, sg in zip(optim.param_groups, saved["param_groups"]):
@@ -493,8 +548,13 @@ class FlatShardCheckpointer(Checkpointer):
     ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
         """Reassemble full tensors offline (no process group needed): shard files are read by a thread pool, full
         buffers start as NaN and are verified finite after the copy so a missing shard cannot go unnoticed."""
-        if is_torch_dcp_checkpoint(load_path):
-            return unshard_torch_dcp_checkpoint(load_path, load_optimizer_state=load_optimizer_state, load_trainer_state=load_trainer_state)
+        foreign = self._foreign_layout(load_path)
+        if foreign is not None:
+            from .checkpoint_compat import unshard_reference_checkpoint
+
+            return unshard_reference_checkpoint(
+                load_path, layout=foreign, load_optimizer_state=load_optimizer_state, load_trainer_state=load_trainer_state, device=device
+            )
         meta = self._read_meta(load_path, local_cache)
         sw = meta["shard_world"]
         dev = "cpu" if device is None else str(device)
@@ -610,34 +670,14 @@ def unshard_torch_dcp_checkpoint(
     return model_state, optim_state, trainer_state
 
 
-class TorchNewStyleShardedCheckpointer(FlatShardCheckpointer):
-    """``sharded_checkpointer: torch_new`` — stored in the flat-shard format."""
-
-
-class TorchLegacyShardedCheckpointer(FlatShardCheckpointer):
-    """``sharded_checkpointer: torch_legacy`` — stored in the flat-shard format."""
-
-    def __init__(self, cfg: TrainConfig, thread_count: Optional[int] = None, use_shared_mem_impl: bool = False):
-        super().__init__(cfg, thread_count)
-        self.use_shared_mem_impl = use_shared_mem_impl
-
-
-class LocalShardedCheckpointer(FlatShardCheckpointer):
-    """``sharded_checkpointer: local`` — stored in the flat-shard format."""
-
-
-class OlmoCoreCheckpointer(FlatShardCheckpointer):
-    """``sharded_checkpointer: olmo_core`` — stored in the flat-shard format (the ``olmo_core`` package is not required)."""
-
-
 def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckpointerType] = None, use_shared_mem_impl: bool = False) -> Checkpointer:
-    name = name or cfg.sharded_checkpointer
-    if name == ShardedCheckpointerType.torch_new:
-        return TorchNewStyleShardedCheckpointer(cfg)
-    if name == ShardedCheckpointerType.torch_legacy:
-        return TorchLegacyShardedCheckpointer(cfg, use_shared_mem_impl=use_shared_mem_impl)
-    if name == ShardedCheckpointerType.local:
-        return LocalShardedCheckpointer(cfg)
-    if name == ShardedCheckpointerType.olmo_core:
-        return OlmoCoreCheckpointer(cfg)
-    raise NotImplementedError(name)
+    """The sharded checkpointer of this framework.
+
+    ``sharded_checkpointer`` (``torch_new``, ``torch_legacy``, ``local``, ``olmo_core``) names layouts of the reference's
+    FSDP1 checkpointers.  This engine has no FSDP1 flat parameters or ``ShardedTensor`` objects to serialise, so every
+    value *writes* the one flat-shard layout described in :class:`FlatShardCheckpointer`; the key is accepted so that
+    reference configs load unchanged.  On the *read* side the layout of a directory is detected, and checkpoints written
+    by the reference in the ``torch_new``, ``torch_legacy`` and ``local`` layouts are restored, resharded or unsharded
+    (:mod:`olmo_b200.checkpoint_compat`); ``olmo_core`` directories raise an error that says what to do."""
+    del name, use_shared_mem_impl
+    return FlatShardCheckpointer(cfg)

@@ -42,6 +42,8 @@ na_final_kernel(const float* __restrict__ partials, int nparts, float* __restric
 
 // Device address of g_noalloc_partials per device ordinal.  In host code the array's name is only a handle for the
 // runtime, not an address a kernel could use, so the address is obtained once per device with that device current.
+// The table is filled without a lock: two host threads that make the first call on a device at the same time both look
+// the address up and both store the same value.
 float* g_partials_addr[NA_MAX_DEVICES] = {nullptr};
 
 int scratch_for_current_device(float** out) {
@@ -71,6 +73,7 @@ extern "C" const char* ob_noalloc_strerror(int code) {
     case OB_NOALLOC_ERR_SYMBOL: return "cudaGetSymbolAddress failed for the built-in scratch array";
     case OB_NOALLOC_ERR_LAUNCH: return "kernel launch failed";
     case OB_NOALLOC_ERR_DEVICE: return "no current CUDA device, or its ordinal is out of range";
+    case OB_NOALLOC_ERR_NULL: return "out is null, or g is null while n > 0";
     default: return "unknown error";
   }
 }
@@ -78,6 +81,7 @@ extern "C" const char* ob_noalloc_strerror(int code) {
 extern "C" int ob_sumsq_f32_noalloc(const float* g, long long n, float* out, int accumulate, cudaStream_t stream) {
   using namespace ob;
   if (n < 0 || n > ob_sumsq_f32_noalloc_max_elements()) return OB_NOALLOC_ERR_TOO_LARGE;
+  if (out == nullptr || (n > 0 && g == nullptr)) return OB_NOALLOC_ERR_NULL;  // a launch on a null pointer would fault the device
   if ((reinterpret_cast<uintptr_t>(g) & 15) != 0) return OB_NOALLOC_ERR_ALIGNMENT;
   float* partials = nullptr;
   const int rc = scratch_for_current_device(&partials);  // first call on a device: one symbol lookup, no allocation

@@ -14,7 +14,9 @@
 //     OB_NOALLOC_MAX_PARTIALS * OB_NOALLOC_QUANTUM = 2^31 elements (8 GiB of fp32); a larger n is rejected with
 //     OB_NOALLOC_ERR_TOO_LARGE and nothing is launched;
 //   * the first call on a device looks up the array's device address (one cudaGetSymbolAddress, no allocation) and
-//     caches it; make that first call outside any stream capture;
+//     caches it; make that first call outside any stream capture.  Host threads may make it concurrently (they store the
+//     same address);
+//   * `out` must not be null, and `g` must not be null unless n is 0 (OB_NOALLOC_ERR_NULL, nothing is launched);
 //   * every call on a device shares the one array, which keeps the previous call's partials.  A call overwrites every
 //     entry it later reads, so nothing needs clearing, but two calls whose kernels overlap on the GPU (different
 //     streams without ordering) race on it — serialise them.
@@ -33,6 +35,7 @@
 #define OB_NOALLOC_ERR_SYMBOL (-103)
 #define OB_NOALLOC_ERR_LAUNCH (-104)
 #define OB_NOALLOC_ERR_DEVICE (-105)
+#define OB_NOALLOC_ERR_NULL (-106)
 
 #ifdef __cplusplus
 extern "C" {

@@ -45,8 +45,28 @@ def select_device(cfg: TrainConfig) -> torch.device:
     return torch.device("cuda", torch.cuda.current_device())
 
 
+def needs_portable_path(cfg: TrainConfig) -> Optional[str]:
+    """Why this run cannot use the fused kernel sequence for its training steps, or ``None``.  The choice between the
+    fused and the portable (autograd) path is made once, when the engine is built: a fused engine has no autograd graph
+    to fall back on for a single odd batch."""
+    mc = cfg.model
+    if cfg.module_outputs_save_steps:
+        return "module_outputs_save_steps records module outputs through forward hooks"
+    data = cfg.data
+    if data is not None and getattr(data, "generate_doc_lengths", False):
+        if mc.d_model // mc.n_heads != 128 or mc.max_sequence_length % 128 != 0:
+            return "intra-document masking needs head dimension 128 and a sequence length that is a multiple of 128 on the fused path"
+    if data is not None and getattr(data, "generate_attention_mask", False):
+        return "padded batches (generate_attention_mask) carry an attention mask"
+    return None
+
+
 def build_model_and_engine(cfg: TrainConfig, device: torch.device, **engine_kwargs) -> ShardedModel:
     """Instantiate the model without storage, then let the engine materialise, initialise and shard it."""
+    why = needs_portable_path(cfg)
+    if why is not None and not engine_kwargs.get("force_portable", False):
+        log.info("using the portable (autograd) path: %s", why)
+        engine_kwargs["force_portable"] = True
     model_cfg = cfg.model
     prior = model_cfg.init_device
     model_cfg.init_device = "meta"

@@ -571,6 +571,13 @@ class Trainer:
         micro_batches = self.split_batch(batch)
         batch_size_in_tokens = batch["input_ids"].numel()
         fused = self._fused_step_usable(batch)
+        if self._fused and not fused:
+            # a fused engine keeps no autograd graph (its module parameters do not require gradients)
+            raise OLMoConfigurationError(
+                "this batch cannot run on the fused kernel path (attention mask with padding, attention bias, document "
+                "lengths outside head dimension 128 / sequence length multiple of 128, or a module-output trace step) and "
+                "the engine was built for it; build the engine with force_portable=True (set OLMO_B200_KERNELS=0) for such data"
+            )
         del batch
         ce_batch_loss = torch.tensor(0.0, device=self.device)
         z_batch_loss = torch.tensor(0.0, device=self.device) if self.cfg.softmax_auxiliary_loss else None

@@ -1,6 +1,10 @@
 #!/usr/bin/env python
 """Convert a sharded checkpoint into the unsharded layout (``model.pt``, ``optim.pt``, ``train.pt``, ``config.yaml``) that
-both this framework and the reference load (reference: ``scripts/unshard.py:15-115``).  Runs offline on one CPU process."""
+both this framework and the reference load (reference: ``scripts/unshard.py:15-115``).  Runs offline on one CPU process.
+
+The layout of the input directory is detected: this framework's flat-shard format, or the reference's ``torch_legacy``
+(``rank*.pt`` holding ``ShardedTensor`` pickles), ``torch_new`` (``model_and_optim/``) and ``local`` (raw flat-parameter
+pieces) layouts.  ``--type`` is checked against what is found, so a wrong guess is reported instead of misread."""
 from __future__ import annotations
 
 import argparse
@@ -28,6 +32,11 @@ def main(
     input_dir, output_dir = Path(input_dir), Path(output_dir)
     output_dir.mkdir(parents=True, exist_ok=True)
     config = TrainConfig.load(input_dir / "config.yaml", validate_paths=False)
+    from olmo_b200.checkpoint_compat import detect_layout
+
+    found = detect_layout(input_dir)
+    if found not in ("flat_shard", str(getattr(sharded_checkpoint_type, "value", sharded_checkpoint_type))):
+        logger.warning("--type says %s but %s holds a '%s' checkpoint; reading it as '%s'", sharded_checkpoint_type, input_dir, found, found)
     checkpointer = build_sharded_checkpointer(config, name=sharded_checkpoint_type, use_shared_mem_impl=use_shared_mem_impl)
     model_state, optim_state, trainer_state = checkpointer.unshard_checkpoint(
         input_dir, load_optimizer_state=not model_only, load_trainer_state=not model_only

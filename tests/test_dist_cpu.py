@@ -95,6 +95,15 @@ def test_checkpoint_resharding_across_world_sizes(tmp_path, checkpointer):
     assert trainer_state["global_step"] == 3
     assert optim_state is not None and len(optim_state["state"]) == len(saved["state"])
 
+    # the unsharded optimizer file must carry every parameter, including those whose shard on rank 0 is empty (the
+    # per-parameter optimizer keeps no state for an empty shard), with the step count and moments of the sharded one
+    full_optim = torch.load(unsharded / "optim.pt", map_location="cpu", weights_only=False)
+    assert set(full_optim["state"]) == set(saved["state"])
+    for name, st in full_optim["state"].items():
+        assert int(st["step"]) == 3, (name, st["step"])
+        for key in ("exp_avg", "exp_avg_sq"):
+            torch.testing.assert_close(st[key], optim_state["state"][name][key], rtol=0, atol=0, msg=lambda m: f"{name}.{key}: {m}")
+
 
 def test_all_ranks_agree_on_cancellation(tmp_path):
     got = launch(2, "cancel", tmp_path / "c.pt", tmp_path / "w", "--time-limit", "100")

@@ -185,6 +185,63 @@ def test_sharded_checkpoint_of_the_reference_layout_is_unsharded_offline(tmp_pat
     assert abs(again - expect) < 1e-5
 
 
+def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
+    """``rank{r}.pt`` files holding ``ShardedTensor`` pickles (the reference's default sharded layout,
+    ``olmo/checkpoint.py:969-1453``), written here by two gloo ranks from a trainer's full state, are detected by
+    ``Trainer.restore_checkpoint`` and resumed from on one rank: weights, moments, step count and the next loss agree."""
+    import os
+    import socket
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "a")
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    batches = iter(trainer.train_loader)
+    for _ in range(3):
+        trainer.global_step += 1
+        trainer.global_train_examples_seen_this_epoch += cfg.global_train_batch_size
+        trainer.global_train_tokens_seen += cfg.global_train_batch_size * cfg.model.max_sequence_length
+        trainer.train_step(next(batches))
+    named = list(trainer.dist_model.engine.named_parameters_for_optimizer())
+    wrapped = {n: n.replace("transformer.blocks.", "transformer.blocks._fsdp_wrapped_module.") for n, _ in named}  # FSDP's name noise
+    source = {
+        "model": {wrapped[n]: p.detach().clone() for n, p in named},
+        "optim": {
+            "state": {wrapped[n]: {k: v.detach().clone() for k, v in trainer.optim.state[p].items()} for n, p in named},
+            "param_groups": [{**{k: v for k, v in g.items() if k not in ("params", "param_names")},
+                              "params": [wrapped[n] for n in g["param_names"]], "param_names": [wrapped[n] for n in g["param_names"]]}
+                             for g in trainer.optim.param_groups],
+        },
+        "trainer": trainer.trainer_state_dict(),
+    }
+    torch.save(source, tmp_path / "source.pt")
+    legacy = tmp_path / "step3"
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    worker = Path(__file__).resolve().parent / "ref_layout_worker.py"
+    proc = subprocess.run(
+        [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1", "--master-port", str(port),
+         str(worker), "--source", str(tmp_path / "source.pt"), "--out", str(legacy)],
+        stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, timeout=300, env=dict(os.environ),
+    )
+    assert proc.returncode == 0, proc.stdout[-3000:]
+    cfg.save(legacy / "config.yaml")
+
+    cfg2 = tiny_train_config(tmp_path / "b")
+    t2 = build_trainer(cfg2, device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+    t2.restore_checkpoint(str(legacy))
+    assert t2.global_step == 3
+    for n, p in t2.dist_model.engine.named_parameters_for_optimizer():
+        assert torch.equal(p.detach(), source["model"][wrapped[n]]), n
+        assert torch.allclose(t2.optim.state[p]["exp_avg_sq"], source["optim"]["state"][wrapped[n]]["exp_avg_sq"]), n
+    expect = trainer.train_step(next(batches))["train/CrossEntropyLoss"]
+    again = t2.train_step(next(iter(t2.train_loader)))["train/CrossEntropyLoss"]
+    assert abs(again - expect) < 1e-5
+
+
 def test_kept_activation_decision_follows_free_memory(monkeypatch):
     """``OLMO_B200_KEEP_ACTS=auto``: the extra activations are kept only when they fit in the memory still free after the
     first step with a margin (the decision itself needs no GPU: the memory query is replaced)."""

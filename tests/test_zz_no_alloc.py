@@ -48,6 +48,8 @@ def test_no_alloc_sumsq_matches_allocating_entry_point_twice_in_a_row():
         assert after == before  # nothing was requested from torch's allocator either
         torch.cuda.synchronize()
         assert torch.allclose(got, want, rtol=1e-4), (got.item(), want.item())
+        exact = g.double().pow(2).sum().item()  # and both against a float64 sum
+        assert abs(got.item() - exact) <= 2e-5 * exact, (got.item(), exact)
         rc = _noalloc(lib, g, got, accumulate=True)
         assert rc == 0
         torch.cuda.synchronize()
@@ -65,5 +67,23 @@ def test_no_alloc_sumsq_rejects_oversize_and_misaligned_input():
     assert rc == -101 and b"exceeds" in lib.ob_noalloc_strerror(rc)  # refused before any launch
     rc = lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(g.data_ptr() + 4), ctypes.c_longlong(8), ctypes.c_void_p(out.data_ptr()), 0, stream)
     assert rc == -102
+    # null pointers are refused on the host: launching on them would fault the device
+    assert lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(g.data_ptr()), ctypes.c_longlong(8), ctypes.c_void_p(None), 0, stream) == -106
+    assert lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(None), ctypes.c_longlong(8), ctypes.c_void_p(out.data_ptr()), 0, stream) == -106
     torch.cuda.synchronize()
     assert out.item() == 0.0
+    # exactly the documented maximum passes the size check (it is then refused for the null input, before any launch)
+    assert lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(None), ctypes.c_longlong(limit), ctypes.c_void_p(out.data_ptr()), 0, stream) == -106
+
+
+def test_no_alloc_sumsq_of_nothing_is_zero():
+    lib = _lib()
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    out = torch.full((1,), 7.0, device="cuda")
+    assert lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(None), ctypes.c_longlong(0), ctypes.c_void_p(out.data_ptr()), 0, stream) == 0
+    torch.cuda.synchronize()
+    assert out.item() == 0.0
+    out.fill_(7.0)
+    assert lib.ob_sumsq_f32_noalloc(ctypes.c_void_p(None), ctypes.c_longlong(0), ctypes.c_void_p(out.data_ptr()), 1, stream) == 0
+    torch.cuda.synchronize()
+    assert out.item() == 7.0
