@@ -92,7 +92,14 @@ def load_state_dict(checkpoint_dir: PathOrStr, fname: str, *, local_cache: Optio
         except FileNotFoundError:
             pass
     path = resource_path(str(checkpoint_dir).rstrip("/"), fname, local_cache=local_cache)
-    return torch.load(path, map_location=map_location, weights_only=False)
+    try:
+        return torch.load(path, map_location=map_location, weights_only=False)
+    except (RuntimeError, EOFError, pickle.UnpicklingError, ValueError, OSError) as e:
+        if isinstance(e, FileNotFoundError):
+            raise
+        # a file cut short by a crash or a failed transfer must stop the restore with the file's name, not surface as an
+        # archive-format error from deep inside the loader
+        raise OLMoCheckpointError(f"{path} is truncated or corrupt ({type(e).__name__}: {str(e)[:200]})") from e
 
 
 def _engine_of(dist_model: nn.Module):

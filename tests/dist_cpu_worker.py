@@ -67,7 +67,7 @@ def full_state(trainer):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("scenario", choices=["train", "save", "restore", "cancel", "lost_rank"])
+    ap.add_argument("scenario", choices=["train", "save", "restore", "cancel", "lost_rank", "save_crash"])
     ap.add_argument("--out", required=True)
     ap.add_argument("--work", required=True)
     ap.add_argument("--steps", type=int, default=3)
@@ -113,6 +113,24 @@ def main() -> None:
             result["state"] = state
         batches = iter(trainer.train_loader)
         result["next"] = run_steps(trainer, cfg, 1, batches)
+    elif args.scenario == "save_crash":
+        # a good checkpoint at step 2; during the save at step 3 the last rank dies after its shards are written and
+        # before the temporary folder is renamed (host-side fault: the process exits, nothing is in flight on a device)
+        run_steps(trainer, cfg, 2, batches)
+        good, _ = trainer.save_checkpoint()
+        run_steps(trainer, cfg, 1, batches)
+        from olmo_b200 import checkpoint as ckpt
+
+        if rank == world - 1:
+            ckpt.Checkpointer._save_config = lambda self, *a, **k: os._exit(17)  # called last inside the temporary folder
+        if rank == 0:
+            torch.save({"good": str(good), "world": world}, args.out)
+        try:
+            trainer.save_checkpoint()
+        except Exception as e:  # noqa: BLE001 - the surviving ranks must get an error from their next collective
+            torch.save({"error": type(e).__name__}, f"{args.out}.rank{rank}")
+            os._exit(3)
+        os._exit(0)
     elif args.scenario == "cancel":
         # rank 0 alone owns the clock; every rank must learn of the cancellation at the same step
         trainer._start_time = time.time() - (10_000.0 if rank == 0 else 0.0)

@@ -117,3 +117,59 @@ def test_lost_rank_is_reported_not_hung(tmp_path):
     assert torch.load(f"{out}.rank1", weights_only=False)["left"]
     assert survivor["error"] is not None, proc.stdout[-3000:]
     assert survivor["waited"] < 60
+
+
+# ------------------------------------------------------------------------------ host-side checkpoint faults
+
+
+def test_rank_lost_during_a_save_leaves_no_half_written_checkpoint(tmp_path):
+    """The save protocol writes into ``step{N}-tmp`` and renames after every rank has finished
+    (reference: ``olmo/checkpoint.py:550-603``).  A rank that dies between its shard write and the rename must leave
+    the earlier checkpoint as the latest valid one and no ``step3`` folder at all."""
+    proc = launch(2, "save_crash", tmp_path / "crash.pt", tmp_path / "run", "--pg-timeout", "20", expect_ok=False, timeout=300)
+    assert proc.returncode != 0
+    info = torch.load(tmp_path / "crash.pt", weights_only=False)
+    run = tmp_path / "run"
+    assert Path(info["good"]).name == "step2" and (run / "step2" / "metadata.yaml").is_file()
+    assert not (run / "step3").exists(), sorted(p.name for p in run.iterdir())
+    assert (run / "step3-tmp").is_dir()  # what was written stays out of the way under the temporary name
+    assert (run / "latest").resolve().name == "step2"
+    survivor = torch.load(f"{tmp_path / 'crash.pt'}.rank0", weights_only=False)
+    assert survivor["error"]  # rank 0 got an exception from the barrier, it did not hang
+    # and a new job resumes from the good one
+    got = launch(2, "restore", tmp_path / "resume.pt", tmp_path / "w2", "--load", str(run / "step2"), "--force-fsdp")
+    assert got["global_step"] == 2
+
+
+def _saved_two_rank_checkpoint(tmp_path) -> Path:
+    saved = launch(2, "save", tmp_path / "saved.pt", tmp_path / "run")
+    return Path(saved["sharded"])
+
+
+def test_truncated_and_missing_shard_files_stop_the_restore(tmp_path):
+    import shutil
+
+    from olmo_b200.checkpoint import build_sharded_checkpointer
+    from olmo_b200.config import TrainConfig
+    from olmo_b200.exceptions import OLMoCheckpointError
+
+    good = _saved_two_rank_checkpoint(tmp_path)
+    cfg = TrainConfig.load(good / "config.yaml", validate_paths=False)
+
+    cut = tmp_path / "cut"
+    shutil.copytree(good, cut)
+    victim = cut / "model" / "rank1.pt"
+    victim.write_bytes(victim.read_bytes()[: victim.stat().st_size // 2])
+    with pytest.raises(OLMoCheckpointError, match="rank1.pt.*(truncated|corrupt)"):
+        build_sharded_checkpointer(cfg).unshard_checkpoint(cut)
+    proc = launch(2, "restore", tmp_path / "r_cut.pt", tmp_path / "w_cut", "--load", str(cut), "--force-fsdp", "--pg-timeout", "20", expect_ok=False, timeout=300)
+    assert proc.returncode != 0 and "truncated or corrupt" in proc.stdout
+
+    gone = tmp_path / "gone"
+    shutil.copytree(good, gone)
+    (gone / "optim" / "rank0.pt").unlink()
+    with pytest.raises(FileNotFoundError, match="rank0.pt"):
+        build_sharded_checkpointer(cfg).unshard_checkpoint(gone)
+    # the weights alone are still readable
+    model_state, optim_state, _ = build_sharded_checkpointer(cfg).unshard_checkpoint(gone, load_optimizer_state=False)
+    assert optim_state is None and len(model_state) > 0
