@@ -99,7 +99,24 @@ def _register_path_resolvers(validate_paths: bool) -> None:
             return ""
         return str(latest)
 
+    def data_mix(name: str, local_glob: str = "") -> List[str]:
+        """Token files of a run: the files ``local_glob`` matches when it is given and matches something (a local copy
+        of the data), else the packaged list ``data_mixes/<name>.txt`` (the URLs the official run read, in order)."""
+        if local_glob:
+            hits = sorted(glob(local_glob))
+            if hits:
+                return hits
+        from .data.named_data_mixes import DATA_PATHS
+
+        try:
+            return list(DATA_PATHS[name])
+        except KeyError:
+            if validate_paths:
+                raise FileNotFoundError(f"no local files match '{local_glob}' and there is no packaged data mix '{name}'") from None
+            return []
+
     S.register_resolver("path.glob", path_glob)
+    S.register_resolver("data.mix", data_mix)
     S.register_resolver("path.choose", path_choose)
     S.register_resolver("path.last_checkpoint", path_last_checkpoint)
 

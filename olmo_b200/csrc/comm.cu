@@ -8,11 +8,10 @@ namespace {
 
 constexpr int COMM_THREADS = 512;
 
-constexpr int COMM_SMEM = 1024 + COMM_MAX_STAGES * COMM_STAGE_BYTES + 256;
-
-__global__ void __launch_bounds__(COMM_THREADS) comm_kernel(const __grid_constant__ CommTask task, int smem_bytes) {
-  extern __shared__ uint8_t comm_smem[];
-  comm_run(task, blockIdx.x, gridDim.x, smem_bytes > 0 ? comm_smem : nullptr, smem_bytes);
+__global__ void __launch_bounds__(COMM_THREADS) comm_kernel(const __grid_constant__ CommTask task) {
+  __shared__ CommScratch scratch;
+  const CommGroup g = {static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x), 1};
+  comm_run(task, blockIdx.x, gridDim.x, &scratch, g);
 }
 
 struct WaitList {
@@ -80,16 +79,8 @@ extern "C" int ob_comm_launch(const void* task, int nctas, cudaStream_t stream) 
   if (t == nullptr || t->world < 1 || t->world > COMM_MAX_WORLD || nctas < 1) return -1;
   if (t->kind == COMM_ALL_GATHER && (t->elems % 8 != 0)) return -2;
   if (t->kind == COMM_REDUCE_SCATTER && (t->elems % 4 != 0)) return -2;
-  int smem = 0;
-  if (t->mode & COMM_MODE_BULK) {
-    static bool configured = false;
-    if (!configured) {
-      if (cudaFuncSetAttribute(comm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, COMM_SMEM) != cudaSuccess) return -10;
-      configured = true;
-    }
-    smem = COMM_SMEM;
-  }
-  comm_kernel<<<nctas, COMM_THREADS, smem, stream>>>(*t, smem);
+  if (nctas > COMM_MAX_PARTS) return -1;
+  comm_kernel<<<nctas, COMM_THREADS, 0, stream>>>(*t);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 

@@ -10,7 +10,8 @@
 //   warps 2..5  epilogue            (tcgen05.ld 32x32b from one of two 256-column accumulators -> global)
 // The two TMEM accumulators let the epilogue of tile i overlap the main loop of tile i+1.
 //
-// Optional communication CTAs: when `comm_ctas` > 0 the first `comm_ctas` blocks of the grid execute a CommTask
+// A launch may carry a collective (CommTask, comm.cuh).  With `comm_ctas` == 0 the spare warps 6..15 of every CTA execute
+// their CTA's share of it next to the tensor-core pipeline; with `comm_ctas` > 0 the first `comm_ctas` blocks of the grid execute it
 // (comm.cuh: peer all-gather of the next unit's weights, or the gradient reduce-scatter of the previous unit) and
 // exit; the remaining blocks are the persistent GEMM.  One launch therefore overlaps NVLink traffic with the math.
 //
@@ -61,8 +62,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
                  const int* __restrict__ b_ready, int rows_per_flag, int ready_value, int* __restrict__ status,
                  const __grid_constant__ CommTask comm_task, int comm_ctas) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ CommScratch comm_scratch;
   if (static_cast<int>(blockIdx.x) < comm_ctas) {  // communication role: no TMEM, no barriers
-    comm_run(comm_task, blockIdx.x, comm_ctas, smem_raw, SMEM_BYTES);
+    const CommGroup g = {static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x), 1};
+    comm_run(comm_task, blockIdx.x, comm_ctas, &comm_scratch, g);
     return;
   }
   const int cta = static_cast<int>(blockIdx.x) - comm_ctas;
@@ -291,6 +294,10 @@ gemm_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constan
         acc_phase ^= 1u;
       }
     }
+  } else if (comm_ctas == 0 && comm_task.kind != COMM_NONE) {
+    // ------------------------------------------------ communication warps (6..15) of a launch that carries a collective
+    const CommGroup g = {static_cast<int>(threadIdx.x) - NUM_THREADS, static_cast<int>(blockDim.x) - NUM_THREADS, 1};
+    if (g.nthr >= 32) comm_run(comm_task, blockIdx.x, gridDim.x, &comm_scratch, g);
   }
 
   tc_fence_before();
@@ -365,7 +372,8 @@ static int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, void* C, co
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   if (comm_ctas < 0 || comm_ctas >= num_sms) return -12;
   const int gemm_ctas = tiles < num_sms - comm_ctas ? tiles : num_sms - comm_ctas;
-  kern<<<gemm_ctas + comm_ctas, comm_ctas > 0 ? NUM_THREADS_COMM : NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc,
+  const bool carries = comm_ctas > 0 || comm_task.kind != COMM_NONE;
+  kern<<<gemm_ctas + comm_ctas, carries ? NUM_THREADS_COMM : NUM_THREADS, SMEM_BYTES, stream>>>(ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc,
                                                                   vec_ok, b_ready, rows_per_flag, ready_value, status,
                                                                   comm_task, comm_ctas);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;

@@ -4,8 +4,9 @@
 // own TMEM.  Compared with the single-CTA kernel (gemm.cu) every SM loads a third less operand data per FLOP, which
 // leaves room for a six-stage ring (192 KiB) and keeps the tensor pipe fed under L2 latency.
 //
-// Roles per CTA (512 threads when communication CTAs ride along, else 192): warp 0 TMA producer, warp 1 MMA issuer
-// (leader CTA only; owns the TMEM allocation in both CTAs), warps 2..5 epilogue.
+// Roles per CTA (512 threads when the launch carries a collective, else 192): warp 0 TMA producer, warp 1 MMA issuer
+// (leader CTA only; owns the TMEM allocation in both CTAs), warps 2..5 epilogue, warps 6..15 communication (comm.cuh:
+// every CTA moves its share of the collective with its spare warps; alternatively whole CTA pairs are set aside for it).
 // Cross-CTA signalling: operand loads of both CTAs complete on the leader's `full` barrier (the `cta_group::2` form of
 // the tensor copy takes a cluster address for its barrier; each CTA still fetches only its own tile); the leader's tcgen05.commit arrives
 // on the `empty` / `accumulator full` barriers of both CTAs; epilogue threads of both CTAs arrive on the leader's
@@ -108,8 +109,10 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
                   void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
                   int* __restrict__ status, const __grid_constant__ CommTask comm_task, int comm_ctas) {
   extern __shared__ uint8_t smem_raw[];
+  __shared__ CommScratch comm_scratch;
   if (static_cast<int>(blockIdx.x) < comm_ctas) {  // communication pairs (comm_ctas is even): no TMEM, no barriers
-    comm_run(comm_task, blockIdx.x, comm_ctas, smem_raw, G2_SMEM);
+    const CommGroup g = {static_cast<int>(threadIdx.x), static_cast<int>(blockDim.x), 1};
+    comm_run(comm_task, blockIdx.x, comm_ctas, &comm_scratch, g);
     return;
   }
   const uint32_t rank = cluster_ctarank();
@@ -339,6 +342,11 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
         acc_phase ^= 1u;
       }
     }
+  } else if (comm_ctas == 0 && comm_task.kind != COMM_NONE) {
+    // ------------------------------------------------ communication warps (6..15) of a launch that carries a collective:
+    // this CTA's share of the task, moved by plain peer loads while the six role warps above run the tiles
+    const CommGroup g = {static_cast<int>(threadIdx.x) - G2_THREADS, static_cast<int>(blockDim.x) - G2_THREADS, 1};
+    if (g.nthr >= 32) comm_run(comm_task, blockIdx.x, gridDim.x, &comm_scratch, g);
   }
 
   tc_fence_before();
@@ -364,7 +372,8 @@ int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const vo
   const int tiles = ((M + 2 * G2_BM - 1) / (2 * G2_BM)) * ((N + G2_BN - 1) / G2_BN);
   int pairs = (num_sms - comm_ctas) / 2;
   if (tiles < pairs) pairs = tiles;
-  kern<<<2 * pairs + comm_ctas, comm_ctas > 0 ? G2_THREADS_COMM : G2_THREADS, G2_SMEM, stream>>>(
+  const bool carries = comm_ctas > 0 || comm_task.kind != COMM_NONE;
+  kern<<<2 * pairs + comm_ctas, carries ? G2_THREADS_COMM : G2_THREADS, G2_SMEM, stream>>>(
       ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc, vec_ok, status, comm_task, comm_ctas);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }

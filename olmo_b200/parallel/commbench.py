@@ -66,7 +66,7 @@ def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--tokens", type=int, default=8192, help="rows of the activation matrix (micro-batch 2 x 4096)")
-    ap.add_argument("--ag-ctas", type=int, default=None, help="communication CTAs per gather-carrying launch (default: engine default)")
+    ap.add_argument("--ag-ctas", type=int, default=None, help="CTAs set aside per gather-carrying launch; 0 = the spare warps of every GEMM CTA (default: engine default)")
     ap.add_argument("--rs-ctas", type=int, default=None, help="communication CTAs per reduce-scatter-carrying launch")
     args = ap.parse_args()
 
@@ -85,8 +85,8 @@ def main() -> None:
     unit = SimpleNamespace(index=0, numel=numel, shard_size=shard, grad=torch.zeros(shard, dtype=torch.float32, device=dev))
     engine = SimpleNamespace(device=dev, shard_world=world, shard_rank=rank, world=world, compute_dtype=torch.bfloat16, units=[unit])
     comm = PeerComm(engine, dist.group.WORLD)
-    ctas = args.ag_ctas or comm.comm_ctas
-    rs_ctas = args.rs_ctas or comm.rs_ctas
+    ctas = comm.comm_ctas if args.ag_ctas is None else args.ag_ctas
+    rs_ctas = comm.rs_ctas if args.rs_ctas is None else args.rs_ctas
     comm.full_all.normal_(0, 0.02)
     comm.gfull_all.normal_(0, 1.0)
 

@@ -71,7 +71,7 @@ class CommTask(ctypes.Structure):
     ]
 
 
-COMM_MODE_BULK, COMM_MODE_SELF = 1, 2
+COMM_MODE_SELF = 2
 N_GSLOTS, N_FULL_SLOTS = 3, 2
 
 
@@ -142,18 +142,16 @@ class PeerComm:
         self.gfull_ptrs = [int(p) for p in self.h_gfull.buffer_ptrs]
         self.ctrl_ptrs = [int(p) for p in self.h_ctrl.buffer_ptrs]
         self.gslot_use = [0] * N_GSLOTS  # how often each gradient slot has been handed out (same on every rank)
-        # bulk-async copies through shared memory (default) or plain per-thread peer loads
-        self.bulk = os.environ.get("OLMO_B200_COMM_BULK", "1").strip().lower() not in ("0", "false", "no", "off")
         self.slot_ptrs_dev = torch.tensor([p + 4 * self.slot_off for p in self.ctrl_ptrs], dtype=torch.int64, device=dev)
         self.param_epoch = 0
         self.grad_epoch = 0
         self.scalar_epoch = 0
-        # Communication CTAs per fused launch.  A gather is a pure copy and needs few CTAs to keep pace with the GEMM it
-        # rides on; a reduce-scatter moves twice the bytes and does arithmetic, so it gets more.  Both are even numbers
-        # (the two-CTA GEMM schedules CTA pairs).
-        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "4" if self.bulk else "8"))
-        self.rs_ctas = int(os.environ.get("OLMO_B200_RS_CTAS", "8" if self.bulk else "16"))
-        self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "16" if self.bulk else "64"))
+        # How a GEMM launch carries a collective.  0 (default): the ten spare warps of every GEMM CTA move that CTA's
+        # share, so no SM is taken from the GEMM.  An even number n > 0: the first n CTAs of the grid are set aside for
+        # the collective instead (the two-CTA GEMM schedules CTA pairs).
+        self.comm_ctas = int(os.environ.get("OLMO_B200_COMM_CTAS", "0"))
+        self.rs_ctas = int(os.environ.get("OLMO_B200_RS_CTAS", "0"))
+        self.standalone_ctas = int(os.environ.get("OLMO_B200_COMM_STANDALONE_CTAS", "64"))
         ms = float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000"))
         self.wait_cycles = int(ms * 1.9e6)
         self._scalar_out = torch.zeros(1, dtype=torch.float32, device=dev)
@@ -198,7 +196,7 @@ class PeerComm:
         t.status = status_tensor(self.engine.device).data_ptr()
         t.wait_cycles = self.wait_cycles
         t.sumsq_partials = None
-        t.mode = COMM_MODE_BULK if self.bulk else 0
+        t.mode = 0
         return t
 
     @staticmethod

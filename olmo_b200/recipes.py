@@ -143,6 +143,31 @@ RECIPES: Dict[str, Dict[str, Any]] = {
         "evaluators": _CORE_TASKS,
     },
 }
+# The published stage-2 ("mid-training") runs: the same recipe from the stage-1 endpoint with different data-order
+# seeds (their weights are averaged afterwards); reference: configs/official-1124/OLMo2-{7B,13B}-stage2-seed*.yaml and
+# configs/official-0425/OLMo2-1B-stage2-seed*.yaml.
+for _seed in (42, 42069, 666):
+    RECIPES[f"OLMo2-7B-stage2-seed{_seed}"] = {
+        **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": f"official-1124/OLMo2-7B-stage2-seed{_seed}.yaml", "seed": _seed,
+        "load_path": "${oc.env:OLMO_STAGE1_CHECKPOINT,https://olmo-checkpoints.org/ai2-llm/peteish7/step928646-unsharded}",
+    }
+    RECIPES[f"OLMo2-1B-stage2-seed{_seed}"] = {
+        **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": f"official-0425/OLMo2-1B-stage2-seed{_seed}.yaml", "family": "olmo2-1b",
+        "seed": _seed, "optimizer": _adamw(0.000074487, **_OLMO2_OPT), "global_train_batch_size": 512,
+        "device_train_microbatch_size": 4, "max_duration": "50e9T", "stop_at": 23852,
+        "load_path": "${oc.env:OLMO_STAGE1_CHECKPOINT,https://olmo-checkpoints.org/ai2-llm/peteish1/step1907359-unsharded/}",
+    }
+for _seed, _tokens, _stop in ((1110, "100B", 11931), (2662, "100B", 11931), (6209, "100B", 11931), (2662, "300B", 35773)):
+    RECIPES[f"OLMo2-13B-stage2-seed{_seed}-{_tokens}"] = {
+        **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": f"official-1124/OLMo2-13B-stage2-seed{_seed}-{_tokens}.yaml",
+        "family": "olmo2-13b", "seed": _seed, "optimizer": _adamw(9e-5, **_OLMO2_OPT),
+        "scheduler": {"name": "linear_with_warmup", "units": "steps", "t_warmup": 0, "alpha_f": 0.0},
+        "global_train_batch_size": 2048, "device_train_microbatch_size": 2, "max_duration": f"{_tokens[:-1]}e9T", "stop_at": _stop,
+        "load_path": "${oc.env:OLMO_STAGE1_CHECKPOINT,https://olmo-checkpoints.org/ai2-llm/peteish13/step596057-unsharded}",
+    }
+# OLMo-7B-0424 is the run OLMo-7B-0724 continued; the two published configs are the same file
+RECIPES["OLMo-7B-0424"] = {**deepcopy(RECIPES["OLMo-7B-0724"]), "file": "official-0724/OLMo-7B-0424.yaml"}
+
 for _name, _mb in (("20M", 16), ("60M", 8), ("150M", 4), ("300M", 4), ("700M", 2)):
     RECIPES[f"OLMo-{_name}"] = {
         "file": f"tiny/OLMo-{_name}.yaml", "family": f"tiny-{_name.lower()}", "tokenizer": _TOK_DOLMA15,
@@ -185,6 +210,12 @@ RECIPES["custom-dataset-example"] = {
             "collate_config": {"input_id_field": "token_ids", "label_mask_field": None, "metadata_field": None},
         },
     },
+}
+
+#: recipe name -> packaged ``data_mixes/<name>.txt`` when the two differ
+_MIX_ALIASES = {
+    "OLMo2-7B-stage2": "OLMo2-7B-stage2-seed42", "peteish1": "peteish1-weka", "peteish7": "peteish7-weka", "peteish13": "peteish13-weka",
+    "OLMo2-7B-anneal-example": "peteish7-weka-anneal-from-928646-50B-nowup_legal-whammy-2_seed42",
 }
 
 _COMMON: Dict[str, Any] = {
@@ -239,8 +270,12 @@ def recipe_dict(name: str) -> Dict[str, Any]:
     if out["model"]["vocab_size"] < 65536:
         out["data"]["memmap_dtype"] = "uint16"
     out["evaluators"] = [{"label": label, "type": "downstream"} for label in spec.pop("evaluators")]
+    mix = spec.pop("mix", _MIX_ALIASES.get(name, name))
     if "data" in spec:
         out["data"] = S.deep_merge(out["data"], spec.pop("data"))
+    elif mix is not None:
+        # a local copy of the data (OLMO_DATA_GLOB) wins; otherwise the packaged list of the files the published run read
+        out["data"]["paths"] = "${data.mix:" + mix + ",${oc.env:OLMO_DATA_GLOB,}}"
     out.update(spec)
     return out
 
@@ -265,7 +300,8 @@ def write_configs(folder: Path, names: Optional[List[str]] = None) -> List[Path]
         target.parent.mkdir(parents=True, exist_ok=True)
         header = (
             f"# {name}: generated by `python -m olmo_b200.recipes --write <dir>`; edit olmo_b200/recipes.py, not this file.\n"
-            "# Token files: set OLMO_DATA_GLOB (e.g. '/data/dolma/**/*.npy') or override data.paths on the command line.\n"
+            "# Token files: data.paths is the packaged list of the files the published run read (olmo_data/data_mixes/);\n"
+            "# set OLMO_DATA_GLOB (e.g. '/data/dolma/**/*.npy') to train on a local copy, or override data.paths.\n"
         )
         target.write_text(header + S.dump_yaml(recipe_dict(name)))
         written.append(target)

@@ -20,13 +20,14 @@ def main() -> None:
     ap.add_argument("--fused-comm", type=int, default=1)
     ap.add_argument("--strategy", default="FULL_SHARD")
     ap.add_argument("--schedule", default="resident", choices=["resident", "sharded", "auto"])
-    ap.add_argument("--bulk", type=int, default=1)
+    ap.add_argument("--comm-ctas", type=int, default=0, help="0: communication warps in every GEMM CTA; n > 0: n CTAs set aside")
     ap.add_argument("--layers", type=int, default=3)
     ap.add_argument("--activation-checkpointing", default=None)
     args = ap.parse_args()
     os.environ["OLMO_B200_FUSED_COMM"] = str(args.fused_comm)
     os.environ["OLMO_B200_SCHEDULE"] = args.schedule
-    os.environ["OLMO_B200_COMM_BULK"] = str(args.bulk)
+    os.environ["OLMO_B200_COMM_CTAS"] = str(args.comm_ctas)
+    os.environ["OLMO_B200_RS_CTAS"] = str(2 * args.comm_ctas)
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
     from olmo_b200 import ops

@@ -1,5 +1,6 @@
 """Typed config engine: YAML quirks, overrides, interpolation, resolvers, legacy rewrites, recipes."""
 import os
+from pathlib import Path
 
 import pytest
 
@@ -174,3 +175,43 @@ def test_committed_config_files_match_the_recipes():
     for name, spec in RECIPES.items():
         on_disk = TrainConfig.load(root / spec["file"], validate_paths=False)
         assert on_disk == recipe_config(name), f"configs/{spec['file']} is stale: rerun python -m olmo_b200.recipes --write configs"
+
+
+def test_official_config_resolves_tokenizer_data_mix_and_evaluators_from_package_data(monkeypatch):
+    """No environment variable: the tokenizer file, the ordered list of the run's token files and the evaluation sets
+    come from the ``olmo_data`` package."""
+    import torch
+
+    from olmo_b200.eval import build_evaluator
+    from olmo_b200.launch import derive_batch_sizes
+    from olmo_b200.tokenizer import Tokenizer
+
+    monkeypatch.delenv("OLMO_DATA_GLOB", raising=False)
+    monkeypatch.delenv("OLMO_DATA_DIR", raising=False)
+    root = Path(__file__).resolve().parent.parent
+    cfg = TrainConfig.load(root / "configs" / "official-1124" / "OLMo2-7B-stage1.yaml", validate_paths=False)
+    assert len(cfg.data.paths) == 1122 and cfg.data.paths[0].startswith("http") and cfg.data.paths[0].endswith(".npy")
+    derive_batch_sizes(cfg, 1)
+    tok = Tokenizer.from_train_config(cfg)
+    assert tok.vocab_size == 100278 and tok.eos_token_id == 100257
+    labels = [e.label for e in cfg.evaluators]
+    assert len(labels) == 27
+    for ec in cfg.evaluators:
+        if ec.label in ("piqa", "arc_easy", "mmlu_stem_var", "basic_arithmetic"):
+            ev = build_evaluator(cfg, ec, tok, torch.device("cpu"))
+            assert len(ev.eval_loader.dataset) > 0
+    # a local copy of the data takes precedence over the packaged list
+    monkeypatch.setenv("OLMO_DATA_GLOB", str(root / "test_fixtures" / "*.gz"))
+    local = TrainConfig.load(root / "configs" / "official-1124" / "OLMo2-7B-stage1.yaml", validate_paths=False)
+    assert local.data.paths and all(p.endswith(".gz") for p in local.data.paths)
+
+
+def test_named_data_mixes_and_checkpoint_tables_are_packaged():
+    from olmo_b200.data.named_data_mixes import DATA_PATHS, resolve_mix
+
+    assert {"dolma17", "dolma17_flan_sep_rulebased", "olmoe-mix-0924"} <= set(DATA_PATHS)
+    assert len(DATA_PATHS["dolma17"]) == 1033
+    assert resolve_mix("olmoe-mix-0924", "s3://bucket/")[0].startswith("s3://bucket/")
+    root = Path(__file__).resolve().parent.parent / "configs"
+    for rel in ("official-1124/OLMo-2-1124-7B.csv", "official-1124/OLMo-2-1124-13B.csv", "official-0425/OLMo-2-0425-1B.csv", "official-0724/OLMo-7B-0724.csv"):
+        assert (root / rel).is_file(), rel

@@ -52,13 +52,13 @@ def test_two_ranks_match_one(tmp_path, fused_comm):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("bulk", [1, 0])
-def test_sharded_schedule_matches_one(tmp_path, bulk):
+@pytest.mark.parametrize("comm_ctas", [0, 8])
+def test_sharded_schedule_matches_one(tmp_path, comm_ctas):
     """The FULL_SHARD schedule proper (block units streamed through parameter and gradient slots, a gather in forward and
     in backward and a reduce-scatter per micro-batch, all riding on block GEMMs) against one GPU on the same batch."""
     single = _run(1, tmp_path / "one.pt", "--layers", "5")
-    multi = _run(2, tmp_path / f"sharded_{bulk}.pt", "--schedule", "sharded", "--layers", "5", "--bulk", str(bulk))
-    _compare(multi, single, f"2 ranks sharded schedule (bulk={bulk}) vs 1")
+    multi = _run(2, tmp_path / f"sharded_{comm_ctas}.pt", "--schedule", "sharded", "--layers", "5", "--comm-ctas", str(comm_ctas))
+    _compare(multi, single, f"2 ranks sharded schedule (comm_ctas={comm_ctas}) vs 1")
     assert abs(multi["eval_ce"] - multi["module_ce"]) < 2e-2 * abs(multi["module_ce"]), (multi["eval_ce"], multi["module_ce"])
     assert abs(multi["eval_ce"] - single["eval_ce"]) < 2e-2 * abs(single["eval_ce"])
 
