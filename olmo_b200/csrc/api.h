@@ -39,6 +39,7 @@ int ob_attention_bwd(const void* dout, const void* q, const void* k, const void*
 // doc_start (optional, causal only): int32 [B, T], position of the first token of the document each token belongs to.
 void ob_set_gemm_pair_mode(int on);  // 1: two-CTA (cta_group::2) GEMM kernel where applicable
 int ob_get_gemm_pair_mode(void);
+void ob_set_gemm_tma_store(int on);   // 1 (default): the two-CTA GEMM writes its output tiles through shared memory and TMA stores
 
 // ---- comm.cu (peer-memory collectives; `task` points at an ob::CommTask, see comm.cuh)
 int ob_comm_task_size(void);

@@ -19,7 +19,7 @@ namespace ob {
 constexpr int COMM_MAX_WORLD = 8;
 
 enum : int { COMM_NONE = 0, COMM_ALL_GATHER = 1, COMM_REDUCE_SCATTER = 2 };
-enum : int { COMM_MODE_SELF = 2 };
+enum : int { COMM_MODE_SELF = 2, COMM_MODE_STORE = 4 };
 
 struct CommTask {
   int kind;
@@ -35,7 +35,8 @@ struct CommTask {
   float* sumsq_partials;          // reduce-scatter, optional: partial[c] += sum of squares of dst after part c's additions
   int* status;
   long long wait_cycles;          // budget of every flag wait in this task (0: library default)
-  int mode;                       // bit 1 (COMM_MODE_SELF): an all-gather also copies this rank's own region
+  int mode;                       // bit 1 (COMM_MODE_SELF): an all-gather also copies this rank's own region;
+                                  // bit 2 (COMM_MODE_STORE): a reduce-scatter overwrites dst instead of adding to it
   int reserved;
 };
 
@@ -124,7 +125,7 @@ __device__ __forceinline__ void rs_load(const CommTask& t, RsTile<W, U>& r, long
     if (i < vecs) {
 #pragma unroll
       for (int p = 0; p < W; ++p) r.v[p][u] = ld_peer_16(reinterpret_cast<const uint4*>(t.src[p]) + i);
-      r.d[u] = dst[i];
+      r.d[u] = (t.mode & COMM_MODE_STORE) ? make_float4(0.f, 0.f, 0.f, 0.f) : dst[i];
     }
   }
 }

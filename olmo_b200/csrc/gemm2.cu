@@ -20,6 +20,9 @@ namespace ob {
 
 int make_tensor_map_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
                             uint32_t box_inner, uint32_t box_outer);
+int make_tensor_map_f32_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t ld,
+                           uint32_t box_inner, uint32_t box_outer);
+int g_gemm2_tma_store = 1;  // 0: epilogue threads store their rows directly (kept for comparison, see ob_set_gemm_tma_store)
 
 namespace {
 
@@ -33,7 +36,9 @@ constexpr int G2_STAGE_BYTES = G2_A_BYTES + G2_B_BYTES;
 constexpr int G2_CHUNK_BYTES = 64 * G2_BK * 2;
 constexpr int G2_THREADS = 192;
 constexpr int G2_THREADS_COMM = 512;
-constexpr int G2_SMEM = 1024 + G2_STAGES * G2_STAGE_BYTES + 256;
+constexpr int G2_OUT_BYTES = 4096;  // one epilogue warp's staging tile: 32 rows x 128 bytes, 128-byte swizzle
+constexpr int G2_OUT_TOTAL = 4 * 2 * G2_OUT_BYTES;  // four epilogue warps, double buffered
+constexpr int G2_SMEM = 1024 + G2_STAGES * G2_STAGE_BYTES + G2_OUT_TOTAL + 256;
 constexpr int G2_GROUP_M = 8;
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -106,6 +111,7 @@ __device__ __forceinline__ Tile2 tile2_coord(int t, int tiles_m, int tiles_n) {
 template <int A_MN, int B_MN, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(G2_THREADS_COMM, 1)
 gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
+                  const __grid_constant__ CUtensorMap tma_c, int use_tma_c,
                   void* __restrict__ Cptr, const bf16* __restrict__ Rptr, int M, int N, int K, int ldc, int vec_ok,
                   int* __restrict__ status, const __grid_constant__ CommTask comm_task, int comm_ctas) {
   extern __shared__ uint8_t smem_raw[];
@@ -123,7 +129,8 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + G2_STAGES * G2_A_BYTES;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + G2_STAGES * G2_STAGE_BYTES);
+  uint8_t* sOut = smem + G2_STAGES * G2_STAGE_BYTES;  // 1024-byte aligned, as the swizzle pattern of the staging tiles needs
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + G2_OUT_TOTAL);
   uint64_t* empty_bar = full_bar + G2_STAGES;
   uint64_t* tfull_bar = empty_bar + G2_STAGES;
   uint64_t* tempty_bar = tfull_bar + 2;
@@ -256,6 +263,7 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
     const int quarter = warp & 3;
     int acc = 0;
     uint32_t acc_phase = 0;
+    uint32_t out_buf = 0;
     for (int t = pair; t < num_tiles; t += num_pairs) {
       const Tile2 tc = tile2_coord(t, tiles_m, tiles_n);
       const int row = tc.m * 2 * G2_BM + static_cast<int>(rank) * G2_BM + quarter * 32 + lane;
@@ -264,6 +272,75 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
       tc_fence_after();
       __syncwarp();
       const uint32_t t_addr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * G2_BN);
+      if (use_tma_c) {
+        // Output through shared memory: every epilogue warp packs its 32 rows of a 64-column (bf16) or 32-column (fp32)
+        // slab into a 128-byte-swizzled staging tile and one lane hands it to the TMA unit, as a plain store or, for the
+        // accumulating epilogue, as a reduce-add performed at the memory side (the old values are never loaded).  Rows and
+        // columns beyond the matrix are clipped by the tensor map.  Two staging tiles per warp alternate.
+        constexpr bool OUT16 = (EPI == EPI_BF16 || EPI == EPI_BF16_ADD);
+        constexpr int SLAB = OUT16 ? 64 : 32;  // columns per TMA operation (128 bytes per row)
+        const int row0 = tc.m * 2 * G2_BM + static_cast<int>(rank) * G2_BM + quarter * 32;
+#pragma unroll 1
+        for (int sl = 0; sl < G2_BN / SLAB; ++sl) {
+          const int colS = n0 + sl * SLAB;
+          uint8_t* buf = sOut + (quarter * 2 + (out_buf & 1)) * G2_OUT_BYTES;
+          if (lane == 0) tma_store_wait_read<1>();  // the store issued from this buffer two slabs ago has read it
+          __syncwarp();
+          uint8_t* myrow = buf + lane * 128;
+#pragma unroll
+          for (int hc = 0; hc < SLAB / 32; ++hc) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(t_addr + sl * SLAB + hc * 32, r);
+            tmem_ld_wait();
+            if (OUT16) {
+              const int col0 = colS + hc * 32;
+#pragma unroll
+              for (int v = 0; v < 4; ++v) {
+                float f[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) f[j] = __uint_as_float(r[v * 8 + j]);
+                if (EPI == EPI_BF16_ADD && row < M && col0 + v * 8 + 8 <= N) {
+                  const uint4 rv = *reinterpret_cast<const uint4*>(Rptr + static_cast<size_t>(row) * ldc + col0 + v * 8);
+                  const uint32_t ru[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                  for (int j = 0; j < 4; ++j) {
+                    const float2 pr = unpack_bf16x2(ru[j]);
+                    f[2 * j] += pr.x;
+                    f[2 * j + 1] += pr.y;
+                  }
+                }
+                uint4 o;
+                o.x = pack_bf16x2(f[0], f[1]);
+                o.y = pack_bf16x2(f[2], f[3]);
+                o.z = pack_bf16x2(f[4], f[5]);
+                o.w = pack_bf16x2(f[6], f[7]);
+                const int chunk = hc * 4 + v;
+                *reinterpret_cast<uint4*>(myrow + ((chunk ^ (lane & 7)) << 4)) = o;
+              }
+            } else {
+#pragma unroll
+              for (int v = 0; v < 8; ++v)
+                *reinterpret_cast<uint4*>(myrow + ((v ^ (lane & 7)) << 4)) = make_uint4(r[v * 4 + 0], r[v * 4 + 1], r[v * 4 + 2], r[v * 4 + 3]);
+            }
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0 && row0 < M && colS < N) {
+            if (EPI == EPI_F32_ACCUM) tma_reduce_add_2d(&tma_c, buf, colS, row0);
+            else tma_store_2d(&tma_c, buf, colS, row0);
+          }
+          if (lane == 0) tma_store_commit();
+          ++out_buf;
+        }
+        tc_fence_before();
+        if (leader) mbar_arrive(&tempty_bar[acc]);
+        else mbar_arrive_cluster(map_to_cta(smem_u32(&tempty_bar[acc]), 0));
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < G2_BN / 32; ++c) {
         uint32_t r[32];
@@ -342,6 +419,7 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
         acc_phase ^= 1u;
       }
     }
+    if (use_tma_c && lane == 0) tma_store_wait<0>();  // every store / reduce-add of this warp has been performed
   } else if (comm_ctas == 0 && comm_task.kind != COMM_NONE) {
     // ------------------------------------------------ communication warps (6..15) of a launch that carries a collective:
     // this CTA's share of the task, moved by plain peer loads while the six role warps above run the tiles
@@ -359,7 +437,7 @@ gemm2_bf16_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_consta
 }
 
 template <int A_MN, int B_MN, int EPI>
-int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const void* R, int M, int N, int K, int ldc, int vec_ok,
+int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, int use_tma_c, void* C, const void* R, int M, int N, int K, int ldc, int vec_ok,
                  int* status, int num_sms, const CommTask& comm_task, int comm_ctas, cudaStream_t stream) {
   auto kern = gemm2_bf16_kernel<A_MN, B_MN, EPI>;
   static bool configured = false;
@@ -374,7 +452,7 @@ int launch_gemm2(const CUtensorMap& ta, const CUtensorMap& tb, void* C, const vo
   if (tiles < pairs) pairs = tiles;
   const bool carries = comm_ctas > 0 || comm_task.kind != COMM_NONE;
   kern<<<2 * pairs + comm_ctas, carries ? G2_THREADS_COMM : G2_THREADS, G2_SMEM, stream>>>(
-      ta, tb, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc, vec_ok, status, comm_task, comm_ctas);
+      ta, tb, tcm, use_tma_c, C, reinterpret_cast<const bf16*>(R), M, N, K, ldc, vec_ok, status, comm_task, comm_ctas);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }
 
@@ -394,9 +472,17 @@ int gemm2_dispatch(const void* A, const void* B, void* C, const void* R, int M, 
   const int esize = (epi == EPI_BF16 || epi == EPI_BF16_ADD) ? 2 : 4;
   int vec_ok = ((reinterpret_cast<uintptr_t>(C) & 15) == 0) && ((static_cast<size_t>(ldc) * esize) % 16 == 0);
   if (epi == EPI_BF16_ADD) vec_ok = vec_ok && ((reinterpret_cast<uintptr_t>(R) & 15) == 0);
+  // output tiles leave through shared memory and the TMA unit when the output is 16-byte aligned with a 16-byte pitch
+  CUtensorMap tcm = ta;
+  int use_tma_c = vec_ok && (N % 8 == 0) && g_gemm2_tma_store;
+  if (use_tma_c) {
+    rc = esize == 2 ? make_tensor_map_bf16_2d(&tcm, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 64, 32)
+                    : make_tensor_map_f32_2d(&tcm, C, (uint64_t)N, (uint64_t)M, (uint64_t)ldc, 32, 32);
+    if (rc != 0) use_tma_c = 0;
+  }
 #define OB_DISPATCH2(AM, BMJ, E)                                                                                         \
   if (a_mn_major == AM && b_mn_major == BMJ && epi == E)                                                                 \
-    return launch_gemm2<AM, BMJ, E>(ta, tb, C, R, M, N, K, ldc, vec_ok, status, num_sms, comm_task, comm_ctas, stream);
+    return launch_gemm2<AM, BMJ, E>(ta, tb, tcm, use_tma_c, C, R, M, N, K, ldc, vec_ok, status, num_sms, comm_task, comm_ctas, stream);
   OB_DISPATCH2(0, 0, EPI_BF16)
   OB_DISPATCH2(0, 0, EPI_BF16_ADD)
   OB_DISPATCH2(0, 0, EPI_F32_STORE)
@@ -411,3 +497,5 @@ int gemm2_dispatch(const void* A, const void* B, void* C, const void* R, int M, 
 }
 
 }  // namespace ob
+
+extern "C" void ob_set_gemm_tma_store(int on) { ob::g_gemm2_tma_store = on; }

@@ -105,6 +105,7 @@ def lib() -> ctypes.CDLL:
                 )
         _lib = ctypes.CDLL(str(_SO_PATH))
         _lib.ob_set_gemm_pair_mode(ctypes.c_int(int(os.environ.get("OLMO_B200_GEMM_2CTA", "1") not in ("0", "", "false"))))
+        _lib.ob_set_gemm_tma_store(ctypes.c_int(int(os.environ.get("OLMO_B200_GEMM_TMA_STORE", "1") not in ("0", "", "false"))))
     return _lib
 
 

@@ -21,15 +21,28 @@ def _have_symbol(name: str) -> bool:
         return False
 
 
+TILE = 128  # the kernels work on 128-row tiles of 128-wide heads
+
+
+def _needs_padding(q: torch.Tensor) -> bool:
+    return q.shape[-1] != TILE or q.shape[1] % TILE != 0
+
+
 def supports(q: torch.Tensor, k: torch.Tensor, causal: bool, dropout_p: float, varlen: bool) -> bool:
-    """Forward kernel coverage: bf16, head dim 128, no dropout, self-attention (Tq == Tk), T % 128 == 0.  ``varlen`` means
-    packed sequences described by cumulative lengths; document masking inside fixed-length sequences is expressed with
-    ``doc_start`` instead (see :func:`doc_start_from_lengths`) and is covered when ``causal``."""
+    """Kernel coverage: bf16, no dropout, self-attention (Tq == Tk), query heads a multiple of key heads, and either the
+    kernels' own tile shape (head dim 128, T a multiple of 128) or a shape that zero padding brings to it: a head
+    dimension below 128 that is a multiple of 8 (the extra columns add nothing to a score and produce zero outputs), and,
+    for causal attention, any sequence length (padded keys come after every real query, so the causal mask hides them).
+    ``varlen`` means packed sequences described by cumulative lengths; document masking inside fixed-length sequences
+    is expressed with ``doc_start`` instead (see :func:`doc_start_from_lengths`) and is covered when ``causal``."""
     if varlen or dropout_p != 0.0 or q.dtype != torch.bfloat16 or not q.is_cuda:
         return False
-    if q.dim() != 4 or q.shape[-1] != 128 or q.shape[1] != k.shape[1] or q.shape[1] % 128 != 0:
+    if q.dim() != 4 or q.shape[1] != k.shape[1] or q.shape[2] % k.shape[2] != 0:
         return False
-    if q.shape[2] % k.shape[2] != 0:
+    D, T = q.shape[-1], q.shape[1]
+    if D > TILE or D % 8 != 0 or k.shape[-1] != D:
+        return False
+    if T % TILE != 0 and not causal:
         return False
     return _have_symbol("ob_attention_fwd")
 
@@ -63,7 +76,34 @@ def doc_start_from_cu(cu_doc_lens: torch.Tensor, batch: int, seq_len: int) -> to
     return (start - (pos // seq_len) * seq_len).clamp_(min=0).view(batch, seq_len).to(torch.int32).contiguous()
 
 
+def _pad(t: torch.Tensor, T_pad: int) -> torch.Tensor:
+    """``(B, T, H, D)`` -> contiguous ``(B, T_pad, H, 128)`` with zeros in the new rows and columns."""
+    B, T, H, D = t.shape
+    out = t.new_zeros((B, T_pad, H, TILE))
+    out[:, :T, :, :D].copy_(t)
+    return out
+
+
+def _pad_doc_start(doc_start: Optional[torch.Tensor], T_pad: int) -> Optional[torch.Tensor]:
+    if doc_start is None or doc_start.shape[1] == T_pad:
+        return doc_start
+    B, T = doc_start.shape
+    tail = torch.arange(T, T_pad, device=doc_start.device, dtype=torch.int32).expand(B, -1)  # each padded token is its own document
+    return torch.cat([doc_start, tail], dim=1).contiguous()
+
+
 def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = None, doc_start: Optional[torch.Tensor] = None):
+    if _needs_padding(q):
+        B, T, H, D = q.shape
+        T_pad = -(-T // TILE) * TILE
+        o_p, lse_p = forward(_pad(q, T_pad), _pad(k, T_pad), _pad(v, T_pad), causal, scale, doc_start=_pad_doc_start(doc_start, T_pad))
+        o = o_p[:, :T, :, :D]
+        if out is not None:
+            out.copy_(o)
+            o = out
+        else:
+            o = o.contiguous()
+        return o, lse_p[:, :, :T].contiguous()
     B, T, H, D = q.shape
     if doc_start is not None:
         assert causal and doc_start.dtype == torch.int32 and doc_start.shape == (B, T) and doc_start.is_contiguous()
@@ -82,6 +122,18 @@ def forward(q, k, v, causal: bool, scale: float, out: Optional[torch.Tensor] = N
 def backward(do, q, k, v, o, lse, dq, dk, dv, causal: bool, scale: float, doc_start: Optional[torch.Tensor] = None) -> None:
     """Gradients into caller-provided (possibly strided) ``dq``, ``dk``, ``dv``.  Scratch: ``delta`` (B·H·T floats) and
     an fp32 ``dq`` accumulator (B·T·H·128 floats) that key tiles add into with vector reductions."""
+    if _needs_padding(q):
+        B, T, H, D = q.shape
+        T_pad = -(-T // TILE) * TILE
+        qp, kp, vp = _pad(q, T_pad), _pad(k, T_pad), _pad(v, T_pad)
+        lse_p = lse.new_zeros((B, H, T_pad))  # padded query rows have zero dO, so any finite statistic gives zero gradients
+        lse_p[:, :, :T].copy_(lse)
+        dqp, dkp, dvp = torch.empty_like(qp), torch.empty_like(kp), torch.empty_like(vp)
+        backward(_pad(do, T_pad), qp, kp, vp, _pad(o, T_pad), lse_p, dqp, dkp, dvp, causal, scale, doc_start=_pad_doc_start(doc_start, T_pad))
+        dq.copy_(dqp[:, :T, :, :D])
+        dk.copy_(dkp[:, :T, :, :D])
+        dv.copy_(dvp[:, :T, :, :D])
+        return
     B, T, H, D = q.shape
     Hkv = k.shape[2]
     delta = torch.empty((B, H, T), dtype=torch.float32, device=q.device)

@@ -103,10 +103,10 @@ def config_supported(cfg) -> bool:
 
 def eligible(block, x: torch.Tensor, attention_bias, layer_past, use_cache: bool, doc_masking: bool = False) -> bool:
     """True when this call can run on the fused path (training/eval forward without cache or explicit bias).  With
-    intra-document masking the native attention kernel must cover the shape (head dim 128, T a multiple of 128)."""
+    intra-document masking the native attention kernel must cover the shape (head dim up to 128)."""
     if not (x.is_cuda and enabled()) or attention_bias is not None or layer_past is not None or use_cache:
         return False
-    if doc_masking and (block.config.d_model // block.config.n_heads != 128 or x.shape[1] % 128 != 0):
+    if doc_masking and block.config.d_model // block.config.n_heads > 128:
         return False
     if x.dtype != torch.bfloat16 and not (torch.is_autocast_enabled() and torch.get_autocast_dtype("cuda") == torch.bfloat16):
         return False

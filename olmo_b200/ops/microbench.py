@@ -63,6 +63,16 @@ def bench_gemm(args) -> None:
             "dgrad dy·W": lambda: k.gemm(dy, b, b_trans=True),
             "wgrad dyt·x (+= fp32)": lambda: k.gemm(dy, a, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc),
         }
+        # the library GEMM (cuBLAS through torch) on the same operands and layouts, same process, for comparison only;
+        # its weight gradient is a bf16 product (it has no fp32-accumulating epilogue), i.e. it does less work
+        out_fwd = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        out_dg = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+        out_wg = torch.empty(N, K, device="cuda", dtype=torch.bfloat16)
+        library = {
+            "fwd  x·Wt": lambda: torch.matmul(a, b.t(), out=out_fwd),
+            "dgrad dy·W": lambda: torch.matmul(dy, b, out=out_dg),
+            "wgrad dyt·x (+= fp32)": lambda: torch.matmul(dy.t(), a, out=out_wg),
+        }
         for name, fn in cases.items():
             if args.once:
                 for _ in range(3):
@@ -71,7 +81,10 @@ def bench_gemm(args) -> None:
             ms = timeit(fn)
             tf = 2 * M * N * K / ms / 1e9
             frac = f" ({tf / peak:.2f} of measured cuBLAS burst)" if peak else ""
-            print(f"gemm {M}x{N}x{K} {name}: {ms:.3f} ms  {tf:.0f} TFLOP/s{frac}", flush=True)
+            lib_ms = timeit(library[name])
+            print(f"gemm {M}x{N}x{K} {name}: {ms:.3f} ms  {tf:.0f} TFLOP/s{frac}; library GEMM on the same operands "
+                  f"{lib_ms:.3f} ms  {2 * M * N * K / lib_ms / 1e9:.0f} TFLOP/s", flush=True)
+        del out_fwd, out_dg, out_wg
 
 
 def bench_attention(args) -> None:

@@ -257,7 +257,11 @@ class FlatShardEngine:
         return out
 
     def _decide_schedule(self, use_peer: bool) -> str:
-        if not use_peer:
+        if not use_peer or not self.is_sharded:
+            return "resident"
+        if self.num_replicas > 1:
+            if self._schedule_request == "sharded":
+                log.warning("the sharded schedule covers one shard group spanning the job; with model replicas the resident schedule is used")
             return "resident"
         req = self._schedule_request
         if req == "auto":
@@ -301,7 +305,7 @@ class FlatShardEngine:
             self.units.append(unit)
         # 2. schedule; which units are streamed
         use_peer = (
-            self.is_sharded and dev.type == "cuda" and self.fused and self.shard_world == self.world
+            self.world > 1 and dev.type == "cuda" and self.fused
             and os.environ.get("OLMO_B200_FUSED_COMM", "1").strip().lower() not in ("0", "false", "no", "off")
         )
         self.schedule = self._decide_schedule(use_peer)
@@ -324,7 +328,7 @@ class FlatShardEngine:
             if pos == 0:
                 self.schedule = "resident"
         # 3. buffers; module parameters become views of `full` (placeholders on the meta device for streamed units)
-        if self.is_sharded and dev.type == "cuda" and self.fused and os.environ.get("OLMO_B200_FUSED_COMM", "1").strip().lower() not in ("0", "false", "no", "off"):
+        if use_peer:
             from .peer import PeerComm
 
             self.comm = PeerComm.create(self)
@@ -485,11 +489,10 @@ class FlatShardEngine:
             for i, unit in enumerate(self.units):
                 k.sumsq(unit.grad, self._sumsq, accumulate=i > 0)
         self._mark("barrier_wait")
-        if self.is_sharded:
-            if self.comm is not None:
-                self.comm.all_reduce_scalar_(self._sumsq)
-            else:
-                dist.all_reduce(self._sumsq, group=process_group or self.shard_group)
+        if self.comm is not None:  # also the end-of-step barrier of the whole job, so it runs even when nothing is sharded
+            self.comm.all_reduce_scalar_(self._sumsq)
+        elif self.is_sharded:
+            dist.all_reduce(self._sumsq, group=process_group or self.shard_group)
         self._mark("clip")
         k.clip_coef(self._sumsq, float(max_norm) if max_norm is not None else float("inf"), self.clip_coef, self._norm_out)
         return self._norm_out[0].clone()
@@ -540,7 +543,10 @@ class FlatShardEngine:
         for unit in self.units:
             shard = unit.lowp.contiguous()
             ref = torch.empty(unit.numel, dtype=shard.dtype, device=self.device)
-            dist.all_gather_into_tensor(ref, shard, group=self.shard_group)
+            if world > 1:
+                dist.all_gather_into_tensor(ref, shard, group=self.shard_group)
+            else:
+                ref.copy_(shard)
             if unit.streamed:
                 st = self.stream
                 st.content[unit.stream_pos % st.n_full] = None
@@ -552,14 +558,19 @@ class FlatShardEngine:
             checked_ag += unit.numel
             del ref
             if not unit.streamed and getattr(unit, "reduced", False):
-                out = torch.empty(unit.shard_size, dtype=torch.float32, device=self.device)
-                dist.reduce_scatter_tensor(out, unit.gfull.clone(), group=self.shard_group)
-                out.div_(world)
+                if world > 1:
+                    out = torch.empty(unit.shard_size, dtype=torch.float32, device=self.device)
+                    dist.reduce_scatter_tensor(out, unit.gfull.clone(), group=self.shard_group)
+                else:
+                    out = unit.gfull.clone()
+                if self.num_replicas > 1:
+                    dist.all_reduce(out, group=self.replica_group)
+                out.div_(self.world)
                 denom = out.abs().max().clamp_min(1e-30)
                 worst_rs = max(worst_rs, float(((unit.grad - out).abs().max() / denom).item()))
                 checked_rs += unit.shard_size
         t = torch.tensor([worst_rs, float(bad_ag)], device=self.device, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.shard_group)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
         worst_rs, bad_ag = float(t[0]), int(t[1])
         return {
             "ok": bool(worst_rs < 1e-5 and bad_ag == 0), "reduce_scatter_max_rel_err_vs_nccl": worst_rs,
@@ -630,6 +641,7 @@ class FlatShardEngine:
                         self.comm.publish_grads(u)
                 self.comm.reduce_scatter_units(pending, scale=1.0 / world)
                 for u in pending:
+                    self.comm.finish_replicas(u)
                     u.reduced = True  # type: ignore[attr-defined]
             self._grad_epoch_open = False
             for u in self.units:
@@ -779,7 +791,8 @@ class FlatShardEngine:
         gather_queue: List[Unit] = []
         gathered: set = set()
         if comm is not None and self._params_stale:
-            gather_queue = self._forward_unit_order()
+            if self.is_sharded:
+                gather_queue = self._forward_unit_order()
             self._params_stale = False
         elif comm is None:
             self.gather_params()
@@ -854,11 +867,14 @@ class FlatShardEngine:
 
             publish(len(blocks))
 
+        riding: List[Unit] = []
+
         def reduce_kwargs() -> Optional[Dict[str, Dict[str, Any]]]:
             if not ready:
                 return None
             u = ready.pop(0)
             u.reduced = True  # type: ignore[attr-defined]
+            riding.append(u)
             return {name: {"comm": (comm.rs_task(u, span=span), comm.rs_ctas)} for name, span in BWD_SPANS.items()}
 
         for i in range(len(blocks) - 1, -1, -1):
@@ -873,6 +889,8 @@ class FlatShardEngine:
                                        gemm_kwargs=reduce_kwargs() if reduce_now else None)
             del payload
             if reduce_now:
+                while riding:  # the block's GEMMs carried this unit's reduce-scatter: now the replica group's turn
+                    comm.finish_replicas(riding.pop())
                 publish(i)
         k.embedding_bwd(input_ids, dx, self.grad_view(t.wte.weight)[0])
         if reduce_now:
@@ -880,6 +898,7 @@ class FlatShardEngine:
             for u in ready:  # whatever found no GEMM to ride on
                 u.reduced = True  # type: ignore[attr-defined]
                 comm.launch(comm.rs_task(u))
+                comm.finish_replicas(u)
             ready.clear()
         self.note_microbatch_backward()
         if self.keep_recomputable is None and is_last:

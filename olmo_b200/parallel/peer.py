@@ -71,7 +71,7 @@ class CommTask(ctypes.Structure):
     ]
 
 
-COMM_MODE_SELF = 2
+COMM_MODE_SELF, COMM_MODE_STORE = 2, 4
 N_GSLOTS, N_FULL_SLOTS = 3, 2
 
 
@@ -92,8 +92,18 @@ class PeerComm:
         import torch.distributed._symmetric_memory as symm_mem
 
         self.engine = engine
+        # `world` / `rank` are those of the shard group (what gathers and reduce-scatters run over).  The buffers are
+        # exchanged over the whole job, so a rank also knows the pointers of its replica group: the ranks that hold the
+        # same shard in the other model replicas (hybrid sharding; plain data parallelism is a shard group of one).
         self.world, self.rank = engine.shard_world, engine.shard_rank
-        assert self.world <= MAX_WORLD
+        self.gworld = getattr(engine, "world", self.world)
+        self.grank = getattr(engine, "rank", self.rank)
+        self.replicas = self.gworld // self.world
+        assert self.gworld <= MAX_WORLD and self.world * self.replicas == self.gworld
+        first = (self.grank // self.world) * self.world
+        self.shard_peers = list(range(first, first + self.world))            # global ranks of my shard group, by shard rank
+        self.replica_peers = list(range(self.rank, self.gworld, self.world))  # global ranks holding my shard, by replica
+        self.replica_index = self.grank // self.world
         dev = engine.device
         assert ctypes.sizeof(CommTask) == lib().ob_comm_task_size(), "CommTask layout mismatch"
         # resident units: gathered copy and full-size gradient accumulator of every unit, end to end
@@ -127,22 +137,38 @@ class PeerComm:
             self.full_slots = torch.zeros(N_FULL_SLOTS * self.slot_numel, dtype=engine.compute_dtype, device=dev)
             self.lowp_all.zero_()
             self.gslots.zero_()
-            self.lowp_ptrs = [int(p) for p in self.h_lowp.buffer_ptrs]
-            self.gslot_ptrs = [int(p) for p in self.h_gslots.buffer_ptrs]
+            self.lowp_ptrs = [int(self.h_lowp.buffer_ptrs[g]) for g in self.shard_peers]
+            self.gslot_ptrs = [int(self.h_gslots.buffer_ptrs[g]) for g in self.shard_peers]
+        # with model replicas, a reduce-scatter lands in a staging shard that the replica group then sums
+        self.stage_all = None
+        self.stage_bases: List[int] = []
+        self.stage_ptrs: List[int] = []
+        if self.replicas > 1:
+            off = 0
+            for u in engine.units:
+                self.stage_bases.append(off)
+                off += u.shard_size
+            self.stage_all = symm_mem.empty(max(off, 1024), dtype=torch.float32, device=dev)
+            self.h_stage = symm_mem.rendezvous(self.stage_all, group)
+            self.stage_all.zero_()
+            self.stage_ptrs = [int(self.h_stage.buffer_ptrs[g]) for g in self.replica_peers]
         self.n_units = len(engine.units)
         self.slot_words = lib().ob_scalar_slots_bytes() // 4
         self.gslot_word0 = 1 + self.n_units  # ready words of the gradient slots, then their done words
-        self.slot_off = (1 + self.n_units + 2 * N_GSLOTS + 15) // 16 * 16
+        self.stage_word0 = self.gslot_word0 + 2 * N_GSLOTS  # per unit: the staged (shard-group reduced) gradient is complete
+        self.slot_off = (self.stage_word0 + self.n_units + 15) // 16 * 16
         self.ctrl = symm_mem.empty(self.slot_off + self.slot_words, dtype=torch.int32, device=dev)
         self.h_ctrl = symm_mem.rendezvous(self.ctrl, group)
         self.full_all.zero_()
         self.gfull_all.zero_()
         self.ctrl.zero_()
-        self.full_ptrs = [int(p) for p in self.h_full.buffer_ptrs]
-        self.gfull_ptrs = [int(p) for p in self.h_gfull.buffer_ptrs]
-        self.ctrl_ptrs = [int(p) for p in self.h_ctrl.buffer_ptrs]
+        self.full_ptrs = [int(self.h_full.buffer_ptrs[g]) for g in self.shard_peers]
+        self.gfull_ptrs = [int(self.h_gfull.buffer_ptrs[g]) for g in self.shard_peers]
+        self.ctrl_ptrs = [int(self.h_ctrl.buffer_ptrs[g]) for g in self.shard_peers]
+        self.ctrl_ptrs_replica = [int(self.h_ctrl.buffer_ptrs[g]) for g in self.replica_peers]
         self.gslot_use = [0] * N_GSLOTS  # how often each gradient slot has been handed out (same on every rank)
-        self.slot_ptrs_dev = torch.tensor([p + 4 * self.slot_off for p in self.ctrl_ptrs], dtype=torch.int64, device=dev)
+        # the scalar all-reduce (and with it the end-of-step barrier) spans the whole job
+        self.slot_ptrs_dev = torch.tensor([int(p) + 4 * self.slot_off for p in self.h_ctrl.buffer_ptrs], dtype=torch.int64, device=dev)
         self.param_epoch = 0
         self.grad_epoch = 0
         self.scalar_epoch = 0
@@ -165,8 +191,11 @@ class PeerComm:
 
     @classmethod
     def create(cls, engine) -> Optional["PeerComm"]:
-        if engine.shard_world != engine.world:
-            log.info("peer-memory collectives cover one shard group spanning the whole job; hybrid sharding uses NCCL")
+        """Peer memory needs every rank of the job on one NVLink domain: at most eight ranks, all on this node."""
+        from ..torch_util import get_local_world_size
+
+        if engine.world > MAX_WORLD or get_local_world_size() != engine.world:
+            log.info("the job spans more than one node (or more than %d ranks): collectives go through NCCL", MAX_WORLD)
             return None
         return cls(engine, dist.group.WORLD)
 
@@ -236,12 +265,41 @@ class PeerComm:
         for p in range(self.world):
             t.src[p] = self.gfull_ptrs[p] + (base + self.rank * S + a) * 4
             t.wait_flags[p] = self.ctrl_ptrs[p] + 4 * (1 + unit.index)
+        t.scale = 1.0 / self.engine.world
+        t.wait_value = self.grad_epoch
+        if self.replicas > 1:  # lands in the staging shard (plain store); the replica group sums it into `grad` afterwards
+            t.dst = self.stage_all.data_ptr() + (self.stage_bases[unit.index] + a) * 4
+            t.mode |= COMM_MODE_STORE
+            return t
         t.dst = unit.grad.data_ptr() + a * 4
         if self.fuse_sumsq:
             t.sumsq_partials = self.rs_partials.data_ptr()
-        t.scale = 1.0 / self.engine.world
+        return t
+
+    def replica_task(self, unit) -> CommTask:
+        """Sum of the staged shard of ``unit`` over the replica group (every replica reads all of them, in replica order,
+        so all end up with bit-identical gradients), added to the fp32 gradient shard, with its Σg²."""
+        t = CommTask()
+        t.kind, t.world, t.rank = COMM_REDUCE_SCATTER, self.replicas, self.replica_index
+        t.status = status_tensor(self.engine.device).data_ptr()
+        t.wait_cycles = self.wait_cycles
+        t.mode = 0
+        t.elems = unit.shard_size
+        for k in range(self.replicas):
+            t.src[k] = self.stage_ptrs[k] + self.stage_bases[unit.index] * 4
+            t.wait_flags[k] = self.ctrl_ptrs_replica[k] + 4 * (self.stage_word0 + unit.index)
+        t.dst = unit.grad.data_ptr()
+        t.sumsq_partials = self.rs_partials.data_ptr() if self.fuse_sumsq else None
+        t.scale = 1.0
         t.wait_value = self.grad_epoch
         return t
+
+    def finish_replicas(self, unit) -> None:
+        """Call once the reduce-scatter of ``unit`` has been enqueued on this stream: publish the staged shard and add
+        the replica group's sum to the gradient shard."""
+        if self.replicas > 1:
+            self.signal(self.stage_word0 + unit.index, self.grad_epoch)
+            self.launch(self.replica_task(unit))
 
     def stream_ag_task(self, unit, slot: int, span=None) -> CommTask:
         """Gather of one slice of every rank's shard of a streamed ``unit`` (this rank's own included) into local
@@ -329,13 +387,16 @@ class PeerComm:
             self.launch(self.rs_task(u))
 
     def all_reduce_scalar_(self, value: torch.Tensor) -> torch.Tensor:
-        """In-place sum of a one-element fp32 tensor over all ranks; also an execution barrier on the stream."""
+        """In-place sum of a one-element fp32 tensor over the shard group (computed as the sum over the whole job divided
+        by the number of replicas, which all hold the same values); also an execution barrier of the whole job on the stream."""
         self.scalar_epoch += 1
         rc = lib().ob_allreduce_scalar(
             ptr(value), ptr(self.slot_ptrs_dev), ctypes.c_void_p(self.ctrl_ptrs[self.rank] + 4 * self.slot_off), ptr(self._scalar_out),
-            ctypes.c_int(self.rank), ctypes.c_int(self.world), ctypes.c_int(self.scalar_epoch),
+            ctypes.c_int(self.grank), ctypes.c_int(self.gworld), ctypes.c_int(self.scalar_epoch),
             ptr(status_tensor(self.engine.device)), ctypes.c_longlong(self.wait_cycles), stream_ptr(),
         )
         check(rc, "ob_allreduce_scalar")
         value.copy_(self._scalar_out)
+        if self.replicas > 1:  # every replica contributed the same per-shard values
+            value.div_(self.replicas)
         return value

@@ -547,7 +547,7 @@ class Trainer:
             return False
         if batch.get("doc_lens") is not None:  # document masking needs the native attention kernel's shape coverage
             mc = self.cfg.model
-            if mc.d_model // mc.n_heads != 128 or batch["input_ids"].shape[1] % 128 != 0:
+            if mc.d_model // mc.n_heads > 128:
                 return False
         steps = self.cfg.module_outputs_save_steps
         return not (steps is not None and self.global_step in steps)
@@ -575,7 +575,7 @@ class Trainer:
             # a fused engine keeps no autograd graph (its module parameters do not require gradients)
             raise OLMoConfigurationError(
                 "this batch cannot run on the fused kernel path (attention mask with padding, attention bias, document "
-                "lengths outside head dimension 128 / sequence length multiple of 128, or a module-output trace step) and "
+                "lengths with a head dimension above 128, or a module-output trace step) and "
                 "the engine was built for it; build the engine with force_portable=True (set OLMO_B200_KERNELS=0) for such data"
             )
         del batch

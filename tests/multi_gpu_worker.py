@@ -22,6 +22,7 @@ def main() -> None:
     ap.add_argument("--schedule", default="resident", choices=["resident", "sharded", "auto"])
     ap.add_argument("--comm-ctas", type=int, default=0, help="0: communication warps in every GEMM CTA; n > 0: n CTAs set aside")
     ap.add_argument("--layers", type=int, default=3)
+    ap.add_argument("--replicas", type=int, default=None)
     ap.add_argument("--activation-checkpointing", default=None)
     args = ap.parse_args()
     os.environ["OLMO_B200_FUSED_COMM"] = str(args.fused_comm)
@@ -57,15 +58,19 @@ def main() -> None:
         model=model, optimizer=OptimizerConfig(name=OptimizerType.adamw, learning_rate=1e-3, eps=1e-8, weight_decay=0.1),
         scheduler=SchedulerConfig(name=SchedulerType.constant), precision="amp_bf16",
         distributed_strategy=DistributedStrategy.fsdp,
-        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy[args.strategy], wrapping_strategy=FSDPWrapStrategy.by_block_and_size, precision=FSDPPrecision.mixed),
+        fsdp=FSDPConfig(sharding_strategy=ShardingStrategy[args.strategy], wrapping_strategy=FSDPWrapStrategy.by_block_and_size, precision=FSDPPrecision.mixed,
+                        hybrid_sharding_num_model_replicas=args.replicas),
         global_train_batch_size=args.global_batch, device_train_microbatch_size=2, max_grad_norm=1.0, save_folder=tempfile.mkdtemp(),
     )
     derive_batch_sizes(cfg, world)
     dist_model = build_model_and_engine(cfg, device)
     engine = dist_model.engine
     assert engine.fused
-    if world > 1 and args.fused_comm and args.strategy == "FULL_SHARD":
+    if world > 1 and args.fused_comm:
         assert engine.comm is not None, "peer-memory collectives should be active"
+        if args.replicas:
+            assert engine.num_replicas == args.replicas and engine.comm.replicas == args.replicas
+    if world > 1 and args.fused_comm and args.strategy == "FULL_SHARD":
         assert engine.schedule == args.schedule, (engine.schedule, args.schedule)
         if args.schedule == "sharded":
             assert sum(u.streamed for u in engine.units) == args.layers and engine.comm.full_slots is not None

@@ -280,6 +280,117 @@ def test_native_attention_backward(causal, H, Hkv, T):
     _close(dq, rdq, rtol=3e-2, atol=3e-2)
 
 
+def _autograd_attention(q, k, v, do, causal, scale, doc_start=None):
+    """fp32 attention written with differentiable torch ops; gradients come from autograd, not from hand-derived formulas."""
+    B, T, H, D = q.shape
+    Hkv = k.shape[2]
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    ke = kf.repeat_interleave(H // Hkv, dim=2) if Hkv != H else kf
+    ve = vf.repeat_interleave(H // Hkv, dim=2) if Hkv != H else vf
+    s_ = torch.einsum("bthd,bshd->bhts", qf, ke) * scale
+    allowed = torch.ones(T, T, dtype=torch.bool, device=q.device)
+    if causal:
+        allowed = torch.tril(allowed)
+    allowed = allowed.view(1, 1, T, T)
+    if doc_start is not None:
+        keys = torch.arange(T, device=q.device).view(1, 1, 1, T)
+        allowed = allowed & (keys >= doc_start.view(B, 1, T, 1).long())
+    s_ = s_.masked_fill(~allowed, float("-inf"))
+    out = torch.einsum("bhts,bshd->bthd", torch.softmax(s_, dim=-1), ve)
+    out.backward(do.float())
+    return out.detach(), qf.grad, kf.grad, vf.grad
+
+
+@pytest.mark.parametrize("causal,H,Hkv,T,D", [
+    (True, 4, 4, 512, 128), (False, 4, 2, 256, 128),   # the kernels' own tile shape
+    (True, 4, 4, 200, 64), (True, 2, 1, 384, 96), (False, 2, 2, 256, 32), (True, 3, 3, 77, 128),  # reached by zero padding
+])
+def test_native_attention_against_fp32_autograd(causal, H, Hkv, T, D):
+    from olmo_b200.ops import attention_native as N
+
+    B = 2
+    fused = _rand(B * T, (H + 2 * Hkv) * D)
+    q = fused[:, : H * D].view(B, T, H, D)
+    k = fused[:, H * D : (H + Hkv) * D].view(B, T, Hkv, D)
+    v = fused[:, (H + Hkv) * D :].view(B, T, Hkv, D)
+    assert N.supports_backward(q, k, causal)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = N.forward(q, k, v, causal, scale)
+    assert o.shape == (B, T, H, D) and lse.shape == (B, H, T)
+    do = _rand(B, T, H, D)
+    dfused = torch.zeros_like(fused)
+    dq = dfused[:, : H * D].view(B, T, H, D)
+    dk = dfused[:, H * D : (H + Hkv) * D].view(B, T, Hkv, D)
+    dv = dfused[:, (H + Hkv) * D :].view(B, T, Hkv, D)
+    N.backward(do, q, k, v, o, lse, dq, dk, dv, causal, scale)
+    ro, rdq, rdk, rdv = _autograd_attention(q, k, v, do, causal, scale)
+    _close(o, ro, rtol=2e-2, atol=2e-2)
+    _close(dv, rdv, rtol=3e-2, atol=3e-2)
+    _close(dk, rdk, rtol=3e-2, atol=3e-2)
+    _close(dq, rdq, rtol=3e-2, atol=3e-2)
+
+
+def test_native_attention_document_masking_with_padding_against_autograd():
+    from olmo_b200.ops import attention_native as N
+
+    B, T, H, D = 2, 300, 2, 64
+    q, k, v, do = _rand(B, T, H, D), _rand(B, T, H, D), _rand(B, T, H, D), _rand(B, T, H, D)
+    doc_lens = torch.tensor([[100, 150, 50], [300, 0, 0]], device="cuda")
+    doc_start = N.doc_start_from_lengths(doc_lens, T)
+    scale = 1.0 / math.sqrt(D)
+    o, lse = N.forward(q, k, v, True, scale, doc_start=doc_start)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    N.backward(do, q, k, v, o, lse, dq, dk, dv, True, scale, doc_start=doc_start)
+    ro, rdq, rdk, rdv = _autograd_attention(q, k, v, do, True, scale, doc_start=doc_start)
+    _close(o, ro, rtol=2e-2, atol=2e-2)
+    for got, want in ((dq, rdq), (dk, rdk), (dv, rdv)):
+        _close(got, want, rtol=3e-2, atol=3e-2)
+
+
+def _gemm_close(got, want, K):
+    """Inputs are bf16 and accumulation is fp32, so the error of an output element is that of its final rounding (bf16
+    outputs: 2^-8 relative) plus accumulation-order noise that grows like sqrt(K) times fp32 epsilon."""
+    got, want = got.float(), want.float()
+    ref = want.abs().max().item()
+    out_eps = 2.0 ** -8
+    tol = (out_eps + 4.0 * math.sqrt(K) * 2.0 ** -23) * max(ref, 1e-6)
+    err = (got - want).abs().max().item()
+    assert err <= tol, f"max err {err} > {tol} (ref max {ref}, K={K})"
+
+
+@pytest.mark.parametrize("tma_store", [1, 0])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 296, 72), (1000, 520, 4096), (8192, 4096, 11008), (257, 264, 128)])
+def test_gemm_pair_epilogues_with_and_without_tma_stores(tma_store, M, N, K):
+    """All four epilogues of the two-CTA kernel, output tiles leaving through shared memory + TMA (store or reduce-add) or
+    through per-thread stores, ragged M and N included; tolerance scaled with sqrt(K)."""
+    import ctypes
+
+    from olmo_b200 import ops
+    from olmo_b200.ops import kernels as k
+
+    lib = ops.lib()
+    lib.ob_set_gemm_pair_mode(ctypes.c_int(1))
+    lib.ob_set_gemm_tma_store(ctypes.c_int(tma_store))
+    try:
+        a, b = _rand(M, K), _rand(N, K)
+        ref = a.float() @ b.float().t()
+        _gemm_close(k.gemm(a, b), ref, K)
+        res = _rand(M, N)
+        _gemm_close(k.gemm(a, b, epilogue=k.EPI_BF16_ADD, residual=res), ref + res.float(), K)
+        dy = _rand(M, N)
+        wref = dy.float().t() @ a.float()  # [N, K]: contraction over M
+        acc = torch.full((N, K), 1.0, device="cuda")
+        k.gemm(dy, a, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc)
+        k.gemm(dy, a, a_trans=True, b_trans=True, epilogue=k.EPI_F32_ACCUM, out=acc)
+        got, want = acc, 2 * wref + 1.0
+        assert (got - want).abs().max().item() <= 8.0 * math.sqrt(M) * 2.0 ** -23 * want.abs().max().item() + 1e-5
+        st = torch.full((N, K), 7.0, device="cuda")
+        k.gemm(dy, a, a_trans=True, b_trans=True, epilogue=k.EPI_F32_STORE, out=st)
+        assert (st - wref).abs().max().item() <= 8.0 * math.sqrt(M) * 2.0 ** -23 * wref.abs().max().item() + 1e-5
+    finally:
+        lib.ob_set_gemm_tma_store(ctypes.c_int(1))
+
+
 @pytest.fixture
 def pair_mode():
     """Route GEMMs through the two-CTA (cta_group::2) kernel for the duration of a test."""

@@ -82,8 +82,21 @@ def test_fused_collectives_are_reproducible(tmp_path, schedule):
         assert torch.equal(t, b["state"][name]), name
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_replicated_data_parallel_on_peer_memory_matches_one(tmp_path):
+    """NO_SHARD (what ``ddp`` maps to): a shard group of one, gradients summed over the replica group by the peer-memory
+    kernel (the worker asserts that the peer-memory runtime is active)."""
+    single = _run(1, tmp_path / "one.pt")
+    multi = _run(2, tmp_path / "ddp.pt", "--strategy", "NO_SHARD")
+    _compare(multi, single, "2 replicas vs 1")
+
+
 @pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs four GPUs")
 def test_hybrid_shard_matches_one(tmp_path):
+    """HYBRID_SHARD, two replicas of two shards: reduce-scatter inside the shard group into a staging shard, then the
+    replica group's sum, both through peer memory (the worker asserts ``engine.comm is not None``)."""
     single = _run(1, tmp_path / "one.pt")
-    multi = _run(4, tmp_path / "hybrid.pt", "--strategy", "HYBRID_SHARD")
+    multi = _run(4, tmp_path / "hybrid.pt", "--strategy", "HYBRID_SHARD", "--replicas", "2")
     _compare(multi, single, "4 ranks hybrid vs 1")
+    again = _run(4, tmp_path / "hybrid2.pt", "--strategy", "HYBRID_SHARD", "--replicas", "2")
+    assert again["norms"] == multi["norms"] and all(torch.equal(t, multi["state"][n]) for n, t in again["state"].items())
