@@ -29,7 +29,7 @@ namespace {
 constexpr int AT_THREADS = 320;
 constexpr int AT_TILE_BYTES = 128 * 128 * 2;  // 32 KiB: one 128 x 128 bf16 tile = two 64-column halves
 constexpr int AT_HALF_BYTES = 128 * 64 * 2;   // 16 KiB
-constexpr int AT_SMEM_BWD = 1024 + 6 * AT_TILE_BYTES + 512;  // alignment slack + tiles + barriers
+constexpr int AT_SMEM_BWD = 1024 + 7 * AT_TILE_BYTES + 512;  // alignment slack + tiles (Q is double buffered) + barriers
 constexpr int AT_SMEM = 1024 + 6 * AT_TILE_BYTES + 4096;  // alignment slack + tiles + barriers and row-statistic exchange (3.3 KiB)
 
 struct AttnParams {
@@ -416,20 +416,26 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
   uint8_t* sdO = sQ + AT_TILE_BYTES;
   uint8_t* sP = sdO + AT_TILE_BYTES;
   uint8_t* sdS = sP + AT_TILE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sdS + AT_TILE_BYTES);
-  uint64_t* kv_full = bars;       // K and V landed
-  uint64_t* qdo_full = bars + 1;  // Q and dO of this iteration landed
-  uint64_t* qdo_empty = bars + 2; // tensor core finished reading Q, dO, P, dS of this iteration
-  uint64_t* sdp_full = bars + 3;  // S and dP complete
-  uint64_t* pds_full = bars + 4;  // P and dS written (256 arrivals)
-  uint64_t* dq_full = bars + 5;   // dQ complete (and dV, dK updated)
-  uint64_t* s_free = bars + 6;    // dQ read out of TMEM (256 arrivals)
+  uint8_t* sQ1 = sdS + AT_TILE_BYTES;  // second Q buffer: iteration it uses buffer it & 1
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQ1 + AT_TILE_BYTES);
+  // Pipeline of one key tile against its query tiles.  Q is double buffered and fetched one iteration ahead; dO is
+  // refetched as soon as the dV product of the previous iteration has read it.  dQ is accumulated in the TMEM columns of
+  // dP (free once P and dS are written), so S of the next iteration can be issued while the softmax warps still read dQ.
+  uint64_t* kv_full = bars;        // K and V landed
+  uint64_t* q_full = bars + 1;     // [2] Q of an iteration landed
+  uint64_t* q_empty = bars + 3;    // [2] tensor core finished reading that Q buffer (S and dK)
+  uint64_t* do_full = bars + 5;    // dO landed
+  uint64_t* do_empty = bars + 6;   // tensor core finished reading dO (dP and dV)
+  uint64_t* sdp_full = bars + 7;   // S and dP complete
+  uint64_t* pds_full = bars + 8;   // P and dS written (256 arrivals)
+  uint64_t* dq_full = bars + 9;    // dQ complete (and dV, dK updated)
+  uint64_t* dq_read = bars + 10;   // dQ read out of TMEM (256 arrivals)
   // The dQ tile leaves through the P / dS buffers, which are idle between the last MMA of an iteration and the softmax
   // of the next one: column half h stages its columns [0,32) in its 16 KiB half of sP and [32,64) in its half of sdS,
   // i.e. exactly the bytes that the same 128 threads overwrite with P and dS later, so only they need to synchronise.
-  uint64_t* stage_full = bars + 7;  // [2] a half's 128 threads have staged their dQ rows
-  uint64_t* stage_free = bars + 9;  // [2] the reduce-add stores have finished reading that half's staging bytes
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  uint64_t* stage_full = bars + 11;  // [2] a half's 128 threads have staged their dQ rows
+  uint64_t* stage_free = bars + 13;  // [2] the reduce-add stores have finished reading that half's staging bytes
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -451,13 +457,15 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
-    mbar_init(qdo_empty, 1);
+    mbar_init(do_full, 1);
+    mbar_init(do_empty, 1);
     mbar_init(sdp_full, 1);
     mbar_init(pds_full, 256);
     mbar_init(dq_full, 1);
-    mbar_init(s_free, 256);
+    mbar_init(dq_read, 256);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
       mbar_init(&stage_full[i], 128);
       mbar_init(&stage_free[i], 1);
     }
@@ -488,12 +496,16 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       for (int it = 0; it < n_it; ++it) {
         const int h = hk * group + it / per_head;
         const int qrow = b * p.T + (i0 + it % per_head) * 128;
-        if (!mbar_wait(qdo_empty, static_cast<uint32_t>((it & 1) ^ 1), abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
-        mbar_expect_tx(qdo_full, 2 * AT_TILE_BYTES);
-        tma_load_2d(sQ, &tm_q, qdo_full, h * 128, qrow);
-        tma_load_2d(sQ + AT_HALF_BYTES, &tm_q, qdo_full, h * 128 + 64, qrow);
-        tma_load_2d(sdO, &tm_do, qdo_full, h * 128, qrow);
-        tma_load_2d(sdO + AT_HALF_BYTES, &tm_do, qdo_full, h * 128 + 64, qrow);
+        const int qb = it & 1;
+        uint8_t* q_dst = qb ? sQ1 : sQ;
+        if (!mbar_wait(&q_empty[qb], static_cast<uint32_t>(((it >> 1) & 1) ^ 1), abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
+        mbar_expect_tx(&q_full[qb], AT_TILE_BYTES);
+        tma_load_2d(q_dst, &tm_q, &q_full[qb], h * 128, qrow);
+        tma_load_2d(q_dst + AT_HALF_BYTES, &tm_q, &q_full[qb], h * 128 + 64, qrow);
+        if (!mbar_wait(do_empty, static_cast<uint32_t>((it & 1) ^ 1), abort_flag, p.status, ST_TIMEOUT_PRODUCER)) break;
+        mbar_expect_tx(do_full, AT_TILE_BYTES);
+        tma_load_2d(sdO, &tm_do, do_full, h * 128, qrow);
+        tma_load_2d(sdO + AT_HALF_BYTES, &tm_do, do_full, h * 128 + 64, qrow);
       }
       if (*abort_flag) {
         const long long t0 = clock64();
@@ -506,25 +518,40 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       constexpr uint32_t idesc_kk = make_idesc_bf16(128, 128, 0, 0);  // A K-major, B K-major
       constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);  // A K-major, B MN-major
       constexpr uint32_t idesc_mm = make_idesc_bf16(128, 128, 1, 1);  // both MN-major
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ), aO = smem_u32(sdO), aP = smem_u32(sP), aS = smem_u32(sdS);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aO = smem_u32(sdO), aP = smem_u32(sP), aS = smem_u32(sdS);
+      const uint32_t aQb[2] = {smem_u32(sQ), smem_u32(sQ1)};
       const uint32_t tS = tmem_base, tdP = tmem_base + 128u, tdV = tmem_base + 256u, tdK = tmem_base + 384u;
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
-      for (int it = 0; it < n_it && ok; ++it) {
-        const uint32_t ph = static_cast<uint32_t>(it & 1);
-        if (!mbar_wait(qdo_full, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
-        if (!mbar_wait(s_free, ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
-        tc_fence_after();
+      auto issue_s = [&](uint32_t aQ) {  // S = Q Kt
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // S = Q Kt
+        for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * AT_HALF_BYTES + (k & 3) * 32;
           umma_f16_ss(tS, make_smem_desc_sw128(aQ + off, 16, 1024), make_smem_desc_sw128(aK + off, 16, 1024), idesc_kk, k > 0 ? 1u : 0u);
         }
+      };
+      auto issue_dp = [&]() {  // dP = dO Vt
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // dP = dO Vt
+        for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * AT_HALF_BYTES + (k & 3) * 32;
           umma_f16_ss(tdP, make_smem_desc_sw128(aO + off, 16, 1024), make_smem_desc_sw128(aV + off, 16, 1024), idesc_kk, k > 0 ? 1u : 0u);
         }
-        umma_commit(sdp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
+      if (ok && n_it > 0) {
+        ok = mbar_wait(&q_full[0], 0, abort_flag, p.status, ST_TIMEOUT_MMA);
+        if (ok) {
+          tc_fence_after();
+          issue_s(aQb[0]);
+          ok = mbar_wait(do_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
+        }
+        if (ok) {
+          tc_fence_after();
+          issue_dp();
+          umma_commit(sdp_full);
+        }
+      }
+      for (int it = 0; it < n_it && ok; ++it) {
+        const uint32_t ph = static_cast<uint32_t>(it & 1);
+        const uint32_t aQ = aQb[it & 1];
         if (!mbar_wait(pds_full, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
         tc_fence_after();
 #pragma unroll
@@ -532,18 +559,30 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           umma_f16_ss(tdV, make_smem_desc_sw128(aP + k * 2048, AT_HALF_BYTES, 1024), make_smem_desc_sw128(aO + k * 2048, AT_HALF_BYTES, 1024),
                       idesc_mm, (it > 0 || k > 0) ? 1u : 0u);
         }
+        umma_commit(do_empty);  // dO of the next iteration may land while dK and dQ are computed
 #pragma unroll
         for (int k = 0; k < 8; ++k) {  // dK += dSt Q
           umma_f16_ss(tdK, make_smem_desc_sw128(aS + k * 2048, AT_HALF_BYTES, 1024), make_smem_desc_sw128(aQ + k * 2048, AT_HALF_BYTES, 1024),
                       idesc_mm, (it > 0 || k > 0) ? 1u : 0u);
         }
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {  // dQ = dS K    (contraction over the 128 key rows)
-          umma_f16_ss(tS, make_smem_desc_sw128(aS + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024),
+        for (int k = 0; k < 8; ++k) {  // dQ = dS K    (contraction over the 128 key rows), into the columns dP has vacated
+          umma_f16_ss(tdP, make_smem_desc_sw128(aS + (k >> 2) * AT_HALF_BYTES + (k & 3) * 32, 16, 1024),
                       make_smem_desc_sw128(aK + k * 2048, AT_HALF_BYTES, 1024), idesc_km, k > 0 ? 1u : 0u);
         }
         umma_commit(dq_full);
-        umma_commit(qdo_empty);
+        umma_commit(&q_empty[it & 1]);
+        if (it + 1 < n_it) {
+          const int nb = (it + 1) & 1;
+          if (!mbar_wait(&q_full[nb], static_cast<uint32_t>(((it + 1) >> 1) & 1), abort_flag, p.status, ST_TIMEOUT_MMA)) break;
+          tc_fence_after();
+          issue_s(aQb[nb]);  // the softmax warps consumed S of this iteration before they published P and dS
+          if (!mbar_wait(do_full, ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
+          if (!mbar_wait(dq_read, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;  // dQ has left the dP columns
+          tc_fence_after();
+          issue_dp();
+          umma_commit(sdp_full);
+        }
       }
     }
   } else {
@@ -632,11 +671,11 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       tc_fence_after();
       __syncwarp();
       uint32_t r0[32], r1[32];
-      tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0), r0);
-      tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + 32), r1);
+      tmem_ld_32x32b_x32(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0), r0);
+      tmem_ld_32x32b_x32(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0 + 32), r1);
       tmem_ld_wait();
       tc_fence_before();
-      mbar_arrive(s_free);  // the accumulator columns may be overwritten by the next S
+      mbar_arrive(dq_read);  // the columns may be overwritten by the next dP
       uint8_t* stage0 = sP + half * AT_HALF_BYTES;   // fp32 [128 rows][32 columns], 128-byte swizzle: columns col0 .. col0+31
       uint8_t* stage1 = sdS + half * AT_HALF_BYTES;  // columns col0+32 .. col0+63
 #pragma unroll
