@@ -106,6 +106,11 @@ int ob_decode_attention(const void* q, const void* k_cache, const void* v_cache,
 int ob_w4a16_gemm_small(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, float* partial, int M, int N,
                         int K, int group, int splits, int* status, cudaStream_t stream);
 int ob_gather_columns_bf16(const void* x, const int* perm, void* out, int M, int K, cudaStream_t stream);
+// 2-, 3-, 4- and 8-bit weights as a little-endian bit stream per row (wna16.cu): qweight [N, K*bits/32] int32.
+int ob_wna16_gemv(const void* x, const void* qweight, const void* scales, const void* zeros, void* y, int M, int N, int K, int group,
+                  int bits, cudaStream_t stream);  // 1 <= M <= 8
+int ob_wna16_dequant(const void* qweight, const void* scales, const void* zeros, void* out, int N, int K, int group, int bits,
+                     cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -404,7 +404,9 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-__global__ void __launch_bounds__(AT_THREADS, 1)
+// 320 threads at 200 registers fit the register file (64,000 of 65,536); the bound derived from the block size alone would
+// be 168 and makes the softmax warps spill inside their loop
+__global__ void __maxnreg__(200)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdParams p) {
@@ -519,7 +521,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       constexpr uint32_t idesc_km = make_idesc_bf16(128, 128, 0, 1);  // A K-major, B MN-major
       constexpr uint32_t idesc_mm = make_idesc_bf16(128, 128, 1, 1);  // both MN-major
       const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aO = smem_u32(sdO), aP = smem_u32(sP), aS = smem_u32(sdS);
-      const uint32_t aQb[2] = {smem_u32(sQ), smem_u32(sQ1)};
+      const uint32_t aQ0 = smem_u32(sQ), aQ1 = smem_u32(sQ1);
       const uint32_t tS = tmem_base, tdP = tmem_base + 128u, tdV = tmem_base + 256u, tdK = tmem_base + 384u;
       auto issue_s = [&](uint32_t aQ) {  // S = Q Kt
 #pragma unroll
@@ -540,7 +542,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         ok = mbar_wait(&q_full[0], 0, abort_flag, p.status, ST_TIMEOUT_MMA);
         if (ok) {
           tc_fence_after();
-          issue_s(aQb[0]);
+          issue_s(aQ0);
           ok = mbar_wait(do_full, 0, abort_flag, p.status, ST_TIMEOUT_MMA);
         }
         if (ok) {
@@ -551,7 +553,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       }
       for (int it = 0; it < n_it && ok; ++it) {
         const uint32_t ph = static_cast<uint32_t>(it & 1);
-        const uint32_t aQ = aQb[it & 1];
+        const uint32_t aQ = (it & 1) ? aQ1 : aQ0;
         if (!mbar_wait(pds_full, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
         tc_fence_after();
 #pragma unroll
@@ -576,7 +578,7 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
           const int nb = (it + 1) & 1;
           if (!mbar_wait(&q_full[nb], static_cast<uint32_t>(((it + 1) >> 1) & 1), abort_flag, p.status, ST_TIMEOUT_MMA)) break;
           tc_fence_after();
-          issue_s(aQb[nb]);  // the softmax warps consumed S of this iteration before they published P and dS
+          issue_s(nb ? aQ1 : aQ0);  // the softmax warps consumed S of this iteration before they published P and dS
           if (!mbar_wait(do_full, ph ^ 1u, abort_flag, p.status, ST_TIMEOUT_MMA)) break;
           if (!mbar_wait(dq_read, ph, abort_flag, p.status, ST_TIMEOUT_MMA)) break;  // dQ has left the dP columns
           tc_fence_after();
@@ -622,29 +624,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       if (!mbar_wait(sdp_full, ph, abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       tc_fence_after();
       __syncwarp();
-      uint32_t pk[32], dsk[32];
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t rs[32], rp[32];
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 32), rs);
-        tmem_ld_32x32b_x32(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0 + cc * 32), rp);
-        tmem_ld_wait();
-#pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = col0 + cc * 32 + 2 * c + e;
-            float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
-            if (p.causal && qi == jt && col > row) pr = 0.f;
-            if (col < first_col) pr = 0.f;
-            pv[e] = pr;
-            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl);
-          }
-          pk[cc * 16 + c] = pack_bf16x2(pv[0], pv[1]);
-          dsk[cc * 16 + c] = pack_bf16x2(dv[0], dv[1]);
-        }
-      }
       // the reduce-add stores of the previous iteration must have read their staging bytes before P / dS overwrite them
       if (it > 0) {
         if (quarter == 0 && lane == 0) {
@@ -653,14 +632,38 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         }
         if (!mbar_wait(&stage_free[half], static_cast<uint32_t>((it - 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       }
-      // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle
+      // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle; 16 columns at a time (two 16-byte
+      // chunks of each tile) so that few registers are live at once
       uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
       uint8_t* srow = sdS + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        const int o = (ch ^ (row & 7)) << 4;
-        *reinterpret_cast<uint4*>(prow + o) = make_uint4(pk[ch * 4 + 0], pk[ch * 4 + 1], pk[ch * 4 + 2], pk[ch * 4 + 3]);
-        *reinterpret_cast<uint4*>(srow + o) = make_uint4(dsk[ch * 4 + 0], dsk[ch * 4 + 1], dsk[ch * 4 + 2], dsk[ch * 4 + 3]);
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t rs[16], rp[16];
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 16), rs);
+        tmem_ld_32x32b_x16(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0 + cc * 16), rp);
+        tmem_ld_wait();
+        uint32_t pk[8], dsk[8];
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = col0 + cc * 16 + 2 * c + e;
+            float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
+            if (p.causal && qi == jt && col > row) pr = 0.f;
+            if (col < first_col) pr = 0.f;
+            pv[e] = pr;
+            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl);
+          }
+          pk[c] = pack_bf16x2(pv[0], pv[1]);
+          dsk[c] = pack_bf16x2(dv[0], dv[1]);
+        }
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int o = ((cc * 2 + hh) ^ (row & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + o) = make_uint4(pk[hh * 4 + 0], pk[hh * 4 + 1], pk[hh * 4 + 2], pk[hh * 4 + 3]);
+          *reinterpret_cast<uint4*>(srow + o) = make_uint4(dsk[hh * 4 + 0], dsk[hh * 4 + 1], dsk[hh * 4 + 2], dsk[hh * 4 + 3]);
+        }
       }
       tc_fence_before();
       fence_proxy_async();

@@ -8,7 +8,7 @@ import torch.nn.functional as F
 pytestmark = pytest.mark.gpu
 
 
-def _cfg(precision: str, flavour: str = "olmo2", n_kv_heads=None):
+def _cfg(precision: str, flavour: str = "olmo2", n_kv_heads=None, n_heads: int = 2, seq: int = 256):
     from olmo_b200.config import (
         DistributedStrategy, LayerNormType, ModelConfig, OptimizerConfig, OptimizerType, SchedulerConfig, SchedulerType, TrainConfig,
     )
@@ -16,11 +16,11 @@ def _cfg(precision: str, flavour: str = "olmo2", n_kv_heads=None):
 
     olmo2 = flavour == "olmo2"
     model = ModelConfig(
-        d_model=256, n_heads=2, n_kv_heads=n_kv_heads, n_layers=2, mlp_hidden_size=1024, weight_tying=False, rope=True,
+        d_model=256, n_heads=n_heads, n_kv_heads=n_kv_heads, n_layers=2, mlp_hidden_size=1024, weight_tying=False, rope=True,
         rope_theta=500000 if olmo2 else 10000, flash_attention=True, attention_dropout=0.0, residual_dropout=0.0,
         embedding_dropout=0.0, include_bias=False, layer_norm_type=LayerNormType.rms if olmo2 else LayerNormType.default,
         layer_norm_with_affine=olmo2, layer_norm_eps=1e-6 if olmo2 else 1e-5, bias_for_layer_norm=False,
-        attention_layer_norm=olmo2, norm_after=olmo2, clip_qkv=None if olmo2 else 2.0, max_sequence_length=256,
+        attention_layer_norm=olmo2, norm_after=olmo2, clip_qkv=None if olmo2 else 2.0, max_sequence_length=seq,
         vocab_size=500, embedding_size=512, eos_token_id=499, pad_token_id=499, init_device="meta", init_std=0.05,
     )
     cfg = TrainConfig(
@@ -108,7 +108,11 @@ def test_train_steps_reduce_loss():
     entry.smoke()
 
 
-def test_fused_document_masking_matches_portable():
+@pytest.mark.parametrize("n_heads,T,doc_lens,max_doc_lens", [
+    (2, 256, [[60, 130, 66, 0], [128, 100, 20, 8]], [130, 128]),   # head dim 128, whole tiles
+    (4, 200, [[60, 100, 40, 0], [128, 50, 14, 8]], [100, 128]),    # head dim 64 and a ragged length: reached by zero padding
+])
+def test_fused_document_masking_matches_portable(n_heads, T, doc_lens, max_doc_lens):
     """Intra-document masking on the fused engine path (native attention kernels with per-token document starts)
     against the portable fp32 autograd path driven by ``doc_lens``."""
     from olmo_b200 import ops
@@ -116,26 +120,27 @@ def test_fused_document_masking_matches_portable():
     from olmo_b200.ops.attention_native import doc_start_from_lengths
 
     device = torch.device("cuda")
-    fused = build_model_and_engine(_cfg("amp_bf16", "olmo2"), device).engine
-    oracle = build_model_and_engine(_cfg("fp32", "olmo2"), device, force_portable=True).engine
+    fused = build_model_and_engine(_cfg("amp_bf16", "olmo2", n_heads=n_heads, seq=T), device).engine
+    oracle = build_model_and_engine(_cfg("fp32", "olmo2", n_heads=n_heads, seq=T), device, force_portable=True).engine
+    assert fused.fused
     state = {s.name: u.full[s.offset : s.offset + s.numel].view(s.shape).float() for u in fused.units for s in u.slots}
     oracle.load_full_model_state_dict(state)
     fused.load_full_model_state_dict(state)
 
     torch.manual_seed(2)
-    ids = torch.randint(0, 500, (2, 256), device=device)
+    ids = torch.randint(0, 500, (2, T), device=device)
     labels = F.pad(ids[:, 1:], (0, 1), value=-100)
-    doc_lens = torch.tensor([[60, 130, 66, 0], [128, 100, 20, 8]], device=device)
+    doc_lens = torch.tensor(doc_lens, device=device)
     divisor = float(ids.numel())
 
     fused.zero_grad()
-    ce, _ = fused.train_microbatch(ids, labels, divisor, z_mult=0.0, doc_start=doc_start_from_lengths(doc_lens, 256))
+    ce, _ = fused.train_microbatch(ids, labels, divisor, z_mult=0.0, doc_start=doc_start_from_lengths(doc_lens, T))
     ops.check_status()
     fused.zero_grad()
     ce_plain, _ = fused.train_microbatch(ids, labels, divisor, z_mult=0.0)
 
     oracle.zero_grad()
-    logits = oracle.model(ids, doc_lens=doc_lens, max_doc_lens=[130, 128]).logits.float().view(-1, 512)
+    logits = oracle.model(ids, doc_lens=doc_lens, max_doc_lens=max_doc_lens).logits.float().view(-1, 512)
     ce_ref = F.cross_entropy(logits, labels.view(-1), ignore_index=-100, reduction="sum") / divisor
     ce_ref.backward()
     oracle.note_microbatch_backward()
@@ -145,7 +150,7 @@ def test_fused_document_masking_matches_portable():
     assert abs(ce_plain.item() - ce.item()) > 1e-4  # the mask changes the loss
 
     fused.zero_grad()
-    fused.train_microbatch(ids, labels, divisor, z_mult=0.0, doc_start=doc_start_from_lengths(doc_lens, 256))
+    fused.train_microbatch(ids, labels, divisor, z_mult=0.0, doc_start=doc_start_from_lengths(doc_lens, T))
     for uf, uo in zip(fused.units, oracle.units):
         for s in uf.slots:
             so = uo.slot(s.name)

@@ -213,3 +213,43 @@ def test_fused_dequant_tensor_core_gemm_matches_cpu_reference(M, N, K, G):
     torch.testing.assert_close(y[:M].float().cpu(), via_matrix, rtol=1e-2, atol=2e-2)
     # the module takes the same kernel for this batch size (with its own choice of K splits, hence not bit-identical)
     torch.testing.assert_close(dev(xd).float().cpu(), y[:M].float().cpu(), rtol=1e-2, atol=6e-2)
+
+
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+def test_bit_stream_packing_round_trips_and_cpu_layer_matches_dense(bits):
+    from olmo_b200.inference.wna16 import BitsLinear, pack_bits, quantize_groups_bits, unpack_bits
+
+    torch.manual_seed(bits)
+    q = torch.randint(0, 2**bits, (5, 96))
+    packed = pack_bits(q, bits)
+    assert packed.shape == (5, 96 * bits // 32) and packed.dtype == torch.int32
+    assert torch.equal(unpack_bits(packed, bits).long(), q)
+    lin = torch.nn.Linear(128, 24, bias=True)
+    layer = BitsLinear.from_linear_rtn(lin, bits, group=32)
+    qq, scales, zeros = quantize_groups_bits(lin.weight.detach(), 32, bits)
+    dense = ((qq.float().reshape(24, 4, 32) - zeros.unsqueeze(-1)) * scales.to(torch.bfloat16).float().unsqueeze(-1)).reshape(24, 128)
+    torch.testing.assert_close(layer.dequantize(), dense, rtol=0, atol=1e-6)
+    x = torch.randn(3, 128)
+    torch.testing.assert_close(layer(x), x @ dense.t() + lin.bias, rtol=1e-4, atol=1e-4)
+    if bits == 8:  # fine grids reproduce the dense layer closely
+        assert (layer(x) - lin(x)).abs().max() < 0.05
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("bits", [2, 3, 4, 8])
+@pytest.mark.parametrize("rows", [1, 5, 8, 19, 100])
+def test_bit_width_kernels_match_the_fp32_reference(bits, rows):
+    """GEMV and reconstruct kernels for every width against the same layer evaluated with plain fp32 tensor ops."""
+    from olmo_b200.inference.wna16 import BitsLinear
+
+    torch.manual_seed(0)
+    lin = torch.nn.Linear(512, 384, bias=False)
+    cpu_layer = BitsLinear.from_linear_rtn(lin, bits, group=128)
+    gpu_layer = BitsLinear.from_linear_rtn(lin, bits, group=128).cuda()
+    ref_w = cpu_layer.dequantize()
+    got_w = gpu_layer.dequantize().float().cpu()
+    assert (got_w - ref_w).abs().max() <= 2.0 ** -8 * ref_w.abs().max() + 1e-6  # bf16 rounding of the reconstructed weights
+    x = torch.randn(rows, 512).to(torch.bfloat16)
+    ref = x.float() @ ref_w.t()
+    got = gpu_layer(x.cuda()).float().cpu()
+    assert (got - ref).abs().max() <= 2e-2 * ref.abs().max() + 1e-3
