@@ -26,6 +26,11 @@ int ob_gemm_bf16_comm(const void* A, const void* B, void* C, const void* R, int 
                       int a_mn_major, int b_mn_major, int epi, int* status, int num_sms, const void* task, int comm_ctas,
                       cudaStream_t stream);
 
+// ---- gemm_smallm.cu: y[M, N] = x[M, K] · w[N, K]ᵀ for 1 <= M <= 256 (weights streamed as the 128-row operand)
+int ob_gemm_smallm_splits(int N, int K, int num_sms);
+int ob_gemm_smallm(const void* x, const void* w, void* y, float* partial, int M, int N, int K, int ldx, int ldw, int splits,
+                   int* status, cudaStream_t stream);
+
 // ---- attention.cu
 int ob_attention_fwd(const void* q, const void* k, const void* v, void* o, float* lse, int B, int T, int H, int Hkv, int q_sb,
                      int q_st, int q_sh, int k_sb, int k_st, int k_sh, int v_sb, int v_st, int v_sh, int o_sb, int o_st,

@@ -250,14 +250,34 @@ void launch_norm_bwd(int grid, int threads, cudaStream_t stream, const bf16* dy,
 }
 
 
-// out[d] (+)= sum_p part[p, d]
-__global__ void reduce_rows_f32_kernel(const float* __restrict__ part, int nparts, int D, float* __restrict__ out,
-                                       int accumulate) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= D) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[static_cast<size_t>(p) * D + d];
-  out[d] = accumulate ? out[d] + s : s;
+// out[d] (+)= sum_p part[p, d].  A block owns 32 columns; its 256 threads are 8 row lanes x 32 columns, every row lane
+// sums each eighth row with four independent accumulators (a warp reads 128 contiguous bytes per row), and the eight
+// lane sums are added in lane order, so the result does not depend on scheduling.
+constexpr int RR_COLS = 32, RR_LANES = 8;
+__global__ void __launch_bounds__(RR_COLS * RR_LANES)
+reduce_rows_f32_kernel(const float* __restrict__ part, int nparts, int D, float* __restrict__ out, int accumulate) {
+  __shared__ float lane_sum[RR_LANES][RR_COLS];
+  const int c = threadIdx.x & (RR_COLS - 1), rl = threadIdx.x >> 5;
+  const int d = blockIdx.x * RR_COLS + c;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  if (d < D) {
+    int p = rl;
+    for (; p + 3 * RR_LANES < nparts; p += 4 * RR_LANES) {
+      a0 += part[static_cast<size_t>(p) * D + d];
+      a1 += part[static_cast<size_t>(p + RR_LANES) * D + d];
+      a2 += part[static_cast<size_t>(p + 2 * RR_LANES) * D + d];
+      a3 += part[static_cast<size_t>(p + 3 * RR_LANES) * D + d];
+    }
+    for (; p < nparts; p += RR_LANES) a0 += part[static_cast<size_t>(p) * D + d];
+  }
+  lane_sum[rl][c] = (a0 + a1) + (a2 + a3);
+  __syncthreads();
+  if (rl == 0 && d < D) {
+    float s = 0.f;
+#pragma unroll
+    for (int l = 0; l < RR_LANES; ++l) s += lane_sum[l][c];
+    out[d] = accumulate ? out[d] + s : s;
+  }
 }
 
 }  // namespace
@@ -310,6 +330,6 @@ extern "C" int ob_reduce_rows_f32(const float* part, int nparts, int D, float* o
                                   cudaStream_t stream) {
   using namespace ob;
   if (D <= 0 || nparts <= 0) return 0;
-  reduce_rows_f32_kernel<<<(D + 255) / 256, 256, 0, stream>>>(part, nparts, D, out, accumulate);
+  reduce_rows_f32_kernel<<<(D + RR_COLS - 1) / RR_COLS, RR_COLS * RR_LANES, 0, stream>>>(part, nparts, D, out, accumulate);
   return cudaGetLastError() == cudaSuccess ? 0 : -11;
 }

@@ -14,6 +14,7 @@ import hashlib
 import os
 import shutil
 import subprocess
+import tempfile
 from pathlib import Path
 from typing import List, Optional
 
@@ -63,8 +64,10 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if not Path(nvcc).exists():
         raise OLMoEnvironmentError("nvcc not found; cannot build the sm_100a kernels")
     objs = []
-    build_dir = _ROOT / "build"
-    build_dir.mkdir(exist_ok=True)
+    # a directory of its own per building process: several ranks that find a stale library at the same time must not
+    # write each other's object files (the final rename of the library is atomic)
+    (_ROOT / "build").mkdir(exist_ok=True)
+    build_dir = Path(tempfile.mkdtemp(prefix=f"p{os.getpid()}_", dir=_ROOT / "build"))
     procs = []
     for src in _sources():
         obj = build_dir / (src.stem + ".o")
@@ -79,7 +82,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
             raise OLMoEnvironmentError(f"nvcc failed on {src.name}:\n{out}")
         if verbose and out:
             print(out)
-    tmp = _SO_PATH.with_suffix(".so.tmp")
+    tmp = _SO_PATH.with_suffix(f".so.tmp{os.getpid()}")
     link = subprocess.run(
         [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *map(str, objs), "-o", str(tmp)],
         stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True,
@@ -88,6 +91,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         raise OLMoEnvironmentError(f"link failed:\n{link.stdout}")
     os.replace(tmp, _SO_PATH)
     _STAMP_PATH.write_text(_source_digest())
+    shutil.rmtree(build_dir, ignore_errors=True)
     _lib = None
     return _SO_PATH
 

@@ -102,6 +102,33 @@ def gemm(
     return out
 
 
+def gemm_small_m_available() -> bool:
+    try:
+        return hasattr(lib(), "ob_gemm_smallm")
+    except Exception:
+        return False
+
+
+def gemm_small_m(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """``x[M, K] · w[N, K]ᵀ`` for a decode-sized batch (``1 <= M <= 256``): the weights are streamed once as the
+    128-row tensor-core operand and the batch is the narrow one (``csrc/gemm_smallm.cu``).  Returns ``[M, N]`` bf16."""
+    _bf16(x, "x")
+    _bf16(w, "w")
+    assert x.dim() == 2 and w.dim() == 2 and x.stride(1) == 1 and w.stride(1) == 1 and x.shape[1] == w.shape[1]
+    M, K = x.shape
+    N = w.shape[0]
+    assert 1 <= M <= 256
+    splits = lib().ob_gemm_smallm_splits(c_int(N), c_int(K), c_int(num_sms()))
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    partial = torch.empty(splits * M * N, dtype=torch.float32, device=x.device) if splits > 1 else None
+    rc = lib().ob_gemm_smallm(
+        ptr(x), ptr(w), ptr(y), ptr(partial), c_int(M), c_int(N), c_int(K), c_int(x.stride(0)), c_int(w.stride(0)), c_int(splits),
+        ptr(status_tensor(x.device)), stream_ptr(),
+    )
+    check(rc, "ob_gemm_smallm", kernels=2 if splits > 1 else 1)
+    return y
+
+
 # ---------------------------------------------------------------------------------------- norms
 
 

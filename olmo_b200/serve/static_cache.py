@@ -16,6 +16,7 @@ a longer prompt, or to reclaim the left part of the window) needs no arithmetic 
 """
 from __future__ import annotations
 
+import os
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import torch
@@ -169,24 +170,37 @@ class StaticWindow:
         def w(norm):
             return None if norm is None else norm.weight
 
+        own_gemm = self.rows <= 256 and k.gemm_small_m_available() and os.environ.get("OLMO_B200_DECODE_GEMM", "native") != "library"
+
+        def proj(linear, h):
+            # dense bf16 layers: this library's weight-streaming GEMM for a handful of rows; quantised layers bring their own
+            if own_gemm and type(linear) is torch.nn.Linear and linear.weight.dtype == torch.bfloat16 and h.dtype == torch.bfloat16:
+                y = k.gemm_small_m(h.contiguous(), linear.weight)
+                return y if linear.bias is None else y + linear.bias
+            return linear(h)
+
         x = t.wte(self.tokens).view(self.rows, cfg.d_model)
         for layer, block in enumerate(t.blocks):
             h = x if spec.norm_after else k.norm_fwd(x, w(block.attn_norm), None, spec.eps, spec.rms, save_stats=False)[0]
-            qkv = block.att_proj(h)
+            qkv = proj(block.att_proj, h)
             q = k.decode_qkv(qkv, w(block.q_norm), w(block.k_norm), cos, sin, self.rope_pos, self.pos, self.k[layer], self.v[layer],
                              spec.Wq, spec.Wk, spec.head_dim, spec.eps, spec.clip_qkv, spec.qk_norm, spec.rope)
             o = k.decode_attention(q, self.k[layer], self.v[layer], bias, length, scale, spec.n_heads)
-            a = block.attn_out(o)
+            a = proj(block.attn_out, o)
             if spec.norm_after:
                 x1 = k.norm_fwd(a, w(block.attn_norm), None, spec.eps, spec.rms, residual=x, save_stats=False)[0]
-                f = block.ff_out(k.swiglu_fwd(block.ff_proj(x1)))
+                f = proj(block.ff_out, k.swiglu_fwd(proj(block.ff_proj, x1)))
                 x = k.norm_fwd(f, w(block.ff_norm), None, spec.eps, spec.rms, residual=x1, save_stats=False)[0]
             else:
                 x1 = x + a
                 h2 = k.norm_fwd(x1, w(block.ff_norm), None, spec.eps, spec.rms, save_stats=False)[0]
-                x = x1 + block.ff_out(k.swiglu_fwd(block.ff_proj(h2)))
+                x = x1 + proj(block.ff_out, k.swiglu_fwd(proj(block.ff_proj, h2)))
         x = k.norm_fwd(x, w(t.ln_f), None, spec.eps, spec.rms, save_stats=False)[0]
-        self.logits.copy_(self.model.output_projection(x))
+        head = getattr(t, "ff_out", None)
+        if head is not None and not cfg.scale_logits:
+            self.logits.copy_(proj(head, x))
+        else:
+            self.logits.copy_(self.model.output_projection(x))
 
     def _forward(self, length: int) -> None:
         if self.fused:

@@ -391,6 +391,26 @@ def test_gemm_pair_epilogues_with_and_without_tma_stores(tma_store, M, N, K):
         lib.ob_set_gemm_tma_store(ctypes.c_int(1))
 
 
+@pytest.mark.parametrize("M", [1, 5, 16, 33, 64, 200])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (1000, 512), (384, 11008), (12288, 4096)])
+def test_gemm_small_m_streams_weights(M, N, K):
+    """Decode-sized products (weights as the 128-row operand, batch as the narrow one, K split over CTAs for layers with
+    few feature tiles) against fp32; rows beyond the batch and features beyond N must not be written."""
+    from olmo_b200 import ops
+    from olmo_b200.ops import kernels as k
+
+    assert k.gemm_small_m_available()
+    x, w = _rand(M, K), _rand(N, K)
+    y = k.gemm_small_m(x, w)
+    ops.check_status()
+    assert y.shape == (M, N)
+    _gemm_close(y, x.float() @ w.float().t(), K)
+    again = k.gemm_small_m(x, w)
+    assert torch.equal(y, again)  # split sums are added in split order: bit-identical from run to run
+    xs = _rand(M, K + 64)[:, :K]  # a strided activation view
+    _gemm_close(k.gemm_small_m(xs, w), xs.float() @ w.float().t(), K)
+
+
 @pytest.fixture
 def pair_mode():
     """Route GEMMs through the two-CTA (cta_group::2) kernel for the duration of a test."""

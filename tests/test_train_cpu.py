@@ -242,6 +242,26 @@ def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
     assert abs(again - expect) < 1e-5
 
 
+def test_fused_or_portable_is_decided_when_the_engine_is_built(tmp_path):
+    """Runs whose batches the fused kernel sequence cannot take (padding masks, module-output traces, document masking
+    with heads wider than 128) get the portable path from the start; the rest keep the fused one."""
+    from olmo_b200.launch import needs_portable_path
+
+    cfg = tiny_train_config(tmp_path)
+    assert needs_portable_path(cfg) is None
+    cfg.data.generate_doc_lengths = True
+    assert needs_portable_path(cfg) is None  # head dimension <= 128: covered by the native attention kernels
+    cfg.model.d_model, cfg.model.n_heads = 512, 2
+    assert "128" in needs_portable_path(cfg)
+    cfg.model.n_heads = 8
+    cfg.data.generate_doc_lengths = False
+    cfg.data.generate_attention_mask = True
+    assert "mask" in needs_portable_path(cfg)
+    cfg.data.generate_attention_mask = False
+    cfg.module_outputs_save_steps = [3]
+    assert "hooks" in needs_portable_path(cfg)
+
+
 def test_kept_activation_decision_follows_free_memory(monkeypatch):
     """``OLMO_B200_KEEP_ACTS=auto``: the extra activations are kept only when they fit in the memory still free after the
     first step with a margin (the decision itself needs no GPU: the memory query is replaced)."""
