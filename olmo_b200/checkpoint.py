@@ -456,7 +456,12 @@ class FlatShardCheckpointer(Checkpointer):
         if foreign is not None:
             return self._restore_foreign(load_path, foreign, dist_model, optim, load_optimizer_state=load_optimizer_state)
         meta = self._read_meta(load_path, local_cache)
-        same_layout = meta["shard_world"] == engine.shard_world and [u["numel"] for u in meta["units"]] == [u.numel for u in engine.units]
+        # raw shards may only be copied when the whole layout agrees: unit order and sizes, and every parameter's name,
+        # shape and offset inside its unit (equal sizes alone would let a changed wrapping put shards into the wrong slots)
+        mine = self._layout(engine)
+        same_layout = meta["shard_world"] == mine["shard_world"] and [
+            (u["name"], u["numel"], [(p["name"], list(p["shape"]), p["offset"]) for p in u["params"]]) for u in meta["units"]
+        ] == [(u["name"], u["numel"], [(p["name"], list(p["shape"]), p["offset"]) for p in u["params"]]) for u in mine["units"]]
         if same_layout:
             shard = load_state_dict(load_path, f"model/rank{engine.shard_rank}.pt", local_cache=local_cache, map_location="cpu")
             for u in engine.units:

@@ -5,11 +5,11 @@
 // are the 128-row A operand (a CTA owns 128 output features), the *activations* are the B operand (UMMA N = the batch,
 // padded to 16/32/64/128/256; rows beyond M are zero-filled by the copy engine), and the accumulator in TMEM is yᵀ
 // (lane = output feature, column = batch row).  Layers with few 128-feature tiles split K over several CTAs so that
-// two to three CTAs per SM stream weights at once; every split writes its own fp32 slab and a second kernel adds the
+// two CTAs per SM stream weights at once in a single wave; every split writes its own fp32 slab and a second kernel adds the
 // slabs in split order (no atomics: the result does not depend on scheduling) and rounds to bf16.
 //
 // Roles per CTA (192 threads): warp 0 TMA producer (weight tile 128 x 64 and activation tile MB x 64 per stage, an
-// eight-stage ring), warp 1 MMA issuer (owns TMEM), warps 2..5 epilogue.  Every wait is bounded and reports through the
+// four-stage ring), warp 1 MMA issuer (owns TMEM), warps 2..5 epilogue.  Every wait is bounded and reports through the
 // status word; an aborting CTA still frees its TMEM.
 #include "common.cuh"
 #include "api.h"
@@ -30,13 +30,13 @@ template <int MB>
 struct SmCfg {
   static constexpr int B_BYTES = MB * SM_BK * 2;
   static constexpr int STAGE_BYTES = SM_A_BYTES + B_BYTES;
-  static constexpr int STAGES = (MB <= 64) ? 8 : (MB == 128 ? 6 : 4);
+  static constexpr int STAGES = 4;  // two CTAs share an SM for MB <= 64: one streams while the other starts up or drains
   static constexpr int SMEM_BYTES = 1024 + STAGES * STAGE_BYTES + 256;
   static constexpr int TMEM_COLS = MB < 32 ? 32 : MB;
 };
 
 template <int MB>
-__global__ void __launch_bounds__(SM_THREADS, 1)
+__global__ void __launch_bounds__(SM_THREADS, 2)
 gemm_smallm_kernel(const __grid_constant__ CUtensorMap tma_w, const __grid_constant__ CUtensorMap tma_x, bf16* __restrict__ y,
                    float* __restrict__ partial, int M, int N, int K, int kb_per_split, int* __restrict__ status) {
   using Cfg = SmCfg<MB>;
@@ -207,8 +207,8 @@ extern "C" int ob_gemm_smallm_splits(int N, int K, int num_sms) {
   if (num_sms <= 0) num_sms = 148;
   const int tiles = (N + ob::SM_ROWS - 1) / ob::SM_ROWS;
   const int k_blocks = (K + ob::SM_BK - 1) / ob::SM_BK;
-  int splits = (2 * num_sms + tiles - 1) / tiles;  // aim at two CTAs' worth of weight stream per SM
-  if (splits > k_blocks / 8) splits = k_blocks / 8;  // at least eight K blocks (a full ring) per CTA
+  int splits = (2 * num_sms) / tiles;  // two CTAs per SM, all resident at once: one wave, no tail
+  if (splits > k_blocks / 8) splits = k_blocks / 8;  // at least eight K blocks (two rings) per CTA
   return splits < 1 ? 1 : splits;
 }
 

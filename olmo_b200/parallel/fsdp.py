@@ -504,13 +504,14 @@ class FlatShardEngine:
         self.finish_grad_sync()
         self._ensure_fused_state(optim, kind)
         self._refresh_segments(optim)
-        step = None
-        for name, p in self._opt_params:
-            st = optim.state[p]
-            st["step"] += 1
-            if step is None:
-                step = int(st["step"].item())
-        step = step or 1
+        # one step count for the whole model: per-parameter counters can lag on ranks whose shard of a parameter is empty
+        # (the per-parameter optimizer skips those), and every rank must apply the same bias correction
+        step = 1 + max((int(optim.state[p]["step"].item()) for _, p in self._opt_params), default=0)
+        for _, p in self._opt_params:
+            optim.state[p]["step"].fill_(float(step))
+        groups = optim.param_groups
+        if any(g["betas"] != groups[0]["betas"] or g.get("eps", 0.0) != groups[0].get("eps", 0.0) for g in groups[1:]):
+            raise OLMoConfigurationError("the fused optimizer kernels take one (betas, eps) for all parameter groups")
         for unit in self.units:
             lowp = unit.lowp if unit.lowp.dtype == torch.bfloat16 else None
             g0 = optim.param_groups[0]

@@ -170,11 +170,18 @@ class StaticWindow:
         def w(norm):
             return None if norm is None else norm.weight
 
-        own_gemm = self.rows <= 256 and k.gemm_small_m_available() and os.environ.get("OLMO_B200_DECODE_GEMM", "native") != "library"
+        # Dense bf16 projections of a handful of rows are a stream of the weight matrix.  This library's weight-streaming
+        # GEMM (csrc/gemm_smallm.cu) was measured against the library GEMM at 32 rows on one B200: 5.5 vs 5.2 TB/s on the
+        # vocabulary projection (100352 x 4096), but 1.6-3.5 vs 2.0-3.8 TB/s on the block projections, whose 20-50 us
+        # are dominated by start-up and by the second launch that adds the K splits.  OLMO_B200_DECODE_GEMM=auto (default)
+        # therefore takes it for projections of at least 32768 features, `native` for all, `library` for none.
+        mode = os.environ.get("OLMO_B200_DECODE_GEMM", "auto").strip().lower()
+        own_gemm = self.rows <= 256 and mode != "library" and k.gemm_small_m_available()
+        min_features = 0 if mode == "native" else 32768
 
         def proj(linear, h):
-            # dense bf16 layers: this library's weight-streaming GEMM for a handful of rows; quantised layers bring their own
-            if own_gemm and type(linear) is torch.nn.Linear and linear.weight.dtype == torch.bfloat16 and h.dtype == torch.bfloat16:
+            if (own_gemm and type(linear) is torch.nn.Linear and linear.out_features >= min_features
+                    and linear.weight.dtype == torch.bfloat16 and h.dtype == torch.bfloat16):
                 y = k.gemm_small_m(h.contiguous(), linear.weight)
                 return y if linear.bias is None else y + linear.bias
             return linear(h)
