@@ -404,9 +404,9 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-// 320 threads at 200 registers fit the register file (64,000 of 65,536); the bound derived from the block size alone would
-// be 168 and makes the softmax warps spill inside their loop
-__global__ void __maxnreg__(200)
+// 320 threads are ten warps, i.e. three on some of the four SM sub-partitions with 16,384 registers each: the bound of
+// 168 registers per thread that the compiler derives from the block size is the real one (the kernel needs 158)
+__global__ void __launch_bounds__(AT_THREADS, 1)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdParams p) {
