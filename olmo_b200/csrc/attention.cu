@@ -404,9 +404,11 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
 }
 
-// 320 threads are ten warps, i.e. three on some of the four SM sub-partitions with 16,384 registers each: the bound of
-// 168 registers per thread that the compiler derives from the block size is the real one (the kernel needs 158)
-__global__ void __launch_bounds__(AT_THREADS, 1)
+// 320 threads are ten warps, i.e. three on some of the four SM sub-partitions with 16,384 registers each, so a launch
+// needs at most 170 registers per thread.  The kernel needs 158.  It is compiled with a looser cap than that on purpose:
+// under the cap derived from the block size (168) the allocator settles on 168 registers plus spills inside the softmax
+// loop, which is measurably slower.  Should a change push the count past 170 the launch fails with an error code.
+__global__ void __maxnreg__(200)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdParams p) {
