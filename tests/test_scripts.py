@@ -198,6 +198,33 @@ def test_storage_cleaner_and_compare(tmp_path, capsys):
     n = cleaner.main(["move", str(root / "good"), str(tmp_path / "moved"), "--keep-latest", "2"])
     assert n == 3 and sorted(p.name for p in (tmp_path / "moved").iterdir()) == ["config.yaml", "step200", "step300"]
 
+    # archives are runs too; one entry can be moved on its own; a move can remove its source
+    import shutil
+
+    arch_root = tmp_path / "archived"
+    arch_root.mkdir()
+    shutil.make_archive(str(arch_root / "good"), "gztar", root_dir=root, base_dir="good")
+    (root / "stale").mkdir()
+    (root / "stale" / "config.yaml").write_text("run_name: y\nwandb:\n  entity: ai2\n  project: olmo\n  name: stale-run\n")
+    shutil.make_archive(str(arch_root / "stale"), "zip", root_dir=root / "stale")
+    (arch_root / "notes").mkdir()
+    (arch_root / "notes" / "readme.txt").write_text("not a run")
+    assert cleaner.archive_entries(str(arch_root / "good.tar.gz"), None) == ["config.yaml", "step100", "step200", "step300"]
+    assert sorted(Path(r).name for r in cleaner.clean(str(arch_root), 0, dry_run=True)) == ["stale.zip"]
+    assert cleaner.clean(str(arch_root), 0, dry_run=True, max_archive_size=1) == []
+    with pytest.raises(SystemExit):
+        cleaner.clean(str(arch_root), 0, dry_run=True, ignore_non_runs=False)
+    cleaner.main(["clean", str(arch_root)])
+    assert sorted(p.name for p in arch_root.iterdir()) == ["good.tar.gz", "notes"]
+    n = cleaner.main(["--temp-dir", str(tmp_path), "move", str(arch_root / "good.tar.gz"), str(tmp_path / "one"), "--entry", "step300"])
+    assert n == 1 and (tmp_path / "one" / "step300" / "model.pt").exists() and (arch_root / "good.tar.gz").exists()
+    n = cleaner.main(["move", str(root / "stale"), str(tmp_path / "by_wandb"), "--append-wandb-path", "--remove-src"])
+    assert (tmp_path / "by_wandb" / "ai2" / "olmo" / "stale-run" / "config.yaml").exists() and not (root / "stale").exists()
+    cleaner.main(["move", str(arch_root / "good.tar.gz"), str(tmp_path / "kept_archive")])
+    assert (tmp_path / "kept_archive" / "good.tar.gz").exists()
+    cleaner.main(["--temp-dir", str(tmp_path), "move", str(arch_root / "good.tar.gz"), str(tmp_path / "unpacked"), "--store-unarchived", "--remove-src"])
+    assert (tmp_path / "unpacked" / "step200" / "model.pt").exists() and not (arch_root / "good.tar.gz").exists()
+
     cmp_state = load_script("compare_model_state")
     a = {"w": torch.ones(3), "only_a": torch.zeros(1), "nest": {"v": torch.ones(2)}}
     b = {"w": torch.ones(3) * 1.5, "nest": {"v": torch.ones(2)}}
