@@ -44,7 +44,7 @@ log = logging.getLogger(__name__)
 
 __all__ = [
     "EvalModel", "load_experiment", "resolve_task_set", "construct_task", "predict_and_calculate_metrics", "run_experiment",
-    "write_rows", "TASK_SET_DIR",
+    "write_rows", "merge_sheet_rows", "append_rows_to_gsheet", "TASK_SET_DIR",
 ]
 
 #: task-set files shipped with the repository (``<repo>/evaluation/task_sets/*.yaml``)
@@ -292,6 +292,8 @@ def run_experiment(spec: Dict[str, Any], loader=EvalModel.load) -> List[Dict[str
         write_rows(rows, spec["output"])
     if spec.get("wandb"):
         _log_to_wandb(rows, spec["wandb"])
+    if spec.get("gsheet"):
+        append_rows_to_gsheet(spec["gsheet"], rows, sheet_title=spec.get("gsheet_title", "Sheet1"))
     return rows
 
 
@@ -311,6 +313,50 @@ def write_rows(rows: List[Dict[str, Any]], output: str) -> Tuple[Path, Path]:
         for row in rows:
             f.write("\t".join("" if row.get(c) is None else str(row[c]) for c in columns) + "\n")
     return out, table
+
+
+def merge_sheet_rows(existing: List[List[Any]], rows: List[Dict[str, Any]]) -> List[List[Any]]:
+    """The table (header row first) that results from appending ``rows`` to a sheet whose current cells are ``existing``.
+    Columns the sheet has keep their position, new columns are added on the right, cells without a value are empty."""
+    header = [str(c) for c in existing[0]] if existing and any(str(c) for c in existing[0]) else []
+    body = [list(r) for r in existing[1:]] if header else []
+    for row in rows:
+        header += [c for c in row if c not in header]
+    body = [r + [""] * (len(header) - len(r)) for r in body]
+    for row in rows:
+        body.append(["" if row.get(c) is None else row[c] for c in header])
+    return [header] + body
+
+
+def append_rows_to_gsheet(gsheet: str, rows: List[Dict[str, Any]], sheet_title: str = "Sheet1", client: Any = None) -> int:
+    """Append result rows to the worksheet ``sheet_title`` of the Google spreadsheet named ``gsheet`` (created when it does not
+    exist yet), stamping each row with the time of writing — the reference's ``write_to_gsheet``
+    (``evaluation/steps/run_catwalk.py:354``).  ``client`` is a ``pygsheets`` client (anything with the same ``open`` /
+    ``worksheets`` / ``add_worksheet`` / ``worksheet_by_title`` / ``get_all_values`` / ``update_values`` methods);
+    by default one is authorised from the service-account file named by ``GDRIVE_SERVICE_ACCOUNT_JSON``.  Returns the number
+    of data rows the worksheet holds afterwards."""
+    import os
+    from datetime import datetime, timezone
+
+    if client is None:
+        try:
+            import pygsheets  # optional dependency: only needed when an experiment names a sheet
+        except ImportError as e:
+            raise RuntimeError("writing to a Google sheet needs the `pygsheets` package; results are still in the output files") from e
+        if "GDRIVE_SERVICE_ACCOUNT_JSON" not in os.environ:
+            raise RuntimeError("set GDRIVE_SERVICE_ACCOUNT_JSON to a service-account key file that may edit the sheet")
+        client = pygsheets.authorize(service_account_json=os.environ["GDRIVE_SERVICE_ACCOUNT_JSON"])
+    stamp = datetime.now(tz=timezone.utc).strftime("%Y-%m-%d %H:%M:%S UTC")
+    stamped = [{"date": stamp, **row} for row in rows]
+    book = client.open(gsheet)
+    if sheet_title not in [w.title for w in book.worksheets()]:
+        width = max((len(r) for r in stamped), default=1)
+        book.add_worksheet(sheet_title, rows=len(stamped) + 1, cols=width)
+    sheet = book.worksheet_by_title(sheet_title)
+    existing = [r for r in sheet.get_all_values() if any(str(c) for c in r)]
+    table = merge_sheet_rows(existing, stamped)
+    sheet.update_values("A1", table)
+    return len(table) - 1
 
 
 def _log_to_wandb(rows: List[Dict[str, Any]], settings: Dict[str, Any]) -> None:

@@ -196,3 +196,48 @@ def test_fixture_experiment_runs_from_the_repository_root(tmp_path, monkeypatch)
     row = json.loads((tmp_path / "rows.jsonl").read_text().splitlines()[0])
     assert row["task"] == "ppl_sample_docs" and row["num_instances"] == 48
     assert 30 < row["metric_ppl_token"] < 200  # an untrained model over a 68-word vocabulary: near-uniform
+
+
+def test_rows_are_appended_to_a_sheet_through_a_fake_client():
+    from olmo_b200.eval.offline import append_rows_to_gsheet, merge_sheet_rows
+
+    class Sheet:
+        def __init__(self, title):
+            self.title, self.cells = title, []
+
+        def get_all_values(self):
+            return [list(r) for r in self.cells] + [["", ""]]  # a real sheet pads with empty rows
+
+        def update_values(self, where, table):
+            assert where == "A1"
+            self.cells = [list(r) for r in table]
+
+    class Book:
+        def __init__(self):
+            self.sheets = [Sheet("Sheet1")]
+
+        def worksheets(self):
+            return self.sheets
+
+        def add_worksheet(self, title, rows, cols):
+            self.sheets.append(Sheet(title))
+
+        def worksheet_by_title(self, title):
+            return next(s for s in self.sheets if s.title == title)
+
+    class Client:
+        def __init__(self):
+            self.books = {}
+
+        def open(self, name):
+            return self.books.setdefault(name, Book())
+
+    client = Client()
+    assert append_rows_to_gsheet("results", [{"task": "piqa", "metric_acc": 0.5}], client=client) == 1
+    assert append_rows_to_gsheet("results", [{"task": "arc", "metric_f1": 0.25, "limit": None}], client=client) == 2
+    cells = client.books["results"].worksheet_by_title("Sheet1").cells
+    assert cells[0] == ["date", "task", "metric_acc", "metric_f1", "limit"]
+    assert cells[1][1:] == ["piqa", 0.5, "", ""] and cells[2][1:] == ["arc", "", 0.25, ""]
+    assert append_rows_to_gsheet("results", [{"task": "x"}], sheet_title="ppl", client=client) == 1
+    assert [s.title for s in client.books["results"].worksheets()] == ["Sheet1", "ppl"]
+    assert merge_sheet_rows([], [{"a": 1}]) == [["a"], [1]]
