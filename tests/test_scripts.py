@@ -2,6 +2,7 @@
 import gzip
 import importlib.util
 import json
+import os
 import subprocess
 import sys
 from pathlib import Path
@@ -344,3 +345,23 @@ def test_ci_data_pipeline_smoke_command(tmp_path):
     assert proc.returncode == 0, proc.stderr[-2000:]
     files = list((tmp_path / "tokens").rglob("*.npy"))
     assert files and sum(np.memmap(f, dtype=np.uint16, mode="r").shape[0] for f in files) == 2765 + 48  # words + one end token per document
+
+
+def test_launch_scripts_parse_and_pick_the_node_layout(tmp_path):
+    launch = SCRIPTS / "launch"
+    for script in sorted(launch.glob("*.sh")) + [SCRIPTS / "test_entrypoint.sh"]:
+        assert subprocess.run(["bash", "-n", str(script)], capture_output=True).returncode == 0, script
+    # the scheduler entry script maps the scheduler's variables and hands over to the single- or multi-node script
+    fake = tmp_path / "launch"
+    fake.mkdir()
+    (fake / "beaker.sh").write_text((launch / "beaker.sh").read_text())
+    for name in ("single_node.sh", "multi_node.sh"):
+        (fake / name).write_text(f'#!/usr/bin/env bash\necho "{name} $NNODES $NODE_RANK $MASTER_ADDR $@"\n')
+    for f in fake.iterdir():
+        f.chmod(0o755)
+    env = {"PATH": os.environ["PATH"], "HOME": str(tmp_path), "AWS_CONFIG": "[default]"}
+    one = subprocess.run(["bash", str(fake / "beaker.sh"), "c.yaml", "--x=1"], capture_output=True, text=True, env=env)
+    assert one.stdout.strip() == "single_node.sh 1 0 127.0.0.1 c.yaml --x=1" and (tmp_path / ".aws" / "config").read_text().strip() == "[default]"
+    env.update(BEAKER_REPLICA_COUNT="4", BEAKER_REPLICA_RANK="2", BEAKER_LEADER_REPLICA_HOSTNAME="node0")
+    many = subprocess.run(["bash", str(fake / "beaker.sh"), "c.yaml"], capture_output=True, text=True, env=env)
+    assert many.stdout.strip() == "multi_node.sh 4 2 node0 c.yaml"
