@@ -14,6 +14,8 @@
 // Layout of operands in global memory: (B, T, heads, 128) with arbitrary row pitch (views into fused QKV buffers are
 // fine); grouped-query attention maps query head h to key/value head h / (H / Hkv).  T must be a multiple of 128.
 // Outputs: O (B, T, H, 128) bf16 and the log-sum-exp (B, H, T) fp32 in natural-log units of the scaled scores.
+#include <type_traits>
+
 #include "common.cuh"
 #include "api.h"
 
@@ -31,6 +33,57 @@ constexpr int AT_TILE_BYTES = 128 * 128 * 2;  // 32 KiB: one 128 x 128 bf16 tile
 constexpr int AT_HALF_BYTES = 128 * 64 * 2;   // 16 KiB
 constexpr int AT_SMEM_BWD = 1024 + 7 * AT_TILE_BYTES + 512;  // alignment slack + tiles (Q is double buffered) + barriers
 constexpr int AT_SMEM = 1024 + 6 * AT_TILE_BYTES + 4096;  // alignment slack + tiles + barriers and row-statistic exchange (3.3 KiB)
+
+// Two fp32 operations per instruction (packed 64-bit register pairs) and a three-input maximum.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// exp2 of two values on the FMA pipe (range reduction + cubic), relative error below 1e-4: enough for values that are
+// rounded to bf16 next.  Takes work off the special-function unit, which is the busiest pipe of the softmax.
+__device__ __forceinline__ void exp2_poly2(uint64_t x2, float& e0, float& e1) {
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const uint64_t xc = f2_pack(x0, x1);
+  const uint64_t magic = f2_pack(12582912.f, 12582912.f), neg_magic = f2_pack(-12582912.f, -12582912.f);
+  const uint64_t t = f2_add(xc, magic);                      // low mantissa bits of t = round(x)
+  const uint64_t r = f2_fma(f2_add(t, neg_magic), f2_pack(-1.f, -1.f), xc);  // x - round(x), in [-0.5, 0.5]
+  uint64_t pl = f2_fma(r, f2_pack(0.055171654f, 0.055171654f), f2_pack(0.24261113f, 0.24261113f));
+  pl = f2_fma(pl, r, f2_pack(0.69326097f, 0.69326097f));
+  pl = f2_fma(pl, r, f2_pack(0.99992806f, 0.99992806f));
+  float p0, p1, t0, t1;
+  f2_unpack(pl, p0, p1);
+  f2_unpack(t, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
 
 struct AttnParams {
   bf16* o;
@@ -235,8 +288,8 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       float pm0 = fmaxf(sc[0], sc[1]), pm1 = fmaxf(sc[2], sc[3]);
 #pragma unroll
       for (int c = 4; c < 64; c += 4) {
-        pm0 = fmaxf(pm0, fmaxf(sc[c], sc[c + 1]));
-        pm1 = fmaxf(pm1, fmaxf(sc[c + 2], sc[c + 3]));
+        pm0 = max3(pm0, sc[c], sc[c + 1]);
+        pm1 = max3(pm1, sc[c + 2], sc[c + 3]);
       }
       float* mx = smax + (j & 1) * 256;
       mx[half * 128 + row] = fmaxf(pm0, pm1);
@@ -248,16 +301,27 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const float m_new = raise ? m_row : m_ref;
       const float alpha = raise ? exp2f((m_ref - m_new) * p.scale_log2) : 1.0f;
       const float neg_m = -m_new * p.scale_log2;
-      float ls0 = 0.f, ls1 = 0.f;
       uint32_t pk[32];
+      const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2), neg_m2 = f2_pack(neg_m, neg_m);
+      uint64_t lsa = f2_pack(0.f, 0.f), lsb = lsa;
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float e0 = exp2f(fmaf(sc[2 * c], p.scale_log2, neg_m));
-        const float e1 = exp2f(fmaf(sc[2 * c + 1], p.scale_log2, neg_m));
-        pk[c] = pack_bf16x2(e0, e1);
-        ls0 += e0;
-        ls1 += e1;
+      for (int c = 0; c < 32; c += 2) {
+        float a0, a1, b0, b1;
+        f2_unpack(f2_fma(f2_pack(sc[2 * c], sc[2 * c + 1]), scale2, neg_m2), a0, a1);
+        f2_unpack(f2_fma(f2_pack(sc[2 * c + 2], sc[2 * c + 3]), scale2, neg_m2), b0, b1);
+        a0 = exp2f(a0); a1 = exp2f(a1);
+        if ((c & 2) == 0) exp2_poly2(f2_pack(b0, b1), b0, b1);  // every fourth pair
+        else { b0 = exp2f(b0); b1 = exp2f(b1); }
+        pk[c] = pack_bf16x2(a0, a1);
+        pk[c + 1] = pack_bf16x2(b0, b1);
+        lsa = f2_add(lsa, f2_pack(a0, a1));
+        lsb = f2_add(lsb, f2_pack(b0, b1));
       }
+      float ls0, ls1, ls2, ls3;
+      f2_unpack(lsa, ls0, ls1);
+      f2_unpack(lsb, ls2, ls3);
+      ls0 += ls2;
+      ls1 += ls3;
       l_run = l_run * alpha + (ls0 + ls1);
       m_ref = m_new;
       if (j > 0) {
@@ -400,15 +464,17 @@ struct AttnBwdParams {
   int* status;
 };
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr)
+               : "memory");
 }
 
 // 320 threads are ten warps, i.e. three on some of the four SM sub-partitions with 16,384 registers each, so a launch
-// needs at most 170 registers per thread.  The kernel needs 158.  It is compiled with a looser cap than that on purpose:
-// under the cap derived from the block size (168) the allocator settles on 168 registers plus spills inside the softmax
-// loop, which is measurably slower.  Should a change push the count past 170 the launch fails with an error code.
-__global__ void __maxnreg__(200)
+// needs at most 170 registers per thread (allocated in steps of 8: 168).  Under that cap the kernel takes 138 registers
+// and spills nothing; should a change push the count past the cap the compiler spills rather than failing the launch.
+__global__ void __maxnreg__(168)
 attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                 const __grid_constant__ CUtensorMap tm_dq, const AttnBwdParams p) {
@@ -614,7 +680,6 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
       const uint32_t ph = static_cast<uint32_t>(it & 1);
       const int h = hk * group + it / per_head;
       const int qi = i0 + it % per_head;
-      const long long t_idx = static_cast<long long>(qi) * 128 + row;
       const float lse2 = lse_next * 1.4426950408889634f;
       const float dl = dl_next;
       const int first_col = ds_next - jt * 128;  // key columns below this index lie before the row's document
@@ -634,39 +699,54 @@ attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant_
         }
         if (!mbar_wait(&stage_free[half], static_cast<uint32_t>((it - 1) & 1), abort_flag, p.status, ST_TIMEOUT_EPILOGUE)) { ok = false; break; }
       }
-      // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle; 16 columns at a time (two 16-byte
-      // chunks of each tile) so that few registers are live at once
+      // P and dS tiles -> shared memory, [query rows][key columns], 128-byte swizzle.  Eight columns (one 16-byte chunk
+      // of each tile) at a time; the TMEM loads of the next eight are in flight while the current ones are processed.
+      // Tiles that need no masking (all but the diagonal tile and those that reach back before a row's document) take
+      // a copy of the loop without the per-element compares.
       uint8_t* prow = sP + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
       uint8_t* srow = sdS + half * AT_HALF_BYTES + (row >> 3) * 1024 + (row & 7) * 128;
+      const bool diag = p.causal && qi == jt;
+      auto pds_tile = [&](auto masked_tag) {
+        constexpr bool MASKED = decltype(masked_tag)::value;
+        const uint32_t ts = tmem_base + lane_addr + static_cast<uint32_t>(col0), tp = ts + 128u;
+        const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+        const uint64_t neg_lse2 = f2_pack(-lse2, -lse2);
+        const uint64_t neg_dl2 = f2_pack(-dl, -dl);
+        uint32_t rs[2][8], rp[2][8];
+        tmem_ld_32x32b_x8(ts, rs[0]);
+        tmem_ld_32x32b_x8(tp, rp[0]);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {
-        uint32_t rs[16], rp[16];
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + static_cast<uint32_t>(col0 + cc * 16), rs);
-        tmem_ld_32x32b_x16(tmem_base + lane_addr + 128u + static_cast<uint32_t>(col0 + cc * 16), rp);
-        tmem_ld_wait();
-        uint32_t pk[8], dsk[8];
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          float pv[2], dv[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = col0 + cc * 16 + 2 * c + e;
-            float pr = exp2f(__uint_as_float(rs[2 * c + e]) * p.scale_log2 - lse2);
-            if (p.causal && qi == jt && col > row) pr = 0.f;
-            if (col < first_col) pr = 0.f;
-            pv[e] = pr;
-            dv[e] = pr * (__uint_as_float(rp[2 * c + e]) - dl);
+        for (int cc = 0; cc < 8; ++cc) {
+          tmem_ld_wait();
+          if (cc + 1 < 8) {
+            tmem_ld_32x32b_x8(ts + static_cast<uint32_t>((cc + 1) * 8), rs[(cc + 1) & 1]);
+            tmem_ld_32x32b_x8(tp + static_cast<uint32_t>((cc + 1) * 8), rp[(cc + 1) & 1]);
           }
-          pk[c] = pack_bf16x2(pv[0], pv[1]);
-          dsk[c] = pack_bf16x2(dv[0], dv[1]);
-        }
+          uint32_t pk[4], dsk[4];
 #pragma unroll
-        for (int hh = 0; hh < 2; ++hh) {
-          const int o = ((cc * 2 + hh) ^ (row & 7)) << 4;
-          *reinterpret_cast<uint4*>(prow + o) = make_uint4(pk[hh * 4 + 0], pk[hh * 4 + 1], pk[hh * 4 + 2], pk[hh * 4 + 3]);
-          *reinterpret_cast<uint4*>(srow + o) = make_uint4(dsk[hh * 4 + 0], dsk[hh * 4 + 1], dsk[hh * 4 + 2], dsk[hh * 4 + 3]);
+          for (int c = 0; c < 4; ++c) {
+            const uint64_t s2 = f2_pack(__uint_as_float(rs[cc & 1][2 * c]), __uint_as_float(rs[cc & 1][2 * c + 1]));
+            const uint64_t dp2 = f2_pack(__uint_as_float(rp[cc & 1][2 * c]), __uint_as_float(rp[cc & 1][2 * c + 1]));
+            float a0, a1;
+            f2_unpack(f2_fma(s2, scale2, neg_lse2), a0, a1);
+            float p0 = exp2f(a0), p1 = exp2f(a1);
+            if (MASKED) {
+              const int col = col0 + cc * 8 + 2 * c;
+              if ((diag && col > row) || col < first_col) p0 = 0.f;
+              if ((diag && col + 1 > row) || col + 1 < first_col) p1 = 0.f;
+            }
+            float d0, d1;
+            f2_unpack(f2_mul(f2_pack(p0, p1), f2_add(dp2, neg_dl2)), d0, d1);
+            pk[c] = pack_bf16x2(p0, p1);
+            dsk[c] = pack_bf16x2(d0, d1);
+          }
+          const int o = (cc ^ (row & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + o) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          *reinterpret_cast<uint4*>(srow + o) = make_uint4(dsk[0], dsk[1], dsk[2], dsk[3]);
         }
-      }
+      };
+      if (diag || __any_sync(0xffffffffu, first_col > col0)) pds_tile(std::true_type{});
+      else pds_tile(std::false_type{});
       tc_fence_before();
       fence_proxy_async();
       mbar_arrive(pds_full);
