@@ -20,27 +20,57 @@ __all__ = ["Predictor", "stdio_predictor_wrapper", "run_quantization", "load_qua
 
 
 class Predictor:
-    """Greedy continuation of text prompts with a KV cache; prompts of one request are batched with left padding."""
+    """Greedy continuation of text prompts with a KV cache; prompts of one request are batched with left padding.
+    ``stop_sequences`` cut a continuation at the first occurrence of any of the strings (the role of the stop-id criterion in
+    the reference's ``generate_completions``, ``inference/eval/utils.py:17-107``)."""
 
-    def __init__(self, model, tokenizer, max_new_tokens: int = 256, device: Optional[torch.device] = None):
+    def __init__(self, model, tokenizer, max_new_tokens: int = 256, device: Optional[torch.device] = None,
+                 stop_sequences: Optional[List[str]] = None):
         self.model, self.tokenizer, self.max_new_tokens = model.eval(), tokenizer, max_new_tokens
         self.device = device or next(model.parameters()).device
+        self.stop_sequences = list(stop_sequences or [])
 
-    @torch.no_grad()
-    def predict(self, inputs: List[str]) -> Iterator[str]:
+    def _left_padded(self, inputs: List[str]):
         encoded = [self.tokenizer.encode(text, add_special_tokens=False) or [self.tokenizer.eos_token_id] for text in inputs]
-        width = max(len(e) for e in encoded)
+        width = min(max(len(e) for e in encoded), self.model.config.max_sequence_length)
         ids = torch.full((len(encoded), width), self.tokenizer.pad_token_id, dtype=torch.long)
         mask = torch.zeros(len(encoded), width)
         for i, e in enumerate(encoded):
+            e = e[-width:]
             ids[i, width - len(e) :] = torch.tensor(e)
             mask[i, width - len(e) :] = 1
+        return ids.to(self.device), mask.to(self.device), width
+
+    @torch.no_grad()
+    def predict(self, inputs: List[str]) -> Iterator[str]:
+        ids, mask, width = self._left_padded(inputs)
         room = self.model.config.max_sequence_length - width
-        out = self.model.generate(ids.to(self.device), attention_mask=mask.to(self.device), max_steps=max(1, min(self.max_new_tokens, room)), beam_size=1)
+        out = self.model.generate(ids, attention_mask=mask, max_steps=max(1, min(self.max_new_tokens, room)), beam_size=1)
         for row in out.token_ids[:, 0].tolist():
             if self.tokenizer.eos_token_id in row:
                 row = row[: row.index(self.tokenizer.eos_token_id)]
-            yield self.tokenizer.decode(row).strip()
+            text = self.tokenizer.decode(row)
+            cuts = [text.index(s) for s in self.stop_sequences if s and s in text]
+            if cuts:
+                text = text[: min(cuts)]
+            yield text.strip()
+
+    @torch.no_grad()
+    def next_token_predictions(self, inputs: List[str], candidate_token_ids: Optional[List[int]] = None, batch_size: int = 8):
+        """For every prompt: the index of the most likely next token among ``candidate_token_ids`` (or in the whole
+        vocabulary) and the probabilities over those candidates (``get_next_word_predictions``,
+        ``inference/eval/utils.py:110-155``)."""
+        picks: List[int] = []
+        probs: List[List[float]] = []
+        for start in range(0, len(inputs), batch_size):
+            ids, mask, _ = self._left_padded(inputs[start : start + batch_size])
+            logits = self.model(ids, attention_mask=mask, last_logits_only=True).logits[:, -1].float()
+            p = torch.softmax(logits, dim=-1)
+            if candidate_token_ids is not None:
+                p = p[:, candidate_token_ids]
+            picks += p.argmax(dim=-1).tolist()
+            probs += p.tolist()
+        return picks, probs
 
 
 def stdio_predictor_wrapper(predictor: Predictor, stdin: TextIO = sys.stdin, stdout: TextIO = sys.stdout) -> int:

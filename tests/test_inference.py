@@ -146,6 +146,17 @@ def test_quantised_checkpoint_round_trip_and_stdio_predictor(tmp_path):
     lines = [json.loads(x) for x in stdout.getvalue().splitlines()]
     assert len(lines) == 2 and len(lines[0]) == 2 and len(lines[1]) == 1 and all(isinstance(s, str) for s in lines[0])
 
+    # stop strings cut a continuation; next-token predictions agree with the logits
+    free = list(Predictor(loaded, predictor.tokenizer, max_new_tokens=4).predict(["t1 t2 t3"]))[0]
+    words = free.split()
+    if len(words) > 1:
+        cut = list(Predictor(loaded, predictor.tokenizer, max_new_tokens=4, stop_sequences=[words[1]]).predict(["t1 t2 t3"]))[0]
+        assert cut == words[0]
+    picks, probs = predictor.next_token_predictions(["t1 t2 t3", "t4"], candidate_token_ids=[5, 6, 7, 8])
+    with torch.no_grad():
+        direct = loaded(torch.tensor([[1, 2, 3]])).logits[0, -1, [5, 6, 7, 8]]
+    assert picks[0] == int(direct.argmax()) and len(probs) == 2 and abs(sum(probs[0]) - 1.0) > 0 and len(probs[0]) == 4
+
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("M", [1, 3, 8, 64])

@@ -8,7 +8,6 @@ import sys
 from pathlib import Path
 
 import numpy as np
-import pytest
 import torch
 
 ROOT = Path(__file__).resolve().parent.parent
