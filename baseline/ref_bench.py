@@ -12,7 +12,6 @@ run touches no remote storage and no evaluators.
 """
 from __future__ import annotations
 
-import json
 import os
 import sys
 import tempfile
