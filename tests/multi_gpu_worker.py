@@ -24,6 +24,8 @@ def main() -> None:
     ap.add_argument("--layers", type=int, default=3)
     ap.add_argument("--replicas", type=int, default=None)
     ap.add_argument("--activation-checkpointing", default=None)
+    ap.add_argument("--resume-at", type=int, default=0, help="after this many steps: save a sharded checkpoint, wipe the live state, restore")
+    ap.add_argument("--ckpt-dir", default=None, help="folder shared by all ranks for --resume-at")
     args = ap.parse_args()
     os.environ["OLMO_B200_FUSED_COMM"] = str(args.fused_comm)
     os.environ["OLMO_B200_SCHEDULE"] = args.schedule
@@ -93,6 +95,23 @@ def main() -> None:
         m = optim.clip_grads_and_collect_metrics(step + 1, collect_param_metrics=False, process_group=engine.process_group)
         norms.append(float(m["total_grad_norm"]))
         optim.step()
+        if args.resume_at and step + 1 == args.resume_at:
+            # a resume inside one process: checkpoint, destroy what the checkpoint has to bring back, restore
+            from olmo_b200.checkpoint import build_sharded_checkpointer
+
+            cfg.save_overwrite = True
+            ckpt = build_sharded_checkpointer(cfg)
+            folder = os.path.join(args.ckpt_dir, "step")
+            ckpt.save_checkpoint(folder, dist_model, optim, {"global_step": step + 1})
+            for u in engine.units:
+                u.master.fill_(7.0)
+            for st in optim.state.values():
+                for v in st.values():
+                    if torch.is_tensor(v):
+                        v.zero_()
+            engine.params_changed()
+            trainer_state = ckpt.restore_checkpoint(folder, dist_model, optim)
+            assert trainer_state["global_step"] == step + 1
     ops.check_status()
     state = engine.full_model_state_dict(rank0_only=True, cpu=True)
     # the fused evaluation pass and the module-level forward (streamed units gathered for its duration) must agree
