@@ -104,26 +104,40 @@ class IterableDataset(torch.utils.data.IterableDataset[Dict[str, Any]]):
         if self.work_dir is not None:
             self._build_and_save_global_indices()
 
-    def __iter__(self) -> Iterator[Dict[str, Any]]:
-        indices = self.get_global_indices()
+    def _my_indices(self) -> np.ndarray:
+        """This rank's (and, inside a data-loader worker, this worker's) slice of the global order, in yield order."""
+        order = self.get_global_indices()
         if self.max_examples is not None:
             assert self.max_examples % self.world_size == 0
-            indices = indices[: self.max_examples]
-        if self.start_index > 0:
-            indices = indices[self.start_index :]
-        indices = indices[self.rank : self.total_size : self.world_size]
-
-        num_threads = self.num_threads
+            order = order[: self.max_examples]
+        mine = order[self.start_index :][self.rank : self.total_size : self.world_size]
         info = torch.utils.data.get_worker_info()
-        if info is not None:
-            bs = self.device_batch_size
-            whole = bs * (len(indices) // bs)
-            tail = indices[whole + info.id :: info.num_workers]
-            mine = indices[:whole].reshape((-1, bs))[info.id :: info.num_workers].reshape((-1,))
-            indices = np.concatenate([mine, tail])
-        elif num_threads is None:
-            num_threads = 4
+        if info is None:
+            return mine
+        # workers take whole device batches in turn (so that the loader emits batches in order); what does not fill a
+        # batch is dealt out instance by instance
+        bs = self.device_batch_size
+        whole = bs * (len(mine) // bs)
+        batches = mine[:whole].reshape((-1, bs))[info.id :: info.num_workers].reshape((-1,))
+        return np.concatenate([batches, mine[whole + info.id :: info.num_workers]])
 
+    def _batched_items(self, indices: np.ndarray) -> Iterator[Dict[str, Any]]:
+        """One batched fetch per device batch (the dataset reads all chunks of a batch in one native call)."""
+        bs = self.device_batch_size
+        for a in range(0, len(indices), bs):
+            ids = [int(i) for i in indices[a : a + bs]]
+            for idx, item in zip(ids, self.dataset.__getitems__(ids)):  # type: ignore[union-attr]
+                yield self._as_item(item, idx)
+
+    def __iter__(self) -> Iterator[Dict[str, Any]]:
+        indices = self._my_indices()
+        num_threads = self.num_threads
+        if num_threads is None and torch.utils.data.get_worker_info() is None:
+            num_threads = 4
+        if hasattr(self.dataset, "__getitems__"):
+            # the parallelism is inside the batched read; one background thread keeps two batches ahead of the consumer
+            items = self._batched_items(indices)
+            return threaded_generator(items, maxsize=2 * self.device_batch_size, thread_name="data prefetch") if num_threads else items
         if not num_threads:
             return (self._get_dataset_item(int(i)) for i in indices)
         depth = math.ceil(self.device_batch_size * 2 / num_threads)
@@ -135,10 +149,13 @@ class IterableDataset(torch.utils.data.IterableDataset[Dict[str, Any]]):
         ]
         return (x for x in roundrobin(*lanes))
 
-    def _get_dataset_item(self, idx: int) -> Dict[str, Any]:
-        item = self.dataset[idx]
+    @staticmethod
+    def _as_item(item: Any, idx: int) -> Dict[str, Any]:
         if isinstance(item, dict):
             return {**item, "index": idx}
         if dataclasses.is_dataclass(item):
             return dict(**dataclasses.asdict(item), index=idx)  # type: ignore[arg-type]
         return {"input_ids": item, "index": idx}
+
+    def _get_dataset_item(self, idx: int) -> Dict[str, Any]:
+        return self._as_item(self.dataset[idx], idx)

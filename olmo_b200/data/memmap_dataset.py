@@ -1,16 +1,18 @@
 """
-Fixed-length instances over concatenated flat token files (reference: ``olmo/data/memmap_dataset.py:20-247``).
+Fixed-length training instances over flat token files (the dataset the reference defines in
+``olmo/data/memmap_dataset.py:20-247``; same constructor and item keys, so configs and downstream code are unchanged).
 
-Files are headerless little-endian arrays of ``memmap_dtype`` tokens; instance ``i`` is tokens
-``[i·chunk, (i+1)·chunk)`` of the concatenation of whole chunks of every file.  Reads are byte-range requests, so
-local paths and every registered URL scheme work alike.  File sizes are resolved once, lazily, in a thread pool.
+Files are headerless little-endian arrays of ``memmap_dtype`` tokens; instance ``i`` is the ``i``-th whole chunk of
+``chunk_size`` tokens of the files laid end to end (the tail of a file that does not fill a chunk is skipped).  The
+dataset is a thin item-assembly layer over :class:`~olmo_b200.data.token_store.TokenStore`, which owns the extent table
+and the reads.  Besides ``dataset[i]`` there is the batched ``dataset.__getitems__([...])`` that ``torch``'s data
+loader prefers when it exists, and ``dataset.read_batch([...])`` which returns the stacked ``[n, chunk]`` tensors
+directly: both fetch all chunks of a batch in one call of the native reader.
 """
 from __future__ import annotations
 
-import bisect
-from concurrent.futures import ThreadPoolExecutor
 from copy import deepcopy
-from typing import Any, Dict, List, Optional, Tuple, Type, Union
+from typing import Any, Dict, List, Optional, Sequence, Tuple, Type, Union
 
 import numpy as np
 import torch
@@ -18,7 +20,7 @@ from torch.utils.data import Dataset
 
 from ..aliases import PathOrStr
 from ..config import InstanceFilterConfig
-from ..util import file_size, get_bytes_range
+from .token_store import TokenStore
 from .util import find_periodic_sequences, get_document_lengths
 
 __all__ = ["MemMapDataset"]
@@ -56,9 +58,11 @@ class MemMapDataset(Dataset[Dict[str, Any]]):
         self._metadata = metadata
         self._label_mask_paths = label_mask_paths
         self._chunk_size = chunk_size
-        self._mmap_offsets: Optional[List[Tuple[int, int]]] = None
-        self._starts: List[int] = []
         self.dtype = memmap_dtype
+        self._tokens = TokenStore(paths, memmap_dtype, chunk_size)
+        # label masks are one byte per token in files that line up with the token files
+        self._masks = TokenStore(label_mask_paths, np.uint8, chunk_size) if label_mask_paths else None
+        self._checked = False
         self._include_instance_metadata = include_instance_metadata
         self._generate_attention_mask = generate_attention_mask
         self._generate_doc_lengths = generate_doc_lengths
@@ -74,68 +78,51 @@ class MemMapDataset(Dataset[Dict[str, Any]]):
     def max_seq_len(self) -> int:
         return self._chunk_size
 
-    def _chunks_in(self, path: PathOrStr, dtype) -> int:
-        return file_size(path) // (np.dtype(dtype).itemsize * self._chunk_size)
+    def _check_masks(self) -> None:
+        if self._checked:
+            return
+        if self._masks is not None:
+            a, b = self._tokens.chunks_per_file(), self._masks.chunks_per_file()
+            for i in np.nonzero(a != b)[0][:1]:
+                raise ValueError(f"masking file '{self._label_mask_paths[i]}' should be the same size as '{self._memmap_paths[i]}'")  # type: ignore[index]
+        self._checked = True
 
     @property
     def offsets(self) -> List[Tuple[int, int]]:
         """``(first instance, one past last instance)`` of every file."""
-        if self._mmap_offsets is None:
-            with ThreadPoolExecutor() as pool:
-                lengths = list(pool.map(lambda p: self._chunks_in(p, self.dtype), self._memmap_paths))
-                mask_lengths = (
-                    list(pool.map(lambda p: self._chunks_in(p, np.bool_), self._label_mask_paths))
-                    if self._label_mask_paths is not None
-                    else None
-                )
-            if mask_lengths is not None:
-                for path, mpath, a, b in zip(self._memmap_paths, self._label_mask_paths, lengths, mask_lengths):  # type: ignore[arg-type]
-                    if a != b:
-                        raise ValueError(f"masking file '{mpath}' should be the same size as '{path}'")
-            offsets, start = [], 0
-            for n in lengths:
-                offsets.append((start, start + n))
-                start += n
-            self._mmap_offsets = offsets
-            self._starts = [o[0] for o in offsets]
-        return self._mmap_offsets
-
-    def _read_chunk(self, path: PathOrStr, index: int, dtype=None) -> torch.Tensor:
-        dtype = dtype or self.dtype
-        nbytes = np.dtype(dtype).itemsize * self._chunk_size
-        array = np.frombuffer(get_bytes_range(path, index * nbytes, nbytes), dtype=dtype)
-        if dtype == np.bool_:
-            return torch.tensor(array)
-        return torch.tensor(array.astype(np.int_), dtype=torch.long)
+        self._check_masks()
+        return self._tokens.file_ranges()
 
     def __len__(self) -> int:
-        return self.offsets[-1][1]
+        self._check_masks()
+        return len(self._tokens)
+
+    # ------------------------------------------------------------------------------ access
+    def read_batch(self, indices: Sequence[int], pin_memory: bool = False) -> Dict[str, Any]:
+        """Stacked tensors for a list of instances: ``input_ids [n, chunk]`` and, where configured, ``label_mask``,
+        ``attention_mask``; per-instance values (``metadata``, ``instance_mask``, ``doc_lens``) come as lists."""
+        self._check_masks()
+        ids = self._tokens.read(indices, pin_memory=pin_memory)
+        out: Dict[str, Any] = {"input_ids": ids}
+        if self.instance_filter_config is not None:
+            out["instance_mask"] = [self._validate_instance(row) for row in ids]
+        if self._masks is not None:
+            out["label_mask"] = self._masks.read(indices).to(torch.bool)
+        if self._include_instance_metadata:
+            files, _ = self._tokens.locate(indices)
+            out["metadata"] = [deepcopy(self._metadata[int(f)]) for f in files]
+        if self._generate_attention_mask:
+            out["attention_mask"] = (ids != self._pad_token_id).to(ids.dtype)
+        if self._generate_doc_lengths:
+            out["doc_lens"] = [get_document_lengths(row, self._eos_token_id) for row in ids]  # type: ignore[arg-type]
+        return out
+
+    def __getitems__(self, indices: Sequence[int]) -> List[Dict[str, Any]]:
+        batch = self.read_batch(indices)
+        return [{key: value[i] for key, value in batch.items()} for i in range(len(indices))]
 
     def __getitem__(self, index: int) -> Dict[str, Any]:
-        index = int(index)
-        n = len(self)
-        pos = index if index >= 0 else n + index
-        if not 0 <= pos < n:
-            raise IndexError(f"{index} is out of bounds for dataset of size {n}")
-        file_idx = bisect.bisect_right(self._starts, pos) - 1
-        while self.offsets[file_idx][1] <= pos:  # skip files that contribute no whole chunk
-            file_idx += 1
-        local = pos - self.offsets[file_idx][0]
-        input_ids = self._read_chunk(self._memmap_paths[file_idx], local)
-        out: Dict[str, Any] = {"input_ids": input_ids}
-        if self.instance_filter_config is not None:
-            out["instance_mask"] = self._validate_instance(input_ids)
-        if self._label_mask_paths is not None:
-            out["label_mask"] = self._read_chunk(self._label_mask_paths[file_idx], local, dtype=np.bool_)
-        if self._include_instance_metadata:
-            out["metadata"] = deepcopy(self._metadata[file_idx])
-        if self._generate_attention_mask:
-            mask = torch.ones_like(input_ids)
-            mask.masked_fill_(input_ids == self._pad_token_id, 0)
-            out["attention_mask"] = mask
-        if self._generate_doc_lengths:
-            out["doc_lens"] = get_document_lengths(input_ids, self._eos_token_id)  # type: ignore[arg-type]
-        return out
+        return self.__getitems__([int(index)])[0]
 
     def __add__(self, other: "MemMapDataset") -> "MemMapDataset":
         if not isinstance(other, MemMapDataset):
