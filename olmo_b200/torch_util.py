@@ -58,58 +58,86 @@ def is_distributed() -> bool:
     return dist.is_available() and dist.is_initialized()
 
 
-def _env_int(name: str) -> Optional[int]:
-    v = os.environ.get(name)
-    return None if v is None or v == "" else int(v)
+class _Placement:
+    """Where this process sits in the job.  The process group answers when there is one; otherwise the variables the
+    launcher exported (``RANK``, ``LOCAL_RANK``, ``LOCAL_WORLD_SIZE``, ``NODE_RANK``); otherwise a job of one."""
+
+    @staticmethod
+    def env(name: str, default: Optional[int] = None) -> Optional[int]:
+        text = os.environ.get(name, "")
+        return int(text) if text != "" else default
+
+    @classmethod
+    def world(cls) -> int:
+        return dist.get_world_size() if is_distributed() else 1
+
+    @classmethod
+    def rank(cls) -> int:
+        return dist.get_rank() if is_distributed() else cls.env("RANK", 0)  # type: ignore[return-value]
+
+    @classmethod
+    def local_rank(cls) -> int:
+        return cls.env("LOCAL_RANK", 0)  # type: ignore[return-value]
+
+    @classmethod
+    def local_world(cls) -> int:
+        return cls.env("LOCAL_WORLD_SIZE") or 1
+
+    @classmethod
+    def node(cls) -> int:
+        given = cls.env("NODE_RANK")
+        return given if given is not None else (cls.rank() - cls.local_rank()) // cls.local_world()
+
+    @classmethod
+    def fs_local_rank(cls) -> int:
+        explicit = cls.env("FS_LOCAL_RANK")
+        if explicit is not None:
+            return explicit
+        # one filesystem for the whole job: only global rank 0 is "first on its filesystem"
+        return cls.rank() if os.environ.get("OLMO_SHARED_FS") else cls.local_rank()
 
 
 def get_node_rank() -> int:
-    v = _env_int("NODE_RANK")
-    if v is not None:
-        return v
-    return (get_global_rank() - get_local_rank()) // get_local_world_size()
+    return _Placement.node()
 
 
 def get_world_size() -> int:
-    return dist.get_world_size() if is_distributed() else 1
+    return _Placement.world()
 
 
 def get_local_world_size() -> int:
-    return _env_int("LOCAL_WORLD_SIZE") or 1
+    return _Placement.local_world()
 
 
 def get_global_rank() -> int:
-    if is_distributed():
-        return dist.get_rank()
-    return _env_int("RANK") or 0
+    return _Placement.rank()
 
 
 def get_local_rank() -> int:
-    return _env_int("LOCAL_RANK") or 0
+    return _Placement.local_rank()
 
 
 def get_fs_local_rank() -> int:
-    """Rank among the processes that share this process's filesystem.
+    """Rank among the processes that share this process's filesystem: ``FS_LOCAL_RANK`` when set; the global rank when
+    ``OLMO_SHARED_FS`` says every rank sees the same files (so only global rank 0 writes shared artefacts); else the
+    local rank."""
+    return _Placement.fs_local_rank()
 
-    With ``OLMO_SHARED_FS`` set every rank sees the same files, so this is the global rank and
-    only global rank 0 writes shared artefacts; otherwise it is ``FS_LOCAL_RANK`` or the local rank.
-    """
-    if os.environ.get("OLMO_SHARED_FS"):
-        return int(os.environ.get("FS_LOCAL_RANK") or get_global_rank())
-    return int(os.environ.get("FS_LOCAL_RANK") or get_local_rank())
+
+def _map_tensors(o: Any, fn):
+    """Apply ``fn`` to every tensor inside nested dicts / lists / tuples; everything else passes through."""
+    if isinstance(o, torch.Tensor):
+        return fn(o)
+    if isinstance(o, dict):
+        return {k: _map_tensors(v, fn) for k, v in o.items()}
+    if isinstance(o, (list, tuple)):
+        return type(o)(_map_tensors(x, fn) for x in o)
+    return o
 
 
 def move_to_device(o: T, device: torch.device) -> T:
-    """Recursively move tensors in dicts / lists / tuples; ``non_blocking`` so pinned sources overlap."""
-    if isinstance(o, torch.Tensor):
-        return o.to(device, non_blocking=True)  # type: ignore[return-value]
-    if isinstance(o, dict):
-        return {k: move_to_device(v, device) for k, v in o.items()}  # type: ignore[return-value]
-    if isinstance(o, list):
-        return [move_to_device(x, device) for x in o]  # type: ignore[return-value]
-    if isinstance(o, tuple):
-        return tuple(move_to_device(x, device) for x in o)  # type: ignore[return-value]
-    return o
+    """Move the tensors of a nested batch; ``non_blocking`` so that copies from pinned memory overlap."""
+    return _map_tensors(o, lambda t: t.to(device, non_blocking=True))
 
 
 def ensure_finite_(x: torch.Tensor, check_neg_inf: bool = True, check_pos_inf: bool = False) -> None:
