@@ -41,21 +41,19 @@ class MemMapDataset(Dataset[Dict[str, Any]]):
         label_mask_paths: Optional[List[PathOrStr]] = None,
         instance_filter_config: Optional[InstanceFilterConfig] = None,
     ):
-        if not paths:
-            raise ValueError("At least one path is required")
-        if generate_attention_mask and pad_token_id is None:
-            raise ValueError("'pad_token_id' is required for 'generate_attention_mask'")
-        if generate_doc_lengths and eos_token_id is None:
-            raise ValueError("'eos_token_id' is required for 'generate_cu_doc_lengths'")
-        if label_mask_paths and len(label_mask_paths) != len(paths):
-            raise ValueError("There must be the same number of 'label_mask_paths' as there are 'paths'")
-        if isinstance(metadata, list):
-            if len(metadata) != len(paths):
-                raise ValueError("'metadata' should have the same length as the number of file paths")
-        else:
-            metadata = [metadata or {}] * len(paths)
+        n_files = len(paths)
+        problems = {
+            "At least one path is required": n_files == 0,
+            "'pad_token_id' is required for 'generate_attention_mask'": generate_attention_mask and pad_token_id is None,
+            "'eos_token_id' is required for 'generate_doc_lengths'": generate_doc_lengths and eos_token_id is None,
+            "'label_mask_paths' needs one mask file per token file": bool(label_mask_paths) and len(label_mask_paths or ()) != n_files,
+            "'metadata' given as a list needs one entry per token file": isinstance(metadata, list) and len(metadata) != n_files,
+        }
+        for message, broken in problems.items():
+            if broken:
+                raise ValueError(message)
         self._memmap_paths = paths
-        self._metadata = metadata
+        self._metadata: List[Dict[str, Any]] = metadata if isinstance(metadata, list) else [metadata or {}] * n_files
         self._label_mask_paths = label_mask_paths
         self._chunk_size = chunk_size
         self.dtype = memmap_dtype
