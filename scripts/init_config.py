@@ -1,9 +1,17 @@
 #!/usr/bin/env python
-"""Write a default training config: ``scripts/init_config.py OUT.yaml [--dotted.key=value ...]``
-(reference: ``scripts/init_config.py``)."""
+"""Write a starting training config.
+
+    scripts/init_config.py OUT.yaml [--from RECIPE] [--dotted.key=value ...]
+    scripts/init_config.py --list
+
+Without ``--from`` the file holds the defaults of every field (what the reference's ``scripts/init_config.py`` writes);
+with it, the named recipe of ``olmo_b200.recipes`` (an official OLMo / OLMo-2 run, a tiny model, ...).  Dotted overrides are
+applied on top and the result is validated before it is written.
+"""
 import logging
 import sys
 from pathlib import Path
+from typing import List, Optional
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
@@ -15,17 +23,36 @@ from olmo_b200.utils import structured as S
 log = logging.getLogger(__name__)
 
 
-def main(save_path: Path, overrides) -> None:
-    raw = S.deep_merge(S.to_container(TrainConfig()), S.parse_dotlist(overrides))
-    cfg = S.build(TrainConfig, S.resolve_interpolations(raw))
-    log.info("Saving config to %s", save_path)
+def main(save_path: Path, overrides: List[str], recipe: Optional[str] = None) -> TrainConfig:
+    if recipe is None:
+        merged = S.deep_merge(S.to_container(TrainConfig()), S.parse_dotlist(overrides))
+        cfg = S.build(TrainConfig, S.resolve_interpolations(merged))
+    else:
+        from olmo_b200.recipes import RECIPES, recipe_config
+
+        if recipe not in RECIPES:
+            raise OLMoCliError(f"unknown recipe '{recipe}'; `--list` shows the names")
+        cfg = recipe_config(recipe, overrides)
     cfg.save(save_path)
+    log.info("wrote %s (%s)", save_path, f"recipe {recipe}" if recipe else "field defaults")
+    return cfg
 
 
 if __name__ == "__main__":
     prepare_cli_environment()
-    try:
-        out, args = sys.argv[1], sys.argv[2:]
-    except IndexError:
-        raise OLMoCliError(f"Usage: {sys.argv[0]} [SAVE_PATH] [OPTIONS]")
-    main(Path(out), [clean_opt(s) for s in args])
+    argv = sys.argv[1:]
+    if "--list" in argv:
+        from olmo_b200.recipes import RECIPES
+
+        print("\n".join(sorted(RECIPES)))
+        sys.exit(0)
+    recipe = None
+    if "--from" in argv:
+        at = argv.index("--from")
+        if at + 1 >= len(argv):
+            raise OLMoCliError("--from needs a recipe name")
+        recipe = argv[at + 1]
+        del argv[at : at + 2]
+    if not argv:
+        raise OLMoCliError(f"Usage: {sys.argv[0]} SAVE_PATH [--from RECIPE] [OPTIONS]")
+    main(Path(argv[0]), [clean_opt(s) for s in argv[1:]], recipe)

@@ -365,3 +365,29 @@ def test_launch_scripts_parse_and_pick_the_node_layout(tmp_path):
     env.update(BEAKER_REPLICA_COUNT="4", BEAKER_REPLICA_RANK="2", BEAKER_LEADER_REPLICA_HOSTNAME="node0")
     many = subprocess.run(["bash", str(fake / "beaker.sh"), "c.yaml"], capture_output=True, text=True, env=env)
     assert many.stdout.strip() == "multi_node.sh 4 2 node0 c.yaml"
+
+
+def test_model_size_breakdown_and_config_starter(tmp_path):
+    from olmo_b200.config import ModelConfig, TrainConfig
+    from olmo_b200.models.olmo import OLMo
+
+    sizes_mod = load_script("show_model_size")
+    cfg = TrainConfig(model=ModelConfig(d_model=64, n_heads=4, n_layers=3, mlp_ratio=4, vocab_size=200, embedding_size=256, weight_tying=False,
+                                        max_sequence_length=32, include_bias=False, init_device="cpu"))
+    sizes = sizes_mod.count(cfg)
+    real = OLMo(cfg.model, init_params=False)
+    assert cfg.model.n_layers == 3 and sizes["total"] == real.num_params() and sizes["non_embedding"] == real.num_params(include_embedding=False)
+    assert sizes["embedding"] + sizes["head"] + sizes["other"] + sizes["blocks"] * sizes["block"] == sizes["total"] and sizes["head"] == 256 * 64
+    plans = [sizes_mod.memory_plan(sizes, n) for n in (1, 2, 4, 8)]
+    assert plans[0]["resident"] == pytest.approx(18 * sizes["total"] / 1e9)
+    assert all(a["resident"] > b["resident"] and b["sharded"] < b["resident"] for a, b in zip(plans, plans[1:]))
+
+    starter = load_script("init_config")
+    plain = starter.main(tmp_path / "plain.yaml", ["model.d_model=96"])
+    assert plain.model.d_model == 96 and TrainConfig.load(tmp_path / "plain.yaml", validate_paths=False).model.d_model == 96
+    recipe = starter.main(tmp_path / "r.yaml", ["seed=11"], recipe="OLMo2-1B-stage1")
+    assert recipe.seed == 11 and recipe.model.d_model == 2048 and (tmp_path / "r.yaml").is_file()
+    from olmo_b200.exceptions import OLMoCliError
+
+    with pytest.raises(OLMoCliError):
+        starter.main(tmp_path / "x.yaml", [], recipe="no-such-recipe")
