@@ -198,6 +198,64 @@ RECIPES["OLMo2-7B-anneal-example"] = {
     **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": "annealing/OLMo2-7B-anneal-example.yaml",
 }
 
+# The same development runs as the reference files them, one file per storage system (configs/peteish{1,7,13}-{weka,
+# google,s3}.yaml): the recipe of the size with that storage's file list (``data_mixes/<name>.txt``) and the few settings in
+# which the files differ (epoch vs token budget, cosine horizon, activation checkpointing on the smaller-memory pool).
+for _size, _store, _diff in (
+    ("1", "google", {"max_duration": "4e12T"}),
+    ("1", "weka", {"max_duration": "1ep", "scheduler": {**_OLMO2_SCHED, "t_max": 3e12}}),
+    ("7", "google", {}), ("7", "weka", {}), ("7", "s3", {"activation_checkpointing": None}),
+    ("13", "google", {"max_duration": "5e12T"}), ("13", "weka", {}), ("13", "s3", {}),
+):
+    RECIPES[f"peteish{_size}-{_store}"] = {**deepcopy(RECIPES[f"peteish{_size}"]), "file": f"peteish{_size}-{_store}.yaml", **_diff}
+
+# Mid-training ("annealing") runs: linear decay to zero from a stage-1 checkpoint over a token budget, new data order,
+# data position not restored.  (reference: configs/annealing/*.yaml; columns: size, file stem, seed, peak lr, tokens,
+# stop step, stage-1 checkpoint, activation checkpointing)
+_ANNEAL_RUNS = (
+    ("1", "peteish1-anneal-from-1907359-50B-nowup-moremath-dclm07-fw2-se-flan-google", 7201, 7.448728958032132e-05, "50e9T", 23852,
+     "gs://ai2-llm/checkpoints/OLMo-small/peteish1/step1907359", "one_in_four"),
+    ("13", "peteish13-anneal-from-596057-100B-legal-whammy-2-google", 7201, 9e-5, "100e9T", 11931,
+     "gs://ai2-llm/checkpoints/OLMo-medium/peteish13-highlr-zlossfix/step596057", None),
+    ("13", "peteish13-anneal-from-596057-300B-legal-whammy-2-google", 7201, 9e-5, "300e9T", 35773,
+     "gs://ai2-llm/checkpoints/OLMo-medium/peteish13-highlr-zlossfix/step596057", None),
+    ("7", "peteish7-anneal-from-477000-100B-moremath-dclm07-fw2-se-flan-google", 7201, 0.00020707, "100e9T", 23852,
+     "gs://ai2-llm/checkpoints/OLMo-medium/peteish7/step477000", None),
+    ("7", "peteish7-medlr-anneal-from-477000-100B-moremath-dclm07-fw2-se-flan-google", 7201, 0.00041414, "100e9T", 23852,
+     "gs://ai2-llm/checkpoints/OLMo-medium/peteish7-medlr/step477000", None),
+) + tuple(
+    ("7", f"peteish7-weka-anneal-from-928646-50B-nowup_legal-whammy-2_seed{_seed}", _seed, 6.1499e-05, "50e9T", 11931,
+     "/weka/oe-training-default/ai2-llm/checkpoints/OLMo-medium/peteish7/step928646", "one_in_four")
+    for _seed in (42, 42069, 666)
+)
+_SIZE_SHAPE = {"1": ("olmo2-1b", 512), "7": ("olmo2-7b", 1024), "13": ("olmo2-13b", 2048)}
+for _size, _stem, _seed, _lr, _tokens, _stop, _ckpt, _ac in _ANNEAL_RUNS:
+    RECIPES[_stem] = {
+        **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": f"annealing/{_stem}.yaml", "family": _SIZE_SHAPE[_size][0], "seed": _seed,
+        "optimizer": _adamw(_lr, **_OLMO2_OPT), "scheduler": {"name": "linear_with_warmup", "units": "steps", "t_warmup": 0, "alpha_f": 0.0},
+        "global_train_batch_size": _SIZE_SHAPE[_size][1], "device_train_microbatch_size": 2, "max_duration": _tokens, "stop_at": _stop,
+        "load_path": "${oc.env:OLMO_STAGE1_CHECKPOINT," + _ckpt + "}", "activation_checkpointing": _ac,
+    }
+
+# "Micro-anneals": the same decay over one pass of a small candidate data source mixed with web text, used to rank data
+# sources cheaply (reference: configs/microannealing/*.yaml).  All start from step 928646 of the 7B run except the last.
+_MICRO_SOURCES = (
+    "automathtext", "bestof-v1", "mathcoder-synthetic", "mathpile", "owm", "pes2o", "reddit-qa-all", "reddit-v1", "se",
+    "small-sources-big-dclm", "small-sources-multiadd", "small-sources", "small-sources_x2", "small-sources_x4", "tiny-gsm-inline",
+    "tiny-gsm-mind", "tiny-gsm-mind_x2",
+)
+_MICRO_RUNS = tuple(
+    (f"peteish7-weka-microanneal-from928646_{_src}", 6.1499e-05, "/weka/oe-training-default/ai2-llm/checkpoints/OLMo-medium/peteish7/step928646")
+    for _src in _MICRO_SOURCES
+) + (("peteish7-weka-microanneal-fromMegaMath1.1-5000_nonmath", 3.5726e-05,
+      "/weka/oe-training-default/ai2-llm/checkpoints/OLMo-medium/peteish7-weka-anneal-from-928646-50B-megamath_v1.1.yaml/step5000/"),)
+for _stem, _lr, _ckpt in _MICRO_RUNS:
+    RECIPES[_stem] = {
+        **deepcopy(RECIPES["OLMo2-7B-stage2"]), "file": f"microannealing/{_stem}.yaml", "seed": 7201, "optimizer": _adamw(_lr, **_OLMO2_OPT),
+        "max_duration": "1ep", "stop_at": None, "load_path": "${oc.env:OLMO_STAGE1_CHECKPOINT," + _ckpt + "}",
+        "activation_checkpointing": "one_in_four",
+    }
+
 # Training on a user-supplied ``torch.utils.data.Dataset`` instead of token memmaps (reference:
 # configs/custom_dataset_example.yaml): ``name`` is ``module.Class`` (or a class name plus ``module``), ``args`` its
 # constructor arguments, ``collate_config`` maps the dataset's field names onto the batch keys the trainer reads.

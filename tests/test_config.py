@@ -215,3 +215,20 @@ def test_named_data_mixes_and_checkpoint_tables_are_packaged():
     root = Path(__file__).resolve().parent.parent / "configs"
     for rel in ("official-1124/OLMo-2-1124-7B.csv", "official-1124/OLMo-2-1124-13B.csv", "official-0425/OLMo-2-0425-1B.csv", "official-0724/OLMo-7B-0724.csv"):
         assert (root / rel).is_file(), rel
+
+
+def test_development_anneal_and_micro_anneal_recipes_are_generated():
+    from olmo_b200.recipes import RECIPES, recipe_config
+
+    files = {spec["file"] for spec in RECIPES.values()}
+    assert sum(f.startswith("annealing/peteish") for f in files) == 8 and sum(f.startswith("microannealing/") for f in files) == 18
+    assert {f"peteish{n}-{s}.yaml" for n, s in (("1", "google"), ("1", "weka"), ("7", "google"), ("7", "weka"), ("7", "s3"), ("13", "google"),
+                                                ("13", "weka"), ("13", "s3"))} <= files
+    repo = Path(__file__).resolve().parent.parent
+    assert all((repo / "configs" / f).is_file() for f in files), "run `python -m olmo_b200.recipes --write configs`"
+    micro = recipe_config("peteish7-weka-microanneal-from928646_owm")
+    assert micro.max_duration == "1ep" and micro.stop_at is None and micro.seed == 7201 and micro.restore_dataloader is False
+    assert micro.optimizer.learning_rate == pytest.approx(6.1499e-05) and micro.load_path.endswith("peteish7/step928646") and len(micro.data.paths) == 25
+    big = recipe_config("peteish13-anneal-from-596057-300B-legal-whammy-2-google")
+    assert big.model.d_model == 5120 and big.stop_at == 35773 and big.max_duration == "300e9T" and big.global_train_batch_size == 2048
+    assert recipe_config("peteish1-weka").scheduler.t_max == 3e12 and recipe_config("peteish7-s3").activation_checkpointing is None
