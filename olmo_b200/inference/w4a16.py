@@ -48,6 +48,19 @@ def quantize_groups(w: torch.Tensor, group: int) -> Tuple[torch.Tensor, torch.Te
     return scales, zeros
 
 
+class _QuantMatmul(torch.autograd.Function):
+    """``x · Wᵀ`` through the quantised kernels with a gradient for ``x`` (the packed weights are constants)."""
+
+    @staticmethod
+    def forward(ctx, x2: torch.Tensor, layer: "QuantLinear") -> torch.Tensor:  # type: ignore[override]
+        ctx.layer = layer
+        return layer._matmul(x2)
+
+    @staticmethod
+    def backward(ctx, dy: torch.Tensor):  # type: ignore[override]
+        return ctx.layer._input_gradient(dy).to(dy.dtype), None
+
+
 class QuantLinear(nn.Module):
     """Drop-in replacement of a bias-free or biased ``nn.Linear`` holding 4-bit weights."""
 
@@ -109,6 +122,29 @@ class QuantLinear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         lead = x.shape[:-1]
         x2 = x.reshape(-1, self.in_features)
+        # the kernels know nothing of autograd: when the input needs a gradient (adapters or prompts trained on top of a
+        # quantised model) the product runs inside a Function whose backward multiplies by the reconstructed weights
+        y = _QuantMatmul.apply(x2, self) if x2.requires_grad and torch.is_grad_enabled() else self._matmul(x2)
+        if self.bias is not None:
+            y = y + self.bias.to(y.dtype)
+        return y.reshape(*lead, self.out_features)
+
+    def _input_gradient(self, dy: torch.Tensor) -> torch.Tensor:
+        """``dy[M, N] · W`` in the input's own column order (``transpose_quant_matmul`` of the reference's Triton kernels,
+        ``auto_gptq/nn_modules/triton_utils/kernels.py:186-278``): reconstruct once, one GEMM, undo the activation order."""
+        w = self.dequantize()
+        if dy.is_cuda and self.in_features % 8 == 0 and self.out_features % 8 == 0:
+            from ..ops import kernels as k
+
+            dx = k.gemm(dy.to(torch.bfloat16).contiguous(), w, b_trans=True)
+        else:
+            dx = dy.to(w.dtype) @ w
+        if self.perm is not None:  # forward read column perm[j] of the input as stored column j
+            dx = torch.empty_like(dx).index_copy_(1, self.perm.long(), dx)
+        return dx
+
+    def _matmul(self, x2: torch.Tensor) -> torch.Tensor:
+        x = x2
         if not x2.is_cuda:
             from . import cpu_ref
 
@@ -151,9 +187,7 @@ class QuantLinear(nn.Module):
             else:
                 y = k.gemm(xb, self.dequantize())
             y = y.to(x.dtype)
-        if self.bias is not None:
-            y = y + self.bias.to(y.dtype)
-        return y.reshape(*lead, self.out_features)
+        return y
 
     def extra_repr(self) -> str:
         return f"in_features={self.in_features}, out_features={self.out_features}, group={self.group}, act_order={self.perm is not None}"

@@ -158,6 +158,46 @@ def test_quantised_checkpoint_round_trip_and_stdio_predictor(tmp_path):
     assert picks[0] == int(direct.argmax()) and len(probs) == 2 and abs(sum(probs[0]) - 1.0) > 0 and len(probs[0]) == 4
 
 
+def _grad_case(act_order: bool, M: int = 5, N: int = 24, K: int = 64, G: int = 32):
+    torch.manual_seed(3)
+    q = torch.randint(0, 16, (N, K))
+    scales = (torch.rand(N, K // G) * 0.2 + 0.05).to(torch.bfloat16).float()
+    zeros = torch.randint(0, 16, (N, K // G))
+    perm = torch.randperm(K) if act_order else None
+    layer = QuantLinear.from_quantized(q, scales, zeros, G, perm=perm, bias=torch.randn(N))
+    x = torch.randn(2, M, K)
+    dy = torch.randn(2, M, N)
+    w_stored = manual_dequant(layer)
+    xr = x.clone().requires_grad_(True)
+    cols = xr if perm is None else xr[..., perm]
+    ((cols @ w_stored.t() + layer.bias) * dy).sum().backward()
+    return layer, x, dy, xr.grad
+
+
+@pytest.mark.parametrize("act_order", [False, True])
+def test_input_gradient_through_quantised_weights_cpu(act_order):
+    layer, x, dy, want = _grad_case(act_order)
+    xg = x.clone().requires_grad_(True)
+    y = layer(xg)
+    assert y.requires_grad and y.shape == dy.shape
+    (y * dy).sum().backward()
+    torch.testing.assert_close(xg.grad, want, rtol=1e-4, atol=1e-4)
+    with torch.no_grad():
+        assert not layer(xg).requires_grad
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("act_order", [False, True])
+def test_input_gradient_through_quantised_weights_gpu(act_order):
+    layer, x, dy, want = _grad_case(act_order, M=100, N=256, K=512, G=128)
+    layer = layer.cuda()
+    xg = x.cuda().to(torch.bfloat16).requires_grad_(True)
+    (layer(xg) * dy.cuda().to(torch.bfloat16)).sum().backward()
+    ref = want.to(torch.bfloat16).float()
+    err = (xg.grad.float().cpu() - ref).abs().max().item()
+    assert err <= 3e-2 * ref.abs().max().item() + 1e-3, err  # bf16 inputs, bf16 reconstructed weights, fp32 accumulation
+
+
 @pytest.mark.gpu
 @pytest.mark.parametrize("M", [1, 3, 8, 64])
 @pytest.mark.parametrize("act_order", [False, True])
