@@ -39,7 +39,7 @@ from .exceptions import OLMoCheckpointError
 
 __all__ = [
     "ShardedTensorRecord", "detect_layout", "load_with_sharded_tensor_records", "unshard_torch_legacy_checkpoint",
-    "unshard_local_checkpoint", "unshard_reference_checkpoint",
+    "unshard_local_checkpoint", "unshard_reference_checkpoint", "export_torch_new_checkpoint",
 ]
 
 log = logging.getLogger(__name__)
@@ -377,3 +377,46 @@ def unshard_reference_checkpoint(
             "framework does not bundle: unshard it with the tool that wrote it, then load the unsharded result here"
         )
     raise OLMoCheckpointError(f"{load_path}: layout '{layout}' is not a reference sharded layout")
+
+
+# ------------------------------------------------------------------------------------------------ export
+
+
+def export_torch_new_checkpoint(
+    out_dir: PathOrStr, model_state: Dict[str, torch.Tensor], optim_state: Optional[Dict[str, Any]] = None,
+    trainer_state: Optional[Dict[str, Any]] = None, *, world_size: int = 1,
+) -> Path:
+    """Write full states in the layout of the reference's ``torch_new`` sharded checkpointer
+    (``olmo/checkpoint.py:99-144,892-966``): ``model_and_optim/`` in torch's distributed-checkpoint format holding
+    ``model.<parameter>`` tensors, ``optim.state.<parameter>.<key>`` tensors and the parameter groups, plus
+    ``train/rank{r}.pt``.  That format records every tensor as chunks with global offsets and is resharded by its
+    reader, so one writer process produces a checkpoint that a job of any world size can load with FSDP's sharded state
+    dicts; ``world_size`` only sets how many per-rank trainer-state files are written (each rank reads its own).
+    ``optim_state`` is keyed by parameter name (``{"state": {name: {...}}, "param_groups": [{"params": [names], ...}]}``),
+    the form of an unsharded ``optim.pt``."""
+    import torch.distributed.checkpoint as dcp
+
+    out = Path(out_dir)
+    folder = out / "model_and_optim"
+    folder.mkdir(parents=True, exist_ok=True)
+    payload: Dict[str, Any] = {"model": {name: t.detach().cpu().contiguous() for name, t in model_state.items()}}
+    if optim_state is not None:
+        groups = optim_state.get("param_groups", [])
+        known = set(model_state)
+        for group in groups:
+            for name in group.get("params", []):
+                if not isinstance(name, str) or name not in known:
+                    raise OLMoCheckpointError(
+                        f"parameter group entry {name!r} is not a parameter name of the model state; the export needs an "
+                        "optimizer state keyed by parameter name"
+                    )
+        state = {
+            name: {key: (v.detach().cpu().contiguous() if isinstance(v, torch.Tensor) else v) for key, v in entry.items()}
+            for name, entry in optim_state.get("state", {}).items()
+        }
+        payload["optim"] = {"state": state, "param_groups": groups}
+    dcp.save(payload, storage_writer=dcp.FileSystemWriter(str(folder)), no_dist=True)
+    (out / "train").mkdir(exist_ok=True)
+    for rank in range(max(1, world_size)):
+        torch.save(trainer_state or {}, out / "train" / f"rank{rank}.pt")
+    return out

@@ -185,6 +185,56 @@ def test_sharded_checkpoint_of_the_reference_layout_is_unsharded_offline(tmp_pat
     assert abs(again - expect) < 1e-5
 
 
+def test_checkpoints_are_exported_to_the_reference_sharded_layout(tmp_path):
+    """``scripts/export_sharded.py`` turns an unsharded checkpoint and a flat-shard checkpoint of this framework into the
+    reference's ``torch_new`` layout; the result is detected as such, holds every tensor under the key the layout
+    prescribes, and a trainer resumes from it with the same weights, moments, step and next loss."""
+    import importlib.util
+    from pathlib import Path
+
+    from torch.distributed.checkpoint import FileSystemReader
+
+    from olmo_b200.checkpoint_compat import detect_layout
+    from olmo_b200.config import CheckpointType, ShardedCheckpointerType, TrainConfig
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "a")
+    cfg.save_overwrite = True
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    batches = iter(trainer.train_loader)
+    for _ in range(3):
+        trainer.global_step += 1
+        trainer.global_train_examples_seen_this_epoch += cfg.global_train_batch_size
+        trainer.global_train_tokens_seen += cfg.global_train_batch_size * cfg.model.max_sequence_length
+        trainer.train_step(next(batches))
+    unsharded, _ = trainer.save_checkpoint(CheckpointType.unsharded)
+    sharded, _ = trainer.save_checkpoint(CheckpointType.sharded)
+    named = dict(trainer.dist_model.engine.named_parameters_for_optimizer())
+
+    spec = importlib.util.spec_from_file_location("export_sharded", str(Path(__file__).resolve().parent.parent / "scripts" / "export_sharded.py"))
+    export = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(export)
+    for source, name in ((unsharded, "export-a"), (sharded, "export-b")):
+        out = export.main(source, tmp_path / name, world_size=2)
+        assert detect_layout(out) == "torch_new" and (out / "train" / "rank1.pt").is_file()
+        assert TrainConfig.load(out / "config.yaml", validate_paths=False).sharded_checkpointer == ShardedCheckpointerType.torch_new
+        keys = set(FileSystemReader(str(out / "model_and_optim")).read_metadata().state_dict_metadata)
+        some = next(iter(named))
+        assert {f"model.{some}", f"optim.state.{some}.exp_avg", f"optim.state.{some}.exp_avg_sq"} <= keys
+        cfg2 = tiny_train_config(tmp_path / f"resume-{name}")
+        t2 = build_trainer(cfg2, device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+        t2.restore_checkpoint(str(out))
+        assert t2.global_step == 3
+        for n, p in t2.dist_model.engine.named_parameters_for_optimizer():
+            assert torch.equal(p.detach(), named[n].detach()), n
+            assert torch.equal(t2.optim.state[p]["exp_avg"], trainer.optim.state[named[n]]["exp_avg"]), n
+    expect = trainer.train_step(next(batches))["train/CrossEntropyLoss"]
+    again = t2.train_step(next(iter(t2.train_loader)))["train/CrossEntropyLoss"]
+    assert abs(again - expect) < 1e-5
+    model_only = export.main(unsharded, tmp_path / "weights", model_only=True)
+    assert not any(k.startswith("optim.") for k in FileSystemReader(str(model_only / "model_and_optim")).read_metadata().state_dict_metadata)
+
+
 def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
     """``rank{r}.pt`` files holding ``ShardedTensor`` pickles (the reference's default sharded layout,
     ``olmo/checkpoint.py:969-1453``), written here by two gloo ranks from a trainer's full state, are detected by
