@@ -23,6 +23,7 @@ copied from pinned host memory and its loss read back.  Rank 0 prints one JSON l
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import os
 import statistics
@@ -114,10 +115,11 @@ def make_train_config(args, world: int):
 class ClockSampler:
     """Samples SM clock and throttle reasons of one GPU with nvidia-smi while the timed region runs."""
 
-    FIELDS = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    FIELDS = "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
     def __init__(self, index: int):
         self.index, self.proc, self.path = index, None, None
+        self.samples = []  # (seconds since the epoch, SM MHz, watts) of every sample, filled by stop()
 
     def start(self) -> None:
         try:
@@ -142,14 +144,19 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in Path(self.path).read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 7:
+            if len(parts) < 8:
                 continue
             try:
-                sm.append(float(parts[0]))
-                mx.append(float(parts[1]))
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
             except ValueError:
                 continue
-            for name, val in zip(names, parts[3:7]):
+            try:
+                stamp = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                self.samples.append((stamp, sm[-1], float(parts[3])))
+            except ValueError:
+                pass
+            for name, val in zip(names, parts[4:8]):
                 if val.lower().startswith("active"):
                     reasons.add(name)
         try:
@@ -204,6 +211,20 @@ class PhaseTimer:
         else:
             m = t[None]
         return {n: {"min": m[:, i].min().item(), "median": m[:, i].median().item(), "max": m[:, i].max().item()} for i, n in enumerate(names)}
+
+
+def clocks_by_phase(samples, t0: float, boundaries) -> dict:
+    """Median SM clock and power per phase.  ``samples``: (epoch seconds, MHz, watts); ``t0``: epoch seconds at which the
+    device started the step; ``boundaries``: (phase name, start offset in ms, end offset in ms) in device time."""
+    bins = {}
+    for stamp, mhz, watts in samples:
+        off = (stamp - t0) * 1e3
+        for name, a, b in boundaries:
+            if a <= off < b:
+                bins.setdefault(name, []).append((mhz, watts))
+                break
+    return {name: {"sm_mhz": statistics.median(v[0] for v in vals), "power_w": statistics.median(v[1] for v in vals), "samples": len(vals)}
+            for name, vals in bins.items()}
 
 
 def run_ours(args) -> dict:
@@ -304,12 +325,22 @@ def run_ours(args) -> dict:
         }
 
     # ---- one more step with per-phase CUDA events on every rank (not part of either timed region)
-    phases = None
+    phases = phase_clocks = None
     if engine.fused:
         engine.phase_timer = PhaseTimer()
+        phase_sampler = ClockSampler(local_rank)
+        phase_sampler.start()
+        time.sleep(0.5)  # the sampler needs a moment to produce its first line
         barrier()
+        t_host0 = time.time()  # the device is idle here, so the event below is recorded at this moment
+        ev_p0 = torch.cuda.Event(enable_timing=True)
+        ev_p0.record()
         step(args.warmup + 2 * args.steps, False)
         barrier()
+        phase_sampler.stop()
+        marks = engine.phase_timer.marks
+        bounds = [(name, ev_p0.elapsed_time(ev), ev_p0.elapsed_time(nxt)) for (name, ev), (_, nxt) in zip(marks, marks[1:])]
+        phase_clocks = clocks_by_phase(phase_sampler.samples, t_host0, bounds)
         phases = engine.phase_timer.summary(world, device)
         engine.phase_timer = None
 
@@ -352,7 +383,7 @@ def run_ours(args) -> dict:
             "reduced_model": f"REDUCED to {args.n_layers} layers (profiling only)" if args.n_layers else None,
         },
         "ms_per_step_x_sm_ghz": (ms_per_step * sm_mhz / 1e3) if sm_mhz else None,
-        "phases_ms": phases, "multi_gpu_check": multi_gpu_check,
+        "phases_ms": phases, "clocks_by_phase_rank0": phase_clocks, "multi_gpu_check": multi_gpu_check,
         "clocks": clocks, "e2e": e2e, "gpu_launches": launches, "checkpoint": checkpoint,
         "peak_mem_gb": torch.cuda.max_memory_allocated() / 1e9,
         # the caching allocator's peak does not see peer-memory (symmetric) buffers; this is the device's own count
