@@ -117,8 +117,8 @@ class ClockSampler:
 
     FIELDS = "timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
 
-    def __init__(self, index: int):
-        self.index, self.proc, self.path = index, None, None
+    def __init__(self, index: int, interval_ms: int = 200):
+        self.index, self.proc, self.path, self.interval_ms = index, None, None, interval_ms
         self.samples = []  # (seconds since the epoch, SM MHz, watts) of every sample, filled by stop()
 
     def start(self) -> None:
@@ -126,7 +126,7 @@ class ClockSampler:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", str(self.interval_ms)],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL,
             )
         except Exception:
@@ -328,7 +328,9 @@ def run_ours(args) -> dict:
     phases = phase_clocks = None
     if engine.fused:
         engine.phase_timer = PhaseTimer()
-        phase_sampler = ClockSampler(local_rank)
+        # a short, odd interval: the 200 ms of the timed region is close to a multiple of a micro-batch's duration for some
+        # model sizes, and then every sample would fall into the same phase
+        phase_sampler = ClockSampler(local_rank, interval_ms=37)
         phase_sampler.start()
         time.sleep(0.5)  # the sampler needs a moment to produce its first line
         barrier()
