@@ -118,7 +118,7 @@ def run_microbatch(st, comm, n_blocks, is_last):
     st.flush_rs(is_last)
 
 
-@pytest.mark.parametrize("n_blocks,per_unit", [(2, 1), (5, 1), (8, 1), (6, 2)])
+@pytest.mark.parametrize("n_blocks,per_unit", [(1, 1), (2, 1), (3, 1), (5, 1), (8, 1), (6, 2), (4, 4)])
 def test_streamed_schedule_invariants(n_blocks, per_unit):
     st, comm, nb = make_state(n_blocks, per_unit)
     n_units = n_blocks // per_unit
