@@ -356,11 +356,16 @@ class Trainer:
         remote: Optional[str] = None
         if self.cfg.remote_save_folder is not None:
             remote = f"{self.cfg.remote_save_folder.rstrip('/')}/{ckpt_dir.name}"
-        current.append(ckpt_dir)
+        current.append(ckpt_dir)  # before the save: the trainer state that is written lists this checkpoint too
         try:
             checkpointer.save_checkpoint(ckpt_dir, self.dist_model, self.optim, self.trainer_state_dict(), upload_to=remote)
-        except FileExistsError:
-            raise OLMoConfigurationError(f"Checkpoint for step {self.global_step} already exists, use --save_overwrite to overwrite it")
+        except BaseException as e:
+            # a save that did not complete (full disk, remote store down, rank lost) must not stay on the books: the
+            # rotation below would count it, and a retry of the same step would list it twice
+            current.remove(ckpt_dir)
+            if isinstance(e, FileExistsError):
+                raise OLMoConfigurationError(f"Checkpoint for step {self.global_step} already exists, use --save_overwrite to overwrite it")
+            raise
         if link_latest:
             latest = Path(self.cfg.save_folder) / f"latest{suffix}"
             latest.unlink(missing_ok=True)

@@ -1,5 +1,6 @@
 """End-to-end plumbing on CPU: a tiny decoder trains for a few AdamW steps and its checkpoints round-trip."""
 import math
+from pathlib import Path
 
 import pytest
 import torch
@@ -233,6 +234,49 @@ def test_checkpoints_are_exported_to_the_reference_sharded_layout(tmp_path):
     assert abs(again - expect) < 1e-5
     model_only = export.main(unsharded, tmp_path / "weights", model_only=True)
     assert not any(k.startswith("optim.") for k in FileSystemReader(str(model_only / "model_and_optim")).read_metadata().state_dict_metadata)
+
+
+@pytest.mark.parametrize("kind", ["sharded", "unsharded"])
+def test_failing_upload_leaves_no_checkpoint_behind_and_a_retry_succeeds(tmp_path, monkeypatch, kind):
+    """The remote store rejects the second file of a checkpoint.  The save raises, the step's folder does not appear under
+    its final name (only the ``-tmp`` one exists, which the next attempt clears), nothing is registered as the latest
+    checkpoint, and once the store works again the same step is saved and restores."""
+    import olmo_b200.checkpoint as ckpt_mod
+    from olmo_b200.config import CheckpointType
+    from olmo_b200.exceptions import OLMoNetworkError
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "run")
+    cfg.remote_save_folder = "s3://bucket/run"
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    trainer.global_step = 1
+    trainer.train_step(next(iter(trainer.train_loader)))
+    uploaded, calls = [], {"n": 0}
+
+    def flaky_upload(source, target, save_overwrite=False):
+        calls["n"] += 1
+        if calls["n"] == 2:
+            raise OLMoNetworkError(f"simulated outage while writing {target}")
+        uploaded.append(str(target))
+
+    monkeypatch.setattr(ckpt_mod, "upload", flaky_upload)
+    which = CheckpointType.sharded if kind == "sharded" else CheckpointType.unsharded
+    with pytest.raises(OLMoNetworkError, match="simulated outage"):
+        trainer.save_checkpoint(which)
+    name = "step1" if kind == "sharded" else "step1-unsharded"
+    folder = tmp_path / "run" / name
+    assert not folder.exists() and (tmp_path / "run" / f"{name}-tmp").exists()
+    assert not (tmp_path / "run" / ("latest" if kind == "sharded" else "latest-unsharded")).exists()
+    assert (trainer.checkpoints if kind == "sharded" else trainer.unsharded_checkpoints) == []
+
+    calls["n"] = 100  # the store is back
+    remote, local = trainer.save_checkpoint(which)  # with a remote folder the remote location comes first
+    assert Path(local) == folder and folder.is_dir() and not (tmp_path / "run" / f"{name}-tmp").exists()
+    assert remote == f"s3://bucket/run/{name}" and any(t.endswith("config.yaml") for t in uploaded)
+    cfg2 = tiny_train_config(tmp_path / "again")
+    t2 = build_trainer(cfg2, device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+    t2.restore_checkpoint(str(folder))
+    assert t2.global_step == 1
 
 
 def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
