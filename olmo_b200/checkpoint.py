@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import io
 import logging
+import os
 import pickle
 import shutil
 from abc import ABCMeta, abstractmethod
@@ -682,6 +683,85 @@ def unshard_torch_dcp_checkpoint(
     return model_state, optim_state, trainer_state
 
 
+# ------------------------------------------------------------------ the reference's ``torch_new`` layout, live
+
+
+def save_fsdp_model_and_optim_state(
+    checkpoint_dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, upload_to: Optional[str] = None, save_overwrite: bool = False,
+) -> None:
+    """Write ``checkpoint_dir/model_and_optim/`` in the layout of the reference's function of the same name
+    (``olmo/checkpoint.py:99-144``): torch's distributed-checkpoint format with ``model.<name>`` and
+    ``optim.state.<name>.<key>`` entries.  The full tensors are gathered to rank 0, which writes them (the format stores
+    global offsets and is resharded on load, so the writer's world size is not part of it)."""
+    from .checkpoint_compat import export_torch_new_checkpoint
+
+    target = Path(checkpoint_dir) / MODEL_AND_OPTIM_FOLDER
+    if get_fs_local_rank() == 0 and target.is_dir() and any(target.iterdir()):
+        if not save_overwrite:
+            raise FileExistsError(target)
+        shutil.rmtree(target, ignore_errors=True)
+    barrier()
+    gatherer = FullCheckpointer(None)  # type: ignore[arg-type]  # only its gather helpers are used; they read no settings
+    model_state = gatherer._full_model_state(dist_model)
+    optim_state = gatherer._full_optim_state(dist_model, optim)
+    if get_global_rank() == 0:
+        export_torch_new_checkpoint(checkpoint_dir, model_state, optim_state, None, world_size=0)
+        if upload_to is not None:
+            for path in sorted(target.rglob("*")):
+                if path.is_file():
+                    upload(path, f"{upload_to.rstrip('/')}/{MODEL_AND_OPTIM_FOLDER}/{path.relative_to(target)}", save_overwrite=save_overwrite)
+    del model_state, optim_state
+    barrier()
+
+
+def load_fsdp_model_and_optim_state(
+    checkpoint_dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+    load_optimizer_state: bool = True,
+) -> None:
+    """Restore model (and optimizer) in place from a ``model_and_optim/`` folder in the reference's ``torch_new`` layout,
+    whoever wrote it and at whatever world size (``olmo/checkpoint.py:147-216``)."""
+    source = local_cache if local_cache is not None and is_torch_dcp_checkpoint(local_cache) else checkpoint_dir
+    model_state, optim_state, _ = unshard_torch_dcp_checkpoint(source, load_optimizer_state=load_optimizer_state, load_trainer_state=False)
+    engine = _engine_of(dist_model)
+    if engine is not None:
+        engine.load_full_model_state_dict(model_state)
+    else:
+        _plain_module(dist_model).load_state_dict(model_state)
+    if load_optimizer_state and optim_state is not None:
+        FullCheckpointer.load_optim_state_into(dist_model, optim, FullCheckpointer._normalise_optim_state(optim_state, {}))
+    barrier()
+
+
+class TorchNewStyleShardedCheckpointer(Checkpointer):
+    """Reads *and writes* the reference's ``torch_new`` sharded layout (``olmo/checkpoint.py:892-966``): ``model_and_optim/``
+    through the two functions above plus ``train/rank{r}.pt`` per rank.  Selected by ``sharded_checkpointer: torch_new``
+    together with ``OLMO_B200_WRITE_REFERENCE_LAYOUT=1`` (otherwise that value, like the others, writes the flat-shard
+    format, which saves without gathering anything to one rank)."""
+
+    def save_checkpoint(self, dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, trainer_state: Dict[str, Any], *, upload_to: Optional[str] = None) -> None:
+        with self._temporary_wd(dir) as tmp:
+            save_fsdp_model_and_optim_state(tmp, dist_model, optim, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite)
+            save_state_dict(tmp, f"train/rank{get_global_rank()}.pt", trainer_state, upload_to=upload_to, save_overwrite=self.cfg.save_overwrite,
+                            synchronize=False)
+            self._save_config(tmp, upload_to=upload_to)
+
+    def restore_checkpoint(
+        self, load_path: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+        load_optimizer_state: bool = True,
+    ) -> Dict[str, Any]:
+        load_fsdp_model_and_optim_state(load_path, dist_model, optim, local_cache=local_cache, load_optimizer_state=load_optimizer_state)
+        try:
+            return load_state_dict(load_path, f"train/rank{get_global_rank()}.pt", local_cache=local_cache)
+        except FileNotFoundError:
+            return load_state_dict(load_path, "train/rank0.pt", local_cache=local_cache)  # written by a smaller job
+
+    def unshard_checkpoint(
+        self, load_path: PathOrStr, *, local_cache: Optional[PathOrStr] = None, load_optimizer_state: bool = True,
+        load_trainer_state: bool = True, device: Optional[torch.device] = None,
+    ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
+        return unshard_torch_dcp_checkpoint(load_path, load_optimizer_state=load_optimizer_state, load_trainer_state=load_trainer_state)
+
+
 def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckpointerType] = None, use_shared_mem_impl: bool = False) -> Checkpointer:
     """The sharded checkpointer of this framework.
 
@@ -691,5 +771,9 @@ def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckp
     reference configs load unchanged.  On the *read* side the layout of a directory is detected, and checkpoints written
     by the reference in the ``torch_new``, ``torch_legacy`` and ``local`` layouts are restored, resharded or unsharded
     (:mod:`olmo_b200.checkpoint_compat`); ``olmo_core`` directories raise an error that says what to do."""
-    del name, use_shared_mem_impl
+    del use_shared_mem_impl
+    chosen = name if name is not None else cfg.sharded_checkpointer
+    wants_reference = os.environ.get("OLMO_B200_WRITE_REFERENCE_LAYOUT", "0").strip().lower() in ("1", "true", "yes", "on")
+    if wants_reference and str(getattr(chosen, "value", chosen)) == "torch_new":
+        return TorchNewStyleShardedCheckpointer(cfg)
     return FlatShardCheckpointer(cfg)

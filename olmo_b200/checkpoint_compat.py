@@ -391,7 +391,8 @@ def export_torch_new_checkpoint(
     ``model.<parameter>`` tensors, ``optim.state.<parameter>.<key>`` tensors and the parameter groups, plus
     ``train/rank{r}.pt``.  That format records every tensor as chunks with global offsets and is resharded by its
     reader, so one writer process produces a checkpoint that a job of any world size can load with FSDP's sharded state
-    dicts; ``world_size`` only sets how many per-rank trainer-state files are written (each rank reads its own).
+    dicts; ``world_size`` only sets how many per-rank trainer-state files are written (each rank reads its own; 0: none,
+    the caller writes them).
     ``optim_state`` is keyed by parameter name (``{"state": {name: {...}}, "param_groups": [{"params": [names], ...}]}``),
     the form of an unsharded ``optim.pt``."""
     import torch.distributed.checkpoint as dcp
@@ -416,7 +417,8 @@ def export_torch_new_checkpoint(
         }
         payload["optim"] = {"state": state, "param_groups": groups}
     dcp.save(payload, storage_writer=dcp.FileSystemWriter(str(folder)), no_dist=True)
-    (out / "train").mkdir(exist_ok=True)
-    for rank in range(max(1, world_size)):
-        torch.save(trainer_state or {}, out / "train" / f"rank{rank}.pt")
+    if world_size > 0:
+        (out / "train").mkdir(exist_ok=True)
+        for rank in range(world_size):
+            torch.save(trainer_state or {}, out / "train" / f"rank{rank}.pt")
     return out

@@ -105,6 +105,24 @@ def test_checkpoint_resharding_across_world_sizes(tmp_path, checkpointer):
             torch.testing.assert_close(st[key], optim_state["state"][name][key], rtol=0, atol=0, msg=lambda m: f"{name}.{key}: {m}")
 
 
+def test_reference_torch_new_layout_is_written_by_two_ranks_and_read_by_one(tmp_path, monkeypatch):
+    """Two ranks write their sharded checkpoint in the reference's ``torch_new`` layout (full tensors gathered to rank 0,
+    one trainer-state file per rank); one rank and two ranks resume from it with the saved weights and the same next loss."""
+    from olmo_b200.checkpoint_compat import detect_layout
+
+    monkeypatch.setenv("OLMO_B200_WRITE_REFERENCE_LAYOUT", "1")
+    saved = launch(2, "save", tmp_path / "saved.pt", tmp_path / "run", "--checkpointer", "torch_new")
+    sharded = Path(saved["sharded"])
+    assert detect_layout(sharded) == "torch_new" and (sharded / "train" / "rank1.pt").is_file()
+    for nproc in (1, 2):
+        got = launch(nproc, "restore", tmp_path / f"r{nproc}.pt", tmp_path / f"w{nproc}", "--load", str(sharded), "--checkpointer", "torch_new",
+                     "--force-fsdp")
+        assert got["global_step"] == 3
+        for name, t in got["state"].items():
+            torch.testing.assert_close(t, saved["state"][name], rtol=0, atol=0, msg=lambda m: f"{nproc} ranks: {name}: {m}")
+        assert abs(got["next"][0]["loss"] - saved["next"][0]["loss"]) < 1e-4, nproc
+
+
 def test_all_ranks_agree_on_cancellation(tmp_path):
     got = launch(2, "cancel", tmp_path / "c.pt", tmp_path / "w", "--time-limit", "100")
     assert got["stopped_at"] == 1

@@ -279,6 +279,42 @@ def test_failing_upload_leaves_no_checkpoint_behind_and_a_retry_succeeds(tmp_pat
     assert t2.global_step == 1
 
 
+def test_reference_layout_can_be_written_during_training(tmp_path, monkeypatch):
+    """With ``sharded_checkpointer: torch_new`` and the opt-in switch, the trainer's sharded checkpoints are written in the
+    reference's ``torch_new`` layout, and resumed from, by the named checkpointer; without the switch the same setting
+    writes the flat-shard format."""
+    from olmo_b200.checkpoint import FlatShardCheckpointer, TorchNewStyleShardedCheckpointer, build_sharded_checkpointer
+    from olmo_b200.checkpoint_compat import detect_layout
+    from olmo_b200.config import CheckpointType, ShardedCheckpointerType
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "run")
+    cfg.sharded_checkpointer = ShardedCheckpointerType.torch_new
+    assert isinstance(build_sharded_checkpointer(cfg), FlatShardCheckpointer)
+    monkeypatch.setenv("OLMO_B200_WRITE_REFERENCE_LAYOUT", "1")
+    assert isinstance(build_sharded_checkpointer(cfg), TorchNewStyleShardedCheckpointer)
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    batches = iter(trainer.train_loader)
+    for _ in range(2):
+        trainer.global_step += 1
+        trainer.train_step(next(batches))
+    folder, _ = trainer.save_checkpoint(CheckpointType.sharded)
+    assert detect_layout(folder) == "torch_new" and (Path(folder) / "train" / "rank0.pt").is_file() and (Path(folder) / "config.yaml").is_file()
+    named = dict(trainer.dist_model.engine.named_parameters_for_optimizer())
+    cfg2 = tiny_train_config(tmp_path / "again")
+    cfg2.sharded_checkpointer = ShardedCheckpointerType.torch_new
+    t2 = build_trainer(cfg2, device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+    t2.restore_checkpoint(str(folder))
+    assert t2.global_step == 2
+    for n, p in t2.dist_model.engine.named_parameters_for_optimizer():
+        assert torch.equal(p.detach(), named[n].detach()), n
+        assert torch.equal(t2.optim.state[p]["exp_avg_sq"], trainer.optim.state[named[n]]["exp_avg_sq"]), n
+    monkeypatch.delenv("OLMO_B200_WRITE_REFERENCE_LAYOUT")
+    t3 = build_trainer(tiny_train_config(tmp_path / "third"), device=torch.device("cpu"), train_loader=make_loader(cfg2), with_evaluators=False)
+    t3.restore_checkpoint(str(folder))  # the flat-shard checkpointer detects the foreign layout
+    assert t3.global_step == 2
+
+
 def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
     """``rank{r}.pt`` files holding ``ShardedTensor`` pickles (the reference's default sharded layout,
     ``olmo/checkpoint.py:969-1453``), written here by two gloo ranks from a trainer's full state, are detected by
