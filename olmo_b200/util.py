@@ -43,6 +43,9 @@ __all__ = [
     "log_extra_field",
     "setup_logging",
     "install_excepthook",
+    "excepthook",
+    "get_progress_bar",
+    "save_hf_dataset_to_disk",
     "filter_warnings",
     "set_env_variables",
     "prepare_cli_environment",
@@ -194,7 +197,9 @@ def _rich_handler() -> logging.Handler:
     return _Handler()
 
 
-def _excepthook(exctype, value, traceback) -> None:
+def excepthook(exctype, value, traceback) -> None:
+    """``sys.excepthook`` replacement: command-line mistakes print one line, everything else is logged with its traceback
+    (so that it reaches the log handlers of every rank), Ctrl-C keeps Python's own behaviour."""
     if issubclass(exctype, KeyboardInterrupt):
         sys.__excepthook__(exctype, value, traceback)
     elif issubclass(exctype, OLMoCliError):
@@ -205,8 +210,20 @@ def _excepthook(exctype, value, traceback) -> None:
         log.critical("Uncaught %s: %s", exctype.__name__, value, exc_info=(exctype, value, traceback))
 
 
+_excepthook = excepthook  # earlier name
+
+
 def install_excepthook() -> None:
-    sys.excepthook = _excepthook
+    sys.excepthook = excepthook
+
+
+def get_progress_bar():
+    """A ``rich`` progress display for transfers (description, bar, bytes done, rate, time left), as used while
+    checkpoint files are fetched (``resource_path(..., progress=...)``)."""
+    from rich.progress import BarColumn, DownloadColumn, Progress, TextColumn, TimeRemainingColumn, TransferSpeedColumn
+
+    return Progress(TextColumn("[progress.description]{task.description}"), BarColumn(), DownloadColumn(), TransferSpeedColumn(),
+                    TimeRemainingColumn(), transient=True)
 
 
 def filter_warnings() -> None:
@@ -792,6 +809,16 @@ def load_hf_dataset(path: str, name: Optional[str], split: str):
         return datasets.load_from_disk(str(get_data_path(rel)))
     except FileNotFoundError as e:
         raise FileNotFoundError(f"HF dataset {path} name {name} split {split} not found under {rel}") from e
+
+
+def save_hf_dataset_to_disk(dataset, hf_path: str, name: Optional[str], split: str, datasets_dir: PathOrStr) -> Path:
+    """Store a ``datasets`` dataset where :func:`load_hf_dataset` looks for it: ``datasets_dir/<hf_path>/<name or "none">/<split>``
+    (``datasets_dir`` is ``olmo_data/hf_datasets`` to add an evaluation set to the package data, or the ``hf_datasets`` folder
+    of an ``OLMO_DATA_DIR`` tree).  Returns the folder."""
+    target = Path(datasets_dir) / hf_path / (name or "none") / split
+    target.parent.mkdir(parents=True, exist_ok=True)
+    dataset.save_to_disk(str(target))
+    return target
 
 
 def load_oe_eval_requests(path: str, name: Optional[str] = None, split: Optional[str] = None):

@@ -192,3 +192,20 @@ def test_olmo_data_package_locates_files(tmp_path, monkeypatch):
     with pytest.raises(FileNotFoundError):
         with get_data_path("hf_datasets/none"):
             pass
+
+
+def test_dataset_saver_writes_where_the_loader_looks_and_hooks_are_public(tmp_path, monkeypatch, capsys):
+    datasets = pytest.importorskip("datasets")
+    from olmo_b200.exceptions import OLMoCliError
+
+    ds = datasets.Dataset.from_dict({"question": ["a", "b"], "label": [0, 1]})
+    folder = util.save_hf_dataset_to_disk(ds, "toy/set", None, "validation", tmp_path / "hf_datasets")
+    assert folder == tmp_path / "hf_datasets" / "toy" / "set" / "none" / "validation"
+    monkeypatch.setenv("OLMO_DATA_DIR", str(tmp_path))
+    assert list(util.load_hf_dataset("toy/set", None, "validation")["question"]) == ["a", "b"]
+    util.excepthook(OLMoCliError, OLMoCliError("bad flag"), None)
+    assert "bad flag" in capsys.readouterr().err
+    bar = util.get_progress_bar()
+    task = bar.add_task("fetch", total=10)
+    bar.update(task, advance=10)
+    assert bar.tasks[0].finished
