@@ -1,6 +1,7 @@
 """HuggingFace interoperability: auto classes, save/load round trip, and exact agreement between this model and the
 architectures that ship inside ``transformers`` after conversion (an independent implementation of the same maths)."""
 import json
+from pathlib import Path
 
 import pytest
 import torch
@@ -164,3 +165,62 @@ def test_text_generation_pipeline_with_converted_checkpoint_and_tokenizer(tmp_pa
     with torch.no_grad():
         first = int(model(torch.tensor([ids])).logits[0, -1].argmax())
     assert words[3] == {v: k for k, v in vocab.items()}[first]
+
+
+def test_hf_olmo_converter_steps_local_and_remote(tmp_path):
+    """The converter command: into another folder (source untouched), in place, from and to a remote store; and the
+    reference's module paths resolve."""
+    import importlib
+
+    from hf_olmo import convert_olmo_to_hf as conv
+    from olmo_b200 import util
+
+    for mod, name in (("configuration_olmo", "OLMoConfig"), ("modeling_olmo", "OLMoForCausalLM"), ("tokenization_olmo_fast", "OLMoTokenizerFast")):
+        assert getattr(importlib.import_module(f"hf_olmo.{mod}"), name) is getattr(hf_olmo, name)
+    assert conv.longest_common_prefix(["s3://b/run/step1/model.pt", "s3://b/run/step1/config.yaml"]) == "s3://b/run/step1/"
+    assert conv.longest_common_prefix([]) == "" and conv.longest_common_prefix(["abc"]) == "abc"
+
+    model = native(OLMO2)
+    src = save_unsharded(model, tmp_path / "ckpt")
+    (src / "optim.pt").write_bytes(b"x")
+    ids = torch.randint(0, 118, (2, 9))
+
+    out = tmp_path / "converted"
+    conv.main(["--checkpoint-dir", str(src), "--destination-dir", str(out)])
+    assert sorted(p.name for p in out.iterdir()) == ["config.json", "pytorch_model.bin"]  # no tokenizer: the configured file is missing
+    assert (src / "model.pt").is_file() and (src / "optim.pt").is_file() and not (src / "config.json").exists()
+    loaded = transformers.AutoModelForCausalLM.from_pretrained(str(out), torch_dtype=torch.float32).eval()
+    with torch.no_grad():
+        torch.testing.assert_close(loaded(ids).logits, model(ids).logits)
+
+    inplace = save_unsharded(model, tmp_path / "inplace")
+    conv.main(["--checkpoint-dir", str(inplace), "--keep-olmo-artifacts", "--safetensors"])
+    assert {"config.json", "model.safetensors", "config.yaml", "model.pt"} <= {p.name for p in inplace.iterdir()}
+
+    class Store(util.StorageBackend):
+        def __init__(self):
+            self.blobs = {}
+
+        def file_size(self, url):
+            return len(self.blobs[url])
+
+        def get_bytes_range(self, url, start, num):
+            return self.blobs[url][start : start + num]
+
+        def upload(self, source, url, save_overwrite=False):
+            self.blobs[url] = Path(source).read_bytes()
+
+        def list_files(self, url):
+            return sorted(k for k in self.blobs if k.startswith(url.rstrip("/") + "/"))
+
+    store = Store()
+    util.register_storage_backend("mem", store)
+    try:
+        for p in src.iterdir():
+            store.blobs[f"mem://bucket/run/step5-unsharded/{p.name}"] = p.read_bytes()
+        conv.main(["--checkpoint-dir", "mem://bucket/run/step5-unsharded", "--destination-dir", "mem://bucket/hf/step5"])
+        names = sorted(k.rsplit("/", 1)[1] for k in store.blobs if k.startswith("mem://bucket/hf/step5/"))
+        assert names == ["config.json", "pytorch_model.bin"]
+        assert "mem://bucket/run/step5-unsharded/model.pt" in store.blobs  # the source is left alone
+    finally:
+        util._BACKENDS.pop("mem", None)
