@@ -175,8 +175,11 @@ def to_transformers_state_dict(state: Dict[str, torch.Tensor], cfg: ModelConfig)
 
 def write_transformers_checkpoint(
     checkpoint_dir: PathOrStr, out_dir: PathOrStr, *, tokenizer_path: Optional[PathOrStr] = None, dtype: Optional[torch.dtype] = None,
+    include_tokenizer: bool = True, safe_serialization: bool = True, fix_eos_token_id: bool = True,
 ) -> Tuple[Path, str]:
-    """Convert an unsharded checkpoint for the in-library architecture; returns ``(out_dir, model_type)``."""
+    """Convert an unsharded checkpoint for the in-library architecture; returns ``(out_dir, model_type)``.
+    ``fix_eos_token_id``: configs of early OLMo-1 runs carry ``eos_token_id: 0`` although their tokenizer ends documents
+    with 50279; the exported files then say 50279 (the reference's converters apply the same correction)."""
     from safetensors.torch import save_file
 
     src, dst = Path(checkpoint_dir), Path(out_dir)
@@ -190,13 +193,21 @@ def write_transformers_checkpoint(
     config["torch_dtype"] = str(next(iter(state.values())).dtype).replace("torch.", "")
     if cfg.weight_tying:
         state.pop("lm_head.weight")
+    eos = cfg.eos_token_id
+    if fix_eos_token_id and eos == 0:
+        eos = 50279
+        config["eos_token_id"] = eos
     (dst / "config.json").write_text(json.dumps(config, indent=2) + "\n")
-    save_file({k: v.contiguous() for k, v in state.items()}, str(dst / "model.safetensors"), metadata={"format": "pt"})
-    (dst / "generation_config.json").write_text(
-        json.dumps({"_from_model_config": True, "eos_token_id": cfg.eos_token_id, "pad_token_id": cfg.pad_token_id}, indent=2) + "\n"
-    )
-    if tokenizer_path is not None and Path(tokenizer_path).is_file():
-        shutil.copyfile(tokenizer_path, dst / "tokenizer.json")
+    if safe_serialization:
+        save_file({k: v.contiguous() for k, v in state.items()}, str(dst / "model.safetensors"), metadata={"format": "pt"})
     else:
-        _copy_tokenizer(train_config, dst, None)
+        torch.save({k: v.contiguous() for k, v in state.items()}, dst / "pytorch_model.bin")
+    (dst / "generation_config.json").write_text(
+        json.dumps({"_from_model_config": True, "eos_token_id": eos, "pad_token_id": cfg.pad_token_id}, indent=2) + "\n"
+    )
+    if include_tokenizer:
+        if tokenizer_path is not None and Path(tokenizer_path).is_file():
+            shutil.copyfile(tokenizer_path, dst / "tokenizer.json")
+        else:
+            _copy_tokenizer(train_config, dst, None)
     return dst, config["model_type"]

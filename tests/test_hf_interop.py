@@ -224,3 +224,14 @@ def test_hf_olmo_converter_steps_local_and_remote(tmp_path):
         assert "mem://bucket/run/step5-unsharded/model.pt" in store.blobs  # the source is left alone
     finally:
         util._BACKENDS.pop("mem", None)
+
+
+def test_transformers_export_options(tmp_path):
+    model = native({**OLMO1, "eos_token_id": 0})
+    src = save_unsharded(model, tmp_path / "ckpt")
+    fixed, _ = write_transformers_checkpoint(src, tmp_path / "fixed", include_tokenizer=False, safe_serialization=False)
+    assert json.loads((fixed / "config.json").read_text())["eos_token_id"] == 50279
+    assert json.loads((fixed / "generation_config.json").read_text())["eos_token_id"] == 50279
+    assert (fixed / "pytorch_model.bin").is_file() and not (fixed / "model.safetensors").exists() and not (fixed / "tokenizer.json").exists()
+    kept, _ = write_transformers_checkpoint(src, tmp_path / "kept", fix_eos_token_id=False)
+    assert json.loads((kept / "config.json").read_text())["eos_token_id"] == 0 and (kept / "model.safetensors").is_file()
