@@ -315,6 +315,41 @@ def test_reference_layout_can_be_written_during_training(tmp_path, monkeypatch):
     assert t3.global_step == 2
 
 
+def test_unshard_and_convert_pipeline_runs_stage_by_stage(tmp_path):
+    """``scripts/s3_unshard_to_hf.py`` on local "buckets": fetch, unshard, convert, upload; a second call picks up from the
+    unsharded stage; the converted weights load in ``transformers`` and reproduce the trainer's logits."""
+    import importlib.util
+
+    import transformers
+
+    from olmo_b200.config import CheckpointType
+
+    torch.manual_seed(0)
+    cfg = tiny_train_config(tmp_path / "run")
+    trainer = build_trainer(cfg, device=torch.device("cpu"), train_loader=make_loader(cfg), with_evaluators=False)
+    trainer.global_step = 1
+    trainer.train_step(next(iter(trainer.train_loader)))
+    sharded, _ = trainer.save_checkpoint(CheckpointType.sharded)
+    spec = importlib.util.spec_from_file_location("s3_unshard_to_hf", str(Path(__file__).resolve().parent.parent / "scripts" / "s3_unshard_to_hf.py"))
+    tool = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(tool)
+    work = tmp_path / "work"
+    tool.main(["--sharded_bucket", str(sharded), "--unsharded_bucket", str(tmp_path / "bucket" / "unsharded"), "--hf_bucket", str(tmp_path / "bucket" / "hf"),
+               "--local_dir", str(work), "--checkpoint_style", "transformers", "--model_only", "--quiet"])
+    assert (work / "sharded" / "metadata.yaml").is_file() and (work / "unsharded" / "model.pt").is_file()
+    assert (tmp_path / "bucket" / "unsharded" / "model.pt").is_file() and (tmp_path / "bucket" / "hf" / "config.json").is_file()
+    hf = transformers.AutoModelForCausalLM.from_pretrained(str(tmp_path / "bucket" / "hf"), torch_dtype=torch.float32, attn_implementation="eager").eval()
+    ids = torch.randint(0, cfg.model.vocab_size - 1, (1, 12))
+    with torch.no_grad():
+        want = trainer.model(ids).logits
+        torch.testing.assert_close(hf(ids).logits[..., : want.shape[-1]], want[..., : hf.config.vocab_size], rtol=1e-4, atol=1e-4)
+    shutil_target = tmp_path / "bucket" / "hf2"
+    tool.main(["--already_unsharded", "--hf_bucket", str(shutil_target), "--local_dir", str(work), "--hf_olmo", "--cleanup_local_dir", "--quiet"])
+    assert (shutil_target / "config.json").is_file() and not work.exists()
+    with pytest.raises(SystemExit):
+        tool.main(["--hf_bucket", str(tmp_path / "x")])
+
+
 def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
     """``rank{r}.pt`` files holding ``ShardedTensor`` pickles (the reference's default sharded layout,
     ``olmo/checkpoint.py:969-1453``), written here by two gloo ranks from a trainer's full state, are detected by
