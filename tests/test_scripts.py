@@ -146,6 +146,17 @@ def test_run_dataloader_and_inspect_agree(tiny_run, capsys):
     for row in first[0]:
         assert str(row.tolist()) in printed
 
+    # anchored at a checkpoint's trainer state: step 3 follows the two batches the checkpoint of step 2 had consumed
+    (run / "step2" / "train").mkdir(parents=True)
+    torch.save({"global_step": 2, "epoch": 0, "global_train_examples_seen_this_epoch": 8}, run / "step2" / "train" / "rank0.pt")
+    inspect.main([str(run), "1", "3", "--world_size", "2", "--no_data_indices", "--ids", "--checkpoint_num", "2"])
+    printed = capsys.readouterr().out
+    for row in first[2]:
+        assert str(row.tolist()) in printed
+    with pytest.raises(SystemExit):
+        inspect.main([str(run), "1", "2", "--world_size", "2", "--no_data_indices", "--ids", "--checkpoint_num", "2"])
+    assert inspect.remount(["/weka/data/a.npy", "/other/b.npy"], [["weka://", "/weka/"]]) == ["weka://data/a.npy", "/other/b.npy"]
+
 
 def test_ladder_power_laws_and_node_counts():
     from olmo_b200.ladder import batch_size_for, ladder_config, learning_rate_for, node_counts, parse_length, parse_size, size_for_model
