@@ -3,6 +3,10 @@
 and report where they first diverge (reference: ``scripts/compare_module_outputs.py``).
 
     python scripts/compare_module_outputs.py RUN_A/traces/step1 RUN_B/traces/step1 [--rtol 1e-3] [--verbose]
+                                             [--include_non_tensor_outputs]
+
+Dumps whose content is not made of tensors (for example an attention layer's cache entry of ``None``) are skipped unless
+``--include_non_tensor_outputs``, with which they are compared for equality.
 """
 import argparse
 import re
@@ -35,6 +39,7 @@ def main() -> int:
     ap.add_argument("compare")
     ap.add_argument("--rtol", type=float, default=1e-3)
     ap.add_argument("--verbose", action="store_true")
+    ap.add_argument("--include_non_tensor_outputs", action="store_true", help="also compare dumps that hold no tensors, by equality")
     args = ap.parse_args()
     a_dir, b_dir = Path(args.base), Path(args.compare)
     a_files = {p.name: p for p in a_dir.glob("*.pt")}
@@ -43,9 +48,18 @@ def main() -> int:
         print(f"only in {'base' if name in a_files else 'compare'}: {name}")
     first_bad = None
     for name in sorted(set(a_files) & set(b_files), key=lambda n: order_key(a_files[n])):
-        xa = list(tensors(torch.load(a_files[name], map_location="cpu", weights_only=False)))
-        xb = list(tensors(torch.load(b_files[name], map_location="cpu", weights_only=False)))
-        worst = 0.0
+        raw_a = torch.load(a_files[name], map_location="cpu", weights_only=False)
+        raw_b = torch.load(b_files[name], map_location="cpu", weights_only=False)
+        xa, xb = list(tensors(raw_a)), list(tensors(raw_b))
+        if not xa and not xb:
+            if args.include_non_tensor_outputs:
+                same = raw_a == raw_b
+                if not same and first_bad is None:
+                    first_bad = name
+                if not same or args.verbose:
+                    print(f"{'ok  ' if same else 'DIFF'} {name}: {raw_a!r} vs {raw_b!r}")
+            continue
+        worst = 0.0 if len(xa) == len(xb) else float("inf")
         for x, y in zip(xa, xb):
             if x.shape != y.shape:
                 worst = float("inf")

@@ -402,3 +402,24 @@ def test_model_size_breakdown_and_config_starter(tmp_path):
 
     with pytest.raises(OLMoCliError):
         starter.main(tmp_path / "x.yaml", [], recipe="no-such-recipe")
+
+
+def test_split_gz_by_size_and_by_lines(tmp_path):
+    split = load_script("split_gz")
+    src = tmp_path / "in"
+    src.mkdir()
+    for name, n in (("a.json.gz", 10), ("b.json.gz", 3)):
+        with gzip.open(src / name, "wt") as f:
+            for i in range(n):
+                f.write(json.dumps({"i": i, "pad": "x" * 20}) + "\n")
+    (src / "notes.txt").write_text("skip me")
+    line = len(json.dumps({"i": 0, "pad": "x" * 20}) + "\n")
+    written = split.split_directory(str(src), str(tmp_path / "out"), ".json.gz", ".jsonl.gz", size_limit=4 * line, workers=1)
+    assert [Path(p).name for p in written] == ["a_0000.jsonl.gz", "a_0001.jsonl.gz", "a_0002.jsonl.gz", "b_0000.jsonl.gz"]
+    back = []
+    for p in written[:3]:
+        with gzip.open(p, "rt") as f:
+            back += [json.loads(x)["i"] for x in f]
+    assert back == list(range(10))
+    assert split.main(["--input_dir", str(src), "--output_dir", str(tmp_path / "out2"), "--input_ext", ".json.gz", "--lines", "5"]) == 3
+    assert split.main([str(src / "a.json.gz"), str(tmp_path / "single"), "--lines", "4"]) == 3 and (tmp_path / "single_0002.json.gz").is_file()
