@@ -328,13 +328,14 @@ def main(argv=None) -> int:
     g = p.add_mutually_exclusive_group()
     g.add_argument("--ignore-non-runs", action="store_true", default=True, help="skip entries that do not look like runs (default)")
     g.add_argument("--fail-on-non-runs", dest="ignore_non_runs", action="store_false", help="stop at the first entry that does not look like a run")
-    g.add_argument("--skip-run-verification", action="store_true", help="(unsafe) treat every entry as a run")
+    g.add_argument("--skip-run-verification", "--bypass_run_verification", dest="skip_run_verification", action="store_true",
+                   help="(unsafe) treat every entry as a run")
     p.add_argument("--max-archive-size", type=int, default=None, help="archives larger than this many bytes are left alone")
     p.add_argument("--dry-run", action="store_true")
     p = sub.add_parser("unshard", help="unshard the checkpoints of a run")
     p.add_argument("run", help="run folder, run archive or remote prefix")
     p.add_argument("dest", nargs="?", default=None, help="where the unsharded checkpoints go (default: next to the sharded ones)")
-    p.add_argument("--latest-only", action="store_true", help="only the newest sharded checkpoint")
+    p.add_argument("--latest-only", "--latest_checkpoint_only", dest="latest_only", action="store_true", help="only the newest sharded checkpoint")
     p.add_argument("--checkpoint-num", type=int, default=None, help="only the checkpoint of this step")
     p.add_argument("--delete-sharded", action="store_true", help="remove a sharded checkpoint once it has been unsharded")
     p.add_argument("--safe-tensors", action="store_true")
@@ -345,7 +346,8 @@ def main(argv=None) -> int:
     p.add_argument("--entry", default=None, help="only this folder or file of the run, e.g. step0-unsharded")
     p.add_argument("--keep-src", action="store_true", default=True, help="leave the source in place (default)")
     p.add_argument("--remove-src", dest="keep_src", action="store_false", help="delete the source after the copy")
-    p.add_argument("--store-unarchived", action="store_true", help="an archived run is stored unpacked at the destination")
+    p.add_argument("--store-unarchived", "--unarchive", dest="store_unarchived", action="store_true",
+                   help="an archived run is stored unpacked at the destination")
     p.add_argument("--append-wandb-path", action="store_true", help="append entity/project/group/name from the run's config to DST")
     p.add_argument("--dry-run", action="store_true")
     args = ap.parse_args(argv)

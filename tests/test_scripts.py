@@ -423,3 +423,52 @@ def test_split_gz_by_size_and_by_lines(tmp_path):
     assert back == list(range(10))
     assert split.main(["--input_dir", str(src), "--output_dir", str(tmp_path / "out2"), "--input_ext", ".json.gz", "--lines", "5"]) == 3
     assert split.main([str(src / "a.json.gz"), str(tmp_path / "single"), "--lines", "4"]) == 3 and (tmp_path / "single_0002.json.gz").is_file()
+
+
+def _token_dir(root, name, sizes):
+    d = root / name
+    d.mkdir(parents=True)
+    for i, n in enumerate(sizes):
+        np.zeros(n, dtype=np.uint32).tofile(d / f"part-{i:02d}.npy")
+    (d / "notes.txt").write_text("ignored")
+    return str(d)
+
+
+def test_mix_builder_and_config_makers(tmp_path, capsys):
+    from olmo_b200.config import TrainConfig
+    from olmo_b200.data import mix_builder as mb
+
+    web = _token_dir(tmp_path, "web", [1000] * 10)      # 10 k tokens
+    math = _token_dir(tmp_path, "math", [500, 700, 300])  # 1.5 k tokens
+    assert mb.parse_source("s3://b/x/=0.25") == mb.Source("s3://b/x/", fraction=0.25)
+    assert mb.parse_source("s3://b/x/=2B").tokens == 2e9 and mb.parse_source("/d/x=x2").repeat == 2 and mb.parse_source("s3://b/k=v/").prefix == "s3://b/k=v/"
+    with pytest.raises(ValueError):
+        mb.Source("x", fraction=1.5)
+    paths, rows = mb.build_mix([f"{web}=0.3", math, f"{math}=x2", f"{web}=2500"], seed=3)
+    assert [r["files"] for r in rows] == [3, 3, 6, 3] and [r["tokens"] for r in rows] == [3000, 1500, 3000, 3000]
+    assert rows[0]["available"] == 10000 and abs(sum(r["share"] for r in rows) - 1) < 1e-9
+    again, _ = mb.build_mix([f"{web}=0.3", math, f"{math}=x2", f"{web}=2500"], seed=3)
+    other, _ = mb.build_mix([f"{web}=0.3"], seed=4)
+    assert again == paths and all(p.endswith(".npy") for p in paths) and other != paths[:3]
+    with pytest.raises(ValueError, match="repeat"):
+        mb.build_mix([f"{math}=5000"])
+    with pytest.raises(FileNotFoundError):
+        mb.build_mix([str(tmp_path / "nothing")])
+    table = mb.examine(paths)
+    assert {Path(r["source"]).name: r["tokens"] for r in table} == {"web": 6000, "math": 4500}
+    assert mb.human_count(1.5e9) == "1.50B" and mb.human_count(12) == "12"
+
+    micro = load_script("microanneal_config_maker")
+    out = tmp_path / "micro.yaml"
+    micro.main(["--name", "candidate", "-o", str(out), "--source", math, "--source", f"{web}=0.2"])
+    cfg = TrainConfig.load(out, validate_paths=False)
+    assert len(cfg.data.paths) == 5 and cfg.seed == 7201 and cfg.max_duration == "3500T" and cfg.optimizer.learning_rate == pytest.approx(6.1499e-05)
+    assert cfg.scheduler.alpha_f == 0.0 and cfg.restore_dataloader is False and cfg.model.d_model == 4096
+    capsys.readouterr()
+    micro.main(["--examine", str(out)])
+    printed = capsys.readouterr().out
+    assert "math" in printed and "web" in printed and "total" in printed
+    big = load_script("peteish7_config_maker")
+    big.main(["--name", "anneal", "--tokens", "50e9", "-o", str(tmp_path / "anneal.yaml"), "--source", web])
+    cfg = TrainConfig.load(tmp_path / "anneal.yaml", validate_paths=False)
+    assert cfg.stop_at == 11931 and cfg.seed == 42 and len(cfg.data.paths) == 10
