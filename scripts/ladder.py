@@ -20,11 +20,29 @@ from olmo_b200.util import flatten_dict
 
 def config_from_args(args) -> "TrainConfig":  # noqa: F821
     return ladder_config(
-        args.model, args.length, args.name, getattr(args, "data", None), read_location=args.read_location or "/data",
-        remote_save_folder=(args.write_location.rstrip("/") + f"/{args.name}-{args.model.upper()}-{args.length}") if getattr(args, "write_location", None) else None,
+        args.model, args.length, args.name, getattr(args, "data", None), read_location=_read_location(args),
+        remote_save_folder=(_write_location(args).rstrip("/") + f"/{args.name}-{args.model.upper()}-{args.length}") if _write_location(args) else None,
         load_path=getattr(args, "load_path", None), wandb=getattr(args, "wandb", False), save_overwrite=getattr(args, "save_overwrite", False),
         eval_on_load=getattr(args, "eval_on_load", False),
     )
+
+
+def _read_location(args) -> str:
+    """``--read_location`` wins; ``--s3`` reads from the bucket named by ``OLMO_S3_DATA_ROOT`` (the reference hard-codes its
+    own bucket there); otherwise the local data root."""
+    if getattr(args, "read_location", None):
+        return args.read_location
+    if getattr(args, "s3", False):
+        return os.environ.get("OLMO_S3_DATA_ROOT", "s3://ai2-llm")
+    return "/data"
+
+
+def _write_location(args):
+    if getattr(args, "write_location", None):
+        return args.write_location
+    if getattr(args, "s3", False):
+        return os.environ.get("OLMO_S3_CHECKPOINT_ROOT", "s3://ai2-llm/checkpoints/OLMo-ladder")
+    return None
 
 
 def nodecounts_cmd(args) -> None:
@@ -82,6 +100,7 @@ if __name__ == "__main__":
         p.add_argument("--length", default="2xC")
         p.add_argument("--name", required=True)
         p.add_argument("--wandb", action=argparse.BooleanOptionalAction, default=False)
+        p.add_argument("--s3", action=argparse.BooleanOptionalAction, default=False, help="read data from and write checkpoints to object storage")
         p.add_argument("--read_location", default=None)
         p.add_argument("--write_location", default=None)
         p.add_argument("--save_overwrite", action="store_true")

@@ -13,10 +13,11 @@ import concurrent.futures
 import gzip
 import json
 import logging
+import os
 import random
 import sys
 from pathlib import Path
-from typing import Iterator, List, Sequence, Tuple
+from typing import Iterator, List, Optional, Sequence, Tuple
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
@@ -25,20 +26,58 @@ import numpy as np
 log = logging.getLogger("prepare_memmap_dataset")
 
 
-def list_sources(prefixes: Sequence[str]) -> List[Path]:
-    out: List[Path] = []
+_DOC_SUFFIXES = ("gz", "json", "jsonl")
+
+#: where remote sources are copied before they are read (``--cache-dir``; a temporary folder when unset)
+_CACHE_DIR: Optional[str] = None
+
+
+def list_sources(prefixes: Sequence[str]) -> List[str]:
+    """Document files below local folders or remote prefixes (any storage scheme the framework knows)."""
+    from olmo_b200.util import is_url, list_files
+
+    out: List[str] = []
     for prefix in prefixes:
+        if is_url(prefix):
+            found = [u for u in list_files(prefix) if u.rsplit(".", 1)[-1] in _DOC_SUFFIXES]
+            if not found:
+                found = [prefix]  # a single remote file
+            out.extend(found)
+            continue
         p = Path(prefix)
         if p.is_dir():
-            out.extend(sorted(q for q in p.rglob("*") if q.is_file() and q.name.split(".")[-1] in ("gz", "json", "jsonl")))
+            out.extend(sorted(str(q) for q in p.rglob("*") if q.is_file() and q.name.split(".")[-1] in _DOC_SUFFIXES))
         elif p.is_file():
-            out.append(p)
+            out.append(str(p))
         else:
             raise FileNotFoundError(prefix)
     return out
 
 
-def read_documents(path: Path) -> Iterator[str]:
+def local_copy(source: str) -> Path:
+    """The file itself when it is local; otherwise a copy in the cache folder (kept, so a rerun does not fetch it again)."""
+    from olmo_b200.util import file_size, get_bytes_range, is_url
+
+    if not is_url(source):
+        return Path(source)
+    import hashlib
+    import tempfile
+
+    root = Path(_CACHE_DIR or tempfile.gettempdir()) / "prepare_memmap_cache"
+    root.mkdir(parents=True, exist_ok=True)
+    target = root / (hashlib.sha256(source.encode()).hexdigest()[:16] + "-" + source.rstrip("/").rsplit("/", 1)[-1])
+    size = file_size(source)
+    if not target.is_file() or target.stat().st_size != size:
+        tmp = target.with_suffix(target.suffix + f".part{os.getpid()}")
+        with open(tmp, "wb") as f:
+            for off in range(0, size, 64 << 20):
+                f.write(get_bytes_range(source, off, min(64 << 20, size - off)))
+        os.replace(tmp, target)
+    return target
+
+
+def read_documents(path) -> Iterator[str]:
+    path = local_copy(str(path))
     opener = gzip.open if path.suffix == ".gz" else open
     with opener(path, "rt", encoding="utf-8") as f:
         for line in f:
@@ -80,8 +119,9 @@ class MemmapWriter:
         return self.used
 
 
-def fill(job: Tuple[List[str], str, str, str, int, float, int, int, object]) -> int:
-    sources, out_stem, tokenizer_id, dtype_str, max_tokens, sample_rate, seed, repeat, eos = job
+def fill(job: Tuple[List[str], str, str, str, int, float, int, int, object, Optional[str]]) -> int:
+    global _CACHE_DIR
+    sources, out_stem, tokenizer_id, dtype_str, max_tokens, sample_rate, seed, repeat, eos, _CACHE_DIR = job
     tok = load_tokenizer(tokenizer_id, eos)
     dtype = np.dtype(dtype_str)
     limit = np.iinfo(dtype).max
@@ -89,7 +129,7 @@ def fill(job: Tuple[List[str], str, str, str, int, float, int, int, object]) -> 
     part, total = 0, 0
     writer = MemmapWriter(Path(f"{out_stem}_{part:05d}.npy"), dtype, max_tokens)
     for src in sources:
-        for text in read_documents(Path(src)):
+        for text in read_documents(src):
             if sample_rate < 1.0 and rng.random() > sample_rate:
                 continue
             ids = tok.encode(text, add_special_tokens=True)
@@ -122,7 +162,11 @@ def main(argv=None) -> int:
     ap.add_argument("--workers", "--max-workers", dest="workers", type=int, default=1)
     ap.add_argument("--validate", action="store_true")
     ap.add_argument("--ack-deprecated", action="store_true", help="accepted for command-line compatibility")
+    ap.add_argument("--cache-dir", default=None, help="where remote source files are copied before they are read (kept for reruns)")
+    ap.add_argument("--safe-mode", action="store_true", help="accepted for compatibility: remote files are always copied before they are read")
     args = ap.parse_args(argv)
+    global _CACHE_DIR
+    _CACHE_DIR = args.cache_dir
     logging.basicConfig(level=logging.INFO)
 
     sources = list_sources(args.src)
@@ -131,7 +175,7 @@ def main(argv=None) -> int:
     out = Path(args.output)
     jobs = [
         ([str(s) for s in group], str(out / f"part-{i:03d}"), args.tokenizer, args.dtype, args.max_tokens, args.sample_rate,
-         args.random_seed + i, args.repeat_sequence, args.eos_token_id)
+         args.random_seed + i, args.repeat_sequence, args.eos_token_id, args.cache_dir)
         for i, group in enumerate(groups)
     ]
     if args.workers <= 1 or len(jobs) == 1:

@@ -65,13 +65,20 @@ def main(argv=None) -> int:
     ap.add_argument("-s", "--seq-len", type=int, default=2048)
     ap.add_argument("--eos", type=int, default=50279)
     ap.add_argument("--pad", type=int, default=1)
+    ap.add_argument("-j", "--num-proc", type=int, default=1, help="worker threads that render and tokenise conversations")
     args = ap.parse_args(argv)
     logging.basicConfig(level=logging.INFO)
     from olmo_b200.tokenizer import Tokenizer
 
     kwargs = dict(eos_token_id=args.eos, pad_token_id=args.pad)
     tok = Tokenizer.from_file(args.tokenizer, **kwargs) if Path(args.tokenizer).is_file() else Tokenizer.from_pretrained(args.tokenizer, **kwargs)
-    rows = [r for r in (render(m, tok, args.seq_len) for m in conversations(args.source))]
+    if args.num_proc > 1:  # the tokenizer library releases the interpreter lock while it encodes
+        from concurrent.futures import ThreadPoolExecutor
+
+        with ThreadPoolExecutor(max_workers=args.num_proc) as pool:
+            rows = list(pool.map(lambda m: render(m, tok, args.seq_len), conversations(args.source)))
+    else:
+        rows = [render(m, tok, args.seq_len) for m in conversations(args.source)]
     kept = [r for r in rows if r["n_labels"] > 0]
     log.info("kept %d of %d conversations", len(kept), len(rows))
     out = Path(args.output_dir)

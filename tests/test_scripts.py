@@ -472,3 +472,53 @@ def test_mix_builder_and_config_makers(tmp_path, capsys):
     big.main(["--name", "anneal", "--tokens", "50e9", "-o", str(tmp_path / "anneal.yaml"), "--source", web])
     cfg = TrainConfig.load(tmp_path / "anneal.yaml", validate_paths=False)
     assert cfg.stop_at == 11931 and cfg.seed == 42 and len(cfg.data.paths) == 10
+
+
+def test_memmap_preparation_reads_remote_sources_through_a_cache(tmp_path):
+    """Documents listed under a remote prefix are copied into the cache folder once and tokenised from there."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    from olmo_b200 import util
+
+    vocab = {f"w{i}": i for i in range(20)}
+    vocab["<eos>"] = 20
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="w0"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.save(str(tmp_path / "tok.json"))
+
+    class Store(util.StorageBackend):
+        def __init__(self):
+            self.blobs, self.reads = {}, 0
+
+        def file_size(self, url):
+            return len(self.blobs[url])
+
+        def get_bytes_range(self, url, start, num):
+            self.reads += 1
+            return self.blobs[url][start : start + num]
+
+        def list_files(self, url):
+            return sorted(k for k in self.blobs if k.startswith(url.rstrip("/") + "/"))
+
+    store = Store()
+    import io
+
+    buf = io.BytesIO()
+    with gzip.GzipFile(fileobj=buf, mode="wb") as f:
+        f.write(b'{"text": "w1 w2 w3"}\n{"text": "w4 w5"}\n')
+    store.blobs["mem://bucket/docs/a.json.gz"] = buf.getvalue()
+    store.blobs["mem://bucket/docs/readme.txt"] = b"not documents"
+    util.register_storage_backend("mem", store)
+    try:
+        prep = load_script("prepare_memmap_dataset")
+        assert prep.list_sources(["mem://bucket/docs"]) == ["mem://bucket/docs/a.json.gz"]
+        args = ["mem://bucket/docs", "-o", str(tmp_path / "out"), "--tokenizer", str(tmp_path / "tok.json"), "--eos-token-id", "20",
+                "--cache-dir", str(tmp_path / "cache"), "--max-tokens", "64"]
+        assert prep.main(args) == 7  # five words and an end-of-text token after each of the two documents
+        reads = store.reads
+        assert prep.main([*args[:2], str(tmp_path / "out2"), *args[3:]]) == 7 and store.reads == reads  # served from the cache
+        assert len(list((tmp_path / "cache").rglob("*a.json.gz"))) == 1
+    finally:
+        util._BACKENDS.pop("mem", None)
