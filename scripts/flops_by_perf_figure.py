@@ -15,7 +15,7 @@ import csv
 import math
 import sys
 from pathlib import Path
-from typing import Dict, List, Tuple
+from typing import Dict, List, Optional, Tuple
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
@@ -50,7 +50,7 @@ def read_points(path: Path) -> List[Dict[str, object]]:
 
 
 def render_svg(points: List[Dict[str, object]], title: str = "", xlabel: str = "Approximate training FLOPs", ylabel: str = "Score",
-               width: int = 860, height: int = 520) -> str:
+               width: int = 860, height: int = 520, font_path: Optional[str] = None) -> str:
     left, right, top, bottom = 70, 200, 40, 60
     xs = [math.log10(p["flops"]) for p in points]  # type: ignore[arg-type]
     ys = [float(p["score"]) for p in points]  # type: ignore[arg-type]
@@ -70,8 +70,17 @@ def render_svg(points: List[Dict[str, object]], title: str = "", xlabel: str = "
     for p in points:
         if p["group"] not in groups:
             groups.append(p["group"])  # type: ignore[arg-type]
-    out = [f'<svg xmlns="http://www.w3.org/2000/svg" width="{width}" height="{height}" font-family="sans-serif" font-size="12">',
-           f'<rect width="{width}" height="{height}" fill="white"/>']
+    family = "sans-serif"
+    font_face = ""
+    if font_path:  # embed the font file so that the figure renders the same everywhere
+        import base64
+
+        data = base64.b64encode(Path(font_path).read_bytes()).decode()
+        kind = "opentype" if str(font_path).lower().endswith(".otf") else "truetype"
+        family = "FigureFont, sans-serif"
+        font_face = f'<style>@font-face {{ font-family: FigureFont; src: url(data:font/{kind};base64,{data}) format("{kind}"); }}</style>'
+    out = [f'<svg xmlns="http://www.w3.org/2000/svg" width="{width}" height="{height}" font-family="{family}" font-size="12">',
+           font_face, f'<rect width="{width}" height="{height}" fill="white"/>']
     if title:
         out.append(f'<text x="{width / 2}" y="22" text-anchor="middle" font-size="15">{title}</text>')
     tick = x0
@@ -108,6 +117,8 @@ def main(argv=None) -> int:
     ap.add_argument("--ylabel", default="Score")
     ap.add_argument("--flops-of", default=None, metavar="RECIPE")
     ap.add_argument("--tokens", type=float, default=None)
+    ap.add_argument("--manrope-medium-font-path", "--font-path", dest="font_path", default=None,
+                    help="a .ttf/.otf file to embed in the figure and use for all text (the published figure uses Manrope Medium)")
     args = ap.parse_args(argv)
     if args.flops_of:
         if args.tokens is None:
@@ -116,7 +127,7 @@ def main(argv=None) -> int:
         return 0
     if not args.points or not args.output:
         ap.error("points.csv and figure.svg are required")
-    Path(args.output).write_text(render_svg(read_points(Path(args.points)), title=args.title, ylabel=args.ylabel))
+    Path(args.output).write_text(render_svg(read_points(Path(args.points)), title=args.title, ylabel=args.ylabel, font_path=args.font_path))
     print(args.output)
     return 0
 

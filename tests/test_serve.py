@@ -469,3 +469,48 @@ def test_chat_template_from_file(tmp_path):
     (tmp_path / "strict.jinja").write_text("{% if messages[0]['role'] != 'user' %}{{ raise_exception('first message must come from the user') }}{% endif %}ok")
     with pytest.raises(ValueError, match="first message"):
         load_chat_template(str(tmp_path / "strict.jinja"))([{"role": "system", "content": "x"}])
+
+
+def test_environment_driven_endpoint_script(tmp_path, monkeypatch):
+    """``scripts/olmo2_modal_openai.py`` without Modal: the app is assembled from environment variables, reports the
+    configured model name and asks for the bearer token."""
+    tokenizers = pytest.importorskip("tokenizers")
+    pytest.importorskip("fastapi")
+    import importlib.util
+    from pathlib import Path
+
+    from fastapi.testclient import TestClient
+    from tokenizers.models import WordLevel
+    from tokenizers.pre_tokenizers import WhitespaceSplit
+
+    from olmo_b200.config import TokenizerConfig, TrainConfig
+
+    vocab = {f"w{i}": i + 2 for i in range(60)}
+    vocab["<pad>"], vocab["<eos>"] = 0, 1
+    tok = tokenizers.Tokenizer(WordLevel(vocab, unk_token="<pad>"))
+    tok.pre_tokenizer = WhitespaceSplit()
+    tok.add_special_tokens(["<eos>", "<pad>"])
+    tok.save(str(tmp_path / "tokenizer.json"))
+    model = tiny_model(vocab_size=62, embedding_size=64)
+    ckpt = tmp_path / "step0-unsharded"
+    ckpt.mkdir()
+    torch.save(model.state_dict(), ckpt / "model.pt")
+    TrainConfig(model=model.config, tokenizer=TokenizerConfig(identifier=str(tmp_path / "tokenizer.json"))).save(ckpt / "config.yaml")
+
+    spec = importlib.util.spec_from_file_location("olmo2_modal_openai", str(Path(__file__).resolve().parent.parent / "scripts" / "olmo2_modal_openai.py"))
+    script = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(script)
+    monkeypatch.delenv("OLMO_SERVE_CHECKPOINT", raising=False)
+    with pytest.raises(SystemExit):
+        script.build_asgi_app()
+    monkeypatch.setenv("OLMO_SERVE_CHECKPOINT", str(ckpt))
+    monkeypatch.setenv("OLMO_SERVE_MODEL_NAME", "olmo-test")
+    monkeypatch.setenv("MODAL_TOKEN", "secret")
+    monkeypatch.setenv("OLMO_SERVE_MAX_BATCH", "2")
+    with TestClient(script.build_asgi_app()) as client:
+        assert client.post("/v1/completions", json={"model": "olmo-test", "prompt": "w1", "max_tokens": 1}).status_code == 401
+        listed = client.get("/v1/models", headers={"Authorization": "Bearer secret"}).json()
+        assert [m["id"] for m in listed["data"]] == ["olmo-test"]
+        out = client.post("/v1/completions", headers={"Authorization": "Bearer secret"},
+                          json={"model": "olmo-test", "prompt": "w1 w2 w3", "max_tokens": 3, "temperature": 0}).json()
+        assert out["choices"][0]["finish_reason"] in ("length", "stop") and out["usage"]["prompt_tokens"] == 3
