@@ -160,3 +160,55 @@ def size_for_model(model_config) -> Tuple[int, int]:
     per_block = sum(p.numel() for p in one.transformer.blocks[0].parameters())
     extra = per_block * (layers - 1)
     return one.num_params() + extra, one.num_params(include_embedding=False) + extra
+
+
+# ------------------------------------------------------------------------------------------- analysis
+
+
+_RUN_NAME = re.compile(r"^(?P<name>.+)-(?P<size>\d+[KMB])-(?P<length>\d+x?C|\d+[KMBT])$", re.IGNORECASE)
+
+
+def parse_run_name(run: str) -> Tuple[str, str, str]:
+    """``baseline-300M-5xC`` -> ``("baseline", "300M", "5xC")`` (the naming scheme of ``scripts/ladder.py train --name``)."""
+    m = _RUN_NAME.match(run.strip())
+    if m is None:
+        raise ValueError(f"'{run}' is not a ladder run name (<name>-<size>-<length>)")
+    return m.group("name"), m.group("size").upper(), m.group("length")
+
+
+def power_law(x, a: float, b: float, c: float):
+    """``a * x**b + c`` with ``b <= 0``: the irreducible loss ``c`` plus a term that shrinks with scale."""
+    return a * x**b + c
+
+
+def fit_power_law(x: List[float], y: List[float]) -> Tuple[float, float, float]:
+    """Least-squares ``(a, b, c)`` of :func:`power_law` under ``a >= 0``, ``b <= 0``, ``c >= 0`` (what the reference's
+    ``scripts/ladder.ipynb`` fits to ladder results).  ``x`` is rescaled internally so that parameter counts of 1e8–1e10
+    do not wreck the conditioning."""
+    import numpy as np
+    from scipy.optimize import curve_fit
+
+    xs, ys = np.asarray(x, dtype=np.float64), np.asarray(y, dtype=np.float64)
+    if len(xs) < 3:
+        raise ValueError("a three-parameter power law needs at least three points")
+    scale = float(xs.min())
+    guess = (max(ys.max() - ys.min(), 1e-3), -0.3, max(ys.min() * 0.8, 0.0))
+    (a, b, c), _ = curve_fit(power_law, xs / scale, ys, p0=guess, bounds=([0, -np.inf, 0], [np.inf, 0, np.inf]), maxfev=20000)
+    return float(a * scale ** (-b)), float(b), float(c)
+
+
+def ladder_fit(results: Dict[str, float], by: str = "size", hold_out: int = 1) -> Dict[str, Any]:
+    """Fit loss against model size (non-embedding parameters) or against training length (tokens) over the runs in
+    ``results`` (run name -> loss), keeping the ``hold_out`` largest ones aside, and report how well they are predicted."""
+    points = []
+    for run, loss in results.items():
+        _, size, length = parse_run_name(run)
+        _, non_embedding = size_for_model(size)
+        x = non_embedding if by == "size" else parse_length(length, non_embedding)
+        points.append((float(x), float(loss), run))
+    points.sort()
+    train = points[: len(points) - hold_out] if hold_out else points
+    a, b, c = fit_power_law([p[0] for p in train], [p[1] for p in train])
+    rows = [{"run": run, "x": x, "loss": loss, "predicted": power_law(x, a, b, c), "held_out": i >= len(train)}
+            for i, (x, loss, run) in enumerate(points)]
+    return {"a": a, "b": b, "c": c, "by": by, "points": rows}

@@ -66,6 +66,21 @@ def dump_cmd(args) -> None:
         print(f"{key}: {value}")
 
 
+def fit_cmd(args) -> None:
+    """Fit ``a * x**b + c`` to the losses in a CSV (``run,loss`` lines; run names as ``train --name`` builds them)."""
+    import csv
+
+    from olmo_b200.ladder import ladder_fit
+
+    with open(args.results) as f:
+        results = {row[0].strip(): float(row[1]) for row in csv.reader(f) if len(row) >= 2 and not row[0].startswith("#") and row[0] != "run"}
+    fit = ladder_fit(results, by=args.by, hold_out=args.hold_out)
+    print(f"loss = {fit['a']:.4g} * {args.by}^{fit['b']:.4f} + {fit['c']:.4f}")
+    for row in fit["points"]:
+        mark = "  (held out)" if row["held_out"] else ""
+        print(f"{row['run']:32s} {row['x']:.3e}  loss {row['loss']:.4f}  predicted {row['predicted']:.4f}{mark}")
+
+
 def train_cmd(args) -> None:
     from train import init_distributed, main
     from olmo_b200.util import prepare_cli_environment
@@ -88,6 +103,11 @@ if __name__ == "__main__":
     p = sub.add_parser("size")
     p.set_defaults(func=size_cmd, **quiet)
     p.add_argument("--model", required=True)
+    p = sub.add_parser("fit", help="fit a power law to ladder results")
+    p.set_defaults(func=fit_cmd)
+    p.add_argument("results", help="CSV file of run,loss lines")
+    p.add_argument("--by", choices=["size", "length"], default="size")
+    p.add_argument("--hold-out", type=int, default=1, help="how many of the largest runs to predict instead of fit")
     dump = sub.add_parser("dump")
     dump.set_defaults(func=dump_cmd)
     dump.add_argument("--dump_evaluators", action=argparse.BooleanOptionalAction, default=False)

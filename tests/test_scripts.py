@@ -522,3 +522,21 @@ def test_memmap_preparation_reads_remote_sources_through_a_cache(tmp_path):
         assert len(list((tmp_path / "cache").rglob("*a.json.gz"))) == 1
     finally:
         util._BACKENDS.pop("mem", None)
+
+
+def test_ladder_power_law_fit_recovers_a_known_law():
+    pytest.importorskip("scipy")
+    from olmo_b200.ladder import fit_power_law, ladder_fit, parse_run_name, power_law, size_for_model
+
+    assert parse_run_name("baseline2-300M-5xC") == ("baseline2", "300M", "5xC")
+    with pytest.raises(ValueError):
+        parse_run_name("not a run")
+    xs = [1.5e8, 3e8, 7.5e8, 1e9, 7e9]
+    ys = [power_law(x, 420.0, -0.3, 1.8) for x in xs]
+    a, b, c = fit_power_law(xs, ys)
+    assert abs(b + 0.3) < 1e-3 and abs(c - 1.8) < 1e-3 and abs(a / 420.0 - 1) < 2e-2
+    sizes = {s: size_for_model(s)[1] for s in ("150M", "300M", "750M", "1B")}
+    results = {f"base-{s}-2xC": power_law(n, 50.0, -0.2, 2.0) for s, n in sizes.items()}
+    fit = ladder_fit(results, by="size", hold_out=1)
+    held = [p for p in fit["points"] if p["held_out"]]
+    assert len(held) == 1 and held[0]["run"] == "base-1B-2xC" and abs(held[0]["predicted"] - held[0]["loss"]) < 1e-2
