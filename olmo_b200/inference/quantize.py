@@ -147,7 +147,11 @@ def quantize_model(
         for name in names:
             old = getattr(block, name)
             new = quantize_linear(old, sums.get(name), group=group, act_order=act_order, method=method)
-            probe = torch.cat(kept_in[name]).to(old.weight.dtype)
+            if kept_in[name]:
+                probe = torch.cat(kept_in[name]).to(old.weight.dtype)
+            else:  # no calibration inputs (round-to-nearest needs none): report the error on unit-variance noise
+                probe = torch.randn(64, old.in_features, device=old.weight.device, dtype=old.weight.dtype,
+                                    generator=torch.Generator(device=old.weight.device).manual_seed(index))
             want = old(probe).float()
             got = new(probe).float()
             report[f"blocks.{index}.{name}"] = float((got - want).norm() / want.norm().clamp_min(1e-12))
