@@ -637,8 +637,12 @@ def unshard_torch_dcp_checkpoint(
     from torch.distributed.checkpoint.metadata import BytesStorageMetadata, TensorStorageMetadata
     from torch.distributed.checkpoint.state_dict_loader import _load_state_dict
 
-    folder = Path(load_path) / "model_and_optim"
-    reader = FileSystemReader(str(folder))
+    if is_url(str(load_path)):
+        reader = RemoteFileSystemReader(f"{str(load_path).rstrip('/')}/model_and_optim")
+        folder = f"{str(load_path).rstrip('/')}/model_and_optim"
+    else:
+        folder = Path(load_path) / "model_and_optim"
+        reader = FileSystemReader(str(folder))
     table = reader.read_metadata().state_dict_metadata
     wanted: Dict[str, Any] = {}
     for key, entry in table.items():
@@ -677,10 +681,142 @@ def unshard_torch_dcp_checkpoint(
     trainer_state = None
     if load_trainer_state:
         for candidate in ("train/rank0.pt", "train.pt"):
-            if (Path(load_path) / candidate).is_file():
-                trainer_state = torch.load(Path(load_path) / candidate, map_location="cpu", weights_only=False)
+            try:
+                trainer_state = load_state_dict(load_path, candidate, map_location="cpu")
                 break
+            except FileNotFoundError:
+                continue
     return model_state, optim_state, trainer_state
+
+
+# ------------------------------------------------------------- torch distributed-checkpoint files on remote storage
+
+
+class _RangeReader(io.RawIOBase):
+    """A seekable read-only view of one remote object that fetches byte ranges on demand."""
+
+    def __init__(self, url: str):
+        super().__init__()
+        from .util import file_size
+
+        self.url, self.size, self.pos = url, file_size(url), 0
+
+    def readable(self) -> bool:
+        return True
+
+    def seekable(self) -> bool:
+        return True
+
+    def tell(self) -> int:
+        return self.pos
+
+    def seek(self, offset: int, whence: int = io.SEEK_SET) -> int:
+        base = {io.SEEK_SET: 0, io.SEEK_CUR: self.pos, io.SEEK_END: self.size}[whence]
+        self.pos = max(0, min(self.size, base + offset))
+        return self.pos
+
+    def readinto(self, buffer) -> int:
+        from .util import get_bytes_range
+
+        want = min(len(buffer), self.size - self.pos)
+        if want <= 0:
+            return 0
+        data = get_bytes_range(self.url, self.pos, want)
+        buffer[: len(data)] = data
+        self.pos += len(data)
+        return len(data)
+
+
+def _remote_file_system():
+    """torch's checkpoint file-system interface over this framework's storage layer (any registered URL scheme).
+    Writes go to a local temporary file that is uploaded when the stream closes; reads fetch byte ranges on demand."""
+    import tempfile
+
+    from torch.distributed.checkpoint.filesystem import FileSystemBase
+
+    from .util import delete_file, file_size
+
+    class RemoteFileSystem(FileSystemBase):
+        @contextmanager
+        def create_stream(self, path, mode: str):
+            url = str(path)
+            if mode == "rb":
+                stream = io.BufferedReader(_RangeReader(url), buffer_size=8 << 20)
+                try:
+                    yield stream
+                finally:
+                    stream.close()
+            elif mode == "wb":
+                fd, tmp = tempfile.mkstemp(suffix=".distcp")
+                try:
+                    with os.fdopen(fd, "wb") as f:
+                        yield f
+                    upload(Path(tmp), url, save_overwrite=True)
+                finally:
+                    Path(tmp).unlink(missing_ok=True)
+            else:
+                raise ValueError(f"unsupported mode {mode!r}")
+
+        def concat_path(self, path, suffix: str) -> str:
+            return f"{str(path).rstrip('/')}/{suffix}"
+
+        def init_path(self, path) -> str:
+            return str(path)
+
+        def rename(self, path, new_path) -> None:  # object stores have no rename: copy, then remove the source
+            with self.create_stream(path, "rb") as src, self.create_stream(new_path, "wb") as dst:
+                shutil.copyfileobj(src, dst, length=8 << 20)
+            delete_file(str(path))
+
+        def mkdir(self, path) -> None:
+            pass  # prefixes need no creation
+
+        @classmethod
+        def validate_checkpoint_id(cls, checkpoint_id) -> bool:
+            return is_url(str(checkpoint_id))
+
+        def exists(self, path) -> bool:
+            try:
+                file_size(str(path))
+                return True
+            except FileNotFoundError:
+                return False
+
+        def rm_file(self, path) -> None:
+            delete_file(str(path))
+
+    return RemoteFileSystem()
+
+
+def RemoteFileSystemWriter(path: PathOrStr, **kwargs):
+    """A ``torch.distributed.checkpoint`` storage writer whose destination is a URL (the reference's class of this name,
+    ``olmo/checkpoint.py:219-372``, writes locally and uploads per file as well).  Returns a ``FileSystemWriter`` bound to
+    the remote file system."""
+    from torch.distributed.checkpoint import FileSystemWriter
+
+    kwargs.setdefault("sync_files", False)
+    writer = FileSystemWriter(tempfile_safe_path(), **kwargs)
+    writer.fs = _remote_file_system()
+    writer.path = writer.fs.init_path(str(path))
+    return writer
+
+
+def RemoteFileSystemReader(path: PathOrStr, **kwargs):
+    """The matching storage reader: reads ``.metadata`` and the data files of a checkpoint under a URL by byte range
+    (``olmo/checkpoint.py:375-474``)."""
+    from torch.distributed.checkpoint import FileSystemReader
+
+    reader = FileSystemReader(tempfile_safe_path(), **kwargs)
+    reader.fs = _remote_file_system()
+    reader.path = reader.fs.init_path(str(path))
+    return reader
+
+
+def tempfile_safe_path() -> str:
+    """A local path handed to the base classes' constructors (they normalise it as a local path; it is replaced at once)."""
+    import tempfile
+
+    return tempfile.gettempdir()
 
 
 # ------------------------------------------------------------------ the reference's ``torch_new`` layout, live

@@ -385,7 +385,7 @@ def unshard_reference_checkpoint(
 def export_torch_new_checkpoint(
     out_dir: PathOrStr, model_state: Dict[str, torch.Tensor], optim_state: Optional[Dict[str, Any]] = None,
     trainer_state: Optional[Dict[str, Any]] = None, *, world_size: int = 1,
-) -> Path:
+) -> PathOrStr:
     """Write full states in the layout of the reference's ``torch_new`` sharded checkpointer
     (``olmo/checkpoint.py:99-144,892-966``): ``model_and_optim/`` in torch's distributed-checkpoint format holding
     ``model.<parameter>`` tensors, ``optim.state.<parameter>.<key>`` tensors and the parameter groups, plus
@@ -397,9 +397,20 @@ def export_torch_new_checkpoint(
     the form of an unsharded ``optim.pt``."""
     import torch.distributed.checkpoint as dcp
 
-    out = Path(out_dir)
-    folder = out / "model_and_optim"
-    folder.mkdir(parents=True, exist_ok=True)
+    from .util import is_url, upload
+
+    remote = is_url(str(out_dir))
+    if remote:
+        from .checkpoint import RemoteFileSystemWriter
+
+        root = str(out_dir).rstrip("/")
+        writer = RemoteFileSystemWriter(f"{root}/model_and_optim")
+        out = root  # type: ignore[assignment]
+    else:
+        out = Path(out_dir)
+        folder = out / "model_and_optim"
+        folder.mkdir(parents=True, exist_ok=True)
+        writer = dcp.FileSystemWriter(str(folder))
     payload: Dict[str, Any] = {"model": {name: t.detach().cpu().contiguous() for name, t in model_state.items()}}
     if optim_state is not None:
         groups = optim_state.get("param_groups", [])
@@ -416,8 +427,15 @@ def export_torch_new_checkpoint(
             for name, entry in optim_state.get("state", {}).items()
         }
         payload["optim"] = {"state": state, "param_groups": groups}
-    dcp.save(payload, storage_writer=dcp.FileSystemWriter(str(folder)), no_dist=True)
-    if world_size > 0:
+    dcp.save(payload, storage_writer=writer, no_dist=True)
+    if world_size > 0 and remote:
+        import tempfile
+
+        with tempfile.TemporaryDirectory() as tmp:
+            torch.save(trainer_state or {}, Path(tmp) / "train.pt")
+            for rank in range(world_size):
+                upload(Path(tmp) / "train.pt", f"{out}/train/rank{rank}.pt", save_overwrite=True)
+    elif world_size > 0:
         (out / "train").mkdir(exist_ok=True)
         for rank in range(world_size):
             torch.save(trainer_state or {}, out / "train" / f"rank{rank}.pt")

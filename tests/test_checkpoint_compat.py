@@ -175,3 +175,60 @@ def test_unshard_script_reads_a_torch_legacy_directory(legacy_dir, tmp_path):
     for n in NAMES:
         torch.testing.assert_close(model[_clean(n)], src["model"][n], rtol=0, atol=0)
     assert (out / "optim.pt").is_file() and (out / "train.pt").is_file() and (out / "config.yaml").is_file()
+
+
+def test_torch_new_layout_is_written_to_and_read_from_a_remote_store():
+    """The distributed-checkpoint files go to a URL through the storage layer (temporary file + upload per stream) and come
+    back by byte-range reads; nothing but the registered backend touches the "remote" side."""
+    from pathlib import Path
+
+    from olmo_b200 import util
+    from olmo_b200.checkpoint import unshard_torch_dcp_checkpoint
+    from olmo_b200.checkpoint_compat import export_torch_new_checkpoint
+
+    class Store(util.StorageBackend):
+        def __init__(self):
+            self.blobs, self.range_reads = {}, 0
+
+        def file_size(self, url):
+            if url not in self.blobs:
+                raise FileNotFoundError(url)
+            return len(self.blobs[url])
+
+        def get_bytes_range(self, url, start, num):
+            self.range_reads += 1
+            if url not in self.blobs:
+                raise FileNotFoundError(url)
+            return self.blobs[url][start : start + num]
+
+        def upload(self, source, url, save_overwrite=False):
+            self.blobs[url] = Path(source).read_bytes()
+
+        def list_files(self, url):
+            return sorted(k for k in self.blobs if k.startswith(url.rstrip("/") + "/"))
+
+        def delete(self, url):
+            self.blobs.pop(url, None)
+
+    store = Store()
+    util.register_storage_backend("mem", store)
+    try:
+        torch.manual_seed(0)
+        model = {"transformer.wte.weight": torch.randn(32, 8), "transformer.blocks.0.ff_out.weight": torch.randn(8, 16)}
+        optim = {
+            "state": {n: {"exp_avg": torch.randn_like(t), "exp_avg_sq": torch.rand_like(t), "step": torch.tensor(7.0)} for n, t in model.items()},
+            "param_groups": [{"lr": 1e-3, "params": list(model)}],
+        }
+        export_torch_new_checkpoint("mem://bucket/run/step7", model, optim, {"global_step": 7}, world_size=2)
+        names = sorted(k[len("mem://bucket/run/step7/"):] for k in store.blobs)
+        assert "model_and_optim/.metadata" in names and "train/rank1.pt" in names and any(n.endswith(".distcp") for n in names)
+        assert not any(n.endswith(".tmp") for n in names)  # the metadata file was published under its final name
+        got_model, got_optim, trainer = unshard_torch_dcp_checkpoint("mem://bucket/run/step7")
+        assert store.range_reads > 0 and trainer == {"global_step": 7}
+        for n, t in model.items():
+            assert torch.equal(got_model[n], t)
+            assert torch.equal(got_optim["state"][n]["exp_avg_sq"], optim["state"][n]["exp_avg_sq"])
+            assert float(got_optim["state"][n]["step"]) == 7.0
+        assert got_optim["param_groups"][0]["params"] == list(model)
+    finally:
+        util._BACKENDS.pop("mem", None)
