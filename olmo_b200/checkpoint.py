@@ -51,7 +51,9 @@ from .util import default_thread_count, dir_is_empty, is_url, resource_path, upl
 
 __all__ = [
     "save_state_dict", "load_state_dict", "load_model_state", "Checkpointer", "FullCheckpointer",
-    "FlatShardCheckpointer", "build_sharded_checkpointer",
+    "FlatShardCheckpointer", "build_sharded_checkpointer", "TorchNewStyleShardedCheckpointer", "TorchLegacyShardedCheckpointer",
+    "LocalShardedCheckpointer", "OlmoCoreCheckpointer", "RemoteFileSystemWriter", "RemoteFileSystemReader",
+    "save_fsdp_model_and_optim_state", "load_fsdp_model_and_optim_state", "unshard_torch_dcp_checkpoint", "is_torch_dcp_checkpoint",
 ]
 
 log = logging.getLogger(__name__)
@@ -896,6 +898,54 @@ class TorchNewStyleShardedCheckpointer(Checkpointer):
         load_trainer_state: bool = True, device: Optional[torch.device] = None,
     ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
         return unshard_torch_dcp_checkpoint(load_path, load_optimizer_state=load_optimizer_state, load_trainer_state=load_trainer_state)
+
+
+class _ReferenceLayoutReader(Checkpointer):
+    """Read-only checkpointer for one sharded layout of the reference implementation (:mod:`olmo_b200.checkpoint_compat`
+    does the work).  These layouts serialise FSDP1 objects this engine does not have, so ``save_checkpoint`` refuses and
+    names the two ways of producing a checkpoint the reference loads."""
+
+    layout = ""
+
+    def save_checkpoint(self, dir: PathOrStr, dist_model: nn.Module, optim: Optimizer, trainer_state: Dict[str, Any], *, upload_to: Optional[str] = None) -> None:
+        raise OLMoCheckpointError(
+            f"the '{self.layout}' layout is read-only here; save an unsharded checkpoint (both implementations read it) or write the "
+            "'torch_new' layout (TorchNewStyleShardedCheckpointer, scripts/export_sharded.py)"
+        )
+
+    def restore_checkpoint(
+        self, load_path: PathOrStr, dist_model: nn.Module, optim: Optimizer, *, local_cache: Optional[PathOrStr] = None,
+        load_optimizer_state: bool = True,
+    ) -> Dict[str, Any]:
+        return FlatShardCheckpointer(self.cfg)._restore_foreign(load_path, self.layout, dist_model, optim, load_optimizer_state=load_optimizer_state)
+
+    def unshard_checkpoint(
+        self, load_path: PathOrStr, *, local_cache: Optional[PathOrStr] = None, load_optimizer_state: bool = True,
+        load_trainer_state: bool = True, device: Optional[torch.device] = None,
+    ) -> Tuple[Dict[str, torch.Tensor], Optional[Dict[str, Any]], Optional[Dict[str, Any]]]:
+        from .checkpoint_compat import unshard_reference_checkpoint
+
+        return unshard_reference_checkpoint(load_path, layout=self.layout, load_optimizer_state=load_optimizer_state,
+                                            load_trainer_state=load_trainer_state, device=device)
+
+
+class TorchLegacyShardedCheckpointer(_ReferenceLayoutReader):
+    """``rank{r}.pt`` files of pickled ``ShardedTensor`` objects (the reference's default, ``olmo/checkpoint.py:969-1453``)."""
+
+    layout = "torch_legacy"
+
+
+class LocalShardedCheckpointer(_ReferenceLayoutReader):
+    """Raw FSDP flat-parameter pieces per rank (``olmo/checkpoint.py:1474-1906``)."""
+
+    layout = "local"
+
+
+class OlmoCoreCheckpointer(_ReferenceLayoutReader):
+    """The layout written through the ``olmo_core`` package (``olmo/checkpoint.py:1909-2014``): reading it needs that
+    package's own loader, which is not bundled; every operation says so."""
+
+    layout = "olmo_core"
 
 
 def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckpointerType] = None, use_shared_mem_impl: bool = False) -> Checkpointer:

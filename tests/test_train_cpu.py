@@ -406,6 +406,23 @@ def test_training_resumes_from_a_torch_legacy_sharded_checkpoint(tmp_path):
     again = t2.train_step(next(iter(t2.train_loader)))["train/CrossEntropyLoss"]
     assert abs(again - expect) < 1e-5
 
+    # the named checkpointers: the legacy one reads (restore and unshard) and refuses to write; the olmo_core one says what it needs
+    from olmo_b200.checkpoint import OlmoCoreCheckpointer, TorchLegacyShardedCheckpointer
+    from olmo_b200.exceptions import OLMoCheckpointError
+
+    reader = TorchLegacyShardedCheckpointer(cfg2)
+    model_state, optim_state, trainer_state = reader.unshard_checkpoint(legacy)
+    assert trainer_state["global_step"] == 3 and set(model_state) == set(wrapped) and optim_state is not None
+    cfg3 = tiny_train_config(tmp_path / "c")
+    t3 = build_trainer(cfg3, device=torch.device("cpu"), train_loader=make_loader(cfg3), with_evaluators=False)
+    assert reader.restore_checkpoint(legacy, t3.dist_model, t3.optim)["global_step"] == 3
+    for n, p in t3.dist_model.engine.named_parameters_for_optimizer():
+        assert torch.equal(p.detach(), source["model"][wrapped[n]]), n
+    with pytest.raises(OLMoCheckpointError, match="read-only"):
+        reader.save_checkpoint(tmp_path / "nope", t3.dist_model, t3.optim, {})
+    with pytest.raises(OLMoCheckpointError, match="olmo_core"):
+        OlmoCoreCheckpointer(cfg2).unshard_checkpoint(legacy)
+
 
 def test_fused_or_portable_is_decided_when_the_engine_is_built(tmp_path):
     """Runs whose batches the fused kernel sequence cannot take (padding masks, module-output traces, document masking
