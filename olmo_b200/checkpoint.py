@@ -53,7 +53,7 @@ __all__ = [
     "save_state_dict", "load_state_dict", "load_model_state", "Checkpointer", "FullCheckpointer",
     "FlatShardCheckpointer", "build_sharded_checkpointer", "TorchNewStyleShardedCheckpointer", "TorchLegacyShardedCheckpointer",
     "LocalShardedCheckpointer", "OlmoCoreCheckpointer", "RemoteFileSystemWriter", "RemoteFileSystemReader",
-    "save_fsdp_model_and_optim_state", "load_fsdp_model_and_optim_state", "unshard_torch_dcp_checkpoint", "is_torch_dcp_checkpoint",
+    "save_fsdp_model_and_optim_state", "load_fsdp_model_and_optim_state", "load_fsdp_optim_state", "unshard_torch_dcp_checkpoint", "is_torch_dcp_checkpoint",
 ]
 
 log = logging.getLogger(__name__)
@@ -868,6 +868,13 @@ def load_fsdp_model_and_optim_state(
     if load_optimizer_state and optim_state is not None:
         FullCheckpointer.load_optim_state_into(dist_model, optim, FullCheckpointer._normalise_optim_state(optim_state, {}))
     barrier()
+
+
+def load_fsdp_optim_state(dist_model: nn.Module, optim: Optimizer, optim_state: Dict[str, Any]) -> None:
+    """Load a *full* optimizer state dict (keyed by parameter name or by integer id with ``param_names``) into the live,
+    sharded optimizer: every rank keeps the ranges of its shards (the reference's function of this name,
+    ``olmo/checkpoint.py:202-216``)."""
+    FullCheckpointer.load_optim_state_into(dist_model, optim, FullCheckpointer._normalise_optim_state(optim_state, {}))
 
 
 class TorchNewStyleShardedCheckpointer(Checkpointer):

@@ -43,6 +43,7 @@ __all__ = [
     "log_extra_field",
     "setup_logging",
     "install_excepthook",
+    "RichHandler",
     "excepthook",
     "get_progress_bar",
     "save_hf_dataset_to_disk",
@@ -170,31 +171,43 @@ def setup_logging(log_filter_type: LogFilterType = LogFilterType.rank0_only) -> 
     logging.getLogger("urllib3").setLevel(logging.ERROR)
 
 
+class RichHandler(logging.Handler):
+    """Log records on a ``rich`` console: time, level, ``[logger:line, rank=…]``, message, and a formatted traceback when
+    the record carries one (the look of the reference's handler of this name, ``olmo/util.py:222-286``).  ``rich`` is imported
+    when the first record arrives, so the class can be named on machines without it."""
+
+    def __init__(self, level: int = logging.NOTSET, markup: bool = False):
+        super().__init__(level=level)
+        self.markup = markup
+
+    def emit(self, record: logging.LogRecord) -> None:
+        try:
+            import rich
+            from rich.text import Text
+
+            console = rich.get_console()
+            stamp = datetime.fromtimestamp(record.created).strftime("[%Y-%m-%d %X]")
+            where = f"{record.name}:{record.lineno}" if record.name != "root" else "root"
+            message = record.getMessage()
+            console.print(
+                Text(stamp, style="log.time", end=" "),
+                Text(record.levelname.ljust(8), style="log.level", end=" "),
+                Text(f"[{where}, rank={getattr(record, 'local_rank', 0)}]", style="log.path"),
+                Text.from_markup(message) if self.markup else Text(message),
+            )
+            if record.exc_info:
+                from rich.traceback import Traceback
+
+                console.print(Traceback.from_exception(*record.exc_info))  # type: ignore[arg-type]
+        except Exception:
+            self.handleError(record)
+
+
 def _rich_handler() -> logging.Handler:
     import rich
-    from rich.text import Text
-
-    class _Handler(logging.Handler):
-        def emit(self, record: logging.LogRecord) -> None:
-            try:
-                console = rich.get_console()
-                stamp = datetime.fromtimestamp(record.created).strftime("[%Y-%m-%d %X]")
-                where = f"{record.name}:{record.lineno}" if record.name != "root" else "root"
-                console.print(
-                    Text(stamp, style="log.time", end=" "),
-                    Text(record.levelname.ljust(8), style="log.level", end=" "),
-                    Text(f"[{where}, rank={getattr(record, 'local_rank', 0)}]", style="log.path"),
-                    Text(record.getMessage()),
-                )
-                if record.exc_info:
-                    from rich.traceback import Traceback
-
-                    console.print(Traceback.from_exception(*record.exc_info))  # type: ignore[arg-type]
-            except Exception:
-                self.handleError(record)
 
     rich.reconfigure(width=max(rich.get_console().width, 180), soft_wrap=True)
-    return _Handler()
+    return RichHandler()
 
 
 def excepthook(exctype, value, traceback) -> None:

@@ -209,3 +209,31 @@ def test_dataset_saver_writes_where_the_loader_looks_and_hooks_are_public(tmp_pa
     task = bar.add_task("fetch", total=10)
     bar.update(task, advance=10)
     assert bar.tasks[0].finished
+
+
+def test_rich_handler_formats_records_and_tracebacks():
+    rich = pytest.importorskip("rich")
+    import io
+    import logging
+
+    from rich.console import Console
+
+    previous = rich.get_console()
+    buffer = io.StringIO()
+    rich._console = Console(file=buffer, width=200, force_terminal=False)
+    logger = logging.getLogger("rich-handler-test")
+    handler = util.RichHandler()
+    logger.addHandler(handler)
+    logger.setLevel(logging.INFO)
+    logger.propagate = False
+    try:
+        logger.info("hello %s", "world", extra={"local_rank": 3})
+        try:
+            raise ValueError("boom")
+        except ValueError:
+            logger.exception("failed")
+    finally:
+        logger.removeHandler(handler)
+        rich._console = previous
+    out = buffer.getvalue()
+    assert "hello world" in out and "rank=3" in out and "[rich-handler-test:" in out and "ValueError" in out and "boom" in out
