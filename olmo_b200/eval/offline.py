@@ -20,7 +20,9 @@ file:
         tasks:
           - {task_name: ppl, task_kwargs: {files: [/data/val.jsonl.gz]}, prediction_kwargs: {model_max_length: 2048}}
 
-Two task kinds exist.  A *ranked-classification* task is any label of
+Three task kinds exist.  A *generation* task (``gen``) reads prompts and reference answers from ``.jsonl[.gz]`` files, continues
+each prompt greedily (optionally after ``num_shots`` examples) and reports ``exact_match``, ``f1`` and ``rouge_l``.
+A *ranked-classification* task is any label of
 :data:`olmo_b200.eval.downstream.label_to_task_map` and reports that task's metric.  A *perplexity* task (``ppl``) reads
 documents from ``.jsonl[.gz]`` files with a ``text`` field, or token ids from ``.npy`` memmaps, and reports
 ``ppl_token``, ``ppl_char``, ``ppl_word``, ``ppl_byte`` and ``bits_per_byte``.
@@ -32,7 +34,10 @@ import hashlib
 import json
 import logging
 import math
+import os
+import string
 import time
+from collections import Counter
 from dataclasses import dataclass, field
 from pathlib import Path
 from typing import Any, Dict, Iterable, Iterator, List, Optional, Sequence, Tuple
@@ -44,7 +49,8 @@ log = logging.getLogger(__name__)
 
 __all__ = [
     "EvalModel", "load_experiment", "resolve_task_set", "construct_task", "predict_and_calculate_metrics", "run_experiment",
-    "write_rows", "merge_sheet_rows", "append_rows_to_gsheet", "TASK_SET_DIR",
+    "write_rows", "merge_sheet_rows", "append_rows_to_gsheet", "TASK_SET_DIR", "GenerationTask", "PerplexityTask", "exact_match",
+    "token_f1", "rouge_l",
 ]
 
 #: task-set files shipped with the repository (``<repo>/evaluation/task_sets/*.yaml``)
@@ -79,6 +85,16 @@ class EvalModel:
     @property
     def max_length(self) -> int:
         return self.model.config.max_sequence_length
+
+    @torch.no_grad()
+    def generate_text(self, prompt_ids: Sequence[int], max_new_tokens: int) -> str:
+        """Greedy continuation of one prompt, decoded, cut at the end-of-text token."""
+        ids = torch.tensor([list(prompt_ids)], dtype=torch.long, device=self.device)
+        out = self.model.generate(ids, max_steps=max_new_tokens, beam_size=1).token_ids[0, 0].tolist()
+        eos = self.tokenizer.eos_token_id
+        if eos in out:
+            out = out[: out.index(eos)]
+        return self.tokenizer.decode(out)
 
     @torch.no_grad()
     def logits(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -138,7 +154,7 @@ class PerplexityTask:
     def documents(self, tokenizer) -> Iterator[Tuple[List[int], str]]:
         import numpy as np
 
-        for file in self.files:
+        for file in _data_files(self.files):
             if str(file).endswith(".npy"):
                 tokens = np.memmap(file, dtype=getattr(np, self.memmap_dtype), mode="r")
                 eos = tokenizer.eos_token_id
@@ -157,11 +173,114 @@ class PerplexityTask:
                             yield tokenizer.encode(text, add_special_tokens=False), text
 
 
+def _expand(path: str) -> str:
+    """``$EVAL_DATA_PATH/...`` and ``~`` in task files; a relative path is taken below ``EVAL_DATA_PATH`` when that is set
+    and the file exists there (how the reference's perplexity suites locate their data)."""
+    expanded = os.path.expanduser(os.path.expandvars(str(path)))
+    root = os.environ.get("EVAL_DATA_PATH")
+    if root and not os.path.isabs(expanded) and not os.path.exists(expanded):
+        for candidate in (os.path.join(root, expanded), os.path.join(root, expanded + ".jsonl.gz"), os.path.join(root, expanded + ".jsonl")):
+            if os.path.exists(candidate):
+                return candidate
+    return expanded
+
+
+def _data_files(paths: Sequence[str]) -> List[str]:
+    """Every data file named by a task: a path may be a file or a folder of ``.jsonl[.gz]`` / ``.npy`` files."""
+    out: List[str] = []
+    for path in paths:
+        path = _expand(path)
+        if os.path.isdir(path):
+            out += sorted(os.path.join(path, n) for n in os.listdir(path) if n.endswith((".jsonl", ".jsonl.gz", ".json.gz", ".npy")))
+        else:
+            out.append(path)
+    return out
+
+
+def _normalise_answer(text: str) -> str:
+    """Lower case, no punctuation, no articles, single spaces (the usual normalisation of reading-comprehension scoring)."""
+    text = "".join(ch for ch in text.lower() if ch not in string.punctuation)
+    return " ".join(w for w in text.split() if w not in ("a", "an", "the"))
+
+
+def exact_match(prediction: str, answers: Sequence[str]) -> float:
+    return float(any(_normalise_answer(prediction) == _normalise_answer(a) for a in answers))
+
+
+def token_f1(prediction: str, answers: Sequence[str]) -> float:
+    """Best bag-of-words F1 against any reference answer."""
+    best = 0.0
+    pred = _normalise_answer(prediction).split()
+    for answer in answers:
+        gold = _normalise_answer(answer).split()
+        common = sum((Counter(pred) & Counter(gold)).values())
+        if not pred or not gold:
+            best = max(best, float(pred == gold))
+        elif common:
+            precision, recall = common / len(pred), common / len(gold)
+            best = max(best, 2 * precision * recall / (precision + recall))
+    return best
+
+
+def rouge_l(prediction: str, answers: Sequence[str]) -> float:
+    """Best ROUGE-L F-measure (longest common subsequence of words) against any reference."""
+    best = 0.0
+    pred = _normalise_answer(prediction).split()
+    for answer in answers:
+        gold = _normalise_answer(answer).split()
+        if not pred or not gold:
+            continue
+        row = [0] * (len(gold) + 1)
+        for p_word in pred:
+            prev = 0
+            for j, g_word in enumerate(gold, start=1):
+                cur = row[j]
+                row[j] = prev + 1 if p_word == g_word else max(row[j], row[j - 1])
+                prev = cur
+        lcs = row[-1]
+        if lcs:
+            precision, recall = lcs / len(pred), lcs / len(gold)
+            best = max(best, 2 * precision * recall / (precision + recall))
+    return best
+
+
+@dataclass
+class GenerationTask:
+    """Free-form answers: every line of ``files`` holds a prompt (``input_field``) and one or more reference answers
+    (``answer_field``: a string or a list).  ``num_shots`` examples drawn with ``fewshot_seed`` from the same files are put in
+    front of every prompt; the model continues greedily up to ``max_new_tokens`` or the first ``stop`` string.  Metrics:
+    exact match, word F1 and ROUGE-L (question answering and summarisation suites of the reference, ``gen_tasks`` and
+    ``summary_tasks``, run through generation the same way)."""
+
+    files: Sequence[str]
+    input_field: str = "input"
+    answer_field: str = "answers"
+    template: str = "{input}\nAnswer:"
+    separator: str = "\n\n"
+    max_new_tokens: int = 32
+    stop: Sequence[str] = ("\n",)
+    name: str = "gen"
+
+    def examples(self) -> List[Tuple[str, List[str]]]:
+        rows = []
+        for file in _data_files(self.files):
+            opener = gzip.open if str(file).endswith(".gz") else open
+            with opener(file, "rt", encoding="utf-8") as f:
+                for line in f:
+                    if line.strip():
+                        rec = json.loads(line)
+                        answers = rec[self.answer_field]
+                        rows.append((str(rec[self.input_field]), [answers] if isinstance(answers, str) else [str(a) for a in answers]))
+        return rows
+
+
 def construct_task(task_name: str, tokenizer, task_kwargs: Optional[Dict[str, Any]] = None, model_max_length: Optional[int] = None):
     """Build the task object: a :class:`PerplexityTask` for ``ppl``, else the labelled multiple-choice dataset."""
     task_kwargs = dict(task_kwargs or {})
     if task_name == "ppl":
         return PerplexityTask(**task_kwargs)
+    if task_name == "gen":
+        return GenerationTask(**task_kwargs)
     from .downstream import label_to_task_map
 
     if task_name not in label_to_task_map:
@@ -234,9 +353,37 @@ def _score_ranked(model: EvalModel, task, limit: Optional[int], batch_size: int,
     return {"metrics": {task.metric_type: float(metric.compute())}, "num_instances": documents, "recorded_inputs": recorded}
 
 
+def _score_generation(model: EvalModel, task: GenerationTask, limit: Optional[int], max_length: int, num_shots: int, fewshot_seed: int,
+                      num_recorded_inputs: int) -> Dict[str, Any]:
+    import random
+
+    rows = task.examples()
+    rng = random.Random(fewshot_seed)
+    totals = {"exact_match": 0.0, "f1": 0.0, "rouge_l": 0.0}
+    recorded = []
+    todo = rows if limit is None else rows[:limit]
+    for n, (question, answers) in enumerate(todo):
+        pool = [r for r in rows if r[0] != question]
+        shots = rng.sample(pool, min(num_shots, len(pool))) if num_shots else []
+        prompt = task.separator.join([task.template.format(input=q) + " " + a[0] for q, a in shots] + [task.template.format(input=question)])
+        ids = model.tokenizer.encode(prompt, add_special_tokens=False)
+        room = max(1, min(task.max_new_tokens, max_length - 1))
+        ids = ids[-(max_length - room):]  # keep the end of an over-long prompt: the question is there
+        text = model.generate_text(ids, room)
+        cuts = [text.index(s) for s in task.stop if s and s in text]
+        text = (text[: min(cuts)] if cuts else text).strip()
+        totals["exact_match"] += exact_match(text, answers)
+        totals["f1"] += token_f1(text, answers)
+        totals["rouge_l"] += rouge_l(text, answers)
+        if n < num_recorded_inputs:
+            recorded.append({"prompt": prompt, "prediction": text, "answers": answers})
+    count = max(1, len(todo))
+    return {"metrics": {k: v / count for k, v in totals.items()}, "num_instances": len(todo), "recorded_inputs": recorded}
+
+
 def predict_and_calculate_metrics(model: EvalModel, task, prediction_kwargs: Optional[Dict[str, Any]] = None) -> Dict[str, Any]:
     """Run one task.  Understood ``prediction_kwargs``: ``limit`` (documents), ``batch_size``, ``model_max_length``,
-    ``num_recorded_inputs``."""
+    ``num_recorded_inputs``, and for generation tasks ``num_shots`` and ``fewshot_seed``."""
     kw = dict(prediction_kwargs or {})
     limit = kw.get("limit")
     batch_size = int(kw.get("batch_size", 8))
@@ -244,6 +391,9 @@ def predict_and_calculate_metrics(model: EvalModel, task, prediction_kwargs: Opt
     started = time.time()
     if isinstance(task, PerplexityTask):
         out = _score_perplexity(model, task, limit, max_length, batch_size)
+    elif isinstance(task, GenerationTask):
+        out = _score_generation(model, task, limit, max_length, int(kw.get("num_shots", 0)), int(kw.get("fewshot_seed", 1234)),
+                                int(kw.get("num_recorded_inputs", 0)))
     else:
         out = _score_ranked(model, task, limit, batch_size, int(kw.get("num_recorded_inputs", 0)))
     out["processing_time"] = time.time() - started

@@ -136,7 +136,7 @@ def test_shipped_task_sets_name_known_tasks():
         task_set = offline.resolve_task_set(file.stem)
         assert task_set["name"] == file.stem and task_set["tasks"]
         for task in task_set["tasks"]:
-            assert task["task_name"] == "ppl" or task["task_name"] in label_to_task_map, (file.name, task["task_name"])
+            assert task["task_name"] in ("ppl", "gen") or task["task_name"] in label_to_task_map, (file.name, task["task_name"])
 
 
 def test_run_eval_command_line_on_a_checkpoint_folder(tmp_path, monkeypatch):
@@ -241,3 +241,56 @@ def test_rows_are_appended_to_a_sheet_through_a_fake_client():
     assert append_rows_to_gsheet("results", [{"task": "x"}], sheet_title="ppl", client=client) == 1
     assert [s.title for s in client.books["results"].worksheets()] == ["Sheet1", "ppl"]
     assert merge_sheet_rows([], [{"a": 1}]) == [["a"], [1]]
+
+
+def test_generation_metrics_and_task(tmp_path, eval_model, monkeypatch):
+    assert offline.exact_match("The Eiffel Tower.", ["eiffel tower"]) == 1.0 and offline.exact_match("a tower", ["eiffel tower"]) == 0.0
+    assert offline.token_f1("the big red dog", ["red dog", "cat"]) == pytest.approx(2 * (2 / 3) * 1.0 / (2 / 3 + 1.0))
+    assert offline.token_f1("", ["x"]) == 0.0 and offline.token_f1("", [""]) == 1.0
+    # longest common subsequence "quick fox jumps" (3 words) of 4 predicted and 5 reference words
+    assert offline.rouge_l("quick brown fox jumps", ["the quick lazy fox often jumps"]) == pytest.approx(2 * (3 / 4) * (3 / 5) / (3 / 4 + 3 / 5))
+
+    data = tmp_path / "gen" / "toy"
+    data.mkdir(parents=True)
+    rows = [{"input": f"what follows {w}", "answers": [w[::-1], "other"]} for w in ("abc", "def", "ghi", "jkl")]
+    with gzip.open(data / "validation.jsonl.gz", "wt") as f:
+        for r in rows:
+            f.write(json.dumps(r) + "\n")
+    monkeypatch.setenv("EVAL_DATA_PATH", str(tmp_path))
+    task = offline.construct_task("gen", eval_model.tokenizer, {"files": ["gen/toy"], "max_new_tokens": 4, "template": "{input} ->"})
+    assert isinstance(task, offline.GenerationTask) and len(task.examples()) == 4
+
+    prompts = []
+
+    def oracle(prompt_ids, max_new_tokens):  # answers every question correctly except the last, and keeps talking after a newline
+        prompt = eval_model.tokenizer.decode(list(prompt_ids))
+        prompts.append(prompt)
+        word = prompt.rsplit("what follows ", 1)[1].split(" ->")[0]
+        return (" " + word[::-1] if word != "jkl" else " nope") + "\nextra text"
+
+    monkeypatch.setattr(eval_model, "generate_text", oracle)
+    out = offline.predict_and_calculate_metrics(eval_model, task, {"num_shots": 2, "fewshot_seed": 5, "num_recorded_inputs": 1})
+    assert out["num_instances"] == 4 and out["metrics"]["exact_match"] == 0.75 and out["metrics"]["f1"] == 0.75 and out["metrics"]["rouge_l"] == 0.75
+    full = out["recorded_inputs"][0]["prompt"]  # what the model is shown is the tail of this that fits its context
+    assert full.count("->") == 3 and full.endswith("what follows abc ->") and prompts[0] == full[-len(prompts[0]):]
+    assert "what follows abc" not in full.rsplit("\n\n", 1)[0]  # the question itself is never one of its own examples
+    assert out["recorded_inputs"][0]["prediction"] == "cba"
+    limited = offline.predict_and_calculate_metrics(eval_model, task, {"limit": 2})
+    assert limited["num_instances"] == 2 and limited["metrics"]["exact_match"] == 1.0
+
+    # the real generation path of a model wrapper: greedy continuation, decoded, bounded
+    monkeypatch.undo()
+    text = eval_model.generate_text(eval_model.tokenizer.encode("abc", add_special_tokens=False), 5)
+    assert isinstance(text, str) and len(eval_model.tokenizer.encode(text, add_special_tokens=False)) <= 5
+
+
+def test_reference_named_task_sets_resolve():
+    for name in ("rc20_tasks", "gen_tasks", "summary_tasks", "eval_suite_ppl_val_v3", "eval_suite_ppl_val_v3_small", "eval_suite_ppl_val_v2_small"):
+        resolved = offline.resolve_task_set(name)
+        assert resolved["tasks"] and all("task_name" in t for t in resolved["tasks"]), name
+    assert len(offline.resolve_task_set("eval_suite_ppl_val_v3")["tasks"]) == 17
+    from olmo_b200.eval.downstream import label_to_task_map
+
+    assert all(t["task_name"] in label_to_task_map for t in offline.resolve_task_set("rc20_tasks")["tasks"])
+    spec = offline.load_experiment(str(offline.TASK_SET_DIR.parent / "experiments" / "evaluation_2023_07_26.yaml"))
+    assert [ts["name"] for ts in spec["task_sets"]] == ["rc20_tasks", "gen_tasks", "summary_tasks", "eval_suite_ppl_val_v2_small"]
