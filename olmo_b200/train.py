@@ -850,7 +850,12 @@ class Trainer:
                 for batch in self.train_loader:
                     batch_size, seq_len = batch["input_ids"].shape
                     assert seq_len == cfg.model.max_sequence_length
-                    assert batch_size == cfg.device_train_batch_size
+                    if batch_size != cfg.device_train_batch_size:
+                        # the tail of an epoch that does not fill a device batch (the reference asserts here as well)
+                        raise OLMoConfigurationError(
+                            f"a training batch holds {batch_size} instances instead of {cfg.device_train_batch_size}: the epoch does not "
+                            "divide into whole batches; set data.drop_last=true (as the published configs do) to skip the remainder"
+                        )
                     global_batch = batch_size * get_world_size()
                     self.global_step += 1
                     self.global_train_examples_seen_this_epoch += global_batch

@@ -157,3 +157,23 @@ def test_train_script_end_to_end_and_resume(tmp_path):
         logits = model(ids).logits
     loss = torch.nn.functional.cross_entropy(logits[:, :-1].reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
     assert float(loss) < 4.5  # ln(250) = 5.5 at initialisation; the data has ln(16) = 2.8 of entropy
+
+
+def test_fixture_configs_train_from_the_repository_root(tmp_path):
+    """``test_fixtures/train_tiny.yaml`` and ``train_tiny_with_evaluator.yaml`` run as committed (fixture tokenizer and token
+    file, CPU, one epoch of ten batches), and an epoch that does not divide into whole batches is explained instead of
+    tripping a bare assertion."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", OMP_NUM_THREADS="2")
+    for name, expect_eval in (("train_tiny.yaml", False), ("train_tiny_with_evaluator.yaml", True)):
+        env["OLMO_TINY_SAVE_FOLDER"] = str(tmp_path / name)
+        proc = subprocess.run([sys.executable, "scripts/train.py", f"test_fixtures/{name}"], cwd=ROOT, env=env, stdout=subprocess.PIPE,
+                              stderr=subprocess.STDOUT, text=True, timeout=600)
+        assert proc.returncode == 0, proc.stdout[-3000:]
+        assert "Training complete" in proc.stdout and (tmp_path / name / "step4-unsharded" / "model.pt").is_file()
+        assert ("eval/sample-docs/Perplexity" in proc.stdout) == expect_eval
+        losses = [float(x) for x in re.findall(r"train/CrossEntropyLoss=([0-9.]+)", proc.stdout)]
+        assert len(losses) == 10 and losses[-1] < losses[0]
+    env["OLMO_TINY_SAVE_FOLDER"] = str(tmp_path / "short")
+    proc = subprocess.run([sys.executable, "scripts/train.py", "test_fixtures/train_tiny.yaml", "--data.drop_last=false"], cwd=ROOT, env=env,
+                          stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True, timeout=600)
+    assert proc.returncode != 0 and "data.drop_last=true" in proc.stdout
