@@ -224,3 +224,60 @@ def test_state_dict_upgrade_from_single_group():
     assert len(fixed["param_groups"]) == 2 and fixed["param_groups"][1]["weight_decay"] == 0.0
     assert fixed["param_groups"][0]["param_names"] == opt.param_groups[0]["param_names"]
     assert sorted(fixed["param_groups"][0]["params"] + fixed["param_groups"][1]["params"]) == list(range(n))
+
+
+def test_ten_step_trajectory_matches_torch_adamw_with_clip_grad_norm():
+    """A whole training trajectory, not one update: ten steps of this package's AdamW with its own global clipping and
+    a warm-up schedule against ``torch.optim.AdamW`` + ``clip_grad_norm_`` on a copy of the model with the same
+    decay / no-decay groups (the comparison the reference makes in ``tests/grad_norm_test.py:226-262``)."""
+    from copy import deepcopy
+
+    torch.manual_seed(0)
+    max_norm, steps = 1.0, 10
+    cfg = tiny_config(optimizer=OptimizerConfig(name=OptimizerType.adamw, learning_rate=3e-3, weight_decay=0.1, decay_norm_and_bias=False,
+                                                betas=(0.9, 0.95), eps=1e-8),
+                      scheduler=SchedulerConfig(name=SchedulerType.linear_with_warmup, t_warmup=4, alpha_f=0.1, **BASE),
+                      max_grad_norm=max_norm, max_duration=steps)
+    ours = OLMo(cfg.model)
+    ours.reset_parameters()
+    ours.eval()  # dropout off: the two copies must see the same function
+    theirs = deepcopy(ours)
+    opt = build_optimizer(cfg, ours)
+    sched = build_scheduler(cfg)
+    by_name = dict(theirs.named_parameters())
+    torch_opt = torch.optim.AdamW(
+        [{"params": [by_name[n] for n in g["param_names"]], "weight_decay": g["weight_decay"]} for g in opt.param_groups],
+        lr=cfg.optimizer.learning_rate, betas=(0.9, 0.95), eps=1e-8)
+
+    def loss_of(model, ids):
+        logits = model(ids).logits[:, :-1]
+        return torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]), ids[:, 1:].reshape(-1))
+
+    clipped = 0
+    for step in range(1, steps + 1):
+        ids = torch.randint(0, 64, (4, 16))
+        lr = sched.get_lr(cfg.optimizer.learning_rate, step, steps)
+        for group in opt.param_groups:
+            group["lr"] = lr
+            group["max_grad_norm"] = sched.get_max_grad_norm(max_norm, step, steps)
+        for group in torch_opt.param_groups:
+            group["lr"] = lr
+
+        opt.zero_grad(set_to_none=True)
+        a = loss_of(ours, ids)
+        a.backward()
+        metrics = opt.clip_grads_and_collect_metrics(global_step=step, device=torch.device("cpu"))
+        opt.step()
+
+        torch_opt.zero_grad(set_to_none=True)
+        b = loss_of(theirs, ids)
+        b.backward()
+        norm = torch.nn.utils.clip_grad_norm_(theirs.parameters(), max_norm)
+        torch_opt.step()
+
+        clipped += int(float(norm) > max_norm)
+        assert a.item() == pytest.approx(b.item(), rel=1e-5), step
+        assert float(metrics["total_grad_norm"]) == pytest.approx(float(norm), rel=1e-4), step
+        for (name, p), q in zip(ours.named_parameters(), theirs.parameters()):
+            torch.testing.assert_close(p, q, rtol=2e-5, atol=2e-6, msg=lambda m: f"step {step}, {name}: {m}")
+    assert clipped > 0  # the clipping branch was exercised, not only the pass-through
