@@ -959,9 +959,11 @@ def build_sharded_checkpointer(cfg: TrainConfig, *, name: Optional[ShardedCheckp
     """The sharded checkpointer of this framework.
 
     ``sharded_checkpointer`` (``torch_new``, ``torch_legacy``, ``local``, ``olmo_core``) names layouts of the reference's
-    FSDP1 checkpointers.  This engine has no FSDP1 flat parameters or ``ShardedTensor`` objects to serialise, so every
-    value *writes* the one flat-shard layout described in :class:`FlatShardCheckpointer`; the key is accepted so that
-    reference configs load unchanged.  On the *read* side the layout of a directory is detected, and checkpoints written
+    FSDP1 checkpointers.  This engine has no FSDP1 flat parameters or ``ShardedTensor`` objects to serialise, so by
+    default every value *writes* the one flat-shard layout described in :class:`FlatShardCheckpointer`; the key is
+    accepted so that reference configs load unchanged.  The exception is opt-in: ``torch_new`` together with
+    ``OLMO_B200_WRITE_REFERENCE_LAYOUT=1`` in the environment selects :class:`TorchNewStyleShardedCheckpointer`, which
+    writes the reference's ``torch_new`` layout.  On the *read* side the layout of a directory is detected, and checkpoints written
     by the reference in the ``torch_new``, ``torch_legacy`` and ``local`` layouts are restored, resharded or unsharded
     (:mod:`olmo_b200.checkpoint_compat`); ``olmo_core`` directories raise an error that says what to do."""
     del use_shared_mem_impl

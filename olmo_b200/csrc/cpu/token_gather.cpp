@@ -92,7 +92,7 @@ void ob_token_store_close(void* handle) {
 int ob_token_store_read(void* handle, const int32_t* file, const int64_t* chunk, int64_t n, int64_t chunk_tokens, int itemsize,
                         int64_t* out, int threads, int64_t* failed_at) {
   Store* s = static_cast<Store*>(handle);
-  if (s == nullptr || n < 0 || chunk_tokens <= 0 || out == nullptr || (n > 0 && (file == nullptr || chunk == nullptr))) return -1;
+  if (s == nullptr || n < 0 || chunk_tokens <= 0 || (n > 0 && (out == nullptr || file == nullptr || chunk == nullptr))) return -1;
   if (itemsize != 1 && itemsize != 2 && itemsize != 4 && itemsize != 8) return -1;
   for (int64_t i = 0; i < n; ++i)
     if (file[i] < 0 || file[i] >= static_cast<int32_t>(s->paths.size()) || chunk[i] < 0) return -1;

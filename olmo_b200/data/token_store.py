@@ -150,6 +150,8 @@ class TokenStore:
         if out is None:
             out = torch.empty((n, self.chunk), dtype=torch.int64, pin_memory=pin_memory and torch.cuda.is_available())
         assert out.shape == (n, self.chunk) and out.dtype == torch.int64 and out.is_contiguous() and not out.is_cuda
+        if n == 0:
+            return out
         lib = self._native()
         if lib is not None:
             failed = ctypes.c_int64(-1)

@@ -25,8 +25,6 @@ from ..config import (
     FSDPWrapStrategy,
     InitFnType,
     ModelConfig,
-    ShardedCheckpointerType,
-    TrainConfig,
 )
 from ..exceptions import OLMoConfigurationError
 from ..initialization import init_normal

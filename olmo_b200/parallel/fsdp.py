@@ -55,7 +55,7 @@ import math
 import os
 from contextlib import contextmanager
 from dataclasses import dataclass, field
-from typing import Any, Callable, Dict, Iterable, Iterator, List, Optional, Sequence, Tuple
+from typing import Any, Dict, Iterator, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -70,7 +70,7 @@ from ..config import (
 from ..exceptions import OLMoConfigurationError
 from ..models.blocks import OLMoBlock, should_checkpoint_block
 from ..models.olmo import OLMo, OLMoOutput
-from ..torch_util import get_global_rank, get_world_size, is_distributed, nvtx_range
+from ..torch_util import get_global_rank, get_world_size, nvtx_range
 
 __all__ = ["FlatShardEngine", "ShardedModel", "Unit", "ParamSlot", "build_sharded_model"]
 

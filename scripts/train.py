@@ -24,7 +24,7 @@ from olmo_b200.config import CheckpointType, DistributedStrategy, TrainConfig
 from olmo_b200.exceptions import OLMoCliError, OLMoConfigurationError
 from olmo_b200.launch import build_trainer, derive_batch_sizes
 from olmo_b200.optim import BoltOnWarmupScheduler
-from olmo_b200.torch_util import barrier, get_global_rank, get_local_rank, get_world_size, peak_gpu_memory, seed_all
+from olmo_b200.torch_util import barrier, get_global_rank, get_local_rank, peak_gpu_memory, seed_all
 from olmo_b200.util import add_cached_path_clients, clean_opt, find_latest_checkpoint, log_extra_field, prepare_cli_environment
 
 log = logging.getLogger("train")

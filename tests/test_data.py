@@ -265,3 +265,42 @@ def test_synthetic_tokens_are_reproducible():
     assert not torch.equal(a, ds[4]["input_ids"])
     batch = ds.batch(8, 4)
     assert batch.shape == (4, 64) and torch.equal(batch[0], ds[8]["input_ids"])
+
+
+def test_iterable_dataset_partition_property(monkeypatch):
+    """Property test over dataset size, world size, worker count, device batch size, ``drop_last`` and restart point:
+    the slices taken by all ranks and all their data-loader workers are disjoint positions of the global order and
+    together cover exactly what is left of it; every rank gets the same number of instances."""
+    from collections import Counter
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=60, deadline=None)
+    @given(n=st.integers(1, 90), world=st.integers(1, 5), workers=st.integers(0, 3), device_bs=st.integers(1, 4), drop_last=st.booleans(),
+           consumed_batches=st.integers(0, 6), seed=st.integers(0, 99))
+    def check(n, world, workers, device_bs, drop_last, consumed_batches, seed):
+        data = [{"v": i} for i in range(n)]
+        kw = dict(global_batch_size=device_bs * world, seed=seed, world_size=world, drop_last=drop_last, num_threads=0)
+        whole = IterableDataset(data, rank=0, **kw)
+        order = [int(i) for i in whole.get_global_indices()]
+        assert len(order) == whole.total_size and whole.total_size % world == 0
+        if drop_last:
+            assert whole.total_size <= n and len(set(order)) == len(order)
+        else:
+            assert whole.total_size >= n and set(order) == set(range(n))  # padding repeats instances, never drops one
+        start = min(consumed_batches * device_bs * world, whole.total_size)
+        seen, per_rank = Counter(), []
+        for rank in range(world):
+            ds = IterableDataset(data, rank=rank, start_index=start, **kw)
+            count = 0
+            for wid in range(max(workers, 1)):
+                monkeypatch.setattr(torch.utils.data, "get_worker_info", (lambda wid=wid: _Info(wid, workers)) if workers else (lambda: None))
+                got = [item["index"] for item in ds]
+                seen.update(got)
+                count += len(got)
+            per_rank.append(count)
+        assert seen == Counter(order[start:])
+        assert len(set(per_rank)) == 1
+
+    check()

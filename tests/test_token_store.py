@@ -91,3 +91,46 @@ def test_dataset_batches_match_single_items(tmp_path):
     np.zeros(7, dtype=np.bool_).tofile(masks[0])
     with pytest.raises(ValueError, match="same size"):
         len(MemMapDataset(*paths, chunk_size=chunk, label_mask_paths=masks))
+
+
+def test_locate_and_read_against_brute_force_on_random_layouts(tmp_path):
+    """Property test: for random file lengths (files shorter than a chunk and empty files included), chunk sizes and
+    index sets, ``locate`` agrees with walking the files one by one, and ``read`` returns exactly the tokens numpy sees."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    counter = [0]
+
+    @settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture])
+    @given(lengths=st.lists(st.integers(0, 70), min_size=1, max_size=6), chunk=st.integers(1, 9), seed=st.integers(0, 2**16))
+    def check(lengths, chunk, seed):
+        counter[0] += 1
+        folder = tmp_path / f"case{counter[0]}"
+        folder.mkdir()
+        rng = np.random.default_rng(seed)
+        paths, arrays = [], []
+        for i, n in enumerate(lengths):
+            arr = rng.integers(0, 60000, size=n, dtype=np.uint16)
+            arr.tofile(folder / f"f{i}.npy")
+            paths.append(str(folder / f"f{i}.npy"))
+            arrays.append(arr)
+        store = ts.TokenStore(paths, np.uint16, chunk, threads=3)
+        expected = [(f, c) for f, arr in enumerate(arrays) for c in range(len(arr) // chunk)]
+        assert len(store) == len(expected)
+        assert store.chunks_per_file().tolist() == [len(a) // chunk for a in arrays]
+        if not expected:
+            assert store.read([]).shape == (0, chunk)
+            with pytest.raises(IndexError):
+                store.locate([0])
+            return
+        picks = rng.integers(-len(expected), len(expected), size=min(12, 2 * len(expected)))
+        files, chunks = store.locate(picks)
+        assert [(int(f), int(c)) for f, c in zip(files, chunks)] == [expected[int(i)] for i in picks]
+        got = store.read(picks)
+        want = np.stack([arrays[f][c * chunk:(c + 1) * chunk].astype(np.int64) for f, c in (expected[int(i)] for i in picks)])
+        assert got.dtype == torch.int64 and np.array_equal(got.numpy(), want)
+        with pytest.raises(IndexError):
+            store.locate([len(expected)])
+        store.close()
+
+    check()
