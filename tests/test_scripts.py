@@ -540,3 +540,47 @@ def test_ladder_power_law_fit_recovers_a_known_law():
     fit = ladder_fit(results, by="size", hold_out=1)
     held = [p for p in fit["points"] if p["held_out"]]
     assert len(held) == 1 and held[0]["run"] == "base-1B-2xC" and abs(held[0]["predicted"] - held[0]["loss"]) < 1e-2
+
+
+@pytest.mark.parametrize("run, env", [
+    ("peteish1", {"STORAGE": "google"}),
+    ("peteish7", {"STORAGE": "s3"}),
+    ("peteish7-medlr", {}),
+    ("peteish13", {"NNODES": "4", "REMOTE_ROOT": "gs://bucket/checkpoints"}),
+    ("peteish13-medlr", {}),
+    ("peteish13-highlr", {}),
+    ("peteish7-lr-anneal", {"START_STEP": "477000", "START_LR": "2.1e-4", "LOAD_PATH": "/ckpt/step477000", "ANNEAL_TOKENS": "50e9"}),
+    ("anneal", {"CONFIG": "configs/annealing/OLMo2-7B-anneal-example.yaml", "SEED": "42"}),
+    ("tiny", {"SIZE": "60M"}),
+])
+def test_published_run_launcher_builds_a_valid_command(run, env, tmp_path):
+    """The launcher's dry run prints the command of a published run; its config exists and every override it passes is
+    a key of the configuration schema (the settings come from ``scripts/beaker/peteish/*.sh`` and ``scripts/augusta/*.sh``)."""
+    from olmo_b200.config import TrainConfig
+    from olmo_b200.util import clean_opt
+
+    full_env = {**os.environ, "DRY_RUN": "1", "CHECKPOINT_ROOT": str(tmp_path), **env}
+    full_env.pop("BEAKER_REPLICA_COUNT", None)
+    out = subprocess.run(["bash", str(SCRIPTS / "launch" / "published_runs.sh"), run, "--global_train_batch_size=64"], env=full_env, cwd=ROOT,
+                         capture_output=True, text=True)
+    assert out.returncode == 0, out.stderr
+    words = out.stdout.split("\n")[:-1]
+    assert words[0].endswith("launch/beaker.sh") and Path(words[0]).is_file()
+    config, overrides = words[1], words[2:]
+    assert Path(config).is_file() and overrides[-1] == "--global_train_batch_size=64"
+    cfg = TrainConfig.load(config, [clean_opt(o) for o in overrides], validate_paths=False)
+    assert cfg.run_name == run and cfg.save_folder == f"{tmp_path}/{run}" and cfg.try_load_latest_save and cfg.global_train_batch_size == 64
+    if env.get("NNODES"):
+        assert str(cfg.fsdp.sharding_strategy).endswith("HYBRID_SHARD") and cfg.fsdp.hybrid_sharding_num_model_replicas == 4
+        assert cfg.remote_save_folder == f"gs://bucket/checkpoints/{run}/"
+    if run == "peteish7-lr-anneal":
+        assert cfg.max_duration == 477000 + round(50e9 / (1024 * 4096)) and cfg.stop_at == cfg.max_duration + 10
+        assert cfg.scheduler.t_warmup == 477000 and cfg.scheduler.alpha_f == 0 and cfg.load_path == "/ckpt/step477000"
+    if run == "anneal":
+        assert cfg.seed == 42 and cfg.no_pre_train_checkpoint
+
+
+def test_published_run_launcher_rejects_unknown_runs():
+    out = subprocess.run(["bash", str(SCRIPTS / "launch" / "published_runs.sh"), "peteish99"], env={**os.environ, "DRY_RUN": "1"}, cwd=ROOT,
+                         capture_output=True, text=True)
+    assert out.returncode == 2 and "unknown run" in out.stderr
