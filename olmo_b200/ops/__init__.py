@@ -103,10 +103,9 @@ def lib() -> ctypes.CDLL:
         if is_stale():
             if shutil.which("nvcc") or Path("/usr/local/cuda/bin/nvcc").exists():
                 build()
-            elif not _SO_PATH.exists():
-                raise OLMoEnvironmentError(
-                    f"{_SO_PATH} is missing and nvcc is unavailable; run `python -m olmo_b200.ops` where nvcc exists"
-                )
+            else:
+                state = "does not match the sources under csrc/ (stale build)" if _SO_PATH.exists() else "is missing"
+                raise OLMoEnvironmentError(f"{_SO_PATH} {state} and nvcc is unavailable; run `python -m olmo_b200.ops` where nvcc exists")
         _lib = ctypes.CDLL(str(_SO_PATH))
         _lib.ob_set_gemm_pair_mode(ctypes.c_int(int(os.environ.get("OLMO_B200_GEMM_2CTA", "1") not in ("0", "", "false"))))
         _lib.ob_set_gemm_tma_store(ctypes.c_int(int(os.environ.get("OLMO_B200_GEMM_TMA_STORE", "1") not in ("0", "", "false"))))
