@@ -25,7 +25,7 @@ from enum import Enum
 from pathlib import Path
 from queue import Queue
 from threading import Thread
-from typing import Any, Callable, Dict, Iterable, Iterator, MutableMapping, Optional, Tuple, Union
+from typing import Any, Callable, Dict, Iterable, Iterator, List, MutableMapping, Optional, Sequence, Tuple, Union
 from urllib.parse import urlparse
 
 from .aliases import PathOrStr
@@ -51,6 +51,7 @@ __all__ = [
     "set_env_variables",
     "prepare_cli_environment",
     "clean_opt",
+    "positional_args",
     "wait_for",
     "is_url",
     "dir_is_empty",
@@ -271,6 +272,19 @@ def clean_opt(arg: str) -> str:
         val = "True"
     key = key.strip("-").replace("-", "_")
     return f"{key}={val}"
+
+
+def positional_args(doc: Optional[str], minimum: int, argv: Optional[Sequence[str]] = None) -> List[str]:
+    """The arguments of a small positional-argument script: ``-h`` / ``--help`` prints ``doc`` and exits 0, fewer than
+    ``minimum`` arguments print it to stderr and exit 2; otherwise ``argv[1:]`` is returned."""
+    args = list(sys.argv[1:] if argv is None else argv)
+    if any(a in ("-h", "--help") for a in args):
+        print((doc or "").strip())
+        raise SystemExit(0)
+    if len(args) < minimum:
+        print((doc or "").strip(), file=sys.stderr)
+        raise SystemExit(2)
+    return args
 
 
 def wait_for(condition: Callable[[], bool], description: str, timeout: float = 10.0) -> None:

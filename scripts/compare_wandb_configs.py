@@ -7,7 +7,7 @@ from pathlib import Path
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
-from olmo_b200.util import flatten_dict
+from olmo_b200.util import flatten_dict, positional_args
 
 NOISE = re.compile(r"(save_folder|remote_save_folder|load_path|run_name|wandb\.|time_limit|_wandb)")
 
@@ -30,11 +30,10 @@ def diff(a: dict, b: dict, show_noise: bool = False):
 
 
 if __name__ == "__main__":
-    if len(sys.argv) < 3:
-        raise SystemExit(__doc__)
+    args = positional_args((__doc__ or "") + "\n\n    python scripts/compare_wandb_configs.py RUN_A RUN_B [--all]", 2)
     import wandb
 
     api = wandb.Api()
-    left, right = (api.run(parse_run_path(s)) for s in sys.argv[1:3])
-    for key, va, vb in diff(left._attrs["rawconfig"], right._attrs["rawconfig"], "--all" in sys.argv):
+    left, right = (api.run(parse_run_path(s)) for s in args[:2])
+    for key, va, vb in diff(left._attrs["rawconfig"], right._attrs["rawconfig"], "--all" in args):
         print(f"{key}\n\t{va}\n\t{vb}")

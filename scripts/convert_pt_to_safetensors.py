@@ -9,11 +9,10 @@ sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 import torch
 
 from olmo_b200.safetensors_util import state_dict_to_safetensors_file
+from olmo_b200.util import positional_args
 
 if __name__ == "__main__":
-    if len(sys.argv) < 2:
-        raise SystemExit(__doc__)
-    for name in sys.argv[1:]:
+    for name in positional_args(__doc__, 1):
         src = Path(name)
         state = torch.load(src, map_location="cpu", weights_only=False)
         dst = src.with_suffix(".safetensors")

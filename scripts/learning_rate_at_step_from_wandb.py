@@ -8,13 +8,17 @@ import sys
 from pathlib import Path
 
 sys.path.insert(0, str(Path(__file__).resolve().parent))
+sys.path.insert(1, str(Path(__file__).resolve().parent.parent))
 from compare_wandb_configs import parse_run_path
 
+from olmo_b200.util import positional_args
+
 if __name__ == "__main__":
+    run_path, step_text = positional_args(__doc__, 2)[:2]
     import wandb
 
-    run = wandb.Api().run(parse_run_path(sys.argv[1]))
-    step = int(sys.argv[2])
+    run = wandb.Api().run(parse_run_path(run_path))
+    step = int(step_text)
     key = "optim/learning_rate_group0"
     rows = run.scan_history(keys=[key, "_step"], min_step=step, max_step=step + 1, page_size=5)
     for row in rows:

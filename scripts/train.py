@@ -141,6 +141,12 @@ def init_distributed() -> None:
 
 
 if __name__ == "__main__":
+    if len(sys.argv) < 2 or sys.argv[1] in ("-h", "--help"):
+        print(f"{(__doc__ or '').strip()}\n\nEvery key of the configuration (olmo_b200/config.py: TrainConfig) can be overridden, for example\n"
+              "  --run_name=NAME --save_folder=DIR --load_path=DIR_OR_URL --try_load_latest_save --model.n_layers=16\n"
+              "  --optimizer.learning_rate=3e-4 --global_train_batch_size=1024 --device_train_microbatch_size=2\n"
+              "  --fsdp.sharding_strategy=FULL_SHARD|HYBRID_SHARD|NO_SHARD --distributed_strategy=fsdp|ddp|single")
+        raise SystemExit(0 if len(sys.argv) >= 2 else 2)
     try:
         mp.set_start_method("spawn", force=True)
     except RuntimeError as e:

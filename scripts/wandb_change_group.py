@@ -5,13 +5,16 @@
 """
 import re
 import sys
+from pathlib import Path
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from olmo_b200.util import positional_args
 
 if __name__ == "__main__":
-    if len(sys.argv) < 4:
-        raise SystemExit(__doc__)
+    project, pattern, group = positional_args(__doc__, 3)[:3]
     import wandb
 
-    project, pattern, group = sys.argv[1:4]
     for run in wandb.Api().runs(project):
         if re.search(pattern, run.name):
             print(f"{run.name}: {run.group} -> {group}")

@@ -584,3 +584,31 @@ def test_published_run_launcher_rejects_unknown_runs():
     out = subprocess.run(["bash", str(SCRIPTS / "launch" / "published_runs.sh"), "peteish99"], env={**os.environ, "DRY_RUN": "1"}, cwd=ROOT,
                          capture_output=True, text=True)
     assert out.returncode == 2 and "unknown run" in out.stderr
+
+
+def test_every_script_answers_help():
+    """``--help`` prints a usage text and exits 0 for every entry point under ``scripts/`` (none of them starts work,
+    opens a file called ``--help`` or contacts a service first)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    def ask(script):
+        out = subprocess.run([sys.executable, str(script), "--help"], capture_output=True, text=True, cwd=ROOT, timeout=600)
+        if out.returncode != 0 or not out.stdout.strip():
+            return script.name, out.returncode, out.stderr.strip().splitlines()[-1:] or out.stdout[-200:]
+        return None
+
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
+        failures = [f for f in pool.map(ask, sorted(SCRIPTS.glob("*.py"))) if f is not None]
+    assert not failures, failures
+
+
+def test_positional_args_helper(capsys):
+    from olmo_b200.util import positional_args
+
+    assert positional_args("doc", 2, ["a", "b", "--flag"]) == ["a", "b", "--flag"]
+    with pytest.raises(SystemExit) as e:
+        positional_args("the usage", 2, ["a"])
+    assert e.value.code == 2 and "the usage" in capsys.readouterr().err
+    with pytest.raises(SystemExit) as e:
+        positional_args("the usage", 0, ["-h"])
+    assert e.value.code == 0 and "the usage" in capsys.readouterr().out
