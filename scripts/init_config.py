@@ -41,6 +41,9 @@ def main(save_path: Path, overrides: List[str], recipe: Optional[str] = None) ->
 if __name__ == "__main__":
     prepare_cli_environment()
     argv = sys.argv[1:]
+    if "-h" in argv or "--help" in argv:
+        print((__doc__ or "").strip())
+        sys.exit(0)
     if "--list" in argv:
         from olmo_b200.recipes import RECIPES
 
@@ -55,4 +58,6 @@ if __name__ == "__main__":
         del argv[at : at + 2]
     if not argv:
         raise OLMoCliError(f"Usage: {sys.argv[0]} SAVE_PATH [--from RECIPE] [OPTIONS]")
+    if argv[0].startswith("-"):
+        raise OLMoCliError(f"the first argument is the file to write, not an option ('{argv[0]}')")
     main(Path(argv[0]), [clean_opt(s) for s in argv[1:]], recipe)

@@ -9,4 +9,4 @@ sys.path.insert(0, str(Path(__file__).resolve().parent))
 from release import main
 
 if __name__ == "__main__":
-    sys.exit(main(["stamp"]))
+    sys.exit(main(["stamp", *sys.argv[1:]]))  # no options of its own: anything else (``--help`` too) goes to the parser

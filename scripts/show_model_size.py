@@ -70,6 +70,9 @@ def main(cfg: TrainConfig) -> Dict[str, int]:
 
 if __name__ == "__main__":
     prepare_cli_environment()
+    if len(sys.argv) >= 2 and sys.argv[1] in ("-h", "--help"):
+        print(f"{(__doc__ or '').strip()}\n\nUsage: {sys.argv[0]} CONFIG_PATH [--dotted.key=value ...]")
+        sys.exit(0)
     if len(sys.argv) < 2:
         raise OLMoCliError(f"Usage: {sys.argv[0]} CONFIG_PATH [OPTIONS]")
     main(TrainConfig.load(sys.argv[1], [clean_opt(s) for s in sys.argv[2:]], validate_paths=False))

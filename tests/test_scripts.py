@@ -586,13 +586,16 @@ def test_published_run_launcher_rejects_unknown_runs():
     assert out.returncode == 2 and "unknown run" in out.stderr
 
 
-def test_every_script_answers_help():
-    """``--help`` prints a usage text and exits 0 for every entry point under ``scripts/`` (none of them starts work,
-    opens a file called ``--help`` or contacts a service first)."""
+def test_every_script_answers_help(tmp_path):
+    """``--help`` prints a usage text and exits 0 for every entry point under ``scripts/``, and does nothing else: no
+    file appears in the working directory (one script used to write a config named ``--help``), the changelog is not
+    stamped, no service is contacted."""
     from concurrent.futures import ThreadPoolExecutor
 
+    changelog = (ROOT / "CHANGELOG.md").read_text()
+
     def ask(script):
-        out = subprocess.run([sys.executable, str(script), "--help"], capture_output=True, text=True, cwd=ROOT, timeout=600)
+        out = subprocess.run([sys.executable, str(script), "--help"], capture_output=True, text=True, cwd=tmp_path, timeout=600)
         if out.returncode != 0 or not out.stdout.strip():
             return script.name, out.returncode, out.stderr.strip().splitlines()[-1:] or out.stdout[-200:]
         return None
@@ -600,6 +603,7 @@ def test_every_script_answers_help():
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as pool:
         failures = [f for f in pool.map(ask, sorted(SCRIPTS.glob("*.py"))) if f is not None]
     assert not failures, failures
+    assert list(tmp_path.iterdir()) == [] and (ROOT / "CHANGELOG.md").read_text() == changelog
 
 
 def test_positional_args_helper(capsys):
