@@ -391,10 +391,14 @@ def build(cls: Type, data: Optional[Dict[str, Any]] = None, where: str = "") -> 
     fields = {f.name: f for f in dataclasses.fields(cls) if f.init}
     unknown = [k for k in data if k not in fields]
     if unknown:
+        import difflib
+
         prefix = f"{where}." if where else ""
+        near = difflib.get_close_matches(str(unknown[0]), list(fields), n=2, cutoff=0.7)
         raise OLMoConfigurationError(
             f"Key '{prefix}{unknown[0]}' is not in struct {cls.__name__}"
             + (f" (also: {unknown[1:]})" if len(unknown) > 1 else "")
+            + (f"; did you mean {' or '.join(repr(prefix + n) for n in near)}?" if near else "")
         )
     kwargs: Dict[str, Any] = {}
     for name, f in fields.items():

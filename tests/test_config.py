@@ -232,3 +232,11 @@ def test_development_anneal_and_micro_anneal_recipes_are_generated():
     big = recipe_config("peteish13-anneal-from-596057-300B-legal-whammy-2-google")
     assert big.model.d_model == 5120 and big.stop_at == 35773 and big.max_duration == "300e9T" and big.global_train_batch_size == 2048
     assert recipe_config("peteish1-weka").scheduler.t_max == 3e12 and recipe_config("peteish7-s3").activation_checkpointing is None
+
+
+def test_unknown_key_names_the_nearest_field():
+    with pytest.raises(OLMoConfigurationError, match=r"Key 'optimizer.learning_rat' is not in struct OptimizerConfig; did you mean 'optimizer.learning_rate'\?"):
+        TrainConfig.new(optimizer={"learning_rat": 1e-3})
+    with pytest.raises(OLMoConfigurationError) as e:
+        TrainConfig.new(zzz_nothing_like_it=1)
+    assert "did you mean" not in str(e.value)
