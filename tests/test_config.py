@@ -240,3 +240,80 @@ def test_unknown_key_names_the_nearest_field():
     with pytest.raises(OLMoConfigurationError) as e:
         TrainConfig.new(zzz_nothing_like_it=1)
     assert "did you mean" not in str(e.value)
+
+
+def test_random_overrides_round_trip_through_dotlist_and_yaml(tmp_path):
+    """Property test over the whole schema: random values for randomly chosen scalar fields (at any depth, every scalar
+    type the schema has: int, float, bool, str, enums and their Optional forms), given as dotted command-line overrides,
+    land in the right field with the right type, survive ``save`` + ``load``, and leave every other field at its default."""
+    import dataclasses
+    import typing
+    from enum import Enum
+
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    from olmo_b200.utils import structured as S
+
+    def scalar_fields(cls, prefix=""):
+        hints = S._hints(cls)
+        for f in dataclasses.fields(cls):
+            if not f.init:
+                continue
+            tp = hints[f.name]
+            args = [a for a in typing.get_args(tp) if a is not type(None)] if typing.get_origin(tp) is typing.Union else [tp]
+            optional = type(None) in typing.get_args(tp)
+            if len(args) != 1:
+                continue
+            inner = args[0]
+            if dataclasses.is_dataclass(inner):
+                if not optional:  # optional sub-configs default to None; setting one field would create the rest
+                    yield from scalar_fields(inner, f"{prefix}{f.name}.")
+            elif inner in (int, float, bool, str) or (isinstance(inner, type) and issubclass(inner, Enum)):
+                yield f"{prefix}{f.name}", inner, optional
+
+    fields = list(scalar_fields(TrainConfig))
+    assert len(fields) > 100 and {tp for _, tp, _ in fields} >= {int, float, bool, str}
+    defaults = TrainConfig.new().asdict()
+
+    def value_for(tp, optional):
+        if isinstance(tp, type) and issubclass(tp, Enum):
+            base = st.sampled_from(list(tp))
+        else:
+            base = {int: st.integers(0, 10**9), bool: st.booleans(),
+                    float: st.one_of(st.floats(1e-9, 1e9, allow_nan=False), st.sampled_from([0.0, 1e-5, 3e-4, 0.95, 1.0])),
+                    str: st.text(alphabet="abcdefgh_-/.XYZ", min_size=1, max_size=12).filter(lambda t: t.strip("-. ") == t and not t[0].isdigit())}[tp]
+        return st.one_of(st.none(), base) if optional else base
+
+    picks = st.lists(st.sampled_from(fields), min_size=1, max_size=6, unique_by=lambda f: f[0]).flatmap(
+        lambda chosen: st.tuples(*[st.tuples(st.just(name), st.just(tp), value_for(tp, opt)) for name, tp, opt in chosen]))
+
+    def lookup(tree, dotted):
+        for part in dotted.split("."):
+            tree = tree[part]
+        return tree
+
+    def plain(v):
+        return v.value if isinstance(v, Enum) else v
+
+    @settings(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.too_slow, HealthCheck.function_scoped_fixture])
+    @given(picks)
+    def check(chosen):
+        overrides = []
+        for name, tp, value in chosen:
+            text = "null" if value is None else repr(value) if tp is float else str(plain(value)).lower() if tp is bool else str(plain(value))
+            overrides.append(f"{name}={text}")
+        cfg = TrainConfig.new(**S.parse_dotlist(overrides))
+        path = tmp_path / "cfg.yaml"
+        cfg.save(path)
+        again = TrainConfig.load(path, validate_paths=False)
+        for tree in (cfg.asdict(), again.asdict()):
+            for name, tp, value in chosen:
+                got = plain(lookup(tree, name))
+                assert got == plain(value) and (value is None or type(got) is type(plain(value))), (name, got, value)
+        touched = {name for name, _, _ in chosen}
+        for name, _, _ in fields:
+            if name not in touched:
+                assert plain(lookup(again.asdict(), name)) == plain(lookup(defaults, name)), name
+
+    check()
