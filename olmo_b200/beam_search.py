@@ -425,7 +425,17 @@ class BeamSearch:
         if self.min_steps >= 1:
             first_scores[:, end] = _lowest(first_scores)
 
-        beam_scores, tokens, sampler_state = self.sampler.sample_beams(first_scores, B, sampler_state)
+        if B > vocab:
+            # More beams than first tokens: take every token once and fill the spare beams with finished sequences of
+            # score -inf, which can never displace a real candidate.  (Only meaningful for the deterministic sampler;
+            # the stochastic ones keep per-beam state that cannot be padded.)
+            if type(self.sampler) is not DeterministicSampler:
+                raise ValueError(f"beam_size ({B:d}) exceeds the vocabulary size ({vocab:d}); decrease beam_size")
+            beam_scores, tokens, sampler_state = self.sampler.sample_beams(first_scores, vocab, sampler_state)
+            beam_scores = torch.cat([beam_scores, beam_scores.new_full((batch, B - vocab), float("-inf"))], dim=1)
+            tokens = torch.cat([tokens, tokens.new_full((batch, B - vocab), end)], dim=1)
+        else:
+            beam_scores, tokens, sampler_state = self.sampler.sample_beams(first_scores, B, sampler_state)
         if B == 1 and bool((tokens == end).all()):
             warnings.warn(
                 "Empty sequences predicted. You may want to increase the beam size or ensure "

@@ -351,3 +351,55 @@ def test_ngram_blocking_end_to_end():
     expect(*go(3, 5), [[1, 2, 3, 1, 3], [1, 2, 3, 1, 2]], [0.24, 0.16])
     # finished beams keep emitting the end token even though a unigram constraint would block it
     expect(*go(1, 10), [[1, 3, 5, 5], [1, 2, 3, 5]], [0.6e-9, 0.4e-9])
+
+
+def test_wide_beam_equals_exhaustive_enumeration_on_random_chains():
+    """Property test: with a beam as wide as the number of distinct sequences, beam search is exhaustive, so on a random
+    Markov chain its ranked output must equal a brute-force enumeration of all sequences (a sequence stops at the end
+    token; the score is the sum of its transition log-probabilities up to and including the end token)."""
+    import itertools
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=25, deadline=None)
+    @given(vocab=st.integers(2, 4), steps=st.integers(1, 3), seed=st.integers(0, 10**6), batch=st.integers(1, 2))
+    def check(vocab, steps, seed, batch):
+        g = torch.Generator().manual_seed(seed)
+        chain = torch.softmax(3 * torch.randn(vocab, vocab, generator=g), dim=-1).log()  # row: last token, column: next
+        end = vocab - 1
+        starts = torch.randint(0, vocab - 1, (batch,), generator=g)
+
+        def brute(start):
+            found = {}
+            for seq in itertools.product(range(vocab), repeat=steps):
+                score, last, out = 0.0, start, []
+                for tok in seq:
+                    score += float(chain[last, tok])
+                    out.append(tok)
+                    last = tok
+                    if tok == end:
+                        break
+                out = tuple(out + [end] * (steps - len(out)))  # a finished beam keeps emitting the end token at no cost
+                found[out] = score
+            return sorted(found.items(), key=lambda kv: -kv[1])
+
+        beam = vocab**steps
+        search = BeamSearch(end, max_steps=steps, beam_size=beam, per_node_beam_size=vocab)
+        with quiet():
+            preds, scores = search.search(starts, {}, lambda last, state, t: (chain[last], state))
+        for b in range(batch):
+            want = brute(int(starts[b]))
+            got = [(tuple(int(x) for x in preds[b, i]), float(scores[b, i])) for i in range(beam) if float(scores[b, i]) > -1e30]  # spare beams carry -inf or the 'negligible' floor
+            seen = {}
+            for seq, score in got:  # duplicates of a finished sequence may fill spare beams; keep the first (best) of each
+                seen.setdefault(seq, score)
+            ranked = list(seen.items())
+            assert [s for _, s in ranked] == sorted((s for _, s in ranked), reverse=True)
+            assert len(ranked) == len(want)
+            for (seq_a, score_a), (seq_b, score_b) in zip(ranked, want):
+                assert score_a == pytest.approx(score_b, abs=1e-4)
+            assert dict(ranked).keys() == dict(want).keys()
+            assert ranked[0][0] == want[0][0] or ranked[0][1] == pytest.approx(want[1][1], abs=1e-5)
+
+    check()
