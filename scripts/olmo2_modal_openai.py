@@ -44,12 +44,14 @@ try:  # the Modal deployment exists only where the package does
 except ImportError:
     modal = None
 
+IMAGE_SOURCE_DIR = "/opt/olmo"  # where the two packages are copied inside the container image
+
 if modal is not None:
     image = (
         modal.Image.from_registry("nvidia/cuda:12.9.0-devel-ubuntu24.04", add_python="3.12")
         .pip_install("torch", "numpy", "pyyaml", "tokenizers", "fastapi", "uvicorn", "safetensors")
-        .add_local_dir(str(ROOT / "olmo_b200"), "/root/olmo_b200")
-        .add_local_dir(str(ROOT / "olmo_data"), "/root/olmo_data")
+        .add_local_dir(str(ROOT / "olmo_b200"), f"{IMAGE_SOURCE_DIR}/olmo_b200")
+        .add_local_dir(str(ROOT / "olmo_data"), f"{IMAGE_SOURCE_DIR}/olmo_data")
     )
     app = modal.App(APP_NAME)
 
@@ -58,7 +60,7 @@ if modal is not None:
     @modal.concurrent(max_inputs=256)
     @modal.asgi_app()
     def serve():
-        sys.path.insert(0, "/root")
+        sys.path.insert(0, IMAGE_SOURCE_DIR)
         return build_asgi_app()
 
 
