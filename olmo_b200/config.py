@@ -678,40 +678,58 @@ def _env_flag(name: str, default: bool) -> bool:
 class B200Runtime:
     """
     Knobs specific to this framework.  They are environment variables, not config keys, so a saved
-    ``config.yaml`` stays loadable by the reference.
+    ``config.yaml`` stays loadable by the reference.  Each is read where it acts (the module is named); this class
+    gathers the ones that select a code path, for logging at start-up (``B200Runtime.from_env()``).
 
-    ``OLMO_B200_KERNELS``        use the sm_100a extension on CUDA devices (default on; the extension
-                                 being absent on a GPU box is an error, not a silent fallback).
-    ``OLMO_B200_FUSED_COMM``     fuse all-gather into the consuming GEMM and reduce-scatter into the
-                                 optimizer (default on when world size > 1).
-    ``OLMO_B200_MULTIMEM``       use NVLS ``multimem`` reductions in the gradient reduce-scatter
-                                 (default off: plain peer loads).
-    ``OLMO_B200_WAIT_BUDGET``    iteration budget of every device-side bounded wait.
-    ``OLMO_B200_ATTENTION``      ``native`` (tcgen05 kernel) or ``library`` (flash-attn package).
-    ``OLMO_B200_GEMM_2CTA``      use the two-CTA ``cta_group::2`` GEMM kernel (default on).
-    ``OLMO_B200_KEEP_ACTS``      ``auto`` (default), ``1`` or ``0``: keep the rotated q/k and SwiGLU outputs of every
-                                 block for the backward pass instead of recomputing them; ``auto`` decides after the
-                                 first step from the device memory still free (read in ``parallel/fsdp.py``).
-    ``OLMO_B200_COMM_CTAS``, ``OLMO_B200_RS_CTAS``, ``OLMO_B200_RS_SUMSQ``   communication CTAs riding on GEMM launches
-                                 for the all-gather / reduce-scatter and the fused gradient-norm partials
-                                 (read in ``parallel/peer.py``).
-    ``OLMO_B200_HEAD_CHUNK``     rows of logits materialised at a time by the LM-head + loss path (default 8192).
-    ``OLMO_B200_NVTX``           ``1`` adds NVTX spans around trainer phases and every block's forward / backward.
-    ``OLMO_B200_W4_TARGET_CTAS`` CTAs the 4-bit decode GEMM aims at when it splits K (default 444).
+    Execution
+      ``OLMO_B200_KERNELS``        use the sm_100a kernel library on CUDA devices (default on; the library being absent
+                                   on a GPU machine is an error, not a silent fallback).  ``ops/__init__.py``
+      ``OLMO_B200_SCHEDULE``       ``auto`` (default), ``resident`` (every unit stays gathered between uses) or
+                                   ``sharded`` (FULL_SHARD proper: block units streamed through slots, gathered in
+                                   forward and in backward, reduced per micro-batch).  ``parallel/fsdp.py``
+      ``OLMO_B200_FUSED_COMM``     carry all-gathers and reduce-scatters over peer memory inside GEMM launches
+                                   (default on when several GPUs share a node; ``0``: NCCL collectives).  ``parallel/fsdp.py``
+      ``OLMO_B200_KEEP_ACTS``      ``auto`` (default), ``1`` or ``0``: keep the rotated q/k and SwiGLU outputs of every
+                                   block for the backward pass instead of recomputing them; ``auto`` decides after the
+                                   first step from the device memory still free.  ``parallel/fsdp.py``
+      ``OLMO_B200_ATTENTION``      ``native`` (tcgen05 kernel; other head sizes and lengths are zero-padded onto it) or
+                                   ``library`` (the flash-attn package).  ``ops/attention.py``
+      ``OLMO_B200_HEAD_CHUNK``     rows of logits materialised at a time by the LM-head + loss path (default 8192).
+    Kernel variants (for A/B measurements; the defaults are the fast ones)
+      ``OLMO_B200_GEMM_2CTA``      two-CTA ``cta_group::2`` GEMM (default on); ``OLMO_B200_GEMM_TMA_STORE`` its
+                                   shared-memory-staged TMA-store epilogue (default on).  ``ops/__init__.py``
+      ``OLMO_B200_COMM_CTAS``, ``OLMO_B200_RS_CTAS``, ``OLMO_B200_COMM_STANDALONE_CTAS``   CTAs that carry an all-gather /
+                                   a reduce-scatter inside a GEMM launch / in a stand-alone launch (0: chosen from the
+                                   sizes).  ``OLMO_B200_RS_SUMSQ`` (default on): gradient-norm partials come out of
+                                   the reduce-scatter.  ``parallel/peer.py``
+      ``OLMO_B200_WAIT_BUDGET_MS`` time limit of every device-side wait on a peer's flag (default 30000 ms); when it runs
+                                   out the kernel records a status word and returns, and the host raises.  ``parallel/peer.py``
+      ``OLMO_B200_DECODE_GEMM``    ``auto`` (default), ``native`` or ``library`` for the serving decode projections;
+                                   ``OLMO_B200_W4_TARGET_CTAS`` CTAs the 4-bit decode GEMM aims at when it splits K
+                                   (default 444).  ``serve/static_cache.py``, ``csrc/w4a16_mma.cu``
+    Host side
+      ``OLMO_B200_NATIVE_DATA``    ``0`` disables the C++ token reader (byte-range reads from Python instead).
+      ``OLMO_B200_NVTX``           ``1`` adds NVTX spans around trainer phases and every block's forward / backward.
+      ``OLMO_B200_WRITE_REFERENCE_LAYOUT``  ``1`` with ``sharded_checkpointer: torch_new`` writes sharded checkpoints in the
+                                   reference's ``torch_new`` layout.  ``checkpoint.py``
+    Shared with the reference: ``OLMO_SHARED_FS``, ``FS_LOCAL_RANK``, ``OLMO_NUM_THREADS``, ``OLMO_NO_SSL``; package data is
+    looked up under ``OLMO_DATA_DIR`` first, downloads are cached under ``OLMO_CACHE_DIR``.
     """
 
     kernels: bool = True
     fused_comm: bool = True
-    multimem: bool = False
-    wait_budget: int = 200_000_000
+    schedule: str = "auto"
+    keep_acts: str = "auto"
     attention: str = "native"
+    wait_budget_ms: float = 30000.0
 
     @classmethod
     def from_env(cls) -> "B200Runtime":
         return cls(
             kernels=_env_flag("OLMO_B200_KERNELS", True),
             fused_comm=_env_flag("OLMO_B200_FUSED_COMM", True),
-            multimem=_env_flag("OLMO_B200_MULTIMEM", False),
-            wait_budget=int(os.environ.get("OLMO_B200_WAIT_BUDGET", 200_000_000)),
-            attention=os.environ.get("OLMO_B200_ATTENTION", "native"),
+            schedule=os.environ.get("OLMO_B200_SCHEDULE", "auto").strip().lower(),
+            keep_acts=os.environ.get("OLMO_B200_KEEP_ACTS", "auto").strip().lower(),
+            attention=os.environ.get("OLMO_B200_ATTENTION", "native").strip().lower(),
+            wait_budget_ms=float(os.environ.get("OLMO_B200_WAIT_BUDGET_MS", "30000")),
         )

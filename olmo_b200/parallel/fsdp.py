@@ -159,7 +159,7 @@ class FlatShardEngine:
         )
         sched = os.environ.get("OLMO_B200_SCHEDULE", "auto").strip().lower()
         if os.environ.get("OLMO_B200_RESHARD", "0") not in ("0", "", "false"):
-            sched = "sharded"
+            sched = "sharded"  # older spelling of OLMO_B200_SCHEDULE=sharded, still honoured
         if sched not in ("auto", "resident", "sharded"):
             raise OLMoConfigurationError("OLMO_B200_SCHEDULE must be one of auto, resident, sharded")
         self._schedule_request = sched
