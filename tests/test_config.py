@@ -317,3 +317,24 @@ def test_random_overrides_round_trip_through_dotlist_and_yaml(tmp_path):
                 assert plain(lookup(again.asdict(), name)) == plain(lookup(defaults, name)), name
 
     check()
+
+
+def test_every_runtime_environment_variable_is_documented():
+    """The docstring of ``B200Runtime`` is the list of this framework's environment variables: every ``OLMO_B200_*`` name
+    read anywhere in the package (Python or device code) appears there, and it names none that nothing reads."""
+    import re
+    from pathlib import Path
+
+    from olmo_b200.config import B200Runtime
+
+    pkg = Path(__file__).resolve().parent.parent / "olmo_b200"
+    read = set()
+    for path in list(pkg.rglob("*.py")) + list((pkg / "csrc").rglob("*.cu")) + list((pkg / "csrc").rglob("*.cuh")):
+        text = path.read_text()
+        if path.name == "config.py":
+            text = text.replace(B200Runtime.__doc__ or "", "")
+        read |= set(re.findall(r"OLMO_B200_[A-Z0-9_]+", text))
+    documented = set(re.findall(r"OLMO_B200_[A-Z0-9_]+", B200Runtime.__doc__ or ""))
+    read.discard("OLMO_B200_RESHARD")  # older spelling of OLMO_B200_SCHEDULE=sharded, honoured but not advertised
+    assert read - documented == set(), f"undocumented: {sorted(read - documented)}"
+    assert documented - read == set(), f"documented but never read: {sorted(documented - read)}"
