@@ -248,12 +248,6 @@ class Optimizer(OptimizerBase):
         return None
 
 
-def _step_count(state: Dict[str, Any], param: torch.Tensor) -> torch.Tensor:
-    if "step" not in state:
-        state["step"] = torch.tensor(0.0, dtype=torch.float32)
-    return state["step"]
-
-
 class LionW(Optimizer):
     """Lion with decoupled weight decay: ``p ← p(1 − lr·wd) − lr·sign(β₁m + (1−β₁)g)``, ``m ← β₂m + (1−β₂)g``."""
 
