@@ -616,3 +616,42 @@ def test_positional_args_helper(capsys):
     with pytest.raises(SystemExit) as e:
         positional_args("the usage", 0, ["-h"])
     assert e.value.code == 0 and "the usage" in capsys.readouterr().out
+
+
+def test_mix_builder_properties():
+    """Property test of the data-mix builder on random sources: a fraction or token target is met by whole files and
+    overshoots by less than one file, a repetition of ``k + f`` holds every file ``k`` or ``k + 1`` times, the same seed
+    gives the same mix, asking for more than a source holds is refused, and the shares sum to one."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from olmo_b200.data.mix_builder import Source, build_mix
+
+    files = st.lists(st.integers(1, 500), min_size=1, max_size=12)
+
+    @settings(max_examples=80, deadline=None)
+    @given(sizes_a=files, sizes_b=files, fraction=st.floats(0.05, 1.0), repeat=st.floats(1.0, 3.5), seed=st.integers(0, 1000))
+    def check(sizes_a, sizes_b, fraction, repeat, seed):
+        a = Source("mem://a", fraction=fraction, files=[(f"mem://a/{i:03d}.npy", 4 * n) for i, n in enumerate(sizes_a)])
+        b = Source("mem://b", repeat=repeat, files=[(f"mem://b/{i:03d}.npy", 4 * n) for i, n in enumerate(sizes_b)])
+        paths, rows = build_mix([a, b], bytes_per_token=4, seed=seed)
+        again, _ = build_mix([a, b], bytes_per_token=4, seed=seed)
+        assert paths == again
+        size_of = dict(a.files + b.files)
+        got_a = [p for p in paths if p.startswith("mem://a/")]
+        got_b = [p for p in paths if p.startswith("mem://b/")]
+        assert len(set(got_a)) == len(got_a)  # a fraction never takes a file twice
+        tokens_a, target_a = sum(size_of[p] // 4 for p in got_a), fraction * sum(sizes_a)
+        assert tokens_a >= min(target_a, sum(sizes_a)) - 1e-6
+        assert tokens_a - target_a < max(sizes_a) + 1e-6  # overshoot: less than one (the last) file
+        whole = int(repeat)
+        counts = {p: got_b.count(p) for p, _ in b.files}
+        assert set(counts.values()) <= {whole, whole + 1}
+        tokens_b = sum(size_of[p] // 4 for p in got_b)
+        assert tokens_b >= repeat * sum(sizes_b) - 1e-6 or all(c == whole + 1 for c in counts.values())
+        assert rows[0]["tokens"] == tokens_a and rows[1]["tokens"] == tokens_b
+        assert sum(r["share"] for r in rows) == pytest.approx(1.0)
+
+    check()
+    with pytest.raises(ValueError, match="use repeat"):
+        build_mix([Source("mem://a", tokens=1000, files=[("mem://a/0.npy", 400)])], bytes_per_token=4)
