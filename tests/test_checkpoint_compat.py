@@ -232,3 +232,60 @@ def test_torch_new_layout_is_written_to_and_read_from_a_remote_store():
         assert got_optim["param_groups"][0]["params"] == list(model)
     finally:
         util._BACKENDS.pop("mem", None)
+
+
+def test_range_reader_behaves_like_a_file_under_random_seeks_and_reads():
+    """Property test: the byte-range view of a remote object, wrapped in a buffered reader the way the checkpoint
+    reader wraps it, returns what ``io.BytesIO`` returns for any sequence of seeks (all three origins, past either end)
+    and reads (sized, to the end, zero-length)."""
+    import io
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from olmo_b200 import util
+    from olmo_b200.checkpoint import _RangeReader
+
+    class Store(util.StorageBackend):
+        def __init__(self):
+            self.blobs = {}
+
+        def file_size(self, url):
+            return len(self.blobs[url])
+
+        def get_bytes_range(self, url, start, num):
+            assert start >= 0 and num > 0 and start + num <= len(self.blobs[url])  # never asks outside the object
+            return self.blobs[url][start : start + num]
+
+    store = Store()
+    util.register_storage_backend("memrr", store)
+    ops = st.lists(st.one_of(
+        st.tuples(st.just("seek"), st.integers(-40, 300), st.sampled_from([io.SEEK_SET, io.SEEK_CUR, io.SEEK_END])),
+        st.tuples(st.just("read"), st.one_of(st.integers(0, 120), st.just(-1)), st.just(0)),
+    ), min_size=1, max_size=12)
+
+    @settings(max_examples=80, deadline=None)
+    @given(size=st.integers(0, 256), buffer_size=st.sampled_from([1, 7, 64, 1024]), script=ops, seed=st.integers(0, 99))
+    def check(size, buffer_size, script, seed):
+        data = bytes((seed + 31 * i) % 251 for i in range(size))
+        store.blobs["memrr://b/x"] = data
+        ours, theirs = io.BufferedReader(_RangeReader("memrr://b/x"), buffer_size=buffer_size), io.BytesIO(data)
+        for op, a, b in script:
+            if op == "seek":
+                if (b == io.SEEK_SET and a < 0) or (b == io.SEEK_CUR and theirs.tell() + a < 0) or (b == io.SEEK_END and size + a < 0):
+                    continue  # BytesIO raises on negative absolute positions; the view clamps: not comparable
+                want = theirs.seek(a, b)
+                if want > size:  # BytesIO may sit past the end, the view clamps to the end: both then read nothing
+                    theirs.seek(size)
+                    ours.seek(a, b)
+                    assert ours.read(5) == b""
+                    continue
+                assert ours.seek(a, b) == want
+            else:
+                assert ours.read(a) == theirs.read(a)
+            assert ours.tell() == theirs.tell()
+
+    try:
+        check()
+    finally:
+        util._BACKENDS.pop("memrr", None)
