@@ -47,10 +47,10 @@ def flatten_dict(d: Dict) -> Dict[STKey, torch.Tensor]:
     def walk(node: Any, path: Tuple) -> None:
         if isinstance(node, torch.Tensor):
             out[STKey(path, False)] = node
-        elif isinstance(node, dict):
+        elif isinstance(node, dict) and (node or not path):
             for k, v in node.items():
                 walk(v, path + (k,))
-        else:
+        else:  # any other leaf, an empty dictionary included (walking into it would lose its key), is stored pickled
             blob = torch.frombuffer(bytearray(pickle.dumps(node)), dtype=torch.uint8)
             out[STKey(path, True)] = blob
 
@@ -73,6 +73,16 @@ def state_dict_to_safetensors_file(state_dict: Dict, filename: PathOrStr) -> Non
     import safetensors.torch
 
     flat = {encode_key(k): v.contiguous() for k, v in flatten_dict(state_dict).items()}
+    # The file format stores every tensor on its own and its writer refuses tensors whose memory overlaps (two names for
+    # one tensor, overlapping views).  Disjoint slices of one buffer are fine; of overlapping ones all but the first
+    # are copied, so what is written is what the caller passed.
+    spans = sorted((t.data_ptr(), t.data_ptr() + t.numel() * t.element_size(), name) for name, t in flat.items() if t.numel() > 0)
+    reach = -1
+    for start, end, name in spans:
+        if start < reach:
+            flat[name] = flat[name].clone()
+        else:
+            reach = end  # only tensors that are written in place occupy their range
     safetensors.torch.save_file(flat, str(filename))
 
 

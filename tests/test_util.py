@@ -237,3 +237,47 @@ def test_rich_handler_formats_records_and_tracebacks():
         rich._console = previous
     out = buffer.getvalue()
     assert "hello world" in out and "rank=" in out and "[rich-handler-test:" in out and "ValueError" in out and "boom" in out
+
+
+def test_safetensors_flavour_round_trips_random_nested_states(tmp_path):
+    """Property test: nested dictionaries of tensors (several dtypes, zero-size, non-contiguous, views of one buffer) and
+    plain Python leaves (numbers, strings, ``None``, lists, empty dictionaries) come back equal, types included."""
+    from hypothesis import HealthCheck, given, settings
+    from hypothesis import strategies as st
+
+    dtypes = [torch.float32, torch.bfloat16, torch.int64, torch.uint8, torch.bool, torch.float16]
+    flat = torch.arange(64, dtype=torch.float32)
+
+    def tensor_of(kind, seed):
+        g = torch.Generator().manual_seed(seed)
+        if kind == "view":
+            a = seed % 32
+            return flat[a : a + 8 + seed % 8]
+        if kind == "transposed":
+            return torch.randn(3, 4, generator=g).t()
+        if kind == "empty":
+            return torch.zeros(0, 5)
+        if kind == "scalar":
+            return torch.tensor(float(seed))
+        return (torch.randn(2, 3, generator=g) * 5).to(dtypes[seed % len(dtypes)])
+
+    tensors = st.builds(tensor_of, st.sampled_from(["view", "transposed", "empty", "scalar", "dense"]), st.integers(0, 1000))
+    plain = st.one_of(st.integers(-5, 5), st.floats(-1, 1), st.text(max_size=5), st.none(), st.lists(st.integers(0, 3), max_size=3), st.just({}))
+    keys = st.one_of(st.text(alphabet="abc._", min_size=1, max_size=6), st.integers(0, 9))
+    trees = st.recursive(st.one_of(tensors, plain), lambda kids: st.dictionaries(keys, kids, min_size=1, max_size=4), max_leaves=10)
+
+    def same(a, b):
+        if isinstance(a, torch.Tensor):
+            return isinstance(b, torch.Tensor) and a.dtype == b.dtype and a.shape == b.shape and torch.equal(a, b)
+        if isinstance(a, dict):
+            return isinstance(b, dict) and a.keys() == b.keys() and all(same(a[k], b[k]) for k in a)
+        return type(a) is type(b) and a == b
+
+    @settings(max_examples=60, deadline=None, suppress_health_check=[HealthCheck.function_scoped_fixture, HealthCheck.too_slow])
+    @given(st.dictionaries(keys, trees, min_size=0, max_size=4))
+    def check(state):
+        path = tmp_path / "s.safetensors"
+        state_dict_to_safetensors_file(state, path)
+        assert same(state, safetensors_file_to_state_dict(path))
+
+    check()
