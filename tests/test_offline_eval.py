@@ -294,3 +294,44 @@ def test_reference_named_task_sets_resolve():
     assert all(t["task_name"] in label_to_task_map for t in offline.resolve_task_set("rc20_tasks")["tasks"])
     spec = offline.load_experiment(str(offline.TASK_SET_DIR.parent / "experiments" / "evaluation_2023_07_26.yaml"))
     assert [ts["name"] for ts in spec["task_sets"]] == ["rc20_tasks", "gen_tasks", "summary_tasks", "eval_suite_ppl_val_v2_small"]
+
+
+def test_generation_metrics_against_brute_force():
+    """Property test: ROUGE-L's longest common subsequence equals an exhaustive search over subsequences, word F1 equals
+    the multiset-overlap definition, both are symmetric in their F-measure, 1 on identical texts and 0 on disjoint ones."""
+    from itertools import combinations
+
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    from olmo_b200.eval.offline import exact_match, rouge_l, token_f1
+
+    words = st.lists(st.sampled_from(["red", "green", "blue", "cat", "dog"]), min_size=0, max_size=7)
+
+    def lcs_brute(a, b):
+        for n in range(min(len(a), len(b)), 0, -1):
+            subs = {tuple(a[i] for i in idx) for idx in combinations(range(len(a)), n)}
+            if any(tuple(b[i] for i in idx) in subs for idx in combinations(range(len(b)), n)):
+                return n
+        return 0
+
+    def f(p, r):
+        return 0.0 if p == 0 or r == 0 else 2 * p * r / (p + r)
+
+    @settings(max_examples=120, deadline=None)
+    @given(a=words, b=words)
+    def check(a, b):
+        ta, tb = " ".join(a), " ".join(b)
+        got = rouge_l(ta, [tb])
+        want = f(lcs_brute(a, b) / len(a), lcs_brute(a, b) / len(b)) if a and b else 0.0
+        assert got == pytest.approx(want)
+        assert rouge_l(tb, [ta]) == pytest.approx(got)
+        overlap = sum(min(a.count(w), b.count(w)) for w in set(a))
+        want_f1 = float(a == b) if not a or not b else f(overlap / len(a), overlap / len(b))
+        assert token_f1(ta, [tb]) == pytest.approx(want_f1) and token_f1(tb, [ta]) == pytest.approx(want_f1)
+        assert token_f1(ta, [tb]) >= rouge_l(ta, [tb]) - 1e-12  # a subsequence is also a multiset overlap
+        if a:
+            assert rouge_l(ta, [ta]) == 1.0 and token_f1(ta, ["The " + ta + "."]) == 1.0 and exact_match(ta.upper() + "!", [ta]) == 1.0
+        assert rouge_l(ta, [tb, ta]) >= got  # the best reference counts
+
+    check()
