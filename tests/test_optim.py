@@ -281,3 +281,30 @@ def test_ten_step_trajectory_matches_torch_adamw_with_clip_grad_norm():
         for (name, p), q in zip(ours.named_parameters(), theirs.parameters()):
             torch.testing.assert_close(p, q, rtol=2e-5, atol=2e-6, msg=lambda m: f"step {step}, {name}: {m}")
     assert clipped > 0  # the clipping branch was exercised, not only the pass-through
+
+
+def test_schedule_shape_properties():
+    """Property test of the warm-up + decay schedules: the rate never leaves [floor, peak] after warm-up, rises during
+    warm-up, does not rise afterwards, reaches the peak at the end of warm-up and the floor at the horizon and beyond."""
+    from hypothesis import given, settings
+    from hypothesis import strategies as st
+
+    @settings(max_examples=80, deadline=None)
+    @given(kind=st.sampled_from(["cos", "linear"]), warmup=st.integers(0, 50), extra=st.integers(1, 200), alpha=st.floats(0.0, 1.0),
+           peak=st.floats(1e-6, 1.0), use_t_max=st.booleans())
+    def check(kind, warmup, extra, alpha, peak, use_t_max):
+        horizon = warmup + extra
+        cls = CosWithWarmup if kind == "cos" else LinearWithWarmup
+        sched = cls(warmup_steps=warmup, alpha_f=alpha, t_max=horizon if use_t_max else None, **BASE)
+        max_steps = horizon if not use_t_max else horizon + 37  # with t_max the trainer's own horizon must not matter
+        rates = [sched.get_lr(peak, s, max_steps) for s in range(horizon + 5)]
+        floor = peak * alpha
+        tol = 1e-12 + 1e-9 * peak
+        assert rates[warmup] == pytest.approx(peak, rel=1e-9)
+        assert all(a <= b + tol for a, b in zip(rates[:warmup], rates[1 : warmup + 1]))  # warm-up rises
+        assert all(a + tol >= b for a, b in zip(rates[warmup:], rates[warmup + 1 :]))  # decay never rises
+        assert all(floor - tol <= r <= peak + tol for r in rates[warmup:])
+        assert all(r == pytest.approx(floor, abs=tol) for r in rates[horizon:])
+        assert all(0 <= r <= peak + tol for r in rates[:warmup])
+
+    check()
