@@ -36,6 +36,7 @@ from pathlib import Path
 from typing import Any, Dict, Generator, List, Optional, Set, Tuple
 
 import torch
+import torch.distributed as dist
 import torch.nn as nn
 import yaml
 
@@ -44,8 +45,6 @@ from .config import ShardedCheckpointerType, TrainConfig
 from .exceptions import OLMoCheckpointError
 from .optim import Optimizer, fix_optim_state_dict
 from .safetensors_util import safetensors_file_to_state_dict
-import torch.distributed as dist
-
 from .torch_util import barrier, get_fs_local_rank, get_global_rank, get_world_size, is_distributed
 from .util import default_thread_count, dir_is_empty, is_url, resource_path, upload, wait_for
 
@@ -96,6 +95,15 @@ def load_state_dict(checkpoint_dir: PathOrStr, fname: str, *, local_cache: Optio
             pass
     path = resource_path(str(checkpoint_dir).rstrip("/"), fname, local_cache=local_cache)
     try:
+        if str(map_location) == "cpu":
+            # Map the file instead of reading it: the ranks of a node that restore from the same file then share its pages
+            # through the page cache instead of each holding a private copy (the mapping is private: writes to the tensors
+            # never reach the file).  Files in torch's older, non-archive format cannot be mapped and are read.
+            try:
+                return torch.load(path, map_location=map_location, weights_only=False, mmap=True)
+            except (RuntimeError, ValueError) as e:
+                if "mmap" not in str(e):
+                    raise
         return torch.load(path, map_location=map_location, weights_only=False)
     except (RuntimeError, EOFError, pickle.UnpicklingError, ValueError, OSError) as e:
         if isinstance(e, FileNotFoundError):
